@@ -1,0 +1,461 @@
+// Python bindings of the sm_100a kernels (module elysium_wan_b200._C).
+//
+// Thin: each function checks dtypes, contiguity of the innermost dimension and
+// alignment, derives leading dimensions from tensor strides, launches on the
+// current CUDA stream and raises on any rejected argument or launch error.
+// The launch counter is how the benchmark reports how many of this library's
+// kernels ran inside its timed region.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <execinfo.h>
+#include <signal.h>
+#include <unistd.h>
+
+#include <atomic>
+
+#include "gemm.h"
+#include "kernels.h"
+
+namespace {
+
+std::atomic<long long> g_launches{0};
+
+void count(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+// One device status word per GPU (an int in device memory): kernels that time
+// out on a bounded wait record a code there; the host reads it after a step.
+int* status_word(int dev) {
+  static int* words[64] = {nullptr};
+  if (dev < 0 || dev >= 64) return nullptr;
+  if (words[dev] == nullptr) {
+    int* p = nullptr;
+    TORCH_CHECK(cudaMalloc(&p, sizeof(int)) == cudaSuccess, "status word allocation failed");
+    TORCH_CHECK(cudaMemset(p, 0, sizeof(int)) == cudaSuccess, "status word init failed");
+    words[dev] = p;
+  }
+  return words[dev];
+}
+
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void check_cuda(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+}
+
+void check_2d_rowmajor(const at::Tensor& t, const char* name) {
+  check_cuda(t, name);
+  TORCH_CHECK(t.dim() == 2, name, " must be 2-D");
+  TORCH_CHECK(t.stride(1) == 1, name, " must have a contiguous inner dimension");
+}
+
+void ok(int rc, const char* what) { TORCH_CHECK(rc == 0, what, " failed with code ", rc); }
+
+template <typename T>
+T* ptr_or_null(const c10::optional<at::Tensor>& t) {
+  return t.has_value() && t->defined() ? reinterpret_cast<T*>(t->data_ptr()) : nullptr;
+}
+
+// C[m, n] = sum_k A[m, k] B[n, k]; A is [M, K] (a_mn=False) or [K, M]; B is
+// [N, K] (b_mn=False) or [K, N].
+void gemm(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor out, int64_t epi,
+          c10::optional<at::Tensor> bias, c10::optional<at::Tensor> resid,
+          c10::optional<at::Tensor> resid_scale, c10::optional<at::Tensor> aux,
+          c10::optional<at::Tensor> scale_out, double beta, int64_t bn) {
+  check_2d_rowmajor(a, "a");
+  check_2d_rowmajor(b, "b");
+  check_2d_rowmajor(out, "out");
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16,
+              "gemm operands must be bf16");
+  const int M = a_mn ? a.size(1) : a.size(0);
+  const int K = a_mn ? a.size(0) : a.size(1);
+  const int N = b_mn ? b.size(1) : b.size(0);
+  const int Kb = b_mn ? b.size(0) : b.size(1);
+  TORCH_CHECK(K == Kb, "gemm K mismatch: ", K, " vs ", Kb);
+  TORCH_CHECK(out.size(0) == M && out.size(1) == N, "gemm out shape mismatch");
+  c10::cuda::CUDAGuard guard(a.device());
+  ewb::GemmArgs g{};
+  g.a = a.data_ptr();
+  g.lda = a.stride(0);
+  g.a_mn = a_mn;
+  g.b = b.data_ptr();
+  g.ldb = b.stride(0);
+  g.b_mn = b_mn;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.bn = bn;
+  g.status = status_word(a.get_device());
+  ewb::GemmEpilogue& e = g.ep;
+  e.kind = static_cast<int>(epi);
+  e.out = out.data_ptr();
+  e.ldo = out.stride(0);
+  e.bias = ptr_or_null<const float>(bias);
+  if (bias.has_value() && bias->defined())
+    TORCH_CHECK(bias->scalar_type() == at::kFloat && bias->numel() >= N, "bias must be fp32 [N]");
+  if (resid.has_value() && resid->defined()) {
+    check_2d_rowmajor(*resid, "resid");
+    e.resid = resid->data_ptr();
+    e.ldr = resid->stride(0);
+    e.resid_fp8 = resid->scalar_type() == at::kFloat8_e4m3fn ? 1 : 0;
+    if (e.resid_fp8) {
+      TORCH_CHECK(resid_scale.has_value() && resid_scale->defined(), "fp8 resid needs scales");
+      e.resid_scale = resid_scale->data_ptr<float>();
+      e.ld_resid_scale = resid_scale->stride(0);
+    } else {
+      TORCH_CHECK(resid->scalar_type() == at::kBFloat16, "resid must be bf16 or e4m3");
+    }
+  }
+  if (aux.has_value() && aux->defined()) {
+    check_2d_rowmajor(*aux, "aux");
+    e.aux = aux->data_ptr();
+    e.ldaux = aux->stride(0);
+  }
+  if (scale_out.has_value() && scale_out->defined()) {
+    e.scale_out = scale_out->data_ptr<float>();
+    e.ld_scale_out = scale_out->stride(0);
+  }
+  e.beta = static_cast<float>(beta);
+  switch (e.kind) {
+    case ewb::kEpiBf16:
+    case ewb::kEpiGelu:
+    case ewb::kEpiResid:
+    case ewb::kEpiDGelu:
+      TORCH_CHECK(out.scalar_type() == at::kBFloat16, "out must be bf16 for this epilogue");
+      break;
+    case ewb::kEpiAccF32:
+    case ewb::kEpiF32:
+      TORCH_CHECK(out.scalar_type() == at::kFloat, "out must be fp32 for this epilogue");
+      break;
+    case ewb::kEpiResidQ8:
+      TORCH_CHECK(out.scalar_type() == at::kFloat8_e4m3fn, "out must be e4m3");
+      TORCH_CHECK(e.scale_out != nullptr, "scale_out required");
+      break;
+    default: TORCH_CHECK(false, "unknown epilogue ", epi);
+  }
+  if (e.kind == ewb::kEpiGelu || e.kind == ewb::kEpiDGelu) TORCH_CHECK(e.aux, "aux required");
+  if (e.kind == ewb::kEpiResid || e.kind == ewb::kEpiResidQ8) TORCH_CHECK(e.resid, "resid required");
+  ok(ewb::gemm_launch(g, cur_stream()), "gemm");
+  count(1);
+}
+
+int64_t gemm_pick_bn(int64_t M, int64_t N) { return ewb::gemm_pick_bn(M, N); }
+
+void layernorm_fwd(at::Tensor x, c10::optional<at::Tensor> x_scale, at::Tensor gamma,
+                   at::Tensor beta, at::Tensor y, at::Tensor mean, at::Tensor rstd, double eps) {
+  check_2d_rowmajor(x, "x");
+  check_2d_rowmajor(y, "y");
+  c10::cuda::CUDAGuard guard(x.device());
+  ewb::LnArgs a{};
+  a.x = x.data_ptr();
+  a.x_fp8 = x.scalar_type() == at::kFloat8_e4m3fn;
+  a.ldx = x.stride(0);
+  if (a.x_fp8) {
+    TORCH_CHECK(x_scale.has_value(), "fp8 input needs scales");
+    a.x_scale = x_scale->data_ptr<float>();
+    a.ldxs = x_scale->stride(0);
+  } else {
+    TORCH_CHECK(x.scalar_type() == at::kBFloat16, "x must be bf16 or e4m3");
+  }
+  a.gamma = gamma.data_ptr<float>();
+  a.beta = beta.data_ptr<float>();
+  a.y = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
+  a.ldy = y.stride(0);
+  a.mean = mean.data_ptr<float>();
+  a.rstd = rstd.data_ptr<float>();
+  a.rows = x.size(0);
+  a.d = x.size(1);
+  a.eps = static_cast<float>(eps);
+  ok(ewb::layernorm_fwd(a, cur_stream()), "layernorm_fwd");
+  count(1);
+}
+
+int64_t layernorm_bwd_chunks(int64_t rows) {
+  const int rpc = ewb::layernorm_bwd_rows_per_chunk(rows);
+  return (rows + rpc - 1) / rpc;
+}
+
+void layernorm_bwd(at::Tensor dy, at::Tensor x, c10::optional<at::Tensor> x_scale, at::Tensor mean,
+                   at::Tensor rstd, at::Tensor gamma, c10::optional<at::Tensor> dres,
+                   at::Tensor dx, at::Tensor part_g, at::Tensor part_b, at::Tensor dgamma,
+                   at::Tensor dbeta, bool accumulate) {
+  check_2d_rowmajor(dy, "dy");
+  check_2d_rowmajor(x, "x");
+  check_2d_rowmajor(dx, "dx");
+  c10::cuda::CUDAGuard guard(x.device());
+  ewb::LnBwdArgs a{};
+  a.dy = reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr());
+  a.lddy = dy.stride(0);
+  a.x = x.data_ptr();
+  a.x_fp8 = x.scalar_type() == at::kFloat8_e4m3fn;
+  a.ldx = x.stride(0);
+  if (a.x_fp8) {
+    a.x_scale = x_scale->data_ptr<float>();
+    a.ldxs = x_scale->stride(0);
+  }
+  a.mean = mean.data_ptr<float>();
+  a.rstd = rstd.data_ptr<float>();
+  a.gamma = gamma.data_ptr<float>();
+  if (dres.has_value() && dres->defined()) {
+    a.dres = reinterpret_cast<const __nv_bfloat16*>(dres->data_ptr());
+    a.lddres = dres->stride(0);
+  }
+  a.dx = reinterpret_cast<__nv_bfloat16*>(dx.data_ptr());
+  a.lddx = dx.stride(0);
+  a.rows = x.size(0);
+  a.d = x.size(1);
+  a.rows_per_chunk = ewb::layernorm_bwd_rows_per_chunk(a.rows);
+  const int chunks = (a.rows + a.rows_per_chunk - 1) / a.rows_per_chunk;
+  TORCH_CHECK(part_g.numel() >= static_cast<int64_t>(chunks) * a.d, "part_g too small");
+  TORCH_CHECK(part_b.numel() >= static_cast<int64_t>(chunks) * a.d, "part_b too small");
+  a.part_g = part_g.data_ptr<float>();
+  a.part_b = part_b.data_ptr<float>();
+  a.dgamma = dgamma.data_ptr<float>();
+  a.dbeta = dbeta.data_ptr<float>();
+  a.accumulate = accumulate ? 1 : 0;
+  ok(ewb::layernorm_bwd(a, cur_stream()), "layernorm_bwd");
+  count(3);
+}
+
+void attention_fwd(at::Tensor qkv, at::Tensor o, at::Tensor lse, int64_t B, int64_t S, int64_t H,
+                   int64_t hd, double scale) {
+  check_cuda(qkv, "qkv");
+  TORCH_CHECK(qkv.is_contiguous() && o.is_contiguous() && lse.is_contiguous(), "contiguous");
+  c10::cuda::CUDAGuard guard(qkv.device());
+  ewb::AttnArgs a{};
+  a.qkv = reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr());
+  a.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
+  a.lse = lse.data_ptr<float>();
+  a.B = B;
+  a.S = S;
+  a.H = H;
+  a.hd = hd;
+  a.d = H * hd;
+  a.scale = static_cast<float>(scale);
+  TORCH_CHECK(qkv.numel() == B * S * 3 * a.d, "qkv shape");
+  ok(ewb::attention_fwd(a, cur_stream()), "attention_fwd");
+  count(1);
+}
+
+void attention_bwd(at::Tensor qkv, at::Tensor o, at::Tensor dout, at::Tensor lse, at::Tensor Dbuf,
+                   at::Tensor dqkv, int64_t B, int64_t S, int64_t H, int64_t hd, double scale) {
+  TORCH_CHECK(qkv.is_contiguous() && o.is_contiguous() && dout.is_contiguous() &&
+                  dqkv.is_contiguous(),
+              "contiguous");
+  c10::cuda::CUDAGuard guard(qkv.device());
+  ewb::AttnBwdArgs a{};
+  a.qkv = reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr());
+  a.o = reinterpret_cast<const __nv_bfloat16*>(o.data_ptr());
+  a.dout = reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr());
+  a.lse = lse.data_ptr<float>();
+  a.Dbuf = Dbuf.data_ptr<float>();
+  a.dqkv = reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr());
+  a.B = B;
+  a.S = S;
+  a.H = H;
+  a.hd = hd;
+  a.d = H * hd;
+  a.scale = static_cast<float>(scale);
+  ok(ewb::attention_bwd(a, cur_stream()), "attention_bwd");
+  count(3);
+}
+
+void cross_entropy(at::Tensor logits, int64_t V, at::Tensor targets, at::Tensor loss_rows,
+                   c10::optional<at::Tensor> dlogits, double grad_scale) {
+  check_2d_rowmajor(logits, "logits");
+  TORCH_CHECK(logits.scalar_type() == at::kFloat, "logits fp32");
+  TORCH_CHECK(targets.scalar_type() == at::kLong, "targets int64");
+  c10::cuda::CUDAGuard guard(logits.device());
+  ewb::CeArgs a{};
+  a.logits = logits.data_ptr<float>();
+  a.ldl = logits.stride(0);
+  a.targets = targets.data_ptr<int64_t>();
+  a.T = logits.size(0);
+  a.V = V;
+  a.loss_rows = loss_rows.data_ptr<float>();
+  if (dlogits.has_value() && dlogits->defined()) {
+    check_2d_rowmajor(*dlogits, "dlogits");
+    a.dlogits = reinterpret_cast<__nv_bfloat16*>(dlogits->data_ptr());
+    a.ldg = dlogits->size(1);
+    TORCH_CHECK(dlogits->stride(0) == a.ldg, "dlogits must be dense");
+  }
+  a.grad_scale = static_cast<float>(grad_scale);
+  ok(ewb::cross_entropy(a, cur_stream()), "cross_entropy");
+  count(1);
+}
+
+void mean_reduce(at::Tensor x, at::Tensor out) {
+  c10::cuda::CUDAGuard guard(x.device());
+  ok(ewb::mean_reduce(x.data_ptr<float>(), x.numel(), out.data_ptr<float>(), cur_stream()),
+     "mean_reduce");
+  count(1);
+}
+
+void embed_fwd(at::Tensor idx, at::Tensor wte, at::Tensor wpe, int64_t S,
+               c10::optional<at::Tensor> out_bf16, c10::optional<at::Tensor> out_q8,
+               c10::optional<at::Tensor> out_scale) {
+  c10::cuda::CUDAGuard guard(idx.device());
+  ewb::EmbedArgs a{};
+  a.idx = idx.data_ptr<int64_t>();
+  a.wte = wte.data_ptr<float>();
+  a.wpe = wpe.data_ptr<float>();
+  a.T = idx.numel();
+  a.S = S;
+  a.d = wte.size(1);
+  a.out_bf16 = ptr_or_null<__nv_bfloat16>(out_bf16);
+  a.out_q8 = ptr_or_null<uint8_t>(out_q8);
+  a.out_scale = ptr_or_null<float>(out_scale);
+  TORCH_CHECK((a.out_bf16 != nullptr) != (a.out_q8 != nullptr), "exactly one output format");
+  ok(ewb::embed_fwd(a, cur_stream()), "embed_fwd");
+  count(1);
+}
+
+void embed_bwd(at::Tensor idx, at::Tensor dx, int64_t S, at::Tensor order, at::Tensor dwte,
+               at::Tensor dwpe) {
+  c10::cuda::CUDAGuard guard(idx.device());
+  ewb::EmbedBwdArgs a{};
+  a.idx = idx.data_ptr<int64_t>();
+  a.dx = reinterpret_cast<const __nv_bfloat16*>(dx.data_ptr());
+  a.T = idx.numel();
+  a.S = S;
+  a.d = dwte.size(1);
+  a.V = dwte.size(0);
+  a.order = order.data_ptr<int>();
+  a.dwte = dwte.data_ptr<float>();
+  a.dwpe = dwpe.data_ptr<float>();
+  ok(ewb::embed_bwd(a, cur_stream()), "embed_bwd");
+  count(3);
+}
+
+void adamw(at::Tensor p, at::Tensor m, at::Tensor v, at::Tensor g,
+           c10::optional<at::Tensor> p_bf16, double lr, double b1, double b2, double eps,
+           double wd, int64_t step) {
+  TORCH_CHECK(p.scalar_type() == at::kFloat && m.scalar_type() == at::kFloat &&
+                  v.scalar_type() == at::kFloat && g.scalar_type() == at::kFloat,
+              "adamw state must be fp32");
+  TORCH_CHECK(p.numel() == m.numel() && p.numel() == v.numel() && p.numel() == g.numel(),
+              "adamw size mismatch");
+  c10::cuda::CUDAGuard guard(p.device());
+  ewb::AdamWArgs a{};
+  a.p = p.data_ptr<float>();
+  a.m = m.data_ptr<float>();
+  a.v = v.data_ptr<float>();
+  a.g = g.data_ptr<float>();
+  a.p_bf16 = ptr_or_null<__nv_bfloat16>(p_bf16);
+  a.n = p.numel();
+  a.lr = lr;
+  a.beta1 = b1;
+  a.beta2 = b2;
+  a.eps = eps;
+  a.wd = wd;
+  a.bc1 = static_cast<float>(1.0 - std::pow(b1, static_cast<double>(step)));
+  a.bc2 = static_cast<float>(1.0 - std::pow(b2, static_cast<double>(step)));
+  ok(ewb::adamw_step(a, cur_stream()), "adamw");
+  count(1);
+}
+
+int64_t colsum_chunks(int64_t T) { return ewb::colsum_part_rows(T); }
+
+void colsum(at::Tensor x, at::Tensor part, at::Tensor grad, bool accumulate) {
+  check_2d_rowmajor(x, "x");
+  c10::cuda::CUDAGuard guard(x.device());
+  TORCH_CHECK(part.numel() >= ewb::colsum_part_rows(x.size(0)) * x.size(1), "part too small");
+  ok(ewb::colsum_bf16(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.size(0), x.size(1),
+                      x.stride(0), part.data_ptr<float>(), grad.data_ptr<float>(),
+                      accumulate ? 1 : 0, cur_stream()),
+     "colsum");
+  count(2);
+}
+
+void quant_e4m3(at::Tensor x, at::Tensor q, at::Tensor scale) {
+  TORCH_CHECK(x.is_contiguous() && q.is_contiguous() && scale.is_contiguous(), "contiguous");
+  c10::cuda::CUDAGuard guard(x.device());
+  ok(ewb::quant_e4m3_rows(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.size(0),
+                          x.size(1), reinterpret_cast<uint8_t*>(q.data_ptr()),
+                          scale.data_ptr<float>(), cur_stream()),
+     "quant_e4m3");
+  count(1);
+}
+
+void dequant_e4m3(at::Tensor q, at::Tensor scale, at::Tensor y) {
+  TORCH_CHECK(y.is_contiguous() && q.is_contiguous() && scale.is_contiguous(), "contiguous");
+  c10::cuda::CUDAGuard guard(q.device());
+  ok(ewb::dequant_e4m3_rows(reinterpret_cast<const uint8_t*>(q.data_ptr()),
+                            scale.data_ptr<float>(), q.size(0), q.size(1),
+                            reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), cur_stream()),
+     "dequant_e4m3");
+  count(1);
+}
+
+void cast_bf16(at::Tensor x, at::Tensor y) {
+  TORCH_CHECK(x.is_contiguous() && y.is_contiguous() && x.numel() == y.numel(), "cast shapes");
+  c10::cuda::CUDAGuard guard(x.device());
+  ok(ewb::cast_f32_bf16(x.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(y.data_ptr()),
+                        x.numel(), cur_stream()),
+     "cast_bf16");
+  count(1);
+}
+
+int64_t launch_count() { return g_launches.load(); }
+
+// Opt-in diagnostics: print the native backtrace of a host SIGSEGV to stderr.
+void segv_backtrace(int sig) {
+  void* frames[64];
+  const int n = backtrace(frames, 64);
+  const char msg[] = "\n[ewb] native backtrace of the fatal signal:\n";
+  (void)!write(2, msg, sizeof(msg) - 1);
+  backtrace_symbols_fd(frames, n, 2);
+  signal(sig, SIG_DFL);
+  raise(sig);
+}
+
+void install_segv_backtrace() {
+  signal(SIGSEGV, segv_backtrace);
+  signal(SIGBUS, segv_backtrace);
+}
+
+// Read and clear the device status word of the current device (synchronises).
+int64_t status_read_clear() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int* p = status_word(dev);
+  int v = 0;
+  TORCH_CHECK(cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess,
+              "status read failed");
+  if (v != 0) cudaMemset(p, 0, sizeof(int));
+  return v;
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "sm_100a kernels of elysium_wan_b200";
+  m.def("gemm", &gemm);
+  m.def("gemm_pick_bn", &gemm_pick_bn);
+  m.def("layernorm_fwd", &layernorm_fwd);
+  m.def("layernorm_bwd", &layernorm_bwd);
+  m.def("layernorm_bwd_chunks", &layernorm_bwd_chunks);
+  m.def("attention_fwd", &attention_fwd);
+  m.def("attention_bwd", &attention_bwd);
+  m.def("cross_entropy", &cross_entropy);
+  m.def("mean_reduce", &mean_reduce);
+  m.def("embed_fwd", &embed_fwd);
+  m.def("embed_bwd", &embed_bwd);
+  m.def("adamw", &adamw);
+  m.def("colsum", &colsum);
+  m.def("colsum_chunks", &colsum_chunks);
+  m.def("quant_e4m3", &quant_e4m3);
+  m.def("dequant_e4m3", &dequant_e4m3);
+  m.def("cast_bf16", &cast_bf16);
+  m.def("launch_count", &launch_count);
+  m.def("install_segv_backtrace", &install_segv_backtrace);
+  m.def("status_read_clear", &status_read_clear);
+  m.attr("EPI_BF16") = static_cast<int>(ewb::kEpiBf16);
+  m.attr("EPI_GELU") = static_cast<int>(ewb::kEpiGelu);
+  m.attr("EPI_RESID") = static_cast<int>(ewb::kEpiResid);
+  m.attr("EPI_RESID_Q8") = static_cast<int>(ewb::kEpiResidQ8);
+  m.attr("EPI_ACC_F32") = static_cast<int>(ewb::kEpiAccF32);
+  m.attr("EPI_DGELU") = static_cast<int>(ewb::kEpiDGelu);
+  m.attr("EPI_F32") = static_cast<int>(ewb::kEpiF32);
+}

@@ -1,0 +1,130 @@
+// Token + learned position embedding, forward and deterministic backward.
+//
+// Reference op: Embed (src/wantrain/model/gpt.py:320-338): x = wte[idx] +
+// wpe[pos], cast to the compute dtype, then the boundary narrowing. Forward
+// reads the fp32 master tables directly and writes either bf16 or the fp8
+// e4m3 1x128 boundary format (the quantisation is this kernel's epilogue).
+//
+// Backward without atomics: one CTA ranks every position by (token, position),
+// so equal tokens form runs in position order; a second kernel gives each run
+// head one CTA that sums the run's rows in that order into the fp32 table
+// gradient. Position gradients sum the batch rows in batch order.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace ewb {
+namespace {
+
+__global__ void __launch_bounds__(128)
+    embed_fwd_kernel(const int64_t* __restrict__ idx, const float* __restrict__ wte,
+                     const float* __restrict__ wpe, int S, int d,
+                     __nv_bfloat16* __restrict__ out_bf16, uint8_t* __restrict__ out_q8,
+                     float* __restrict__ out_scale) {
+  const int t = blockIdx.x;
+  const int64_t tok = idx[t];
+  const int pos = t % S;
+  const float* er = wte + static_cast<size_t>(tok) * d;
+  const float* pr = wpe + static_cast<size_t>(pos) * d;
+  for (int c0 = 0; c0 < d; c0 += 1024) {
+    const int c = c0 + threadIdx.x * 8;
+    float v[8];
+    const bool ok = c < d;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = ok ? er[c + i] + pr[c + i] : 0.f;
+    if (out_q8 != nullptr) {
+      // 16 consecutive threads cover one 128-column block.
+      float amax = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      const float scale = e4m3_block_scale(amax);
+      const float inv = 1.0f / scale;
+      if (ok) {
+        uint32_t w[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(
+              make_float2(v[4 * h] * inv, v[4 * h + 1] * inv), __NV_SATFINITE, __NV_E4M3);
+          const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(
+              make_float2(v[4 * h + 2] * inv, v[4 * h + 3] * inv), __NV_SATFINITE, __NV_E4M3);
+          w[h] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+        }
+        *reinterpret_cast<uint2*>(out_q8 + static_cast<size_t>(t) * d + c) = make_uint2(w[0], w[1]);
+        if ((threadIdx.x & 15) == 0) out_scale[static_cast<size_t>(t) * (d / 128) + c / 128] = scale;
+      }
+    } else if (ok) {
+      uint4 w;
+      w.x = pack_bf16x2(v[0], v[1]);
+      w.y = pack_bf16x2(v[2], v[3]);
+      w.z = pack_bf16x2(v[4], v[5]);
+      w.w = pack_bf16x2(v[6], v[7]);
+      *reinterpret_cast<uint4*>(out_bf16 + static_cast<size_t>(t) * d + c) = w;
+    }
+  }
+}
+
+// order[rank(t)] = t with rank by (token, position); T <= 16384.
+__global__ void __launch_bounds__(1024) embed_rank_kernel(const int64_t* __restrict__ idx, int T,
+                                                          int* __restrict__ order) {
+  extern __shared__ int sidx[];
+  for (int i = threadIdx.x; i < T; i += 1024) sidx[i] = static_cast<int>(idx[i]);
+  __syncthreads();
+  for (int t = threadIdx.x; t < T; t += 1024) {
+    const int v = sidx[t];
+    int r = 0;
+    for (int u = 0; u < T; ++u) {
+      const int w = sidx[u];
+      r += (w < v) || (w == v && u < t);
+    }
+    order[r] = t;
+  }
+}
+
+__global__ void __launch_bounds__(256)
+    embed_wte_bwd_kernel(const int64_t* __restrict__ idx, const __nv_bfloat16* __restrict__ dx,
+                         const int* __restrict__ order, int T, int d, float* __restrict__ dwte) {
+  const int i = blockIdx.x;
+  const int t0 = order[i];
+  const int64_t tok = idx[t0];
+  if (i > 0 && idx[order[i - 1]] == tok) return;  // not a run head
+  int end = i + 1;
+  while (end < T && idx[order[end]] == tok) ++end;
+  float* g = dwte + static_cast<size_t>(tok) * d;
+  for (int c = threadIdx.x; c < d; c += 256) {
+    float s = g[c];
+    for (int k = i; k < end; ++k) s += __bfloat162float(dx[static_cast<size_t>(order[k]) * d + c]);
+    g[c] = s;
+  }
+}
+
+__global__ void __launch_bounds__(256)
+    embed_wpe_bwd_kernel(const __nv_bfloat16* __restrict__ dx, int T, int S, int d,
+                         float* __restrict__ dwpe) {
+  const int s = blockIdx.x;
+  const int nb = T / S;
+  for (int c = threadIdx.x; c < d; c += 256) {
+    float acc = dwpe[static_cast<size_t>(s) * d + c];
+    for (int b = 0; b < nb; ++b) acc += __bfloat162float(dx[(static_cast<size_t>(b) * S + s) * d + c]);
+    dwpe[static_cast<size_t>(s) * d + c] = acc;
+  }
+}
+
+}  // namespace
+
+int embed_fwd(const EmbedArgs& a, cudaStream_t stream) {
+  if (a.d % 8 || (a.out_q8 && a.d % 128) || a.T % a.S) return 1;
+  embed_fwd_kernel<<<a.T, 128, 0, stream>>>(a.idx, a.wte, a.wpe, a.S, a.d, a.out_bf16, a.out_q8,
+                                            a.out_scale);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+int embed_bwd(const EmbedBwdArgs& a, cudaStream_t stream) {
+  if (a.T > 16384 || a.T % a.S) return 1;
+  embed_rank_kernel<<<1, 1024, a.T * sizeof(int), stream>>>(a.idx, a.T, a.order);
+  embed_wte_bwd_kernel<<<a.T, 256, 0, stream>>>(a.idx, a.dx, a.order, a.T, a.d, a.dwte);
+  embed_wpe_bwd_kernel<<<a.S, 256, 0, stream>>>(a.dx, a.T, a.S, a.d, a.dwpe);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+}  // namespace ewb

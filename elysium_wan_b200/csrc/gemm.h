@@ -1,0 +1,61 @@
+// Host-visible interface of the tcgen05 GEMM (gemm.cu). Plain C++: no torch
+// headers, so the launcher can be reached from any host code.
+#pragma once
+
+#include <cuda_runtime.h>
+
+namespace ewb {
+
+enum GemmEpilogueKind : int {
+  kEpiBf16 = 0,     // out bf16 = acc (+ bias)
+  kEpiGelu = 1,     // aux bf16 = acc + bias; out bf16 = gelu(aux)
+  kEpiResid = 2,    // out bf16 = resid + acc (+ bias)            (resid bf16 or fp8+scale)
+  kEpiResidQ8 = 3,  // out e4m3 + 1x128 scales = quant(resid + acc (+ bias))
+  kEpiAccF32 = 4,   // out f32 = (beta != 0 ? out : 0) + acc     (ordered gradient fold)
+  kEpiDGelu = 5,    // out bf16 = acc * gelu'(aux)
+  kEpiF32 = 6,      // out f32 = acc (+ bias)
+};
+
+enum GemmStatus : int {
+  kGemmOk = 0,
+  kGemmErrShape = 1,
+  kGemmErrAlign = 2,
+  kGemmErrTensorMap = 3,
+  kGemmErrLaunch = 4,
+  kGemmErrUnsupported = 5,
+};
+
+struct GemmEpilogue {
+  int kind;
+  void* out;
+  int ldo;
+  const float* bias;  // fp32 [N] or null
+  const void* resid;  // bf16 or e4m3 [M][ldr]
+  int ldr;
+  int resid_fp8;
+  const float* resid_scale;  // [M][ld_resid_scale] when resid_fp8
+  int ld_resid_scale;
+  void* aux;  // bf16 [M][ldaux]
+  int ldaux;
+  float* scale_out;  // [M][ld_scale_out] for kEpiResidQ8
+  int ld_scale_out;
+  float beta;
+};
+
+struct GemmArgs {
+  const void* a;  // bf16
+  int lda;
+  bool a_mn;  // false: A stored [M][lda] (K contiguous); true: [K][lda] (M contiguous)
+  const void* b;
+  int ldb;
+  bool b_mn;  // false: B stored [N][ldb]; true: [K][ldb]
+  int M, N, K;
+  int bn;  // 128 / 256, anything else = pick by wave efficiency
+  GemmEpilogue ep;
+  int* status;  // device status word (may be null)
+};
+
+int gemm_launch(const GemmArgs& args, cudaStream_t stream);
+int gemm_pick_bn(int M, int N);
+
+}  // namespace ewb

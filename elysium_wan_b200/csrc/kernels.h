@@ -1,0 +1,139 @@
+// Host-visible launchers of the non-GEMM kernels. Plain C++ (no torch), so the
+// same entry points serve the Python bindings and any native caller. Every
+// launcher returns 0 on success, 1 for a rejected argument, 2 for a launch
+// error.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ewb {
+
+// ---------------------------------------------------------------- LayerNorm
+struct LnArgs {
+  const void* x;  // bf16 [rows][ldx] or e4m3 [rows][ldx]
+  const float* x_scale;  // e4m3 block scales [rows][ldxs]
+  int x_fp8, ldx, ldxs;
+  const float* gamma;
+  const float* beta;
+  __nv_bfloat16* y;
+  int ldy;
+  float* mean;
+  float* rstd;
+  int rows, d;
+  float eps;
+};
+int layernorm_fwd(const LnArgs& a, cudaStream_t stream);
+
+struct LnBwdArgs {
+  const __nv_bfloat16* dy;
+  int lddy;
+  const void* x;
+  const float* x_scale;
+  int x_fp8, ldx, ldxs;
+  const float* mean;
+  const float* rstd;
+  const float* gamma;
+  const __nv_bfloat16* dres;  // optional residual-stream gradient added to dx
+  int lddres;
+  __nv_bfloat16* dx;
+  int lddx;
+  float* part_g;  // [chunks][d] scratch
+  float* part_b;
+  float* dgamma;  // fp32 gradients, accumulated when `accumulate`
+  float* dbeta;
+  int accumulate;
+  int rows, d, rows_per_chunk;
+};
+int layernorm_bwd(const LnBwdArgs& a, cudaStream_t stream);
+int layernorm_bwd_rows_per_chunk(int rows);
+
+// ---------------------------------------------------------------- attention
+struct AttnArgs {
+  const __nv_bfloat16* qkv;  // [B*S][3d]
+  __nv_bfloat16* o;  // [B*S][d]
+  float* lse;  // [B][H][S] base-2 log-sum-exp
+  int B, S, H, hd, d;
+  float scale;  // softmax scale, 1/sqrt(hd)
+};
+int attention_fwd(const AttnArgs& a, cudaStream_t stream);
+
+struct AttnBwdArgs {
+  const __nv_bfloat16* qkv;
+  const __nv_bfloat16* o;
+  const __nv_bfloat16* dout;
+  const float* lse;
+  float* Dbuf;  // [B][H][S] scratch
+  __nv_bfloat16* dqkv;  // [B*S][3d]
+  int B, S, H, hd, d;
+  float scale;
+};
+int attention_bwd(const AttnBwdArgs& a, cudaStream_t stream);
+
+// ---------------------------------------------------------------- cross-entropy
+// Row-wise softmax cross-entropy over fp32 logits [T][ldl] (V valid columns).
+// Writes loss_rows[T], and when dlogits != null the bf16 gradient
+// (softmax - onehot) * grad_scale into [T][ldg] (pad columns zeroed).
+struct CeArgs {
+  const float* logits;
+  int ldl;
+  const int64_t* targets;
+  int T, V;
+  float* loss_rows;
+  __nv_bfloat16* dlogits;
+  int ldg;
+  float grad_scale;
+};
+int cross_entropy(const CeArgs& a, cudaStream_t stream);
+// out[0] = sum(x[0..n)) / n, fixed-order tree (deterministic).
+int mean_reduce(const float* x, int n, float* out, cudaStream_t stream);
+
+// ---------------------------------------------------------------- embedding
+struct EmbedArgs {
+  const int64_t* idx;  // [B*S]
+  const float* wte;  // [V][d] fp32 master
+  const float* wpe;  // [S][d]
+  int T, S, d;
+  __nv_bfloat16* out_bf16;  // either bf16 out...
+  uint8_t* out_q8;  // ...or e4m3 + 1x128 scales
+  float* out_scale;
+};
+int embed_fwd(const EmbedArgs& a, cudaStream_t stream);
+
+struct EmbedBwdArgs {
+  const int64_t* idx;
+  const __nv_bfloat16* dx;  // [T][d]
+  int T, S, d, V;
+  int* order;  // [T] scratch: positions sorted by (token, position)
+  float* dwte;  // [V][d] fp32 gradient (accumulated)
+  float* dwpe;  // [S][d]
+};
+int embed_bwd(const EmbedBwdArgs& a, cudaStream_t stream);
+
+// ---------------------------------------------------------------- optimizer
+struct AdamWArgs {
+  float* p;  // fp32 master
+  float* m;
+  float* v;
+  const float* g;
+  __nv_bfloat16* p_bf16;  // optional working copy
+  int64_t n;
+  float lr, beta1, beta2, eps, wd;
+  float bc1, bc2;  // 1 - beta^t
+};
+int adamw_step(const AdamWArgs& a, cudaStream_t stream);
+
+// ---------------------------------------------------------------- misc
+// grad[n] (+)= sum_t x[t][n] in row order (bias gradients), deterministic.
+int colsum_bf16(const __nv_bfloat16* x, int T, int N, int ld, float* part, float* grad,
+                int accumulate, cudaStream_t stream);
+int colsum_part_rows(int T);
+// e4m3 with 1x128 power-of-two scales, standalone (tests, boundary tooling).
+int quant_e4m3_rows(const __nv_bfloat16* x, int T, int d, uint8_t* q, float* scale,
+                    cudaStream_t stream);
+int dequant_e4m3_rows(const uint8_t* q, const float* scale, int T, int d, __nv_bfloat16* y,
+                      cudaStream_t stream);
+int cast_f32_bf16(const float* x, __nv_bfloat16* y, int64_t n, cudaStream_t stream);
+
+}  // namespace ewb

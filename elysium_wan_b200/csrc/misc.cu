@@ -1,0 +1,114 @@
+// Small deterministic helpers: bias-gradient column sums, standalone fp8
+// e4m3 1x128 quantise / dequantise, fp32 -> bf16 cast.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace ewb {
+namespace {
+
+constexpr int kColRows = 64;  // rows per partial-sum chunk
+
+__global__ void __launch_bounds__(256)
+    colsum_part_kernel(const __nv_bfloat16* __restrict__ x, int T, int N, int ld,
+                       float* __restrict__ part) {
+  const int n = blockIdx.x * 256 + threadIdx.x;
+  const int chunk = blockIdx.y;
+  if (n >= N) return;
+  const int r0 = chunk * kColRows, r1 = min(T, r0 + kColRows);
+  float s = 0.f;
+  for (int r = r0; r < r1; ++r) s += __bfloat162float(x[static_cast<size_t>(r) * ld + n]);
+  part[static_cast<size_t>(chunk) * N + n] = s;
+}
+
+__global__ void __launch_bounds__(256)
+    colsum_fold_kernel(const float* __restrict__ part, int chunks, int N, float* __restrict__ grad,
+                       int accumulate) {
+  const int n = blockIdx.x * 256 + threadIdx.x;
+  if (n >= N) return;
+  float s = 0.f;
+  for (int k = 0; k < chunks; ++k) s += part[static_cast<size_t>(k) * N + n];
+  grad[n] = accumulate ? grad[n] + s : s;
+}
+
+// One warp per 128-column block of a row.
+__global__ void quant_kernel(const __nv_bfloat16* __restrict__ x, int T, int d,
+                             uint8_t* __restrict__ q, float* __restrict__ scale) {
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int l = threadIdx.x & 31;
+  const int nb = d / 128;
+  if (w >= T * nb) return;
+  const int row = w / nb, blk = w % nb;
+  const __nv_bfloat16* p = x + static_cast<size_t>(row) * d + blk * 128 + 4 * l;
+  float v[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = __bfloat162float(p[i]);
+  float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float s = e4m3_block_scale(amax);
+  const float inv = 1.0f / s;
+  const __nv_fp8x2_storage_t lo =
+      __nv_cvt_float2_to_fp8x2(make_float2(v[0] * inv, v[1] * inv), __NV_SATFINITE, __NV_E4M3);
+  const __nv_fp8x2_storage_t hi =
+      __nv_cvt_float2_to_fp8x2(make_float2(v[2] * inv, v[3] * inv), __NV_SATFINITE, __NV_E4M3);
+  *reinterpret_cast<uint32_t*>(q + static_cast<size_t>(row) * d + blk * 128 + 4 * l) =
+      static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+  if (l == 0) scale[static_cast<size_t>(row) * nb + blk] = s;
+}
+
+__global__ void dequant_kernel(const uint8_t* __restrict__ q, const float* __restrict__ scale,
+                               int64_t n, int d, __nv_bfloat16* __restrict__ y) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int64_t row = i / d;
+  const int col = static_cast<int>(i % d);
+  __nv_fp8_e4m3 v;
+  v.__x = q[i];
+  y[i] = __float2bfloat16_rn(static_cast<float>(v) * scale[row * (d / 128) + col / 128]);
+}
+
+__global__ void cast_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, int64_t n) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
+    y[i] = __float2bfloat16_rn(x[i]);
+}
+
+}  // namespace
+
+int colsum_part_rows(int T) { return (T + kColRows - 1) / kColRows; }
+
+int colsum_bf16(const __nv_bfloat16* x, int T, int N, int ld, float* part, float* grad,
+                int accumulate, cudaStream_t stream) {
+  if (T <= 0 || N <= 0) return 1;
+  const int chunks = colsum_part_rows(T);
+  dim3 g1((N + 255) / 256, chunks);
+  colsum_part_kernel<<<g1, 256, 0, stream>>>(x, T, N, ld, part);
+  colsum_fold_kernel<<<(N + 255) / 256, 256, 0, stream>>>(part, chunks, N, grad, accumulate);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+int quant_e4m3_rows(const __nv_bfloat16* x, int T, int d, uint8_t* q, float* scale,
+                    cudaStream_t stream) {
+  if (d % 128) return 1;
+  const int warps = T * (d / 128);
+  quant_kernel<<<(warps * 32 + 255) / 256, 256, 0, stream>>>(x, T, d, q, scale);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+int dequant_e4m3_rows(const uint8_t* q, const float* scale, int T, int d, __nv_bfloat16* y,
+                      cudaStream_t stream) {
+  if (d % 128) return 1;
+  const int64_t n = static_cast<int64_t>(T) * d;
+  dequant_kernel<<<static_cast<int>((n + 255) / 256), 256, 0, stream>>>(q, scale, n, d, y);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+int cast_f32_bf16(const float* x, __nv_bfloat16* y, int64_t n, cudaStream_t stream) {
+  if (n <= 0) return 0;
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  cast_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(x, y, n);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+}  // namespace ewb

@@ -1,0 +1,271 @@
+// LayerNorm forward / backward for sm_100a (reference op: nn.LayerNorm in
+// src/wantrain/model/gpt.py:346-389,402-415, fp32 statistics under autocast).
+//
+// Forward: one CTA of 128 threads per row; the row is held in registers as
+// fp32 (8 contiguous elements per thread per 1024-column slice), mean and
+// variance are two-pass over the registers with a fixed reduction tree, so the
+// result is deterministic. The input is either bf16 or the fp8 e4m3 boundary
+// format with one power-of-two scale per 128 columns: the dequantisation is the
+// prologue of this kernel (the next stage's first op after a stage cut).
+//
+// Backward: one CTA per chunk of rows. Each thread owns the same columns in
+// every row of its chunk, so dgamma/dbeta partial sums accumulate in registers
+// and are written once per chunk; a second kernel folds the chunk partials in
+// chunk order into the fp32 gradients. No atomics anywhere.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace ewb {
+namespace {
+
+constexpr int kLnThreads = 128;
+constexpr int kLnMaxSlices = 8;  // d <= 8192 (S = ceil(d / 1024) slices per thread)
+
+__device__ __forceinline__ float block_sum_128(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5;
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[w] = v;
+  __syncthreads();
+  return (red[0] + red[1]) + (red[2] + red[3]);
+}
+
+// Load 8 contiguous input elements (bf16 or e4m3 + block scale) as fp32.
+__device__ __forceinline__ void load8(const void* x, const float* xs, int x_fp8, int ld, int lds,
+                                      int row, int col, float* v) {
+  if (x_fp8) {
+    const uint8_t* p = reinterpret_cast<const uint8_t*>(x) + static_cast<size_t>(row) * ld + col;
+    const uint2 raw = *reinterpret_cast<const uint2*>(p);
+    const float s = xs[static_cast<size_t>(row) * lds + (col >> 7)];
+    const uint8_t* b = reinterpret_cast<const uint8_t*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      __nv_fp8_e4m3 q;
+      q.__x = b[i];
+      v[i] = static_cast<float>(q) * s;
+    }
+  } else {
+    const __nv_bfloat16* p =
+        reinterpret_cast<const __nv_bfloat16*>(x) + static_cast<size_t>(row) * ld + col;
+    const uint4 raw = *reinterpret_cast<const uint4*>(p);
+    const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __bfloat162float(b[i]);
+  }
+}
+
+__device__ __forceinline__ void store8_bf16(__nv_bfloat16* p, const float* v) {
+  uint4 w;
+  w.x = pack_bf16x2(v[0], v[1]);
+  w.y = pack_bf16x2(v[2], v[3]);
+  w.z = pack_bf16x2(v[4], v[5]);
+  w.w = pack_bf16x2(v[6], v[7]);
+  *reinterpret_cast<uint4*>(p) = w;
+}
+
+template <int S>
+__global__ void __launch_bounds__(kLnThreads)
+    layernorm_fwd_kernel(const void* __restrict__ x, const float* __restrict__ xs, int x_fp8,
+                         int ldx, int ldxs, const float* __restrict__ gamma,
+                         const float* __restrict__ beta, __nv_bfloat16* __restrict__ y, int ldy,
+                         float* __restrict__ mean_out, float* __restrict__ rstd_out, int d,
+                         float eps) {
+  __shared__ float red[4];
+  const int row = blockIdx.x;
+  float v[S][8];
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < S; ++j) {
+    const int col = j * 1024 + threadIdx.x * 8;
+    if (col < d) {
+      load8(x, xs, x_fp8, ldx, ldxs, row, col, v[j]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s += v[j][i];
+    }
+  }
+  const float mean = block_sum_128(s, red) / static_cast<float>(d);
+  float q = 0.f;
+#pragma unroll
+  for (int j = 0; j < S; ++j) {
+    const int col = j * 1024 + threadIdx.x * 8;
+    if (col < d) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float c = v[j][i] - mean;
+        q += c * c;
+      }
+    }
+  }
+  const float var = block_sum_128(q, red) / static_cast<float>(d);
+  const float rstd = rsqrtf(var + eps);
+#pragma unroll
+  for (int j = 0; j < S; ++j) {
+    const int col = j * 1024 + threadIdx.x * 8;
+    if (col < d) {
+      float o[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = (v[j][i] - mean) * rstd * gamma[col + i] + beta[col + i];
+      store8_bf16(y + static_cast<size_t>(row) * ldy + col, o);
+    }
+  }
+  if (threadIdx.x == 0) {
+    mean_out[row] = mean;
+    rstd_out[row] = rstd;
+  }
+}
+
+// dx = rstd * (g - mean(g) - xhat * mean(g * xhat)) (+ dres), g = dy * gamma.
+// Partial dgamma = sum dy * xhat and dbeta = sum dy over the rows of the chunk.
+template <int S>
+__global__ void __launch_bounds__(kLnThreads)
+    layernorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, int lddy, const void* __restrict__ x,
+                         const float* __restrict__ xs, int x_fp8, int ldx, int ldxs,
+                         const float* __restrict__ mean, const float* __restrict__ rstd,
+                         const float* __restrict__ gamma, const __nv_bfloat16* __restrict__ dres,
+                         int lddres, __nv_bfloat16* __restrict__ dx, int lddx,
+                         float* __restrict__ part_g, float* __restrict__ part_b, int rows, int d,
+                         int rows_per_chunk) {
+  __shared__ float red[4];
+  const int chunk = blockIdx.x;
+  const int r0 = chunk * rows_per_chunk;
+  const int r1 = min(rows, r0 + rows_per_chunk);
+  float pg[S][8];
+  float pb[S][8];
+#pragma unroll
+  for (int j = 0; j < S; ++j)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      pg[j][i] = 0.f;
+      pb[j][i] = 0.f;
+    }
+  for (int row = r0; row < r1; ++row) {
+    const float mu = mean[row];
+    const float rs = rstd[row];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int j = 0; j < S; ++j) {
+      const int col = j * 1024 + threadIdx.x * 8;
+      if (col < d) {
+        float xv[8], dv[8];
+        load8(x, xs, x_fp8, ldx, ldxs, row, col, xv);
+        load8(dy, nullptr, 0, lddy, 0, row, col, dv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float xh = (xv[i] - mu) * rs;
+          const float g = dv[i] * gamma[col + i];
+          s1 += g;
+          s2 += g * xh;
+          pg[j][i] += dv[i] * xh;
+          pb[j][i] += dv[i];
+        }
+      }
+    }
+    const float m1 = block_sum_128(s1, red) / static_cast<float>(d);
+    const float m2 = block_sum_128(s2, red) / static_cast<float>(d);
+    // Second pass re-reads the row (L1/L2 resident) instead of holding it.
+#pragma unroll
+    for (int j = 0; j < S; ++j) {
+      const int col = j * 1024 + threadIdx.x * 8;
+      if (col < d) {
+        float xv[8], dv[8], o[8];
+        load8(x, xs, x_fp8, ldx, ldxs, row, col, xv);
+        load8(dy, nullptr, 0, lddy, 0, row, col, dv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float xh = (xv[i] - mu) * rs;
+          const float g = dv[i] * gamma[col + i];
+          o[i] = rs * (g - m1 - xh * m2);
+        }
+        if (dres != nullptr) {
+          float rv[8];
+          load8(dres, nullptr, 0, lddres, 0, row, col, rv);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) o[i] += rv[i];
+        }
+        store8_bf16(dx + static_cast<size_t>(row) * lddx + col, o);
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < S; ++j) {
+    const int col = j * 1024 + threadIdx.x * 8;
+    if (col < d) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        part_g[static_cast<size_t>(chunk) * d + col + i] = pg[j][i];
+        part_b[static_cast<size_t>(chunk) * d + col + i] = pb[j][i];
+      }
+    }
+  }
+}
+
+// grad[c] (+)= sum over chunks, in chunk order, of part[chunk][c].
+__global__ void fold_partials_kernel(const float* __restrict__ part, int chunks, int d,
+                                     float* __restrict__ grad, int accumulate) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= d) return;
+  float s = 0.f;
+  for (int k = 0; k < chunks; ++k) s += part[static_cast<size_t>(k) * d + c];
+  grad[c] = accumulate ? grad[c] + s : s;
+}
+
+}  // namespace
+
+int layernorm_fwd(const LnArgs& a, cudaStream_t stream) {
+  if (a.d % 8 || a.d > 1024 * kLnMaxSlices || (a.x_fp8 && a.d % 128)) return 1;
+  const int S = (a.d + 1023) / 1024;
+#define EWB_LN_FWD(SS)                                                                         \
+  layernorm_fwd_kernel<SS><<<a.rows, kLnThreads, 0, stream>>>(a.x, a.x_scale, a.x_fp8, a.ldx,  \
+                                                              a.ldxs, a.gamma, a.beta, a.y,    \
+                                                              a.ldy, a.mean, a.rstd, a.d, a.eps)
+  switch (S) {
+    case 1: EWB_LN_FWD(1); break;
+    case 2: EWB_LN_FWD(2); break;
+    case 3: EWB_LN_FWD(3); break;
+    case 4: EWB_LN_FWD(4); break;
+    case 5: EWB_LN_FWD(5); break;
+    case 6: EWB_LN_FWD(6); break;
+    case 7: EWB_LN_FWD(7); break;
+    default: EWB_LN_FWD(8); break;
+  }
+#undef EWB_LN_FWD
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+int layernorm_bwd_rows_per_chunk(int rows) {
+  // Enough chunks to fill the GPU twice, few enough that the fold stays cheap.
+  int rpc = (rows + 295) / 296;
+  return rpc < 1 ? 1 : rpc;
+}
+
+int layernorm_bwd(const LnBwdArgs& a, cudaStream_t stream) {
+  if (a.d % 8 || a.d > 1024 * kLnMaxSlices || (a.x_fp8 && a.d % 128)) return 1;
+  const int rpc = a.rows_per_chunk;
+  const int chunks = (a.rows + rpc - 1) / rpc;
+  const int S = (a.d + 1023) / 1024;
+#define EWB_LN_BWD(SS)                                                                      \
+  layernorm_bwd_kernel<SS><<<chunks, kLnThreads, 0, stream>>>(                              \
+      a.dy, a.lddy, a.x, a.x_scale, a.x_fp8, a.ldx, a.ldxs, a.mean, a.rstd, a.gamma, a.dres, \
+      a.lddres, a.dx, a.lddx, a.part_g, a.part_b, a.rows, a.d, rpc)
+  switch (S) {
+    case 1: EWB_LN_BWD(1); break;
+    case 2: EWB_LN_BWD(2); break;
+    case 3: EWB_LN_BWD(3); break;
+    case 4: EWB_LN_BWD(4); break;
+    case 5: EWB_LN_BWD(5); break;
+    case 6: EWB_LN_BWD(6); break;
+    case 7: EWB_LN_BWD(7); break;
+    default: EWB_LN_BWD(8); break;
+  }
+#undef EWB_LN_BWD
+  if (cudaGetLastError() != cudaSuccess) return 2;
+  const int tb = 256;
+  fold_partials_kernel<<<(a.d + tb - 1) / tb, tb, 0, stream>>>(a.part_g, chunks, a.d, a.dgamma,
+                                                               a.accumulate);
+  fold_partials_kernel<<<(a.d + tb - 1) / tb, tb, 0, stream>>>(a.part_b, chunks, a.d, a.dbeta,
+                                                               a.accumulate);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+}  // namespace ewb

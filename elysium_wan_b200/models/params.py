@@ -1,0 +1,119 @@
+"""Flat parameter store of one stage.
+
+All parameters of a stage live in one contiguous fp32 master buffer (each
+tensor starts on a 256-byte boundary so any view can be a TMA operand), with a
+matching fp32 gradient buffer and, on the GPU, a bf16 working copy that the
+GEMMs read. One flat buffer per stage makes the optimizer one kernel, a ZeRO-1
+shard one contiguous slice, and a checkpoint one tensor.
+
+The reference keeps fp32 nn.Parameters and casts them to bf16 per use under
+autocast (src/wantrain/model/wgrad.py:257-265; 31% of block F time on H100 per
+benchmarks/wan/runs/2026-10-13-h100/REPORT.md:116-121); here the cast happens
+once per step, fused into the AdamW kernel.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+ALIGN = 64  # elements (256 bytes of fp32)
+
+
+@dataclass
+class ParamSpec:
+    name: str
+    shape: tuple
+    init: str  # "normal" | "normal_resid" | "embed" | "bias" | "zeros" | "ones"
+    fan_in: int = 1
+    matrix: bool = False  # read by a GEMM (needs the bf16 working copy)
+
+
+class ParamStore:
+    def __init__(self, specs: list[ParamSpec], device: torch.device, work_dtype=None):
+        self.specs = list(specs)
+        self.device = torch.device(device)
+        self.index: dict[str, tuple[int, tuple]] = {}
+        off = 0
+        for s in self.specs:
+            self.index[s.name] = (off, tuple(s.shape))
+            n = math.prod(s.shape)
+            off += (n + ALIGN - 1) // ALIGN * ALIGN
+        self.numel = max(off, ALIGN)
+        self.master = torch.zeros(self.numel, dtype=torch.float32, device=self.device)
+        self.grad = torch.zeros(self.numel, dtype=torch.float32, device=self.device)
+        self.work_dtype = work_dtype
+        self.work = (torch.zeros(self.numel, dtype=work_dtype, device=self.device)
+                     if work_dtype is not None else None)
+
+    def names(self) -> list[str]:
+        return [s.name for s in self.specs]
+
+    def _view(self, buf, name):
+        off, shape = self.index[name]
+        return buf[off: off + math.prod(shape)].view(shape)
+
+    def p(self, name):
+        """fp32 master view."""
+        return self._view(self.master, name)
+
+    def w(self, name):
+        """Compute-dtype view (bf16 working copy on the GPU, the master on CPU)."""
+        return self._view(self.work if self.work is not None else self.master, name)
+
+    def g(self, name):
+        return self._view(self.grad, name)
+
+    def zero_grad(self):
+        self.grad.zero_()
+
+    def sync_work(self):
+        if self.work is not None:
+            if self.master.is_cuda:
+                from elysium_wan_b200 import ops
+
+                ops.ext().cast_bf16(self.master, self.work)
+            else:
+                self.work.copy_(self.master)
+
+    def state_dict(self) -> dict:
+        return {name: self.p(name).detach().cpu().clone() for name in self.names()}
+
+    def load_state_dict(self, sd: dict):
+        for name in self.names():
+            self.p(name).copy_(sd[name].to(self.device))
+        self.sync_work()
+
+
+def init_params(store: ParamStore, seed: int, entry_of: dict, std: float, n_layer: int,
+                scheme: str = "gpt2"):
+    """Deterministic init: parameter j of entry e draws from its own generator
+    seeded by (seed, e, j), so a stage initialises only its own slice and gets
+    the same values as the single-device oracle on the same device type."""
+    dev = store.device
+    per_entry_count: dict[int, int] = {}
+    for s in store.specs:
+        e = entry_of[s.name]
+        j = per_entry_count.get(e, 0)
+        per_entry_count[e] = j + 1
+        gen = torch.Generator(device=dev)
+        gen.manual_seed((seed * 1_000_003 + e * 7919 + j) % (2**63 - 1))
+        v = store.p(s.name)
+        if s.init == "zeros":
+            v.zero_()
+        elif s.init == "ones":
+            v.fill_(1.0)
+        elif scheme == "torch_default":
+            if s.init == "embed":
+                v.copy_(torch.randn(s.shape, generator=gen, device=dev))
+            else:  # nn.Linear weight and bias: U(-1/sqrt(fan_in), 1/sqrt(fan_in))
+                b = 1.0 / math.sqrt(max(1, s.fan_in))
+                v.copy_(torch.rand(s.shape, generator=gen, device=dev) * (2 * b) - b)
+        elif s.init == "bias":
+            v.zero_()
+        else:  # gpt2: N(0, std), residual projections scaled by 1/sqrt(2 n_layer)
+            sd = std / math.sqrt(2.0 * n_layer) if s.init == "normal_resid" else std
+            v.copy_(torch.randn(s.shape, generator=gen, device=dev) * sd)
+    store.sync_work()

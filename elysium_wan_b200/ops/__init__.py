@@ -1,0 +1,343 @@
+"""Hot ops of the framework, one function per op, no autograd.
+
+CUDA tensors run the hand-written sm_100a kernels of ``elysium_wan_b200._C``
+(tcgen05 GEMM with fused epilogues, attention, LayerNorm, cross-entropy,
+embedding, AdamW, fp8 boundary quantisation). CPU tensors run a plain fp32
+torch restatement of the same math; that path serves the CPU/gloo plumbing
+configuration and is the oracle of the kernel tests.
+
+Reference ops being replaced (all PyTorch library calls in the reference):
+``F.linear``/``SplitLinear`` (src/wantrain/model/wgrad.py:193-265),
+``nn.LayerNorm`` and SDPA (src/wantrain/model/gpt.py:346-418),
+``F.cross_entropy`` (gpt.py:556), ``torch.optim.AdamW``
+(src/wantrain/runtime/optim.py:45), the fp8 boundary (src/wantrain/model/fp8.py).
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+from ._ext import ext, launch_count  # noqa: F401
+
+E4M3 = torch.float8_e4m3fn
+
+# Epilogue kinds of the GEMM (mirrors csrc/gemm.h).
+EPI_BF16, EPI_GELU, EPI_RESID, EPI_RESID_Q8, EPI_ACC_F32, EPI_DGELU, EPI_F32 = range(7)
+
+
+def _cuda(t: torch.Tensor) -> bool:
+    return t.is_cuda
+
+
+# ----------------------------------------------------------------------------- fp8 boundary
+def e4m3_block_scale_ref(amax: torch.Tensor) -> torch.Tensor:
+    """Power-of-two scale 2^(e-8) with amax = f * 2^e, f in [0.5, 1); 1 where amax == 0."""
+    _, e = torch.frexp(amax)
+    s = torch.ldexp(torch.ones_like(amax), e - 8)
+    return torch.where(amax > 0, s, torch.ones_like(amax))
+
+
+def quant_e4m3(x: torch.Tensor):
+    """1x128 block-scaled e4m3: returns (q [T,d] e4m3, scale [T,d/128] fp32)."""
+    T, d = x.shape
+    assert d % 128 == 0, "fp8 boundary needs d_model % 128 == 0"
+    if _cuda(x):
+        q = torch.empty((T, d), dtype=E4M3, device=x.device)
+        s = torch.empty((T, d // 128), dtype=torch.float32, device=x.device)
+        ext().quant_e4m3(x.contiguous(), q, s)
+        return q, s
+    xf = x.float().view(T, d // 128, 128)
+    s = e4m3_block_scale_ref(xf.abs().amax(dim=2))
+    q = (xf / s[..., None]).clamp(-448, 448).to(E4M3).view(T, d)
+    return q, s
+
+
+def dequant_e4m3(q: torch.Tensor, s: torch.Tensor, dtype=torch.bfloat16) -> torch.Tensor:
+    T, d = q.shape
+    if _cuda(q) and dtype == torch.bfloat16:
+        y = torch.empty((T, d), dtype=torch.bfloat16, device=q.device)
+        ext().dequant_e4m3(q.contiguous(), s.contiguous(), y)
+        return y
+    return (q.float().view(T, d // 128, 128) * s[..., None]).view(T, d).to(dtype)
+
+
+# ----------------------------------------------------------------------------- GEMM
+def gemm(a, b, out, epi=EPI_BF16, *, a_mn=False, b_mn=False, bias=None, resid=None,
+         resid_scale=None, aux=None, scale_out=None, beta=0.0, bn=0):
+    """out[m, n] (epi)= sum_k A[m, k] B[n, k] on the tcgen05 kernel (CUDA only).
+
+    A is [M, K] (a_mn=False) or stored transposed [K, M]; B is [N, K] or [K, N].
+    """
+    ext().gemm(a, a_mn, b, b_mn, out, epi, bias, resid, resid_scale, aux, scale_out, float(beta),
+               int(bn))
+    return out
+
+
+def _resid_value(resid, resid_scale):
+    if resid.dtype == E4M3:
+        return dequant_e4m3(resid, resid_scale, torch.float32)
+    return resid.float()
+
+
+def linear_fwd(x, w, bias=None, *, epi="none", resid=None, resid_scale=None, out=None):
+    """Y = X W^T (+ b) with a fused epilogue.
+
+    epi: "none" -> Y; "gelu" -> (gelu(U), U) with U = XW^T+b kept for the
+    backward; "resid" -> resid + XW^T + b; "resid_q8" -> e4m3 + scales of that.
+    """
+    T = x.shape[0]
+    N = w.shape[0]
+    if _cuda(x):
+        dev = x.device
+        if epi == "none":
+            out = out if out is not None else torch.empty((T, N), dtype=torch.bfloat16, device=dev)
+            return gemm(x, w, out, EPI_BF16, bias=bias)
+        if epi == "gelu":
+            u = torch.empty((T, N), dtype=torch.bfloat16, device=dev)
+            g = out if out is not None else torch.empty((T, N), dtype=torch.bfloat16, device=dev)
+            gemm(x, w, g, EPI_GELU, bias=bias, aux=u)
+            return g, u
+        if epi == "resid":
+            out = out if out is not None else torch.empty((T, N), dtype=torch.bfloat16, device=dev)
+            return gemm(x, w, out, EPI_RESID, bias=bias, resid=resid, resid_scale=resid_scale)
+        if epi == "resid_q8":
+            q = torch.empty((T, N), dtype=E4M3, device=dev)
+            s = torch.empty((T, N // 128), dtype=torch.float32, device=dev)
+            gemm(x, w, q, EPI_RESID_Q8, bias=bias, resid=resid, resid_scale=resid_scale,
+                 scale_out=s)
+            return q, s
+        if epi == "f32":
+            out = out if out is not None else torch.empty((T, N), dtype=torch.float32, device=dev)
+            return gemm(x, w, out, EPI_F32, bias=bias)
+        raise ValueError(epi)
+    # CPU restatement (fp32)
+    y = x.float() @ w.float().t()
+    if bias is not None:
+        y = y + bias.float()
+    if epi == "none" or epi == "f32":
+        return y.to(x.dtype) if epi == "none" else y
+    if epi == "gelu":
+        return F.gelu(y), y
+    if epi == "resid":
+        return _resid_value(resid, resid_scale) + y
+    if epi == "resid_q8":
+        return quant_e4m3(_resid_value(resid, resid_scale) + y)
+    raise ValueError(epi)
+
+
+def linear_dx(dy, w, *, gelu_u=None, out=None):
+    """dX = dY W (B pass); with gelu_u, returns dY W * gelu'(u) (fc1's input grad of GELU)."""
+    T = dy.shape[0]
+    K = w.shape[1]
+    if _cuda(dy):
+        out = out if out is not None else torch.empty((T, K), dtype=torch.bfloat16, device=dy.device)
+        if gelu_u is not None:
+            return gemm(dy, w, out, EPI_DGELU, b_mn=True, aux=gelu_u)
+        return gemm(dy, w, out, EPI_BF16, b_mn=True)
+    g = dy.float() @ w.float()
+    if gelu_u is not None:
+        u = gelu_u.float()
+        cdf = 0.5 * (1.0 + torch.erf(u * (1.0 / math.sqrt(2.0))))
+        pdf = torch.exp(-0.5 * u * u) / math.sqrt(2.0 * math.pi)
+        g = g * (cdf + u * pdf)
+    return g
+
+
+def linear_dw(dy, x, grad, accumulate: bool):
+    """grad (+)= dY^T X (W pass): the deferred weight gradient, folded in call order."""
+    if _cuda(dy):
+        return gemm(dy, x, grad, EPI_ACC_F32, a_mn=True, b_mn=True,
+                    beta=1.0 if accumulate else 0.0)
+    g = dy.float().t() @ x.float()
+    if accumulate:
+        grad.add_(g)
+    else:
+        grad.copy_(g)
+    return grad
+
+
+def colsum(x, grad, accumulate: bool):
+    """grad (+)= sum over rows of x (bias gradients), fixed order."""
+    if _cuda(x):
+        part = torch.empty((ext().colsum_chunks(x.shape[0]), x.shape[1]), dtype=torch.float32,
+                           device=x.device)
+        ext().colsum(x, part, grad, accumulate)
+        return grad
+    s = x.float().sum(0)
+    if accumulate:
+        grad.add_(s)
+    else:
+        grad.copy_(s)
+    return grad
+
+
+# ----------------------------------------------------------------------------- LayerNorm
+def layernorm_fwd(x, x_scale, gamma, beta, eps=1e-5):
+    """Returns (y bf16/fp32, mean, rstd). x may be e4m3 with 1x128 scales (dequant prologue)."""
+    T, d = x.shape
+    if _cuda(x):
+        y = torch.empty((T, d), dtype=torch.bfloat16, device=x.device)
+        mean = torch.empty(T, dtype=torch.float32, device=x.device)
+        rstd = torch.empty(T, dtype=torch.float32, device=x.device)
+        ext().layernorm_fwd(x, x_scale, gamma, beta, y, mean, rstd, eps)
+        return y, mean, rstd
+    xf = _resid_value(x, x_scale)
+    mean = xf.mean(dim=1)
+    var = ((xf - mean[:, None]) ** 2).mean(dim=1)
+    rstd = torch.rsqrt(var + eps)
+    y = (xf - mean[:, None]) * rstd[:, None] * gamma + beta
+    return y, mean, rstd
+
+
+def layernorm_bwd(dy, x, x_scale, mean, rstd, gamma, dres, dgamma, dbeta, accumulate: bool):
+    """dx (+ dres); dgamma/dbeta (+)= their row sums (fixed order)."""
+    T, d = x.shape
+    if _cuda(x):
+        dx = torch.empty((T, d), dtype=torch.bfloat16, device=x.device)
+        chunks = ext().layernorm_bwd_chunks(T)
+        pg = torch.empty((chunks, d), dtype=torch.float32, device=x.device)
+        pb = torch.empty((chunks, d), dtype=torch.float32, device=x.device)
+        ext().layernorm_bwd(dy, x, x_scale, mean, rstd, gamma, dres, dx, pg, pb, dgamma, dbeta,
+                            accumulate)
+        return dx
+    xf = _resid_value(x, x_scale)
+    xh = (xf - mean[:, None]) * rstd[:, None]
+    dyf = dy.float()
+    g = dyf * gamma
+    dx = rstd[:, None] * (g - g.mean(1, keepdim=True) - xh * (g * xh).mean(1, keepdim=True))
+    if dres is not None:
+        dx = dx + dres.float()
+    pg, pb = (dyf * xh).sum(0), dyf.sum(0)
+    if accumulate:
+        dgamma.add_(pg)
+        dbeta.add_(pb)
+    else:
+        dgamma.copy_(pg)
+        dbeta.copy_(pb)
+    return dx
+
+
+# ----------------------------------------------------------------------------- attention
+def attention_fwd(qkv, B, S, H, hd):
+    """Causal attention on the fused qkv buffer [B*S, 3*H*hd] -> (o [B*S, H*hd], lse)."""
+    d = H * hd
+    scale = 1.0 / math.sqrt(hd)
+    if _cuda(qkv):
+        o = torch.empty((B * S, d), dtype=torch.bfloat16, device=qkv.device)
+        lse = torch.empty((B, H, S), dtype=torch.float32, device=qkv.device)
+        ext().attention_fwd(qkv, o, lse, B, S, H, hd, scale)
+        return o, lse
+    q, k, v = qkv.float().view(B, S, 3, H, hd).permute(2, 0, 3, 1, 4)
+    att = (q @ k.transpose(-2, -1)) * scale
+    mask = torch.triu(torch.ones(S, S, dtype=torch.bool), 1)
+    att = att.masked_fill(mask, float("-inf"))
+    lse = torch.logsumexp(att, dim=-1) * (1.0 / math.log(2.0))
+    o = (torch.softmax(att, dim=-1) @ v).transpose(1, 2).reshape(B * S, d)
+    return o, lse
+
+
+def attention_bwd(qkv, o, dout, lse, B, S, H, hd):
+    """Gradient of causal attention w.r.t. the fused qkv buffer."""
+    d = H * hd
+    scale = 1.0 / math.sqrt(hd)
+    if _cuda(qkv):
+        dqkv = torch.empty_like(qkv)
+        D = torch.empty((B, H, S), dtype=torch.float32, device=qkv.device)
+        ext().attention_bwd(qkv, o, dout, lse, D, dqkv, B, S, H, hd, scale)
+        return dqkv
+    q, k, v = qkv.float().view(B, S, 3, H, hd).permute(2, 0, 3, 1, 4)
+    do = dout.float().view(B, S, H, hd).transpose(1, 2)
+    att = (q @ k.transpose(-2, -1)) * scale
+    mask = torch.triu(torch.ones(S, S, dtype=torch.bool), 1)
+    p = torch.softmax(att.masked_fill(mask, float("-inf")), dim=-1)
+    dv = p.transpose(-2, -1) @ do
+    dp = do @ v.transpose(-2, -1)
+    ds = p * (dp - (dp * p).sum(-1, keepdim=True))
+    dq = ds @ k * scale
+    dk = ds.transpose(-2, -1) @ q * scale
+    out = torch.stack([dq, dk, dv], dim=0).permute(1, 3, 0, 2, 4).reshape(B * S, 3 * d)
+    return out
+
+
+# ----------------------------------------------------------------------------- cross-entropy
+def cross_entropy(logits, V, targets, grad_scale, want_grad=True, ld_grad=None):
+    """Mean CE over rows of fp32 logits; returns (loss scalar tensor, dlogits or None).
+
+    dlogits = (softmax - onehot) * grad_scale, bf16 with row length ld_grad
+    (a multiple of 8 so it can feed TMA), pad columns zero.
+    """
+    T = logits.shape[0]
+    if _cuda(logits):
+        rows = torch.empty(T, dtype=torch.float32, device=logits.device)
+        dl = None
+        if want_grad:
+            ldg = ld_grad or ((V + 7) // 8) * 8
+            dl = torch.empty((T, ldg), dtype=torch.bfloat16, device=logits.device)
+        ext().cross_entropy(logits, V, targets, rows, dl, grad_scale)
+        loss = torch.empty(1, dtype=torch.float32, device=logits.device)
+        ext().mean_reduce(rows, loss)
+        return loss[0], dl
+    lg = logits[:, :V].float()
+    loss = F.cross_entropy(lg, targets)
+    dl = None
+    if want_grad:
+        p = torch.softmax(lg, dim=-1)
+        p[torch.arange(T), targets] -= 1.0
+        dl = p * grad_scale
+    return loss, dl
+
+
+# ----------------------------------------------------------------------------- embedding
+def embed_fwd(idx, wte, wpe, S, fp8: bool, out_dtype=torch.bfloat16):
+    """x = wte[idx] + wpe[pos]; bf16, or (e4m3, scales) when fp8."""
+    T = idx.numel()
+    d = wte.shape[1]
+    if _cuda(idx):
+        if fp8:
+            q = torch.empty((T, d), dtype=E4M3, device=idx.device)
+            s = torch.empty((T, d // 128), dtype=torch.float32, device=idx.device)
+            ext().embed_fwd(idx, wte, wpe, S, None, q, s)
+            return q, s
+        x = torch.empty((T, d), dtype=torch.bfloat16, device=idx.device)
+        ext().embed_fwd(idx, wte, wpe, S, x, None, None)
+        return x
+    flat = idx.reshape(-1)
+    pos = torch.arange(T) % S
+    x = wte[flat] + wpe[pos]
+    if fp8:
+        return quant_e4m3(x)
+    return x.to(out_dtype)
+
+
+def embed_bwd(idx, dx, S, dwte, dwpe):
+    """dwte[tok] += rows of dx in position order; dwpe[s] += rows in batch order."""
+    if _cuda(idx):
+        order = torch.empty(idx.numel(), dtype=torch.int32, device=idx.device)
+        ext().embed_bwd(idx.reshape(-1), dx, S, order, dwte, dwpe)
+        return
+    flat = idx.reshape(-1)
+    T = flat.numel()
+    dxf = dx.float()
+    dwte.index_add_(0, flat, dxf)
+    dwpe.add_(dxf.view(T // S, S, -1).sum(0))
+
+
+# ----------------------------------------------------------------------------- AdamW
+def adamw(p, m, v, g, p_bf16, lr, b1, b2, eps, wd, step):
+    """One AdamW step on flat fp32 state (torch AdamW update order)."""
+    if _cuda(p):
+        ext().adamw(p, m, v, g, p_bf16, lr, b1, b2, eps, wd, step)
+        return
+    bc1 = 1.0 - b1 ** step
+    bc2 = 1.0 - b2 ** step
+    m.mul_(b1).add_(g, alpha=1.0 - b1)
+    v.mul_(b2).addcmul_(g, g, value=1.0 - b2)
+    if wd != 0.0:
+        p.mul_(1.0 - lr * wd)
+    denom = (v.sqrt() / math.sqrt(bc2)).add_(eps)
+    p.addcdiv_(m, denom, value=-lr / bc1)
+    if p_bf16 is not None:
+        p_bf16.copy_(p)

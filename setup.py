@@ -1,0 +1,46 @@
+"""Build of the in-tree sm_100a extension `elysium_wan_b200._C`.
+
+    python setup.py build_ext --inplace
+
+Every CUDA source is compiled for sm_100a only (-gencode arch=compute_100a,
+code=sm_100a); passing -gencode makes torch's extension builder skip its own
+architecture list.
+"""
+
+import os
+
+from setuptools import setup
+from torch.utils.cpp_extension import BuildExtension, CUDAExtension
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+# The image's default CC/CXX wrapper links libstdc++ statically into shared
+# objects; a static libstdc++ inside a torch extension crashes the first time
+# it formats a number (any error message). Use the system compilers, which
+# link the process-wide libstdc++.so.6.
+for var, path in (("CC", "/usr/bin/gcc"), ("CXX", "/usr/bin/g++")):
+    if os.path.exists(path):
+        os.environ[var] = path
+CSRC = os.path.join("elysium_wan_b200", "csrc")
+CU = ["gemm.cu", "norm.cu", "attention.cu", "ce.cu", "embed.cu", "optim.cu", "misc.cu"]
+
+NVCC = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-O3", "-std=c++17", "-lineinfo",
+    "--expt-relaxed-constexpr",
+    "-U__CUDA_NO_HALF_OPERATORS__", "-U__CUDA_NO_HALF_CONVERSIONS__",
+    "-U__CUDA_NO_BFLOAT16_CONVERSIONS__", "-U__CUDA_NO_BFLOAT16_OPERATORS__",
+]
+
+setup(
+    name="elysium_wan_b200",
+    ext_modules=[
+        CUDAExtension(
+            name="elysium_wan_b200._C",
+            sources=[os.path.join(CSRC, "bindings.cpp")] + [os.path.join(CSRC, f) for f in CU],
+            include_dirs=[os.path.join(HERE, CSRC)],
+            extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC},
+        )
+    ],
+    cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+)

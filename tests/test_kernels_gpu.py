@@ -1,0 +1,246 @@
+"""Numerics of every sm_100a kernel against a plain fp32 PyTorch reference.
+
+Would fail if: a tcgen05 descriptor, TMA box or epilogue of the GEMM were
+wrong for any operand layout or tile tail; attention, LayerNorm, CE,
+embedding, AdamW or the fp8 boundary diverged from their definitions; or a
+kernel were not bitwise reproducible run to run.
+"""
+
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from elysium_wan_b200 import ops
+
+pytestmark = pytest.mark.gpu
+
+
+def rel_err(a, b):
+    a = a.float()
+    b = b.float()
+    return ((a - b).norm() / (b.norm() + 1e-12)).item()
+
+
+def bf(*shape, dev, scale=1.0):
+    return (torch.randn(*shape, device=dev) * scale).to(torch.bfloat16)
+
+
+GEMM_SHAPES = [(256, 512, 256), (128, 256, 64), (384, 640, 1024), (200, 264, 200), (1000, 1536, 512)]
+
+
+@pytest.mark.parametrize("M,N,K", GEMM_SHAPES)
+@pytest.mark.parametrize("bn", [128, 256])
+def test_gemm_forward_layouts(cuda, M, N, K, bn):
+    torch.manual_seed(0)
+    x = bf(M, K, dev=cuda)
+    w = bf(N, K, dev=cuda)
+    ref = x.float() @ w.float().t()
+    out = torch.empty(M, N, dtype=torch.float32, device=cuda)
+    ops.gemm(x, w, out, ops.EPI_F32, bn=bn)
+    assert rel_err(out, ref) < 1e-5
+    # dX layout: B stored [K, N] (MN-major)
+    wt = w.t().contiguous()  # [K, N]
+    out2 = torch.empty(M, N, dtype=torch.float32, device=cuda)
+    ops.gemm(x, wt, out2, ops.EPI_F32, b_mn=True, bn=bn)
+    assert rel_err(out2, ref) < 1e-5
+    # dW layout: A stored [K, M], B stored [K, N]
+    xt = x.t().contiguous()
+    out3 = torch.empty(M, N, dtype=torch.float32, device=cuda)
+    ops.gemm(xt, wt, out3, ops.EPI_ACC_F32, a_mn=True, b_mn=True, beta=0.0, bn=bn)
+    assert rel_err(out3, ref) < 1e-5
+    ops.gemm(xt, wt, out3, ops.EPI_ACC_F32, a_mn=True, b_mn=True, beta=1.0, bn=bn)
+    assert rel_err(out3, 2 * ref) < 1e-5
+
+
+def test_gemm_epilogues(cuda):
+    torch.manual_seed(1)
+    M, N, K = 512, 768, 384
+    x = bf(M, K, dev=cuda)
+    w = bf(N, K, dev=cuda, scale=0.05)
+    b = torch.randn(N, device=cuda)
+    acc = x.float() @ w.float().t() + b
+    y = ops.linear_fwd(x, w, b)
+    assert rel_err(y, acc) < 8e-3
+    g, u = ops.linear_fwd(x, w, b, epi="gelu")
+    assert rel_err(u, acc) < 8e-3
+    assert rel_err(g, F.gelu(u.float())) < 8e-3
+    r = bf(M, N, dev=cuda)
+    y = ops.linear_fwd(x, w, b, epi="resid", resid=r)
+    assert rel_err(y, acc + r.float()) < 8e-3
+    q, s = ops.linear_fwd(x, w, b, epi="resid_q8", resid=r)
+    deq = ops.dequant_e4m3(q, s, torch.float32)
+    assert rel_err(deq, acc + r.float()) < 6e-2
+    qr, sr = ops.quant_e4m3((acc + r.float()).to(torch.bfloat16))
+    # same scales as quantising the bf16-free fp32 sum up to bf16 rounding of the input
+    assert (sr == s).float().mean().item() > 0.95
+    # fp8 residual input
+    y2 = ops.linear_fwd(x, w, b, epi="resid", resid=q, resid_scale=s)
+    assert rel_err(y2, acc + deq) < 8e-3
+    # dgelu epilogue: acc * gelu'(u)
+    dy = bf(M, N, dev=cuda)
+    wn = bf(N, K, dev=cuda, scale=0.05)  # dX = dY W with W [N, K]
+    dx = ops.linear_dx(dy, wn)
+    assert rel_err(dx, dy.float() @ wn.float()) < 8e-3
+    uu = bf(M, K, dev=cuda)
+    dg = ops.linear_dx(dy, wn, gelu_u=uu)
+    uf = uu.float()
+    gp = 0.5 * (1 + torch.erf(uf / math.sqrt(2))) + uf * torch.exp(-0.5 * uf * uf) / math.sqrt(2 * math.pi)
+    assert rel_err(dg, (dy.float() @ wn.float()) * gp) < 8e-3
+
+
+def test_gemm_weight_grad_fold_and_determinism(cuda):
+    torch.manual_seed(2)
+    T, N, K = 2048, 1536, 512
+    dys = [bf(T, N, dev=cuda) for _ in range(3)]
+    xs = [bf(T, K, dev=cuda) for _ in range(3)]
+    grad = torch.empty(N, K, device=cuda)
+    for i, (dy, x) in enumerate(zip(dys, xs)):
+        ops.linear_dw(dy, x, grad, accumulate=i > 0)
+    ref = sum(dy.float().t() @ x.float() for dy, x in zip(dys, xs))
+    assert rel_err(grad, ref) < 1e-5
+    grad2 = torch.empty_like(grad)
+    for i, (dy, x) in enumerate(zip(dys, xs)):
+        ops.linear_dw(dy, x, grad2, accumulate=i > 0)
+    assert torch.equal(grad, grad2)
+
+
+def test_gemm_vocab_tail(cuda):
+    torch.manual_seed(3)
+    T, V, d = 256, 50257, 256
+    x = bf(T, d, dev=cuda)
+    w = bf(V, d, dev=cuda, scale=0.05)
+    ld = ((V + 7) // 8) * 8
+    logits = torch.empty(T, ld, device=cuda)[:, :V]
+    ops.gemm(x, w, logits, ops.EPI_F32)
+    assert rel_err(logits, x.float() @ w.float().t()) < 1e-5
+
+
+@pytest.mark.parametrize("d", [256, 1536, 5120])
+@pytest.mark.parametrize("fp8", [False, True])
+def test_layernorm(cuda, d, fp8):
+    torch.manual_seed(4)
+    T = 300
+    x = bf(T, d, dev=cuda, scale=3.0)
+    xs = None
+    xin = x
+    if fp8:
+        xin, xs = ops.quant_e4m3(x)
+        xf = ops.dequant_e4m3(xin, xs, torch.float32)
+    else:
+        xf = x.float()
+    gamma = torch.randn(d, device=cuda)
+    beta = torch.randn(d, device=cuda)
+    y, mean, rstd = ops.layernorm_fwd(xin, xs, gamma, beta)
+    ref = F.layer_norm(xf, (d,), gamma, beta, 1e-5)
+    assert rel_err(y, ref) < 8e-3
+    # backward vs autograd
+    xr = xf.clone().requires_grad_(True)
+    g_ = gamma.clone().requires_grad_(True)
+    b_ = beta.clone().requires_grad_(True)
+    out = F.layer_norm(xr, (d,), g_, b_, 1e-5)
+    dy = bf(T, d, dev=cuda)
+    dres = bf(T, d, dev=cuda)
+    out.backward(dy.float())
+    dg = torch.zeros(d, device=cuda)
+    db = torch.zeros(d, device=cuda)
+    dx = ops.layernorm_bwd(dy, xin, xs, mean, rstd, gamma, dres, dg, db, accumulate=True)
+    assert rel_err(dx, xr.grad + dres.float()) < 1e-2
+    assert rel_err(dg, g_.grad) < 1e-4
+    assert rel_err(db, b_.grad) < 1e-4
+
+
+@pytest.mark.parametrize("hd", [64, 80, 128])
+def test_attention(cuda, hd):
+    torch.manual_seed(5)
+    B, S, H = 2, 256, 3
+    d = H * hd
+    qkv = bf(B * S, 3 * d, dev=cuda)
+    o, lse = ops.attention_fwd(qkv, B, S, H, hd)
+    q, k, v = qkv.float().view(B, S, 3, H, hd).permute(2, 0, 3, 1, 4)
+    qr, kr, vr = (t.clone().requires_grad_(True) for t in (q, k, v))
+    ref = F.scaled_dot_product_attention(qr, kr, vr, is_causal=True)
+    ref_o = ref.transpose(1, 2).reshape(B * S, d)
+    assert rel_err(o, ref_o) < 1e-2
+    att = (q @ k.transpose(-2, -1)) / math.sqrt(hd)
+    att = att.masked_fill(torch.triu(torch.ones(S, S, dtype=torch.bool, device=cuda), 1), float("-inf"))
+    assert rel_err(lse, torch.logsumexp(att, -1) / math.log(2)) < 1e-5
+    dout = bf(B * S, d, dev=cuda)
+    ref.backward(dout.float().view(B, S, H, hd).transpose(1, 2))
+    dqkv = ops.attention_bwd(qkv, o, dout, lse, B, S, H, hd)
+    dq, dk, dv = dqkv.float().view(B, S, 3, H, hd).permute(2, 0, 3, 1, 4)
+    assert rel_err(dq, qr.grad) < 2e-2
+    assert rel_err(dk, kr.grad) < 2e-2
+    assert rel_err(dv, vr.grad) < 2e-2
+    dqkv2 = ops.attention_bwd(qkv, o, dout, lse, B, S, H, hd)
+    assert torch.equal(dqkv, dqkv2)
+
+
+def test_cross_entropy(cuda):
+    torch.manual_seed(6)
+    T, V = 333, 50257
+    ld = ((V + 7) // 8) * 8
+    logits = torch.randn(T, ld, device=cuda) * 3
+    tgt = torch.randint(0, V, (T,), device=cuda)
+    loss, dl = ops.cross_entropy(logits[:, :V], V, tgt, 1.0 / T)
+    lr = logits[:, :V].clone().requires_grad_(True)
+    ref = F.cross_entropy(lr, tgt)
+    ref.backward()
+    assert abs(loss.item() - ref.item()) < 1e-5 * abs(ref.item())
+    assert rel_err(dl[:, :V], lr.grad) < 1e-2
+    assert dl[:, V:].abs().max().item() == 0
+
+
+@pytest.mark.parametrize("fp8", [False, True])
+def test_embedding(cuda, fp8):
+    torch.manual_seed(7)
+    V, S, d, B = 1000, 128, 256, 4
+    wte = torch.randn(V, d, device=cuda)
+    wpe = torch.randn(S, d, device=cuda)
+    idx = torch.randint(0, 50, (B, S), device=cuda)  # many repeats
+    out = ops.embed_fwd(idx, wte, wpe, S, fp8)
+    ref = wte[idx.view(-1)] + wpe[torch.arange(B * S, device=cuda) % S]
+    got = ops.dequant_e4m3(*out, torch.float32) if fp8 else out.float()
+    assert rel_err(got, ref) < (6e-2 if fp8 else 8e-3)
+    dx = bf(B * S, d, dev=cuda)
+    dwte = torch.zeros(V, d, device=cuda)
+    dwpe = torch.zeros(S, d, device=cuda)
+    ops.embed_bwd(idx, dx, S, dwte, dwpe)
+    rte = torch.zeros(V, d, device=cuda).index_add_(0, idx.view(-1), dx.float())
+    assert rel_err(dwte, rte) < 1e-6
+    assert rel_err(dwpe, dx.float().view(B, S, d).sum(0)) < 1e-6
+    dwte2 = torch.zeros(V, d, device=cuda)
+    ops.embed_bwd(idx, dx, S, dwte2, torch.zeros(S, d, device=cuda))
+    assert torch.equal(dwte, dwte2)
+
+
+def test_adamw(cuda):
+    torch.manual_seed(8)
+    n = 100_003
+    p = torch.randn(n, device=cuda)
+    g = torch.randn(n, device=cuda)
+    m = torch.zeros(n, device=cuda)
+    v = torch.zeros(n, device=cuda)
+    pb = torch.empty(n, dtype=torch.bfloat16, device=cuda)
+    pr = p.clone().requires_grad_(True)
+    opt = torch.optim.AdamW([pr], lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+    for step in (1, 2, 3):
+        ops.adamw(p, m, v, g, pb, 1e-3, 0.9, 0.95, 1e-8, 0.1, step)
+        pr.grad = g.clone()
+        opt.step()
+    assert rel_err(p, pr.detach()) < 1e-6
+    assert torch.equal(pb, p.to(torch.bfloat16))
+
+
+def test_colsum_and_fp8(cuda):
+    torch.manual_seed(9)
+    x = bf(3000, 777, dev=cuda)
+    g = torch.zeros(777, device=cuda)
+    ops.colsum(x, g, accumulate=False)
+    assert rel_err(g, x.float().sum(0)) < 1e-6
+    y = bf(64, 512, dev=cuda, scale=10)
+    q, s = ops.quant_e4m3(y)
+    qc, sc = ops.quant_e4m3(y.cpu())
+    assert torch.equal(s.cpu(), sc)
+    assert torch.equal(q.cpu().view(torch.uint8), qc.view(torch.uint8))
