@@ -1,0 +1,294 @@
+#!/usr/bin/env python
+"""Headline benchmark: whole-job tokens/s of the 15.8B GPT pipeline.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P \
+        bench.py --gpus N --steps K --warmup W
+
+Config (BASELINE): dense GPT, 48 layers, d_model 5120, 40 heads, MLP 20480,
+seq 2048, vocab 50257, bf16 compute, fp8 e4m3 1x128 boundaries, zero-bubble
+schedule, 64 microbatches of 1 sequence per step (131,072 tokens), synthetic
+seeded-uniform tokens and random-init weights. The SAME model and step run at
+every N: N pipeline stages of 48/N layers (strong scaling). Memory plan per
+stage: fp32 master + fp32 gradient + bf16 working copy on the device; AdamW
+moments on the device when they fit, else in pinned host memory ("adamw-host",
+the same kernel and bits); per-layer recompute only where a microbatch's
+activations would not fit.
+
+Timing: W untimed warm-up steps; then a barrier + cuda synchronize, CUDA
+events on each rank's compute stream around exactly K steps, synchronize +
+barrier, max over ranks. Every step's working set (GBs of weights) is larger
+than L2. `e2e` times the same K steps on the host clock through the public
+engine API, including each step's host->device copy of the token ids and
+targets from pinned memory and the device->host read of the step's losses.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+BASELINE_TOK_S = 3344.0  # 15.8B GPT, 2x H100 NVL over WAN, run 3
+METRIC = "tokens/s (8xB200, max over ranks) 15.8B GPT PP+ZeRO-1"
+GiB = 1 << 30
+
+
+def _env_rank():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    def __init__(self, gpus: list):
+        self.gpus = gpus
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        self.p.wait()
+        self.f.flush()
+        self.f.seek(0)
+        mhz, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.f.read().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                idx = int(parts[0])
+            except ValueError:
+                continue
+            if idx not in self.gpus:
+                continue
+            try:
+                mhz.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                pass
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.f.name)
+        return {"sm_mhz": statistics.median(mhz) if mhz else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(mhz)}
+
+
+def plan_spec(args, n: int, free_bytes: float | None):
+    """The 15.8B spec at N stages, with the per-stage memory plan."""
+    from elysium_wan_b200.models.config import make_config
+    from elysium_wan_b200.runtime.spec import JobSpec
+    from elysium_wan_b200.scheduler import partition as part
+
+    cfg = make_config(args.model)
+    spec = JobSpec(model=cfg, stages=n, microbatches=args.microbatches, mb_size=args.mb_size,
+                   steps=args.warmup + args.steps, device="cuda", backend="nccl",
+                   init_seed=1234, data_seed=5678, lr=1e-4, out_dir=tempfile.gettempdir(),
+                   tag="bench")
+    spec.partition = part.even_blocks_partition(cfg, n)
+    # Largest stage decides the plan (all ranks must agree on the spec).
+    from elysium_wan_b200.models.gpt import entry_specs
+
+    def numel(stage):
+        a, b = spec.partition[stage]
+        tot = 0
+        for e in range(a, b):
+            for s in entry_specs(cfg, e):
+                k = 1
+                for x in s.shape:
+                    k *= x
+                tot += k
+        return tot
+
+    biggest = max(numel(r) for r in range(n))
+    cap = free_bytes if free_bytes else 178 * GiB
+    resident = biggest * (4 + 4 + 2)
+    slack = 8 * GiB
+    host_adam = resident + 8 * biggest > 0.80 * cap
+    spec.optimizer = "adamw-host" if host_adam else "adamw"
+    budget = cap - resident - (0 if host_adam else 8 * biggest) - slack
+    spec.stage_widths = [1] * n
+    from elysium_wan_b200.scheduler.planner import stage_memory_model
+
+    spec.peer_weights = [[1.0]] * n
+    spec.recompute = False
+    if n == 1:
+        # Single device: F, B, W per microbatch (W inline in B); recompute if one
+        # microbatch's activations do not fit.
+        f, _, _ = stage_memory_model(spec, 0)
+        spec.recompute = f > budget
+        spec.schedule_order = [[sum(([["F", mb], ["B", mb], ["W", mb]]
+                                     for mb in range(spec.microbatches)), [])]]
+    else:
+        from elysium_wan_b200.scheduler.planner import default_schedule
+
+        spec.zb_mem_mode = "auto"
+        spec.mb_owner = [[0] * spec.microbatches for _ in range(n)]
+        try:
+            spec.schedule_order = default_schedule(spec, [budget] * n)
+        except ValueError:  # one microbatch does not fit without recompute
+            spec.recompute = True
+            spec.schedule_order = default_schedule(spec, [budget] * n)
+    spec.finalize()
+    return spec
+
+
+def run_ours(args) -> dict | None:
+    import torch
+    import torch.distributed as dist
+
+    from elysium_wan_b200 import ops
+    from elysium_wan_b200.parallel.p2p import PipeComm
+    from elysium_wan_b200.runtime.engine import StageEngine
+    from elysium_wan_b200.runtime.stage_main import init_group
+    from elysium_wan_b200.utils.determinism import setup_determinism
+
+    rank, world, local = _env_rank()
+    n = args.gpus
+    if world != n:
+        raise SystemExit(f"--gpus {n} but WORLD_SIZE={world}: launch N>1 with torchrun")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    ops.ext()
+    free, _ = torch.cuda.mem_get_info(dev)
+    if world > 1:
+        os.environ.setdefault("TORCH_NCCL_ASYNC_ERROR_HANDLING", "1")
+    spec = plan_spec(args, n, float(free))
+    setup_determinism(spec.init_seed)
+    init_group(spec, rank, timeout_s=600.0)
+    comm = PipeComm(spec, rank, 0, dev) if world > 1 else None
+    eng = StageEngine(spec, rank, 0, comm, dev)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    for s in range(args.warmup):
+        eng.run_step(s)
+    torch.cuda.synchronize()
+    st = ops.ext().status_read_clear()
+    if st != 0:
+        raise RuntimeError(f"device status word {st} after warm-up")
+    barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(list(range(n))) if local == 0 else None
+    l0 = ops.launch_count()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    e0.record()
+    for s in range(args.warmup, args.warmup + args.steps):
+        eng.run_step(s)
+    e1.record()
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    barrier()
+    launches = ops.launch_count() - l0
+    clocks = sampler.stop() if sampler else None
+    dev_ms = e0.elapsed_time(e1)
+    wall_ms = (t1 - t0) * 1e3
+    busy = None
+    ot = eng.op_times_ms()
+    if ot:
+        from elysium_wan_b200.runtime.telemetry import summarize_step
+
+        busy = summarize_step(0, rank, 0, 0.0, ot, 0, 0)["busy_frac"]
+    vec = torch.tensor([dev_ms, wall_ms, float(launches), busy or 0.0, busy or 2.0],
+                       dtype=torch.float64, device=dev)
+    if world > 1:
+        mx = vec.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = vec.clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        mn = vec.clone()
+        dist.all_reduce(mn, op=dist.ReduceOp.MIN)
+        dev_ms, wall_ms = mx[0].item(), mx[1].item()
+        launches = int(sm[2].item())
+        busy_min = mn[4].item()
+    else:
+        busy_min = busy
+    st = ops.ext().status_read_clear()
+    losses = [v for _, v in eng.losses[-spec.microbatches:]] if eng.last else []
+    if comm is not None:
+        comm.close()
+    if world > 1:
+        dist.destroy_process_group()
+    if st != 0:
+        raise RuntimeError(f"device status word {st} after the timed steps")
+    if rank != 0:
+        return None
+    tokens = spec.microbatches * spec.mb_size * spec.model.seq_len
+    value = tokens * args.steps / (dev_ms / 1e3)
+    e2e = tokens * args.steps / (wall_ms / 1e3)
+    h2d = spec.microbatches * spec.mb_size * spec.model.seq_len * 8 * 2
+    return {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": n,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 3),
+        "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": round(value / BASELINE_TOK_S, 3), "dtype": "bf16",
+        "data": "synthetic (seeded uniform token ids, random-init weights)",
+        "config": {"model": f"{args.model} (48L d5120 40h MLP20480 seq2048 vocab50257, fp8 e4m3 1x128 boundaries)",
+                   "global_batch": spec.microbatches * spec.mb_size, "seq_len": spec.model.seq_len,
+                   "parallelism": f"pp{n}", "microbatches": spec.microbatches,
+                   "schedule": "zero-bubble", "optimizer": spec.optimizer,
+                   "recompute": spec.recompute, "l2": "working set larger than L2 (no flush)"},
+        "clocks": clocks,
+        "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": spec.microbatches * 4},
+        "gpu_launches": launches,
+        "busy_frac_min_over_stages": None if busy_min is None else round(busy_min, 4),
+        "last_losses": losses[:4],
+    }
+
+
+def run_reference(args) -> dict:
+    from elysium_wan_b200.utils.refbench import run_reference_arm
+
+    return run_reference_arm(args)
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--model", default="gpt15b")
+    ap.add_argument("--microbatches", type=int, default=64)
+    ap.add_argument("--mb-size", type=int, default=1)
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        out = run_reference(args)
+    else:
+        out = run_ours(args)
+    if out is not None:
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

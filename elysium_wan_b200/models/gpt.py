@@ -235,24 +235,43 @@ class StageModel:
     def last(self) -> bool:
         return self.hi == self.cfg.n_layer + 2
 
-    def forward(self, inp, targets=None):
+    def forward(self, inp, targets=None, keep: str = "all"):
         """F of one microbatch. inp: token ids (first stage) or an Act.
-        Returns (output Act or loss, per-layer contexts)."""
-        ctxs = []
+        keep="all" saves every layer's context for B; keep="inputs" saves only
+        each layer's input (per-layer recompute in B). Returns (output Act or
+        loss, per-layer saved state)."""
+        saved = []
         h = inp
         for layer in self.layers:
             ctx: dict = {}
+            x_in = h
             if isinstance(layer, Head):
                 h = layer.forward(h, ctx, targets)
             else:
                 h = layer.forward(h, ctx)
-            ctxs.append(ctx)
-        return h, ctxs
+            if keep == "all" or isinstance(layer, (Head, Embed)):
+                saved.append(("ctx", ctx))
+            else:
+                ctx.clear()
+                saved.append(("input", x_in))
+        return h, saved
 
-    def backward(self, ctxs, dy, wq: list):
+    def backward(self, saved, dy, wq: list, run_w_inline: bool = False):
         """B of one microbatch: returns the input gradient (None on the first
-        stage) and appends the deferred W tasks, last layer first."""
+        stage) and appends the deferred W tasks, last layer first. Layers saved
+        as inputs are re-run forward just before their backward. With
+        run_w_inline each layer's W tasks run right after its B (same fold
+        order per parameter: one contribution per microbatch)."""
         g = dy
-        for layer, ctx in zip(reversed(self.layers), reversed(ctxs)):
-            g = layer.backward(ctx, g, wq)
+        for layer, (kind, obj) in zip(reversed(self.layers), reversed(saved)):
+            if kind == "input":
+                ctx: dict = {}
+                layer.forward(obj, ctx)
+            else:
+                ctx = obj
+            tasks: list = [] if run_w_inline else wq
+            g = layer.backward(ctx, g, tasks)
+            if run_w_inline:
+                for t in tasks:
+                    t.run()
         return g

@@ -1,0 +1,190 @@
+"""The stage engine: executes one slot's zero-bubble order per step.
+
+Reference: StageRuntime (src/wantrain/runtime/stage.py:193-3985): per step it
+walks schedule_order[stage][peer], runs F / B / W, routes activations and
+gradients to the neighbouring stages, folds gradients in microbatch order and
+steps AdamW. Here the data plane is torch.distributed (NCCL over NVLink on the
+GPU, gloo on CPU), every op is a short sequence of sm_100a kernels on the
+compute stream, receives are posted one op ahead so NCCL moves the next input
+while the current op computes, and W folds dW straight into the fp32
+gradient in the GEMM epilogue (the order of W ops is the fold order, and the
+spec checks it is ascending).
+
+Per-op device time comes from CUDA events (busy fraction per stage); the
+`WT_TELEM` summary keeps the reference's schema (runtime/telemetry.py).
+"""
+
+from __future__ import annotations
+
+import time
+
+import torch
+
+from elysium_wan_b200.models.data import make_batch
+from elysium_wan_b200.models.gpt import Act, StageModel
+from elysium_wan_b200.runtime import optim
+
+
+class StageEngine:
+    def __init__(self, spec, stage: int, peer: int, comm=None, device=None):
+        self.spec, self.stage, self.peer = spec, stage, peer
+        self.device = torch.device(device or spec.device_for(stage, peer))
+        if self.device.type == "cuda":
+            torch.cuda.set_device(self.device)
+        self.model = StageModel(spec.model, tuple(spec.partition[stage]), self.device, spec.init_seed)
+        self.store = self.model.store
+        self.comm = comm
+        self.order = [(op, int(mb)) for op, mb in spec.schedule_order[stage][peer]]
+        self.recompute = spec.recomputes(stage)
+        st = self.store
+        self.opt = optim.build(spec.optimizer, st.master, st.grad, st.work, spec.lr, spec.adamw)
+        self.width = spec.stage_widths[stage]
+        self.step_done = 0
+        self.losses: list = []  # (step, mb, float)
+        self.events: list = []  # per-op (op, mb, start_event, end_event)
+        self.timing = spec.device_for(stage, peer).startswith("cuda")
+        self.telemetry: list = []
+        self.zero1 = None
+        if self.width > 1:
+            from elysium_wan_b200.parallel.zero1 import Zero1
+
+            self.zero1 = Zero1(self, comm)
+
+    @property
+    def first(self) -> bool:
+        return self.model.first
+
+    @property
+    def last(self) -> bool:
+        return self.model.last
+
+    # ----------------------------------------------------------------- data
+    def _batch(self, step: int, mb: int):
+        s = self.spec
+        x, t = make_batch(s.data_seed, step, mb, s.mb_size, s.model.seq_len, s.model.vocab_size,
+                          dataset=s.dataset_path, data_shards=s.data_shards)
+        if self.device.type == "cuda":
+            x = x.pin_memory().to(self.device, non_blocking=True)
+            t = t.pin_memory().to(self.device, non_blocking=True)
+        return x, t
+
+    # ----------------------------------------------------------------- one step
+    def run_step(self, step: int) -> list:
+        """Execute this slot's order for `step`; returns [(mb, loss)] on the
+        last stage (floats after one device->host read), else []."""
+        spec = self.spec
+        comm = self.comm
+        self.store.zero_grad()
+        f_mbs = [mb for op, mb in self.order if op == "F"]
+        b_mbs = [mb for op, mb in self.order if op == "B"]
+        act_q: dict = {}
+        grad_q: dict = {}
+        fi = bi = 0
+        if not self.first:
+            act_q[f_mbs[0]] = comm.irecv_act(f_mbs[0])
+        if not self.last:
+            grad_q[b_mbs[0]] = comm.irecv_grad(b_mbs[0])
+        batches = {}
+        if self.first or self.last:
+            for mb in f_mbs:
+                batches[mb] = self._batch(step, mb)
+        saved: dict = {}
+        wq: dict = {}
+        sends: list = []
+        dev_losses: list = []
+        ev = self.timing
+        self.events = []
+        inline_done: set = set()
+        keep = "inputs" if self.recompute else "all"
+        for idx, (op, mb) in enumerate(self.order):
+            if op == "W" and mb in inline_done:
+                continue
+            if ev:
+                e0 = torch.cuda.Event(enable_timing=True)
+                e0.record()
+            if op == "F":
+                if self.first:
+                    inp = batches[mb][0]
+                else:
+                    inp = comm.as_act(comm.wait(act_q.pop(mb)))
+                fi += 1
+                if not self.first and fi < len(f_mbs):
+                    act_q[f_mbs[fi]] = comm.irecv_act(f_mbs[fi])
+                tgt = batches[mb][1] if self.last else None
+                out, st = self.model.forward(inp, tgt, keep=keep)
+                saved[mb] = st
+                if self.last:
+                    dev_losses.append((mb, out))
+                else:
+                    sends += comm.send_act(mb, out)
+            elif op == "B":
+                st = saved.pop(mb)
+                if self.last:
+                    dy = None
+                else:
+                    dy = comm.wait(grad_q.pop(mb))[0]
+                    bi += 1
+                    if bi < len(b_mbs):
+                        grad_q[b_mbs[bi]] = comm.irecv_grad(b_mbs[bi])
+                # A W that directly follows its own B runs layer by layer inside
+                # B, releasing each layer's W inputs at once (same fold order).
+                inline = idx + 1 < len(self.order) and self.order[idx + 1] == ("W", mb)
+                tasks: list = []
+                dx = self.model.backward(st, dy, tasks, run_w_inline=inline)
+                if inline:
+                    inline_done.add(mb)
+                else:
+                    wq[mb] = tasks
+                if not self.first:
+                    sends += comm.send_grad(mb, dx)
+            else:  # W
+                for t in wq.pop(mb):
+                    t.run()
+            if ev:
+                e1 = torch.cuda.Event(enable_timing=True)
+                e1.record()
+                self.events.append((op, mb, e0, e1))
+        for w in sends:
+            w.wait()
+        if comm is not None:
+            comm.flush()
+        if self.zero1 is not None:
+            self.zero1.sync_and_step()
+        else:
+            self.opt.step()
+        self.step_done = step + 1
+        out = []
+        if self.last and dev_losses:
+            vals = torch.stack([l.reshape(()) for _, l in dev_losses]).float().cpu().tolist()
+            out = [(mb, v) for (mb, _), v in zip(dev_losses, vals)]
+            for mb, v in out:
+                self.losses.append((step, mb, v))
+        return out
+
+    def op_times_ms(self) -> list:
+        """[(op, mb, start_ms, dur_ms)] of the last step (after a synchronize)."""
+        if not self.events:
+            return []
+        base = self.events[0][2]
+        return [(op, mb, base.elapsed_time(a), a.elapsed_time(b)) for op, mb, a, b in self.events]
+
+    # ----------------------------------------------------------------- state
+    def state_dict(self) -> dict:
+        return {"step": self.step_done, "params": self.store.master.detach().cpu().clone(),
+                "names": self.store.names(), "opt": self.opt.state_dict(),
+                "losses": {f"{s}:{m}": v for s, m, v in self.losses},
+                "rng": torch.get_rng_state()}
+
+    def load_state_dict(self, sd: dict):
+        self.store.master.copy_(sd["params"].to(self.store.master.device))
+        self.store.sync_work()
+        self.opt.load_state_dict(sd["opt"])
+        self.step_done = int(sd["step"])
+        self.losses = [(int(k.split(":")[0]), int(k.split(":")[1]), float(v))
+                       for k, v in sd.get("losses", {}).items()]
+        if "rng" in sd:
+            torch.set_rng_state(sd["rng"])
+
+
+def wall() -> float:
+    return time.perf_counter()

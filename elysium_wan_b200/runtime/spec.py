@@ -1,0 +1,262 @@
+"""JobSpec: the single JSON object that determines a run.
+
+Field names follow the reference (src/wantrain/runtime/spec.py:51-171) so a
+wantrain spec loads unchanged; `finalize()` derives the partition, stage
+widths, microbatch ownership (IWRR) and the zero-bubble order, and validates
+them; `pins()` lists the fields a checkpoint's bytes depend on.
+
+B200 additions: `backend` (nccl on GPUs, gloo / tcp on CPU), `zb_mem_mode`,
+`fold` (the declared ZeRO-1 gradient fold, a recipe pin) and `grad_sync`
+(how wide stages move gradients: "fused" in-kernel peer stores or "nccl";
+both produce the same bits, so it is not a pin).
+"""
+
+from __future__ import annotations
+
+import json
+from dataclasses import asdict, dataclass, field
+from typing import Any
+
+from elysium_wan_b200.models.config import GPTConfig
+
+OPS = ("F", "B", "W")
+ADAMW: dict[str, Any] = {"betas": [0.9, 0.95], "eps": 1e-8, "weight_decay": 0.0}
+OPTIMIZERS = ("adamw", "adamw-host")
+BACKENDS = ("nccl", "gloo", "tcp")
+FOLDS = ("dp_tree",)
+
+
+@dataclass
+class LinkCfg:
+    latency_ms: float = 0.0
+    bw_mbps: float = 0.0
+    jitter_ms: float = 0.0
+    jitter_seed: int = 0
+
+
+@dataclass
+class JobSpec:
+    # ------------------------------------------------------------- recipe
+    model: GPTConfig = field(default_factory=GPTConfig)
+    init_seed: int = 1234
+    data_seed: int = 5678
+    lr: float = 1e-3
+    optimizer: str = "adamw"
+    adamw: dict = field(default_factory=lambda: dict(ADAMW))
+    device: str = "cpu"
+    devices: list | None = None
+    dataset_path: str | None = None
+    dataset_sha256: str | None = None
+    data_shards: int = 1
+    dataset_source: str | None = None
+    steps: int = 8
+    microbatches: int = 8
+    mb_size: int = 4
+    recompute: bool = False
+    recompute_stages: list | None = None
+    # ------------------------------------------------------------- checkpoints
+    ckpt_every: int = 0
+    resume: bool = False
+    resume_step: int | None = None
+    # ------------------------------------------------------------- topology
+    stages: int = 2
+    stage_widths: list | None = None
+    partition: list | None = None
+    peer_weights: list | None = None
+    mb_owner: list | None = None
+    stream_grads: bool = False
+    # ------------------------------------------------------------- schedule
+    schedule_order: list | None = None
+    schedule_fill: bool = True
+    zb_mem_mode: str = "auto"  # auto | 1p | 2p | given
+    stage_costs: list | None = None  # measured [F, B, W] seconds per stage (profiled)
+    # ------------------------------------------------------------- transport
+    backend: str = "gloo"
+    port_base: int = 29000
+    host: str = "127.0.0.1"
+    p2p_streams: int = 1
+    endpoints: list | None = None
+    trusted_peers: list | None = None
+    slot_peers: list | None = None
+    dial_timeout_s: float = 0.0
+    wire_codec: str = "raw"
+    links: list = field(default_factory=list)
+    # ------------------------------------------------------------- wide stages
+    wire: str = "fp32"
+    shard: str = "zero1"
+    fold: str = "dp_tree"
+    grad_sync: str = "fused"  # fused | nccl
+    # ------------------------------------------------------------- output
+    out_dir: str = "runs"
+    tag: str = "run"
+
+    # ------------------------------------------------------------- derived
+    @property
+    def world_size(self) -> int:
+        return sum(self.stage_widths or [1] * self.stages)
+
+    def slots(self) -> list:
+        """[(stage, peer)] in rank order: stage-major."""
+        return [(r, p) for r, w in enumerate(self.stage_widths) for p in range(w)]
+
+    def rank_of(self, stage: int, peer: int) -> int:
+        return sum(self.stage_widths[:stage]) + peer
+
+    def slot_of(self, rank: int) -> tuple[int, int]:
+        return self.slots()[rank]
+
+    def owned(self, rank: int, peer: int) -> list:
+        """Microbatches slot (stage `rank`, `peer`) computes, ascending."""
+        return [mb for mb, p in enumerate(self.mb_owner[rank]) if p == peer]
+
+    def device_for(self, stage: int, peer: int = 0) -> str:
+        if self.devices is not None:
+            return self.devices[stage][peer]
+        return self.device
+
+    def recomputes(self, stage: int) -> bool:
+        if self.recompute_stages is None:
+            return bool(self.recompute)
+        return bool(self.recompute_stages[stage])
+
+    def finalize(self) -> "JobSpec":
+        from elysium_wan_b200.scheduler import partition as part
+        from elysium_wan_b200.scheduler.zero_bubble import iwrr
+        from elysium_wan_b200.scheduler.planner import default_schedule
+
+        self.model.validate()
+        if self.optimizer not in OPTIMIZERS:
+            raise ValueError(f"optimizer {self.optimizer!r} is not one of {OPTIMIZERS}")
+        if self.backend not in BACKENDS:
+            raise ValueError(f"backend {self.backend!r} is not one of {BACKENDS}")
+        if self.fold not in FOLDS:
+            raise ValueError(f"fold {self.fold!r} is not one of {FOLDS}")
+        if self.shard != "zero1":
+            raise NotImplementedError("shard 'pieces' is not implemented; use 'zero1'")
+        if self.partition is None:
+            try:
+                self.partition = part.even_blocks_partition(self.model, self.stages)
+            except ValueError:
+                self.partition = part.proportional_partition(self.model, [1.0] * self.stages)
+        self.partition = [list(map(int, r)) for r in self.partition]
+        if len(self.partition) != self.stages:
+            raise ValueError("partition needs one [start, end) per stage")
+        prev = 0
+        for a, b in self.partition:
+            if a != prev or b <= a:
+                raise ValueError(f"partition must tile the layer list contiguously: {self.partition}")
+            prev = b
+        if prev != self.model.n_entries:
+            raise ValueError(f"partition ends at {prev}, the model has {self.model.n_entries} entries")
+        if not self.links:
+            self.links = [asdict(LinkCfg()) for _ in range(self.stages)]
+        if self.stage_widths is None:
+            self.stage_widths = [1] * self.stages
+        if len(self.stage_widths) != self.stages:
+            raise ValueError("stage_widths needs one entry per stage")
+        if self.recompute_stages is not None and len(self.recompute_stages) != self.stages:
+            raise ValueError("recompute_stages must name every stage")
+        if self.peer_weights is None:
+            self.peer_weights = [[1.0] * w for w in self.stage_widths]
+        if [len(w) for w in self.peer_weights] != list(self.stage_widths):
+            raise ValueError("peer_weights must have the shape of stage_widths")
+        if self.mb_owner is None:
+            self.mb_owner = [iwrr(self.microbatches, w) for w in self.peer_weights]
+        for r, row in enumerate(self.mb_owner):
+            if len(row) != self.microbatches or not all(0 <= p < self.stage_widths[r] for p in row):
+                raise ValueError(f"mb_owner[{r}] must map every microbatch to a peer of stage {r}")
+        if self.schedule_order is None:
+            self.schedule_order = default_schedule(self)
+        self._check_schedule_order()
+        if self.resume_step is not None and not self.resume:
+            raise ValueError("resume_step needs resume")
+        return self
+
+    def reschedule(self) -> "JobSpec":
+        self.mb_owner = None
+        self.schedule_order = None
+        return self.finalize()
+
+    def _check_schedule_order(self):
+        if len(self.schedule_order) != self.stages:
+            raise ValueError("schedule_order needs every stage")
+        for r, per_peer in enumerate(self.schedule_order):
+            if len(per_peer) != self.stage_widths[r]:
+                raise ValueError(f"schedule_order[{r}] needs every peer")
+            for p, order in enumerate(per_peer):
+                want = self.owned(r, p)
+                seen = {op: [] for op in OPS}
+                for op, mb in order:
+                    if op not in OPS:
+                        raise ValueError(f"unknown op {op!r}")
+                    seen[op].append(int(mb))
+                for op in OPS:
+                    if sorted(seen[op]) != want:
+                        raise ValueError(f"slot ({r}, {p}): {op} must cover exactly its microbatches")
+                # Gradients fold in microbatch order: B and W of a slot run ascending.
+                for op in ("B", "W"):
+                    if seen[op] != sorted(seen[op]):
+                        raise ValueError(f"slot ({r}, {p}): {op} must run in microbatch order")
+
+    def pins(self) -> dict:
+        """Fields a checkpoint's bytes depend on; a resume must match them.
+        Not pins: ownership, schedule, endpoints, devices, steps, out_dir,
+        grad_sync (who computes what and how bytes move never changes a bit)."""
+        pins = {
+            "model": self.model.to_dict(),
+            "init_seed": self.init_seed,
+            "data_seed": self.data_seed,
+            "dataset_path": self.dataset_path,
+            "data_shards": self.data_shards,
+            "microbatches": self.microbatches,
+            "mb_size": self.mb_size,
+            "lr": self.lr,
+            "adamw": self.adamw,
+            "wire_codec": self.wire_codec,
+            "recompute": self.recompute,
+            "partition": self.partition,
+            "device_types": [sorted({self.device_for(r, p).split(":")[0] for p in range(w)})
+                             for r, w in enumerate(self.stage_widths)],
+            "zero1_widths": self.stage_widths,
+            "fold": self.fold,
+        }
+        if self.optimizer != "adamw":
+            pins["optimizer"] = self.optimizer
+        if self.dataset_sha256:
+            pins["dataset_sha256"] = self.dataset_sha256
+        return json.loads(json.dumps(pins))
+
+    def to_dict(self) -> dict:
+        d = asdict(self)
+        d["model"] = self.model.to_dict()
+        return d
+
+    def to_json(self) -> str:
+        return json.dumps(self.to_dict(), indent=2)
+
+    @staticmethod
+    def from_dict(d: dict) -> "JobSpec":
+        d = dict(d)
+        d["model"] = GPTConfig.from_dict(d.get("model", {}))
+        known = set(JobSpec.__dataclass_fields__)
+        return JobSpec(**{k: v for k, v in d.items() if k in known})
+
+    @staticmethod
+    def from_json(s: str) -> "JobSpec":
+        return JobSpec.from_dict(json.loads(s))
+
+    @staticmethod
+    def load(path: str) -> "JobSpec":
+        with open(path) as f:
+            return JobSpec.from_json(f.read())
+
+
+def first_pin_difference(want: dict, have: dict) -> str | None:
+    for k in list(want) + [k for k in have if k not in want]:
+        a, b = want.get(k), have.get(k)
+        if a == b and (k in want) == (k in have):
+            continue
+        if isinstance(a, dict) and isinstance(b, dict):
+            return f"{k}.{first_pin_difference(a, b)}"
+        return k
+    return None

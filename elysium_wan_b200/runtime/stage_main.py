@@ -1,0 +1,127 @@
+"""One slot (stage, peer) as its own OS process.
+
+Reference: src/wantrain/worker/stage_main.py (run_stage; WT_* stdout markers;
+`WT_DONE <rc>` always last). The process joins the job's torch.distributed
+group (NCCL on GPUs, gloo on CPU; rank = stage-major slot index), builds its
+StageEngine, resumes from its newest checkpoint wave when asked, runs the
+steps and writes its losses.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import sys
+import time
+import traceback
+
+import torch
+import torch.distributed as dist
+
+
+def _print(tag: str, obj) -> None:
+    print(f"{tag} {json.dumps(obj) if not isinstance(obj, str) else obj}", flush=True)
+
+
+def init_group(spec, rank: int, timeout_s: float):
+    backend = "nccl" if spec.backend == "nccl" else "gloo"
+    if spec.world_size == 1:
+        return
+    if "MASTER_ADDR" in os.environ and "WORLD_SIZE" in os.environ:
+        init = "env://"
+    else:
+        init = f"tcp://{spec.host}:{spec.port_base}"
+    kw = {}
+    if backend == "nccl":
+        kw["device_id"] = torch.device("cuda", torch.cuda.current_device())
+    dist.init_process_group(backend, init_method=init, rank=rank, world_size=spec.world_size,
+                            timeout=datetime.timedelta(seconds=timeout_s), **kw)
+
+
+def loss_path(spec, stage, peer) -> str:
+    return os.path.join(spec.out_dir, f"{spec.tag}_losses_r{stage}p{peer}.json")
+
+
+def run_stage(spec, stage: int, peer: int, timeout_s: float = 600.0) -> int:
+    from elysium_wan_b200.fault_tolerance import checkpoint as ckpt
+    from elysium_wan_b200.parallel.p2p import PipeComm
+    from elysium_wan_b200.runtime.engine import StageEngine
+    from elysium_wan_b200.runtime.telemetry import summarize_step
+    from elysium_wan_b200.utils.determinism import float_hex, setup_determinism
+    from elysium_wan_b200.validation.reference import loss_records
+
+    setup_determinism(spec.init_seed)
+    rank = spec.rank_of(stage, peer)
+    dev = spec.device_for(stage, peer)
+    if dev.startswith("cuda"):
+        local = int(os.environ.get("LOCAL_RANK", rank % max(1, torch.cuda.device_count())))
+        dev = f"cuda:{local}" if dev == "cuda" else dev
+        torch.cuda.set_device(torch.device(dev))
+    _print("WT_PHASE", {"phase": "init", "stage": stage, "peer": peer, "rank": rank})
+    init_group(spec, rank, timeout_s)
+    comm = PipeComm(spec, stage, peer, torch.device(dev)) if spec.world_size > 1 else None
+    eng = StageEngine(spec, stage, peer, comm, dev)
+    _print("WT_STAGE", {"stage": stage, "peer": peer, "span": spec.partition[stage],
+                        "params": eng.store.numel, "device": dev})
+    start = 0
+    if spec.resume:
+        sd, step = ckpt.load_latest(spec, stage, peer, spec.resume_step)
+        eng.load_state_dict(sd)
+        start = step
+        _print("WT_RESUME", {"step": step})
+    os.makedirs(spec.out_dir, exist_ok=True)
+    stream = open(os.path.join(spec.out_dir, f"{spec.tag}_loss_stream.jsonl"), "a") if eng.last else None
+    for step in range(start, spec.steps):
+        t0 = time.perf_counter()
+        res = eng.run_step(step)
+        if eng.timing:
+            torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        for mb, v in res:
+            rec = {"step": step, "mb": mb, "loss_hex": float_hex(v), "loss": v}
+            if stream is not None:
+                stream.write(json.dumps(rec) + "\n")
+                stream.flush()
+            _print("WT_METRIC", {"step": step, "mb": mb, "loss": v})
+        summary = summarize_step(step, stage, peer, dt * 1e3, eng.op_times_ms(),
+                                 comm.bytes_sent if comm else 0, comm.frames if comm else 0)
+        _print("WT_TELEM", summary)
+        if spec.ckpt_every and (step + 1) % spec.ckpt_every == 0:
+            path = ckpt.commit_wave(spec, stage, peer, step + 1, eng.state_dict())
+            _print("WT_WAVE", {"step": step + 1, "dir": path})
+        _print("WT_STEP", {"step": step, "ms": round(dt * 1e3, 3)})
+    if eng.last:
+        with open(loss_path(spec, stage, peer), "w") as f:
+            json.dump({"losses": loss_records(eng.losses)}, f, indent=1)
+    if comm is not None:
+        comm.close()
+    if spec.world_size > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main(argv=None) -> int:
+    from elysium_wan_b200.runtime.spec import JobSpec
+
+    ap = argparse.ArgumentParser(prog="wantrain stage")
+    ap.add_argument("--spec", required=True)
+    ap.add_argument("--rank", type=int, required=True, help="stage index")
+    ap.add_argument("--peer", type=int, default=0)
+    ap.add_argument("--timeout", type=float, default=600.0)
+    a = ap.parse_args(argv)
+    rc = 1
+    try:
+        spec = JobSpec.load(a.spec).finalize()
+        rc = run_stage(spec, a.rank, a.peer, a.timeout)
+    except Exception:
+        traceback.print_exc()
+        rc = 1
+    print(f"WT_DONE {rc}", flush=True)
+    return rc
+
+
+if __name__ == "__main__":
+    sys.exit(main())
