@@ -102,7 +102,8 @@ def plan_spec(args, n: int, free_bytes: float | None):
     from elysium_wan_b200.runtime.spec import JobSpec
     from elysium_wan_b200.scheduler import partition as part
 
-    cfg = make_config(args.model)
+    over = {"n_layer": args.n_layer} if getattr(args, "n_layer", None) else {}
+    cfg = make_config(args.model, **over)
     spec = JobSpec(model=cfg, stages=n, microbatches=args.microbatches, mb_size=args.mb_size,
                    steps=args.warmup + args.steps, device="cuda", backend="nccl",
                    init_seed=1234, data_seed=5678, lr=1e-4, out_dir=tempfile.gettempdir(),
@@ -187,7 +188,13 @@ def run_ours(args) -> dict | None:
             dist.barrier(device_ids=[local])
 
     for s in range(args.warmup):
+        t = time.perf_counter()
         eng.run_step(s)
+        torch.cuda.synchronize()
+        if rank == 0:
+            print(f"[bench] warm-up step {s}: {time.perf_counter() - t:.2f} s "
+                  f"(max alloc {torch.cuda.max_memory_allocated() / 2**30:.1f} GiB)",
+                  file=sys.stderr, flush=True)
     torch.cuda.synchronize()
     st = ops.ext().status_read_clear()
     if st != 0:
@@ -231,7 +238,7 @@ def run_ours(args) -> dict | None:
     else:
         busy_min = busy
     st = ops.ext().status_read_clear()
-    losses = [v for _, v in eng.losses[-spec.microbatches:]] if eng.last else []
+    losses = [v for _, _, v in eng.losses[-spec.microbatches:]] if eng.last else []
     if comm is not None:
         comm.close()
     if world > 1:
@@ -279,6 +286,9 @@ def main(argv=None):
     ap.add_argument("--model", default="gpt15b")
     ap.add_argument("--microbatches", type=int, default=64)
     ap.add_argument("--mb-size", type=int, default=1)
+    # Diagnostics only (profiling on a shallower model of the same width): a
+    # line printed with it is marked "diagnostic" and is not the benchmark.
+    ap.add_argument("--n-layer", type=int, default=None)
     args = ap.parse_args(argv)
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
@@ -287,6 +297,8 @@ def main(argv=None):
     else:
         out = run_ours(args)
     if out is not None:
+        if args.n_layer or args.microbatches != 64 or args.mb_size != 1:
+            out["diagnostic"] = "reduced config: not the benchmark"
         print(json.dumps(out), flush=True)
 
 

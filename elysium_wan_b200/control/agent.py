@@ -1,0 +1,298 @@
+"""Worker agent: one per machine (or per GPU on a B200 box).
+
+Reference: WorkerAgent (src/wantrain/worker/agent.py:403-1301). The agent
+dials the coordinator, answers the CHALLENGE with an HMAC'd HELLO carrying its
+measured capabilities, heartbeats every second, and supervises one stage
+subprocess (`python -m elysium_wan_b200.runtime.stage_main`). It turns the
+stage's WT_* stdout markers into PROGRESS / TELEM_STEP messages, ships every
+checkpoint wave to the coordinator (CKPT, files with sha256), reports EXIT
+{rc, done_marker, log tail} and, from the last stage, RESULT {losses}. It
+obeys ABORT (kill the stage's process group), RESTORE (write shipped wave
+files), RELEASE and SHUTDOWN, and reconnects with backoff when the control
+connection drops.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import signal
+import subprocess
+import sys
+import threading
+import time
+import traceback
+
+from elysium_wan_b200.transport.control import Channel, control_dial, token_mac
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+class StageProcess:
+    """One stage subprocess in its own process group, stdout read line by line."""
+
+    def __init__(self, cmd: list, env: dict, on_line, log_path: str):
+        self.log = open(log_path, "a")
+        self.p = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, env=env,
+                                  text=True, bufsize=1, start_new_session=True)
+        self.tail: list = []
+        self.done_marker = False
+        self.t = threading.Thread(target=self._read, args=(on_line,), daemon=True)
+        self.t.start()
+
+    def _read(self, on_line):
+        for line in self.p.stdout:
+            self.log.write(line)
+            self.log.flush()
+            line = line.rstrip("\n")
+            self.tail = (self.tail + [line])[-40:]
+            if line.startswith("WT_DONE"):
+                self.done_marker = True
+            try:
+                on_line(line)
+            except Exception:
+                traceback.print_exc()
+
+    def alive(self) -> bool:
+        return self.p.poll() is None
+
+    def kill(self):
+        if self.p.poll() is None:
+            try:
+                os.killpg(self.p.pid, signal.SIGKILL)
+            except ProcessLookupError:
+                pass
+        self.p.wait()
+        self.t.join(timeout=5)
+        self.log.close()
+
+    def wait(self) -> int:
+        rc = self.p.wait()
+        self.t.join(timeout=10)
+        self.log.close()
+        return rc
+
+
+class WorkerAgent:
+    def __init__(self, coordinator: str, coordinator_id: str = "", token: str | None = None,
+                 name: str | None = None, workdir: str = "worker", device: str = "cpu",
+                 region: str = "default", wan_profile: str | None = None, declare: dict | None = None,
+                 no_bench: bool = True, advertise_host: str = "127.0.0.1", heartbeat_s: float = 1.0):
+        host, _, port = coordinator.rpartition(":")
+        self.addr = (host or "127.0.0.1", int(port))
+        self.coordinator_id = coordinator_id
+        self.token = token if token is not None else os.environ.get("WANTRAIN_COORD_TOKEN", "")
+        self.name = name or f"worker-{os.getpid()}"
+        self.workdir = os.path.abspath(workdir)
+        os.makedirs(self.workdir, exist_ok=True)
+        self.device = device
+        self.region = region
+        self.wan_profile = wan_profile
+        self.declare = declare or {}
+        self.no_bench = no_bench
+        self.advertise_host = advertise_host
+        self.heartbeat_s = heartbeat_s
+        self.ch: Channel | None = None
+        self.stage: StageProcess | None = None
+        self.assign: dict | None = None
+        self.stop = threading.Event()
+        self.lock = threading.Lock()
+        self.node_id = None
+
+    # ----------------------------------------------------------------- connection
+    def _caps(self) -> dict:
+        from elysium_wan_b200.resources.probe import measure
+
+        caps = measure(self.device, bench=not self.no_bench)
+        caps.update(self.declare)
+        caps.update(name=self.name, region=self.region, host=self.advertise_host,
+                    wan_profile=self.wan_profile, pid=os.getpid())
+        return caps
+
+    def _connect(self):
+        ch = control_dial(*self.addr)
+        hdr, _ = ch.recv()
+        if hdr.get("kind") != "CHALLENGE":
+            raise ConnectionError(f"expected CHALLENGE, got {hdr.get('kind')}")
+        cid = hdr.get("coordinator_id", "")
+        if self.coordinator_id and cid != self.coordinator_id:
+            raise ConnectionError(f"coordinator id {cid} is not the expected {self.coordinator_id}")
+        ch.send("HELLO", caps=self._caps(), node_id=self.node_id,
+                mac=token_mac(self.token, hdr["nonce"], cid))
+        hdr, _ = ch.recv()
+        if hdr.get("kind") != "WELCOME":
+            raise PermissionError(f"coordinator refused: {hdr}")
+        self.node_id = hdr["node_id"]
+        self.ch = ch
+
+    def send(self, kind: str, body: bytes = b"", **fields):
+        ch = self.ch
+        if ch is None:
+            return
+        try:
+            ch.send(kind, body, **fields)
+        except OSError:
+            pass
+
+    def run(self):
+        backoff = 0.2
+        hb = threading.Thread(target=self._heartbeat, daemon=True)
+        hb.start()
+        while not self.stop.is_set():
+            try:
+                self._connect()
+                backoff = 0.2
+                self._serve()
+            except (ConnectionError, OSError):
+                pass
+            except PermissionError as e:
+                print(f"WORKER refused: {e}", flush=True)
+                return 2
+            self.ch = None
+            if self.stop.is_set():
+                break
+            time.sleep(backoff)
+            backoff = min(5.0, backoff * 2)
+        self._kill_stage()
+        return 0
+
+    def _heartbeat(self):
+        while not self.stop.is_set():
+            st = self.stage
+            self.send("HEARTBEAT", stage_alive=(st.alive() if st else None), t=time.time())
+            self.stop.wait(self.heartbeat_s)
+
+    # ----------------------------------------------------------------- messages
+    def _serve(self):
+        while not self.stop.is_set():
+            hdr, body = self.ch.recv()
+            kind = hdr["kind"]
+            handler = getattr(self, f"_on_{kind.lower()}", None)
+            if handler is None:
+                self.send(f"{kind}_ACK", ok=False, why="unknown message")
+                continue
+            handler(hdr, body)
+
+    def _on_probe(self, hdr, body):
+        self.send("PROBE_RESULT", caps=self._caps())
+
+    def _on_measure(self, hdr, body):
+        from elysium_wan_b200.resources.probe import measure
+
+        self.send("MEASURE_RESULT", caps=measure(self.device, bench=True))
+
+    def _on_fit(self, hdr, body):
+        from elysium_wan_b200.resources.fit import measure as fit_measure
+        from elysium_wan_b200.runtime.spec import JobSpec
+
+        try:
+            spec = JobSpec.from_dict(hdr["spec"]).finalize()
+            r = fit_measure(spec, hdr["stage"], self.device)
+            self.send("FIT_RESULT", ok=True, **r)
+        except Exception as e:
+            self.send("FIT_RESULT", ok=False, why=repr(e))
+
+    def _on_profile(self, hdr, body):
+        from elysium_wan_b200.resources.profile import profile_stage
+        from elysium_wan_b200.runtime.spec import JobSpec
+
+        try:
+            spec = JobSpec.from_dict(hdr["spec"]).finalize()
+            self.send("PROFILE_RESULT", ok=True, **profile_stage(spec, hdr["stage"], self.device))
+        except Exception as e:
+            self.send("PROFILE_RESULT", ok=False, why=repr(e))
+
+    def _run_dir(self, run_id: str) -> str:
+        d = os.path.join(self.workdir, run_id)
+        os.makedirs(d, exist_ok=True)
+        return d
+
+    def _on_assign(self, hdr, body):
+        self._kill_stage()
+        run_id, attempt = hdr["run_id"], hdr["attempt"]
+        stage, peer = hdr["stage"], hdr["peer"]
+        d = self._run_dir(run_id)
+        spec = dict(hdr["spec"])
+        spec["out_dir"] = d
+        if self.device != "cpu" and spec.get("device", "cpu").startswith("cuda"):
+            spec["device"] = self.device
+        sp = os.path.join(d, f"spec-a{attempt}-r{stage}p{peer}.json")
+        with open(sp, "w") as f:
+            json.dump(spec, f)
+        env = dict(os.environ)
+        from elysium_wan_b200.utils.determinism import PINNED_ENV
+
+        env.update(PINNED_ENV)
+        env["PYTHONPATH"] = ROOT + os.pathsep + env.get("PYTHONPATH", "")
+        cmd = [sys.executable, "-m", "elysium_wan_b200.runtime.stage_main", "--spec", sp,
+               "--rank", str(stage), "--peer", str(peer), "--timeout", str(hdr.get("timeout", 120))]
+        self.assign = dict(hdr, spec_path=sp, dir=d)
+        log = os.path.join(d, f"stage-a{attempt}-r{stage}p{peer}.log")
+        self.stage = StageProcess(cmd, env, self._on_stage_line, log)
+        self.send("ASSIGN_ACK", ok=True, run_id=run_id, attempt=attempt)
+        threading.Thread(target=self._supervise, args=(self.stage, dict(self.assign)), daemon=True).start()
+
+    def _on_stage_line(self, line: str):
+        a = self.assign or {}
+        tag, _, rest = line.partition(" ")
+        if tag == "WT_STEP":
+            self.send("PROGRESS", step=json.loads(rest)["step"], attempt=a.get("attempt"))
+        elif tag == "WT_TELEM":
+            self.send("TELEM_STEP", telem=json.loads(rest), attempt=a.get("attempt"))
+        elif tag == "WT_WAVE":
+            w = json.loads(rest)
+            self._ship_wave(w["dir"], a)
+        elif tag == "WT_METRIC":
+            self.send("METRIC", metric=json.loads(rest), attempt=a.get("attempt"))
+
+    def _ship_wave(self, wave_dir: str, a: dict):
+        """Send every file of a committed wave (wave.json last) to the coordinator."""
+        rel = os.path.relpath(wave_dir, a["dir"])
+        names = sorted(os.listdir(wave_dir), key=lambda n: n == "wave.json")
+        for n in names:
+            self.ch and self.ch.send_file("CKPT", os.path.join(wave_dir, n), rel=os.path.join(rel, n),
+                                          run_id=a["run_id"], last=(n == "wave.json"))
+
+    def _supervise(self, proc: StageProcess, a: dict):
+        rc = proc.wait()
+        if self.stage is not proc:
+            return
+        self.send("EXIT", rc=rc, done_marker=proc.done_marker, tail="\n".join(proc.tail[-20:]),
+                  run_id=a["run_id"], attempt=a["attempt"], stage=a["stage"], peer=a["peer"])
+        spec = a["spec"]
+        if rc == 0 and a["stage"] == spec["stages"] - 1:
+            p = os.path.join(a["dir"], f"{spec['tag']}_losses_r{a['stage']}p{a['peer']}.json")
+            if os.path.exists(p):
+                with open(p) as f:
+                    self.send("RESULT", losses=json.load(f)["losses"], run_id=a["run_id"],
+                              attempt=a["attempt"], stage=a["stage"], peer=a["peer"])
+
+    def _kill_stage(self):
+        st = self.stage
+        self.stage = None
+        if st is not None:
+            st.kill()
+
+    def _on_abort(self, hdr, body):
+        self._kill_stage()
+        self.send("ABORT_ACK", ok=True)
+
+    def _on_restore(self, hdr, body):
+        d = self._run_dir(hdr["run_id"])
+        p = os.path.join(d, hdr["rel"])
+        os.makedirs(os.path.dirname(p), exist_ok=True)
+        with open(p, "wb") as f:
+            f.write(body)
+        if hdr.get("last"):
+            self.send("RESTORE_ACK", ok=True, rel=hdr["rel"])
+
+    def _on_release(self, hdr, body):
+        self._kill_stage()
+        self.send("RELEASE_ACK", ok=True)
+
+    def _on_shutdown(self, hdr, body):
+        self._kill_stage()
+        self.stop.set()
+        self.send("SHUTDOWN_ACK", ok=True)
+        if self.ch:
+            self.ch.close()

@@ -1,0 +1,444 @@
+"""Coordinator: runs one job over registered worker agents.
+
+Reference lifecycle (src/wantrain/coordinator/coordinator.py:316-2420):
+register -> measure -> plan -> fit-check -> profile -> solve -> launch ->
+monitor -> heal / restart -> complete. This coordinator keeps that lifecycle
+and its message kinds:
+
+  * register: agents dial in, answer the HMAC CHALLENGE (HELLO with
+    capabilities), get WELCOME + a node id; a reconnect with the same node id
+    rebinds the slot's channel.
+  * plan: a job is {"spec": JobSpec} or {"plan": {...}, "stages": N}
+    (scheduler/fleetplan.py). Workers are placed in rank order grouped by
+    region; the rest are spares. Hops between regions get the worker's WAN
+    link profile (the CPU/gloo configuration emulates it in the transport).
+  * fit-check (FIT) and profile (PROFILE) are optional round trips.
+  * launch: ASSIGN to every slot, last rank first, with a fresh rendezvous
+    port per attempt (a heal relaunches every slot, so NCCL / gloo groups are
+    always new).
+  * monitor: HEARTBEAT / PROGRESS / EXIT into SlotStates judged by the
+    LivenessJudge every poll_s.
+  * heal: ABORT all, pick a spare for the convicted slot, resume from the
+    newest wave every slot holds (shipped CKPT files, sha256-checked), RESTORE
+    that slot's wave to the spare, relaunch with resume=true.
+  * stalled: restart in place from the common wave.
+  * complete: RESULT losses of the last stage -> runs/<id>/losses.json and
+    result.json.
+"""
+
+from __future__ import annotations
+
+import copy
+import hashlib
+import json
+import os
+import socket
+import threading
+import time
+import uuid
+from dataclasses import dataclass, field
+
+from elysium_wan_b200.fault_tolerance import checkpoint as ckpt
+from elysium_wan_b200.fault_tolerance.liveness import LivenessJudge, SlotState
+from elysium_wan_b200.fault_tolerance.replacement import find_replacement
+from elysium_wan_b200.resources.node import NodeInfo, mixed_fleet
+from elysium_wan_b200.runtime.spec import JobSpec
+from elysium_wan_b200.transport.control import Channel, check_mac, control_listen, new_nonce
+
+
+@dataclass
+class CoordinatorConfig:
+    state_dir: str = "coordinator_state"
+    token: str = ""
+    wait_workers_s: float = 120.0
+    poll_s: float = 0.25
+    max_heals: int = 3
+    max_restarts: int = 2
+    no_probe: bool = True
+    no_fit_check: bool = True
+    group_by: str = "region"
+    allow_shared_hosts: bool = True
+    any_region: bool = True
+    zb_mem_mode: str = "auto"
+    replacement_match: str = "any"
+    keep_workers: bool = False
+    stage_timeout_s: float = 60.0
+    liveness: dict = field(default_factory=dict)
+    wan_links: dict = field(default_factory=dict)  # {"regionA|regionB": {bw_mbps, latency_ms}}
+    job_timeout_s: float = 3600.0
+
+
+@dataclass
+class Job:
+    spec: JobSpec | None = None
+    plan: dict | None = None
+    stages: int | None = None
+
+
+@dataclass
+class RunResult:
+    ok: bool
+    run_id: str
+    losses_path: str | None
+    attempts: int
+    heals: int
+    restarts: int
+    why: str = ""
+    run_dir: str = ""
+
+
+class _Node:
+    def __init__(self, info: NodeInfo, ch: Channel):
+        self.info = info
+        self.ch = ch
+        self.connected = True
+        self.disconnected_at = None
+        self.last_heartbeat = time.time()
+        self.stage_alive = None
+        self.dead = False
+
+
+def _free_port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+class Coordinator:
+    def __init__(self, host: str = "127.0.0.1", port: int = 28000, cfg: CoordinatorConfig | None = None):
+        self.host, self.port = host, port
+        self.cfg = cfg or CoordinatorConfig()
+        self.id = uuid.uuid4().hex[:16]
+        self.nodes: dict[str, _Node] = {}
+        self.order: list = []  # node ids in registration order
+        self.lock = threading.RLock()
+        self.stop_ev = threading.Event()
+        self.sock = None
+        self.slots: dict = {}  # (stage, peer) -> SlotState
+        self.slot_node: dict = {}  # (stage, peer) -> node id
+        self.results: dict = {}
+        self.run_id = None
+        self.attempt = 0
+        self.store = None
+        self.events: list = []
+        self.on_progress = None  # callback(slot, step, node_id)
+        self._pending_ckpt: dict = {}
+
+    # ----------------------------------------------------------------- server
+    def start(self):
+        self.sock = control_listen(self.host, self.port)
+        self.port = self.sock.getsockname()[1]
+        os.makedirs(self.cfg.state_dir, exist_ok=True)
+        print(f"COORDINATOR_ID {self.id}", flush=True)
+        threading.Thread(target=self._accept_loop, daemon=True).start()
+        return self
+
+    def stop(self):
+        self.stop_ev.set()
+        with self.lock:
+            for n in self.nodes.values():
+                if n.connected and not self.cfg.keep_workers:
+                    try:
+                        n.ch.send("SHUTDOWN")
+                    except OSError:
+                        pass
+        try:
+            self.sock.close()
+        except OSError:
+            pass
+
+    def _accept_loop(self):
+        while not self.stop_ev.is_set():
+            try:
+                s, _ = self.sock.accept()
+            except OSError:
+                return
+            threading.Thread(target=self._handshake, args=(Channel(s),), daemon=True).start()
+
+    def _handshake(self, ch: Channel):
+        nonce = new_nonce()
+        try:
+            ch.send("CHALLENGE", nonce=nonce, coordinator_id=self.id)
+            hdr, _ = ch.recv()
+            if hdr.get("kind") != "HELLO" or not check_mac(self.cfg.token, nonce, self.id, hdr.get("mac", "")):
+                ch.send("REJECT", why="bad token or protocol")
+                ch.close()
+                return
+            nid = self._register(hdr, ch)
+            ch.send("WELCOME", node_id=nid, coordinator_id=self.id)
+        except (OSError, ConnectionError, ValueError):
+            ch.close()
+            return
+        self._conn_loop(nid, ch)
+
+    def _register(self, hdr: dict, ch: Channel) -> str:
+        with self.lock:
+            nid = hdr.get("node_id")
+            if nid and nid in self.nodes and not self.nodes[nid].dead:
+                n = self.nodes[nid]
+                n.ch, n.connected, n.disconnected_at = ch, True, None
+                n.last_heartbeat = time.time()
+                self._sync_slot(nid)
+                return nid
+            caps = hdr.get("caps", {})
+            nid = f"n{len(self.order)}-{caps.get('name', 'worker')}"
+            self.nodes[nid] = _Node(NodeInfo.from_caps(nid, caps), ch)
+            self.order.append(nid)
+            return nid
+
+    def _slot_of(self, nid):
+        for s, n in self.slot_node.items():
+            if n == nid:
+                return s
+        return None
+
+    def _sync_slot(self, nid):
+        s = self._slot_of(nid)
+        if s is not None and s in self.slots:
+            n = self.nodes[nid]
+            st = self.slots[s]
+            st.connected, st.disconnected_at = n.connected, n.disconnected_at
+            st.last_heartbeat, st.stage_alive = n.last_heartbeat, n.stage_alive
+
+    def _conn_loop(self, nid: str, ch: Channel):
+        while not self.stop_ev.is_set():
+            try:
+                hdr, body = ch.recv()
+            except (OSError, ConnectionError, ValueError):
+                with self.lock:
+                    n = self.nodes.get(nid)
+                    if n is not None and n.ch is ch:
+                        n.connected = False
+                        n.disconnected_at = time.time()
+                        self._sync_slot(nid)
+                return
+            self._dispatch(nid, hdr, body)
+
+    def _dispatch(self, nid: str, hdr: dict, body: bytes):
+        kind = hdr["kind"]
+        with self.lock:
+            n = self.nodes[nid]
+            slot = self._slot_of(nid)
+            st = self.slots.get(slot) if slot is not None else None
+            current = hdr.get("attempt") in (None, self.attempt)
+            if kind == "HEARTBEAT":
+                n.last_heartbeat = time.time()
+                n.stage_alive = hdr.get("stage_alive")
+                self._sync_slot(nid)
+            elif kind == "PROGRESS" and st is not None and current:
+                if st.add_progress(int(hdr["step"]), time.time(), self._final_step):
+                    if self.on_progress:
+                        self.on_progress(slot, int(hdr["step"]), nid)
+            elif kind == "EXIT" and st is not None and hdr.get("attempt") == self.attempt:
+                st.exit_code = int(hdr["rc"])
+                st.done_marker = bool(hdr["done_marker"])
+                st.log_tail = hdr.get("tail", "")
+            elif kind == "RESULT" and hdr.get("attempt") == self.attempt:
+                self.results[(hdr["stage"], hdr["peer"])] = hdr["losses"]
+            elif kind == "CKPT" and self.store is not None and hdr.get("run_id") == self.run_id:
+                if hashlib.sha256(body).hexdigest() == hdr.get("sha256"):
+                    rel = os.path.join(self.run_id, hdr["rel"])
+                    self.store.stage_part(rel, body)
+                    if hdr.get("last"):
+                        self.store.commit_staged(os.path.dirname(rel))
+            elif kind == "TELEM_STEP":
+                self.events.append(("telem", nid, hdr.get("telem")))
+            else:
+                self.events.append((kind, nid, {k: v for k, v in hdr.items() if k != "kind"}))
+
+    # ----------------------------------------------------------------- job
+    def wait_for_workers(self, n: int, timeout: float) -> list:
+        t0 = time.time()
+        while time.time() - t0 < timeout:
+            with self.lock:
+                live = [nid for nid in self.order if self.nodes[nid].connected and not self.nodes[nid].dead]
+            if len(live) >= n:
+                return live
+            time.sleep(0.1)
+        raise TimeoutError(f"only {len(live)} of {n} workers registered in {timeout:.0f}s")
+
+    def _spec_for(self, job: Job) -> JobSpec:
+        if job.spec is not None:
+            return job.spec
+        from elysium_wan_b200.scheduler.fleetplan import build_spec
+
+        with self.lock:
+            fleet = [self.nodes[n].info for n in self.order]
+        return build_spec(job.plan, job.stages, fleet)
+
+    def _place(self, spec: JobSpec, live: list) -> list:
+        """Slots in rank order take workers grouped by region (stable), the rest are spares."""
+        infos = [self.nodes[n].info for n in live]
+        why = mixed_fleet(infos)
+        if why:
+            raise ValueError(why)
+        if self.cfg.group_by == "region":
+            regions = []
+            for i in infos:
+                if i.region not in regions:
+                    regions.append(i.region)
+            live = sorted(live, key=lambda n: regions.index(self.nodes[n].info.region))
+        return live
+
+    def _links(self, spec: JobSpec):
+        links = []
+        for j in range(spec.stages):
+            link = {"latency_ms": 0.0, "bw_mbps": 0.0, "jitter_ms": 0.0, "jitter_seed": j}
+            if j + 1 < spec.stages:
+                a = self.nodes[self.slot_node[(j, 0)]].info
+                b = self.nodes[self.slot_node[(j + 1, 0)]].info
+                if a.region != b.region:
+                    key = "|".join(sorted([a.region, b.region]))
+                    link.update(self.cfg.wan_links.get(key, self.cfg.wan_links.get("*", {})))
+            links.append(link)
+        spec.links = links
+
+    def run_job(self, job: Job) -> RunResult:
+        spec = self._spec_for(job)
+        spec.zb_mem_mode = spec.zb_mem_mode or self.cfg.zb_mem_mode
+        spec.finalize()
+        self.run_id = time.strftime("%Y%m%d-%H%M%S") + "-" + uuid.uuid4().hex[:6]
+        run_dir = os.path.join(self.cfg.state_dir, "runs", self.run_id)
+        os.makedirs(run_dir, exist_ok=True)
+        self.store = ckpt.CheckpointStore(os.path.join(self.cfg.state_dir, "store"))
+        live = self.wait_for_workers(spec.world_size, self.cfg.wait_workers_s)
+        live = self._place(spec, live)
+        slots = spec.slots()
+        self.slot_node = {s: live[i] for i, s in enumerate(slots)}
+        spares = live[len(slots):]
+        self._links(spec)
+        spec.finalize()
+        self._final_step = spec.steps - 1
+        with open(os.path.join(run_dir, "spec.json"), "w") as f:
+            f.write(spec.to_json())
+        with open(os.path.join(run_dir, "rationale.json"), "w") as f:
+            json.dump({"placement": {f"{s[0]}:{s[1]}": self.slot_node[s] for s in slots},
+                       "spares": spares, "links": spec.links}, f, indent=1)
+        heals = restarts = 0
+        resume_step = None
+        t_start = time.time()
+        why = ""
+        while True:
+            self._launch(spec, resume_step)
+            verdict = self._monitor(spec, t_start)
+            if verdict.kind == "done":
+                losses = self._collect(spec, run_dir)
+                res = RunResult(True, self.run_id, losses, self.attempt + 1, heals, restarts, "",
+                                run_dir)
+                break
+            self._abort_all()
+            if verdict.kind == "convict" and heals < self.cfg.max_heals:
+                heals += 1
+                dead = self.slot_node[verdict.slot]
+                with self.lock:
+                    self.nodes[dead].dead = True
+                    cands = [self.nodes[n].info for n in spares if self.nodes[n].connected]
+                rep = find_replacement(self.nodes[dead].info, cands, self.cfg.replacement_match)
+                if rep is None:
+                    res = RunResult(False, self.run_id, None, self.attempt + 1, heals, restarts,
+                                    f"no spare for {verdict.slot}: {verdict.why}", run_dir)
+                    break
+                spares.remove(rep.node_id)
+                self.slot_node[verdict.slot] = rep.node_id
+                resume_step = self._resume_point(spec)
+                self._restore(spec, verdict.slot, rep.node_id, resume_step)
+                self.events.append(("heal", verdict.slot, {"from": dead, "to": rep.node_id,
+                                                           "step": resume_step, "why": verdict.why}))
+            elif verdict.kind == "stalled" and restarts < self.cfg.max_restarts:
+                restarts += 1
+                resume_step = self._resume_point(spec)
+                self.events.append(("restart", None, {"step": resume_step, "why": verdict.why}))
+            else:
+                why = verdict.why
+                res = RunResult(False, self.run_id, None, self.attempt + 1, heals, restarts, why, run_dir)
+                break
+            self.attempt += 1
+        with open(os.path.join(run_dir, "result.json"), "w") as f:
+            json.dump({"ok": res.ok, "run_id": res.run_id, "attempts": res.attempts, "heals": res.heals,
+                       "restarts": res.restarts, "why": res.why, "losses": res.losses_path,
+                       "events": [list(map(str, e)) for e in self.events if e[0] in ("heal", "restart")]},
+                      f, indent=1)
+        return res
+
+    def _resume_point(self, spec) -> int | None:
+        view = copy.copy(spec)
+        view.out_dir = os.path.join(self.store.root, self.run_id)
+        return ckpt.common_step(view)
+
+    def _restore(self, spec, slot, nid, step):
+        """Ship the slot's wave at `step` from the store to its new worker."""
+        if step is None:
+            return
+        stage, peer = slot
+        rel_dir = os.path.relpath(ckpt.wave_dir("", spec.tag, stage, peer, step), "")
+        src = os.path.join(self.store.root, self.run_id, rel_dir)
+        ch = self.nodes[nid].ch
+        names = sorted(os.listdir(src), key=lambda n: n == "wave.json")
+        for n in names:
+            with open(os.path.join(src, n), "rb") as f:
+                ch.send("RESTORE", f.read(), run_id=self.run_id, rel=os.path.join(rel_dir, n),
+                        last=(n == "wave.json"))
+
+    def _launch(self, spec: JobSpec, resume_step):
+        a = copy.deepcopy(spec)
+        a.port_base = _free_port()
+        a.resume = resume_step is not None
+        a.resume_step = resume_step
+        start = 0 if resume_step is None else resume_step
+        with self.lock:
+            self.results = {}
+            self.slots = {}
+            for s in spec.slots():
+                nid = self.slot_node[s]
+                n = self.nodes[nid]
+                self.slots[s] = SlotState(slot=s, node_id=nid, launched=True, connected=n.connected,
+                                          last_heartbeat=time.time(), started_at=time.time(),
+                                          start_step=start)
+        for s in reversed(spec.slots()):
+            self.nodes[self.slot_node[s]].ch.send(
+                "ASSIGN", spec=a.to_dict(), stage=s[0], peer=s[1], run_id=self.run_id,
+                attempt=self.attempt, timeout=self.cfg.stage_timeout_s)
+
+    def _monitor(self, spec, t_start):
+        judge = LivenessJudge(final_step=spec.steps - 1, **self.cfg.liveness)
+        while True:
+            time.sleep(self.cfg.poll_s)
+            with self.lock:
+                v = judge.judge(list(self.slots.values()))
+                if v.kind == "done":
+                    last = spec.stages - 1
+                    want = {(last, p) for p in range(spec.stage_widths[last])}
+                    if not want <= set(self.results):
+                        if time.time() - max(st.started_at for st in self.slots.values()) < 30:
+                            continue
+                    return v
+                if v.kind in ("convict", "stalled", "failed"):
+                    return v
+            if time.time() - t_start > self.cfg.job_timeout_s:
+                from elysium_wan_b200.fault_tolerance.liveness import Verdict
+
+                return Verdict("failed", None, "job timeout")
+
+    def _abort_all(self):
+        with self.lock:
+            for s, nid in self.slot_node.items():
+                n = self.nodes[nid]
+                if n.connected and not n.dead:
+                    try:
+                        n.ch.send("ABORT")
+                    except OSError:
+                        pass
+        time.sleep(0.5)
+
+    def _collect(self, spec, run_dir) -> str:
+        recs = []
+        for losses in self.results.values():
+            recs += losses
+        recs.sort(key=lambda r: (r["step"], r["mb"]))
+        p = os.path.join(run_dir, "losses.json")
+        with open(p, "w") as f:
+            json.dump({"losses": recs}, f, indent=1)
+        return p
+

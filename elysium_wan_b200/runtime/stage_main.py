@@ -116,8 +116,14 @@ def main(argv=None) -> int:
     try:
         spec = JobSpec.load(a.spec).finalize()
         rc = run_stage(spec, a.rank, a.peer, a.timeout)
-    except Exception:
+    except Exception as e:
         traceback.print_exc()
+        msg = str(e).lower()
+        # A neighbour that vanished surfaces as a transport error or timeout of
+        # a collective / p2p op; the liveness judge keys on this phrase.
+        if any(k in msg for k in ("connection", "closed", "reset", "timed out", "timeout",
+                                  "broken pipe", "nccl", "gloo")):
+            print(f"WT_ERROR peer connection lost: {e}", flush=True)
         rc = 1
     print(f"WT_DONE {rc}", flush=True)
     return rc
