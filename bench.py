@@ -34,6 +34,11 @@ import sys
 import tempfile
 import time
 
+# Every kernel is loaded when the CUDA context is created (before torch
+# initialises CUDA): a module loaded lazily while an NCCL receive is pending can
+# wait on that receive, a cross-rank deadlock.
+os.environ.setdefault("CUDA_MODULE_LOADING", "EAGER")
+
 ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
@@ -178,9 +183,11 @@ def run_ours(args) -> dict | None:
         os.environ.setdefault("TORCH_NCCL_ASYNC_ERROR_HANDLING", "1")
     spec = plan_spec(args, n, float(free))
     setup_determinism(spec.init_seed)
-    init_group(spec, rank, timeout_s=600.0)
+    init_group(spec, rank, timeout_s=float(os.environ.get("EWB_PG_TIMEOUT_S", "600")))
+    eng = StageEngine(spec, rank, 0, None, dev)
+    eng.warm_kernels()
     comm = PipeComm(spec, rank, 0, dev) if world > 1 else None
-    eng = StageEngine(spec, rank, 0, comm, dev)
+    eng.attach_comm(comm)
     torch.cuda.synchronize()
 
     def barrier():

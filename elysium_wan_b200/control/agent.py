@@ -223,6 +223,7 @@ class WorkerAgent:
         from elysium_wan_b200.utils.determinism import PINNED_ENV
 
         env.update(PINNED_ENV)
+        env.setdefault("CUDA_MODULE_LOADING", "EAGER")
         env["PYTHONPATH"] = ROOT + os.pathsep + env.get("PYTHONPATH", "")
         cmd = [sys.executable, "-m", "elysium_wan_b200.runtime.stage_main", "--spec", sp,
                "--rank", str(stage), "--peer", str(peer), "--timeout", str(hdr.get("timeout", 120))]

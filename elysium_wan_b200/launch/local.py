@@ -44,6 +44,9 @@ def run_local(spec, timeout: float = 1800.0, log_dir: str | None = None, extra_e
     env = pinned_env()
     root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
     env["PYTHONPATH"] = root + os.pathsep + env.get("PYTHONPATH", "")
+    # Load every kernel at context creation: a module loaded lazily while an
+    # NCCL receive is pending can wait on that receive (cross-rank deadlock).
+    env.setdefault("CUDA_MODULE_LOADING", "EAGER")
     if extra_env:
         env.update(extra_env)
     procs = []

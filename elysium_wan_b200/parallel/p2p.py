@@ -17,10 +17,20 @@ plus serialisation at the link rate, seeded jitter.
 
 from __future__ import annotations
 
+import os
 import queue
 import random
+import sys
 import threading
 import time
+
+_DEBUG = os.environ.get("EWB_DEBUG") == "1"
+
+
+def dbg(msg: str):
+    """Opt-in trace of communication steps (EWB_DEBUG=1) to stderr."""
+    if _DEBUG:
+        print(f"[ewb {time.monotonic():.3f} pid {os.getpid()}] {msg}", file=sys.stderr, flush=True)
 
 import torch
 import torch.distributed as dist
@@ -85,10 +95,18 @@ class PipeComm:
         self.spec, self.stage, self.peer, self.device = spec, stage, peer, torch.device(device)
         self.rank = spec.rank_of(stage, peer)
         world = spec.world_size
-        ranks = list(range(world))
-        # Every rank creates the same groups in the same order.
-        self.g_fwd = dist.new_group(ranks) if world > 1 else None
-        self.g_bwd = dist.new_group(ranks) if world > 1 else None
+        # One group per pipeline hop and direction (the ranks of stages j and
+        # j+1). With NCCL's eager initialisation every group owns one
+        # communicator and one stream and runs its point-to-point ops in issue
+        # order; separate groups keep a middle stage's receive from upstream,
+        # send downstream, and the two gradient directions independent.
+        # Every rank creates every group in the same order.
+        self.hop_fwd, self.hop_bwd = [], []
+        for j in range(spec.stages - 1):
+            ranks = [spec.rank_of(j, p) for p in range(spec.stage_widths[j])] + \
+                    [spec.rank_of(j + 1, q) for q in range(spec.stage_widths[j + 1])]
+            self.hop_fwd.append(dist.new_group(ranks) if world > 1 else None)
+            self.hop_bwd.append(dist.new_group(ranks) if world > 1 else None)
         self.g_stage = None
         for r, w in enumerate(spec.stage_widths):
             g = dist.new_group([spec.rank_of(r, q) for q in range(w)]) if world > 1 else None
@@ -106,6 +124,57 @@ class PipeComm:
         self.shim_prev = _Shim(back) if not self.cuda else None
         self.bytes_sent = 0
         self.frames = 0
+        if world > 1:
+            self._init_pairs()
+
+    # groups this slot uses
+    @property
+    def g_act_in(self):
+        return self.hop_fwd[self.stage - 1]
+
+    @property
+    def g_act_out(self):
+        return self.hop_fwd[self.stage]
+
+    @property
+    def g_grad_in(self):
+        return self.hop_bwd[self.stage]
+
+    @property
+    def g_grad_out(self):
+        return self.hop_bwd[self.stage - 1]
+
+    def _init_pairs(self):
+        """Create every communicator up front, in one global order.
+
+        A communicator is built on the first operation of its group and that
+        build blocks until every member joins; built lazily, stage r's early
+        gradient receive (hop r backward) would wait for stage r+1 while stage
+        r+1 waits for stage r's activation (hop r forward): a deadlock. Here
+        every rank walks the same list of (group, sender, receiver) and
+        exchanges one element on each entry it belongs to; the earliest
+        unfinished entry always has both of its ranks ready, so the walk
+        cannot deadlock."""
+        spec = self.spec
+        steps = []
+        for j in range(spec.stages - 1):
+            for group in (self.hop_fwd[j], self.hop_bwd[j]):
+                for p in range(spec.stage_widths[j]):
+                    for q in range(spec.stage_widths[j + 1]):
+                        steps.append((group, spec.rank_of(j, p), spec.rank_of(j + 1, q)))
+        t = torch.zeros(1, dtype=torch.float32, device=self.device)
+        for i, (group, a, b) in enumerate(steps):
+            if self.rank == a:
+                dbg(f"rank {self.rank} init pair {i}: send to {b}")
+                dist.send(t, b, group=group)
+            elif self.rank == b:
+                dbg(f"rank {self.rank} init pair {i}: recv from {a}")
+                dist.recv(t, a, group=group)
+        dbg(f"rank {self.rank} init pairs done")
+        if self.g_stage is not None and self.spec.stage_widths[self.stage] > 1:
+            dist.barrier(group=self.g_stage)
+        if self.cuda:
+            torch.cuda.synchronize(self.device)
 
     # ----------------------------------------------------------------- routing
     def next_rank(self, mb: int) -> int:
@@ -143,26 +212,30 @@ class PipeComm:
         return [dist.isend(t, dst, group=group) for t in tensors]
 
     def send_act(self, mb: int, act: Act):
+        dbg(f"rank {self.rank} send act mb {mb} -> {self.next_rank(mb)}")
         ts = act.tensors()
         if self.fp8:
             ts = [ts[0].view(torch.uint8), ts[1]]
-        return self._send([t.contiguous() for t in ts], self.next_rank(mb), self.g_fwd,
+        return self._send([t.contiguous() for t in ts], self.next_rank(mb), self.g_act_out,
                           self.shim_next)
 
     def send_grad(self, mb: int, g: torch.Tensor):
+        dbg(f"rank {self.rank} send grad mb {mb} -> {self.prev_rank(mb)}")
         g = g.to(self.act_dtype).contiguous()
-        return self._send([g], self.prev_rank(mb), self.g_bwd, self.shim_prev)
+        return self._send([g], self.prev_rank(mb), self.g_grad_out, self.shim_prev)
 
     # ----------------------------------------------------------------- receives
     def irecv_act(self, mb: int):
         bufs = self._act_buffers()
         src = self.prev_rank(mb)
-        works = [dist.irecv(b, src, group=self.g_fwd) for b in bufs]
+        dbg(f"rank {self.rank} post recv act mb {mb} <- {src}")
+        works = [dist.irecv(b, src, group=self.g_act_in) for b in bufs]
         return bufs, works
 
     def irecv_grad(self, mb: int):
         buf = self._grad_buffer()
-        return [buf], [dist.irecv(buf, self.next_rank(mb), group=self.g_bwd)]
+        dbg(f"rank {self.rank} post recv grad mb {mb} <- {self.next_rank(mb)}")
+        return [buf], [dist.irecv(buf, self.next_rank(mb), group=self.g_grad_in)]
 
     @staticmethod
     def wait(handle):

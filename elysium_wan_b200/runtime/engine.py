@@ -22,6 +22,7 @@ import torch
 
 from elysium_wan_b200.models.data import make_batch
 from elysium_wan_b200.models.gpt import Act, StageModel
+from elysium_wan_b200.parallel.p2p import dbg
 from elysium_wan_b200.runtime import optim
 
 
@@ -44,8 +45,15 @@ class StageEngine:
         self.events: list = []  # per-op (op, mb, start_event, end_event)
         self.timing = spec.device_for(stage, peer).startswith("cuda")
         self.telemetry: list = []
+        self._host_x = None
         self.zero1 = None
-        if self.width > 1:
+        if comm is not None:
+            self.attach_comm(comm)
+
+    def attach_comm(self, comm):
+        """Bind the stage channels (after warm_kernels, before the first step)."""
+        self.comm = comm
+        if self.width > 1 and self.zero1 is None:
             from elysium_wan_b200.parallel.zero1 import Zero1
 
             self.zero1 = Zero1(self, comm)
@@ -59,14 +67,61 @@ class StageEngine:
         return self.model.last
 
     # ----------------------------------------------------------------- data
-    def _batch(self, step: int, mb: int):
+    def _stage_batches(self, step: int, mbs: list) -> dict:
+        """The step's token ids and targets, generated on the host (the data
+        rule is a CPU generator), written into pinned staging buffers that are
+        allocated once, and copied to the device in one transfer each.
+
+        No pinned allocation ever happens inside a step: allocating pinned
+        memory can wait on the whole device, and a device-wide wait while a
+        receive from a neighbouring stage is pending deadlocks the pipeline."""
         s = self.spec
-        x, t = make_batch(s.data_seed, step, mb, s.mb_size, s.model.seq_len, s.model.vocab_size,
-                          dataset=s.dataset_path, data_shards=s.data_shards)
+        shape = (len(mbs), s.mb_size, s.model.seq_len)
+        if self._host_x is None or self._host_x.shape != shape:
+            pin = self.device.type == "cuda"
+            self._host_x = torch.empty(shape, dtype=torch.int64, pin_memory=pin)
+            self._host_t = torch.empty(shape, dtype=torch.int64, pin_memory=pin)
+            self._dev_x = torch.empty(shape, dtype=torch.int64, device=self.device)
+            self._dev_t = torch.empty(shape, dtype=torch.int64, device=self.device)
+        for i, mb in enumerate(mbs):
+            x, t = make_batch(s.data_seed, step, mb, s.mb_size, s.model.seq_len, s.model.vocab_size,
+                              dataset=s.dataset_path, data_shards=s.data_shards)
+            self._host_x[i].copy_(x)
+            self._host_t[i].copy_(t)
         if self.device.type == "cuda":
-            x = x.pin_memory().to(self.device, non_blocking=True)
-            t = t.pin_memory().to(self.device, non_blocking=True)
-        return x, t
+            self._dev_x.copy_(self._host_x, non_blocking=True)
+            self._dev_t.copy_(self._host_t, non_blocking=True)
+            xs, ts = self._dev_x, self._dev_t
+        else:
+            xs, ts = self._host_x.clone(), self._host_t.clone()
+        return {mb: (xs[i], ts[i]) for i, mb in enumerate(mbs)}
+
+    def warm_kernels(self):
+        """Run one F, B and W on a dummy microbatch so every kernel of the
+        stage is loaded and configured before the first NCCL operation (module
+        loading and first-launch set-up must not happen while a receive is
+        pending). Touches only gradients, which every step zeroes."""
+        s = self.spec
+        T = s.mb_size * s.model.seq_len
+        x = torch.zeros((s.mb_size, s.model.seq_len), dtype=torch.int64, device=self.device)
+        if self.first:
+            inp = x
+        else:
+            from elysium_wan_b200 import ops
+
+            dt = torch.bfloat16 if self.device.type == "cuda" else torch.float32
+            z = torch.zeros((T, s.model.d_model), dtype=dt, device=self.device)
+            inp = Act(*ops.quant_e4m3(z)) if s.model.fp8_boundary() else Act(z)
+        out, st = self.model.forward(inp, x if self.last else None)
+        dt = torch.bfloat16 if self.device.type == "cuda" else torch.float32
+        dy = None if self.last else torch.zeros((T, s.model.d_model), dtype=dt, device=self.device)
+        tasks: list = []
+        self.model.backward(st, dy, tasks)
+        for t in tasks:
+            t.run()
+        self.store.zero_grad()
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
 
     # ----------------------------------------------------------------- one step
     def run_step(self, step: int) -> list:
@@ -77,6 +132,7 @@ class StageEngine:
         self.store.zero_grad()
         f_mbs = [mb for op, mb in self.order if op == "F"]
         b_mbs = [mb for op, mb in self.order if op == "B"]
+        batches = self._stage_batches(step, f_mbs) if (self.first or self.last) else {}
         act_q: dict = {}
         grad_q: dict = {}
         fi = bi = 0
@@ -84,10 +140,6 @@ class StageEngine:
             act_q[f_mbs[0]] = comm.irecv_act(f_mbs[0])
         if not self.last:
             grad_q[b_mbs[0]] = comm.irecv_grad(b_mbs[0])
-        batches = {}
-        if self.first or self.last:
-            for mb in f_mbs:
-                batches[mb] = self._batch(step, mb)
         saved: dict = {}
         wq: dict = {}
         sends: list = []
@@ -99,6 +151,7 @@ class StageEngine:
         for idx, (op, mb) in enumerate(self.order):
             if op == "W" and mb in inline_done:
                 continue
+            dbg(f"stage {self.stage} op {op}{mb} start")
             if ev:
                 e0 = torch.cuda.Event(enable_timing=True)
                 e0.record()
@@ -144,6 +197,7 @@ class StageEngine:
                 e1 = torch.cuda.Event(enable_timing=True)
                 e1.record()
                 self.events.append((op, mb, e0, e1))
+        dbg(f"stage {self.stage} ops done; waiting {len(sends)} sends")
         for w in sends:
             w.wait()
         if comm is not None:

@@ -29,6 +29,9 @@ def init_group(spec, rank: int, timeout_s: float):
     backend = "nccl" if spec.backend == "nccl" else "gloo"
     if spec.world_size == 1:
         return
+    # Point-to-point ops are serialised per group by design (one group per hop
+    # and direction); the warning about it is noise here.
+    os.environ.setdefault("TORCH_NCCL_SHOW_EAGER_INIT_P2P_SERIALIZATION_WARNING", "false")
     if "MASTER_ADDR" in os.environ and "WORLD_SIZE" in os.environ:
         init = "env://"
     else:

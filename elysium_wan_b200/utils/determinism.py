@@ -31,6 +31,9 @@ def setup_determinism(seed: int = 0):
     np.random.seed(seed % (2 ** 32))
     torch.manual_seed(seed)
     torch.use_deterministic_algorithms(True, warn_only=True)
+    # Deterministic mode NaN-fills every torch.empty; the kernels here write
+    # every element they later read, so that fill is pure overhead.
+    torch.utils.deterministic.fill_uninitialized_memory = False
     torch.backends.cuda.matmul.allow_tf32 = False
     torch.backends.cudnn.allow_tf32 = False
     torch.set_num_threads(1)
