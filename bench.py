@@ -182,6 +182,9 @@ def run_ours(args) -> dict | None:
     if world > 1:
         os.environ.setdefault("TORCH_NCCL_ASYNC_ERROR_HANDLING", "1")
     spec = plan_spec(args, n, float(free))
+    # W GEMMs on a side stream need memory headroom (deferred frees); a stage
+    # that keeps its AdamW moments on the host has none.
+    os.environ.setdefault("EWB_W_STREAM", "0" if spec.optimizer == "adamw-host" else "1")
     setup_determinism(spec.init_seed)
     init_group(spec, rank, timeout_s=float(os.environ.get("EWB_PG_TIMEOUT_S", "600")))
     eng = StageEngine(spec, rank, 0, None, dev)
@@ -199,8 +202,10 @@ def run_ours(args) -> dict | None:
         eng.run_step(s)
         torch.cuda.synchronize()
         if rank == 0:
+            ms = torch.cuda.memory_stats()
             print(f"[bench] warm-up step {s}: {time.perf_counter() - t:.2f} s "
-                  f"(max alloc {torch.cuda.max_memory_allocated() / 2**30:.1f} GiB)",
+                  f"(max alloc {torch.cuda.max_memory_allocated() / 2**30:.1f} GiB, "
+                  f"alloc retries {ms.get('num_alloc_retries', 0)}, phases {eng.phase_ms()})",
                   file=sys.stderr, flush=True)
     torch.cuda.synchronize()
     st = ops.ext().status_read_clear()

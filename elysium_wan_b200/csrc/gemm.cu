@@ -41,15 +41,26 @@ constexpr int kBK = 64;
 constexpr int kThreads = 192;
 constexpr int kGroupM = 16;
 
-template <int BN>
+// Epilogues whose output leaves through shared memory and TMA (bf16 / fp32
+// stores, fp32 reduce-add); the others store from registers.
+template <int EPI>
+struct EpiTraits {
+  static constexpr bool kTma = (EPI == kEpiBf16 || EPI == kEpiF32 || EPI == kEpiAccF32);
+  static constexpr int kOutBytes = kTma ? 2 * 16384 : 0;  // two staging buffers
+};
+
+template <int BN, int EPI>
 struct GemmCfg {
   static constexpr int A_BYTES = kBM * kBK * 2;
   static constexpr int B_BYTES = BN * kBK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (BN == 256) ? 4 : 6;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int OUT_BYTES = EpiTraits<EPI>::kOutBytes;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + OUT_BYTES + 1024 /*align*/ + 256 /*barriers*/;
   static constexpr int TMEM_COLS = 2 * BN;
 };
+
+constexpr int kTileQueue = 4;  // depth of the producer -> MMA/epilogue tile-id ring
 
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
   const int per_group = kGroupM * num_n;
@@ -96,56 +107,67 @@ __device__ __forceinline__ void store_bf16_32(__nv_bfloat16* dst, const float* f
   }
 }
 
+// Register epilogues (everything but the TMA-staged kinds). `taddr` is this
+// warp's TMEM lane quarter of the accumulator; `gm` this thread's row.
 template <int EPI, int BN>
-__device__ __forceinline__ void epilogue_tile(uint32_t taddr, int gm, int nbase, int M, int N,
-                                              const GemmEpilogue& ep) {
+__device__ __forceinline__ void epilogue_tile_regs(uint32_t taddr, int gm, int nbase, int M, int N,
+                                                   const GemmEpilogue& ep) {
   const bool row_ok = gm < M;
   if constexpr (EPI == kEpiResidQ8) {
-    // fp8 e4m3 with one power-of-two scale per 128 columns of a row.
+    // fp8 e4m3 with one power-of-two scale per 128 columns of a row, in two
+    // passes over TMEM (amax, then quantise) so no 128-value array is held.
     const int nblk = ep.ld_scale_out;
 #pragma unroll 1
     for (int c = 0; c < BN; c += 128) {
-      float y[128];
-#pragma unroll
+      const int n0 = nbase + c;
+      float amax = 0.f;
+#pragma unroll 1
       for (int j = 0; j < 4; ++j) {
         uint32_t v[32];
         tmem_ld32(taddr + c + 32 * j, v);
         tmem_wait_ld();
+        if (row_ok && n0 < N) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) y[32 * j + i] = __uint_as_float(v[i]);
-      }
-      const int n0 = nbase + c;
-      if (row_ok && n0 < N) {
-        float amax = 0.f;
-#pragma unroll
-        for (int i = 0; i < 128; ++i) {
-          const int n = n0 + i;
-          const float b = ep.bias ? ep.bias[n] : 0.f;
-          y[i] = resid_at(ep, gm, n) + (y[i] + b);
-          amax = fmaxf(amax, fabsf(y[i]));
+          for (int i = 0; i < 32; ++i) {
+            const int n = n0 + 32 * j + i;
+            const float b = ep.bias ? ep.bias[n] : 0.f;
+            amax = fmaxf(amax, fabsf(resid_at(ep, gm, n) + (__uint_as_float(v[i]) + b)));
+          }
         }
-        const float scale = e4m3_block_scale(amax);
-        const float inv = 1.0f / scale;  // exact: scale is a power of two
-        uint8_t* dst = reinterpret_cast<uint8_t*>(ep.out) + static_cast<size_t>(gm) * ep.ldo + n0;
-        uint4* d4 = reinterpret_cast<uint4*>(dst);
+      }
+      const float scale = e4m3_block_scale(amax);
+      const float inv = 1.0f / scale;  // exact: scale is a power of two
+#pragma unroll 1
+      for (int j = 0; j < 4; ++j) {
+        uint32_t v[32];
+        tmem_ld32(taddr + c + 32 * j, v);
+        tmem_wait_ld();
+        if (row_ok && n0 < N) {
+          uint32_t w[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          uint32_t w[4];
+          for (int h = 0; h < 8; ++h) {
+            float y[4];
 #pragma unroll
-          for (int h = 0; h < 4; ++h) {
-            const int i = 16 * j + 4 * h;
-            const __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(
-                make_float2(y[i] * inv, y[i + 1] * inv), __NV_SATFINITE, __NV_E4M3);
-            const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(
-                make_float2(y[i + 2] * inv, y[i + 3] * inv), __NV_SATFINITE, __NV_E4M3);
+            for (int e = 0; e < 4; ++e) {
+              const int i = 4 * h + e;
+              const int n = n0 + 32 * j + i;
+              const float b = ep.bias ? ep.bias[n] : 0.f;
+              y[e] = (resid_at(ep, gm, n) + (__uint_as_float(v[i]) + b)) * inv;
+            }
+            const __nv_fp8x2_storage_t lo =
+                __nv_cvt_float2_to_fp8x2(make_float2(y[0], y[1]), __NV_SATFINITE, __NV_E4M3);
+            const __nv_fp8x2_storage_t hi =
+                __nv_cvt_float2_to_fp8x2(make_float2(y[2], y[3]), __NV_SATFINITE, __NV_E4M3);
             w[h] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
           }
-          d4[j] = make_uint4(w[0], w[1], w[2], w[3]);
+          uint4* d4 = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(ep.out) +
+                                               static_cast<size_t>(gm) * ep.ldo + n0 + 32 * j);
+          d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
+          d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
         }
-        ep.scale_out[static_cast<size_t>(gm) * nblk + (n0 >> 7)] = scale;
       }
+      if (row_ok && n0 < N) ep.scale_out[static_cast<size_t>(gm) * nblk + (n0 >> 7)] = scale;
     }
-    return;
   } else {
 #pragma unroll 1
     for (int c = 0; c < BN; c += 32) {
@@ -158,84 +180,120 @@ __device__ __forceinline__ void epilogue_tile(uint32_t taddr, int gm, int nbase,
       float f[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(v[i]);
-      if constexpr (EPI == kEpiAccF32) {
-        float* dst = reinterpret_cast<float*>(ep.out) + static_cast<size_t>(gm) * ep.ldo + n0;
-        if (valid >= 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-          float4* d4 = reinterpret_cast<float4*>(dst);
+      if (ep.bias != nullptr && EPI != kEpiDGelu) {
+        const float* bp = ep.bias + n0;
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            float4 o = make_float4(f[4 * j], f[4 * j + 1], f[4 * j + 2], f[4 * j + 3]);
-            if (ep.beta != 0.f) {
-              const float4 p = d4[j];
-              o.x = p.x + o.x;
-              o.y = p.y + o.y;
-              o.z = p.z + o.z;
-              o.w = p.w + o.w;
-            }
-            d4[j] = o;
-          }
-        } else {
-          for (int i = 0; i < valid; ++i) dst[i] = (ep.beta != 0.f) ? dst[i] + f[i] : f[i];
-        }
-      } else if constexpr (EPI == kEpiF32) {
-        float* dst = reinterpret_cast<float*>(ep.out) + static_cast<size_t>(gm) * ep.ldo + n0;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          if (i < valid) {
-            const float b = ep.bias ? ep.bias[n0 + i] : 0.f;
-            dst[i] = f[i] + b;
-          }
-        }
-      } else {
-        if (ep.bias != nullptr && EPI != kEpiDGelu) {
-          const float* bp = ep.bias + n0;
-#pragma unroll
-          for (int i = 0; i < 32; ++i) f[i] += (i < valid) ? bp[i] : 0.f;
-        }
-        if constexpr (EPI == kEpiGelu) {
-          // aux keeps the bf16 pre-activation u for the backward; out = gelu(u).
-          __nv_bfloat16* aux =
-              reinterpret_cast<__nv_bfloat16*>(ep.aux) + static_cast<size_t>(gm) * ep.ldaux + n0;
-#pragma unroll
-          for (int i = 0; i < 32; ++i) f[i] = bf16_round(f[i]);
-          store_bf16_32(aux, f, valid);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) f[i] = gelu_erf(f[i]);
-        } else if constexpr (EPI == kEpiDGelu) {
-          const __nv_bfloat16* aux = reinterpret_cast<const __nv_bfloat16*>(ep.aux) +
-                                     static_cast<size_t>(gm) * ep.ldaux + n0;
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (i < valid) f[i] = f[i] * gelu_erf_grad(ld_bf16(aux + i));
-        } else if constexpr (EPI == kEpiResid) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (i < valid) f[i] = resid_at(ep, gm, n0 + i) + f[i];
-        }
-        __nv_bfloat16* dst =
-            reinterpret_cast<__nv_bfloat16*>(ep.out) + static_cast<size_t>(gm) * ep.ldo + n0;
-        store_bf16_32(dst, f, valid);
+        for (int i = 0; i < 32; ++i) f[i] += (i < valid) ? bp[i] : 0.f;
       }
+      if constexpr (EPI == kEpiGelu) {
+        // aux keeps the bf16 pre-activation u for the backward; out = gelu(u).
+        __nv_bfloat16* aux =
+            reinterpret_cast<__nv_bfloat16*>(ep.aux) + static_cast<size_t>(gm) * ep.ldaux + n0;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) f[i] = bf16_round(f[i]);
+        store_bf16_32(aux, f, valid);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) f[i] = gelu_erf(f[i]);
+      } else if constexpr (EPI == kEpiDGelu) {
+        const __nv_bfloat16* aux = reinterpret_cast<const __nv_bfloat16*>(ep.aux) +
+                                   static_cast<size_t>(gm) * ep.ldaux + n0;
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (i < valid) f[i] = f[i] * gelu_erf_grad(ld_bf16(aux + i));
+      } else if constexpr (EPI == kEpiResid) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (i < valid) f[i] = resid_at(ep, gm, n0 + i) + f[i];
+      }
+      __nv_bfloat16* dst =
+          reinterpret_cast<__nv_bfloat16*>(ep.out) + static_cast<size_t>(gm) * ep.ldo + n0;
+      store_bf16_32(dst, f, valid);
     }
+  }
+}
+
+// TMA-staged epilogue: each 128-byte-wide column chunk of the tile (32 fp32 or
+// 64 bf16 columns x 128 rows) goes TMEM -> registers -> 128B-swizzled shared
+// memory -> one bulk tensor store (or fp32 reduce-add for the gradient fold).
+// Two staging buffers alternate; `leader` is the one thread that issues and
+// tracks the bulk groups. Each output element receives exactly one store or
+// add per launch, so the fold stays deterministic.
+template <int EPI, int BN>
+__device__ __forceinline__ void epilogue_tile_tma(uint32_t taddr, int row, int m0, int nbase, int N,
+                                                  const GemmEpilogue& ep, const CUtensorMap* tmC,
+                                                  uint8_t* out_smem, bool leader, int& chunk) {
+  constexpr int CW = (EPI == kEpiBf16) ? 64 : 32;
+  const bool reduce = (EPI == kEpiAccF32) && ep.beta != 0.f;
+#pragma unroll 1
+  for (int c = 0; c < BN; c += CW) {
+    float f[CW];
+#pragma unroll
+    for (int j = 0; j < CW / 32; ++j) {
+      uint32_t v[32];
+      tmem_ld32(taddr + c + 32 * j, v);
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) f[32 * j + i] = __uint_as_float(v[i]);
+    }
+    const int n0 = nbase + c;
+    if (EPI != kEpiAccF32 && ep.bias != nullptr) {
+#pragma unroll
+      for (int i = 0; i < CW; ++i) f[i] += (n0 + i < N) ? ep.bias[n0 + i] : 0.f;
+    }
+    uint8_t* buf = out_smem + (chunk & 1) * 16384;
+    if (leader) bulk_wait_read<1>();  // this buffer's store from two chunks ago has read it
+    named_bar_sync(1, 128);
+    uint8_t* rowp = buf + row * 128;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      uint4 w;
+      if constexpr (EPI == kEpiBf16) {
+        w.x = pack_bf16x2(f[8 * j + 0], f[8 * j + 1]);
+        w.y = pack_bf16x2(f[8 * j + 2], f[8 * j + 3]);
+        w.z = pack_bf16x2(f[8 * j + 4], f[8 * j + 5]);
+        w.w = pack_bf16x2(f[8 * j + 6], f[8 * j + 7]);
+      } else {
+        w.x = __float_as_uint(f[4 * j + 0]);
+        w.y = __float_as_uint(f[4 * j + 1]);
+        w.z = __float_as_uint(f[4 * j + 2]);
+        w.w = __float_as_uint(f[4 * j + 3]);
+      }
+      *reinterpret_cast<uint4*>(rowp + ((j ^ (row & 7)) << 4)) = w;
+    }
+    fence_proxy_async_smem();
+    named_bar_sync(1, 128);
+    if (leader) {
+      if (reduce)
+        tma_reduce_add_2d(tmC, buf, n0, m0);
+      else
+        tma_store_2d(tmC, buf, n0, m0);
+      bulk_commit();
+    }
+    ++chunk;
   }
 }
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
-                        const __grid_constant__ CUtensorMap tmB, const GemmEpilogue ep, int M,
-                        int N, int K, int* status) {
-  using Cfg = GemmCfg<BN>;
+                        const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmC, const GemmEpilogue ep, int M,
+                        int N, int K, int* status, int* sched) {
+  using Cfg = GemmCfg<BN, EPI>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint8_t* out_smem = smem + STAGES * Cfg::STAGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(out_smem + Cfg::OUT_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* tq_full = drain + 1;
+  uint64_t* tq_empty = tq_full + kTileQueue;
+  int* tile_ring = reinterpret_cast<int*>(tq_empty + kTileQueue);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tile_ring + kTileQueue);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -250,9 +308,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tempty[b], 4);
     }
     mbar_init(drain, 1);
+    for (int q = 0; q < kTileQueue; ++q) {
+      mbar_init(&tq_full[q], 1);
+      mbar_init(&tq_empty[q], 5);  // the MMA thread + the four epilogue warps
+    }
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (EpiTraits<EPI>::kTma) tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
@@ -268,11 +331,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int num_tiles = num_m * num_n;
   const int kblocks = (K + kBK - 1) / kBK;
 
+  // Tiles are claimed dynamically from sched[0]; the claimed id travels to the
+  // MMA and epilogue roles through a small ring guarded by mbarriers; -1 ends.
+  auto next_tile = [&](int k) -> int {
+    const int q = k % kTileQueue;
+    if (!mbar_wait(&tq_full[q], (k / kTileQueue) & 1, status, kStatusTimeoutSmemFull)) return -1;
+    return *reinterpret_cast<volatile int*>(&tile_ring[q]);
+  };
+
   if (warp == 0) {
     if (lane == 0) {
       int it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      for (int k = 0; ok; ++k) {
+        int t = atomicAdd(&sched[0], 1);
+        if (t >= num_tiles) t = -1;
+        const int q = k % kTileQueue;
+        if (!mbar_wait(&tq_empty[q], ((k / kTileQueue) & 1) ^ 1, status, kStatusTimeoutSmemEmpty)) {
+          ok = false;
+          break;
+        }
+        tile_ring[q] = t;
+        mbar_arrive(&tq_full[q]);
+        if (t < 0) break;
         int mb, nb;
         tile_coords(t, num_m, num_n, mb, nb);
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
@@ -304,7 +385,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) {
         for (int j = 0; j < STAGES && j < it; ++j) {
           const int i2 = it - 1 - j;
-          mbar_wait(&full[i2 % STAGES], (i2 / STAGES) & 1, nullptr, 0);
+          mbar_wait(&full[i2 % STAGES], (i2 / STAGES) & 1, nullptr, kStatusTimeoutDrain);
         }
       }
     }
@@ -312,11 +393,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t IDESC = idesc_bf16_f32(kBM, BN, A_MN, B_MN);
       int it = 0;
-      int local = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
-        const int b = local & 1;
-        const uint32_t use = static_cast<uint32_t>(local >> 1);
+      for (int k = 0; ok; ++k) {
+        const int t = next_tile(k);
+        mbar_arrive(&tq_empty[k % kTileQueue]);
+        if (t < 0) break;
+        const int b = k & 1;
+        const uint32_t use = static_cast<uint32_t>(k >> 1);
         if (!mbar_wait(&tempty[b], (use & 1) ^ 1, status, kStatusTimeoutTmemEmpty)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * BN);
@@ -349,21 +432,32 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     const int q = warp & 3;
     const int row = q * 32 + lane;
-    int local = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+    const bool leader = (warp == 2 && lane == 0);
+    int chunk = 0;
+    for (int k = 0;; ++k) {
+      const int t = next_tile(k);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tq_empty[k % kTileQueue]);
+      if (t < 0) break;
       int mb, nb;
       tile_coords(t, num_m, num_n, mb, nb);
-      const int b = local & 1;
-      const uint32_t use = static_cast<uint32_t>(local >> 1);
+      const int b = k & 1;
+      const uint32_t use = static_cast<uint32_t>(k >> 1);
       if (!mbar_wait(&tfull[b], use & 1, status, kStatusTimeoutTmemFull)) break;
       tc_fence_after();
       const uint32_t taddr =
           tmem_base + static_cast<uint32_t>(b * BN) + (static_cast<uint32_t>(q * 32) << 16);
-      epilogue_tile<EPI, BN>(taddr, mb * kBM + row, nb * BN, M, N, ep);
+      if constexpr (EpiTraits<EPI>::kTma) {
+        epilogue_tile_tma<EPI, BN>(taddr, row, mb * kBM, nb * BN, N, ep, &tmC, out_smem, leader,
+                                   chunk);
+      } else {
+        epilogue_tile_regs<EPI, BN>(taddr, mb * kBM + row, nb * BN, M, N, ep);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[b]);
     }
+    if (EpiTraits<EPI>::kTma && leader) bulk_wait<0>();
   }
 
   tc_fence_before();
@@ -371,6 +465,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+  // The last CTA to finish resets the tile counter for the next launch on this
+  // stream (launches on one stream are ordered, so no other CTA can still read it).
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int done = atomicAdd(&sched[1], 1);
+    if (done == static_cast<int>(gridDim.x) - 1) {
+      sched[0] = 0;
+      sched[1] = 0;
+      __threadfence();
+    }
   }
 }
 
@@ -394,18 +499,25 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// bf16 2D map: `inner` contiguous elements per row, `outer` rows, row stride ld.
-bool make_map_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t ld,
-                   uint32_t box_inner, uint32_t box_outer) {
+// 2D map: `inner` contiguous elements per row, `outer` rows, row stride `ld`
+// elements of `esize` bytes, 128-byte swizzle.
+bool make_map(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* base, uint64_t inner,
+              uint64_t outer, uint64_t ld, uint32_t box_inner, uint32_t box_outer) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return false;
   cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {ld * 2};
+  cuuint64_t strides[1] = {ld * static_cast<uint64_t>(esize)};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
-            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+  return fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool make_map_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t ld,
+                   uint32_t box_inner, uint32_t box_outer) {
+  return make_map(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, inner, outer, ld, box_inner,
+                  box_outer);
 }
 
 int num_sms_cached() {
@@ -417,6 +529,29 @@ int num_sms_cached() {
   return sms[dev];
 }
 
+// Tile-scheduler counters: two ints per (device, stream), zeroed once; each
+// launch leaves them zeroed for the next launch on the same stream.
+constexpr int kSchedSlots = 256;
+int* sched_counters(cudaStream_t stream) {
+  static std::mutex mu;
+  static int* base[64] = {nullptr};
+  static cudaStream_t owner[64][kSchedSlots];
+  static int used[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (base[dev] == nullptr) {
+    if (cudaMalloc(&base[dev], kSchedSlots * 2 * sizeof(int)) != cudaSuccess) return nullptr;
+    if (cudaMemset(base[dev], 0, kSchedSlots * 2 * sizeof(int)) != cudaSuccess) return nullptr;
+  }
+  for (int i = 0; i < used[dev]; ++i)
+    if (owner[dev][i] == stream) return base[dev] + 2 * i;
+  if (used[dev] >= kSchedSlots) return nullptr;
+  owner[dev][used[dev]] = stream;
+  return base[dev] + 2 * (used[dev]++);
+}
+
 // EWB_TRACE=1 prints each launch step to stderr (flushed), to localise host faults.
 bool trace_on() {
   static int on = -1;
@@ -426,17 +561,17 @@ bool trace_on() {
   }
   return on == 1;
 }
-#define EWB_TRACE(...)                  \
-  do {                                  \
-    if (trace_on()) {                   \
+#define EWB_TRACE(...)                   \
+  do {                                   \
+    if (trace_on()) {                    \
       std::fprintf(stderr, __VA_ARGS__); \
-      std::fflush(stderr);              \
-    }                                   \
+      std::fflush(stderr);               \
+    }                                    \
   } while (0)
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
-int launch_cfg(const GemmArgs& g, cudaStream_t stream) {
-  using Cfg = GemmCfg<BN>;
+int launch_cfg(const GemmArgs& g, cudaStream_t stream, int* sched) {
+  using Cfg = GemmCfg<BN, EPI>;
   EWB_TRACE("[gemm] BN=%d a_mn=%d b_mn=%d epi=%d M=%d N=%d K=%d lda=%d ldb=%d ldo=%d smem=%d\n",
             BN, (int)A_MN, (int)B_MN, EPI, g.M, g.N, g.K, g.lda, g.ldb, g.ep.ldo, Cfg::SMEM);
   auto kern = gemm_tcgen05_kernel<BN, A_MN, B_MN, EPI>;
@@ -444,55 +579,59 @@ int launch_cfg(const GemmArgs& g, cudaStream_t stream) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev & 63]) {
-    EWB_TRACE("[gemm] set smem attribute\n");
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM) !=
         cudaSuccess)
       return kGemmErrLaunch;
     attr_set[dev & 63] = true;
   }
-  EWB_TRACE("[gemm] encode maps\n");
-  CUtensorMap ma, mbm;
+  CUtensorMap ma, mbm, mc;
   const bool ok_a = A_MN ? make_map_bf16(&ma, g.a, g.M, g.K, g.lda, 64, 64)
                          : make_map_bf16(&ma, g.a, g.K, g.M, g.lda, 64, kBM);
   const bool ok_b = B_MN ? make_map_bf16(&mbm, g.b, g.N, g.K, g.ldb, 64, 64)
                          : make_map_bf16(&mbm, g.b, g.K, g.N, g.ldb, 64, BN);
-  if (!ok_a || !ok_b) return kGemmErrTensorMap;
-  EWB_TRACE("[gemm] maps ok\n");
+  bool ok_c = true;
+  if constexpr (EPI == kEpiBf16) {
+    ok_c = make_map_bf16(&mc, g.ep.out, g.N, g.M, g.ep.ldo, 64, kBM);
+  } else if constexpr (EPI == kEpiF32 || EPI == kEpiAccF32) {
+    ok_c = make_map(&mc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, g.ep.out, g.N, g.M, g.ep.ldo, 32, kBM);
+  } else {
+    mc = ma;  // unused by register epilogues
+  }
+  if (!ok_a || !ok_b || !ok_c) return kGemmErrTensorMap;
   const int tiles = ((g.M + kBM - 1) / kBM) * ((g.N + BN - 1) / BN);
   const int grid = std::max(1, std::min(tiles, num_sms_cached()));
-  EWB_TRACE("[gemm] launch grid=%d\n", grid);
-  kern<<<grid, kThreads, Cfg::SMEM, stream>>>(ma, mbm, g.ep, g.M, g.N, g.K, g.status);
+  kern<<<grid, kThreads, Cfg::SMEM, stream>>>(ma, mbm, mc, g.ep, g.M, g.N, g.K, g.status, sched);
   const cudaError_t err = cudaGetLastError();
-  EWB_TRACE("[gemm] launched: %s\n", cudaGetErrorString(err));
+  EWB_TRACE("[gemm] launched grid=%d: %s\n", grid, cudaGetErrorString(err));
   return err == cudaSuccess ? kGemmOk : kGemmErrLaunch;
 }
 
 template <int BN>
-int dispatch_bn(const GemmArgs& g, cudaStream_t s) {
+int dispatch_bn(const GemmArgs& g, cudaStream_t s, int* sc) {
   const int e = g.ep.kind;
   if (!g.a_mn && !g.b_mn) {
     switch (e) {
-      case kEpiBf16: return launch_cfg<BN, false, false, kEpiBf16>(g, s);
-      case kEpiGelu: return launch_cfg<BN, false, false, kEpiGelu>(g, s);
-      case kEpiResid: return launch_cfg<BN, false, false, kEpiResid>(g, s);
-      case kEpiResidQ8: return launch_cfg<BN, false, false, kEpiResidQ8>(g, s);
-      case kEpiF32: return launch_cfg<BN, false, false, kEpiF32>(g, s);
-      case kEpiAccF32: return launch_cfg<BN, false, false, kEpiAccF32>(g, s);
+      case kEpiBf16: return launch_cfg<BN, false, false, kEpiBf16>(g, s, sc);
+      case kEpiGelu: return launch_cfg<BN, false, false, kEpiGelu>(g, s, sc);
+      case kEpiResid: return launch_cfg<BN, false, false, kEpiResid>(g, s, sc);
+      case kEpiResidQ8: return launch_cfg<BN, false, false, kEpiResidQ8>(g, s, sc);
+      case kEpiF32: return launch_cfg<BN, false, false, kEpiF32>(g, s, sc);
+      case kEpiAccF32: return launch_cfg<BN, false, false, kEpiAccF32>(g, s, sc);
       default: break;
     }
   } else if (!g.a_mn && g.b_mn) {
     switch (e) {
-      case kEpiBf16: return launch_cfg<BN, false, true, kEpiBf16>(g, s);
-      case kEpiDGelu: return launch_cfg<BN, false, true, kEpiDGelu>(g, s);
-      case kEpiAccF32: return launch_cfg<BN, false, true, kEpiAccF32>(g, s);
-      case kEpiF32: return launch_cfg<BN, false, true, kEpiF32>(g, s);
+      case kEpiBf16: return launch_cfg<BN, false, true, kEpiBf16>(g, s, sc);
+      case kEpiDGelu: return launch_cfg<BN, false, true, kEpiDGelu>(g, s, sc);
+      case kEpiAccF32: return launch_cfg<BN, false, true, kEpiAccF32>(g, s, sc);
+      case kEpiF32: return launch_cfg<BN, false, true, kEpiF32>(g, s, sc);
       default: break;
     }
   } else if (g.a_mn && g.b_mn) {
     switch (e) {
-      case kEpiAccF32: return launch_cfg<BN, true, true, kEpiAccF32>(g, s);
-      case kEpiBf16: return launch_cfg<BN, true, true, kEpiBf16>(g, s);
-      case kEpiF32: return launch_cfg<BN, true, true, kEpiF32>(g, s);
+      case kEpiAccF32: return launch_cfg<BN, true, true, kEpiAccF32>(g, s, sc);
+      case kEpiBf16: return launch_cfg<BN, true, true, kEpiBf16>(g, s, sc);
+      case kEpiF32: return launch_cfg<BN, true, true, kEpiF32>(g, s, sc);
       default: break;
     }
   }
@@ -525,10 +664,16 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
     return kGemmErrAlign;
   if ((g.lda % 8) || (g.ldb % 8)) return kGemmErrAlign;
   if (g.ep.kind == kEpiResidQ8 && (g.N % 128 || g.ep.ldo % 16)) return kGemmErrShape;
+  if (reinterpret_cast<uintptr_t>(g.ep.out) & 15) return kGemmErrAlign;
+  if ((g.ep.kind == kEpiBf16 && g.ep.ldo % 8) ||
+      ((g.ep.kind == kEpiF32 || g.ep.kind == kEpiAccF32) && g.ep.ldo % 4))
+    return kGemmErrAlign;
   int bn = g.bn;
   if (g.ep.kind == kEpiResidQ8) bn = 256;
   if (bn != 128 && bn != 256) bn = gemm_pick_bn(g.M, g.N);
-  return bn == 128 ? dispatch_bn<128>(g, stream) : dispatch_bn<256>(g, stream);
+  int* sc = g.sched != nullptr ? g.sched : sched_counters(stream);
+  if (sc == nullptr) return kGemmErrLaunch;
+  return bn == 128 ? dispatch_bn<128>(g, stream, sc) : dispatch_bn<256>(g, stream, sc);
 }
 
 }  // namespace ewb

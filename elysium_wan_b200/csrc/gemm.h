@@ -53,6 +53,7 @@ struct GemmArgs {
   int bn;  // 128 / 256, anything else = pick by wave efficiency
   GemmEpilogue ep;
   int* status;  // device status word (may be null)
+  int* sched;  // two zeroed ints for the tile scheduler (null: per-stream pool)
 };
 
 int gemm_launch(const GemmArgs& args, cudaStream_t stream);

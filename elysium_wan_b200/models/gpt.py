@@ -93,6 +93,38 @@ class WTask:
             ops.colsum(self.dy, self.b_grad, accumulate=True)
         self.dy = self.x = None
 
+    def record_stream(self, stream):
+        """Keep the inputs' memory alive until `stream` has consumed them."""
+        self.dy.record_stream(stream)
+        self.x.record_stream(stream)
+
+
+class WExecutor:
+    """Runs W tasks on a side CUDA stream so the weight-gradient GEMMs fill the
+    SMs the critical-path B GEMMs leave idle (their last wave). Each submission
+    waits for everything enqueued on the compute stream so far; tasks run in
+    submission order, so every parameter still folds its microbatches in order.
+    On CPU the tasks run inline."""
+
+    def __init__(self, device, enabled: bool = True):
+        self.cuda = torch.device(device).type == "cuda" and enabled
+        self.stream = torch.cuda.Stream(device=device) if self.cuda else None
+
+    def run(self, tasks: list):
+        if not self.cuda:
+            for t in tasks:
+                t.run()
+            return
+        self.stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(self.stream):
+            for t in tasks:
+                t.record_stream(self.stream)
+                t.run()
+
+    def join(self):
+        if self.cuda:
+            torch.cuda.current_stream().wait_stream(self.stream)
+
 
 class Embed:
     def __init__(self, cfg, store: ParamStore, e: int):
@@ -256,7 +288,7 @@ class StageModel:
                 saved.append(("input", x_in))
         return h, saved
 
-    def backward(self, saved, dy, wq: list, run_w_inline: bool = False):
+    def backward(self, saved, dy, wq: list, run_w_inline: bool = False, w_exec=None):
         """B of one microbatch: returns the input gradient (None on the first
         stage) and appends the deferred W tasks, last layer first. Layers saved
         as inputs are re-run forward just before their backward. With
@@ -272,6 +304,9 @@ class StageModel:
             tasks: list = [] if run_w_inline else wq
             g = layer.backward(ctx, g, tasks)
             if run_w_inline:
-                for t in tasks:
-                    t.run()
+                if w_exec is not None:
+                    w_exec(tasks)
+                else:
+                    for t in tasks:
+                        t.run()
         return g

@@ -21,7 +21,7 @@ import time
 import torch
 
 from elysium_wan_b200.models.data import make_batch
-from elysium_wan_b200.models.gpt import Act, StageModel
+from elysium_wan_b200.models.gpt import Act, StageModel, WExecutor
 from elysium_wan_b200.parallel.p2p import dbg
 from elysium_wan_b200.runtime import optim
 
@@ -46,6 +46,11 @@ class StageEngine:
         self.timing = spec.device_for(stage, peer).startswith("cuda")
         self.telemetry: list = []
         self._host_x = None
+        import os
+
+        side = os.environ.get("EWB_W_STREAM", "1") == "1"
+        self.wexec = WExecutor(self.device, enabled=side)
+        self.phase: dict = {}
         self.zero1 = None
         if comm is not None:
             self.attach_comm(comm)
@@ -183,7 +188,7 @@ class StageEngine:
                 # B, releasing each layer's W inputs at once (same fold order).
                 inline = idx + 1 < len(self.order) and self.order[idx + 1] == ("W", mb)
                 tasks: list = []
-                dx = self.model.backward(st, dy, tasks, run_w_inline=inline)
+                dx = self.model.backward(st, dy, tasks, run_w_inline=inline, w_exec=self.wexec.run)
                 if inline:
                     inline_done.add(mb)
                 else:
@@ -191,13 +196,16 @@ class StageEngine:
                 if not self.first:
                     sends += comm.send_grad(mb, dx)
             else:  # W
-                for t in wq.pop(mb):
-                    t.run()
+                self.wexec.run(wq.pop(mb))
             if ev:
                 e1 = torch.cuda.Event(enable_timing=True)
                 e1.record()
                 self.events.append((op, mb, e0, e1))
         dbg(f"stage {self.stage} ops done; waiting {len(sends)} sends")
+        self.wexec.join()
+        if ev:
+            e_ops = torch.cuda.Event(enable_timing=True)
+            e_ops.record()
         for w in sends:
             w.wait()
         if comm is not None:
@@ -206,6 +214,11 @@ class StageEngine:
             self.zero1.sync_and_step()
         else:
             self.opt.step()
+        if ev:
+            e_opt = torch.cuda.Event(enable_timing=True)
+            e_opt.record()
+            self.phase = {"first": self.events[0][2] if self.events else None, "ops_end": e_ops,
+                          "opt_end": e_opt}
         self.step_done = step + 1
         out = []
         if self.last and dev_losses:
@@ -214,6 +227,14 @@ class StageEngine:
             for mb, v in out:
                 self.losses.append((step, mb, v))
         return out
+
+    def phase_ms(self) -> dict:
+        """{ops_ms, opt_ms} of the last step (after a synchronize)."""
+        p = self.phase
+        if not p or p.get("first") is None:
+            return {}
+        return {"ops_ms": round(p["first"].elapsed_time(p["ops_end"]), 2),
+                "opt_ms": round(p["ops_end"].elapsed_time(p["opt_end"]), 2)}
 
     def op_times_ms(self) -> list:
         """[(op, mb, start_ms, dur_ms)] of the last step (after a synchronize)."""

@@ -61,7 +61,10 @@ class HostAdamW(DeviceAdamW):
             dev = master.device
             self.stage = [(torch.empty(self.chunk, device=dev), torch.empty(self.chunk, device=dev))
                           for _ in range(2)]
+            # Loads and stores on separate streams so the two copy engines run
+            # host->device and device->host at the same time.
             self.copy = torch.cuda.Stream(device=dev)
+            self.copy_out = torch.cuda.Stream(device=dev)
 
     def step(self):
         self.t += 1
@@ -99,12 +102,12 @@ class HostAdamW(DeviceAdamW):
             ops.adamw(self.p[lo:hi], mm, vv, self.g[lo:hi], work, self.lr, self.b1, self.b2,
                       self.eps, self.wd, self.t)
             computed[b].record(comp)
-            with torch.cuda.stream(self.copy):
-                self.copy.wait_event(computed[b])
+            with torch.cuda.stream(self.copy_out):
+                self.copy_out.wait_event(computed[b])
                 self.m[lo:hi].copy_(mm, non_blocking=True)
                 self.v[lo:hi].copy_(vv, non_blocking=True)
                 ev = torch.cuda.Event()
-                ev.record(self.copy)
+                ev.record(self.copy_out)
                 stored[b] = ev
         for ev in stored:
             if ev is not None:
