@@ -269,3 +269,85 @@ int layernorm_bwd(const LnBwdArgs& a, cudaStream_t stream) {
 }
 
 }  // namespace ewb
+
+// ---------------------------------------------------------------- allocation-free entry point
+// ewb_layernorm_bwd_noalloc (declared and documented in noalloc.h): the
+// partial-sum scratch lives in this file-scope device array instead of a
+// caller-allocated buffer. Host code must not use the array's name as a
+// device address; the address comes from cudaGetSymbolAddress, per device.
+#include <mutex>
+
+#include "noalloc.h"
+
+static __device__ __align__(256) float
+    g_ln_bwd_noalloc_scratch[2 * EWB_NOALLOC_LN_MAX_CHUNKS * EWB_NOALLOC_LN_MAX_D];
+
+namespace {
+
+std::mutex g_noalloc_mu;
+float* g_noalloc_addr[64] = {nullptr};
+
+// Device address of the scratch array on the current device, looked up once
+// per device (with that device current) and cached.
+float* noalloc_scratch(int* err) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    *err = EWB_NOALLOC_ERR_SETUP;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t rc = cudaGetSymbolAddress(&p, g_ln_bwd_noalloc_scratch);
+    if (rc != cudaSuccess || p == nullptr) {
+      *err = EWB_NOALLOC_ERR_SETUP;
+      return nullptr;
+    }
+    g_noalloc_addr[dev] = static_cast<float*>(p);
+  }
+  return g_noalloc_addr[dev];
+}
+
+}  // namespace
+
+extern "C" int ewb_layernorm_bwd_noalloc(const void* dy, int lddy, const void* x,
+                                         const float* x_scale, int x_fp8, int ldx, int ldxs,
+                                         const float* mean, const float* rstd, const float* gamma,
+                                         const void* dres, int lddres, void* dx, int lddx,
+                                         float* dgamma, float* dbeta, int accumulate, int rows,
+                                         int d, void* stream) {
+  if (dy == nullptr || x == nullptr || mean == nullptr || rstd == nullptr || gamma == nullptr ||
+      dx == nullptr || dgamma == nullptr || dbeta == nullptr || rows <= 0 || d <= 0 || d % 8 ||
+      (x_fp8 && (x_scale == nullptr || d % 128)))
+    return EWB_NOALLOC_ERR_ARGUMENT;
+  if (d > EWB_NOALLOC_LN_MAX_D) return EWB_NOALLOC_ERR_TOO_LARGE;
+  int err = EWB_NOALLOC_OK;
+  float* scratch = noalloc_scratch(&err);
+  if (scratch == nullptr) return err;
+  ewb::LnBwdArgs a{};
+  a.dy = static_cast<const __nv_bfloat16*>(dy);
+  a.lddy = lddy;
+  a.x = x;
+  a.x_scale = x_scale;
+  a.x_fp8 = x_fp8;
+  a.ldx = ldx;
+  a.ldxs = ldxs;
+  a.mean = mean;
+  a.rstd = rstd;
+  a.gamma = gamma;
+  a.dres = static_cast<const __nv_bfloat16*>(dres);
+  a.lddres = lddres;
+  a.dx = static_cast<__nv_bfloat16*>(dx);
+  a.lddx = lddx;
+  a.part_g = scratch;
+  a.part_b = scratch + EWB_NOALLOC_LN_MAX_CHUNKS * EWB_NOALLOC_LN_MAX_D;
+  a.dgamma = dgamma;
+  a.dbeta = dbeta;
+  a.accumulate = accumulate ? 1 : 0;
+  a.rows = rows;
+  a.d = d;
+  a.rows_per_chunk = (rows + EWB_NOALLOC_LN_MAX_CHUNKS - 1) / EWB_NOALLOC_LN_MAX_CHUNKS;
+  const int rc = ewb::layernorm_bwd(a, static_cast<cudaStream_t>(stream));
+  if (rc == 0) return EWB_NOALLOC_OK;
+  return rc == 1 ? EWB_NOALLOC_ERR_ARGUMENT : EWB_NOALLOC_ERR_LAUNCH;
+}

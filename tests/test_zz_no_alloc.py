@@ -1,0 +1,89 @@
+"""The allocation-free LayerNorm backward (ewb_layernorm_bwd_noalloc, a C
+entry point for callers that cannot allocate device memory: their own pool
+already owns the GPU, or their path must not fail or wait on an allocation)
+gives the regular entry point's results, on two calls in a row.
+
+The symbol is called through its exported C name, the way such a caller
+would, with caller-owned inputs and outputs; the only scratch is the fixed
+device array the library reserves at load time. Would fail if: the cached
+device address of that array were wrong or looked up without the device
+current, a second call read stale partial sums, the size check let an
+over-wide row through, or the kernel diverged from the regular path.
+"""
+
+import ctypes
+
+import pytest
+import torch
+
+from elysium_wan_b200 import ops
+
+pytestmark = pytest.mark.gpu
+
+MAX_D = 8192
+ERR_TOO_LARGE = 3
+
+
+def _fn():
+    lib = ctypes.CDLL(ops.ext().__file__)
+    f = lib.ewb_layernorm_bwd_noalloc
+    vp, i = ctypes.c_void_p, ctypes.c_int
+    f.argtypes = [vp, i, vp, vp, i, i, i, vp, vp, vp, vp, i, vp, i, vp, vp, i, i, i, vp]
+    f.restype = i
+    return f
+
+
+def _call(f, dy, x, mean, rstd, gamma, dres, dx, dg, db, accumulate):
+    rows, d = x.shape
+    stream = torch.cuda.current_stream().cuda_stream
+    return f(dy.data_ptr(), dy.stride(0), x.data_ptr(), None, 0, x.stride(0), 0, mean.data_ptr(),
+             rstd.data_ptr(), gamma.data_ptr(), dres.data_ptr(), dres.stride(0), dx.data_ptr(),
+             dx.stride(0), dg.data_ptr(), db.data_ptr(), 1 if accumulate else 0, rows, d, stream)
+
+
+def rel(a, b):
+    return ((a.float() - b.float()).norm() / (b.float().norm() + 1e-12)).item()
+
+
+@pytest.mark.parametrize("rows,d", [(2048, 5120), (300, 1536)])
+def test_noalloc_matches_regular_entry_point(rows, d):
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    torch.manual_seed(11)
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    f = _fn()
+    x = (torch.randn(rows, d, device=dev) * 2).to(torch.bfloat16)
+    gamma = torch.randn(d, device=dev)
+    beta = torch.randn(d, device=dev)
+    _, mean, rstd = ops.layernorm_fwd(x, None, gamma, beta)
+    for call in range(2):
+        dy = torch.randn(rows, d, device=dev).to(torch.bfloat16)
+        dres = torch.randn(rows, d, device=dev).to(torch.bfloat16)
+        dg_ref = torch.zeros(d, device=dev)
+        db_ref = torch.zeros(d, device=dev)
+        dx_ref = ops.layernorm_bwd(dy, x, None, mean, rstd, gamma, dres, dg_ref, db_ref,
+                                   accumulate=False)
+        dx = torch.empty_like(dx_ref)
+        dg = torch.full((d,), float("nan"), device=dev)
+        db = torch.full((d,), float("nan"), device=dev)
+        rc = _call(f, dy, x, mean, rstd, gamma, dres, dx, dg, db, accumulate=False)
+        torch.cuda.synchronize()
+        assert rc == 0, (call, rc)
+        assert torch.equal(dx, dx_ref), call
+        assert rel(dg, dg_ref) < 1e-5, call
+        assert rel(db, db_ref) < 1e-5, call
+
+
+def test_noalloc_rejects_rows_wider_than_its_scratch():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    dev = torch.device("cuda:0")
+    f = _fn()
+    d = MAX_D + 8
+    x = torch.zeros(4, d, device=dev, dtype=torch.bfloat16)
+    stats = torch.ones(4, device=dev)
+    g = torch.ones(d, device=dev)
+    out = torch.empty_like(x)
+    rc = _call(f, x, x, stats, stats, g, x, out, g.clone(), g.clone(), accumulate=False)
+    assert rc == ERR_TOO_LARGE
