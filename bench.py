@@ -37,7 +37,8 @@ import time
 # Every kernel is loaded when the CUDA context is created (before torch
 # initialises CUDA): a module loaded lazily while an NCCL receive is pending can
 # wait on that receive, a cross-rank deadlock.
-os.environ.setdefault("CUDA_MODULE_LOADING", "EAGER")
+if "reference" not in sys.argv:  # the reference arm runs the reference's own environment
+    os.environ.setdefault("CUDA_MODULE_LOADING", "EAGER")
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:

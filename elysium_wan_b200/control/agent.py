@@ -28,13 +28,25 @@ from elysium_wan_b200.transport.control import Channel, control_dial, token_mac
 ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 
+def _die_with_parent():
+    """Child-side: receive SIGKILL when the agent dies (Linux prctl), so a dead
+    worker machine takes its stage with it."""
+    try:
+        import ctypes
+
+        ctypes.CDLL("libc.so.6", use_errno=True).prctl(1, signal.SIGKILL)  # PR_SET_PDEATHSIG
+    except Exception:
+        pass
+
+
 class StageProcess:
     """One stage subprocess in its own process group, stdout read line by line."""
 
     def __init__(self, cmd: list, env: dict, on_line, log_path: str):
         self.log = open(log_path, "a")
         self.p = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, env=env,
-                                  text=True, bufsize=1, start_new_session=True)
+                                  text=True, bufsize=1, start_new_session=True,
+                                  preexec_fn=_die_with_parent)
         self.tail: list = []
         self.done_marker = False
         self.t = threading.Thread(target=self._read, args=(on_line,), daemon=True)

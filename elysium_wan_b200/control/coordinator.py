@@ -66,6 +66,7 @@ class CoordinatorConfig:
     liveness: dict = field(default_factory=dict)
     wan_links: dict = field(default_factory=dict)  # {"regionA|regionB": {bw_mbps, latency_ms}}
     job_timeout_s: float = 3600.0
+    min_workers: int = 0  # wait for at least this many (slots + spares) before placing
 
 
 @dataclass
@@ -303,7 +304,8 @@ class Coordinator:
         run_dir = os.path.join(self.cfg.state_dir, "runs", self.run_id)
         os.makedirs(run_dir, exist_ok=True)
         self.store = ckpt.CheckpointStore(os.path.join(self.cfg.state_dir, "store"))
-        live = self.wait_for_workers(spec.world_size, self.cfg.wait_workers_s)
+        live = self.wait_for_workers(max(spec.world_size, self.cfg.min_workers),
+                                     self.cfg.wait_workers_s)
         live = self._place(spec, live)
         slots = spec.slots()
         self.slot_node = {s: live[i] for i, s in enumerate(slots)}
@@ -334,7 +336,12 @@ class Coordinator:
                 dead = self.slot_node[verdict.slot]
                 with self.lock:
                     self.nodes[dead].dead = True
-                    cands = [self.nodes[n].info for n in spares if self.nodes[n].connected]
+                    # Any registered, live worker that holds no slot is a spare
+                    # (including workers that joined after placement).
+                    busy = set(self.slot_node.values())
+                    spares = [n for n in self.order if n not in busy and not self.nodes[n].dead
+                              and self.nodes[n].connected]
+                    cands = [self.nodes[n].info for n in spares]
                 rep = find_replacement(self.nodes[dead].info, cands, self.cfg.replacement_match)
                 if rep is None:
                     res = RunResult(False, self.run_id, None, self.attempt + 1, heals, restarts,

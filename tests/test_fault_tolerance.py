@@ -1,0 +1,153 @@
+"""Liveness verdicts on crafted slot states, checkpoint waves, replacement.
+
+Would fail if: a killed stage were not convicted at once, a WAN blip inside
+the reconnect grace convicted anyone, two simultaneous failures triggered a
+heal instead of "failed", heartbeat silence convicted on the first strike, a
+deterministic crash were healed, a stall with everyone alive were not a
+restart, a wave with a flipped byte validated, or pruning kept more than
+WAVE_KEEP waves.
+"""
+
+import os
+
+import pytest
+
+from elysium_wan_b200.fault_tolerance import checkpoint as ckpt
+from elysium_wan_b200.fault_tolerance.liveness import PEER_LOST, LivenessJudge, SlotState
+from elysium_wan_b200.fault_tolerance.replacement import find_replacement
+from elysium_wan_b200.models.config import make_config
+from elysium_wan_b200.resources.node import NodeInfo
+from elysium_wan_b200.runtime.spec import JobSpec
+
+NOW = 1000.0
+
+
+def slots(n=3, **kw):
+    out = []
+    for i in range(n):
+        st = SlotState(slot=(i, 0), node_id=f"n{i}", launched=True, last_heartbeat=NOW - 1,
+                       started_at=NOW - 50)
+        for k, v in kw.items():
+            setattr(st, k, v)
+        out.append(st)
+    return out
+
+
+def test_all_exit_clean_is_done():
+    ss = slots(exit_code=0, done_marker=True)
+    assert LivenessJudge().judge(ss, NOW).kind == "done"
+
+
+def test_killed_stage_is_convicted_at_once():
+    ss = slots()
+    ss[1].exit_code, ss[1].done_marker = -9, False
+    v = LivenessJudge().judge(ss, NOW)
+    assert v.kind == "convict" and v.slot == (1, 0)
+
+
+def test_blip_inside_reconnect_grace_is_only_suspect():
+    ss = slots()
+    ss[2].connected, ss[2].disconnected_at = False, NOW - 5
+    v = LivenessJudge(reconnect_grace_s=30).judge(ss, NOW)
+    assert v.kind == "suspect"
+
+
+def test_disconnect_past_grace_convicts():
+    ss = slots()
+    ss[2].connected, ss[2].disconnected_at = False, NOW - 40
+    v = LivenessJudge(reconnect_grace_s=30).judge(ss, NOW)
+    assert v.kind == "convict" and v.slot == (2, 0)
+
+
+def test_two_failures_at_once_fail_without_heal():
+    ss = slots()
+    for i in (0, 2):
+        ss[i].exit_code, ss[i].done_marker = -9, False
+    assert LivenessJudge().judge(ss, NOW).kind == "failed"
+
+
+def test_deterministic_crash_is_failed_not_healed():
+    ss = slots()
+    ss[0].exit_code, ss[0].done_marker, ss[0].log_tail = 1, True, "ValueError: bad"
+    assert LivenessJudge().judge(ss, NOW).kind == "failed"
+
+
+def test_heartbeat_silence_needs_two_strikes():
+    j = LivenessJudge(heartbeat_timeout_s=10, strike_gap_s=5)
+    ss = slots()
+    ss[1].last_heartbeat = NOW - 20
+    assert j.judge(ss, NOW).kind == "suspect"
+    assert j.judge(ss, NOW + 2).kind == "suspect"
+    v = j.judge(ss, NOW + 6)
+    assert v.kind == "convict" and v.slot == (1, 0)
+
+
+def test_peer_lost_with_silent_slot_convicts_the_silent_one():
+    j = LivenessJudge(heartbeat_timeout_s=10, strike_gap_s=1, exit_report_grace_s=1)
+    ss = slots()
+    ss[0].exit_code, ss[0].done_marker, ss[0].log_tail = 1, True, f"WT_ERROR {PEER_LOST}: x"
+    ss[2].last_heartbeat = NOW - 30
+    assert j.judge(ss, NOW).kind == "suspect"
+    v = j.judge(ss, NOW + 2)
+    assert v.kind == "convict" and v.slot == (2, 0)
+
+
+def test_everyone_alive_but_no_progress_is_stalled():
+    j = LivenessJudge(first_step_timeout_s=100)
+    ss = slots(started_at=NOW - 500)
+    assert j.judge(ss, NOW).kind == "stalled"
+
+
+def test_progress_must_increase_within_attempt():
+    st = SlotState(slot=(0, 0), node_id="n", start_step=4)
+    assert not st.add_progress(3, 1.0, 10)
+    assert st.add_progress(4, 1.0, 10)
+    assert not st.add_progress(4, 2.0, 10)
+    assert not st.add_progress(11, 3.0, 10)
+
+
+def _spec(tmp_path):
+    return JobSpec(model=make_config("toy", n_layer=2), stages=2, out_dir=str(tmp_path), tag="t").finalize()
+
+
+def test_wave_commit_validate_prune_and_corruption(tmp_path):
+    spec = _spec(tmp_path)
+    for step in (2, 4, 6, 8):
+        ckpt.commit_wave(spec, 1, 0, step, {"step": step, "x": list(range(10))})
+    assert ckpt.list_waves(spec.out_dir, "t", 1, 0) == [4, 6, 8]
+    d = ckpt.wave_dir(spec.out_dir, "t", 1, 0, 8)
+    ckpt.validate_wave(d)
+    assert os.path.exists(os.path.join(spec.out_dir, "t_ckpt_rank1p0.pt"))
+    p = os.path.join(d, "state.pt")
+    b = bytearray(open(p, "rb").read())
+    b[-5] ^= 0xFF
+    open(p, "wb").write(bytes(b))
+    with pytest.raises(ValueError):
+        ckpt.validate_wave(d)
+    state, step = ckpt.load_latest(spec, 1, 0)
+    assert step == 6  # the corrupted newest wave is skipped
+
+
+def test_resume_refuses_other_recipe(tmp_path):
+    spec = _spec(tmp_path)
+    ckpt.commit_wave(spec, 0, 0, 2, {"step": 2})
+    spec.lr = 0.5
+    with pytest.raises(ValueError, match="lr"):
+        ckpt.load_latest(spec, 0, 0)
+
+
+def test_common_step(tmp_path):
+    spec = _spec(tmp_path)
+    ckpt.commit_wave(spec, 0, 0, 2, {})
+    ckpt.commit_wave(spec, 0, 0, 4, {})
+    ckpt.commit_wave(spec, 1, 0, 2, {})
+    assert ckpt.common_step(spec) == 2
+
+
+def test_replacement_prefers_same_class_and_region():
+    dead = NodeInfo("n0", "w0", region="eu", device_class="b200")
+    cands = [NodeInfo("n1", "w1", region="us", device_class="b200"),
+             NodeInfo("n2", "w2", region="eu", device_class="b200"),
+             NodeInfo("n3", "w3", region="eu", device_class="cpu")]
+    assert find_replacement(dead, cands).node_id == "n2"
+    assert find_replacement(dead, [cands[2]], match="device") is None
