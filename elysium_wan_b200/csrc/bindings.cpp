@@ -59,10 +59,42 @@ T* ptr_or_null(const c10::optional<at::Tensor>& t) {
 
 // C[m, n] = sum_k A[m, k] B[n, k]; A is [M, K] (a_mn=False) or [K, M]; B is
 // [N, K] (b_mn=False) or [K, N].
+void gemm_impl(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor out, int64_t epi,
+               c10::optional<at::Tensor> bias, c10::optional<at::Tensor> resid,
+               c10::optional<at::Tensor> resid_scale, c10::optional<at::Tensor> aux,
+               c10::optional<at::Tensor> scale_out, double beta, int64_t bn,
+               const ewb::PeerScatter* peer);
+
 void gemm(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor out, int64_t epi,
           c10::optional<at::Tensor> bias, c10::optional<at::Tensor> resid,
           c10::optional<at::Tensor> resid_scale, c10::optional<at::Tensor> aux,
           c10::optional<at::Tensor> scale_out, double beta, int64_t bn) {
+  gemm_impl(a, a_mn, b, b_mn, out, epi, bias, resid, resid_scale, aux, scale_out, beta, bn, nullptr);
+}
+
+// dW GEMM whose epilogue scatters (local partial + tile) into the ZeRO-1
+// owners' slots: slots = peer pointers (int64), lo = world+1 flat bounds.
+void gemm_peer_scatter(at::Tensor a, at::Tensor b, at::Tensor out, std::vector<int64_t> slots,
+                       std::vector<int64_t> lo, int64_t stride, int64_t flat_off, int64_t rank,
+                       int64_t bn) {
+  TORCH_CHECK(slots.size() >= 1 && slots.size() <= ewb::kMaxPeers, "1..8 owners");
+  TORCH_CHECK(lo.size() == slots.size() + 1, "lo must have world+1 bounds");
+  ewb::PeerScatter ps{};
+  for (size_t k = 0; k < slots.size(); ++k) ps.slots[k] = reinterpret_cast<float*>(slots[k]);
+  for (size_t k = 0; k < lo.size(); ++k) ps.shard_lo[k] = lo[k];
+  ps.slot_stride = stride;
+  ps.flat_off = flat_off;
+  ps.rank = static_cast<int>(rank);
+  ps.world = static_cast<int>(slots.size());
+  gemm_impl(a, true, b, true, out, ewb::kEpiAccF32Peer, c10::nullopt, c10::nullopt, c10::nullopt,
+            c10::nullopt, c10::nullopt, 1.0, bn, &ps);
+}
+
+void gemm_impl(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor out, int64_t epi,
+               c10::optional<at::Tensor> bias, c10::optional<at::Tensor> resid,
+               c10::optional<at::Tensor> resid_scale, c10::optional<at::Tensor> aux,
+               c10::optional<at::Tensor> scale_out, double beta, int64_t bn,
+               const ewb::PeerScatter* peer) {
   check_2d_rowmajor(a, "a");
   check_2d_rowmajor(b, "b");
   check_2d_rowmajor(out, "out");
@@ -117,6 +149,7 @@ void gemm(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor out, int6
     e.ld_scale_out = scale_out->stride(0);
   }
   e.beta = static_cast<float>(beta);
+  if (peer != nullptr) e.peer = *peer;
   switch (e.kind) {
     case ewb::kEpiBf16:
     case ewb::kEpiGelu:
@@ -126,6 +159,7 @@ void gemm(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor out, int6
       break;
     case ewb::kEpiAccF32:
     case ewb::kEpiF32:
+    case ewb::kEpiAccF32Peer:
       TORCH_CHECK(out.scalar_type() == at::kFloat, "out must be fp32 for this epilogue");
       break;
     case ewb::kEpiResidQ8:
@@ -399,6 +433,47 @@ void cast_bf16(at::Tensor x, at::Tensor y) {
 
 int64_t launch_count() { return g_launches.load(); }
 
+void zero1_push_partials(at::Tensor partial, at::Tensor ranges, std::vector<int64_t> slots,
+                         std::vector<int64_t> lo, int64_t stride, int64_t rank) {
+  c10::cuda::CUDAGuard guard(partial.device());
+  std::vector<float*> sp;
+  for (auto s : slots) sp.push_back(reinterpret_cast<float*>(s));
+  std::vector<long long> l(lo.begin(), lo.end());
+  TORCH_CHECK(ranges.scalar_type() == at::kLong && ranges.is_cuda(), "ranges: int64 cuda");
+  ok(ewb::zero1_push_partials(partial.data_ptr<float>(),
+                              reinterpret_cast<const long long*>(ranges.data_ptr<int64_t>()),
+                              ranges.numel() / 2, sp.data(), l.data(), stride, rank,
+                              static_cast<int>(slots.size()), partial.numel(), cur_stream()),
+     "zero1_push_partials");
+  count(1);
+}
+
+void zero1_fold_slots(at::Tensor slots, int64_t stride, int64_t world, int64_t n, at::Tensor out) {
+  c10::cuda::CUDAGuard guard(slots.device());
+  ok(ewb::zero1_fold_slots(slots.data_ptr<float>(), stride, world, n, out.data_ptr<float>(),
+                           cur_stream()),
+     "zero1_fold_slots");
+  count(1);
+}
+
+void zero1_adamw_push(at::Tensor master, at::Tensor m, at::Tensor v, at::Tensor g, int64_t lo,
+                      int64_t n, std::vector<int64_t> masters, std::vector<int64_t> works,
+                      double lr, double b1, double b2, double eps, double wd, int64_t step) {
+  c10::cuda::CUDAGuard guard(master.device());
+  std::vector<float*> mp;
+  std::vector<__nv_bfloat16*> wp;
+  for (auto x : masters) mp.push_back(reinterpret_cast<float*>(x));
+  for (auto x : works) wp.push_back(reinterpret_cast<__nv_bfloat16*>(x));
+  const float bc1 = static_cast<float>(1.0 - std::pow(b1, static_cast<double>(step)));
+  const float bc2 = static_cast<float>(1.0 - std::pow(b2, static_cast<double>(step)));
+  ok(ewb::zero1_adamw_push(master.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
+                           g.data_ptr<float>(), lo, n, mp.data(), wp.data(),
+                           static_cast<int>(mp.size()), lr, b1, b2, eps, wd, bc1, bc2,
+                           cur_stream()),
+     "zero1_adamw_push");
+  count(1);
+}
+
 // Opt-in diagnostics: print the native backtrace of a host SIGSEGV to stderr.
 void segv_backtrace(int sig) {
   void* frames[64];
@@ -433,6 +508,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels of elysium_wan_b200";
   m.def("gemm", &gemm);
   m.def("gemm_pick_bn", &gemm_pick_bn);
+  m.def("gemm_peer_scatter", &gemm_peer_scatter);
+  m.def("zero1_push_partials", &zero1_push_partials);
+  m.def("zero1_fold_slots", &zero1_fold_slots);
+  m.def("zero1_adamw_push", &zero1_adamw_push);
   m.def("layernorm_fwd", &layernorm_fwd);
   m.def("layernorm_bwd", &layernorm_bwd);
   m.def("layernorm_bwd_chunks", &layernorm_bwd_chunks);
@@ -458,4 +537,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.attr("EPI_ACC_F32") = static_cast<int>(ewb::kEpiAccF32);
   m.attr("EPI_DGELU") = static_cast<int>(ewb::kEpiDGelu);
   m.attr("EPI_F32") = static_cast<int>(ewb::kEpiF32);
+  m.attr("EPI_ACC_F32_PEER") = static_cast<int>(ewb::kEpiAccF32Peer);
 }

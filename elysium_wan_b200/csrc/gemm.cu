@@ -180,6 +180,35 @@ __device__ __forceinline__ void epilogue_tile_regs(uint32_t taddr, int gm, int n
       float f[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(v[i]);
+      if constexpr (EPI == kEpiAccF32Peer) {
+        // ZeRO-1 reduce-scatter from the epilogue: this replica's final partial
+        // (its earlier microbatches, already folded in `out`, plus this tile)
+        // goes straight into the owning replica's slot over NVLink.
+        const float* lp = reinterpret_cast<const float*>(ep.out) + static_cast<size_t>(gm) * ep.ldo + n0;
+        const PeerScatter& ps = ep.peer;
+        const long long f0 = ps.flat_off + static_cast<long long>(gm) * ep.ldo + n0;
+        int k = 0;
+        while (k + 1 < ps.world && f0 >= ps.shard_lo[k + 1]) ++k;
+        const bool one_owner = (k + 1 >= ps.world) || (f0 + valid <= ps.shard_lo[k + 1]);
+        float* dst0 = ps.slots[k] + static_cast<long long>(ps.rank) * ps.slot_stride + (f0 - ps.shard_lo[k]);
+        if (one_owner && valid == 32 && (reinterpret_cast<uintptr_t>(dst0) & 15) == 0 &&
+            (reinterpret_cast<uintptr_t>(lp) & 15) == 0) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 a = reinterpret_cast<const float4*>(lp)[j];
+            reinterpret_cast<float4*>(dst0)[j] = make_float4(a.x + f[4 * j], a.y + f[4 * j + 1],
+                                                             a.z + f[4 * j + 2], a.w + f[4 * j + 3]);
+          }
+        } else {
+          for (int i = 0; i < valid; ++i) {
+            const long long fi = f0 + i;
+            while (k + 1 < ps.world && fi >= ps.shard_lo[k + 1]) ++k;
+            ps.slots[k][static_cast<long long>(ps.rank) * ps.slot_stride + (fi - ps.shard_lo[k])] =
+                lp[i] + f[i];
+          }
+        }
+        continue;
+      }
       if (ep.bias != nullptr && EPI != kEpiDGelu) {
         const float* bp = ep.bias + n0;
 #pragma unroll
@@ -630,6 +659,7 @@ int dispatch_bn(const GemmArgs& g, cudaStream_t s, int* sc) {
   } else if (g.a_mn && g.b_mn) {
     switch (e) {
       case kEpiAccF32: return launch_cfg<BN, true, true, kEpiAccF32>(g, s, sc);
+      case kEpiAccF32Peer: return launch_cfg<BN, true, true, kEpiAccF32Peer>(g, s, sc);
       case kEpiBf16: return launch_cfg<BN, true, true, kEpiBf16>(g, s, sc);
       case kEpiF32: return launch_cfg<BN, true, true, kEpiF32>(g, s, sc);
       default: break;

@@ -14,6 +14,21 @@ enum GemmEpilogueKind : int {
   kEpiAccF32 = 4,   // out f32 = (beta != 0 ? out : 0) + acc     (ordered gradient fold)
   kEpiDGelu = 5,    // out bf16 = acc * gelu'(aux)
   kEpiF32 = 6,      // out f32 = acc (+ bias)
+  kEpiAccF32Peer = 7,  // owner slot (peer memory) = out (local f32 partial) + acc: ZeRO-1 RS
+};
+
+constexpr int kMaxPeers = 8;
+
+// Where a flat parameter index lands in the ZeRO-1 owners' slot buffers:
+// owner k holds flat range [shard_lo[k], shard_lo[k+1]); replica `rank`
+// writes its partial at slots[k] + rank * slot_stride + (f - shard_lo[k]).
+struct PeerScatter {
+  float* slots[kMaxPeers];
+  long long shard_lo[kMaxPeers + 1];
+  long long slot_stride;
+  long long flat_off;  // flat index of out[0][0]
+  int rank;
+  int world;
 };
 
 enum GemmStatus : int {
@@ -40,6 +55,7 @@ struct GemmEpilogue {
   float* scale_out;  // [M][ld_scale_out] for kEpiResidQ8
   int ld_scale_out;
   float beta;
+  PeerScatter peer;  // kEpiAccF32Peer only
 };
 
 struct GemmArgs {

@@ -136,4 +136,15 @@ int dequant_e4m3_rows(const uint8_t* q, const float* scale, int T, int d, __nv_b
                       cudaStream_t stream);
 int cast_f32_bf16(const float* x, __nv_bfloat16* y, int64_t n, cudaStream_t stream);
 
+// ---------------------------------------------------------------- ZeRO-1 over peer memory
+int zero1_push_partials(const float* partial, const long long* ranges_dev, int nranges,
+                        float* const* slots, const long long* lo, long long stride, int rank,
+                        int world, long long total, cudaStream_t stream);
+int zero1_fold_slots(const float* slots, long long stride, int world, long long n, float* out,
+                     cudaStream_t stream);
+int zero1_adamw_push(const float* master, float* m, float* v, const float* g, long long lo,
+                     long long n, float* const* masters, __nv_bfloat16* const* works, int world,
+                     float lr, float b1, float b2, float eps, float wd, float bc1, float bc2,
+                     cudaStream_t stream);
+
 }  // namespace ewb

@@ -164,10 +164,16 @@ class CheckpointStore:
                 os.replace(os.path.join(d, name), os.path.join(d, name[:-5]))
         try:
             validate_wave(d)
-            return True
         except ValueError:
             shutil.rmtree(d, ignore_errors=True)
             return False
+        # Keep the newest WAVE_KEEP waves of this slot, like the workers do.
+        slot = os.path.dirname(d)
+        steps = sorted(int(x[5:]) for x in os.listdir(slot)
+                       if x.startswith("step-") and not x.endswith(".part") and x[5:].isdigit())
+        for old in steps[:-WAVE_KEEP]:
+            shutil.rmtree(os.path.join(slot, f"step-{old:08d}"), ignore_errors=True)
+        return True
 
     def common_step(self, spec) -> int | None:
         from copy import copy

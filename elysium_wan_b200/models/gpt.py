@@ -82,13 +82,19 @@ def entry_specs(cfg: GPTConfig, e: int) -> list[ParamSpec]:
 class WTask:
     """One deferred weight-gradient unit: grad (+)= dY^T X and the bias row sum."""
 
-    __slots__ = ("dy", "x", "w_grad", "b_grad")
+    __slots__ = ("dy", "x", "w_grad", "b_grad", "peer")
 
     def __init__(self, dy, x, w_grad, b_grad=None):
         self.dy, self.x, self.w_grad, self.b_grad = dy, x, w_grad, b_grad
+        self.peer = None  # ZeRO-1 owners' slots when this dW ends the replica's fold
 
     def run(self):
-        ops.linear_dw(self.dy, self.x, self.w_grad, accumulate=True)
+        if self.peer is not None:
+            slots, lo, stride, flat_off, rank = self.peer
+            ops.ext().gemm_peer_scatter(self.dy, self.x, self.w_grad, slots, lo, stride, flat_off,
+                                        rank, 0)
+        else:
+            ops.linear_dw(self.dy, self.x, self.w_grad, accumulate=True)
         if self.b_grad is not None:
             ops.colsum(self.dy, self.b_grad, accumulate=True)
         self.dy = self.x = None

@@ -59,9 +59,19 @@ class StageEngine:
         """Bind the stage channels (after warm_kernels, before the first step)."""
         self.comm = comm
         if self.width > 1 and self.zero1 is None:
-            from elysium_wan_b200.parallel.zero1 import Zero1
+            if self.spec.grad_sync == "fused" and self.device.type == "cuda":
+                from elysium_wan_b200.parallel.fused import FusedZero1
 
-            self.zero1 = Zero1(self, comm)
+                self.zero1 = FusedZero1(self, comm)
+            else:
+                from elysium_wan_b200.parallel.zero1 import Zero1
+
+                self.zero1 = Zero1(self, comm)
+
+    def _run_w(self, tasks: list, mb: int):
+        if self.zero1 is not None and hasattr(self.zero1, "mark"):
+            self.zero1.mark(tasks, mb)
+        self.wexec.run(tasks)
 
     @property
     def first(self) -> bool:
@@ -188,7 +198,8 @@ class StageEngine:
                 # B, releasing each layer's W inputs at once (same fold order).
                 inline = idx + 1 < len(self.order) and self.order[idx + 1] == ("W", mb)
                 tasks: list = []
-                dx = self.model.backward(st, dy, tasks, run_w_inline=inline, w_exec=self.wexec.run)
+                dx = self.model.backward(st, dy, tasks, run_w_inline=inline,
+                                         w_exec=lambda ts, m=mb: self._run_w(ts, m))
                 if inline:
                     inline_done.add(mb)
                 else:
@@ -196,7 +207,7 @@ class StageEngine:
                 if not self.first:
                     sends += comm.send_grad(mb, dx)
             else:  # W
-                self.wexec.run(wq.pop(mb))
+                self._run_w(wq.pop(mb), mb)
             if ev:
                 e1 = torch.cuda.Event(enable_timing=True)
                 e1.record()

@@ -107,7 +107,8 @@ def run_reference_arm(args) -> dict | None:
     per = n_layer // n
     partition = [[0 if r == 0 else 1 + r * per, n_layer + 2 if r == n - 1 else 1 + (r + 1) * per]
                  for r in range(n)]
-    out_dir = tempfile.mkdtemp(prefix="refbench-")
+    out_dir = os.environ.get("EWB_REF_LOGDIR") or tempfile.mkdtemp(prefix="refbench-")
+    os.makedirs(out_dir, exist_ok=True)
     stage_params = max((b - a) for a, b in partition) * 12 * d * d
     spec = JobSpec(model=model, stages=n, microbatches=args.microbatches, mb_size=args.mb_size,
                    steps=args.warmup + args.steps, device="cuda",
@@ -126,12 +127,15 @@ def run_reference_arm(args) -> dict | None:
         dist.barrier()
         dist.destroy_process_group()
     if not res.get("ok"):
-        tail = ""
-        lp = os.path.join(out_dir, f"refbench_r{n - 1}p0.log")
-        if os.path.exists(lp):
-            with open(lp, errors="replace") as f:
-                tail = " | ".join(f.read().splitlines()[-3:])[-300:]
-        return unavailable(f"the reference run failed (rc {res.get('rc')}): {tail}")
+        first = []
+        for r in range(n):
+            lp = os.path.join(out_dir, f"refbench_r{r}p0.log")
+            if os.path.exists(lp):
+                with open(lp, errors="replace") as f:
+                    errs = [ln for ln in f.read().splitlines()
+                            if re.search(r"Error|error:|Traceback|WT_DONE", ln)]
+                first.append(f"stage {r}: " + " | ".join(errs[-3:])[-240:])
+        return unavailable(f"the reference run failed (rc {res.get('rc')}): " + " ;; ".join(first))
     timed = range(args.warmup, args.warmup + args.steps)
     per_stage = []
     for r in range(n):

@@ -22,7 +22,8 @@ for var, path in (("CC", "/usr/bin/gcc"), ("CXX", "/usr/bin/g++")):
     if os.path.exists(path):
         os.environ[var] = path
 CSRC = os.path.join("elysium_wan_b200", "csrc")
-CU = ["gemm.cu", "norm.cu", "attention.cu", "ce.cu", "embed.cu", "optim.cu", "misc.cu"]
+CU = ["gemm.cu", "norm.cu", "attention.cu", "ce.cu", "embed.cu", "optim.cu", "misc.cu",
+      "collectives.cu"]
 
 NVCC = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -32,3 +32,19 @@ def test_nccl_pipeline_bitwise_vs_oracle(tmp_path, stages, boundary):
     r = run_and_compare(spec, timeout=240)
     assert r["ok"], r
     assert r["compared"] == 12
+
+
+@pytest.mark.parametrize("widths,sync", [([2], "fused"), ([2], "nccl"), ([1, 2], "fused")])
+def test_zero1_wide_stage_bitwise_vs_oracle(tmp_path, widths, sync):
+    """ZeRO-1 wide stages: the fused path (dW epilogue scatters into the owners'
+    slots over NVLink, AdamW pushes the updated shard to every replica) and the
+    NCCL library path both match the oracle's declared fold bit for bit."""
+    _need(sum(widths))
+    cfg = make_config("gpt15b", n_layer=2, d_model=512, n_head=4, seq_len=256, vocab_size=4096,
+                      boundary_dtype="bf16")
+    spec = JobSpec(model=cfg, stages=len(widths), stage_widths=widths, microbatches=4, mb_size=2,
+                   steps=3, device="cuda", backend="nccl", grad_sync=sync, out_dir=str(tmp_path),
+                   port_base=29970 + sum(widths) + len(sync))
+    r = run_and_compare(spec, timeout=240)
+    assert r["ok"], r
+    assert r["compared"] == 12
