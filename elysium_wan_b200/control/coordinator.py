@@ -126,12 +126,16 @@ class Coordinator:
         self.events: list = []
         self.on_progress = None  # callback(slot, step, node_id)
         self._pending_ckpt: dict = {}
+        self.link_memory = None
 
     # ----------------------------------------------------------------- server
     def start(self):
         self.sock = control_listen(self.host, self.port)
         self.port = self.sock.getsockname()[1]
         os.makedirs(self.cfg.state_dir, exist_ok=True)
+        from elysium_wan_b200.scheduler.linkmemory import LinkMemory
+
+        self.link_memory = LinkMemory(self.cfg.state_dir)
         print(f"COORDINATOR_ID {self.id}", flush=True)
         threading.Thread(target=self._accept_loop, daemon=True).start()
         return self
@@ -270,8 +274,20 @@ class Coordinator:
         return build_spec(job.plan, job.stages, fleet)
 
     def _place(self, spec: JobSpec, live: list) -> list:
-        """Slots in rank order take workers grouped by region (stable), the rest are spares."""
+        """Slots in rank order take workers grouped by region (stable), the rest
+        are spares. group_by any / model / series runs the node selector
+        (one device class, remembered-dead hosts skipped, remembered path
+        verdicts ranked) and keeps its choice first."""
         infos = [self.nodes[n].info for n in live]
+        if self.cfg.group_by in ("any", "model", "series"):
+            from elysium_wan_b200.scheduler.selection import SelectionPolicy, select_nodes
+
+            pol = SelectionPolicy(group_by=self.cfg.group_by, same_region=not self.cfg.any_region,
+                                  distinct_hosts=not self.cfg.allow_shared_hosts)
+            sel = select_nodes(infos, spec.world_size, pol, self.link_memory)
+            if not sel.ok:
+                raise ValueError(sel.reason)
+            return [n.node_id for n in sel.chosen] + [n.node_id for n in sel.spares]
         why = mixed_fleet(infos)
         if why:
             raise ValueError(why)
@@ -334,6 +350,10 @@ class Coordinator:
             if verdict.kind == "convict" and heals < self.cfg.max_heals:
                 heals += 1
                 dead = self.slot_node[verdict.slot]
+                if self.link_memory is not None:
+                    di = self.nodes[dead].info
+                    self.link_memory.record_dead(f"{di.name}@{di.host}", verdict.why, self.run_id,
+                                                 host=di.host)
                 with self.lock:
                     self.nodes[dead].dead = True
                     # Any registered, live worker that holds no slot is a spare

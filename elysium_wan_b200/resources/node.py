@@ -18,6 +18,14 @@ class NodeInfo:
     caps: dict = field(default_factory=dict)
     alive: bool = True
 
+    def memory_bytes(self) -> float | None:
+        """Device memory in bytes, or None when the node never measured it."""
+        return None if not self.vram_gb else float(self.vram_gb) * 2**30
+
+    def speed(self) -> float:
+        """Relative compute speed (measured dense bf16 TFLOP/s; 1.0 unknown)."""
+        return float(self.tflops_bf16) if self.tflops_bf16 else 1.0
+
     @staticmethod
     def from_caps(node_id: str, caps: dict) -> "NodeInfo":
         return NodeInfo(node_id=node_id, name=caps.get("name", node_id), host=caps.get("host", "127.0.0.1"),

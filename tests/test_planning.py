@@ -1,0 +1,176 @@
+"""Planning helpers: microbatch / in-flight solvers, shape advisor, precision
+admission, placement, node selection with link memory, production flags.
+Mirrors the reference's scheduler unit tests (tests/unit/test_schedule.py,
+test_autoconfig.py, test_placement.py, test_selection.py in
+virgiliolrf/elysium-wan): pure host logic, no device."""
+
+import pytest
+
+from elysium_wan_b200.models.config import make_config
+from elysium_wan_b200.resources.node import NodeInfo
+from elysium_wan_b200.runtime.spec import JobSpec
+from elysium_wan_b200.scheduler import autoconfig, production, shape, solve
+from elysium_wan_b200.scheduler.linkmemory import LinkMemory, verdict
+from elysium_wan_b200.scheduler.placement import memory_order, place, rank_memory_weights
+from elysium_wan_b200.scheduler.selection import SelectionPolicy, select_nodes
+
+
+def test_fbw_ratios():
+    f, b, w = solve.fbw_costs(4096, 2048)
+    assert w < f < b
+    assert abs((b + w) - 2 * f) < 1e-9 * f  # B + W = 2F
+
+
+def test_solve_microbatches_meets_target_and_is_minimal():
+    r = solve.solve_microbatches(4, bubble_target=0.10, fbw=(1.0, 1.0, 1.0))
+    m = r["microbatches"]
+    assert r["bubble"] <= 0.10
+    assert solve._bubble(4, m - 1, 1.0, 1.0, 1.0, 0.0) > 0.10 if m > 1 else True
+    assert "bubble" in r["reason"]
+
+
+def test_solve_microbatches_token_cap_binds():
+    r = solve.solve_microbatches(8, bubble_target=0.001, tokens_per_step_cap=8 * 2048,
+                                 mb_size=1, seq_len=2048)
+    assert r["microbatches"] == 8
+    assert "step budget" in r["reason"]
+
+
+def test_single_stage_needs_no_fill():
+    assert solve.solve_microbatches(1)["bubble"] == 0.0
+
+
+def test_k_inflight():
+    r = solve.solve_k_inflight(window_s=0.1, rtt_ms=100, boundary_bytes=10e6, link_mbps=1000)
+    # 50 ms one way + 80 ms on the wire over a 100 ms window -> k = 3
+    assert r["k"] == 3
+    r2 = solve.solve_k_inflight(0.1, 100, 10e6, 1000, mem_slack_bytes=1e9, per_inflight_bytes=6e8)
+    assert r2["k"] == 1 and "memory" in r2["reason"]
+
+
+def test_live_graphs_deepest_at_rank0():
+    assert [solve.stage_live_graphs(4, r, 1) for r in range(4)] == [4, 3, 2, 1]
+
+
+def test_fleet_ceiling_latency_binds():
+    r = solve.solve_fleet_ceiling(4e6, 2048, n_params=1e11, rtt_s=0.2, flops_per_gpu=1e15,
+                                  n_stages=8)
+    assert r["fleet_max"] == min(r["fleet_batch_side"], r["fleet_latency_side"])
+
+
+def test_shape_advisor_prefers_largest_within_target():
+    out = shape.advise(8, 160e9, tflops=1000, link_mbps=6e6)
+    best = out["best"]
+    assert out["met_target"]
+    assert all(s.params <= best.params for s in out["fits"] if s.bubble <= 0.2)
+    assert best.stage_bytes <= 160e9
+    # A slow hop forces a smaller bubble-feasible shape or none at all.
+    slow = shape.advise(8, 160e9, tflops=1000, link_mbps=50)
+    assert slow["best"].bubble >= best.bubble
+
+
+def test_precision_admission_policies():
+    cfg = make_config("gpt15b")
+    p = 6 * 12 * cfg.d_model ** 2
+    fast = autoconfig.plan(cfg, p, 6, link_mbps=6e6, window_s=0.2, mem_budget_bytes=180e9)
+    assert fast["chosen"]["boundary"] == "fp32"  # widest lossless rung on NVLink
+    slow = autoconfig.plan(cfg, p, 6, link_mbps=1200, window_s=0.2, mem_budget_bytes=180e9)
+    # 2048 x 5120 bf16 = 21 MB per microbatch -> 839 Mbps floor, 1678 with margin:
+    # balanced takes the lossless bf16 rung at the floor and says so.
+    assert slow["chosen"]["boundary"] == "bf16" and "WITHOUT" in slow["reason"]
+    ll = autoconfig.plan(cfg, p, 6, link_mbps=1200, window_s=0.2, mem_budget_bytes=180e9,
+                         policy="lossless")
+    assert ll["chosen"] is None and "no lossless" in ll["reason"]
+    bal = autoconfig.plan(cfg, p, 6, link_mbps=700, window_s=0.2, mem_budget_bytes=180e9)
+    assert bal["chosen"]["boundary"] == "fp8_e4m3_b128" and "NO LOSSLESS" in bal["reason"]
+    thr = autoconfig.plan(cfg, p, 6, link_mbps=1200, window_s=0.2, mem_budget_bytes=180e9,
+                          policy="max_throughput")
+    assert thr["chosen"]["boundary"] == "fp8_e4m3_b128"
+    pinned = autoconfig.plan(cfg, p, 6, link_mbps=100, window_s=0.2, mem_budget_bytes=1e9,
+                             boundary_override="bf16")
+    assert "WARNING" in pinned["reason"] and "chosen" in pinned["report"]
+
+
+def _nodes(n, vram=(180,), tf=1000.0, cls="cuda:B200", region="r0"):
+    out = []
+    for i in range(n):
+        out.append(NodeInfo(node_id=f"n{i}", name=f"w{i}", host=f"10.0.0.{i + 1}", region=region,
+                            device=f"cuda:{i}", device_class=cls,
+                            vram_gb=vram[i % len(vram)], tflops_bf16=tf))
+    return out
+
+
+def test_memory_order_gives_rank0_the_biggest_card():
+    spec = JobSpec(model=make_config("gpt0_6b"), stages=4, microbatches=8, mb_size=1)
+    w = rank_memory_weights(spec)
+    assert w[0] == max(w[:-1])
+    nodes = _nodes(4, vram=(80, 180, 96, 141))
+    order = memory_order(spec, nodes)
+    assert sorted(order) == [0, 1, 2, 3]
+    big = max(range(4), key=lambda r: w[r])
+    assert nodes[order[big]].vram_gb == 180
+
+
+def test_place_cuts_by_speed():
+    spec = JobSpec(model=make_config("cpu_plumbing"), stages=2, microbatches=4, mb_size=1,
+                   device="cpu")
+    nodes = _nodes(2, cls="cpu")
+    for n in nodes:
+        n.device = "cpu"
+    nodes[0].tflops_bf16 = 3.0
+    nodes[1].tflops_bf16 = 1.0
+    why = place(spec, [[nodes[0]], [nodes[1]]])
+    lay = why["layers_per_stage"]
+    assert lay[0] >= lay[1]
+    assert spec.schedule_order is not None
+
+
+def test_selection_refuses_mixed_and_skips_dead(tmp_path):
+    pool = _nodes(2, cls="cuda:B200") + _nodes(1, cls="cuda:H100")
+    pool[2].node_id, pool[2].name = "n9", "w9"
+    sel = select_nodes(pool, 3)
+    assert not sel.ok and "MIXED-FLEET" in sel.reason
+    mem = LinkMemory(str(tmp_path))
+    pool = _nodes(4)
+    mem.record_dead("w0@10.0.0.1", "heartbeat lost", "run1", host="10.0.0.1")
+    sel = select_nodes(pool, 3, memory=mem)
+    assert sel.ok and "n0" not in [n.node_id for n in sel.chosen]
+    # the memory persists
+    assert "w0@10.0.0.1" in LinkMemory(str(tmp_path)).dead_keys()
+
+
+def test_link_memory_verdicts(tmp_path):
+    mem = LinkMemory(str(tmp_path))
+    mem.record_path("a", "b", 500, 20, "r1")
+    assert verdict(mem.path("b", "a")) == "good"
+    mem.record_path("a", "b", 30, 20, "r2")
+    assert verdict(mem.path("a", "b")) == "variable"
+    mem.record_path("a", "b", 30, 20, "r2")  # replay of the same run
+    assert mem.path("a", "b").samples == 2
+    mem.record_path("c", "d", 500, 200, "r1")
+    assert verdict(mem.path("c", "d")) == "slow"
+
+
+def test_selection_ranks_by_remembered_paths(tmp_path):
+    mem = LinkMemory(str(tmp_path))
+    pool = _nodes(3)
+    pool[0].tflops_bf16 = 2000.0  # fastest, but its path to everyone is slow
+    for o in ("10.0.0.2", "10.0.0.3"):
+        mem.record_path("10.0.0.1", o, 10, 300, "r")
+    sel = select_nodes(pool, 2, SelectionPolicy(), memory=mem)
+    assert sel.ok and "n0" not in [n.node_id for n in sel.chosen]
+
+
+def test_production_fields():
+    f = production.spec_fields([1, 2], {"recompute": False, "lr": None})
+    assert f["recompute"] is False and f["grad_sync"] == "fused" and "lr" not in f
+    assert production.deviations(f) == ["recompute=False (production: True)"]
+    assert production.spec_fields(wan=True)["wire_codec"] == "planes"
+
+
+@pytest.mark.parametrize("policy", ["lossless", "balanced", "max_throughput"])
+def test_choose_returns_reason(policy):
+    cfg = make_config("gpt0_6b")
+    rows = autoconfig.evaluate(cfg, 10**8, 4, 1, 2, 1e5, 0.05, 1e12)
+    row, why = autoconfig.choose(rows, policy)
+    assert row is not None and isinstance(why, str)
