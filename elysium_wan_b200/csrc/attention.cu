@@ -10,8 +10,9 @@
 // base-2 log-sum-exp of the scaled scores, lse2 = max + log2(sum 2^(x - max)),
 // x = (q.k) * log2(e) / sqrt(hd).
 //
-// Tiles: 64 queries x 64 keys per CTA step, 4 warps x 16 query rows, bf16
-// mma.sync m16n8k16 with fp32 accumulation, K/V double-buffered by cp.async.
+// Tiles: 128 (or 64) query rows per CTA, one warp per 16 rows, keys in blocks
+// of 64 double-buffered by cp.async, bf16 mma.sync m16n8k16 with fp32
+// accumulation; exponentials on the hardware ex2 unit.
 // Backward: dK/dV in one kernel (a CTA owns a key block and walks the query
 // blocks), dQ in another (a CTA owns a query block and walks the key blocks).
 // Every output element is produced by one thread in a fixed order: there are
@@ -22,9 +23,6 @@
 namespace ewb {
 namespace {
 
-constexpr int kBQ = 64;
-constexpr int kBK = 64;
-constexpr int kAttnThreads = 128;
 constexpr float kLog2e = 1.4426950408889634f;
 
 __device__ __forceinline__ void cp_async16(uint32_t saddr, const void* gptr) {
@@ -55,16 +53,24 @@ __device__ __forceinline__ void mma16816(float* c, const uint32_t* a, uint32_t b
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// Copy a [64][HD] bf16 tile (row stride ld elements in global) into shared
+// Copy a [ROWS][HD] bf16 tile (row stride ld elements in global) into shared
 // memory with row stride HD + 8 (the padding makes ldmatrix conflict-free).
-template <int HD>
+template <int HD, int ROWS = 64>
 __device__ __forceinline__ void load_tile_async(__nv_bfloat16* s, const __nv_bfloat16* g, int ld) {
   constexpr int CH = HD / 8;  // 16-byte chunks per row
   constexpr int LD = HD + 8;
-  for (int i = threadIdx.x; i < 64 * CH; i += kAttnThreads) {
+  for (int i = threadIdx.x; i < ROWS * CH; i += blockDim.x) {
     const int r = i / CH, c = i % CH;
     cp_async16(smem_u32(s + r * LD + c * 8), g + static_cast<size_t>(r) * ld + c * 8);
   }
+}
+
+// 2^x with the hardware approximation (ex2.approx.ftz.f32): the softmax's
+// exponent; its error (2 ulp) is far below the bf16 rounding of P.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 // A-operand fragments (16 rows x HD) of rows [row0, row0+16) of a smem tile.
@@ -143,29 +149,34 @@ __device__ __forceinline__ void mma_p_tile(const float (*p)[4], const __nv_bfloa
   }
 }
 
-template <int HD>
-__global__ void __launch_bounds__(kAttnThreads)
+// Forward: a CTA owns BQ = 16 * WARPS query rows (one warp per 16 rows) and
+// walks the causal key blocks of 64 (double-buffered by cp.async).
+template <int HD, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32)
     attn_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* __restrict__ o,
-                    float* __restrict__ lse2, int S, int H, int d, float scale_log2) {
+                    float* __restrict__ lse2, int S, int H, int Hkv, int d, float scale_log2) {
   constexpr int LD = HD + 8;
-  constexpr int TILE = 64 * LD;
+  constexpr int BQ = 16 * WARPS;
+  constexpr int KT = 64 * LD;
   extern __shared__ __align__(16) __nv_bfloat16 sm_attn[];
   __nv_bfloat16* sQ = sm_attn;
-  __nv_bfloat16* sK = sQ + TILE;  // [2] tiles
-  __nv_bfloat16* sV = sK + 2 * TILE;
+  __nv_bfloat16* sK = sQ + BQ * LD;  // [2] tiles of 64 keys
+  __nv_bfloat16* sV = sK + 2 * KT;
 
   const int qb = gridDim.x - 1 - blockIdx.x;  // longest rows first
   const int h = blockIdx.y, b = blockIdx.z;
-  const int ldq = 3 * d;
+  const int dkv = Hkv * HD, hk = h / (H / Hkv);  // grouped-query: kv head of this q head
+  const int ldq = d + 2 * dkv;
   const size_t tok0 = static_cast<size_t>(b) * S;
-  const __nv_bfloat16* Qg = qkv + (tok0 + qb * kBQ) * ldq + h * HD;
-  const __nv_bfloat16* Kg = qkv + tok0 * ldq + d + h * HD;
-  const __nv_bfloat16* Vg = qkv + tok0 * ldq + 2 * d + h * HD;
+  const __nv_bfloat16* Qg = qkv + (tok0 + qb * BQ) * ldq + h * HD;
+  const __nv_bfloat16* Kg = qkv + tok0 * ldq + d + hk * HD;
+  const __nv_bfloat16* Vg = qkv + tok0 * ldq + d + dkv + hk * HD;
 
   const int warp = threadIdx.x >> 5, l = threadIdx.x & 31;
   const int g = l >> 2, t4 = l & 3;
+  const int row_base = qb * BQ + warp * 16;  // first global query row of this warp
 
-  load_tile_async<HD>(sQ, Qg, ldq);
+  load_tile_async<HD, BQ>(sQ, Qg, ldq);
   load_tile_async<HD>(sK, Kg, ldq);
   load_tile_async<HD>(sV, Vg, ldq);
   cp_async_commit();
@@ -177,12 +188,12 @@ __global__ void __launch_bounds__(kAttnThreads)
   float m[2] = {-INFINITY, -INFINITY};
   float lsum[2] = {0.f, 0.f};
 
-  const int nblk = qb + 1;
+  const int nblk = ((qb + 1) * BQ) / 64;  // key blocks up to the block diagonal
   for (int j = 0; j < nblk; ++j) {
     const int buf = j & 1;
     if (j + 1 < nblk) {
-      load_tile_async<HD>(sK + (buf ^ 1) * TILE, Kg + static_cast<size_t>(j + 1) * kBK * ldq, ldq);
-      load_tile_async<HD>(sV + (buf ^ 1) * TILE, Vg + static_cast<size_t>(j + 1) * kBK * ldq, ldq);
+      load_tile_async<HD>(sK + (buf ^ 1) * KT, Kg + static_cast<size_t>(j + 1) * 64 * ldq, ldq);
+      load_tile_async<HD>(sV + (buf ^ 1) * KT, Vg + static_cast<size_t>(j + 1) * 64 * ldq, ldq);
       cp_async_commit();
       cp_async_wait<1>();
     } else {
@@ -190,49 +201,50 @@ __global__ void __launch_bounds__(kAttnThreads)
     }
     __syncthreads();
     if (j == 0) load_a_frags<HD>(sQ, warp * 16, qf);
-
-    float s[8][4];
+    // Key blocks entirely above this warp's rows contribute nothing.
+    if (j * 64 <= row_base + 15) {
+      float sc[8][4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
-    mma_a_tileT<HD>(qf, sK + buf * TILE, s);
-
-    const bool diag = (j == qb);
+      for (int i = 0; i < 8; ++i) sc[i][0] = sc[i][1] = sc[i][2] = sc[i][3] = 0.f;
+      mma_a_tileT<HD>(qf, sK + buf * KT, sc);
+      const bool diag = (j * 64 + 63 > row_base);
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      const int qrow = warp * 16 + g + 8 * r;
-      float mx = -INFINITY;
+      for (int r = 0; r < 2; ++r) {
+        const int qrow = row_base + g + 8 * r;
+        float mx = -INFINITY;
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt)
+        for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int kcol = nt * 8 + 2 * t4 + e;
-          float x = s[nt][2 * r + e] * scale_log2;
-          if (diag && kcol > qrow) x = -INFINITY;
-          s[nt][2 * r + e] = x;
-          mx = fmaxf(mx, x);
+          for (int e = 0; e < 2; ++e) {
+            const int kcol = j * 64 + nt * 8 + 2 * t4 + e;
+            float x = sc[nt][2 * r + e] * scale_log2;
+            if (diag && kcol > qrow) x = -INFINITY;
+            sc[nt][2 * r + e] = x;
+            mx = fmaxf(mx, x);
+          }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float mnew = fmaxf(m[r], mx);
+        const float alpha = (m[r] == -INFINITY) ? 0.f : fast_exp2(m[r] - mnew);
+        m[r] = mnew;
+        float rs = 0.f;
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const float pv = fast_exp2(sc[nt][2 * r + e] - mnew);
+            sc[nt][2 * r + e] = pv;
+            rs += pv;
+          }
+        lsum[r] = lsum[r] * alpha + rs;
+#pragma unroll
+        for (int i = 0; i < HD / 8; ++i) {
+          acc[i][2 * r] *= alpha;
+          acc[i][2 * r + 1] *= alpha;
         }
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      const float mnew = fmaxf(m[r], mx);
-      const float alpha = (m[r] == -INFINITY) ? 0.f : exp2f(m[r] - mnew);
-      m[r] = mnew;
-      float rs = 0.f;
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const float pv = exp2f(s[nt][2 * r + e] - mnew);
-          s[nt][2 * r + e] = pv;
-          rs += pv;
-        }
-      lsum[r] = lsum[r] * alpha + rs;
-#pragma unroll
-      for (int i = 0; i < HD / 8; ++i) {
-        acc[i][2 * r] *= alpha;
-        acc[i][2 * r + 1] *= alpha;
       }
+      mma_p_tile<HD>(sc, sV + buf * KT, acc);
     }
-    mma_p_tile<HD>(s, sV + buf * TILE, acc);
     __syncthreads();
   }
 
@@ -242,7 +254,7 @@ __global__ void __launch_bounds__(kAttnThreads)
     ls += __shfl_xor_sync(0xffffffffu, ls, 1);
     ls += __shfl_xor_sync(0xffffffffu, ls, 2);
     const float inv = 1.0f / ls;
-    const int qrow = qb * kBQ + warp * 16 + g + 8 * r;
+    const int qrow = row_base + g + 8 * r;
     __nv_bfloat16* orow = o + (tok0 + qrow) * d + h * HD;
 #pragma unroll
     for (int i = 0; i < HD / 8; ++i) {
@@ -273,33 +285,37 @@ __global__ void attn_bwd_dot_kernel(const __nv_bfloat16* __restrict__ o,
   }
 }
 
-template <int HD>
-__global__ void __launch_bounds__(kAttnThreads)
+// dQ: a CTA owns BQ = 16 * WARPS query rows and walks the key blocks of 64.
+template <int HD, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32)
     attn_bwd_dq_kernel(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ dout,
                        const float* __restrict__ lse2, const float* __restrict__ Dv,
-                       __nv_bfloat16* __restrict__ dqkv, int S, int H, int d, float scale_log2,
-                       float scale) {
+                       __nv_bfloat16* __restrict__ dqkv, int S, int H, int Hkv, int d,
+                       float scale_log2, float scale) {
   constexpr int LD = HD + 8;
-  constexpr int TILE = 64 * LD;
+  constexpr int BQ = 16 * WARPS;
+  constexpr int KT = 64 * LD;
   extern __shared__ __align__(16) __nv_bfloat16 sm_attn[];
   __nv_bfloat16* sQ = sm_attn;
-  __nv_bfloat16* sdO = sQ + TILE;
-  __nv_bfloat16* sK = sdO + TILE;  // [2]
-  __nv_bfloat16* sV = sK + 2 * TILE;
+  __nv_bfloat16* sdO = sQ + BQ * LD;
+  __nv_bfloat16* sK = sdO + BQ * LD;  // [2]
+  __nv_bfloat16* sV = sK + 2 * KT;
 
   const int qb = gridDim.x - 1 - blockIdx.x;
   const int h = blockIdx.y, b = blockIdx.z;
-  const int ldq = 3 * d;
+  const int dkv = Hkv * HD, hk = h / (H / Hkv);
+  const int ldq = d + 2 * dkv;
   const size_t tok0 = static_cast<size_t>(b) * S;
-  const __nv_bfloat16* Qg = qkv + (tok0 + qb * kBQ) * ldq + h * HD;
-  const __nv_bfloat16* dOg = dout + (tok0 + qb * kBQ) * d + h * HD;
-  const __nv_bfloat16* Kg = qkv + tok0 * ldq + d + h * HD;
-  const __nv_bfloat16* Vg = qkv + tok0 * ldq + 2 * d + h * HD;
+  const __nv_bfloat16* Qg = qkv + (tok0 + qb * BQ) * ldq + h * HD;
+  const __nv_bfloat16* dOg = dout + (tok0 + qb * BQ) * d + h * HD;
+  const __nv_bfloat16* Kg = qkv + tok0 * ldq + d + hk * HD;
+  const __nv_bfloat16* Vg = qkv + tok0 * ldq + d + dkv + hk * HD;
   const int warp = threadIdx.x >> 5, l = threadIdx.x & 31;
   const int g = l >> 2, t4 = l & 3;
+  const int row_base = qb * BQ + warp * 16;
 
-  load_tile_async<HD>(sQ, Qg, ldq);
-  load_tile_async<HD>(sdO, dOg, d);
+  load_tile_async<HD, BQ>(sQ, Qg, ldq);
+  load_tile_async<HD, BQ>(sdO, dOg, d);
   load_tile_async<HD>(sK, Kg, ldq);
   load_tile_async<HD>(sV, Vg, ldq);
   cp_async_commit();
@@ -307,7 +323,7 @@ __global__ void __launch_bounds__(kAttnThreads)
   float lr[2], dr[2];
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
-    const size_t idx = (static_cast<size_t>(b) * H + h) * S + qb * kBQ + warp * 16 + g + 8 * r;
+    const size_t idx = (static_cast<size_t>(b) * H + h) * S + row_base + g + 8 * r;
     lr[r] = lse2[idx];
     dr[r] = Dv[idx];
   }
@@ -317,12 +333,12 @@ __global__ void __launch_bounds__(kAttnThreads)
 #pragma unroll
   for (int i = 0; i < HD / 8; ++i) dq[i][0] = dq[i][1] = dq[i][2] = dq[i][3] = 0.f;
 
-  const int nblk = qb + 1;
+  const int nblk = ((qb + 1) * BQ) / 64;
   for (int j = 0; j < nblk; ++j) {
     const int buf = j & 1;
     if (j + 1 < nblk) {
-      load_tile_async<HD>(sK + (buf ^ 1) * TILE, Kg + static_cast<size_t>(j + 1) * kBK * ldq, ldq);
-      load_tile_async<HD>(sV + (buf ^ 1) * TILE, Vg + static_cast<size_t>(j + 1) * kBK * ldq, ldq);
+      load_tile_async<HD>(sK + (buf ^ 1) * KT, Kg + static_cast<size_t>(j + 1) * 64 * ldq, ldq);
+      load_tile_async<HD>(sV + (buf ^ 1) * KT, Vg + static_cast<size_t>(j + 1) * 64 * ldq, ldq);
       cp_async_commit();
       cp_async_wait<1>();
     } else {
@@ -333,32 +349,34 @@ __global__ void __launch_bounds__(kAttnThreads)
       load_a_frags<HD>(sQ, warp * 16, qf);
       load_a_frags<HD>(sdO, warp * 16, of);
     }
-    float s[8][4], dp[8][4];
+    if (j * 64 <= row_base + 15) {
+      float sc[8][4], dp[8][4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
-      dp[i][0] = dp[i][1] = dp[i][2] = dp[i][3] = 0.f;
-    }
-    mma_a_tileT<HD>(qf, sK + buf * TILE, s);
-    mma_a_tileT<HD>(of, sV + buf * TILE, dp);
-    const bool diag = (j == qb);
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int r = e >> 1;
-        const int qrow = warp * 16 + g + 8 * r;
-        const int kcol = nt * 8 + 2 * t4 + (e & 1);
-        float pv = exp2f(s[nt][e] * scale_log2 - lr[r]);
-        if (diag && kcol > qrow) pv = 0.f;
-        s[nt][e] = pv * (dp[nt][e] - dr[r]);  // dS
+      for (int i = 0; i < 8; ++i) {
+        sc[i][0] = sc[i][1] = sc[i][2] = sc[i][3] = 0.f;
+        dp[i][0] = dp[i][1] = dp[i][2] = dp[i][3] = 0.f;
       }
-    mma_p_tile<HD>(s, sK + buf * TILE, dq);
+      mma_a_tileT<HD>(qf, sK + buf * KT, sc);
+      mma_a_tileT<HD>(of, sV + buf * KT, dp);
+      const bool diag = (j * 64 + 63 > row_base);
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int r = e >> 1;
+          const int qrow = row_base + g + 8 * r;
+          const int kcol = j * 64 + nt * 8 + 2 * t4 + (e & 1);
+          float pv = fast_exp2(sc[nt][e] * scale_log2 - lr[r]);
+          if (diag && kcol > qrow) pv = 0.f;
+          sc[nt][e] = pv * (dp[nt][e] - dr[r]);  // dS
+        }
+      mma_p_tile<HD>(sc, sK + buf * KT, dq);
+    }
     __syncthreads();
   }
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
-    const int qrow = qb * kBQ + warp * 16 + g + 8 * r;
+    const int qrow = row_base + g + 8 * r;
     __nv_bfloat16* out = dqkv + (tok0 + qrow) * ldq + h * HD;
 #pragma unroll
     for (int i = 0; i < HD / 8; ++i)
@@ -367,44 +385,59 @@ __global__ void __launch_bounds__(kAttnThreads)
   }
 }
 
-template <int HD>
-__global__ void __launch_bounds__(kAttnThreads)
+// dK / dV: a CTA owns BKV = 16 * WARPS key rows and walks the query blocks of 64.
+template <int HD, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32)
     attn_bwd_dkdv_kernel(const __nv_bfloat16* __restrict__ qkv,
                          const __nv_bfloat16* __restrict__ dout, const float* __restrict__ lse2,
                          const float* __restrict__ Dv, __nv_bfloat16* __restrict__ dqkv, int S,
-                         int H, int d, float scale_log2, float scale) {
+                         int H, int Hkv, int d, float scale_log2, float scale) {
   constexpr int LD = HD + 8;
-  constexpr int TILE = 64 * LD;
+  constexpr int BKV = 16 * WARPS;
+  constexpr int QT = 64 * LD;
   extern __shared__ __align__(16) __nv_bfloat16 sm_attn[];
   __nv_bfloat16* sK = sm_attn;
-  __nv_bfloat16* sV = sK + TILE;
-  __nv_bfloat16* sQ = sV + TILE;      // [2]
-  __nv_bfloat16* sdO = sQ + 2 * TILE;  // [2]
-  float* sL = reinterpret_cast<float*>(sdO + 2 * TILE);  // [2][64]
-  float* sD = sL + 128;                                  // [2][64]
+  __nv_bfloat16* sV = sK + BKV * LD;
+  __nv_bfloat16* sQ = sV + BKV * LD;  // [2]
+  __nv_bfloat16* sdO = sQ + 2 * QT;   // [2]
+  float* sL = reinterpret_cast<float*>(sdO + 2 * QT);  // [2][64]
+  float* sD = sL + 128;                                 // [2][64]
 
-  const int nq = gridDim.x;
-  const int kb = blockIdx.x;  // key block; later blocks have less work
-  const int h = blockIdx.y, b = blockIdx.z;
-  const int ldq = 3 * d;
+  const int nkb = gridDim.x;
+  const int kb = nkb - 1 - blockIdx.x;  // the heaviest key blocks (earliest keys) last
+  // Grid y runs over kv heads; a kv head sums the rep = H / Hkv query heads
+  // of its group in head order (deterministic, no atomics).
+  const int hk = blockIdx.y, b = blockIdx.z;
+  const int rep = H / Hkv, dkv = Hkv * HD;
+  const int ldq = d + 2 * dkv;
   const size_t tok0 = static_cast<size_t>(b) * S;
-  const __nv_bfloat16* Kg = qkv + (tok0 + kb * kBK) * ldq + d + h * HD;
-  const __nv_bfloat16* Vg = qkv + (tok0 + kb * kBK) * ldq + 2 * d + h * HD;
-  const __nv_bfloat16* Qg = qkv + tok0 * ldq + h * HD;
-  const __nv_bfloat16* dOg = dout + tok0 * d + h * HD;
-  const float* Lg = lse2 + (static_cast<size_t>(b) * H + h) * S;
-  const float* Dg = Dv + (static_cast<size_t>(b) * H + h) * S;
+  const __nv_bfloat16* Kg = qkv + (tok0 + kb * BKV) * ldq + d + hk * HD;
+  const __nv_bfloat16* Vg = qkv + (tok0 + kb * BKV) * ldq + d + dkv + hk * HD;
   const int warp = threadIdx.x >> 5, l = threadIdx.x & 31;
   const int g = l >> 2, t4 = l & 3;
+  const int krow_base = kb * BKV + warp * 16;
+  const int nq = S / 64;
+  const int q0 = (kb * BKV) / 64;  // first query block that sees these keys
+  const int nqs = nq - q0;
+  const int steps = rep * nqs;  // (query head of the group, query block) pairs
 
-  load_tile_async<HD>(sK, Kg, ldq);
-  load_tile_async<HD>(sV, Vg, ldq);
-  load_tile_async<HD>(sQ, Qg + static_cast<size_t>(kb) * kBQ * ldq, ldq);
-  load_tile_async<HD>(sdO, dOg + static_cast<size_t>(kb) * kBQ * d, d);
-  if (threadIdx.x < 64) {
-    sL[threadIdx.x] = Lg[kb * kBQ + threadIdx.x];
-    sD[threadIdx.x] = Dg[kb * kBQ + threadIdx.x];
-  }
+  // Stage step `it` (query head hk * rep + it / nqs, block q0 + it % nqs) into buffer nb.
+  auto stage = [&](int it, int nb) {
+    const int h = hk * rep + it / nqs, qi = q0 + it % nqs;
+    load_tile_async<HD>(sQ + nb * QT, qkv + (tok0 + static_cast<size_t>(qi) * 64) * ldq + h * HD,
+                        ldq);
+    load_tile_async<HD>(sdO + nb * QT, dout + (tok0 + static_cast<size_t>(qi) * 64) * d + h * HD,
+                        d);
+    if (threadIdx.x < 64) {
+      const size_t row = (static_cast<size_t>(b) * H + h) * S + qi * 64 + threadIdx.x;
+      sL[nb * 64 + threadIdx.x] = lse2[row];
+      sD[nb * 64 + threadIdx.x] = Dv[row];
+    }
+  };
+
+  load_tile_async<HD, BKV>(sK, Kg, ldq);
+  load_tile_async<HD, BKV>(sV, Vg, ldq);
+  stage(0, 0);
   cp_async_commit();
 
   float dk[HD / 8][4], dv[HD / 8][4];
@@ -413,66 +446,60 @@ __global__ void __launch_bounds__(kAttnThreads)
     dk[i][0] = dk[i][1] = dk[i][2] = dk[i][3] = 0.f;
     dv[i][0] = dv[i][1] = dv[i][2] = dv[i][3] = 0.f;
   }
-  for (int qi = kb; qi < nq; ++qi) {
-    const int buf = (qi - kb) & 1;
-    if (qi + 1 < nq) {
-      const int nb = buf ^ 1;
-      load_tile_async<HD>(sQ + nb * TILE, Qg + static_cast<size_t>(qi + 1) * kBQ * ldq, ldq);
-      load_tile_async<HD>(sdO + nb * TILE, dOg + static_cast<size_t>(qi + 1) * kBQ * d, d);
-      if (threadIdx.x < 64) {
-        sL[nb * 64 + threadIdx.x] = Lg[(qi + 1) * kBQ + threadIdx.x];
-        sD[nb * 64 + threadIdx.x] = Dg[(qi + 1) * kBQ + threadIdx.x];
-      }
+  for (int it = 0; it < steps; ++it) {
+    const int qi = q0 + it % nqs;
+    const int buf = it & 1;
+    if (it + 1 < steps) {
+      stage(it + 1, buf ^ 1);
       cp_async_commit();
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
     }
     __syncthreads();
-    const __nv_bfloat16* q_s = sQ + buf * TILE;
-    const __nv_bfloat16* do_s = sdO + buf * TILE;
+    const __nv_bfloat16* q_s = sQ + buf * QT;
+    const __nv_bfloat16* do_s = sdO + buf * QT;
     const float* l_s = sL + buf * 64;
     const float* d_s = sD + buf * 64;
-
-    // S^T[kv, q] = K Q^T for this warp's 16 key rows.
-    float st[8][4];
+    // Query blocks entirely before this warp's keys contribute nothing.
+    if (qi * 64 + 63 >= krow_base) {
+      // S^T[kv, q] = K Q^T for this warp's 16 key rows.
+      float st[8][4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) st[i][0] = st[i][1] = st[i][2] = st[i][3] = 0.f;
-    mma_tile_tileT<HD>(sK, warp * 16, q_s, st);
-    const bool diag = (qi == kb);
+      for (int i = 0; i < 8; ++i) st[i][0] = st[i][1] = st[i][2] = st[i][3] = 0.f;
+      mma_tile_tileT<HD>(sK, warp * 16, q_s, st);
+      const bool diag = (qi * 64 < krow_base + 16);
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt)
+      for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int krow = warp * 16 + g + 8 * (e >> 1);
-        const int qcol = nt * 8 + 2 * t4 + (e & 1);
-        float pv = exp2f(st[nt][e] * scale_log2 - l_s[qcol]);
-        if (diag && krow > qcol) pv = 0.f;
-        st[nt][e] = pv;  // P^T
-      }
-    // dV += P^T dO
-    mma_p_tile<HD>(st, do_s, dv);
-    // dP^T = V dO^T, then dS^T = P^T (dP^T - D)
-    float dpt[8][4];
+        for (int e = 0; e < 4; ++e) {
+          const int krow = krow_base + g + 8 * (e >> 1);
+          const int qcol = nt * 8 + 2 * t4 + (e & 1);
+          float pv = fast_exp2(st[nt][e] * scale_log2 - l_s[qcol]);
+          if (diag && krow > qi * 64 + qcol) pv = 0.f;
+          st[nt][e] = pv;  // P^T
+        }
+      mma_p_tile<HD>(st, do_s, dv);  // dV += P^T dO
+      float dpt[8][4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) dpt[i][0] = dpt[i][1] = dpt[i][2] = dpt[i][3] = 0.f;
-    mma_tile_tileT<HD>(sV, warp * 16, do_s, dpt);
+      for (int i = 0; i < 8; ++i) dpt[i][0] = dpt[i][1] = dpt[i][2] = dpt[i][3] = 0.f;
+      mma_tile_tileT<HD>(sV, warp * 16, do_s, dpt);  // dP^T = V dO^T
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt)
+      for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int qcol = nt * 8 + 2 * t4 + (e & 1);
-        st[nt][e] = st[nt][e] * (dpt[nt][e] - d_s[qcol]);
-      }
-    // dK += dS^T Q
-    mma_p_tile<HD>(st, q_s, dk);
+        for (int e = 0; e < 4; ++e) {
+          const int qcol = nt * 8 + 2 * t4 + (e & 1);
+          st[nt][e] = st[nt][e] * (dpt[nt][e] - d_s[qcol]);  // dS^T
+        }
+      mma_p_tile<HD>(st, q_s, dk);  // dK += dS^T Q
+    }
     __syncthreads();
   }
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
-    const int krow = kb * kBK + warp * 16 + g + 8 * r;
-    __nv_bfloat16* outk = dqkv + (tok0 + krow) * ldq + d + h * HD;
-    __nv_bfloat16* outv = dqkv + (tok0 + krow) * ldq + 2 * d + h * HD;
+    const int krow = krow_base + g + 8 * r;
+    __nv_bfloat16* outk = dqkv + (tok0 + krow) * ldq + d + hk * HD;
+    __nv_bfloat16* outv = dqkv + (tok0 + krow) * ldq + d + dkv + hk * HD;
 #pragma unroll
     for (int i = 0; i < HD / 8; ++i) {
       *reinterpret_cast<uint32_t*>(outk + 8 * i + 2 * t4) =
@@ -491,54 +518,59 @@ int set_smem(K kern, int bytes) {
              : 1;
 }
 
-template <int HD>
+template <int HD, int WARPS>
 int attn_fwd_hd(const AttnArgs& a, cudaStream_t stream) {
-  constexpr int TILE_BYTES = 64 * (HD + 8) * 2;
-  const int smem = 5 * TILE_BYTES;
-  if (set_smem(attn_fwd_kernel<HD>, smem)) return 2;
-  dim3 grid(a.S / kBQ, a.H, a.B);
-  attn_fwd_kernel<HD><<<grid, kAttnThreads, smem, stream>>>(a.qkv, a.o, a.lse, a.S, a.H, a.d,
-                                                           a.scale * kLog2e);
+  constexpr int LD = HD + 8;
+  const int smem = (16 * WARPS * LD + 4 * 64 * LD) * 2;
+  if (set_smem(attn_fwd_kernel<HD, WARPS>, smem)) return 2;
+  dim3 grid(a.S / (16 * WARPS), a.H, a.B);
+  attn_fwd_kernel<HD, WARPS><<<grid, WARPS * 32, smem, stream>>>(
+      a.qkv, a.o, a.lse, a.S, a.H, a.Hkv > 0 ? a.Hkv : a.H, a.d, a.scale * kLog2e);
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
 
-template <int HD>
+template <int HD, int WARPS>
 int attn_bwd_hd(const AttnBwdArgs& a, cudaStream_t stream) {
-  constexpr int TILE_BYTES = 64 * (HD + 8) * 2;
+  constexpr int LD = HD + 8;
   const int T = a.B * a.S;
   const int warps = T * a.H;
   attn_bwd_dot_kernel<<<(warps * 32 + 255) / 256, 256, 0, stream>>>(a.o, a.dout, a.Dbuf, T, a.S,
                                                                     a.H, HD, a.d);
-  const int smem_dq = 6 * TILE_BYTES;
-  const int smem_kv = 6 * TILE_BYTES + 4 * 64 * 4;
-  if (set_smem(attn_bwd_dq_kernel<HD>, smem_dq)) return 2;
-  if (set_smem(attn_bwd_dkdv_kernel<HD>, smem_kv)) return 2;
-  dim3 grid(a.S / kBQ, a.H, a.B);
-  attn_bwd_dkdv_kernel<HD><<<grid, kAttnThreads, smem_kv, stream>>>(
-      a.qkv, a.dout, a.lse, a.Dbuf, a.dqkv, a.S, a.H, a.d, a.scale * kLog2e, a.scale);
-  attn_bwd_dq_kernel<HD><<<grid, kAttnThreads, smem_dq, stream>>>(
-      a.qkv, a.dout, a.lse, a.Dbuf, a.dqkv, a.S, a.H, a.d, a.scale * kLog2e, a.scale);
+  const int smem_dq = (2 * 16 * WARPS * LD + 4 * 64 * LD) * 2;
+  const int smem_kv = (2 * 16 * WARPS * LD + 4 * 64 * LD) * 2 + 4 * 64 * 4;
+  if (set_smem(attn_bwd_dq_kernel<HD, WARPS>, smem_dq)) return 2;
+  if (set_smem(attn_bwd_dkdv_kernel<HD, WARPS>, smem_kv)) return 2;
+  const int hkv = a.Hkv > 0 ? a.Hkv : a.H;
+  dim3 grid_kv(a.S / (16 * WARPS), hkv, a.B);
+  dim3 grid_q(a.S / (16 * WARPS), a.H, a.B);
+  attn_bwd_dkdv_kernel<HD, WARPS><<<grid_kv, WARPS * 32, smem_kv, stream>>>(
+      a.qkv, a.dout, a.lse, a.Dbuf, a.dqkv, a.S, a.H, hkv, a.d, a.scale * kLog2e, a.scale);
+  attn_bwd_dq_kernel<HD, WARPS><<<grid_q, WARPS * 32, smem_dq, stream>>>(
+      a.qkv, a.dout, a.lse, a.Dbuf, a.dqkv, a.S, a.H, hkv, a.d, a.scale * kLog2e, a.scale);
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
 
 }  // namespace
 
+// Sequences that are a multiple of 128 use 8-warp CTAs (128 rows); others 4.
 int attention_fwd(const AttnArgs& a, cudaStream_t stream) {
-  if (a.S % 64 || a.d != a.H * a.hd) return 1;
+  if (a.S % 64 || a.d != a.H * a.hd || (a.Hkv > 0 && a.H % a.Hkv)) return 1;
+  const bool big = a.S % 128 == 0;
   switch (a.hd) {
-    case 64: return attn_fwd_hd<64>(a, stream);
-    case 80: return attn_fwd_hd<80>(a, stream);
-    case 128: return attn_fwd_hd<128>(a, stream);
+    case 64: return big ? attn_fwd_hd<64, 8>(a, stream) : attn_fwd_hd<64, 4>(a, stream);
+    case 80: return big ? attn_fwd_hd<80, 8>(a, stream) : attn_fwd_hd<80, 4>(a, stream);
+    case 128: return big ? attn_fwd_hd<128, 8>(a, stream) : attn_fwd_hd<128, 4>(a, stream);
     default: return 1;
   }
 }
 
 int attention_bwd(const AttnBwdArgs& a, cudaStream_t stream) {
-  if (a.S % 64 || a.d != a.H * a.hd) return 1;
+  if (a.S % 64 || a.d != a.H * a.hd || (a.Hkv > 0 && a.H % a.Hkv)) return 1;
+  const bool big = a.S % 128 == 0;
   switch (a.hd) {
-    case 64: return attn_bwd_hd<64>(a, stream);
-    case 80: return attn_bwd_hd<80>(a, stream);
-    case 128: return attn_bwd_hd<128>(a, stream);
+    case 64: return big ? attn_bwd_hd<64, 8>(a, stream) : attn_bwd_hd<64, 4>(a, stream);
+    case 80: return big ? attn_bwd_hd<80, 8>(a, stream) : attn_bwd_hd<80, 4>(a, stream);
+    case 128: return big ? attn_bwd_hd<128, 8>(a, stream) : attn_bwd_hd<128, 4>(a, stream);
     default: return 1;
   }
 }

@@ -176,8 +176,10 @@ void gemm_impl(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor out,
 
 int64_t gemm_pick_bn(int64_t M, int64_t N) { return ewb::gemm_pick_bn(M, N); }
 
+// beta absent = RMSNorm (no centring, no shift).
 void layernorm_fwd(at::Tensor x, c10::optional<at::Tensor> x_scale, at::Tensor gamma,
-                   at::Tensor beta, at::Tensor y, at::Tensor mean, at::Tensor rstd, double eps) {
+                   c10::optional<at::Tensor> beta, at::Tensor y, at::Tensor mean, at::Tensor rstd,
+                   double eps) {
   check_2d_rowmajor(x, "x");
   check_2d_rowmajor(y, "y");
   c10::cuda::CUDAGuard guard(x.device());
@@ -193,7 +195,8 @@ void layernorm_fwd(at::Tensor x, c10::optional<at::Tensor> x_scale, at::Tensor g
     TORCH_CHECK(x.scalar_type() == at::kBFloat16, "x must be bf16 or e4m3");
   }
   a.gamma = gamma.data_ptr<float>();
-  a.beta = beta.data_ptr<float>();
+  a.rms = !(beta.has_value() && beta->defined());
+  a.beta = a.rms ? nullptr : beta->data_ptr<float>();
   a.y = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
   a.ldy = y.stride(0);
   a.mean = mean.data_ptr<float>();
@@ -212,8 +215,8 @@ int64_t layernorm_bwd_chunks(int64_t rows) {
 
 void layernorm_bwd(at::Tensor dy, at::Tensor x, c10::optional<at::Tensor> x_scale, at::Tensor mean,
                    at::Tensor rstd, at::Tensor gamma, c10::optional<at::Tensor> dres,
-                   at::Tensor dx, at::Tensor part_g, at::Tensor part_b, at::Tensor dgamma,
-                   at::Tensor dbeta, bool accumulate) {
+                   at::Tensor dx, at::Tensor part_g, c10::optional<at::Tensor> part_b,
+                   at::Tensor dgamma, c10::optional<at::Tensor> dbeta, bool accumulate) {
   check_2d_rowmajor(dy, "dy");
   check_2d_rowmajor(x, "x");
   check_2d_rowmajor(dx, "dx");
@@ -242,18 +245,23 @@ void layernorm_bwd(at::Tensor dy, at::Tensor x, c10::optional<at::Tensor> x_scal
   a.rows_per_chunk = ewb::layernorm_bwd_rows_per_chunk(a.rows);
   const int chunks = (a.rows + a.rows_per_chunk - 1) / a.rows_per_chunk;
   TORCH_CHECK(part_g.numel() >= static_cast<int64_t>(chunks) * a.d, "part_g too small");
-  TORCH_CHECK(part_b.numel() >= static_cast<int64_t>(chunks) * a.d, "part_b too small");
+  a.rms = !(dbeta.has_value() && dbeta->defined());  // no beta gradient = RMSNorm
   a.part_g = part_g.data_ptr<float>();
-  a.part_b = part_b.data_ptr<float>();
   a.dgamma = dgamma.data_ptr<float>();
-  a.dbeta = dbeta.data_ptr<float>();
+  if (!a.rms) {
+    TORCH_CHECK(part_b.has_value() &&
+                    part_b->numel() >= static_cast<int64_t>(chunks) * a.d,
+                "part_b too small");
+    a.part_b = part_b->data_ptr<float>();
+    a.dbeta = dbeta->data_ptr<float>();
+  }
   a.accumulate = accumulate ? 1 : 0;
   ok(ewb::layernorm_bwd(a, cur_stream()), "layernorm_bwd");
   count(3);
 }
 
 void attention_fwd(at::Tensor qkv, at::Tensor o, at::Tensor lse, int64_t B, int64_t S, int64_t H,
-                   int64_t hd, double scale) {
+                   int64_t hd, double scale, int64_t Hkv) {
   check_cuda(qkv, "qkv");
   TORCH_CHECK(qkv.is_contiguous() && o.is_contiguous() && lse.is_contiguous(), "contiguous");
   c10::cuda::CUDAGuard guard(qkv.device());
@@ -267,13 +275,16 @@ void attention_fwd(at::Tensor qkv, at::Tensor o, at::Tensor lse, int64_t B, int6
   a.hd = hd;
   a.d = H * hd;
   a.scale = static_cast<float>(scale);
-  TORCH_CHECK(qkv.numel() == B * S * 3 * a.d, "qkv shape");
+  a.Hkv = static_cast<int>(Hkv);
+  const int64_t hkv = Hkv > 0 ? Hkv : H;
+  TORCH_CHECK(qkv.numel() == B * S * (a.d + 2 * hkv * hd), "qkv shape");
   ok(ewb::attention_fwd(a, cur_stream()), "attention_fwd");
   count(1);
 }
 
 void attention_bwd(at::Tensor qkv, at::Tensor o, at::Tensor dout, at::Tensor lse, at::Tensor Dbuf,
-                   at::Tensor dqkv, int64_t B, int64_t S, int64_t H, int64_t hd, double scale) {
+                   at::Tensor dqkv, int64_t B, int64_t S, int64_t H, int64_t hd, double scale,
+                   int64_t Hkv) {
   TORCH_CHECK(qkv.is_contiguous() && o.is_contiguous() && dout.is_contiguous() &&
                   dqkv.is_contiguous(),
               "contiguous");
@@ -291,8 +302,68 @@ void attention_bwd(at::Tensor qkv, at::Tensor o, at::Tensor dout, at::Tensor lse
   a.hd = hd;
   a.d = H * hd;
   a.scale = static_cast<float>(scale);
+  a.Hkv = static_cast<int>(Hkv);
+  TORCH_CHECK(dqkv.numel() == qkv.numel(), "dqkv shape");
   ok(ewb::attention_bwd(a, cur_stream()), "attention_bwd");
   count(3);
+}
+
+void rope(at::Tensor x, int64_t S, int64_t ncols, int64_t hd, at::Tensor cos_t, at::Tensor sin_t,
+          bool inverse) {
+  check_2d_rowmajor(x, "x");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16, "rope: x must be bf16");
+  TORCH_CHECK(cos_t.is_cuda() && sin_t.is_cuda() && cos_t.scalar_type() == at::kFloat &&
+                  cos_t.numel() >= S * (hd / 2) && sin_t.numel() >= S * (hd / 2),
+              "rope: tables must be fp32 [S][hd/2] on the device");
+  TORCH_CHECK(ncols <= x.size(1), "rope: ncols exceeds the row");
+  c10::cuda::CUDAGuard guard(x.device());
+  ewb::RopeArgs a{};
+  a.x = reinterpret_cast<__nv_bfloat16*>(x.data_ptr());
+  a.ld = x.stride(0);
+  a.rows = x.size(0);
+  a.S = S;
+  a.ncols = ncols;
+  a.hd = hd;
+  a.cos = cos_t.data_ptr<float>();
+  a.sin = sin_t.data_ptr<float>();
+  a.inverse = inverse ? 1 : 0;
+  ok(ewb::rope_apply(a, cur_stream()), "rope");
+  count(1);
+}
+
+void swiglu_fwd(at::Tensor gu, at::Tensor h) {
+  check_2d_rowmajor(gu, "gu");
+  check_2d_rowmajor(h, "h");
+  TORCH_CHECK(gu.size(1) == 2 * h.size(1) && gu.size(0) == h.size(0), "swiglu shapes");
+  c10::cuda::CUDAGuard guard(gu.device());
+  ewb::SwigluArgs a{};
+  a.gu = reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr());
+  a.ldgu = gu.stride(0);
+  a.h = reinterpret_cast<__nv_bfloat16*>(h.data_ptr());
+  a.ldh = h.stride(0);
+  a.rows = h.size(0);
+  a.f = h.size(1);
+  ok(ewb::swiglu_fwd(a, cur_stream()), "swiglu_fwd");
+  count(1);
+}
+
+void swiglu_bwd(at::Tensor dh, at::Tensor gu, at::Tensor dgu) {
+  check_2d_rowmajor(dh, "dh");
+  check_2d_rowmajor(gu, "gu");
+  check_2d_rowmajor(dgu, "dgu");
+  TORCH_CHECK(gu.sizes() == dgu.sizes() && gu.size(1) == 2 * dh.size(1), "swiglu_bwd shapes");
+  c10::cuda::CUDAGuard guard(gu.device());
+  ewb::SwigluBwdArgs a{};
+  a.dh = reinterpret_cast<const __nv_bfloat16*>(dh.data_ptr());
+  a.lddh = dh.stride(0);
+  a.gu = reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr());
+  a.ldgu = gu.stride(0);
+  a.dgu = reinterpret_cast<__nv_bfloat16*>(dgu.data_ptr());
+  a.lddgu = dgu.stride(0);
+  a.rows = dh.size(0);
+  a.f = dh.size(1);
+  ok(ewb::swiglu_bwd(a, cur_stream()), "swiglu_bwd");
+  count(1);
 }
 
 void cross_entropy(at::Tensor logits, int64_t V, at::Tensor targets, at::Tensor loss_rows,
@@ -326,14 +397,14 @@ void mean_reduce(at::Tensor x, at::Tensor out) {
   count(1);
 }
 
-void embed_fwd(at::Tensor idx, at::Tensor wte, at::Tensor wpe, int64_t S,
+void embed_fwd(at::Tensor idx, at::Tensor wte, c10::optional<at::Tensor> wpe, int64_t S,
                c10::optional<at::Tensor> out_bf16, c10::optional<at::Tensor> out_q8,
                c10::optional<at::Tensor> out_scale) {
   c10::cuda::CUDAGuard guard(idx.device());
   ewb::EmbedArgs a{};
   a.idx = idx.data_ptr<int64_t>();
   a.wte = wte.data_ptr<float>();
-  a.wpe = wpe.data_ptr<float>();
+  a.wpe = ptr_or_null<float>(wpe);
   a.T = idx.numel();
   a.S = S;
   a.d = wte.size(1);
@@ -346,7 +417,7 @@ void embed_fwd(at::Tensor idx, at::Tensor wte, at::Tensor wpe, int64_t S,
 }
 
 void embed_bwd(at::Tensor idx, at::Tensor dx, int64_t S, at::Tensor order, at::Tensor dwte,
-               at::Tensor dwpe) {
+               c10::optional<at::Tensor> dwpe) {
   c10::cuda::CUDAGuard guard(idx.device());
   ewb::EmbedBwdArgs a{};
   a.idx = idx.data_ptr<int64_t>();
@@ -357,7 +428,7 @@ void embed_bwd(at::Tensor idx, at::Tensor dx, int64_t S, at::Tensor order, at::T
   a.V = dwte.size(0);
   a.order = order.data_ptr<int>();
   a.dwte = dwte.data_ptr<float>();
-  a.dwpe = dwpe.data_ptr<float>();
+  a.dwpe = ptr_or_null<float>(dwpe);
   ok(ewb::embed_bwd(a, cur_stream()), "embed_bwd");
   count(3);
 }
@@ -517,6 +588,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("layernorm_bwd_chunks", &layernorm_bwd_chunks);
   m.def("attention_fwd", &attention_fwd);
   m.def("attention_bwd", &attention_bwd);
+  m.def("rope", &rope);
+  m.def("swiglu_fwd", &swiglu_fwd);
+  m.def("swiglu_bwd", &swiglu_bwd);
   m.def("cross_entropy", &cross_entropy);
   m.def("mean_reduce", &mean_reduce);
   m.def("embed_fwd", &embed_fwd);

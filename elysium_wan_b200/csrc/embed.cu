@@ -24,13 +24,13 @@ __global__ void __launch_bounds__(128)
   const int64_t tok = idx[t];
   const int pos = t % S;
   const float* er = wte + static_cast<size_t>(tok) * d;
-  const float* pr = wpe + static_cast<size_t>(pos) * d;
+  const float* pr = wpe != nullptr ? wpe + static_cast<size_t>(pos) * d : nullptr;  // rope: none
   for (int c0 = 0; c0 < d; c0 += 1024) {
     const int c = c0 + threadIdx.x * 8;
     float v[8];
     const bool ok = c < d;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = ok ? er[c + i] + pr[c + i] : 0.f;
+    for (int i = 0; i < 8; ++i) v[i] = ok ? er[c + i] + (pr != nullptr ? pr[c + i] : 0.f) : 0.f;
     if (out_q8 != nullptr) {
       // 16 consecutive threads cover one 128-column block.
       float amax = 0.f;
@@ -123,7 +123,7 @@ int embed_bwd(const EmbedBwdArgs& a, cudaStream_t stream) {
   if (a.T > 16384 || a.T % a.S) return 1;
   embed_rank_kernel<<<1, 1024, a.T * sizeof(int), stream>>>(a.idx, a.T, a.order);
   embed_wte_bwd_kernel<<<a.T, 256, 0, stream>>>(a.idx, a.dx, a.order, a.T, a.d, a.dwte);
-  embed_wpe_bwd_kernel<<<a.S, 256, 0, stream>>>(a.dx, a.T, a.S, a.d, a.dwpe);
+  if (a.dwpe != nullptr) embed_wpe_bwd_kernel<<<a.S, 256, 0, stream>>>(a.dx, a.T, a.S, a.d, a.dwpe);
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
 

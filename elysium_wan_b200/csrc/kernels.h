@@ -23,6 +23,7 @@ struct LnArgs {
   float* rstd;
   int rows, d;
   float eps;
+  int rms;  // RMSNorm: no centring, beta unused (may be null)
 };
 int layernorm_fwd(const LnArgs& a, cudaStream_t stream);
 
@@ -45,17 +46,21 @@ struct LnBwdArgs {
   float* dbeta;
   int accumulate;
   int rows, d, rows_per_chunk;
+  int rms;  // RMSNorm: part_b / dbeta unused (may be null)
 };
 int layernorm_bwd(const LnBwdArgs& a, cudaStream_t stream);
 int layernorm_bwd_rows_per_chunk(int rows);
 
 // ---------------------------------------------------------------- attention
+// qkv rows are [q (H heads) | k (Hkv heads) | v (Hkv heads)], hd columns per
+// head; Hkv = 0 means Hkv = H (multi-head), H % Hkv == 0 (grouped-query).
 struct AttnArgs {
-  const __nv_bfloat16* qkv;  // [B*S][3d]
+  const __nv_bfloat16* qkv;  // [B*S][d + 2 * Hkv * hd]
   __nv_bfloat16* o;  // [B*S][d]
   float* lse;  // [B][H][S] base-2 log-sum-exp
   int B, S, H, hd, d;
   float scale;  // softmax scale, 1/sqrt(hd)
+  int Hkv;
 };
 int attention_fwd(const AttnArgs& a, cudaStream_t stream);
 
@@ -65,9 +70,10 @@ struct AttnBwdArgs {
   const __nv_bfloat16* dout;
   const float* lse;
   float* Dbuf;  // [B][H][S] scratch
-  __nv_bfloat16* dqkv;  // [B*S][3d]
+  __nv_bfloat16* dqkv;  // same layout as qkv
   int B, S, H, hd, d;
   float scale;
+  int Hkv;
 };
 int attention_bwd(const AttnBwdArgs& a, cudaStream_t stream);
 
@@ -146,5 +152,37 @@ int zero1_adamw_push(const float* master, float* m, float* v, const float* g, lo
                      long long n, float* const* masters, __nv_bfloat16* const* works, int world,
                      float lr, float b1, float b2, float eps, float wd, float bc1, float bc2,
                      cudaStream_t stream);
+
+// ---------------------------------------------------------------- Llama family
+// Rotary embedding, in place on columns [0, ncols) of each row (q heads then
+// k heads, hd wide); row r sits at position r % S. Tables [S][hd / 2] fp32.
+struct RopeArgs {
+  __nv_bfloat16* x;
+  int ld, rows, S, ncols, hd;
+  const float* cos;
+  const float* sin;
+  int inverse;  // 1 = rotate back (the backward)
+};
+int rope_apply(const RopeArgs& a, cudaStream_t stream);
+
+// h = silu(gu[:, :f]) * gu[:, f:2f].
+struct SwigluArgs {
+  const __nv_bfloat16* gu;
+  int ldgu;
+  __nv_bfloat16* h;
+  int ldh, rows, f;
+};
+int swiglu_fwd(const SwigluArgs& a, cudaStream_t stream);
+
+// dgu[:, :f] = dh * u * silu'(g), dgu[:, f:] = dh * silu(g).
+struct SwigluBwdArgs {
+  const __nv_bfloat16* dh;
+  int lddh;
+  const __nv_bfloat16* gu;
+  int ldgu;
+  __nv_bfloat16* dgu;
+  int lddgu, rows, f;
+};
+int swiglu_bwd(const SwigluBwdArgs& a, cudaStream_t stream);
 
 }  // namespace ewb

@@ -64,7 +64,7 @@ __device__ __forceinline__ void store8_bf16(__nv_bfloat16* p, const float* v) {
   *reinterpret_cast<uint4*>(p) = w;
 }
 
-template <int S>
+template <int S, bool RMS>
 __global__ void __launch_bounds__(kLnThreads)
     layernorm_fwd_kernel(const void* __restrict__ x, const float* __restrict__ xs, int x_fp8,
                          int ldx, int ldxs, const float* __restrict__ gamma,
@@ -84,7 +84,8 @@ __global__ void __launch_bounds__(kLnThreads)
       for (int i = 0; i < 8; ++i) s += v[j][i];
     }
   }
-  const float mean = block_sum_128(s, red) / static_cast<float>(d);
+  // RMSNorm: no centring (mean 0), no shift.
+  const float mean = RMS ? 0.f : block_sum_128(s, red) / static_cast<float>(d);
   float q = 0.f;
 #pragma unroll
   for (int j = 0; j < S; ++j) {
@@ -105,7 +106,8 @@ __global__ void __launch_bounds__(kLnThreads)
     if (col < d) {
       float o[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = (v[j][i] - mean) * rstd * gamma[col + i] + beta[col + i];
+      for (int i = 0; i < 8; ++i)
+        o[i] = (v[j][i] - mean) * rstd * gamma[col + i] + (RMS ? 0.f : beta[col + i]);
       store8_bf16(y + static_cast<size_t>(row) * ldy + col, o);
     }
   }
@@ -117,7 +119,8 @@ __global__ void __launch_bounds__(kLnThreads)
 
 // dx = rstd * (g - mean(g) - xhat * mean(g * xhat)) (+ dres), g = dy * gamma.
 // Partial dgamma = sum dy * xhat and dbeta = sum dy over the rows of the chunk.
-template <int S>
+// RMSNorm (RMS = true): mean = 0 and no centring of g, dx = rstd * (g - xhat * mean(g * xhat)).
+template <int S, bool RMS>
 __global__ void __launch_bounds__(kLnThreads)
     layernorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, int lddy, const void* __restrict__ x,
                          const float* __restrict__ xs, int x_fp8, int ldx, int ldxs,
@@ -161,7 +164,7 @@ __global__ void __launch_bounds__(kLnThreads)
         }
       }
     }
-    const float m1 = block_sum_128(s1, red) / static_cast<float>(d);
+    const float m1 = RMS ? 0.f : block_sum_128(s1, red) / static_cast<float>(d);
     const float m2 = block_sum_128(s2, red) / static_cast<float>(d);
     // Second pass re-reads the row (L1/L2 resident) instead of holding it.
 #pragma unroll
@@ -194,7 +197,7 @@ __global__ void __launch_bounds__(kLnThreads)
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         part_g[static_cast<size_t>(chunk) * d + col + i] = pg[j][i];
-        part_b[static_cast<size_t>(chunk) * d + col + i] = pb[j][i];
+        if (!RMS) part_b[static_cast<size_t>(chunk) * d + col + i] = pb[j][i];
       }
     }
   }
@@ -215,10 +218,13 @@ __global__ void fold_partials_kernel(const float* __restrict__ part, int chunks,
 int layernorm_fwd(const LnArgs& a, cudaStream_t stream) {
   if (a.d % 8 || a.d > 1024 * kLnMaxSlices || (a.x_fp8 && a.d % 128)) return 1;
   const int S = (a.d + 1023) / 1024;
-#define EWB_LN_FWD(SS)                                                                         \
-  layernorm_fwd_kernel<SS><<<a.rows, kLnThreads, 0, stream>>>(a.x, a.x_scale, a.x_fp8, a.ldx,  \
-                                                              a.ldxs, a.gamma, a.beta, a.y,    \
-                                                              a.ldy, a.mean, a.rstd, a.d, a.eps)
+#define EWB_LN_FWD(SS)                                                                       \
+  (a.rms ? layernorm_fwd_kernel<SS, true><<<a.rows, kLnThreads, 0, stream>>>(                 \
+               a.x, a.x_scale, a.x_fp8, a.ldx, a.ldxs, a.gamma, a.beta, a.y, a.ldy, a.mean,   \
+               a.rstd, a.d, a.eps)                                                            \
+         : layernorm_fwd_kernel<SS, false><<<a.rows, kLnThreads, 0, stream>>>(                \
+               a.x, a.x_scale, a.x_fp8, a.ldx, a.ldxs, a.gamma, a.beta, a.y, a.ldy, a.mean,   \
+               a.rstd, a.d, a.eps))
   switch (S) {
     case 1: EWB_LN_FWD(1); break;
     case 2: EWB_LN_FWD(2); break;
@@ -244,10 +250,13 @@ int layernorm_bwd(const LnBwdArgs& a, cudaStream_t stream) {
   const int rpc = a.rows_per_chunk;
   const int chunks = (a.rows + rpc - 1) / rpc;
   const int S = (a.d + 1023) / 1024;
-#define EWB_LN_BWD(SS)                                                                      \
-  layernorm_bwd_kernel<SS><<<chunks, kLnThreads, 0, stream>>>(                              \
-      a.dy, a.lddy, a.x, a.x_scale, a.x_fp8, a.ldx, a.ldxs, a.mean, a.rstd, a.gamma, a.dres, \
-      a.lddres, a.dx, a.lddx, a.part_g, a.part_b, a.rows, a.d, rpc)
+#define EWB_LN_BWD(SS)                                                                        \
+  (a.rms ? layernorm_bwd_kernel<SS, true><<<chunks, kLnThreads, 0, stream>>>(                  \
+               a.dy, a.lddy, a.x, a.x_scale, a.x_fp8, a.ldx, a.ldxs, a.mean, a.rstd, a.gamma,  \
+               a.dres, a.lddres, a.dx, a.lddx, a.part_g, a.part_b, a.rows, a.d, rpc)          \
+         : layernorm_bwd_kernel<SS, false><<<chunks, kLnThreads, 0, stream>>>(                 \
+               a.dy, a.lddy, a.x, a.x_scale, a.x_fp8, a.ldx, a.ldxs, a.mean, a.rstd, a.gamma,  \
+               a.dres, a.lddres, a.dx, a.lddx, a.part_g, a.part_b, a.rows, a.d, rpc))
   switch (S) {
     case 1: EWB_LN_BWD(1); break;
     case 2: EWB_LN_BWD(2); break;
@@ -263,8 +272,9 @@ int layernorm_bwd(const LnBwdArgs& a, cudaStream_t stream) {
   const int tb = 256;
   fold_partials_kernel<<<(a.d + tb - 1) / tb, tb, 0, stream>>>(a.part_g, chunks, a.d, a.dgamma,
                                                                a.accumulate);
-  fold_partials_kernel<<<(a.d + tb - 1) / tb, tb, 0, stream>>>(a.part_b, chunks, a.d, a.dbeta,
-                                                               a.accumulate);
+  if (!a.rms)
+    fold_partials_kernel<<<(a.d + tb - 1) / tb, tb, 0, stream>>>(a.part_b, chunks, a.d, a.dbeta,
+                                                                 a.accumulate);
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
 

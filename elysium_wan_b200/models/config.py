@@ -1,14 +1,18 @@
 """GPT configuration, presets and precision recipes.
 
 Field names follow the reference's GPTConfig (src/wantrain/model/gpt.py:47-253)
-so a job JSON written for wantrain loads unchanged; knobs of the reference that
-this engine does not build (hf / user archs, MoE, LoRA) are accepted in the
-JSON and refused with a clear message at build time.
+so a job JSON written for wantrain loads unchanged. The block is the reference's
+generalized decoder (src/wantrain/model/arch.py): norm layernorm | rmsnorm,
+mlp gelu | swiglu, pos learned | rope, grouped-query attention (n_kv_head),
+bias on/off, tied embeddings, and the exact MoE block (moe_* fields). Knobs
+this engine does not build (arch "hf", user models) are accepted in the JSON
+and refused with a clear message at build time.
 """
 
 from __future__ import annotations
 
 import dataclasses
+import math
 from dataclasses import dataclass, field
 
 # Precision recipes (reference: src/wantrain/model/precision.py:18-162).
@@ -43,13 +47,69 @@ class GPTConfig:
     init_std: float = 0.02
     ln_eps: float = 1e-5
     n_kv_head: int | None = None
+    rope_theta: float = 10000.0
+    rms_eps: float = 1e-6
     lora_rank: int = 0
+    lora_alpha: float = 16.0
+    lora_targets: str = "attn"  # attn | attn_mlp | all
+    # Mixture of experts (reference arch.py:279-763); 0 experts = dense.
     moe_experts: int = 0
+    moe_top_k: int = 1
+    moe_d_ff: int | None = None
+    moe_shared_d_ff: int = 0
+    moe_shared_gate: str = "sigmoid"  # sigmoid | none
+    moe_layers: list | None = None  # 0-based block indices; None = every block
+    moe_router_dtype: str = "compute"  # compute | fp32
+    moe_router_bias: bool = False
+    moe_score: str = "softmax"  # softmax | softmax_k | sigmoid
+    moe_select: str = "score"  # score | logit | score_bias
+    moe_groups: int = 1
+    moe_topk_groups: int = 1
+    moe_norm: bool = False
+    moe_norm_eps: float = 0.0
+    moe_scale: float = 1.0
+    moe_apply: str = "output"  # output | input (k = 1)
+    moe_expert: str = "swiglu"  # swiglu | swiglu_clamped
+    moe_limit: float = 7.0
+    moe_alpha: float = 1.702
+    moe_lbl_coef: float = 0.0
+    moe_lbl_scope: str = "layer"  # layer | sequence
+    moe_z_coef: float = 0.0
+    moe_bias_rate: float = 0.0
     extras: dict = field(default_factory=dict)
 
     @property
     def ff(self) -> int:
-        return self.d_ff or 4 * self.d_model
+        """MLP width: 4 d for GELU, 8/3 d rounded up to a multiple of 256 for
+        SwiGLU (three matrices at about the parameter count of two)."""
+        if self.d_ff:
+            return self.d_ff
+        if self.mlp == "gelu":
+            return 4 * self.d_model
+        return int(math.ceil(8 * self.d_model / 3 / 256) * 256)
+
+    @property
+    def kv_heads(self) -> int:
+        return self.n_kv_head or self.n_head
+
+    @property
+    def qkv_width(self) -> int:
+        """Columns of the fused projection: q (n_head) + k, v (kv_heads)."""
+        return self.d_model + 2 * self.kv_heads * self.head_dim
+
+    @property
+    def norm_eps(self) -> float:
+        return self.ln_eps if self.norm == "layernorm" else self.rms_eps
+
+    @property
+    def moe_width(self) -> int:
+        return self.moe_d_ff or self.d_ff or int(math.ceil(8 * self.d_model / 3 / 256) * 256)
+
+    def is_moe_layer(self, entry: int) -> bool:
+        """Flat-list entry `entry` (block i is entry i + 1) is an MoE block."""
+        if self.moe_experts <= 0 or entry < 1 or entry > self.n_layer:
+            return False
+        return self.moe_layers is None or (entry - 1) in self.moe_layers
 
     @property
     def head_dim(self) -> int:
@@ -72,15 +132,24 @@ class GPTConfig:
             raise ValueError("d_model must be divisible by n_head")
         if self.arch != "builtin":
             raise NotImplementedError(
-                f"arch {self.arch!r}: only the built-in dense GPT is implemented in this engine")
-        if self.moe_experts or self.lora_rank:
-            raise NotImplementedError("MoE and LoRA are not implemented in this engine")
-        if (self.norm, self.mlp, self.pos, self.tie_embeddings) != ("layernorm", "gelu", "learned", False):
-            raise NotImplementedError("only LayerNorm / GELU / learned positions / untied head")
-        if self.n_kv_head not in (None, self.n_head):
-            raise NotImplementedError("GQA is not implemented")
+                f"arch {self.arch!r}: this engine builds the built-in decoder family only "
+                f"(GPT and Llama-style knobs, MoE); HF module trees and user models are not built")
+        for name, allowed in (("norm", ("layernorm", "rmsnorm")), ("mlp", ("gelu", "swiglu")),
+                              ("pos", ("learned", "rope")),
+                              ("lora_targets", ("attn", "attn_mlp", "all"))):
+            if getattr(self, name) not in allowed:
+                raise ValueError(f"{name}={getattr(self, name)!r} is not one of {allowed}")
+        if self.n_kv_head is not None and (self.n_kv_head < 1 or self.n_head % self.n_kv_head):
+            raise ValueError("n_head must be a multiple of n_kv_head")
+        if self.pos == "rope" and self.head_dim % 2:
+            raise ValueError("rope needs an even head_dim")
+        if self.tie_embeddings and self.init_scheme != "gpt2":
+            raise ValueError("tie_embeddings requires init_scheme='gpt2' (one scale for both uses)")
+        if self.lora_rank < 0:
+            raise ValueError("lora_rank must be >= 0")
         if self.fp8_boundary() and self.d_model % 128:
             raise ValueError("fp8_e4m3_b128 boundaries need d_model % 128 == 0")
+        check_moe(self)
         return self
 
     def to_dict(self) -> dict:
@@ -97,8 +166,20 @@ class GPTConfig:
 
     def n_params(self) -> int:
         d, V, S, f = self.d_model, self.vocab_size, self.seq_len, self.ff
-        block = 4 * d + 3 * d * d + 3 * d + d * d + d + d * f + f + f * d + d
-        return V * d + S * d + self.n_layer * block + 2 * d + V * d
+        b = 1 if self.bias else 0
+        nrm = d * (2 if self.norm == "layernorm" else 1)
+        attn = self.qkv_width * d + b * self.qkv_width + d * d + b * d
+        mats = 3 if self.mlp == "swiglu" else 2
+        dense_mlp = mats * d * f + b * ((mats - 1) * f + d)
+        E = self.moe_experts
+        moe_mlp = (d * E + (E if self.moe_router_bias else 0)
+                   + E * 3 * d * self.moe_width
+                   + (3 * d * self.moe_shared_d_ff if self.moe_shared_d_ff else 0)
+                   + (d if self.moe_shared_d_ff and self.moe_shared_gate == "sigmoid" else 0))
+        total = V * d + (S * d if self.pos == "learned" else 0) + nrm
+        for e in range(1, self.n_layer + 1):
+            total += 2 * nrm + attn + (moe_mlp if self.is_moe_layer(e) else dense_mlp)
+        return total + (0 if self.tie_embeddings else V * d)
 
 
 # Reference presets (gpt.py:258-268) plus the BASELINE shapes.
@@ -120,7 +201,69 @@ PRESETS: dict[str, dict] = {
                    compute_dtype="bf16", boundary_dtype="fp8_e4m3_b128"),
     "gpt25b": dict(vocab_size=50257, n_layer=60, n_head=46, d_model=5888, d_ff=23552,
                    seq_len=2048, compute_dtype="bf16", boundary_dtype="fp8_e4m3_b128"),
+    # Llama-style decoders (RMSNorm, SwiGLU, RoPE, GQA, no bias).
+    "llama_tiny": dict(vocab_size=512, n_layer=4, n_head=4, n_kv_head=2, d_model=256, seq_len=128,
+                       norm="rmsnorm", mlp="swiglu", pos="rope", bias=False, init_scheme="gpt2"),
+    "llama1b": dict(vocab_size=32768, n_layer=16, n_head=32, n_kv_head=8, d_model=2048,
+                    seq_len=2048, norm="rmsnorm", mlp="swiglu", pos="rope", bias=False,
+                    rope_theta=500000.0, init_scheme="gpt2", compute_dtype="bf16",
+                    boundary_dtype="bf16"),
+    "llama8b": dict(vocab_size=128256, n_layer=32, n_head=32, n_kv_head=8, d_model=4096,
+                    d_ff=14336, seq_len=2048, norm="rmsnorm", mlp="swiglu", pos="rope",
+                    bias=False, rope_theta=500000.0, init_scheme="gpt2", compute_dtype="bf16",
+                    boundary_dtype="bf16"),
+    # A small mixture-of-experts decoder (8 experts, top-2, shared expert).
+    "moe_tiny": dict(vocab_size=512, n_layer=4, n_head=4, n_kv_head=2, d_model=256, seq_len=128,
+                     norm="rmsnorm", mlp="swiglu", pos="rope", bias=False, init_scheme="gpt2",
+                     moe_experts=8, moe_top_k=2, moe_d_ff=256, moe_shared_d_ff=256,
+                     moe_lbl_coef=0.01, moe_z_coef=0.001),
 }
+
+
+def check_moe(cfg) -> None:
+    """The MoE construction rules (reference arch.py:338-391); each refusal
+    names the field."""
+    E, k = cfg.moe_experts, cfg.moe_top_k
+    if E < 0:
+        raise ValueError(f"moe_experts={E} must be >= 0")
+    if E == 0:
+        return
+    if not 1 <= k <= E:
+        raise ValueError(f"moe_top_k={k} must satisfy 1 <= moe_top_k <= moe_experts={E}")
+    for name, allowed in (("moe_router_dtype", ("compute", "fp32")),
+                          ("moe_score", ("softmax", "softmax_k", "sigmoid")),
+                          ("moe_select", ("score", "logit", "score_bias")),
+                          ("moe_shared_gate", ("sigmoid", "none")),
+                          ("moe_apply", ("output", "input")),
+                          ("moe_expert", ("swiglu", "swiglu_clamped")),
+                          ("moe_lbl_scope", ("layer", "sequence"))):
+        if getattr(cfg, name) not in allowed:
+            raise ValueError(f"{name}={getattr(cfg, name)!r} is not one of {allowed}")
+    if cfg.moe_apply == "input" and k != 1:
+        raise ValueError(f"moe_apply='input' requires moe_top_k=1, got moe_top_k={k}")
+    G, Gt = cfg.moe_groups, cfg.moe_topk_groups
+    if G < 1:
+        raise ValueError(f"moe_groups={G} must be >= 1")
+    if G > 1:
+        if E % G:
+            raise ValueError(f"moe_groups={G} must divide moe_experts={E}")
+        if E // G < 2:
+            raise ValueError(f"moe_groups={G}: moe_experts/moe_groups={E // G} must be >= 2")
+        if not 1 <= Gt <= G:
+            raise ValueError(f"moe_topk_groups={Gt} must satisfy 1 <= moe_topk_groups <= {G}")
+        if k > Gt * (E // G):
+            raise ValueError(f"moe_top_k={k} exceeds moe_topk_groups*moe_experts/moe_groups="
+                             f"{Gt * (E // G)}")
+    elif Gt != 1:
+        raise ValueError(f"moe_topk_groups={Gt} requires moe_groups > 1")
+    if cfg.moe_d_ff is not None and cfg.moe_d_ff < 1:
+        raise ValueError(f"moe_d_ff={cfg.moe_d_ff} must be >= 1")
+    if cfg.moe_shared_d_ff < 0:
+        raise ValueError(f"moe_shared_d_ff={cfg.moe_shared_d_ff} must be >= 0")
+    if cfg.moe_bias_rate < 0:
+        raise ValueError(f"moe_bias_rate={cfg.moe_bias_rate} must be >= 0")
+    if cfg.moe_lbl_coef < 0 or cfg.moe_z_coef < 0:
+        raise ValueError("moe_lbl_coef and moe_z_coef must be >= 0")
 
 
 def make_config(preset: str, **overrides) -> GPTConfig:

@@ -3,7 +3,9 @@ explicit forward (F), input-gradient backward (B) and deferred weight-gradient
 pass (W) per layer.
 
 Reference: src/wantrain/model/gpt.py:301-557 (Embed / Block / Head, pre-LN,
-learned positions, fused qkv, 4x GELU MLP with biases, untied head) and the
+learned positions, fused qkv, 4x GELU MLP with biases, untied head), the
+generalized block of src/wantrain/model/arch.py:1-270 (RMSNorm, SwiGLU, RoPE,
+GQA, no bias, tied embeddings; MoE in moe.py) and the
 zero-bubble B/W split of src/wantrain/model/wgrad.py:45-303. The reference
 obtains B from autograd and defers dW = dY^T X through a SplitLinear store;
 here each layer writes its backward explicitly, so B is exactly the
@@ -52,31 +54,86 @@ class Act:
         return [self.x] if self.scale is None else [self.x, self.scale]
 
 
+def uses_general_arch(cfg: GPTConfig) -> bool:
+    """Any non-default knob selects the generalized block (the reference's
+    dispatch in src/wantrain/model/gpt.py:470-476), whose parameter names
+    follow src/wantrain/model/arch.py (mlp.fc1, mlp.gate, q / kv, ...)."""
+    return (cfg.norm != "layernorm" or cfg.mlp != "gelu" or cfg.pos != "learned"
+            or cfg.n_kv_head is not None or not cfg.bias or cfg.tie_embeddings
+            or cfg.d_ff is not None or cfg.moe_experts > 0)
+
+
+def _linear(name, out_f, in_f, bias, resid=False, pack=False):
+    """pack: the partner listed next is read together with this one (its
+    weight after this weight, its bias after this bias)."""
+    w = ParamSpec(f"{name}.weight", (out_f, in_f), "normal_resid" if resid else "normal",
+                  fan_in=in_f, matrix=True, pack=pack)
+    return [w], ([ParamSpec(f"{name}.bias", (out_f,), "bias", fan_in=in_f, pack=pack)]
+                 if bias else [])
+
+
+def _norm_specs(name, d, layernorm):
+    out = [ParamSpec(f"{name}.weight", (d,), "ones")]
+    if layernorm:
+        out.append(ParamSpec(f"{name}.bias", (d,), "zeros"))
+    return out
+
+
 def entry_specs(cfg: GPTConfig, e: int) -> list[ParamSpec]:
     """Parameter specs of flat-list entry e, named like the reference's
-    nn.ModuleList ("{e}.qkv.weight", ...)."""
+    nn.ModuleList ("{e}.qkv.weight", ...). Matrices one GEMM reads as one
+    operand (q with kv, gate with up) are listed back to back, then their
+    biases, so the store holds each group contiguously."""
     d, V, S, f, n = cfg.d_model, cfg.vocab_size, cfg.seq_len, cfg.ff, cfg.n_layer
     if e == 0:
-        return [ParamSpec(f"{e}.tok.weight", (V, d), "embed"),
-                ParamSpec(f"{e}.pos.weight", (S, d), "embed")]
+        out = [ParamSpec(f"{e}.tok.weight", (V, d), "embed")]
+        if cfg.pos == "learned":
+            out.append(ParamSpec(f"{e}.pos.weight", (S, d), "embed"))
+        return out
+    ln = cfg.norm == "layernorm"
     if e == n + 1:
-        return [ParamSpec(f"{e}.ln_f.weight", (d,), "ones"),
-                ParamSpec(f"{e}.ln_f.bias", (d,), "zeros"),
-                ParamSpec(f"{e}.out.weight", (V, d), "normal", fan_in=d, matrix=True)]
-    return [
-        ParamSpec(f"{e}.ln1.weight", (d,), "ones"),
-        ParamSpec(f"{e}.ln1.bias", (d,), "zeros"),
-        ParamSpec(f"{e}.qkv.weight", (3 * d, d), "normal", fan_in=d, matrix=True),
-        ParamSpec(f"{e}.qkv.bias", (3 * d,), "bias", fan_in=d),
-        ParamSpec(f"{e}.proj.weight", (d, d), "normal_resid", fan_in=d, matrix=True),
-        ParamSpec(f"{e}.proj.bias", (d,), "bias", fan_in=d),
-        ParamSpec(f"{e}.ln2.weight", (d,), "ones"),
-        ParamSpec(f"{e}.ln2.bias", (d,), "zeros"),
-        ParamSpec(f"{e}.fc1.weight", (f, d), "normal", fan_in=d, matrix=True),
-        ParamSpec(f"{e}.fc1.bias", (f,), "bias", fan_in=d),
-        ParamSpec(f"{e}.fc2.weight", (d, f), "normal_resid", fan_in=f, matrix=True),
-        ParamSpec(f"{e}.fc2.bias", (d,), "bias", fan_in=f),
-    ]
+        out = _norm_specs(f"{e}.ln_f", d, ln)
+        if not cfg.tie_embeddings:
+            out.append(ParamSpec(f"{e}.out.weight", (V, d), "normal", fan_in=d, matrix=True))
+        return out
+    if not uses_general_arch(cfg):
+        return [
+            ParamSpec(f"{e}.ln1.weight", (d,), "ones"),
+            ParamSpec(f"{e}.ln1.bias", (d,), "zeros"),
+            ParamSpec(f"{e}.qkv.weight", (3 * d, d), "normal", fan_in=d, matrix=True),
+            ParamSpec(f"{e}.qkv.bias", (3 * d,), "bias", fan_in=d),
+            ParamSpec(f"{e}.proj.weight", (d, d), "normal_resid", fan_in=d, matrix=True),
+            ParamSpec(f"{e}.proj.bias", (d,), "bias", fan_in=d),
+            ParamSpec(f"{e}.ln2.weight", (d,), "ones"),
+            ParamSpec(f"{e}.ln2.bias", (d,), "zeros"),
+            ParamSpec(f"{e}.fc1.weight", (f, d), "normal", fan_in=d, matrix=True),
+            ParamSpec(f"{e}.fc1.bias", (f,), "bias", fan_in=d),
+            ParamSpec(f"{e}.fc2.weight", (d, f), "normal_resid", fan_in=f, matrix=True),
+            ParamSpec(f"{e}.fc2.bias", (d,), "bias", fan_in=f),
+        ]
+    b = cfg.bias
+    out = _norm_specs(f"{e}.ln1", d, ln)
+    if cfg.kv_heads == cfg.n_head:
+        w, bb = _linear(f"{e}.qkv", 3 * d, d, b)
+        out += w + bb
+    else:
+        wq, bq = _linear(f"{e}.q", d, d, b, pack=True)
+        wkv, bkv = _linear(f"{e}.kv", 2 * cfg.kv_heads * cfg.head_dim, d, b)
+        out += wq + wkv + bq + bkv
+    w, bb = _linear(f"{e}.proj", d, d, b, resid=True)
+    out += w + bb + _norm_specs(f"{e}.ln2", d, ln)
+    if cfg.is_moe_layer(e):
+        from .moe import moe_specs
+
+        return out + moe_specs(cfg, e)
+    if cfg.mlp == "gelu":
+        w1, b1 = _linear(f"{e}.mlp.fc1", f, d, b)
+        w2, b2 = _linear(f"{e}.mlp.fc2", d, f, b, resid=True)
+        return out + w1 + b1 + w2 + b2
+    wg, bg = _linear(f"{e}.mlp.gate", f, d, b, pack=True)
+    wu, bu = _linear(f"{e}.mlp.up", f, d, b)
+    wd, bd = _linear(f"{e}.mlp.down", d, f, b, resid=True)
+    return out + wg + wu + bg + bu + wd + bd
 
 
 class WTask:
@@ -135,68 +192,161 @@ class WExecutor:
 class Embed:
     def __init__(self, cfg, store: ParamStore, e: int):
         self.cfg, self.s, self.e = cfg, store, e
+        self.has_pos = cfg.pos == "learned"
 
     def forward(self, tokens: torch.Tensor, ctx: dict) -> Act:
         c = self.cfg
         ctx["tokens"] = tokens
-        out = ops.embed_fwd(tokens, self.s.p(f"{self.e}.tok.weight"),
-                            self.s.p(f"{self.e}.pos.weight"), c.seq_len, c.fp8_boundary(),
+        wpe = self.s.p(f"{self.e}.pos.weight") if self.has_pos else None
+        out = ops.embed_fwd(tokens, self.s.p(f"{self.e}.tok.weight"), wpe, c.seq_len,
+                            c.fp8_boundary(),
                             out_dtype=torch.float32 if not tokens.is_cuda else torch.bfloat16)
         return Act(*out) if isinstance(out, tuple) else Act(out)
 
     def backward(self, ctx: dict, dy: torch.Tensor, wq: list):
-        ops.embed_bwd(ctx["tokens"], dy, self.cfg.seq_len, self.s.g(f"{self.e}.tok.weight"),
-                      self.s.g(f"{self.e}.pos.weight"))
+        dwpe = self.s.g(f"{self.e}.pos.weight") if self.has_pos else None
+        ops.embed_bwd(ctx["tokens"], dy, self.cfg.seq_len, self.s.g(f"{self.e}.tok.weight"), dwpe)
         return None
 
 
+def _boundary_out(cfg, y) -> Act:
+    """The block output in the boundary dtype (bf16 rounding on the CPU
+    plumbing path when the boundary is bf16)."""
+    if not y.is_cuda and cfg.boundary_dtype == "bf16":
+        y = y.to(torch.bfloat16).float()
+    return Act(y)
+
+
 class Block:
+    """One decoder block. Default knobs: the built-in GPT block (pre-LN,
+    fused qkv, 4x GELU MLP with biases). Otherwise the generalized block:
+    LayerNorm or RMSNorm, q / kv projections for grouped-query attention,
+    rotary positions on q and k, GELU or SwiGLU MLP or the MoE block, biases
+    optional."""
+
     def __init__(self, cfg, store: ParamStore, e: int):
         self.cfg, self.s, self.e = cfg, store, e
         self.n = lambda k: f"{e}.{k}"
+        n = self.n
+        gen = uses_general_arch(cfg)
+        self.rms = cfg.norm == "rmsnorm"
+        self.eps = cfg.norm_eps
+        self.bias = cfg.bias
+        if cfg.kv_heads == cfg.n_head:
+            self.qkv_w, self.qkv_b = [n("qkv.weight")], [n("qkv.bias")]
+        else:
+            self.qkv_w, self.qkv_b = [n("q.weight"), n("kv.weight")], [n("q.bias"), n("kv.bias")]
+        self.moe = None
+        if cfg.is_moe_layer(e):
+            from .moe import MoEMLP
+
+            self.moe = MoEMLP(cfg, store, e)
+            self.mlp = "moe"
+        elif not gen:
+            self.mlp = "gelu"
+            self.up_w, self.up_b = [n("fc1.weight")], [n("fc1.bias")]
+            self.dn_w, self.dn_b = n("fc2.weight"), n("fc2.bias")
+        elif cfg.mlp == "gelu":
+            self.mlp = "gelu"
+            self.up_w, self.up_b = [n("mlp.fc1.weight")], [n("mlp.fc1.bias")]
+            self.dn_w, self.dn_b = n("mlp.fc2.weight"), n("mlp.fc2.bias")
+        else:
+            self.mlp = "swiglu"
+            self.up_w = [n("mlp.gate.weight"), n("mlp.up.weight")]
+            self.up_b = [n("mlp.gate.bias"), n("mlp.up.bias")]
+            self.dn_w, self.dn_b = n("mlp.down.weight"), n("mlp.down.bias")
+
+    # parameter accessors (biases None when the block has none)
+    def _w(self, names):
+        return self.s.wj(names) if len(names) > 1 else self.s.w(names[0])
+
+    def _bp(self, names):
+        if not self.bias:
+            return None
+        return self.s.pj(names) if len(names) > 1 else self.s.p(names[0])
+
+    def _bg(self, names):
+        if not self.bias:
+            return None
+        return self.s.gj(names) if len(names) > 1 else self.s.g(names[0])
+
+    def _gw(self, names):
+        return self.s.gj(names) if len(names) > 1 else self.s.g(names[0])
+
+    def _norm(self, x, xs, which):
+        s, n = self.s, self.n
+        beta = None if self.rms else s.p(n(f"{which}.bias"))
+        return ops.layernorm_fwd(x, xs, s.p(n(f"{which}.weight")), beta, self.eps)
+
+    def _norm_bwd(self, dy, x, xs, m, r, which, dres):
+        s, n = self.s, self.n
+        dbeta = None if self.rms else s.g(n(f"{which}.bias"))
+        return ops.layernorm_bwd(dy, x, xs, m, r, s.p(n(f"{which}.weight")), dres,
+                                 s.g(n(f"{which}.weight")), dbeta, accumulate=True)
 
     def forward(self, x: Act, ctx: dict) -> Act:
         c, s, n = self.cfg, self.s, self.n
         T = x.rows
         B, S, H, hd = T // c.seq_len, c.seq_len, c.n_head, c.head_dim
-        h1, m1, r1 = ops.layernorm_fwd(x.x, x.scale, s.p(n("ln1.weight")), s.p(n("ln1.bias")), c.ln_eps)
-        qkv = ops.linear_fwd(h1, s.w(n("qkv.weight")), s.p(n("qkv.bias")))
-        o, lse = ops.attention_fwd(qkv, B, S, H, hd)
-        x2 = ops.linear_fwd(o, s.w(n("proj.weight")), s.p(n("proj.bias")), epi="resid",
+        h1, m1, r1 = self._norm(x.x, x.scale, "ln1")
+        qkv = ops.linear_fwd(h1, self._w(self.qkv_w), self._bp(self.qkv_b))
+        if c.pos == "rope":
+            ops.rope(qkv, S, c.d_model + c.kv_heads * hd, hd, c.rope_theta)
+        o, lse = ops.attention_fwd(qkv, B, S, H, hd, c.kv_heads)
+        x2 = ops.linear_fwd(o, s.w(n("proj.weight")), self._bp([n("proj.bias")]), epi="resid",
                             resid=x.x, resid_scale=x.scale)
-        h2, m2, r2 = ops.layernorm_fwd(x2, None, s.p(n("ln2.weight")), s.p(n("ln2.bias")), c.ln_eps)
-        g, u = ops.linear_fwd(h2, s.w(n("fc1.weight")), s.p(n("fc1.bias")), epi="gelu")
-        if c.fp8_boundary():
-            q, sc = ops.linear_fwd(g, s.w(n("fc2.weight")), s.p(n("fc2.bias")), epi="resid_q8",
-                                   resid=x2)
-            out = Act(q, sc)
+        h2, m2, r2 = self._norm(x2, None, "ln2")
+        ctx.update(x=x, h1=h1, m1=m1, r1=r1, qkv=qkv, o=o, lse=lse, x2=x2, h2=h2, m2=m2, r2=r2)
+        q8 = c.fp8_boundary()
+        if self.mlp == "moe":
+            y = self.moe.forward(h2, ctx)
+            out = ops.residual_add(x2, y)  # x2 + y in the compute dtype
+            if q8:
+                return Act(*ops.quant_e4m3(out))
+            return _boundary_out(c, out)
+        if self.mlp == "gelu":
+            g, u = ops.linear_fwd(h2, self._w(self.up_w), self._bp(self.up_b), epi="gelu")
+            ctx.update(g=g, u=u)
+            hin = g
         else:
-            y = ops.linear_fwd(g, s.w(n("fc2.weight")), s.p(n("fc2.bias")), epi="resid", resid=x2)
-            if not y.is_cuda and c.boundary_dtype == "bf16":
-                y = y.to(torch.bfloat16).float()
-            out = Act(y)
-        ctx.update(x=x, h1=h1, m1=m1, r1=r1, qkv=qkv, o=o, lse=lse, x2=x2, h2=h2, m2=m2, r2=r2,
-                   g=g, u=u)
-        return out
+            gu = ops.linear_fwd(h2, self._w(self.up_w), self._bp(self.up_b))
+            hin = ops.swiglu_fwd(gu)
+            ctx.update(gu=gu, g=hin)
+        bdn = self._bp([self.dn_b])
+        if q8:
+            q, sc = ops.linear_fwd(hin, s.w(self.dn_w), bdn, epi="resid_q8", resid=x2)
+            return Act(q, sc)
+        y = ops.linear_fwd(hin, s.w(self.dn_w), bdn, epi="resid", resid=x2)
+        return _boundary_out(c, y)
 
     def backward(self, ctx: dict, dy: torch.Tensor, wq: list) -> torch.Tensor:
         c, s, n = self.cfg, self.s, self.n
         T = dy.shape[0]
         B, S, H, hd = T // c.seq_len, c.seq_len, c.n_head, c.head_dim
         x: Act = ctx["x"]
-        du = ops.linear_dx(dy, s.w(n("fc2.weight")), gelu_u=ctx["u"])
-        wq.append(WTask(dy, ctx["g"], s.g(n("fc2.weight")), s.g(n("fc2.bias"))))
-        dh2 = ops.linear_dx(du, s.w(n("fc1.weight")))
-        wq.append(WTask(du, ctx["h2"], s.g(n("fc1.weight")), s.g(n("fc1.bias"))))
-        dx2 = ops.layernorm_bwd(dh2, ctx["x2"], None, ctx["m2"], ctx["r2"], s.p(n("ln2.weight")), dy,
-                                s.g(n("ln2.weight")), s.g(n("ln2.bias")), accumulate=True)
+        if self.mlp == "moe":
+            dh2 = self.moe.backward(ctx, dy, wq)
+        elif self.mlp == "gelu":
+            du = ops.linear_dx(dy, s.w(self.dn_w), gelu_u=ctx["u"])
+            wq.append(WTask(dy, ctx["g"], s.g(self.dn_w), self._bg([self.dn_b])))
+            dh2 = ops.linear_dx(du, self._w(self.up_w))
+            wq.append(WTask(du, ctx["h2"], self._gw(self.up_w), self._bg(self.up_b)))
+        else:
+            dh = ops.linear_dx(dy, s.w(self.dn_w))
+            wq.append(WTask(dy, ctx["g"], s.g(self.dn_w), self._bg([self.dn_b])))
+            dgu = ops.swiglu_bwd(dh, ctx["gu"])
+            del dh
+            dh2 = ops.linear_dx(dgu, self._w(self.up_w))
+            wq.append(WTask(dgu, ctx["h2"], self._gw(self.up_w), self._bg(self.up_b)))
+        dx2 = self._norm_bwd(dh2, ctx["x2"], None, ctx["m2"], ctx["r2"], "ln2", dy)
         do = ops.linear_dx(dx2, s.w(n("proj.weight")))
-        wq.append(WTask(dx2, ctx["o"], s.g(n("proj.weight")), s.g(n("proj.bias"))))
-        dqkv = ops.attention_bwd(ctx["qkv"], ctx["o"], do, ctx["lse"], B, S, H, hd)
-        dh1 = ops.linear_dx(dqkv, s.w(n("qkv.weight")))
-        wq.append(WTask(dqkv, ctx["h1"], s.g(n("qkv.weight")), s.g(n("qkv.bias"))))
-        dx = ops.layernorm_bwd(dh1, x.x, x.scale, ctx["m1"], ctx["r1"], s.p(n("ln1.weight")), dx2,
-                               s.g(n("ln1.weight")), s.g(n("ln1.bias")), accumulate=True)
+        wq.append(WTask(dx2, ctx["o"], s.g(n("proj.weight")), self._bg([n("proj.bias")])))
+        dqkv = ops.attention_bwd(ctx["qkv"], ctx["o"], do, ctx["lse"], B, S, H, hd, c.kv_heads)
+        if c.pos == "rope":
+            ops.rope(dqkv, S, c.d_model + c.kv_heads * hd, hd, c.rope_theta, inverse=True)
+        dh1 = ops.linear_dx(dqkv, self._w(self.qkv_w))
+        wq.append(WTask(dqkv, ctx["h1"], self._gw(self.qkv_w), self._bg(self.qkv_b)))
+        dx = self._norm_bwd(dh1, x.x, x.scale, ctx["m1"], ctx["r1"], "ln1", dx2)
         ctx.clear()
         return dx
 
@@ -205,6 +355,9 @@ class Head:
     def __init__(self, cfg, store: ParamStore, e: int):
         self.cfg, self.s, self.e = cfg, store, e
         self.n = lambda k: f"{e}.{k}"
+        self.rms = cfg.norm == "rmsnorm"
+        # A tied head reads (and adds its gradient into) the embedding table.
+        self.out = "0.tok.weight" if cfg.tie_embeddings else f"{e}.out.weight"
 
     def forward(self, x: Act, ctx: dict, targets: torch.Tensor):
         """LN_f -> logits (fp32) -> mean CE. Returns the loss (device scalar);
@@ -212,13 +365,14 @@ class Head:
         c, s, n = self.cfg, self.s, self.n
         T = x.rows
         V = c.vocab_size
-        h, m, r = ops.layernorm_fwd(x.x, x.scale, s.p(n("ln_f.weight")), s.p(n("ln_f.bias")), c.ln_eps)
+        beta = None if self.rms else s.p(n("ln_f.bias"))
+        h, m, r = ops.layernorm_fwd(x.x, x.scale, s.p(n("ln_f.weight")), beta, c.norm_eps)
         if h.is_cuda:
             ld = (V + 7) // 8 * 8
             logits = torch.empty((T, ld), dtype=torch.float32, device=h.device)[:, :V]
-            ops.gemm(h, s.w(n("out.weight")), logits, ops.EPI_F32)
+            ops.gemm(h, s.w(self.out), logits, ops.EPI_F32)
         else:
-            logits = ops.linear_fwd(h, s.w(n("out.weight")), epi="f32")
+            logits = ops.linear_fwd(h, s.w(self.out), epi="f32")
         loss, dl = ops.cross_entropy(logits, V, targets.reshape(-1), 1.0 / T)
         del logits
         ctx.update(x=x, h=h, m=m, r=r, dl=dl)
@@ -228,11 +382,12 @@ class Head:
         c, s, n = self.cfg, self.s, self.n
         V = c.vocab_size
         dl = ctx["dl"][:, :V]
-        dh = ops.linear_dx(dl, s.w(n("out.weight")))
-        wq.append(WTask(dl, ctx["h"], s.g(n("out.weight")), None))
+        dh = ops.linear_dx(dl, s.w(self.out))
+        wq.append(WTask(dl, ctx["h"], s.g(self.out), None))
         x: Act = ctx["x"]
+        dbeta = None if self.rms else s.g(n("ln_f.bias"))
         dx = ops.layernorm_bwd(dh, x.x, x.scale, ctx["m"], ctx["r"], s.p(n("ln_f.weight")), None,
-                               s.g(n("ln_f.weight")), s.g(n("ln_f.bias")), accumulate=True)
+                               s.g(n("ln_f.weight")), dbeta, accumulate=True)
         ctx.clear()
         return dx
 
@@ -245,6 +400,10 @@ class StageModel:
         cfg.validate()
         self.cfg = cfg
         self.lo, self.hi = span
+        if cfg.tie_embeddings and not (self.lo == 0 and self.hi == cfg.n_layer + 2):
+            raise NotImplementedError(
+                "tie_embeddings with the table and the head on different stages needs the tied "
+                "relay, which this engine does not build: keep both on one stage")
         self.device = torch.device(device)
         if self.device.type == "cuda" and cfg.compute_dtype != "bf16":
             raise ValueError("the sm_100a kernels compute in bf16: set compute_dtype='bf16'")
@@ -268,6 +427,28 @@ class StageModel:
     @property
     def first(self) -> bool:
         return self.lo == 0
+
+    def moe_blocks(self) -> list:
+        """The MoE MLPs of this stage, in entry order."""
+        return [l.moe for l in self.layers if isinstance(l, Block) and l.moe is not None]
+
+    def take_moe_records(self) -> list:
+        """Pop every MoE record of the step, sorted by (layer, call order)."""
+        out = []
+        for m in self.moe_blocks():
+            out += m.take_records()
+        return out
+
+    def moe_bias_update(self, counts: dict, global_tokens: int):
+        """Selection-bias update after the optimizer step; counts maps the
+        entry index to the global batch's int64 expert counts."""
+        for m in self.moe_blocks():
+            if m.e in counts:
+                m.bias_update(counts[m.e], global_tokens)
+
+    def buffers(self) -> dict:
+        """Non-trained state a checkpoint carries (MoE selection biases)."""
+        return {f"{m.p}.sel_bias": m.sel_bias for m in self.moe_blocks()}
 
     @property
     def last(self) -> bool:
@@ -303,7 +484,7 @@ class StageModel:
         g = dy
         for layer, (kind, obj) in zip(reversed(self.layers), reversed(saved)):
             if kind == "input":
-                ctx: dict = {}
+                ctx: dict = {"_recompute": True}
                 layer.forward(obj, ctx)
             else:
                 ctx = obj

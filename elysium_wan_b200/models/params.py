@@ -29,6 +29,7 @@ class ParamSpec:
     init: str  # "normal" | "normal_resid" | "embed" | "bias" | "zeros" | "ones"
     fan_in: int = 1
     matrix: bool = False  # read by a GEMM (needs the bf16 working copy)
+    pack: bool = False  # the next tensor follows with no alignment gap (read as one operand)
 
 
 class ParamStore:
@@ -40,7 +41,7 @@ class ParamStore:
         for s in self.specs:
             self.index[s.name] = (off, tuple(s.shape))
             n = math.prod(s.shape)
-            off += (n + ALIGN - 1) // ALIGN * ALIGN
+            off += n if s.pack else (n + ALIGN - 1) // ALIGN * ALIGN
         self.numel = max(off, ALIGN)
         self.master = torch.zeros(self.numel, dtype=torch.float32, device=self.device)
         self.grad = torch.zeros(self.numel, dtype=torch.float32, device=self.device)
@@ -65,6 +66,36 @@ class ParamStore:
 
     def g(self, name):
         return self._view(self.grad, name)
+
+    def joint_offset(self, names) -> int | None:
+        """Offset of `names` when they sit back to back in the store (same
+        trailing shape), so one GEMM can treat them as one matrix; else None."""
+        off0, shape0 = self.index[names[0]]
+        off = off0
+        for n in names:
+            o, shp = self.index[n]
+            if o != off or tuple(shp[1:]) != tuple(shape0[1:]):
+                return None
+            off += math.prod(shp)
+        return off0
+
+    def _joint(self, buf, names):
+        off = self.joint_offset(names)
+        if off is None:
+            raise ValueError(f"{names} are not contiguous in the store")
+        rows = sum(self.index[n][1][0] for n in names)
+        tail = tuple(self.index[names[0]][1][1:])
+        return buf[off: off + rows * math.prod(tail)].view((rows,) + tail)
+
+    def pj(self, names):
+        """fp32 master view of adjacent parameters as one tensor (rows stacked)."""
+        return self._joint(self.master, names)
+
+    def wj(self, names):
+        return self._joint(self.work if self.work is not None else self.master, names)
+
+    def gj(self, names):
+        return self._joint(self.grad, names)
 
     def zero_grad(self):
         self.grad.zero_()

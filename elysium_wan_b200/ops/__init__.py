@@ -176,7 +176,8 @@ def colsum(x, grad, accumulate: bool):
 
 # ----------------------------------------------------------------------------- LayerNorm
 def layernorm_fwd(x, x_scale, gamma, beta, eps=1e-5):
-    """Returns (y bf16/fp32, mean, rstd). x may be e4m3 with 1x128 scales (dequant prologue)."""
+    """Returns (y bf16/fp32, mean, rstd). x may be e4m3 with 1x128 scales
+    (dequant prologue). beta None = RMSNorm (mean 0, no shift)."""
     T, d = x.shape
     if _cuda(x):
         y = torch.empty((T, d), dtype=torch.bfloat16, device=x.device)
@@ -185,6 +186,10 @@ def layernorm_fwd(x, x_scale, gamma, beta, eps=1e-5):
         ext().layernorm_fwd(x, x_scale, gamma, beta, y, mean, rstd, eps)
         return y, mean, rstd
     xf = _resid_value(x, x_scale)
+    if beta is None:
+        mean = torch.zeros(T, dtype=torch.float32)
+        rstd = torch.rsqrt((xf * xf).mean(dim=1) + eps)
+        return xf * rstd[:, None] * gamma, mean, rstd
     mean = xf.mean(dim=1)
     var = ((xf - mean[:, None]) ** 2).mean(dim=1)
     rstd = torch.rsqrt(var + eps)
@@ -193,13 +198,15 @@ def layernorm_fwd(x, x_scale, gamma, beta, eps=1e-5):
 
 
 def layernorm_bwd(dy, x, x_scale, mean, rstd, gamma, dres, dgamma, dbeta, accumulate: bool):
-    """dx (+ dres); dgamma/dbeta (+)= their row sums (fixed order)."""
+    """dx (+ dres); dgamma/dbeta (+)= their row sums (fixed order). dbeta None
+    = RMSNorm."""
     T, d = x.shape
+    rms = dbeta is None
     if _cuda(x):
         dx = torch.empty((T, d), dtype=torch.bfloat16, device=x.device)
         chunks = ext().layernorm_bwd_chunks(T)
         pg = torch.empty((chunks, d), dtype=torch.float32, device=x.device)
-        pb = torch.empty((chunks, d), dtype=torch.float32, device=x.device)
+        pb = None if rms else torch.empty((chunks, d), dtype=torch.float32, device=x.device)
         ext().layernorm_bwd(dy, x, x_scale, mean, rstd, gamma, dres, dx, pg, pb, dgamma, dbeta,
                             accumulate)
         return dx
@@ -207,30 +214,49 @@ def layernorm_bwd(dy, x, x_scale, mean, rstd, gamma, dres, dgamma, dbeta, accumu
     xh = (xf - mean[:, None]) * rstd[:, None]
     dyf = dy.float()
     g = dyf * gamma
-    dx = rstd[:, None] * (g - g.mean(1, keepdim=True) - xh * (g * xh).mean(1, keepdim=True))
+    centre = 0.0 if rms else g.mean(1, keepdim=True)
+    dx = rstd[:, None] * (g - centre - xh * (g * xh).mean(1, keepdim=True))
     if dres is not None:
         dx = dx + dres.float()
-    pg, pb = (dyf * xh).sum(0), dyf.sum(0)
+    pg = (dyf * xh).sum(0)
     if accumulate:
         dgamma.add_(pg)
-        dbeta.add_(pb)
     else:
         dgamma.copy_(pg)
-        dbeta.copy_(pb)
+    if not rms:
+        pb = dyf.sum(0)
+        if accumulate:
+            dbeta.add_(pb)
+        else:
+            dbeta.copy_(pb)
     return dx
 
 
 # ----------------------------------------------------------------------------- attention
-def attention_fwd(qkv, B, S, H, hd):
-    """Causal attention on the fused qkv buffer [B*S, 3*H*hd] -> (o [B*S, H*hd], lse)."""
+def _split_qkv(qkv, B, S, H, hd, Hkv):
+    """(q, k, v) as fp32 [B, heads, S, hd] from the fused [q | k | v] rows."""
+    d, dkv = H * hd, Hkv * hd
+    x = qkv.float().view(B, S, d + 2 * dkv)
+    q = x[..., :d].reshape(B, S, H, hd).transpose(1, 2)
+    k = x[..., d:d + dkv].reshape(B, S, Hkv, hd).transpose(1, 2)
+    v = x[..., d + dkv:].reshape(B, S, Hkv, hd).transpose(1, 2)
+    return q, k, v
+
+
+def attention_fwd(qkv, B, S, H, hd, Hkv=None):
+    """Causal attention on the fused buffer [B*S, (H + 2*Hkv)*hd] (q | k | v;
+    Hkv < H is grouped-query attention) -> (o [B*S, H*hd], lse base 2)."""
     d = H * hd
+    Hkv = Hkv or H
     scale = 1.0 / math.sqrt(hd)
     if _cuda(qkv):
         o = torch.empty((B * S, d), dtype=torch.bfloat16, device=qkv.device)
         lse = torch.empty((B, H, S), dtype=torch.float32, device=qkv.device)
-        ext().attention_fwd(qkv, o, lse, B, S, H, hd, scale)
+        ext().attention_fwd(qkv, o, lse, B, S, H, hd, scale, Hkv)
         return o, lse
-    q, k, v = qkv.float().view(B, S, 3, H, hd).permute(2, 0, 3, 1, 4)
+    q, k, v = _split_qkv(qkv, B, S, H, hd, Hkv)
+    rep = H // Hkv
+    k, v = k.repeat_interleave(rep, dim=1), v.repeat_interleave(rep, dim=1)
     att = (q @ k.transpose(-2, -1)) * scale
     mask = torch.triu(torch.ones(S, S, dtype=torch.bool), 1)
     att = att.masked_fill(mask, float("-inf"))
@@ -239,27 +265,103 @@ def attention_fwd(qkv, B, S, H, hd):
     return o, lse
 
 
-def attention_bwd(qkv, o, dout, lse, B, S, H, hd):
-    """Gradient of causal attention w.r.t. the fused qkv buffer."""
+def attention_bwd(qkv, o, dout, lse, B, S, H, hd, Hkv=None):
+    """Gradient of causal attention w.r.t. the fused qkv buffer (same layout).
+    With grouped-query attention a kv head's gradient sums its group's query
+    heads in head order."""
     d = H * hd
+    Hkv = Hkv or H
     scale = 1.0 / math.sqrt(hd)
     if _cuda(qkv):
         dqkv = torch.empty_like(qkv)
         D = torch.empty((B, H, S), dtype=torch.float32, device=qkv.device)
-        ext().attention_bwd(qkv, o, dout, lse, D, dqkv, B, S, H, hd, scale)
+        ext().attention_bwd(qkv, o, dout, lse, D, dqkv, B, S, H, hd, scale, Hkv)
         return dqkv
-    q, k, v = qkv.float().view(B, S, 3, H, hd).permute(2, 0, 3, 1, 4)
+    q, k, v = _split_qkv(qkv, B, S, H, hd, Hkv)
+    rep = H // Hkv
+    kr, vr = k.repeat_interleave(rep, dim=1), v.repeat_interleave(rep, dim=1)
     do = dout.float().view(B, S, H, hd).transpose(1, 2)
-    att = (q @ k.transpose(-2, -1)) * scale
+    att = (q @ kr.transpose(-2, -1)) * scale
     mask = torch.triu(torch.ones(S, S, dtype=torch.bool), 1)
     p = torch.softmax(att.masked_fill(mask, float("-inf")), dim=-1)
     dv = p.transpose(-2, -1) @ do
-    dp = do @ v.transpose(-2, -1)
+    dp = do @ vr.transpose(-2, -1)
     ds = p * (dp - (dp * p).sum(-1, keepdim=True))
-    dq = ds @ k * scale
+    dq = ds @ kr * scale
     dk = ds.transpose(-2, -1) @ q * scale
-    out = torch.stack([dq, dk, dv], dim=0).permute(1, 3, 0, 2, 4).reshape(B * S, 3 * d)
-    return out
+    dk = dk.view(B, Hkv, rep, S, hd).sum(2)
+    dv = dv.view(B, Hkv, rep, S, hd).sum(2)
+    rows = lambda t: t.transpose(1, 2).reshape(B * S, -1)  # noqa: E731
+    return torch.cat([rows(dq), rows(dk), rows(dv)], dim=1)
+
+
+# ----------------------------------------------------------------------------- Llama family
+_ROPE_TABLES: dict = {}
+
+
+def rope_tables(S, hd, theta, device):
+    """(cos, sin) fp32 [S, hd/2] of p * theta^(-2i/hd), computed once in fp64
+    on the host so every device type uses the same table."""
+    key = (S, hd, float(theta), str(device))
+    t = _ROPE_TABLES.get(key)
+    if t is None:
+        inv = 1.0 / (float(theta) ** (torch.arange(0, hd, 2, dtype=torch.float64) / hd))
+        ang = torch.outer(torch.arange(S, dtype=torch.float64), inv)
+        t = (torch.cos(ang).float().to(device).contiguous(),
+             torch.sin(ang).float().to(device).contiguous())
+        _ROPE_TABLES[key] = t
+    return t
+
+
+def rope(x, S, ncols, hd, theta, inverse=False):
+    """Rotate adjacent column pairs of columns [0, ncols) of each row in place
+    (q heads then k heads); row r is at position r % S. inverse rotates back
+    (the backward)."""
+    cos, sin = rope_tables(S, hd, theta, x.device)
+    if _cuda(x):
+        ext().rope(x, S, ncols, hd, cos, sin, bool(inverse))
+        return x
+    T = x.shape[0]
+    v = x[:, :ncols].reshape(T, ncols // hd, hd // 2, 2)
+    pos = torch.arange(T) % S
+    c, s_ = cos[pos][:, None, :], sin[pos][:, None, :]
+    if inverse:
+        s_ = -s_
+    x1, x2 = v[..., 0].clone(), v[..., 1].clone()
+    v[..., 0] = x1 * c - x2 * s_
+    v[..., 1] = x1 * s_ + x2 * c
+    return x
+
+
+def swiglu_fwd(gu):
+    """h = silu(gu[:, :f]) * gu[:, f:]."""
+    T, f2 = gu.shape
+    f = f2 // 2
+    if _cuda(gu):
+        h = torch.empty((T, f), dtype=torch.bfloat16, device=gu.device)
+        ext().swiglu_fwd(gu, h)
+        return h
+    g, u = gu[:, :f].float(), gu[:, f:].float()
+    return g * torch.sigmoid(g) * u
+
+
+def swiglu_bwd(dh, gu):
+    """d(gu) from dh: [dh * u * silu'(g) | dh * silu(g)]."""
+    T, f2 = gu.shape
+    f = f2 // 2
+    if _cuda(gu):
+        dgu = torch.empty_like(gu)
+        ext().swiglu_bwd(dh, gu, dgu)
+        return dgu
+    g, u, d = gu[:, :f].float(), gu[:, f:].float(), dh.float()
+    s = torch.sigmoid(g)
+    return torch.cat([d * u * s * (1 + g * (1 - s)), d * g * s], dim=1)
+
+
+def residual_add(x, y):
+    """x + y rounded to x's dtype, y first rounded to x's dtype (the block's
+    `x + mlp(h).to(x.dtype)`)."""
+    return x + y.to(x.dtype)
 
 
 # ----------------------------------------------------------------------------- cross-entropy
@@ -292,7 +394,8 @@ def cross_entropy(logits, V, targets, grad_scale, want_grad=True, ld_grad=None):
 
 # ----------------------------------------------------------------------------- embedding
 def embed_fwd(idx, wte, wpe, S, fp8: bool, out_dtype=torch.bfloat16):
-    """x = wte[idx] + wpe[pos]; bf16, or (e4m3, scales) when fp8."""
+    """x = wte[idx] (+ wpe[pos] when learned positions); bf16, or (e4m3,
+    scales) when fp8."""
     T = idx.numel()
     d = wte.shape[1]
     if _cuda(idx):
@@ -305,8 +408,9 @@ def embed_fwd(idx, wte, wpe, S, fp8: bool, out_dtype=torch.bfloat16):
         ext().embed_fwd(idx, wte, wpe, S, x, None, None)
         return x
     flat = idx.reshape(-1)
-    pos = torch.arange(T) % S
-    x = wte[flat] + wpe[pos]
+    x = wte[flat]
+    if wpe is not None:
+        x = x + wpe[torch.arange(T) % S]
     if fp8:
         return quant_e4m3(x)
     return x.to(out_dtype)
@@ -322,7 +426,8 @@ def embed_bwd(idx, dx, S, dwte, dwpe):
     T = flat.numel()
     dxf = dx.float()
     dwte.index_add_(0, flat, dxf)
-    dwpe.add_(dxf.view(T // S, S, -1).sum(0))
+    if dwpe is not None:
+        dwpe.add_(dxf.view(T // S, S, -1).sum(0))
 
 
 # ----------------------------------------------------------------------------- AdamW

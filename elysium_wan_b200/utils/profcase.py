@@ -1,0 +1,117 @@
+"""One hot op at the 15.8B shapes, a few times: the small case an Nsight
+Compute capture targets (one kernel, one to three launches, a few GB).
+
+    python -m elysium_wan_b200.utils.profcase --op gemm_fwd [--iters 3]
+
+Ops: gemm_fwd (qkv projection), gemm_dx (fc1 input gradient), gemm_dw (fc1
+weight gradient fold), gemm_q8 (fc2 with the fp8 boundary epilogue),
+attn_fwd, attn_bwd, ln_fwd, ln_bwd, ce, adamw, embed_bwd.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import time
+
+import torch
+
+from elysium_wan_b200 import ops
+
+T, D, F, H, V = 2048, 5120, 20480, 40, 50257
+
+
+def _bf(*shape, scale=1.0):
+    return (torch.randn(*shape, device="cuda") * scale).to(torch.bfloat16)
+
+
+def build(op):
+    """Returns (fn, flops, bytes) for one launch of the op."""
+    if op == "gemm_fwd":
+        x, w, b = _bf(T, D), _bf(3 * D, D, scale=0.02), torch.zeros(3 * D, device="cuda")
+        out = torch.empty(T, 3 * D, dtype=torch.bfloat16, device="cuda")
+        return (lambda: ops.gemm(x, w, out, ops.EPI_BF16, bias=b)), 2.0 * T * 3 * D * D, None
+    if op == "gemm_dx":
+        dy, w = _bf(T, F), _bf(F, D, scale=0.02)
+        out = torch.empty(T, D, dtype=torch.bfloat16, device="cuda")
+        return (lambda: ops.gemm(dy, w, out, ops.EPI_BF16, b_mn=True)), 2.0 * T * F * D, None
+    if op == "gemm_dw":
+        dy, x = _bf(T, F), _bf(T, D)
+        g = torch.zeros(F, D, device="cuda")
+        return (lambda: ops.linear_dw(dy, x, g, accumulate=True)), 2.0 * T * F * D, None
+    if op == "gemm_q8":
+        g, w, r = _bf(T, F), _bf(D, F, scale=0.02), _bf(T, D)
+        b = torch.zeros(D, device="cuda")
+        return (lambda: ops.linear_fwd(g, w, b, epi="resid_q8", resid=r)), 2.0 * T * F * D, None
+    if op in ("attn_fwd", "attn_bwd"):
+        qkv = _bf(T, 3 * D)
+        o, lse = ops.attention_fwd(qkv, 1, T, H, D // H)
+        flops_f = 4.0 * T * T * D / 2
+        if op == "attn_fwd":
+            return (lambda: ops.attention_fwd(qkv, 1, T, H, D // H)), flops_f, None
+        do = _bf(T, D)
+        return (lambda: ops.attention_bwd(qkv, o, do, lse, 1, T, H, D // H)), 2.5 * flops_f, None
+    if op in ("ln_fwd", "ln_bwd"):
+        x = _bf(8 * T, D)
+        gam, bet = torch.ones(D, device="cuda"), torch.zeros(D, device="cuda")
+        if op == "ln_fwd":
+            return (lambda: ops.layernorm_fwd(x, None, gam, bet)), None, 8 * T * D * 4
+        y, m, r = ops.layernorm_fwd(x, None, gam, bet)
+        dy = _bf(8 * T, D)
+        dg, db = torch.zeros(D, device="cuda"), torch.zeros(D, device="cuda")
+        return (lambda: ops.layernorm_bwd(dy, x, None, m, r, gam, dy, dg, db, True)), None, 8 * T * D * 8
+    if op == "ce":
+        ld = (V + 7) // 8 * 8
+        logits = torch.randn(T, ld, device="cuda")[:, :V]
+        tgt = torch.randint(0, V, (T,), device="cuda")
+        return (lambda: ops.cross_entropy(logits, V, tgt, 1.0 / T)), None, T * V * 6
+    if op == "adamw":
+        n = 1 << 28
+        p, g = torch.randn(n, device="cuda"), torch.randn(n, device="cuda")
+        m, v = torch.zeros(n, device="cuda"), torch.zeros(n, device="cuda")
+        pb = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+        return (lambda: ops.adamw(p, m, v, g, pb, 1e-4, 0.9, 0.95, 1e-8, 0.0, 1)), None, n * 30
+    if op == "embed_bwd":
+        idx = torch.randint(0, V, (1, T), device="cuda")
+        dx = _bf(T, D)
+        dwte, dwpe = torch.zeros(V, D, device="cuda"), torch.zeros(T, D, device="cuda")
+        return (lambda: ops.embed_bwd(idx, dx, T, dwte, dwpe)), None, None
+    raise ValueError(op)
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--op", required=True)
+    ap.add_argument("--iters", type=int, default=3)
+    ap.add_argument("--time", action="store_true", help="also print CUDA-event timing (no profiler)")
+    a = ap.parse_args(argv)
+    torch.manual_seed(0)
+    fn, flops, nbytes = build(a.op)
+    fn()
+    torch.cuda.synchronize()
+    if a.time:
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+        ts = []
+        for _ in range(10):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        ms = sorted(ts)[len(ts) // 2]
+        out = {"op": a.op, "ms": round(ms, 4)}
+        if flops:
+            out["tflops"] = round(flops / ms / 1e9, 1)
+        if nbytes:
+            out["gbs"] = round(nbytes / ms / 1e6, 1)
+        print(json.dumps(out), flush=True)
+    for _ in range(a.iters):
+        fn()
+    torch.cuda.synchronize()
+    time.sleep(0.01)
+
+
+if __name__ == "__main__":
+    main()

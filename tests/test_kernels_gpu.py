@@ -152,9 +152,11 @@ def test_layernorm(cuda, d, fp8):
 
 
 @pytest.mark.parametrize("hd", [64, 80, 128])
-def test_attention(cuda, hd):
+@pytest.mark.parametrize("S", [192, 256])
+def test_attention(cuda, hd, S):
+    # S = 256 runs the 8-warp (128-row) tiles, S = 192 the 4-warp fallback.
     torch.manual_seed(5)
-    B, S, H = 2, 256, 3
+    B, H = 2, 3
     d = H * hd
     qkv = bf(B * S, 3 * d, dev=cuda)
     o, lse = ops.attention_fwd(qkv, B, S, H, hd)

@@ -82,3 +82,86 @@ def test_fp8_boundary_cpu_roundtrip():
     loss = _run([m], idx, tgt)
     assert torch.isfinite(loss)
     assert m.store.grad.abs().sum() > 0
+
+
+def _general_check(cfg, seed=3, tol=2e-4, B=2):
+    from ._ref_general import ref_loss_general
+
+    torch.manual_seed(0)
+    m = StageModel(cfg, (0, cfg.n_entries), "cpu", seed=seed)
+    idx = torch.randint(0, cfg.vocab_size, (B, cfg.seq_len))
+    tgt = torch.randint(0, cfg.vocab_size, (B, cfg.seq_len))
+    m.store.zero_grad()
+    loss = _run([m], idx, tgt)
+    P = {n: m.store.p(n).detach().clone().requires_grad_(True) for n in m.store.names()}
+    ce, aux = ref_loss_general(cfg, P, idx, tgt)
+    (ce + aux).backward()
+    assert abs(loss.item() - ce.item()) < 1e-5
+    for n in m.store.names():
+        g, r = m.store.g(n), P[n].grad
+        if r is None:
+            r = torch.zeros_like(g)
+        err = ((g - r).norm() / (r.norm() + 1e-12)).item()
+        assert err < tol or (g - r).abs().max().item() < 1e-7, (n, err)
+    return m
+
+
+def test_llama_block_matches_autograd():
+    """RMSNorm, q / kv grouped-query attention with RoPE, SwiGLU, no bias."""
+    cfg = make_config("llama_tiny", n_layer=2, vocab_size=97, d_model=64, n_head=4, n_kv_head=2,
+                      seq_len=16)
+    m = _general_check(cfg)
+    assert "1.q.weight" in m.store.names() and "1.mlp.gate.weight" in m.store.names()
+    assert "0.pos.weight" not in m.store.names()
+
+
+def test_general_block_variants_match_autograd():
+    """LayerNorm + GELU + learned positions with biases under the general
+    names, full multi-head rope, tied embeddings."""
+    cfg = make_config("toy", n_layer=2, vocab_size=97, d_model=64, n_head=4, seq_len=16,
+                      d_ff=96)
+    m = _general_check(cfg)
+    assert "1.mlp.fc1.weight" in m.store.names()
+    cfg = make_config("toy", n_layer=2, vocab_size=97, d_model=64, n_head=4, seq_len=16,
+                      norm="rmsnorm", pos="rope", mlp="swiglu", bias=True, tie_embeddings=True)
+    m = _general_check(cfg)
+    assert "3.out.weight" not in m.store.names()
+
+
+def test_moe_block_matches_autograd():
+    cfg = make_config("moe_tiny", n_layer=2, vocab_size=97, d_model=64, n_head=4, n_kv_head=2,
+                      seq_len=16, moe_experts=4, moe_top_k=2, moe_d_ff=32, moe_shared_d_ff=32,
+                      moe_layers=[1])
+    m = _general_check(cfg)
+    recs = m.take_moe_records()
+    assert [r.layer for r in recs] == [2] and int(recs[0].counts.sum()) == 2 * 16 * 2
+
+
+def test_moe_variants_match_autograd():
+    base = dict(n_layer=1, vocab_size=97, d_model=64, n_head=4, n_kv_head=2, seq_len=16,
+                moe_experts=4, moe_d_ff=32, moe_shared_d_ff=0)
+    for extra in (dict(moe_score="sigmoid", moe_norm=True, moe_norm_eps=1e-6, moe_top_k=2,
+                       moe_lbl_scope="sequence"),
+                  dict(moe_score="softmax_k", moe_top_k=2, moe_router_bias=True,
+                       moe_select="logit"),
+                  dict(moe_apply="input", moe_top_k=1, moe_shared_d_ff=32,
+                       moe_shared_gate="none"),
+                  dict(moe_groups=2, moe_topk_groups=1, moe_top_k=2, moe_scale=2.0),
+                  dict(moe_expert="swiglu_clamped", moe_top_k=2, moe_limit=0.5)):
+        cfg = make_config("moe_tiny", **{**base, **extra})
+        _general_check(cfg)
+
+
+def test_moe_bias_update_moves_by_gamma():
+    cfg = make_config("moe_tiny", n_layer=1, moe_experts=4, moe_top_k=1, moe_bias_rate=0.1,
+                      moe_select="score_bias")
+    m = StageModel(cfg, (0, cfg.n_entries), "cpu", seed=1)
+    blk = m.moe_blocks()[0]
+    m.moe_bias_update({1: torch.tensor([1, 3, 2, 2], dtype=torch.int64)}, 8)
+    # T k = 8, E c = 4, 12, 8, 8 -> signs +, -, 0, 0
+    assert blk.sel_bias.tolist() == [0.1, -0.1, 0.0, 0.0] or \
+        torch.allclose(blk.sel_bias, torch.tensor([0.1, -0.1, 0.0, 0.0]))
+    import pytest
+
+    with pytest.raises(ValueError):
+        m.moe_bias_update({1: torch.tensor([1, 1, 1, 1], dtype=torch.int64)}, 8)
