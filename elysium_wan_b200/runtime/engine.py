@@ -225,6 +225,7 @@ class StageEngine:
             self.zero1.sync_and_step()
         else:
             self.opt.step()
+        self._moe_after_step()
         if ev:
             e_opt = torch.cuda.Event(enable_timing=True)
             e_opt.record()
@@ -238,6 +239,29 @@ class StageEngine:
             for mb, v in out:
                 self.losses.append((step, mb, v))
         return out
+
+    def _moe_after_step(self):
+        """MoE bookkeeping after the optimizer step: the step's int64 expert
+        counts per layer (integer sums, exact in any order; summed over the
+        stage's replicas), the selection-bias update from them, and the aux
+        values for telemetry."""
+        if not self.model.moe_blocks():
+            return
+        recs = self.model.take_moe_records()
+        E = self.spec.model.moe_experts
+        layers = [m.e for m in self.model.moe_blocks()]
+        counts = torch.zeros((len(layers), E), dtype=torch.int64)
+        for r in recs:
+            counts[layers.index(r.layer)] += r.counts
+        if self.width > 1 and self.comm is not None and getattr(self.comm, "g_stage", None):
+            import torch.distributed as dist
+
+            dev_counts = counts.to(self.device)
+            dist.all_reduce(dev_counts, group=self.comm.g_stage)
+            counts = dev_counts.cpu()
+        tokens = self.spec.microbatches * self.spec.mb_size * self.spec.model.seq_len
+        self.model.moe_bias_update({e: counts[i] for i, e in enumerate(layers)}, tokens)
+        self.moe_aux = [(r.layer, r.aux) for r in recs]
 
     def phase_ms(self) -> dict:
         """{ops_ms, opt_ms} of the last step (after a synchronize)."""
@@ -259,12 +283,16 @@ class StageEngine:
         return {"step": self.step_done, "params": self.store.master.detach().cpu().clone(),
                 "names": self.store.names(), "opt": self.opt.state_dict(),
                 "losses": {f"{s}:{m}": v for s, m, v in self.losses},
+                "buffers": {k: v.detach().cpu().clone() for k, v in self.model.buffers().items()},
                 "rng": torch.get_rng_state()}
 
     def load_state_dict(self, sd: dict):
         self.store.master.copy_(sd["params"].to(self.store.master.device))
         self.store.sync_work()
         self.opt.load_state_dict(sd["opt"])
+        for k, v in self.model.buffers().items():
+            if k in sd.get("buffers", {}):
+                v.copy_(sd["buffers"][k].to(v.device))
         self.step_done = int(sd["step"])
         self.losses = [(int(k.split(":")[0]), int(k.split(":")[1]), float(v))
                        for k, v in sd.get("losses", {}).items()]

@@ -102,6 +102,14 @@ class Oracle:
                 o.step()
             if self.partials[r] is not None:
                 m.store.sync_work()
+        # MoE: the global batch's expert counts drive the selection-bias update.
+        tokens = spec.microbatches * spec.mb_size * spec.model.seq_len
+        for m in self.stages:
+            if m.moe_blocks():
+                counts: dict = {}
+                for rec in m.take_moe_records():
+                    counts[rec.layer] = counts.get(rec.layer, 0) + rec.counts
+                m.moe_bias_update(counts, tokens)
         vals = torch.stack([l.reshape(()) for _, l in out]).float().cpu().tolist()
         res = [(mb, v) for (mb, _), v in zip(out, vals)]
         for mb, v in res:

@@ -24,6 +24,16 @@ CASES = {
     "chain3_fp8_recompute": dict(stages=3, recompute=True, model_kw=dict(boundary_dtype="fp8_e4m3_b128")),
     "wide_2_1": dict(stages=2, stage_widths=[2, 1]),
     "wide_1_2": dict(stages=2, stage_widths=[1, 2]),
+    # Llama block (RMSNorm, GQA, RoPE, SwiGLU, no bias) cut over 2 stages.
+    "llama_chain2": dict(stages=2, model_kw=dict(norm="rmsnorm", mlp="swiglu", pos="rope",
+                                                 bias=False, n_kv_head=2)),
+    # MoE block with a selection bias that moves every step, recompute, a
+    # wide second stage (counts summed over its replicas).
+    "moe_wide_1_2": dict(stages=2, stage_widths=[1, 2], recompute=True,
+                         model_kw=dict(norm="rmsnorm", mlp="swiglu", pos="rope", bias=False,
+                                       moe_experts=4, moe_top_k=2, moe_d_ff=64,
+                                       moe_shared_d_ff=64, moe_select="score_bias",
+                                       moe_bias_rate=0.01, moe_lbl_coef=0.01, moe_z_coef=0.001)),
 }
 
 
