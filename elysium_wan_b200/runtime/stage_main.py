@@ -64,7 +64,16 @@ def run_stage(spec, stage: int, peer: int, timeout_s: float = 600.0) -> int:
         torch.cuda.set_device(torch.device(dev))
     _print("WT_PHASE", {"phase": "init", "stage": stage, "peer": peer, "rank": rank})
     init_group(spec, rank, timeout_s)
-    comm = PipeComm(spec, stage, peer, torch.device(dev)) if spec.world_size > 1 else None
+    if spec.world_size == 1:
+        comm = None
+    elif spec.backend == "tcp":
+        # Framed, sealed TCP between stages (runs across machines); the gloo
+        # group still carries the collectives inside a wide stage.
+        from elysium_wan_b200.transport.tcp import TcpPipeComm
+
+        comm = TcpPipeComm(spec, stage, peer, torch.device(dev), timeout_s=timeout_s)
+    else:
+        comm = PipeComm(spec, stage, peer, torch.device(dev))
     eng = StageEngine(spec, stage, peer, comm, dev)
     _print("WT_STAGE", {"stage": stage, "peer": peer, "span": spec.partition[stage],
                         "params": eng.store.numel, "device": dev})

@@ -1,0 +1,339 @@
+"""The TCP data plane: stage-to-stage channels for runs across machines.
+
+Reference behaviour: the framed, sealed TCP data plane of
+src/wantrain/runtime/stage.py (per-hop flows, fragment reassembly, END
+half-close) over transport/framing.py and transport/secure.py. Same interface
+as parallel/p2p.PipeComm, so the engine does not know which plane it runs on:
+
+- every slot listens on its endpoint (spec.endpoints[stage][peer] =
+  [host, data_port, bind_port], else spec.host : port_base + 1000 + rank);
+  the lower stage dials each slot of the next stage with `p2p_streams`
+  flows, says HELLO, and every flow is sealed after an identity handshake
+  (ed25519 + X25519, transport/identity.py), admission by `trusted_peers`;
+- a boundary tensor leaves through the spec's wire codec (raw, planes,
+  f32_planes, fp8_planes; the e4m3_b128 pair as one PLANES payload), cut into
+  one fragment per flow, and is reassembled by concatenation: codecs and
+  fragments never change a bit;
+- one sender thread per destination slot keeps sends asynchronous (flush()
+  waits for them), one reader thread per flow files whole frames by
+  (type, microbatch); a WAN shim per outgoing link can pace and delay sends
+  for experiments (latency, rate, jitter).
+
+Device tensors cross through host memory (a device->host copy before the
+send, a host->device copy after the receive).
+"""
+
+from __future__ import annotations
+
+import collections
+import os
+import queue
+import socket
+import threading
+import time
+
+import torch
+import torch.distributed as dist
+
+from elysium_wan_b200.models.gpt import Act
+from elysium_wan_b200.transport import framing
+from elysium_wan_b200.transport.framing import BWD, END, FWD, HELLO
+
+
+def slot_endpoint(spec, stage: int, peer: int) -> tuple[str, int]:
+    if spec.endpoints:
+        host, port = spec.endpoints[stage][peer][0], int(spec.endpoints[stage][peer][1])
+        return host, port
+    return spec.host, spec.port_base + 1000 + spec.rank_of(stage, peer)
+
+
+class _Inbox:
+    def __init__(self):
+        self.cv = threading.Condition()
+        self.q: dict = collections.defaultdict(collections.deque)
+        self.err: Exception | None = None
+
+    def put(self, key, frame):
+        with self.cv:
+            self.q[key].append(frame)
+            self.cv.notify_all()
+
+    def fail(self, e):
+        with self.cv:
+            if self.err is None:
+                self.err = e
+            self.cv.notify_all()
+
+    def get(self, key, timeout):
+        end = time.monotonic() + timeout
+        with self.cv:
+            while not self.q[key]:
+                if self.err is not None:
+                    raise ConnectionError(f"peer connection lost: {self.err}")
+                left = end - time.monotonic()
+                if left <= 0:
+                    raise TimeoutError(f"no frame {key} within {timeout:.0f}s")
+                self.cv.wait(min(left, 1.0))
+            return self.q[key].popleft()
+
+
+class _Link:
+    """The flows to one neighbour slot and the thread that sends on them."""
+
+    def __init__(self, comm, socks, link_cfg: dict):
+        from elysium_wan_b200.parallel.p2p import _Shim
+
+        self.comm, self.socks = comm, socks
+        self.q: queue.Queue = queue.Queue()
+        self.err: Exception | None = None
+        self.shim = _Shim(link_cfg or {})
+        self.t = threading.Thread(target=self._loop, daemon=True)
+        self.t.start()
+
+    def submit(self, item):
+        self.q.put(item)
+
+    def _send_frame(self, ftype, step, mb, tensors):
+        c = self.comm
+        payload_t = tensors if len(tensors) > 1 else tensors[0]
+        codec_id, payload, shape = framing.encode_tensor(payload_t, c.wire_codec)
+        frags = framing.fragments(payload, len(self.socks))
+        for i, part in enumerate(frags):
+            framing.send_frame(self.socks[i], ftype, step, mb, part, chunk=c.peer,
+                               codec_id=codec_id, shape=shape, frag_idx=i, frag_cnt=len(frags))
+        return len(payload)
+
+    def _loop(self):
+        while True:
+            item = self.q.get()
+            try:
+                if item is None:
+                    return
+                ftype, step, mb, tensors = item
+                if self.shim.active:
+                    nbytes = sum(t.numel() * t.element_size() for t in tensors)
+                    self.shim.submit(lambda: self._send_frame(ftype, step, mb, tensors), nbytes)
+                    self.shim.flush()
+                else:
+                    self._send_frame(ftype, step, mb, tensors)
+            except Exception as e:  # surfaced on the next flush / send
+                self.err = e
+            finally:
+                self.q.task_done()
+
+    def flush(self):
+        self.q.join()
+        if self.err is not None:
+            raise ConnectionError(f"peer connection lost: {self.err}")
+
+    def close(self):
+        try:
+            self.flush()
+            for s in self.socks:
+                framing.send_end(s)
+        except (OSError, ConnectionError):
+            pass
+        self.q.put(None)
+        self.shim.close()
+
+
+class TcpPipeComm:
+    def __init__(self, spec, stage: int, peer: int, device, timeout_s: float = 300.0,
+                 key_path: str | None = None):
+        from elysium_wan_b200.transport import identity
+
+        self.spec, self.stage, self.peer = spec, stage, peer
+        self.device = torch.device(device)
+        self.rank = spec.rank_of(stage, peer)
+        self.timeout = timeout_s
+        self.wire_codec = spec.wire_codec if spec.wire_codec != "native" else "raw"
+        world = spec.world_size
+        # intra-stage group for ZeRO-1 (created by every rank in the same order)
+        self.g_stage = None
+        for r, w in enumerate(spec.stage_widths):
+            g = dist.new_group([spec.rank_of(r, q) for q in range(w)]) if world > 1 else None
+            if r == stage:
+                self.g_stage = g
+        cfg = spec.model
+        self.T, self.d = spec.mb_size * cfg.seq_len, cfg.d_model
+        self.cuda = self.device.type == "cuda"
+        self.fp8 = cfg.fp8_boundary()
+        self.act_dtype = torch.bfloat16 if self.cuda else torch.float32
+        self.key = identity.load_or_create_key(key_path)
+        self.trusted = spec.trusted_peers
+        self.inbox = _Inbox()
+        self.readers: list = []
+        self.next_links: dict = {}  # peer of stage + 1 -> _Link
+        self.prev_links: dict = {}  # peer of stage - 1 -> _Link
+        self.sent = collections.Counter()
+        self.bytes_sent = 0
+        self.frames = 0
+        self.peers_seen: dict = {}
+        self._connect()
+
+    # ----------------------------------------------------------------- setup
+    def _seal(self, sock, role):
+        from elysium_wan_b200.transport import identity, secure
+
+        sock.settimeout(self.timeout)
+        sess = identity.authenticate(sock, self.key, role, identity.P2P_DOMAIN,
+                                     trusted_peers=self.trusted)
+        sock.settimeout(None)
+        return secure.SecureSocket(sock, sess)
+
+    def _connect(self):
+        spec, S = self.spec, self.spec.stages
+        flows = max(1, int(spec.p2p_streams))
+        n_in = spec.stage_widths[self.stage - 1] * flows if self.stage > 0 else 0
+        lsock = None
+        if n_in:
+            host, port = slot_endpoint(spec, self.stage, self.peer)
+            bind = spec.endpoints[self.stage][self.peer][2] if spec.endpoints and \
+                len(spec.endpoints[self.stage][self.peer]) > 2 and \
+                spec.endpoints[self.stage][self.peer][2] else port
+            lsock = socket.socket(socket.AF_INET, socket.SOCK_STREAM)
+            lsock.setsockopt(socket.SOL_SOCKET, socket.SO_REUSEADDR, 1)
+            lsock.bind(("0.0.0.0" if host not in ("127.0.0.1", "localhost") else host, int(bind)))
+            lsock.listen(n_in + 4)
+        accepted: dict = collections.defaultdict(dict)
+        acc_err: list = []
+
+        def accept_all():
+            try:
+                lsock.settimeout(self.timeout)
+                for _ in range(n_in):
+                    c, _ = lsock.accept()
+                    c.setsockopt(socket.IPPROTO_TCP, socket.TCP_NODELAY, 1)
+                    sc = self._seal(c, "listener")
+                    hello = framing.recv_frame(sc)
+                    if hello.type != HELLO:
+                        raise framing.FrameError("expected HELLO")
+                    h = hello.obj()
+                    if h.get("stage") != self.stage - 1:
+                        raise framing.FrameError(f"HELLO from stage {h.get('stage')}")
+                    accepted[int(h["peer"])][int(h["flow"])] = sc
+                    self.peers_seen[f"{h['stage']}:{h['peer']}"] = sc.peer
+            except Exception as e:
+                acc_err.append(e)
+
+        t_acc = threading.Thread(target=accept_all, daemon=True) if n_in else None
+        if t_acc:
+            t_acc.start()
+        if self.stage + 1 < S:
+            for q in range(spec.stage_widths[self.stage + 1]):
+                host, port = slot_endpoint(spec, self.stage + 1, q)
+                socks = []
+                for f in range(flows):
+                    s = self._dial(host, port)
+                    sc = self._seal(s, "dialer")
+                    framing.send_frame(sc, HELLO, 0, 0, {"stage": self.stage, "peer": self.peer,
+                                                          "flow": f})
+                    self.peers_seen[f"{self.stage + 1}:{q}"] = sc.peer
+                    socks.append(sc)
+                link = spec.links[self.stage] if self.stage < len(spec.links) else {}
+                self.next_links[q] = _Link(self, socks, link)
+                for sc in socks:
+                    self._start_reader(sc)
+        if t_acc:
+            t_acc.join(self.timeout + 5)
+            lsock.close()
+            if acc_err:
+                raise ConnectionError(f"data plane accept failed: {acc_err[0]}")
+            back = spec.links[self.stage - 1] if self.stage - 1 < len(spec.links) else {}
+            for p in range(spec.stage_widths[self.stage - 1]):
+                socks = [accepted[p][f] for f in range(flows)]
+                self.prev_links[p] = _Link(self, socks, back)
+                for sc in socks:
+                    self._start_reader(sc)
+
+    def _dial(self, host, port):
+        end = time.monotonic() + self.timeout
+        while True:
+            try:
+                s = socket.create_connection((host, port), timeout=5)
+                s.setsockopt(socket.IPPROTO_TCP, socket.TCP_NODELAY, 1)
+                s.settimeout(None)
+                return s
+            except OSError:
+                if time.monotonic() > end:
+                    raise
+                time.sleep(0.05)
+
+    def _start_reader(self, sock):
+        re = framing.Reassembler()
+
+        def loop():
+            try:
+                while True:
+                    f = framing.recv_frame(sock)
+                    if f.type == END:
+                        return
+                    whole = re.push(f)
+                    if whole is not None:
+                        self.inbox.put((whole.type, whole.mb), whole)
+            except Exception as e:
+                self.inbox.fail(e)
+
+        t = threading.Thread(target=loop, daemon=True)
+        t.start()
+        self.readers.append(t)
+
+    # ----------------------------------------------------------------- routing
+    def next_peer(self, mb: int) -> int:
+        return self.spec.mb_owner[self.stage + 1][mb]
+
+    def prev_peer(self, mb: int) -> int:
+        return self.spec.mb_owner[self.stage - 1][mb]
+
+    # ----------------------------------------------------------------- sends
+    def _host(self, t):
+        return t.detach().to("cpu", copy=True).contiguous()
+
+    def send_act(self, mb: int, act: Act):
+        if act.fp8:
+            ts = [self._host(act.x), self._host(act.scale)]
+        else:
+            ts = [self._host(act.x.to(self.act_dtype))]
+        self._enqueue(self.next_links[self.next_peer(mb)], FWD, mb, ts)
+        return []
+
+    def send_grad(self, mb: int, g: torch.Tensor):
+        self._enqueue(self.prev_links[self.prev_peer(mb)], BWD, mb,
+                      [self._host(g.to(self.act_dtype))])
+        return []
+
+    def _enqueue(self, link, ftype, mb, tensors):
+        if link.err is not None:
+            raise ConnectionError(f"peer connection lost: {link.err}")
+        step = self.sent[(ftype, mb)]
+        self.sent[(ftype, mb)] += 1
+        self.bytes_sent += sum(t.numel() * t.element_size() for t in tensors)
+        self.frames += 1
+        link.submit((ftype, step, mb, tensors))
+
+    # ----------------------------------------------------------------- receives
+    def irecv_act(self, mb: int):
+        return (FWD, mb)
+
+    def irecv_grad(self, mb: int):
+        return (BWD, mb)
+
+    def wait(self, handle):
+        f = self.inbox.get(handle, self.timeout)
+        t = f.tensor()
+        if isinstance(t, tuple):
+            return [t[0].to(self.device), t[1].to(self.device)]
+        return [t.to(self.device)]
+
+    def as_act(self, bufs) -> Act:
+        if self.fp8:
+            return Act(bufs[0].view(torch.float8_e4m3fn), bufs[1])
+        return Act(bufs[0])
+
+    def flush(self):
+        for link in list(self.next_links.values()) + list(self.prev_links.values()):
+            link.flush()
+
+    def close(self):
+        for link in list(self.next_links.values()) + list(self.prev_links.values()):
+            link.close()

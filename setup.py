@@ -1,4 +1,5 @@
-"""Build of the in-tree sm_100a extension `elysium_wan_b200._C`.
+"""Build of the in-tree extensions: `elysium_wan_b200._C` (sm_100a kernels)
+and `elysium_wan_b200._wire` (host codecs and frame I/O of the TCP data plane).
 
     python setup.py build_ext --inplace
 
@@ -9,7 +10,8 @@ architecture list.
 
 import os
 
-from setuptools import setup
+import pybind11
+from setuptools import Extension, setup
 from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 
 HERE = os.path.dirname(os.path.abspath(__file__))
@@ -41,7 +43,15 @@ setup(
             sources=[os.path.join(CSRC, "bindings.cpp")] + [os.path.join(CSRC, f) for f in CU],
             include_dirs=[os.path.join(HERE, CSRC)],
             extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC},
-        )
+        ),
+        Extension(
+            name="elysium_wan_b200._wire",
+            sources=[os.path.join(CSRC, "wire", "wire.cpp")],
+            include_dirs=[pybind11.get_include()],
+            extra_compile_args=["-O3", "-std=c++17", "-fvisibility=hidden"],
+            libraries=["z"],
+            language="c++",
+        ),
     ],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
 )
