@@ -173,6 +173,25 @@ def cmd_prepare_data(a) -> int:
     return 0
 
 
+def cmd_import_hf(a) -> int:
+    """A Hugging Face checkpoint (Llama family or GPT-2) -> a job spec whose
+    model is the matching built-in decoder, initialised from the checkpoint."""
+    from elysium_wan_b200.models import hf
+    from elysium_wan_b200.runtime.spec import JobSpec
+
+    cfg, _ = hf.import_checkpoint(a.path, seq_len=a.seq_len,
+                                  compute_dtype=a.compute_dtype, boundary_dtype=a.boundary_dtype)
+    spec = JobSpec(model=cfg, stages=a.stages, init_from=os.path.abspath(a.path),
+                   init_sha256=hf.checkpoint_digest(a.path), device=a.device,
+                   backend="nccl" if a.device.startswith("cuda") else "gloo")
+    spec.finalize()
+    with open(a.out, "w") as f:
+        f.write(spec.to_json())
+    print("WT_IMPORT " + json.dumps({"out": a.out, "params": cfg.n_params(),
+                                     "init_sha256": spec.init_sha256}))
+    return 0
+
+
 def build_parser() -> argparse.ArgumentParser:
     ap = argparse.ArgumentParser(prog="wantrain")
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -266,6 +285,16 @@ def build_parser() -> argparse.ArgumentParser:
     pd.add_argument("--shards", type=int, default=1)
     pd.add_argument("--limit-tokens", type=int, default=None)
     pd.set_defaults(fn=cmd_prepare_data)
+
+    ih = sub.add_parser("import-hf", help="HF checkpoint (Llama / GPT-2) -> job spec")
+    ih.add_argument("--path", required=True)
+    ih.add_argument("--out", required=True)
+    ih.add_argument("--seq-len", type=int, default=None)
+    ih.add_argument("--stages", type=int, default=1)
+    ih.add_argument("--device", default="cpu")
+    ih.add_argument("--compute-dtype", default="fp32")
+    ih.add_argument("--boundary-dtype", default="fp32")
+    ih.set_defaults(fn=cmd_import_hf)
     return ap
 
 

@@ -33,6 +33,9 @@ class StageEngine:
         if self.device.type == "cuda":
             torch.cuda.set_device(self.device)
         self.model = StageModel(spec.model, tuple(spec.partition[stage]), self.device, spec.init_seed)
+        from elysium_wan_b200.models.hf import init_from_spec
+
+        init_from_spec(self.model, spec)
         self.store = self.model.store
         self.comm = comm
         self.order = [(op, int(mb)) for op, mb in spec.schedule_order[stage][peer]]

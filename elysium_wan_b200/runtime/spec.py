@@ -49,6 +49,10 @@ class JobSpec:
     dataset_sha256: str | None = None
     data_shards: int = 1
     dataset_source: str | None = None
+    # initial weights from a checkpoint (a Hugging Face directory of
+    # config.json + safetensors) instead of the seeded init; its digest pins it
+    init_from: str | None = None
+    init_sha256: str | None = None
     steps: int = 8
     microbatches: int = 8
     mb_size: int = 4
@@ -224,6 +228,8 @@ class JobSpec:
             pins["optimizer"] = self.optimizer
         if self.dataset_sha256:
             pins["dataset_sha256"] = self.dataset_sha256
+        if self.init_from:
+            pins["init_sha256"] = self.init_sha256
         return json.loads(json.dumps(pins))
 
     def to_dict(self) -> dict:

@@ -34,6 +34,10 @@ class Oracle:
         self.device = torch.device(device or spec.device)
         self.stages = [StageModel(spec.model, tuple(rng), self.device, spec.init_seed)
                        for rng in spec.partition]
+        from elysium_wan_b200.models.hf import init_from_spec
+
+        for m in self.stages:
+            init_from_spec(m, spec)
         self.widths = list(spec.stage_widths)
         self.partials = []
         self.opts = []
