@@ -79,7 +79,89 @@ def _norm_specs(name, d, layernorm):
     return out
 
 
+LORA_TARGETS = {
+    "attn": ("qkv", "q", "kv", "proj"),
+    "attn_mlp": ("qkv", "q", "kv", "proj", "gate", "up", "down", "fc1", "fc2"),
+    "all": ("qkv", "q", "kv", "proj", "gate", "up", "down", "fc1", "fc2", "out"),
+}
+
+
 def entry_specs(cfg: GPTConfig, e: int) -> list[ParamSpec]:
+    """Specs of entry e; with LoRA (lora_rank > 0) every base tensor is frozen
+    and each targeted linear gains a trainable adapter `{linear}.A.weight`
+    (r x in, kaiming-uniform from its own positional stream) and
+    `{linear}.B.weight` (out x r, zeros), declared after the entry's base
+    tensors so the base init is the same as without LoRA (reference:
+    src/wantrain/model/lora.py)."""
+    base = _base_specs(cfg, e)
+    if not cfg.lora_rank:
+        return base
+    want = LORA_TARGETS[cfg.lora_targets]
+    out, adapters = [], []
+    for sp in base:
+        out.append(ParamSpec(sp.name, sp.shape, sp.init, sp.fan_in, sp.matrix, sp.pack,
+                             frozen=True))
+        stem = sp.name[:-len(".weight")] if sp.name.endswith(".weight") else None
+        if sp.matrix and stem and stem.split(".")[-1] in want:
+            o, i = sp.shape
+            adapters += [ParamSpec(f"{stem}.A.weight", (cfg.lora_rank, i), "lora_a", fan_in=i,
+                                   matrix=True),
+                         ParamSpec(f"{stem}.B.weight", (o, cfg.lora_rank), "zeros", fan_in=cfg.lora_rank,
+                                   matrix=True)]
+    return out + adapters
+
+
+class LoraWTask:
+    """W of a frozen linear with an adapter y += s * (x A^T) B^T:
+    dA += s (dY B)^T X and dB += s dY^T (X A^T); four skinny GEMMs instead of
+    the full dY^T X."""
+
+    __slots__ = ("dy", "x", "a", "b", "ga", "gb", "scale", "peer")
+
+    def __init__(self, dy, x, a, b, ga, gb, scale):
+        self.dy, self.x, self.a, self.b, self.ga, self.gb = dy, x, a, b, ga, gb
+        self.scale = scale
+        self.peer = None
+
+    def run(self):
+        u = ops.linear_dx(self.dy, self.b)
+        u.mul_(self.scale)
+        ops.linear_dw(u, self.x, self.ga, accumulate=True)
+        t = ops.linear_fwd(self.x, self.a)
+        t.mul_(self.scale)
+        ops.linear_dw(self.dy, t, self.gb, accumulate=True)
+        self.dy = self.x = None
+
+    def record_stream(self, stream):
+        self.dy.record_stream(stream)
+        self.x.record_stream(stream)
+
+
+def w_tasks(store, dy, x, wnames: list, bnames: list | None, scale: float = 1.0) -> list:
+    """The W tasks of a linear, or of linears that share their input and sit
+    back to back (q with kv, gate with up; dy then holds their output columns
+    side by side): one dY^T X task for a trainable base, adapter tasks for a
+    frozen base with LoRA, nothing for a frozen base without one."""
+    gw = store.gj(wnames) if len(wnames) > 1 else store.g(wnames[0])
+    if gw is not None:
+        gb = None
+        if bnames:
+            gb = store.gj(bnames) if len(bnames) > 1 else store.g(bnames[0])
+        return [WTask(dy, x, gw, gb)]
+    out, col = [], 0
+    for wn in wnames:
+        rows = store.index[wn][1][0]
+        stem = wn[:-len(".weight")]
+        a = f"{stem}.A.weight"
+        if a in store.index:
+            d = dy if len(wnames) == 1 else dy[:, col:col + rows]
+            out.append(LoraWTask(d, x, store.w(a), store.w(f"{stem}.B.weight"), store.g(a),
+                                 store.g(f"{stem}.B.weight"), scale))
+        col += rows
+    return out
+
+
+def _base_specs(cfg: GPTConfig, e: int) -> list[ParamSpec]:
     """Parameter specs of flat-list entry e, named like the reference's
     nn.ModuleList ("{e}.qkv.weight", ...). Matrices one GEMM reads as one
     operand (q with kv, gate with up) are listed back to back, then their
@@ -204,8 +286,11 @@ class Embed:
         return Act(*out) if isinstance(out, tuple) else Act(out)
 
     def backward(self, ctx: dict, dy: torch.Tensor, wq: list):
+        dwte = self.s.g(f"{self.e}.tok.weight")
+        if dwte is None:  # frozen table (LoRA): nothing to accumulate
+            return None
         dwpe = self.s.g(f"{self.e}.pos.weight") if self.has_pos else None
-        ops.embed_bwd(ctx["tokens"], dy, self.cfg.seq_len, self.s.g(f"{self.e}.tok.weight"), dwpe)
+        ops.embed_bwd(ctx["tokens"], dy, self.cfg.seq_len, dwte, dwpe)
         return None
 
 
@@ -229,6 +314,7 @@ class Block:
         self.n = lambda k: f"{e}.{k}"
         n = self.n
         gen = uses_general_arch(cfg)
+        self.lora_s = cfg.lora_alpha / cfg.lora_rank if cfg.lora_rank else 1.0
         self.rms = cfg.norm == "rmsnorm"
         self.eps = cfg.norm_eps
         self.bias = cfg.bias
@@ -273,6 +359,9 @@ class Block:
     def _gw(self, names):
         return self.s.gj(names) if len(names) > 1 else self.s.g(names[0])
 
+    def _bn(self, names):
+        return names if self.bias else None
+
     def _norm(self, x, xs, which):
         s, n = self.s, self.n
         beta = None if self.rms else s.p(n(f"{which}.bias"))
@@ -280,9 +369,14 @@ class Block:
 
     def _norm_bwd(self, dy, x, xs, m, r, which, dres):
         s, n = self.s, self.n
+        dg = s.g(n(f"{which}.weight"))
         dbeta = None if self.rms else s.g(n(f"{which}.bias"))
-        return ops.layernorm_bwd(dy, x, xs, m, r, s.p(n(f"{which}.weight")), dres,
-                                 s.g(n(f"{which}.weight")), dbeta, accumulate=True)
+        if dg is None:  # frozen norm: its gradient goes to a scratch nobody reads
+            d = x.shape[1]
+            dg = s.sink(2 * d)[:d]
+            dbeta = None if self.rms else s.sink(2 * d)[d:]
+        return ops.layernorm_bwd(dy, x, xs, m, r, s.p(n(f"{which}.weight")), dres, dg, dbeta,
+                                 accumulate=True)
 
     def forward(self, x: Act, ctx: dict) -> Act:
         c, s, n = self.cfg, self.s, self.n
@@ -328,24 +422,25 @@ class Block:
             dh2 = self.moe.backward(ctx, dy, wq)
         elif self.mlp == "gelu":
             du = ops.linear_dx(dy, s.w(self.dn_w), gelu_u=ctx["u"])
-            wq.append(WTask(dy, ctx["g"], s.g(self.dn_w), self._bg([self.dn_b])))
+            wq += w_tasks(s, dy, ctx["g"], [self.dn_w], self._bn([self.dn_b]), self.lora_s)
             dh2 = ops.linear_dx(du, self._w(self.up_w))
-            wq.append(WTask(du, ctx["h2"], self._gw(self.up_w), self._bg(self.up_b)))
+            wq += w_tasks(s, du, ctx["h2"], self.up_w, self._bn(self.up_b), self.lora_s)
         else:
             dh = ops.linear_dx(dy, s.w(self.dn_w))
-            wq.append(WTask(dy, ctx["g"], s.g(self.dn_w), self._bg([self.dn_b])))
+            wq += w_tasks(s, dy, ctx["g"], [self.dn_w], self._bn([self.dn_b]), self.lora_s)
             dgu = ops.swiglu_bwd(dh, ctx["gu"])
             del dh
             dh2 = ops.linear_dx(dgu, self._w(self.up_w))
-            wq.append(WTask(dgu, ctx["h2"], self._gw(self.up_w), self._bg(self.up_b)))
+            wq += w_tasks(s, dgu, ctx["h2"], self.up_w, self._bn(self.up_b), self.lora_s)
         dx2 = self._norm_bwd(dh2, ctx["x2"], None, ctx["m2"], ctx["r2"], "ln2", dy)
         do = ops.linear_dx(dx2, s.w(n("proj.weight")))
-        wq.append(WTask(dx2, ctx["o"], s.g(n("proj.weight")), self._bg([n("proj.bias")])))
+        wq += w_tasks(s, dx2, ctx["o"], [n("proj.weight")], self._bn([n("proj.bias")]),
+                      self.lora_s)
         dqkv = ops.attention_bwd(ctx["qkv"], ctx["o"], do, ctx["lse"], B, S, H, hd, c.kv_heads)
         if c.pos == "rope":
             ops.rope(dqkv, S, c.d_model + c.kv_heads * hd, hd, c.rope_theta, inverse=True)
         dh1 = ops.linear_dx(dqkv, self._w(self.qkv_w))
-        wq.append(WTask(dqkv, ctx["h1"], self._gw(self.qkv_w), self._bg(self.qkv_b)))
+        wq += w_tasks(s, dqkv, ctx["h1"], self.qkv_w, self._bn(self.qkv_b), self.lora_s)
         dx = self._norm_bwd(dh1, x.x, x.scale, ctx["m1"], ctx["r1"], "ln1", dx2)
         ctx.clear()
         return dx
@@ -383,11 +478,17 @@ class Head:
         V = c.vocab_size
         dl = ctx["dl"][:, :V]
         dh = ops.linear_dx(dl, s.w(self.out))
-        wq.append(WTask(dl, ctx["h"], s.g(self.out), None))
+        scale = c.lora_alpha / c.lora_rank if c.lora_rank else 1.0
+        wq += w_tasks(s, dl, ctx["h"], [self.out], None, scale)
         x: Act = ctx["x"]
+        dg = s.g(n("ln_f.weight"))
         dbeta = None if self.rms else s.g(n("ln_f.bias"))
+        if dg is None:
+            d = x.x.shape[1]
+            dg = s.sink(2 * d)[:d]
+            dbeta = None if self.rms else s.sink(2 * d)[d:]
         dx = ops.layernorm_bwd(dh, x.x, x.scale, ctx["m"], ctx["r"], s.p(n("ln_f.weight")), None,
-                               s.g(n("ln_f.weight")), dbeta, accumulate=True)
+                               dg, dbeta, accumulate=True)
         ctx.clear()
         return dx
 
@@ -412,9 +513,18 @@ class StageModel:
             for sp in entry_specs(cfg, e):
                 specs.append(sp)
                 entry_of[sp.name] = e
-        work = torch.bfloat16 if self.device.type == "cuda" else None
+        work = torch.bfloat16 if self.device.type == "cuda" else (
+            torch.float32 if cfg.lora_rank else None)
+        if cfg.lora_rank and cfg.moe_experts:
+            raise NotImplementedError("LoRA over MoE blocks is not built")
+        if cfg.lora_rank and self.device.type == "cuda" and cfg.lora_rank % 8:
+            raise ValueError("lora_rank must be a multiple of 8 on the GPU kernels")
         self.store = ParamStore(specs, self.device, work_dtype=work)
         init_params(self.store, seed, entry_of, cfg.init_std, cfg.n_layer, cfg.init_scheme)
+        # adapted linears: (base weight, A, B)
+        self.adapters = [(n[:-len(".A.weight")] + ".weight", n, n[:-len(".A.weight")] + ".B.weight")
+                         for n in self.store.names() if n.endswith(".A.weight")]
+        self.after_step()
         self.layers = []
         for e in range(self.lo, self.hi):
             if e == 0:
@@ -427,6 +537,20 @@ class StageModel:
     @property
     def first(self) -> bool:
         return self.lo == 0
+
+    def after_step(self):
+        """Refresh what depends on the trained tensors: with LoRA, the working
+        copy of each adapted base becomes W + (alpha / r) B A (computed in
+        fp32, rounded once), so forward and input-gradient GEMMs run the
+        merged weight unchanged."""
+        if not self.adapters:
+            return
+        s, c = self.store, self.cfg
+        scale = c.lora_alpha / c.lora_rank
+        with torch.no_grad():
+            for w, a, b in self.adapters:
+                merged = s.p(w) + scale * (s.p(b) @ s.p(a))
+                s.w(w).copy_(merged)
 
     def moe_blocks(self) -> list:
         """The MoE MLPs of this stage, in entry order."""

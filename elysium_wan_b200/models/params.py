@@ -30,21 +30,35 @@ class ParamSpec:
     fan_in: int = 1
     matrix: bool = False  # read by a GEMM (needs the bf16 working copy)
     pack: bool = False  # the next tensor follows with no alignment gap (read as one operand)
+    frozen: bool = False  # not trained: no gradient, no optimizer state (LoRA base)
 
 
 class ParamStore:
+    """Trainable tensors first, frozen ones after: the gradient buffer and the
+    optimizer cover only [0, nt)."""
+
     def __init__(self, specs: list[ParamSpec], device: torch.device, work_dtype=None):
-        self.specs = list(specs)
+        self.declared = list(specs)  # declaration order (fixes each tensor's init stream)
+        self.specs = [s for s in specs if not s.frozen] + [s for s in specs if s.frozen]
         self.device = torch.device(device)
         self.index: dict[str, tuple[int, tuple]] = {}
+        self.frozen = {s.name for s in self.specs if s.frozen}
         off = 0
+        self.nt = None
         for s in self.specs:
+            if s.frozen and self.nt is None:
+                off = (off + ALIGN - 1) // ALIGN * ALIGN
+                self.nt = max(off, ALIGN)
+                off = self.nt
             self.index[s.name] = (off, tuple(s.shape))
             n = math.prod(s.shape)
             off += n if s.pack else (n + ALIGN - 1) // ALIGN * ALIGN
         self.numel = max(off, ALIGN)
+        if self.nt is None:
+            self.nt = self.numel
         self.master = torch.zeros(self.numel, dtype=torch.float32, device=self.device)
-        self.grad = torch.zeros(self.numel, dtype=torch.float32, device=self.device)
+        self.grad = torch.zeros(self.nt, dtype=torch.float32, device=self.device)
+        self._sink = None
         self.work_dtype = work_dtype
         self.work = (torch.zeros(self.numel, dtype=work_dtype, device=self.device)
                      if work_dtype is not None else None)
@@ -65,7 +79,17 @@ class ParamStore:
         return self._view(self.work if self.work is not None else self.master, name)
 
     def g(self, name):
+        """fp32 gradient view; None for a frozen tensor."""
+        if name in self.frozen:
+            return None
         return self._view(self.grad, name)
+
+    def sink(self, n: int):
+        """A scratch fp32 buffer of n elements for gradients a kernel must
+        write but nobody reads (a frozen norm's)."""
+        if self._sink is None or self._sink.numel() < n:
+            self._sink = torch.zeros(n, dtype=torch.float32, device=self.device)
+        return self._sink[:n]
 
     def joint_offset(self, names) -> int | None:
         """Offset of `names` when they sit back to back in the store (same
@@ -95,6 +119,8 @@ class ParamStore:
         return self._joint(self.work if self.work is not None else self.master, names)
 
     def gj(self, names):
+        if any(n in self.frozen for n in names):
+            return None
         return self._joint(self.grad, names)
 
     def zero_grad(self):
@@ -125,7 +151,7 @@ def init_params(store: ParamStore, seed: int, entry_of: dict, std: float, n_laye
     the same values as the single-device oracle on the same device type."""
     dev = store.device
     per_entry_count: dict[int, int] = {}
-    for s in store.specs:
+    for s in store.declared:
         e = entry_of[s.name]
         j = per_entry_count.get(e, 0)
         per_entry_count[e] = j + 1
@@ -136,6 +162,9 @@ def init_params(store: ParamStore, seed: int, entry_of: dict, std: float, n_laye
             v.zero_()
         elif s.init == "ones":
             v.fill_(1.0)
+        elif s.init == "lora_a":  # kaiming-uniform on the adapter's A, B starts at zero
+            b = math.sqrt(6.0 / max(1, s.fan_in))
+            v.copy_(torch.rand(s.shape, generator=gen, device=dev) * (2 * b) - b)
         elif scheme == "torch_default":
             if s.init == "embed":
                 v.copy_(torch.randn(s.shape, generator=gen, device=dev))
@@ -144,6 +173,7 @@ def init_params(store: ParamStore, seed: int, entry_of: dict, std: float, n_laye
                 v.copy_(torch.rand(s.shape, generator=gen, device=dev) * (2 * b) - b)
         elif s.init == "bias":
             v.zero_()
+
         else:  # gpt2: N(0, std), residual projections scaled by 1/sqrt(2 n_layer)
             sd = std / math.sqrt(2.0 * n_layer) if s.init == "normal_resid" else std
             v.copy_(torch.randn(s.shape, generator=gen, device=dev) * sd)

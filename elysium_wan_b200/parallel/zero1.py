@@ -52,7 +52,7 @@ class Zero1:
         st = engine.store
         self.w = engine.width
         self.k = engine.peer
-        self.n = st.numel
+        self.n = st.nt  # the trainable region
         self.bounds = shard_bounds(self.n, self.w)
         lo, hi = self.bounds[self.k]
         self.lo, self.hi = lo, hi

@@ -41,7 +41,11 @@ class StageEngine:
         self.order = [(op, int(mb)) for op, mb in spec.schedule_order[stage][peer]]
         self.recompute = spec.recomputes(stage)
         st = self.store
-        self.opt = optim.build(spec.optimizer, st.master, st.grad, st.work, spec.lr, spec.adamw)
+        # The optimizer covers the trainable region [0, nt) (all of it unless
+        # LoRA froze the base).
+        self.opt = optim.build(spec.optimizer, st.master[:st.nt], st.grad,
+                               st.work[:st.nt] if st.work is not None else None, spec.lr,
+                               spec.adamw)
         self.width = spec.stage_widths[stage]
         self.step_done = 0
         self.losses: list = []  # (step, mb, float)
@@ -62,7 +66,8 @@ class StageEngine:
         """Bind the stage channels (after warm_kernels, before the first step)."""
         self.comm = comm
         if self.width > 1 and self.zero1 is None:
-            if self.spec.grad_sync == "fused" and self.device.type == "cuda":
+            if self.spec.grad_sync == "fused" and self.device.type == "cuda" and \
+                    not self.spec.model.lora_rank:
                 from elysium_wan_b200.parallel.fused import FusedZero1
 
                 self.zero1 = FusedZero1(self, comm)
@@ -228,6 +233,7 @@ class StageEngine:
             self.zero1.sync_and_step()
         else:
             self.opt.step()
+        self.model.after_step()
         self._moe_after_step()
         if ev:
             e_opt = torch.cuda.Event(enable_timing=True)
@@ -292,6 +298,7 @@ class StageEngine:
     def load_state_dict(self, sd: dict):
         self.store.master.copy_(sd["params"].to(self.store.master.device))
         self.store.sync_work()
+        self.model.after_step()
         self.opt.load_state_dict(sd["opt"])
         for k, v in self.model.buffers().items():
             if k in sd.get("buffers", {}):

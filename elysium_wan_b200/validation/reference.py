@@ -46,12 +46,13 @@ class Oracle:
             w = self.widths[r]
             self.partials.append([torch.zeros_like(st.grad) for _ in range(w)] if w > 1 else None)
             if w == 1:
-                self.opts.append([optim.build(spec.optimizer, st.master, st.grad, st.work, spec.lr,
-                                              spec.adamw)])
+                self.opts.append([optim.build(spec.optimizer, st.master[:st.nt], st.grad,
+                                              st.work[:st.nt] if st.work is not None else None,
+                                              spec.lr, spec.adamw)])
             else:
                 os_ = []
                 self._grad_shards = getattr(self, "_grad_shards", {})
-                for k, (lo, hi) in enumerate(shard_bounds(st.numel, w)):
+                for k, (lo, hi) in enumerate(shard_bounds(st.nt, w)):
                     work = st.work[lo:hi] if st.work is not None else None
                     os_.append(optim.build(spec.optimizer, st.master[lo:hi], st.grad[lo:hi], work,
                                            spec.lr, spec.adamw))
@@ -100,12 +101,13 @@ class Oracle:
             out.append((mb, loss))
         for r, m in enumerate(self.stages):
             if self.partials[r] is not None:
-                for lo, hi in shard_bounds(m.store.numel, self.widths[r]):
+                for lo, hi in shard_bounds(m.store.nt, self.widths[r]):
                     m.store.grad[lo:hi] = fold_tree([p[lo:hi] for p in self.partials[r]])
             for o in self.opts[r]:
                 o.step()
             if self.partials[r] is not None:
                 m.store.sync_work()
+            m.after_step()
         # MoE: the global batch's expert counts drive the selection-bias update.
         tokens = spec.microbatches * spec.mb_size * spec.model.seq_len
         for m in self.stages:

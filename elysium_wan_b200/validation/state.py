@@ -41,7 +41,7 @@ def reference_manifest(oracle) -> dict:
         ents = store_entries(m.store)
         from elysium_wan_b200.parallel.zero1 import shard_bounds
 
-        bounds = shard_bounds(m.store.numel, oracle.widths[r]) if oracle.widths[r] > 1 else [(0, m.store.numel)]
+        bounds = shard_bounds(m.store.nt, oracle.widths[r]) if oracle.widths[r] > 1 else [(0, m.store.nt)]
         for (lo, hi), o in zip(bounds, oracle.opts[r]):
             mm, vv = o.m, o.v
             sub = store_entries(m.store, mm, vv, lo)

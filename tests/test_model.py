@@ -165,3 +165,48 @@ def test_moe_bias_update_moves_by_gamma():
 
     with pytest.raises(ValueError):
         m.moe_bias_update({1: torch.tensor([1, 1, 1, 1], dtype=torch.int64)}, 8)
+
+
+def test_lora_adapters_match_autograd():
+    """LoRA: base frozen (no gradient, no optimizer state), adapters trained;
+    the forward runs W + (alpha/r) B A and the adapter gradients equal
+    autograd through that merge."""
+    import dataclasses
+
+    from ._ref_general import ref_loss_general
+
+    for targets in ("attn", "all"):
+        cfg = make_config("llama_tiny", n_layer=2, vocab_size=97, d_model=64, n_head=4,
+                          n_kv_head=2, seq_len=16, lora_rank=4, lora_alpha=8.0,
+                          lora_targets=targets)
+        m = StageModel(cfg, (0, cfg.n_entries), "cpu", seed=3)
+        st = m.store
+        torch.manual_seed(1)
+        for n in st.names():  # B starts at zero; give it values so both paths are exercised
+            if n.endswith(".B.weight"):
+                st.p(n).normal_(0, 0.05)
+        st.sync_work()
+        m.after_step()
+        assert st.nt < st.numel and st.grad.numel() == st.nt
+        assert st.g("1.q.weight") is None and st.g("1.q.A.weight") is not None
+        idx = torch.randint(0, 97, (2, 16))
+        tgt = torch.randint(0, 97, (2, 16))
+        st.zero_grad()
+        loss = _run([m], idx, tgt)
+        P = {n: st.p(n).detach().clone().requires_grad_(n.endswith((".A.weight", ".B.weight")))
+             for n in st.names()}
+        eff = dict(P)
+        s = cfg.lora_alpha / cfg.lora_rank
+        for w, a, b in m.adapters:
+            eff[w] = P[w] + s * (P[b] @ P[a])
+        base_cfg = dataclasses.replace(cfg, lora_rank=0)
+        ce, _ = ref_loss_general(base_cfg, eff, idx, tgt)
+        ce.backward()
+        assert abs(loss.item() - ce.item()) < 1e-5
+        for n in st.names():
+            if n.endswith((".A.weight", ".B.weight")):
+                g, r = st.g(n), P[n].grad
+                err = ((g - r).norm() / (r.norm() + 1e-12)).item()
+                assert err < 2e-4, (targets, n, err)
+        if targets == "all":
+            assert "3.out.A.weight" in st.names()

@@ -27,6 +27,10 @@ CASES = {
     # Llama block (RMSNorm, GQA, RoPE, SwiGLU, no bias) cut over 2 stages.
     "llama_chain2": dict(stages=2, model_kw=dict(norm="rmsnorm", mlp="swiglu", pos="rope",
                                                  bias=False, n_kv_head=2)),
+    # LoRA over the Llama block: frozen base, adapters trained, wide stage.
+    "lora_wide_1_2": dict(stages=2, stage_widths=[1, 2],
+                          model_kw=dict(norm="rmsnorm", mlp="swiglu", pos="rope", bias=False,
+                                        n_kv_head=2, lora_rank=8, lora_targets="attn_mlp")),
     # MoE block with a selection bias that moves every step, recompute, a
     # wide second stage (counts summed over its replicas).
     "moe_wide_1_2": dict(stages=2, stage_widths=[1, 2], recompute=True,
