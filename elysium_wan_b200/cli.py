@@ -192,6 +192,18 @@ def cmd_import_hf(a) -> int:
     return 0
 
 
+def cmd_recut(a) -> int:
+    """Move a width-1 chain's waves to another partition (resume with the new spec)."""
+    from elysium_wan_b200.fault_tolerance.recut import recut
+    from elysium_wan_b200.runtime.spec import JobSpec
+
+    old = JobSpec.load(a.spec).finalize()
+    new = JobSpec.load(a.new_spec).finalize()
+    step = recut(old, new, a.step)
+    print("WT_RECUT " + json.dumps({"step": step, "from": old.partition, "to": new.partition}))
+    return 0
+
+
 def build_parser() -> argparse.ArgumentParser:
     ap = argparse.ArgumentParser(prog="wantrain")
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -295,6 +307,12 @@ def build_parser() -> argparse.ArgumentParser:
     ih.add_argument("--compute-dtype", default="fp32")
     ih.add_argument("--boundary-dtype", default="fp32")
     ih.set_defaults(fn=cmd_import_hf)
+
+    rc = sub.add_parser("recut", help="move checkpoint waves to another stage partition")
+    rc.add_argument("--spec", required=True, help="the spec the waves were written under")
+    rc.add_argument("--new-spec", required=True, help="the spec to resume under")
+    rc.add_argument("--step", type=int, default=None)
+    rc.set_defaults(fn=cmd_recut)
     return ap
 
 

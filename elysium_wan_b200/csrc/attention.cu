@@ -555,6 +555,10 @@ int attn_bwd_hd(const AttnBwdArgs& a, cudaStream_t stream) {
 // Sequences that are a multiple of 128 use 8-warp CTAs (128 rows); others 4.
 int attention_fwd(const AttnArgs& a, cudaStream_t stream) {
   if (a.S % 64 || a.d != a.H * a.hd || (a.Hkv > 0 && a.H % a.Hkv)) return 1;
+  if (a.impl == 0 && a.hd == 128 && a.S % 128 == 0) {
+    const int rc = attention_fwd_tc(a, a.status, stream);
+    if (rc != 1) return rc;
+  }
   const bool big = a.S % 128 == 0;
   switch (a.hd) {
     case 64: return big ? attn_fwd_hd<64, 8>(a, stream) : attn_fwd_hd<64, 4>(a, stream);
@@ -566,6 +570,15 @@ int attention_fwd(const AttnArgs& a, cudaStream_t stream) {
 
 int attention_bwd(const AttnBwdArgs& a, cudaStream_t stream) {
   if (a.S % 64 || a.d != a.H * a.hd || (a.Hkv > 0 && a.H % a.Hkv)) return 1;
+  if (a.impl == 0 && a.hd == 128 && a.S % 128 == 0) {
+    const int T = a.B * a.S;
+    const int warps = T * a.H;
+    attn_bwd_dot_kernel<<<(warps * 32 + 255) / 256, 256, 0, stream>>>(a.o, a.dout, a.Dbuf, T,
+                                                                      a.S, a.H, a.hd, a.d);
+    if (cudaGetLastError() != cudaSuccess) return 2;
+    const int rc = attention_bwd_tc(a, a.status, stream);
+    if (rc != 1) return rc;
+  }
   const bool big = a.S % 128 == 0;
   switch (a.hd) {
     case 64: return big ? attn_bwd_hd<64, 8>(a, stream) : attn_bwd_hd<64, 4>(a, stream);

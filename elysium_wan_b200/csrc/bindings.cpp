@@ -14,6 +14,8 @@
 #include <unistd.h>
 
 #include <atomic>
+#include <cstdlib>
+#include <string>
 
 #include "gemm.h"
 #include "kernels.h"
@@ -26,6 +28,15 @@ void count(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
 // One device status word per GPU (an int in device memory): kernels that time
 // out on a bounded wait record a code there; the host reads it after a step.
+// EWB_ATTN_IMPL=mma forces the mma.sync attention kernels (comparisons).
+int attn_impl() {
+  static int v = [] {
+    const char* e = std::getenv("EWB_ATTN_IMPL");
+    return (e != nullptr && std::string(e) == "mma") ? 1 : 0;
+  }();
+  return v;
+}
+
 int* status_word(int dev) {
   static int* words[64] = {nullptr};
   if (dev < 0 || dev >= 64) return nullptr;
@@ -276,6 +287,8 @@ void attention_fwd(at::Tensor qkv, at::Tensor o, at::Tensor lse, int64_t B, int6
   a.d = H * hd;
   a.scale = static_cast<float>(scale);
   a.Hkv = static_cast<int>(Hkv);
+  a.status = status_word(qkv.device().index());
+  a.impl = attn_impl();
   const int64_t hkv = Hkv > 0 ? Hkv : H;
   TORCH_CHECK(qkv.numel() == B * S * (a.d + 2 * hkv * hd), "qkv shape");
   ok(ewb::attention_fwd(a, cur_stream()), "attention_fwd");
@@ -303,6 +316,8 @@ void attention_bwd(at::Tensor qkv, at::Tensor o, at::Tensor dout, at::Tensor lse
   a.d = H * hd;
   a.scale = static_cast<float>(scale);
   a.Hkv = static_cast<int>(Hkv);
+  a.status = status_word(qkv.device().index());
+  a.impl = attn_impl();
   TORCH_CHECK(dqkv.numel() == qkv.numel(), "dqkv shape");
   ok(ewb::attention_bwd(a, cur_stream()), "attention_bwd");
   count(3);

@@ -122,6 +122,18 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// Untiled bulk copy of `bytes` (a multiple of 16; both addresses 16-byte
+// aligned) from global memory into this CTA's shared memory, completing as
+// transaction bytes on `bar`.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // Bulk-tensor store / reduce-add of one box from this CTA's shared memory to
 // global memory (tracked by bulk async-groups of the issuing thread). x is the
 // innermost coordinate; out-of-range parts of the box are not written.
@@ -226,6 +238,22 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
   tmem_ld16(taddr, r);
   tmem_ld16(taddr + 16, r + 16);
+}
+
+// 32 lanes x 32 bit, 16 consecutive columns: thread t of the warp writes lane
+// (base_lane + t), columns [col, col + 16). Complete with tmem_wait_st().
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 // UMMA shared-memory descriptor (sm100 "version 1" layout) for a 128-byte

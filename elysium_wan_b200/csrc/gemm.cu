@@ -706,4 +706,11 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
   return bn == 128 ? dispatch_bn<128>(g, stream, sc) : dispatch_bn<256>(g, stream, sc);
 }
 
+// Exported for the other tcgen05 kernels (attention): a bf16 2D tensor map
+// with 128-byte swizzle over [outer][ld] memory.
+bool tma_map_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                     uint64_t ld, uint32_t box_inner, uint32_t box_outer) {
+  return make_map_bf16(map, base, inner, outer, ld, box_inner, box_outer);
+}
+
 }  // namespace ewb

@@ -75,4 +75,9 @@ struct GemmArgs {
 int gemm_launch(const GemmArgs& args, cudaStream_t stream);
 int gemm_pick_bn(int M, int N);
 
+// bf16 2D tensor map with 128-byte swizzle (inner = contiguous extent in
+// elements, ld = row pitch in elements); false if the driver refuses it.
+bool tma_map_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                     uint64_t ld, uint32_t box_inner, uint32_t box_outer);
+
 }  // namespace ewb

@@ -61,8 +61,12 @@ struct AttnArgs {
   int B, S, H, hd, d;
   float scale;  // softmax scale, 1/sqrt(hd)
   int Hkv;
+  int* status;  // device status word of the bounded waits (may be null)
+  int impl;     // 0 = best available, 1 = mma.sync kernels only
 };
 int attention_fwd(const AttnArgs& a, cudaStream_t stream);
+// tcgen05 / TMEM / TMA forward (hd 128, S % 128 == 0); 1 = shape not supported.
+int attention_fwd_tc(const AttnArgs& a, int* status, cudaStream_t stream);
 
 struct AttnBwdArgs {
   const __nv_bfloat16* qkv;
@@ -74,8 +78,12 @@ struct AttnBwdArgs {
   int B, S, H, hd, d;
   float scale;
   int Hkv;
+  int* status;  // device status word of the bounded waits (may be null)
+  int impl;     // 0 = best available, 1 = mma.sync kernels only
 };
 int attention_bwd(const AttnBwdArgs& a, cudaStream_t stream);
+// tcgen05 backward (hd 128, S % 128 == 0; D already in a.Dbuf); 1 = unsupported.
+int attention_bwd_tc(const AttnBwdArgs& a, int* status, cudaStream_t stream);
 
 // ---------------------------------------------------------------- cross-entropy
 // Row-wise softmax cross-entropy over fp32 logits [T][ldl] (V valid columns).

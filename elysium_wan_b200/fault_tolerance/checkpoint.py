@@ -39,10 +39,13 @@ def wave_dir(out_dir: str, tag: str, stage: int, peer: int, step: int) -> str:
     return os.path.join(slot_dir(out_dir, tag, stage, peer), f"step-{step:08d}")
 
 
-def commit_wave(spec, stage: int, peer: int, step: int, state: dict) -> str:
-    """Write state.pt + wave.json atomically; prune to WAVE_KEEP; refresh the alias."""
+def commit_wave(spec, stage: int, peer: int, step: int, state: dict, replace: bool = False) -> str:
+    """Write state.pt + wave.json atomically; prune to WAVE_KEEP; refresh the
+    alias. An existing wave of the step is kept, unless `replace` (re-cut
+    writes the same step under a new partition): the new wave is staged
+    completely, then swapped in by two renames."""
     final = wave_dir(spec.out_dir, spec.tag, stage, peer, step)
-    if os.path.isdir(final):
+    if os.path.isdir(final) and not replace:
         return final
     tmp = final + ".staging"
     shutil.rmtree(tmp, ignore_errors=True)
@@ -59,7 +62,14 @@ def commit_wave(spec, stage: int, peer: int, step: int, state: dict) -> str:
         json.dump(meta, f, indent=1)
         f.flush()
         os.fsync(f.fileno())
-    os.rename(tmp, final)
+    if os.path.isdir(final):
+        old = final + ".replaced"
+        shutil.rmtree(old, ignore_errors=True)
+        os.rename(final, old)
+        os.rename(tmp, final)
+        shutil.rmtree(old, ignore_errors=True)
+    else:
+        os.rename(tmp, final)
     alias = os.path.join(spec.out_dir, f"{spec.tag}_ckpt_rank{stage}p{peer}.pt")
     try:
         if os.path.exists(alias):
@@ -77,7 +87,7 @@ def list_waves(out_dir: str, tag: str, stage: int, peer: int) -> list:
         return []
     out = []
     for name in os.listdir(d):
-        if name.startswith("step-") and not name.endswith(".staging"):
+        if name.startswith("step-") and not name.endswith((".staging", ".replaced")):
             try:
                 out.append(int(name[5:]))
             except ValueError:

@@ -33,29 +33,34 @@ class ParamSpec:
     frozen: bool = False  # not trained: no gradient, no optimizer state (LoRA base)
 
 
+def plan_layout(specs: list[ParamSpec]):
+    """(ordered specs, {name: (offset, shape)}, nt, numel) of a flat store:
+    trainable tensors first, each on an ALIGN boundary unless its predecessor
+    packs it, frozen tensors after nt."""
+    ordered = [s for s in specs if not s.frozen] + [s for s in specs if s.frozen]
+    index: dict[str, tuple[int, tuple]] = {}
+    off, nt = 0, None
+    for s in ordered:
+        if s.frozen and nt is None:
+            off = (off + ALIGN - 1) // ALIGN * ALIGN
+            nt = max(off, ALIGN)
+            off = nt
+        index[s.name] = (off, tuple(s.shape))
+        n = math.prod(s.shape)
+        off += n if s.pack else (n + ALIGN - 1) // ALIGN * ALIGN
+    numel = max(off, ALIGN)
+    return ordered, index, (numel if nt is None else nt), numel
+
+
 class ParamStore:
     """Trainable tensors first, frozen ones after: the gradient buffer and the
     optimizer cover only [0, nt)."""
 
     def __init__(self, specs: list[ParamSpec], device: torch.device, work_dtype=None):
         self.declared = list(specs)  # declaration order (fixes each tensor's init stream)
-        self.specs = [s for s in specs if not s.frozen] + [s for s in specs if s.frozen]
         self.device = torch.device(device)
-        self.index: dict[str, tuple[int, tuple]] = {}
+        self.specs, self.index, self.nt, self.numel = plan_layout(specs)
         self.frozen = {s.name for s in self.specs if s.frozen}
-        off = 0
-        self.nt = None
-        for s in self.specs:
-            if s.frozen and self.nt is None:
-                off = (off + ALIGN - 1) // ALIGN * ALIGN
-                self.nt = max(off, ALIGN)
-                off = self.nt
-            self.index[s.name] = (off, tuple(s.shape))
-            n = math.prod(s.shape)
-            off += n if s.pack else (n + ALIGN - 1) // ALIGN * ALIGN
-        self.numel = max(off, ALIGN)
-        if self.nt is None:
-            self.nt = self.numel
         self.master = torch.zeros(self.numel, dtype=torch.float32, device=self.device)
         self.grad = torch.zeros(self.nt, dtype=torch.float32, device=self.device)
         self._sink = None

@@ -151,3 +151,37 @@ def test_replacement_prefers_same_class_and_region():
              NodeInfo("n3", "w3", region="eu", device_class="cpu")]
     assert find_replacement(dead, cands).node_id == "n2"
     assert find_replacement(dead, [cands[2]], match="device") is None
+
+
+def test_recut_resume_continues_the_run_bitwise(tmp_path):
+    """Waves of a 2-stage run at step 2, re-cut to a 3-stage partition, resume
+    to step 4: every loss equals the uninterrupted run's."""
+    import json as _json
+    import os as _os
+
+    from elysium_wan_b200.fault_tolerance.recut import recut
+    from elysium_wan_b200.launch.local import run_local
+    from elysium_wan_b200.models.config import make_config
+    from elysium_wan_b200.runtime.spec import JobSpec
+
+    cfg = make_config("toy", n_layer=4, vocab_size=97, d_model=64, n_head=4, seq_len=16)
+    base = 33000 + _os.getpid() % 300 * 11
+
+    def spec(stages, partition, steps, out, tag, resume=False, port=0):
+        s = JobSpec(model=cfg, stages=stages, partition=partition, microbatches=2, mb_size=2,
+                    steps=steps, out_dir=str(out), tag=tag, ckpt_every=1, resume=resume,
+                    port_base=base + port, backend="gloo")
+        return s.finalize()
+
+    full = run_local(spec(2, [[0, 3], [3, 6]], 4, tmp_path / "full", "run"), timeout=300)
+    part = spec(2, [[0, 3], [3, 6]], 2, tmp_path / "cut", "run", port=3)
+    run_local(part, timeout=300)
+    new = spec(3, [[0, 2], [2, 4], [4, 6]], 4, tmp_path / "cut", "run", resume=True, port=6)
+    assert recut(part, new) == 2
+    resumed = run_local(new, timeout=300)
+    with open(full) as f:
+        want = {(r["step"], r["mb"]): r["loss_hex"] for r in _json.load(f)["losses"]}
+    with open(resumed) as f:
+        got = {(r["step"], r["mb"]): r["loss_hex"] for r in _json.load(f)["losses"]}
+    later = {k: v for k, v in want.items() if k[0] >= 2}
+    assert later and all(got.get(k) == v for k, v in later.items()), (later, got)
