@@ -25,7 +25,7 @@ for var, path in (("CC", "/usr/bin/gcc"), ("CXX", "/usr/bin/g++")):
         os.environ[var] = path
 CSRC = os.path.join("elysium_wan_b200", "csrc")
 CU = ["gemm.cu", "norm.cu", "attention.cu", "ce.cu", "embed.cu", "optim.cu", "misc.cu",
-      "collectives.cu", "llama.cu"]
+      "collectives.cu", "llama.cu", "attention_tc.cu"]
 
 NVCC = [
     "-gencode", "arch=compute_100a,code=sm_100a",
