@@ -63,6 +63,13 @@ def run_stage(spec, stage: int, peer: int, timeout_s: float = 600.0) -> int:
         dev = f"cuda:{local}" if dev == "cuda" else dev
         torch.cuda.set_device(torch.device(dev))
     _print("WT_PHASE", {"phase": "init", "stage": stage, "peer": peer, "rank": rank})
+    if spec.dataset_path:
+        # A data-reading slot verifies (and fetches) its shards before it connects.
+        from elysium_wan_b200.models.provision import provision_slot
+
+        rep = provision_slot(spec, stage, peer)
+        if rep is not None:
+            _print("WT_PHASE", {"phase": "provision", **rep})
     init_group(spec, rank, timeout_s)
     if spec.world_size == 1:
         comm = None
