@@ -55,6 +55,14 @@ __device__ __forceinline__ void load8(const void* x, const float* xs, int x_fp8,
   }
 }
 
+// 8 consecutive fp32 parameters (gamma / beta) as two 16-byte loads.
+__device__ __forceinline__ void load8_f32(const float* p, float* v) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+  const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
 __device__ __forceinline__ void store8_bf16(__nv_bfloat16* p, const float* v) {
   uint4 w;
   w.x = pack_bf16x2(v[0], v[1]);
@@ -104,10 +112,11 @@ __global__ void __launch_bounds__(kLnThreads)
   for (int j = 0; j < S; ++j) {
     const int col = j * 1024 + threadIdx.x * 8;
     if (col < d) {
-      float o[8];
+      float o[8], gm[8], bt[8];
+      load8_f32(gamma + col, gm);
+      if (!RMS) load8_f32(beta + col, bt);
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-        o[i] = (v[j][i] - mean) * rstd * gamma[col + i] + (RMS ? 0.f : beta[col + i]);
+      for (int i = 0; i < 8; ++i) o[i] = (v[j][i] - mean) * rstd * gm[i] + (RMS ? 0.f : bt[i]);
       store8_bf16(y + static_cast<size_t>(row) * ldy + col, o);
     }
   }
@@ -150,13 +159,14 @@ __global__ void __launch_bounds__(kLnThreads)
     for (int j = 0; j < S; ++j) {
       const int col = j * 1024 + threadIdx.x * 8;
       if (col < d) {
-        float xv[8], dv[8];
+        float xv[8], dv[8], gm[8];
         load8(x, xs, x_fp8, ldx, ldxs, row, col, xv);
         load8(dy, nullptr, 0, lddy, 0, row, col, dv);
+        load8_f32(gamma + col, gm);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const float xh = (xv[i] - mu) * rs;
-          const float g = dv[i] * gamma[col + i];
+          const float g = dv[i] * gm[i];
           s1 += g;
           s2 += g * xh;
           pg[j][i] += dv[i] * xh;
@@ -171,13 +181,14 @@ __global__ void __launch_bounds__(kLnThreads)
     for (int j = 0; j < S; ++j) {
       const int col = j * 1024 + threadIdx.x * 8;
       if (col < d) {
-        float xv[8], dv[8], o[8];
+        float xv[8], dv[8], o[8], gm[8];
         load8(x, xs, x_fp8, ldx, ldxs, row, col, xv);
         load8(dy, nullptr, 0, lddy, 0, row, col, dv);
+        load8_f32(gamma + col, gm);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const float xh = (xv[i] - mu) * rs;
-          const float g = dv[i] * gamma[col + i];
+          const float g = dv[i] * gm[i];
           o[i] = rs * (g - m1 - xh * m2);
         }
         if (dres != nullptr) {

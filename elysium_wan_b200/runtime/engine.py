@@ -16,6 +16,7 @@ Per-op device time comes from CUDA events (busy fraction per stage); the
 
 from __future__ import annotations
 
+import os
 import time
 
 import torch
@@ -51,6 +52,8 @@ class StageEngine:
         self.losses: list = []  # (step, mb, float)
         self.events: list = []  # per-op (op, mb, start_event, end_event)
         self.timing = spec.device_for(stage, peer).startswith("cuda")
+        # NVTX range per F / B / W op (EWB_NVTX=1), for external timeline tools.
+        self.nvtx = self.timing and os.environ.get("EWB_NVTX") == "1"
         self.telemetry: list = []
         self._host_x = None
         import os
@@ -175,9 +178,18 @@ class StageEngine:
             if op == "W" and mb in inline_done:
                 continue
             dbg(f"stage {self.stage} op {op}{mb} start")
-            if ev:
-                e0 = torch.cuda.Event(enable_timing=True)
-                e0.record()
+            e0 = None
+
+            def mark():
+                # The op's start event goes after its input receive, so waiting
+                # on a peer counts as idle, not busy.
+                nonlocal e0
+                if ev:
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                if self.nvtx:
+                    torch.cuda.nvtx.range_push(f"{op}{mb}")
+
             if op == "F":
                 if self.first:
                     inp = batches[mb][0]
@@ -187,6 +199,7 @@ class StageEngine:
                 if not self.first and fi < len(f_mbs):
                     act_q[f_mbs[fi]] = comm.irecv_act(f_mbs[fi])
                 tgt = batches[mb][1] if self.last else None
+                mark()
                 out, st = self.model.forward(inp, tgt, keep=keep)
                 saved[mb] = st
                 if self.last:
@@ -206,6 +219,7 @@ class StageEngine:
                 # B, releasing each layer's W inputs at once (same fold order).
                 inline = idx + 1 < len(self.order) and self.order[idx + 1] == ("W", mb)
                 tasks: list = []
+                mark()
                 dx = self.model.backward(st, dy, tasks, run_w_inline=inline,
                                          w_exec=lambda ts, m=mb: self._run_w(ts, m))
                 if inline:
@@ -215,7 +229,10 @@ class StageEngine:
                 if not self.first:
                     sends += comm.send_grad(mb, dx)
             else:  # W
+                mark()
                 self._run_w(wq.pop(mb), mb)
+            if self.nvtx:
+                torch.cuda.nvtx.range_pop()
             if ev:
                 e1 = torch.cuda.Event(enable_timing=True)
                 e1.record()

@@ -43,6 +43,22 @@ def init_group(spec, rank: int, timeout_s: float):
                             timeout=datetime.timedelta(seconds=timeout_s), **kw)
 
 
+def env_fingerprint(dev: str) -> dict:
+    """What the run's numbers depend on besides the spec: versions, device,
+    host (written once per run as <tag>_env.json)."""
+    import platform
+
+    fp = {"python": platform.python_version(), "torch": torch.__version__,
+          "cuda": torch.version.cuda, "host": platform.node(), "device": dev}
+    if dev.startswith("cuda") and torch.cuda.is_available():
+        p = torch.cuda.get_device_properties(torch.device(dev))
+        fp.update(gpu=p.name, sm=f"{p.major}.{p.minor}", gpu_mem_gib=round(p.total_memory / 2**30, 1),
+                  nccl=".".join(map(str, torch.cuda.nccl.version())))
+    fp["env"] = {k: v for k, v in os.environ.items()
+                 if k.startswith(("EWB_", "NCCL_", "TORCH_NCCL", "CUDA_MODULE", "ELYSIUM_"))}
+    return fp
+
+
 def loss_path(spec, stage, peer) -> str:
     return os.path.join(spec.out_dir, f"{spec.tag}_losses_r{stage}p{peer}.json")
 
@@ -84,6 +100,19 @@ def run_stage(spec, stage: int, peer: int, timeout_s: float = 600.0) -> int:
     eng = StageEngine(spec, stage, peer, comm, dev)
     _print("WT_STAGE", {"stage": stage, "peer": peer, "span": spec.partition[stage],
                         "params": eng.store.numel, "device": dev})
+    _print("WT_OPT", {"optimizer": spec.optimizer, "trainable": eng.store.nt,
+                      "frozen": eng.store.numel - eng.store.nt,
+                      "zero1": type(eng.zero1).__name__ if eng.zero1 is not None else None})
+    if spec.model.lora_rank:
+        _print("WT_LORA", {"rank": spec.model.lora_rank, "targets": spec.model.lora_targets,
+                           "adapted": len(eng.model.adapters), "trainable_params": eng.store.nt,
+                           "frozen_params": eng.store.numel - eng.store.nt})
+    if getattr(comm, "peers_seen", None):
+        _print("WT_AEAD", {"cipher": "chacha20-poly1305", "peers": comm.peers_seen})
+    if stage == 0 and peer == 0:
+        os.makedirs(spec.out_dir, exist_ok=True)
+        with open(os.path.join(spec.out_dir, f"{spec.tag}_env.json"), "w") as f:
+            json.dump(env_fingerprint(dev), f, indent=1)
     start = 0
     if spec.resume:
         sd, step = ckpt.load_latest(spec, stage, peer, spec.resume_step)
@@ -92,6 +121,9 @@ def run_stage(spec, stage: int, peer: int, timeout_s: float = 600.0) -> int:
         _print("WT_RESUME", {"step": step})
     os.makedirs(spec.out_dir, exist_ok=True)
     stream = open(os.path.join(spec.out_dir, f"{spec.tag}_loss_stream.jsonl"), "a") if eng.last else None
+    tel = open(os.path.join(spec.out_dir, f"{spec.tag}_rank{stage}p{peer}_telemetry.jsonl"), "a")
+    net0 = (0, 0)
+    t_run = time.perf_counter()
     for step in range(start, spec.steps):
         t0 = time.perf_counter()
         res = eng.run_step(step)
@@ -107,10 +139,27 @@ def run_stage(spec, stage: int, peer: int, timeout_s: float = 600.0) -> int:
         summary = summarize_step(step, stage, peer, dt * 1e3, eng.op_times_ms(),
                                  comm.bytes_sent if comm else 0, comm.frames if comm else 0)
         _print("WT_TELEM", summary)
+        tel.write(json.dumps({"step": step, "events": [[o, m, round(a, 4), round(d, 4)]
+                                                        for o, m, a, d in eng.op_times_ms()]})
+                  + "\n")
+        tel.flush()
+        if comm is not None:
+            net = (comm.frames, comm.bytes_sent)
+            _print("WT_NET", {"step": step, "frames": net[0] - net0[0], "bytes": net[1] - net0[1]})
+            net0 = net
+        if eng.timing:
+            _print("WT_MEM", {"step": step,
+                              "max_alloc_gib": round(torch.cuda.max_memory_allocated() / 2**30, 3),
+                              "reserved_gib": round(torch.cuda.memory_reserved() / 2**30, 3)})
         if spec.ckpt_every and (step + 1) % spec.ckpt_every == 0:
             path = ckpt.commit_wave(spec, stage, peer, step + 1, eng.state_dict())
             _print("WT_WAVE", {"step": step + 1, "dir": path})
         _print("WT_STEP", {"step": step, "ms": round(dt * 1e3, 3)})
+    tel.close()
+    n_run = spec.steps - start
+    _print("WT_TIMING", {"steps": n_run, "total_s": round(time.perf_counter() - t_run, 3),
+                         "mean_step_ms": round((time.perf_counter() - t_run) * 1e3 / max(1, n_run),
+                                               3)})
     if eng.last:
         with open(loss_path(spec, stage, peer), "w") as f:
             json.dump({"losses": loss_records(eng.losses)}, f, indent=1)
