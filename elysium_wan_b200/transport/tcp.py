@@ -169,6 +169,7 @@ class TcpPipeComm:
         self.bytes_sent = 0
         self.frames = 0
         self.peers_seen: dict = {}
+        self.tuning: dict = {}
         self._connect()
 
     # ----------------------------------------------------------------- setup
@@ -193,6 +194,9 @@ class TcpPipeComm:
                 spec.endpoints[self.stage][self.peer][2] else port
             lsock = socket.socket(socket.AF_INET, socket.SOCK_STREAM)
             lsock.setsockopt(socket.SOL_SOCKET, socket.SO_REUSEADDR, 1)
+            from elysium_wan_b200.transport import tuning
+
+            self.tuning = tuning.tune(lsock)  # accepted flows inherit it
             lsock.bind(("0.0.0.0" if host not in ("127.0.0.1", "localhost") else host, int(bind)))
             lsock.listen(n_in + 4)
         accepted: dict = collections.defaultdict(dict)
@@ -247,12 +251,13 @@ class TcpPipeComm:
                     self._start_reader(sc)
 
     def _dial(self, host, port):
+        from elysium_wan_b200.transport import tuning
+
         end = time.monotonic() + self.timeout
         while True:
             try:
-                s = socket.create_connection((host, port), timeout=5)
-                s.setsockopt(socket.IPPROTO_TCP, socket.TCP_NODELAY, 1)
-                s.settimeout(None)
+                s, applied = tuning.connect(host, port, 5.0)
+                self.tuning = applied
                 return s
             except OSError:
                 if time.monotonic() > end:

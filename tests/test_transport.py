@@ -168,3 +168,16 @@ def test_pipeline_over_sealed_tcp_is_bitwise(tmp_path, monkeypatch):
     r = run_and_compare(spec, timeout=300)
     assert r["ok"], r
     assert r["compared"] == 8
+
+
+def test_socket_tuning_plan_and_apply():
+    from elysium_wan_b200.transport import tuning
+
+    caps = {"wmem_max": 64 << 20, "rmem_max": 8 << 20, "tcp_wmem": 4 << 20, "tcp_rmem": 6 << 20}
+    p = tuning.plan(32 << 20, caps)
+    assert p == {"sndbuf": 32 << 20, "rcvbuf": None}  # rcvbuf hard cap too low: autotuning kept
+    assert tuning.plan(2 << 20, caps) == {"sndbuf": None, "rcvbuf": None}  # below the ceilings
+    s = socket.socket()
+    rep = tuning.tune(s)  # never raises; reports what holds
+    assert set(rep) == {"cc", "sndbuf", "rcvbuf", "pace"}
+    s.close()
