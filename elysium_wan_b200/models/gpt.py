@@ -479,7 +479,11 @@ class Head:
         dl = ctx["dl"][:, :V]
         dh = ops.linear_dx(dl, s.w(self.out))
         scale = c.lora_alpha / c.lora_rank if c.lora_rank else 1.0
-        wq += w_tasks(s, dl, ctx["h"], [self.out], None, scale)
+        if c.tie_embeddings:
+            if not c.lora_rank or c.lora_targets == "all":
+                wq.append(WTask(dl, ctx["h"], s.tied_grad, None))
+        else:
+            wq += w_tasks(s, dl, ctx["h"], [self.out], None, scale)
         x: Act = ctx["x"]
         dg = s.g(n("ln_f.weight"))
         dbeta = None if self.rms else s.g(n("ln_f.bias"))
@@ -501,10 +505,6 @@ class StageModel:
         cfg.validate()
         self.cfg = cfg
         self.lo, self.hi = span
-        if cfg.tie_embeddings and not (self.lo == 0 and self.hi == cfg.n_layer + 2):
-            raise NotImplementedError(
-                "tie_embeddings with the table and the head on different stages needs the tied "
-                "relay, which this engine does not build: keep both on one stage")
         self.device = torch.device(device)
         if self.device.type == "cuda" and cfg.compute_dtype != "bf16":
             raise ValueError("the sm_100a kernels compute in bf16: set compute_dtype='bf16'")
@@ -513,6 +513,15 @@ class StageModel:
             for sp in entry_specs(cfg, e):
                 specs.append(sp)
                 entry_of[sp.name] = e
+        # Tied embeddings: the head's stage without the table holds a relay copy
+        # of it (not trained here: stage 0 sends the updated values each step);
+        # it draws the same init stream as the table (entry 0, index 0).
+        self.tied = cfg.tie_embeddings and self.hi == cfg.n_entries
+        if self.tied and self.lo > 0:
+            V, d = cfg.vocab_size, cfg.d_model
+            specs.append(ParamSpec("0.tok.weight", (V, d), "embed", fan_in=d, matrix=True,
+                                   frozen=True))
+            entry_of["0.tok.weight"] = 0
         work = torch.bfloat16 if self.device.type == "cuda" else (
             torch.float32 if cfg.lora_rank else None)
         if cfg.lora_rank and cfg.moe_experts:
@@ -520,7 +529,13 @@ class StageModel:
         if cfg.lora_rank and self.device.type == "cuda" and cfg.lora_rank % 8:
             raise ValueError("lora_rank must be a multiple of 8 on the GPU kernels")
         self.store = ParamStore(specs, self.device, work_dtype=work)
-        init_params(self.store, seed, entry_of, cfg.init_std, cfg.n_layer, cfg.init_scheme)
+        init_params(self.store, seed, entry_of, cfg.init_std, cfg.n_layer, cfg.init_scheme,
+                    first_of_entry={"0.tok.weight": 0} if self.tied and self.lo > 0 else None)
+        # The head's gradient of a tied table accumulates apart from the
+        # embedding's (its own fold, microbatch order); before the optimizer the
+        # table's gradient becomes (embedding part) + (head part) on every cut.
+        self.store.tied_grad = (torch.zeros((cfg.vocab_size, cfg.d_model), dtype=torch.float32,
+                                            device=self.device) if self.tied else None)
         # adapted linears: (base weight, A, B)
         self.adapters = [(n[:-len(".A.weight")] + ".weight", n, n[:-len(".A.weight")] + ".B.weight")
                          for n in self.store.names() if n.endswith(".A.weight")]
@@ -537,6 +552,25 @@ class StageModel:
     @property
     def first(self) -> bool:
         return self.lo == 0
+
+    def zero_grad(self):
+        self.store.zero_grad()
+        if self.store.tied_grad is not None:
+            self.store.tied_grad.zero_()
+
+    def fold_tied(self, head_part=None):
+        """Table gradient += the head's part (its own, or one received from the
+        head's stage). Called once per step, after every microbatch."""
+        g = self.store.g("0.tok.weight")
+        if g is None:
+            return
+        g.add_(self.store.tied_grad if head_part is None else head_part)
+
+    def set_tied_table(self, values):
+        """The relay copy takes stage 0's updated table (and its working copy)."""
+        s = self.store
+        s.p("0.tok.weight").copy_(values)
+        s.w("0.tok.weight").copy_(values)
 
     def after_step(self):
         """Refresh what depends on the trained tensors: with LoRA, the working

@@ -64,6 +64,7 @@ class ParamStore:
         self.master = torch.zeros(self.numel, dtype=torch.float32, device=self.device)
         self.grad = torch.zeros(self.nt, dtype=torch.float32, device=self.device)
         self._sink = None
+        self.tied_grad = None
         self.work_dtype = work_dtype
         self.work = (torch.zeros(self.numel, dtype=work_dtype, device=self.device)
                      if work_dtype is not None else None)
@@ -150,7 +151,7 @@ class ParamStore:
 
 
 def init_params(store: ParamStore, seed: int, entry_of: dict, std: float, n_layer: int,
-                scheme: str = "gpt2"):
+                scheme: str = "gpt2", first_of_entry: dict | None = None):
     """Deterministic init: parameter j of entry e draws from its own generator
     seeded by (seed, e, j), so a stage initialises only its own slice and gets
     the same values as the single-device oracle on the same device type."""
@@ -158,8 +159,11 @@ def init_params(store: ParamStore, seed: int, entry_of: dict, std: float, n_laye
     per_entry_count: dict[int, int] = {}
     for s in store.declared:
         e = entry_of[s.name]
-        j = per_entry_count.get(e, 0)
-        per_entry_count[e] = j + 1
+        if first_of_entry and s.name in first_of_entry:
+            j = first_of_entry[s.name]  # a copy of another stage's tensor: its stream
+        else:
+            j = per_entry_count.get(e, 0)
+            per_entry_count[e] = j + 1
         gen = torch.Generator(device=dev)
         gen.manual_seed((seed * 1_000_003 + e * 7919 + j) % (2**63 - 1))
         v = store.p(s.name)

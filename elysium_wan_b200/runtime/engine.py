@@ -145,7 +145,7 @@ class StageEngine:
         self.model.backward(st, dy, tasks)
         for t in tasks:
             t.run()
-        self.store.zero_grad()
+        self.model.zero_grad()
         if self.device.type == "cuda":
             torch.cuda.synchronize(self.device)
 
@@ -155,7 +155,7 @@ class StageEngine:
         last stage (floats after one device->host read), else []."""
         spec = self.spec
         comm = self.comm
-        self.store.zero_grad()
+        self.model.zero_grad()
         f_mbs = [mb for op, mb in self.order if op == "F"]
         b_mbs = [mb for op, mb in self.order if op == "B"]
         batches = self._stage_batches(step, f_mbs) if (self.first or self.last) else {}
@@ -246,10 +246,12 @@ class StageEngine:
             w.wait()
         if comm is not None:
             comm.flush()
+        self._tied_fold()
         if self.zero1 is not None:
             self.zero1.sync_and_step()
         else:
             self.opt.step()
+        self._tied_relay()
         self.model.after_step()
         self._moe_after_step()
         if ev:
@@ -265,6 +267,32 @@ class StageEngine:
             for mb, v in out:
                 self.losses.append((step, mb, v))
         return out
+
+    def _tied_fold(self):
+        """Tied embeddings: the table's gradient becomes (embedding part) +
+        (head part); across a cut the head's stage sends its part to stage 0."""
+        if not self.spec.model.tie_embeddings:
+            return
+        if self.first and self.last:
+            self.model.fold_tied()
+        elif self.last:
+            self.comm.tied_send(self.store.tied_grad)
+        elif self.first:
+            buf = torch.empty_like(self.store.p("0.tok.weight"))
+            self.comm.tied_recv(buf)
+            self.model.fold_tied(buf)
+
+    def _tied_relay(self):
+        """After the optimizer, stage 0 sends the updated table to the head's
+        stage, whose relay copy (and working copy) take it."""
+        if not self.spec.model.tie_embeddings or (self.first and self.last):
+            return
+        if self.first:
+            self.comm.tied_send(self.store.p("0.tok.weight"))
+        elif self.last:
+            buf = torch.empty_like(self.store.p("0.tok.weight"))
+            self.comm.tied_recv(buf)
+            self.model.set_tied_table(buf)
 
     def _moe_after_step(self):
         """MoE bookkeeping after the optimizer step: the step's int64 expert

@@ -169,6 +169,10 @@ class JobSpec:
         for r, row in enumerate(self.mb_owner):
             if len(row) != self.microbatches or not all(0 <= p < self.stage_widths[r] for p in row):
                 raise ValueError(f"mb_owner[{r}] must map every microbatch to a peer of stage {r}")
+        if self.model.tie_embeddings and self.stages > 1 and \
+                (self.stage_widths[0] != 1 or self.stage_widths[-1] != 1):
+            raise NotImplementedError("a tied table across a cut needs width-1 first and last "
+                                      "stages")
         if self.schedule_order is None:
             self.schedule_order = default_schedule(self)
         self._check_schedule_order()

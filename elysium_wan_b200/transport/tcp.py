@@ -154,6 +154,15 @@ class TcpPipeComm:
             g = dist.new_group([spec.rank_of(r, q) for q in range(w)]) if world > 1 else None
             if r == stage:
                 self.g_stage = g
+        # Tied embeddings across a cut: stage 0 and the head's stage exchange
+        # the head's table gradient and the updated table once per step.
+        self.g_tied = None
+        if spec.model.tie_embeddings and spec.stages > 1 and world > 1:
+            a, b = spec.rank_of(0, 0), spec.rank_of(spec.stages - 1, 0)
+            g = dist.new_group([a, b])
+            if self.rank in (a, b):
+                self.g_tied = g
+            self.tied_peer = b if self.rank == a else a
         cfg = spec.model
         self.T, self.d = spec.mb_size * cfg.seq_len, cfg.d_model
         self.cuda = self.device.type == "cuda"
@@ -334,6 +343,12 @@ class TcpPipeComm:
         if self.fp8:
             return Act(bufs[0].view(torch.float8_e4m3fn), bufs[1])
         return Act(bufs[0])
+
+    def tied_send(self, t):
+        dist.send(t.contiguous(), self.tied_peer, group=self.g_tied)
+
+    def tied_recv(self, buf):
+        dist.recv(buf, self.tied_peer, group=self.g_tied)
 
     def flush(self):
         for link in list(self.next_links.values()) + list(self.prev_links.values()):

@@ -62,7 +62,7 @@ class Oracle:
     def step(self, step: int) -> list:
         spec = self.spec
         for m in self.stages:
-            m.store.zero_grad()
+            m.zero_grad()
         for part in self.partials:
             if part is not None:
                 for p in part:
@@ -99,6 +99,8 @@ class Oracle:
                     m.store.grad = saved_grads[i]
                     i += 1
             out.append((mb, loss))
+        if spec.model.tie_embeddings:  # table gradient = embedding part + head part
+            self.stages[0].fold_tied(self.stages[-1].store.tied_grad)
         for r, m in enumerate(self.stages):
             if self.partials[r] is not None:
                 for lo, hi in shard_bounds(m.store.nt, self.widths[r]):
@@ -108,6 +110,8 @@ class Oracle:
             if self.partials[r] is not None:
                 m.store.sync_work()
             m.after_step()
+        if spec.model.tie_embeddings and len(self.stages) > 1:
+            self.stages[-1].set_tied_table(self.stages[0].store.p("0.tok.weight"))
         # MoE: the global batch's expert counts drive the selection-bias update.
         tokens = spec.microbatches * spec.mb_size * spec.model.seq_len
         for m in self.stages:

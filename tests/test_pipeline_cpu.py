@@ -51,3 +51,25 @@ def test_pipeline_bitwise_vs_oracle(tmp_path, name):
     r = run_and_compare(spec, timeout=240)
     assert r["ok"], r
     assert r["compared"] == 8
+
+
+def test_tied_embeddings_across_a_cut_equal_one_stage(tmp_path):
+    """A tied table split from its head by a cut (relay copy on the last
+    stage, head gradient sent to stage 0, updated table sent back) gives the
+    same losses as the single-device oracle, and the oracle of a 3-stage cut
+    equals the oracle of one stage: the tied fold does not depend on the cut."""
+    from elysium_wan_b200.validation.reference import Oracle
+
+    mk = dict(norm="rmsnorm", mlp="swiglu", pos="rope", bias=False, tie_embeddings=True)
+    port = 34000 + (os.getpid() % 300) * 9
+    spec = JobSpec(model=_cfg(**mk), stages=3, microbatches=4, mb_size=2, steps=2,
+                   out_dir=str(tmp_path), port_base=port, backend="gloo")
+    r = run_and_compare(spec, timeout=240)
+    assert r["ok"], r
+    one = JobSpec(model=_cfg(**mk), stages=1, microbatches=4, mb_size=2, steps=2,
+                  out_dir=str(tmp_path / "one")).finalize()
+    o1, o3 = Oracle(one), Oracle(spec)
+    for step in range(2):
+        a = [v.hex() for _, v in o1.step(step)]
+        b = [v.hex() for _, v in o3.step(step)]
+        assert a == b
