@@ -56,7 +56,6 @@ class StageEngine:
         self.nvtx = self.timing and os.environ.get("EWB_NVTX") == "1"
         self.telemetry: list = []
         self._host_x = None
-        import os
 
         side = os.environ.get("EWB_W_STREAM", "1") == "1"
         self.wexec = WExecutor(self.device, enabled=side)

@@ -30,6 +30,8 @@ def _run(models, idx, tgt):
     for wq in wqs:
         for t in wq:
             t.run()
+    if models[0].cfg.tie_embeddings:  # the step's tied fold (engine: before the optimizer)
+        models[0].fold_tied(models[-1].store.tied_grad if len(models) > 1 else None)
     return loss
 
 
