@@ -235,7 +235,13 @@ def run_ours(args) -> dict | None:
     if ot:
         from elysium_wan_b200.runtime.telemetry import summarize_step
 
-        busy = summarize_step(0, rank, 0, 0.0, ot, 0, 0)["busy_frac"]
+        summ = summarize_step(0, rank, 0, 0.0, ot, 0, 0)
+        busy = summ["busy_frac"]
+        # Per-rank diagnostics of the last timed step (stderr): busy fraction
+        # of the op span, op medians, ops / optimizer phase split.
+        print("[bench] rank %d: %s" % (rank, json.dumps(
+            {"busy_frac": busy, "busy_ms": summ["busy_ms"], "ops": summ.get("ops"),
+             "phases": eng.phase_ms()})), file=sys.stderr, flush=True)
     vec = torch.tensor([dev_ms, wall_ms, float(launches), busy or 0.0, busy or 2.0],
                        dtype=torch.float64, device=dev)
     if world > 1:
