@@ -501,7 +501,8 @@ class StageModel:
     """The entries [lo, hi) of the flat layer list on one device, with their
     parameter store. lo == 0 owns the embedding; hi == n_layer + 2 owns the head."""
 
-    def __init__(self, cfg: GPTConfig, span: tuple[int, int], device, seed: int):
+    def __init__(self, cfg: GPTConfig, span: tuple[int, int], device, seed: int,
+                 shard: tuple | None = None):
         cfg.validate()
         self.cfg = cfg
         self.lo, self.hi = span
@@ -522,13 +523,15 @@ class StageModel:
             specs.append(ParamSpec("0.tok.weight", (V, d), "embed", fan_in=d, matrix=True,
                                    frozen=True))
             entry_of["0.tok.weight"] = 0
+        # CPU stores read the master directly unless a working copy must differ
+        # from it (LoRA's merged weights) or hold more than it (pieces).
         work = torch.bfloat16 if self.device.type == "cuda" else (
-            torch.float32 if cfg.lora_rank else None)
+            torch.float32 if cfg.lora_rank or shard is not None else None)
         if cfg.lora_rank and cfg.moe_experts:
             raise NotImplementedError("LoRA over MoE blocks is not built")
         if cfg.lora_rank and self.device.type == "cuda" and cfg.lora_rank % 8:
             raise ValueError("lora_rank must be a multiple of 8 on the GPU kernels")
-        self.store = ParamStore(specs, self.device, work_dtype=work)
+        self.store = ParamStore(specs, self.device, work_dtype=work, shard=shard)
         init_params(self.store, seed, entry_of, cfg.init_std, cfg.n_layer, cfg.init_scheme,
                     first_of_entry={"0.tok.weight": 0} if self.tied and self.lo > 0 else None)
         # The head's gradient of a tied table accumulates apart from the

@@ -283,10 +283,10 @@ def load_into(model, state: dict, strict: bool = True):
     for n in names:
         if n in state:
             t = state[n]
-            if tuple(t.shape) != tuple(model.store.p(n).shape):
-                raise ValueError(f"{n}: checkpoint shape {tuple(t.shape)} != "
-                                 f"{tuple(model.store.p(n).shape)}")
-            model.store.p(n).copy_(t.to(model.store.device))
+            want = tuple(model.store.index[n][1])
+            if tuple(t.shape) != want:
+                raise ValueError(f"{n}: checkpoint shape {tuple(t.shape)} != {want}")
+            model.store.set_initial(n, t.to(model.store.device, torch.float32))
     model.store.sync_work()
 
 

@@ -33,35 +33,70 @@ class ParamSpec:
     frozen: bool = False  # not trained: no gradient, no optimizer state (LoRA base)
 
 
-def plan_layout(specs: list[ParamSpec]):
-    """(ordered specs, {name: (offset, shape)}, nt, numel) of a flat store:
+def plan_layout(specs: list[ParamSpec], replicated_first: bool = False):
+    """(ordered specs, {name: (offset, shape)}, nt, numel, nr) of a flat store:
     trainable tensors first, each on an ALIGN boundary unless its predecessor
-    packs it, frozen tensors after nt."""
-    ordered = [s for s in specs if not s.frozen] + [s for s in specs if s.frozen]
+    packs it, frozen tensors after nt. With `replicated_first` (the pieces
+    layout) the trainable non-matrix tensors (norms, biases, tables) come
+    before the matrices; nr is where the matrices start."""
+    train = [s for s in specs if not s.frozen]
+    if replicated_first:
+        train = [s for s in train if not s.matrix] + [s for s in train if s.matrix]
+    ordered = train + [s for s in specs if s.frozen]
     index: dict[str, tuple[int, tuple]] = {}
-    off, nt = 0, None
+    off, nt, nr = 0, None, None
     for s in ordered:
         if s.frozen and nt is None:
             off = (off + ALIGN - 1) // ALIGN * ALIGN
             nt = max(off, ALIGN)
             off = nt
+        if replicated_first and s.matrix and not s.frozen and nr is None:
+            off = (off + ALIGN - 1) // ALIGN * ALIGN
+            nr = off
         index[s.name] = (off, tuple(s.shape))
         n = math.prod(s.shape)
         off += n if s.pack else (n + ALIGN - 1) // ALIGN * ALIGN
     numel = max(off, ALIGN)
-    return ordered, index, (numel if nt is None else nt), numel
+    nt = numel if nt is None else nt
+    return ordered, index, nt, numel, (nt if nr is None else nr)
+
+
+def shard_ranges(n: int, w: int) -> list:
+    """w contiguous [lo, hi) ranges of n elements, boundaries on ALIGN."""
+    per = (n + w - 1) // w
+    per = (per + ALIGN - 1) // ALIGN * ALIGN
+    return [(min(n, k * per), min(n, (k + 1) * per)) for k in range(w)]
 
 
 class ParamStore:
     """Trainable tensors first, frozen ones after: the gradient buffer and the
-    optimizer cover only [0, nt)."""
+    optimizer cover only [0, nt).
 
-    def __init__(self, specs: list[ParamSpec], device: torch.device, work_dtype=None):
+    `shard=(k, w)` is the pieces layout of replica k of a width-w stage: the
+    non-matrix tensors [0, nr) keep a full fp32 master, the matrices [nr, nt)
+    keep only their k-th contiguous range [mlo, mhi) in fp32 (the bf16 working
+    copy stays whole; the replicas all-gather it after every step)."""
+
+    def __init__(self, specs: list[ParamSpec], device: torch.device, work_dtype=None,
+                 shard: tuple | None = None):
         self.declared = list(specs)  # declaration order (fixes each tensor's init stream)
         self.device = torch.device(device)
-        self.specs, self.index, self.nt, self.numel = plan_layout(specs)
+        self.specs, self.index, self.nt, self.numel, self.nr = plan_layout(
+            specs, replicated_first=shard is not None)
         self.frozen = {s.name for s in self.specs if s.frozen}
-        self.master = torch.zeros(self.numel, dtype=torch.float32, device=self.device)
+        self.shard = shard
+        if shard is not None:
+            if self.frozen:
+                raise NotImplementedError("the pieces layout holds no frozen tensors")
+            k, w = shard
+            self.mbounds = [(self.nr + lo, self.nr + hi)
+                            for lo, hi in shard_ranges(self.nt - self.nr, w)]
+            self.mlo, self.mhi = self.mbounds[k]
+            held = self.nr + (self.mhi - self.mlo)
+        else:
+            self.mlo = self.mhi = self.nr
+            held = self.numel
+        self.master = torch.zeros(held, dtype=torch.float32, device=self.device)
         self.grad = torch.zeros(self.nt, dtype=torch.float32, device=self.device)
         self._sink = None
         self.tied_grad = None
@@ -77,8 +112,45 @@ class ParamStore:
         return buf[off: off + math.prod(shape)].view(shape)
 
     def p(self, name):
-        """fp32 master view."""
-        return self._view(self.master, name)
+        """fp32 master view (in the pieces layout: a non-matrix tensor, or a
+        matrix that lies wholly inside this replica's range)."""
+        if self.shard is None:
+            return self._view(self.master, name)
+        off, shape = self.index[name]
+        n = math.prod(shape)
+        if off + n <= self.nr:
+            return self.master[off: off + n].view(shape)
+        if self.mlo <= off and off + n <= self.mhi:
+            o = self.nr + off - self.mlo
+            return self.master[o: o + n].view(shape)
+        raise KeyError(f"{name}: its fp32 master is held by another replica (pieces layout)")
+
+    def holds(self, name) -> bool:
+        try:
+            self.p(name)
+            return True
+        except KeyError:
+            return False
+
+    def master_ranges(self) -> list:
+        """[(flat lo, flat hi, master view)] of what this store holds in fp32."""
+        if self.shard is None:
+            return [(0, self.numel, self.master)]
+        return [(0, self.nr, self.master[:self.nr]),
+                (self.mlo, self.mhi, self.master[self.nr:])]
+
+    def set_initial(self, name, value):
+        """Initial values of one tensor: the held part of the fp32 master and
+        the whole working copy."""
+        off, shape = self.index[name]
+        n = math.prod(shape)
+        flat = value.reshape(-1)
+        for lo, hi, view in self.master_ranges():
+            a, b = max(lo, off), min(hi, off + n)
+            if a < b:
+                view[a - lo: b - lo].copy_(flat[a - off: b - off])
+        if self.work is not None:
+            self.work[off: off + n].copy_(flat)
 
     def w(self, name):
         """Compute-dtype view (bf16 working copy on the GPU, the master on CPU)."""
@@ -133,13 +205,19 @@ class ParamStore:
         self.grad.zero_()
 
     def sync_work(self):
-        if self.work is not None:
-            if self.master.is_cuda:
+        """Working copy of what this store holds in fp32 (in the pieces layout
+        the other replicas' matrix ranges arrive by all-gather)."""
+        if self.work is None:
+            return
+        for lo, hi, view in self.master_ranges():
+            if hi <= lo:
+                continue
+            if self.master.is_cuda and self.work.dtype == torch.bfloat16:
                 from elysium_wan_b200 import ops
 
-                ops.ext().cast_bf16(self.master, self.work)
+                ops.ext().cast_bf16(view, self.work[lo:hi])
             else:
-                self.work.copy_(self.master)
+                self.work[lo:hi].copy_(view)
 
     def state_dict(self) -> dict:
         return {name: self.p(name).detach().cpu().clone() for name in self.names()}
@@ -166,7 +244,8 @@ def init_params(store: ParamStore, seed: int, entry_of: dict, std: float, n_laye
             per_entry_count[e] = j + 1
         gen = torch.Generator(device=dev)
         gen.manual_seed((seed * 1_000_003 + e * 7919 + j) % (2**63 - 1))
-        v = store.p(s.name)
+        direct = store.shard is None
+        v = store.p(s.name) if direct else torch.empty(s.shape, dtype=torch.float32, device=dev)
         if s.init == "zeros":
             v.zero_()
         elif s.init == "ones":
@@ -182,8 +261,9 @@ def init_params(store: ParamStore, seed: int, entry_of: dict, std: float, n_laye
                 v.copy_(torch.rand(s.shape, generator=gen, device=dev) * (2 * b) - b)
         elif s.init == "bias":
             v.zero_()
-
         else:  # gpt2: N(0, std), residual projections scaled by 1/sqrt(2 n_layer)
             sd = std / math.sqrt(2.0 * n_layer) if s.init == "normal_resid" else std
             v.copy_(torch.randn(s.shape, generator=gen, device=dev) * sd)
+        if not direct:
+            store.set_initial(s.name, v)
     store.sync_work()

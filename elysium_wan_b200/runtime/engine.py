@@ -33,7 +33,10 @@ class StageEngine:
         self.device = torch.device(device or spec.device_for(stage, peer))
         if self.device.type == "cuda":
             torch.cuda.set_device(self.device)
-        self.model = StageModel(spec.model, tuple(spec.partition[stage]), self.device, spec.init_seed)
+        width = spec.stage_widths[stage]
+        self.pieces = spec.shard == "pieces" and width > 1
+        self.model = StageModel(spec.model, tuple(spec.partition[stage]), self.device, spec.init_seed,
+                                shard=(peer, width) if self.pieces else None)
         from elysium_wan_b200.models.hf import init_from_spec
 
         init_from_spec(self.model, spec)
@@ -44,9 +47,10 @@ class StageEngine:
         st = self.store
         # The optimizer covers the trainable region [0, nt) (all of it unless
         # LoRA froze the base).
-        self.opt = optim.build(spec.optimizer, st.master[:st.nt], st.grad,
-                               st.work[:st.nt] if st.work is not None else None, spec.lr,
-                               spec.adamw)
+        # (The pieces layout builds its two range optimizers when the comm attaches.)
+        self.opt = None if self.pieces else optim.build(
+            spec.optimizer, st.master[:st.nt], st.grad,
+            st.work[:st.nt] if st.work is not None else None, spec.lr, spec.adamw)
         self.width = spec.stage_widths[stage]
         self.step_done = 0
         self.losses: list = []  # (step, mb, float)
@@ -68,7 +72,11 @@ class StageEngine:
         """Bind the stage channels (after warm_kernels, before the first step)."""
         self.comm = comm
         if self.width > 1 and self.zero1 is None:
-            if self.spec.grad_sync == "fused" and self.device.type == "cuda" and \
+            if self.pieces:
+                from elysium_wan_b200.parallel.pieces import Pieces
+
+                self.zero1 = Pieces(self, comm)
+            elif self.spec.grad_sync == "fused" and self.device.type == "cuda" and \
                     not self.spec.model.lora_rank:
                 from elysium_wan_b200.parallel.fused import FusedZero1
 
@@ -342,6 +350,8 @@ class StageEngine:
     def load_state_dict(self, sd: dict):
         self.store.master.copy_(sd["params"].to(self.store.master.device))
         self.store.sync_work()
+        if self.pieces and self.zero1 is not None:
+            self.zero1._all_gather()  # the other replicas' matrix ranges of the working copy
         self.model.after_step()
         self.opt.load_state_dict(sd["opt"])
         for k, v in self.model.buffers().items():

@@ -9,6 +9,7 @@ fold tree drifted from the oracle, or recompute changed a value.
 import os
 
 import pytest
+import torch
 
 from elysium_wan_b200.launch.local import run_and_compare
 from elysium_wan_b200.models.config import make_config
@@ -27,6 +28,12 @@ CASES = {
     # Llama block (RMSNorm, GQA, RoPE, SwiGLU, no bias) cut over 2 stages.
     "llama_chain2": dict(stages=2, model_kw=dict(norm="rmsnorm", mlp="swiglu", pos="rope",
                                                  bias=False, n_kv_head=2)),
+    # Pieces (FSDP-like): the wide stage holds each matrix's fp32 master and
+    # moments once, gathers the working copy; same bits as ZeRO-1.
+    "pieces_1_2": dict(stages=2, stage_widths=[1, 2], shard="pieces"),
+    "pieces_3_llama": dict(stages=2, stage_widths=[3, 1], shard="pieces",
+                           model_kw=dict(norm="rmsnorm", mlp="swiglu", pos="rope", bias=False,
+                                         n_kv_head=2)),
     # LoRA over the Llama block: frozen base, adapters trained, wide stage.
     "lora_wide_1_2": dict(stages=2, stage_widths=[1, 2],
                           model_kw=dict(norm="rmsnorm", mlp="swiglu", pos="rope", bias=False,
@@ -73,3 +80,38 @@ def test_tied_embeddings_across_a_cut_equal_one_stage(tmp_path):
         a = [v.hex() for _, v in o1.step(step)]
         b = [v.hex() for _, v in o3.step(step)]
         assert a == b
+
+
+def test_pieces_layout_holds_one_range_and_resumes(tmp_path):
+    """A pieces replica holds the non-matrix tensors and 1/w of the matrices in
+    fp32; a run checkpointed and resumed in the pieces layout continues the
+    uninterrupted run bit for bit."""
+    import json
+
+    from elysium_wan_b200.launch.local import run_local
+    from elysium_wan_b200.models.gpt import StageModel
+
+    cfg = _cfg()
+    full = StageModel(cfg, (0, 3), "cpu", seed=1)
+    parts = [StageModel(cfg, (0, 3), "cpu", seed=1, shard=(k, 3)) for k in range(3)]
+    st = parts[0].store
+    assert st.master.numel() < full.store.master.numel() / 2
+    with pytest.raises(KeyError):
+        parts[0].store.p("2.fc2.weight")  # a matrix held by another replica
+    for k, p in enumerate(parts):  # every replica's working copy is the full model
+        assert torch.equal(p.store.w("1.qkv.weight"), full.store.w("1.qkv.weight"))
+    port = 35000 + (os.getpid() % 300) * 11
+
+    def spec(steps, out, resume=False, dp=0):
+        return JobSpec(model=cfg, stages=2, stage_widths=[2, 1], shard="pieces", microbatches=4,
+                       mb_size=2, steps=steps, out_dir=str(out), ckpt_every=1, resume=resume,
+                       port_base=port + dp, backend="gloo").finalize()
+
+    a = run_local(spec(3, tmp_path / "a"), timeout=300)
+    run_local(spec(2, tmp_path / "b", dp=3), timeout=300)
+    b = run_local(spec(3, tmp_path / "b", resume=True, dp=6), timeout=300)
+    with open(a) as f:
+        la = {(r["step"], r["mb"]): r["loss_hex"] for r in json.load(f)["losses"]}
+    with open(b) as f:
+        lb = {(r["step"], r["mb"]): r["loss_hex"] for r in json.load(f)["losses"]}
+    assert all(lb[k] == v for k, v in la.items() if k[0] == 2)
