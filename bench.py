@@ -44,7 +44,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
-BASELINE_TOK_S = 3344.0  # 15.8B GPT, 2x H100 NVL over WAN, run 3
+BASELINE_TOK_S = 3344.0  # the reference's published 15.8B GPT rate (2x H100 NVL over WAN, run 3)
 METRIC = "tokens/s (8xB200, max over ranks) 15.8B GPT PP+ZeRO-1"
 GiB = 1 << 30
 

@@ -5,7 +5,9 @@ Compute capture targets (one kernel, one to three launches, a few GB).
 
 Ops: gemm_fwd (qkv projection), gemm_dx (fc1 input gradient), gemm_dw (fc1
 weight gradient fold), gemm_q8 (fc2 with the fp8 boundary epilogue),
-attn_fwd, attn_bwd, ln_fwd, ln_bwd, ce, adamw, embed_bwd.
+attn_fwd, attn_bwd, ln_fwd, ln_bwd, ce, adamw, embed_bwd, head_gemm (the 50257-way
+logits GEMM, fp32 out), head_fwd (LN + logits + CE of the head entry), head_bwd
+(its forward, backward and W).
 """
 
 from __future__ import annotations
@@ -60,6 +62,31 @@ def build(op):
         dy = _bf(8 * T, D)
         dg, db = torch.zeros(D, device="cuda"), torch.zeros(D, device="cuda")
         return (lambda: ops.layernorm_bwd(dy, x, None, m, r, gam, dy, dg, db, True)), None, 8 * T * D * 8
+    if op == "head_gemm":
+        h, w = _bf(T, D), _bf(V, D, scale=0.02)
+        ld = (V + 7) // 8 * 8
+        logits = torch.empty((T, ld), dtype=torch.float32, device="cuda")[:, :V]
+        return (lambda: ops.gemm(h, w, logits, ops.EPI_F32)), 2.0 * T * V * D, None
+    if op in ("head_fwd", "head_bwd"):
+        from elysium_wan_b200.models.config import make_config
+        from elysium_wan_b200.models.gpt import Act, StageModel
+
+        cfg = make_config("gpt15b", n_layer=1)
+        m = StageModel(cfg, (cfg.n_entries - 1, cfg.n_entries), "cuda", seed=1)
+        head = m.layers[-1]
+        q, sc = ops.quant_e4m3(_bf(T, D).float())
+        tgt = torch.randint(0, V, (1, T), device="cuda")
+        if op == "head_fwd":
+            return (lambda: head.forward(Act(q, sc), {}, tgt)), 2.0 * T * V * D, None
+        ctx: dict = {}
+
+        def fb():
+            head.forward(Act(q, sc), ctx, tgt)
+            wq: list = []
+            head.backward(ctx, None, wq)
+            for t in wq:
+                t.run()
+        return fb, 3 * 2.0 * T * V * D, None
     if op == "ce":
         ld = (V + 7) // 8 * 8
         logits = torch.randn(T, ld, device="cuda")[:, :V]
