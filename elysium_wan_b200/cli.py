@@ -87,7 +87,11 @@ def cmd_worker(a) -> int:
     declare = json.loads(a.declare) if a.declare else {}
     w = WorkerAgent(a.coordinator, coordinator_id=a.coordinator_id, name=a.name,
                     workdir=a.workdir, device=a.device, region=a.region, wan_profile=a.wan_profile,
-                    declare=declare, no_bench=a.no_bench, advertise_host=a.advertise_host)
+                    declare=declare, no_bench=a.no_bench, advertise_host=a.advertise_host,
+                    probe_port=(a.probe_listen_port if a.probe_listen_port is not None
+                                else a.probe_port))
+    if a.probe_port is not None and a.probe_listen_port is not None:
+        w.probe_port = a.probe_port  # advertised (a forwarded port), the server binds the other
     return w.run() or 0
 
 

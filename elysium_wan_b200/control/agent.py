@@ -89,7 +89,8 @@ class WorkerAgent:
     def __init__(self, coordinator: str, coordinator_id: str = "", token: str | None = None,
                  name: str | None = None, workdir: str = "worker", device: str = "cpu",
                  region: str = "default", wan_profile: str | None = None, declare: dict | None = None,
-                 no_bench: bool = True, advertise_host: str = "127.0.0.1", heartbeat_s: float = 1.0):
+                 no_bench: bool = True, advertise_host: str = "127.0.0.1", heartbeat_s: float = 1.0,
+                 probe_port: int | None = None):
         host, _, port = coordinator.rpartition(":")
         self.addr = (host or "127.0.0.1", int(port))
         self.coordinator_id = coordinator_id
@@ -110,6 +111,12 @@ class WorkerAgent:
         self.stop = threading.Event()
         self.lock = threading.Lock()
         self.node_id = None
+        # Link probe server (round trip and bandwidth from other workers).
+        self.probe_port = None
+        if probe_port is not None:
+            from elysium_wan_b200.resources.links import serve_echo
+
+            self._probe_srv, self.probe_port = serve_echo("0.0.0.0", probe_port)
 
     # ----------------------------------------------------------------- connection
     def _caps(self) -> dict:
@@ -118,7 +125,7 @@ class WorkerAgent:
         caps = measure(self.device, bench=not self.no_bench)
         caps.update(self.declare)
         caps.update(name=self.name, region=self.region, host=self.advertise_host,
-                    wan_profile=self.wan_profile, pid=os.getpid())
+                    wan_profile=self.wan_profile, pid=os.getpid(), probe_port=self.probe_port)
         return caps
 
     def _connect(self):
@@ -192,6 +199,21 @@ class WorkerAgent:
         from elysium_wan_b200.resources.probe import measure
 
         self.send("MEASURE_RESULT", caps=measure(self.device, bench=True))
+
+    def _on_link_probe(self, hdr, body):
+        """Measure the path to another worker's probe server (in a thread: the
+        control channel keeps serving meanwhile)."""
+        from elysium_wan_b200.resources.links import measure_pair
+
+        def run():
+            try:
+                r = measure_pair(hdr["host"], int(hdr["port"]), flows=int(hdr.get("flows", 2)),
+                                 secs=float(hdr.get("secs", 0.5)))
+                self.send("LINK_RESULT", ok=True, target=hdr.get("target"), **r)
+            except Exception as e:
+                self.send("LINK_RESULT", ok=False, target=hdr.get("target"), why=repr(e))
+
+        threading.Thread(target=run, daemon=True).start()
 
     def _on_fit(self, hdr, body):
         from elysium_wan_b200.resources.fit import measure as fit_measure

@@ -127,6 +127,7 @@ class Coordinator:
         self.on_progress = None  # callback(slot, step, node_id)
         self._pending_ckpt: dict = {}
         self.link_memory = None
+        self.link_results: dict = {}
 
     # ----------------------------------------------------------------- server
     def start(self):
@@ -250,6 +251,9 @@ class Coordinator:
                         self.store.commit_staged(os.path.dirname(rel))
             elif kind == "TELEM_STEP":
                 self.events.append(("telem", nid, hdr.get("telem")))
+            elif kind == "LINK_RESULT":
+                self.link_results[(nid, hdr.get("target"))] = {k: v for k, v in hdr.items()
+                                                              if k != "kind"}
             else:
                 self.events.append((kind, nid, {k: v for k, v in hdr.items() if k != "kind"}))
 
@@ -299,6 +303,33 @@ class Coordinator:
             live = sorted(live, key=lambda n: regions.index(self.nodes[n].info.region))
         return live
 
+    def _probe_links(self, spec: JobSpec, timeout: float = 30.0) -> dict:
+        """Each pipeline hop measured by its upstream worker against the
+        downstream worker's probe server; results go to the link memory."""
+        asked = []
+        for j in range(spec.stages - 1):
+            a, b = self.slot_node[(j, 0)], self.slot_node[(j + 1, 0)]
+            bi = self.nodes[b].info
+            port = bi.caps.get("probe_port")
+            if not port:
+                continue
+            self.nodes[a].ch.send("LINK_PROBE", host=bi.host, port=int(port), target=b)
+            asked.append((j, a, b))
+        out = {}
+        end = time.time() + timeout
+        for j, a, b in asked:
+            while (a, b) not in self.link_results and time.time() < end:
+                time.sleep(0.05)
+            r = self.link_results.get((a, b))
+            if r and r.get("ok"):
+                ai, bi = self.nodes[a].info, self.nodes[b].info
+                mbps = min(r["up_mbps"], r["down_mbps"])
+                if self.link_memory is not None:
+                    self.link_memory.record_path(ai.host, bi.host, mbps, r["rtt_ms"],
+                                                 self.run_id or "probe")
+                out[f"{j}->{j + 1}"] = r
+        return out
+
     def _links(self, spec: JobSpec):
         links = []
         for j in range(spec.stages):
@@ -326,6 +357,7 @@ class Coordinator:
         slots = spec.slots()
         self.slot_node = {s: live[i] for i, s in enumerate(slots)}
         spares = live[len(slots):]
+        measured = {} if self.cfg.no_probe else self._probe_links(spec)
         self._links(spec)
         spec.finalize()
         self._final_step = spec.steps - 1
@@ -333,7 +365,8 @@ class Coordinator:
             f.write(spec.to_json())
         with open(os.path.join(run_dir, "rationale.json"), "w") as f:
             json.dump({"placement": {f"{s[0]}:{s[1]}": self.slot_node[s] for s in slots},
-                       "spares": spares, "links": spec.links}, f, indent=1)
+                       "spares": spares, "links": spec.links, "measured_links": measured},
+                      f, indent=1)
         heals = restarts = 0
         resume_step = None
         t_start = time.time()

@@ -66,3 +66,35 @@ def test_cluster_run_matches_oracle(tmp_path):
     ref.finalize()
     r = compare(run_baseline(ref, "reference"), res.losses_path)
     assert r["ok"] and r["compared"] == 6, r
+
+
+def test_coordinator_probes_pipeline_hops_into_link_memory(tmp_path):
+    """Workers with probe servers: the coordinator asks each hop's upstream
+    worker to measure the downstream one and remembers the path."""
+    import threading
+    import time as _t
+
+    from elysium_wan_b200.control.agent import WorkerAgent
+    from elysium_wan_b200.control.coordinator import Coordinator, CoordinatorConfig
+    from elysium_wan_b200.runtime.spec import JobSpec
+    from elysium_wan_b200.models.config import make_config
+
+    co = Coordinator(port=0, cfg=CoordinatorConfig(state_dir=str(tmp_path / "co"), no_probe=False))
+    co.start()
+    agents = [WorkerAgent(f"127.0.0.1:{co.port}", name=f"w{i}", workdir=str(tmp_path / f"w{i}"),
+                          probe_port=0) for i in range(2)]
+    for a in agents:
+        threading.Thread(target=a.run, daemon=True).start()
+    try:
+        live = co.wait_for_workers(2, 30)
+        spec = JobSpec(model=make_config("toy"), stages=2, microbatches=2, mb_size=1).finalize()
+        co.slot_node = {(0, 0): live[0], (1, 0): live[1]}
+        co.run_id = "probe-test"
+        got = co._probe_links(spec, timeout=30)
+        assert "0->1" in got and got["0->1"]["rtt_ms"] > 0
+        assert co.link_memory.path("127.0.0.1", "127.0.0.1") is not None
+    finally:
+        for a in agents:
+            a.stop.set()
+        co.stop()
+        _t.sleep(0.2)

@@ -174,3 +174,19 @@ def test_choose_returns_reason(policy):
     rows = autoconfig.evaluate(cfg, 10**8, 4, 1, 2, 1e5, 0.05, 1e12)
     row, why = autoconfig.choose(rows, policy)
     assert row is not None and isinstance(why, str)
+
+
+def test_link_probe_over_loopback_and_duplex_classes():
+    from elysium_wan_b200.resources import links
+
+    srv, port = links.serve_echo("127.0.0.1", 0)
+    try:
+        r = links.measure_pair("127.0.0.1", port, flows=2, secs=0.3)
+    finally:
+        srv.shutdown()
+    assert r["rtt_ms"] > 0 and r["up_mbps"] > 0 and r["down_mbps"] > 0
+    assert links.classify_duplex(100, 100, 190) == "full"
+    assert links.classify_duplex(100, 100, 100) == "half"
+    assert links.classify_duplex(100, 100, 150) == "shared"
+    em = links.Emulation("us", {"eu": {"rtt_ms": 120, "mbps": 500}})
+    assert em.link_to("eu").rtt_ms == 120 and em.link_to("us").mbps == 0.0
