@@ -37,6 +37,17 @@ int attn_impl() {
   return v;
 }
 
+// K-split of a GEMM's last wave (EWB_GEMM_SPLIT=0 turns it off; settable at
+// run time for A/B timing).
+int& gemm_split_flag() {
+  static int v = [] {
+    const char* e = std::getenv("EWB_GEMM_SPLIT");
+    return (e != nullptr && std::string(e) == "0") ? 0 : 1;
+  }();
+  return v;
+}
+void set_gemm_split(bool on) { gemm_split_flag() = on ? 1 : 0; }
+
 int* status_word(int dev) {
   static int* words[64] = {nullptr};
   if (dev < 0 || dev >= 64) return nullptr;
@@ -129,6 +140,7 @@ void gemm_impl(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor out,
   g.N = N;
   g.K = K;
   g.bn = bn;
+  g.split = gemm_split_flag();
   g.status = status_word(a.get_device());
   ewb::GemmEpilogue& e = g.ep;
   e.kind = static_cast<int>(epi);
@@ -185,7 +197,9 @@ void gemm_impl(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor out,
   count(1);
 }
 
-int64_t gemm_pick_bn(int64_t M, int64_t N) { return ewb::gemm_pick_bn(M, N); }
+int64_t gemm_pick_bn(int64_t M, int64_t N, int64_t K) {
+  return ewb::gemm_pick_bn(M, N, K, gemm_split_flag() != 0);
+}
 
 // beta absent = RMSNorm (no centring, no shift).
 void layernorm_fwd(at::Tensor x, c10::optional<at::Tensor> x_scale, at::Tensor gamma,
@@ -401,6 +415,7 @@ void cross_entropy(at::Tensor logits, int64_t V, at::Tensor targets, at::Tensor 
     TORCH_CHECK(dlogits->stride(0) == a.ldg, "dlogits must be dense");
   }
   a.grad_scale = static_cast<float>(grad_scale);
+  a.status = status_word(logits.get_device());
   ok(ewb::cross_entropy(a, cur_stream()), "cross_entropy");
   count(1);
 }
@@ -594,6 +609,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels of elysium_wan_b200";
   m.def("gemm", &gemm);
   m.def("gemm_pick_bn", &gemm_pick_bn);
+  m.def("set_gemm_split", &set_gemm_split);
   m.def("gemm_peer_scatter", &gemm_peer_scatter);
   m.def("zero1_push_partials", &zero1_push_partials);
   m.def("zero1_fold_slots", &zero1_fold_slots);

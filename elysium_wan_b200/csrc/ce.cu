@@ -1,12 +1,18 @@
-// Softmax cross-entropy over a vocabulary row, fwd + bwd in one pass pair.
+// Softmax cross-entropy over a vocabulary row, fwd + bwd in one kernel.
 //
 // Reference op: F.cross_entropy(logits.float(), targets) with mean reduction
 // (src/wantrain/model/gpt.py:556-557, logits made fp32 at gpt.py:418). Here the
-// head GEMM writes fp32 logits directly (tcgen05 epilogue kEpiF32), one CTA
-// per row computes the log-sum-exp with an online (max, sum) pair and a fixed
-// reduction tree, and the same CTA writes the bf16 gradient
-// (softmax - onehot) * grad_scale that feeds the head's dX / dW GEMMs.
-// Deterministic: fixed per-thread strides and a fixed tree, no atomics.
+// head GEMM writes fp32 logits directly (tcgen05 epilogue kEpiF32) and one CTA
+// per row writes the loss and the bf16 gradient (softmax - onehot) * grad_scale
+// that feeds the head's dX / dW GEMMs.
+//
+// Main path (rows up to 56K fp32, the GPT-2 vocabulary among them): the CTA
+// copies its whole row into shared memory with bulk copies (one HBM read of
+// the logits; a 2048 x 50257 fp32 block is 3x the L2, so a second pass would
+// go to DRAM again), then max, sum of exp(x - max) (kept in place) and the
+// gradient run from shared memory. Other rows: an online (max, sum) pass and a
+// gradient pass over global memory.
+// Deterministic: fixed per-thread element sets and fixed reduction trees.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -67,6 +73,106 @@ __global__ void __launch_bounds__(kCeThreads)
   }
 }
 
+constexpr int kCeSmemThreads = 1024;
+constexpr int kCeSmemMaxBytes = 225 * 1024;  // row buffer; 16 bytes of barrier follow
+constexpr int kCeCopyChunk = 32768;
+
+__device__ __forceinline__ float block_reduce(float v, float* red, bool is_max) {
+  // fixed tree: xor butterfly in each warp, then warp 0 over the 32 warp results
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float u = __shfl_xor_sync(0xffffffffu, v, o);
+    v = is_max ? fmaxf(v, u) : v + u;
+  }
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();  // red[] may still be read from the previous reduction
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    v = red[l];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float u = __shfl_xor_sync(0xffffffffu, v, o);
+      v = is_max ? fmaxf(v, u) : v + u;
+    }
+    if (l == 0) red[32] = v;
+  }
+  __syncthreads();
+  return red[32];
+}
+
+__global__ void __launch_bounds__(kCeSmemThreads, 1)
+    ce_smem_kernel(const float* __restrict__ logits, int ldl, const int64_t* __restrict__ targets,
+                   int V, float* __restrict__ loss_rows, __nv_bfloat16* __restrict__ dlogits,
+                   int ldg, float grad_scale, int row_bytes, int* status) {
+  extern __shared__ __align__(16) uint8_t ce_smem[];
+  float* xs = reinterpret_cast<float*>(ce_smem);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(ce_smem + row_bytes);
+  __shared__ float red[33];
+  const int row = blockIdx.x;
+  const float* x = logits + static_cast<size_t>(row) * ldl;
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(bar, static_cast<uint32_t>(row_bytes));
+    for (int off = 0; off < row_bytes; off += kCeCopyChunk)
+      bulk_load(ce_smem + off, reinterpret_cast<const uint8_t*>(x) + off,
+                static_cast<uint32_t>(min(kCeCopyChunk, row_bytes - off)), bar);
+  }
+  const bool landed = __syncthreads_and(mbar_wait(bar, 0, status, kStatusTimeoutSmemFull));
+  if (!landed) {
+    // status recorded; give the copies in flight one more bounded wait before exiting
+    if (threadIdx.x == 0) mbar_wait(bar, 0, nullptr, kStatusTimeoutDrain);
+    return;
+  }
+  const int n4 = (V + 3) >> 2;
+  const float4* x4 = reinterpret_cast<const float4*>(xs);
+  float m = -INFINITY;
+  for (int i = threadIdx.x; i < n4; i += kCeSmemThreads) {
+    const float4 v = x4[i];
+    const int j = 4 * i;
+    m = fmaxf(m, v.x);
+    if (j + 1 < V) m = fmaxf(m, v.y);
+    if (j + 2 < V) m = fmaxf(m, v.z);
+    if (j + 3 < V) m = fmaxf(m, v.w);
+  }
+  const float M = block_reduce(m, red, true);
+  float s = 0.f;
+  float4* e4 = reinterpret_cast<float4*>(xs);
+  for (int i = threadIdx.x; i < n4; i += kCeSmemThreads) {
+    float4 v = x4[i];
+    const int j = 4 * i;
+    v.x = expf(v.x - M);
+    v.y = (j + 1 < V) ? expf(v.y - M) : 0.f;
+    v.z = (j + 2 < V) ? expf(v.z - M) : 0.f;
+    v.w = (j + 3 < V) ? expf(v.w - M) : 0.f;
+    s += (v.x + v.y) + (v.z + v.w);
+    e4[i] = v;
+  }
+  const float S = block_reduce(s, red, false);
+  const float lse = M + logf(S);
+  const int64_t tgt = targets[row];
+  if (threadIdx.x == 0) loss_rows[row] = lse - x[tgt];
+  if (dlogits == nullptr) return;
+  const float inv = 1.0f / S;
+  __nv_bfloat16* g = dlogits + static_cast<size_t>(row) * ldg;
+  for (int i = threadIdx.x; i < n4; i += kCeSmemThreads) {
+    const float4 e = e4[i];
+    const int j = 4 * i;
+    float p[4] = {e.x * inv, e.y * inv, e.z * inv, e.w * inv};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) p[k] = (p[k] - ((j + k) == tgt ? 1.0f : 0.0f)) * grad_scale;
+    uint2 w;
+    w.x = pack_bf16x2(p[0], (j + 1 < V) ? p[1] : 0.f);
+    w.y = pack_bf16x2((j + 2 < V) ? p[2] : 0.f, (j + 3 < V) ? p[3] : 0.f);
+    *reinterpret_cast<uint2*>(g + j) = w;
+  }
+  for (int j = 4 * n4 + threadIdx.x; j < ldg; j += kCeSmemThreads) g[j] = __float2bfloat16_rn(0.f);
+}
+
 __global__ void __launch_bounds__(1024) mean_kernel(const float* __restrict__ x, int n,
                                                     float* __restrict__ out) {
   __shared__ float red[32];
@@ -88,8 +194,33 @@ __global__ void __launch_bounds__(1024) mean_kernel(const float* __restrict__ x,
 
 int cross_entropy(const CeArgs& a, cudaStream_t stream) {
   if (a.T <= 0 || a.V <= 0 || a.ldl < a.V || (a.dlogits && a.ldg < a.V)) return 1;
-  ce_kernel<<<a.T, kCeThreads, 0, stream>>>(a.logits, a.ldl, a.targets, a.V, a.loss_rows,
-                                            a.dlogits, a.ldg, a.grad_scale);
+  // the shared-memory path copies ceil(V / 4) float4 per row: in bounds when
+  // the row pitch covers them; the gradient rows take 8-byte stores
+  const int n4 = (a.V + 3) / 4;
+  const int row_bytes = n4 * 16;
+  const bool smem_ok = row_bytes <= kCeSmemMaxBytes && a.ldl >= 4 * n4 && (a.ldl % 4) == 0 &&
+                       (reinterpret_cast<uintptr_t>(a.logits) & 15) == 0 &&
+                       (a.dlogits == nullptr ||
+                        (a.ldg >= 4 * n4 && (a.ldg % 4) == 0 &&
+                         (reinterpret_cast<uintptr_t>(a.dlogits) & 7) == 0));
+  if (smem_ok) {
+    const int smem = row_bytes + 16;
+    static bool attr[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr[dev & 63]) {
+      if (cudaFuncSetAttribute(ce_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               kCeSmemMaxBytes + 16) != cudaSuccess)
+        return 2;
+      attr[dev & 63] = true;
+    }
+    ce_smem_kernel<<<a.T, kCeSmemThreads, smem, stream>>>(a.logits, a.ldl, a.targets, a.V,
+                                                          a.loss_rows, a.dlogits, a.ldg,
+                                                          a.grad_scale, row_bytes, a.status);
+  } else {
+    ce_kernel<<<a.T, kCeThreads, 0, stream>>>(a.logits, a.ldl, a.targets, a.V, a.loss_rows,
+                                              a.dlogits, a.ldg, a.grad_scale);
+  }
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
 

@@ -49,15 +49,21 @@ struct EpiTraits {
   static constexpr int kOutBytes = kTma ? 2 * 16384 : 0;  // two staging buffers
 };
 
+// Tile widths: 256 (the default), 192 (an output 5120 wide splits into 27
+// tiles of 192 per 128 rows, so a 2048-row GEMM fills 3 waves of 148 SMs at 97%
+// instead of 72% with 256-wide tiles) and 128.
 template <int BN, int EPI>
 struct GemmCfg {
   static constexpr int A_BYTES = kBM * kBK * 2;
   static constexpr int B_BYTES = BN * kBK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (BN == 256) ? 4 : 6;
   static constexpr int OUT_BYTES = EpiTraits<EPI>::kOutBytes;
+  static constexpr int STAGES =
+      (BN == 256) ? 4 : (BN == 192) ? (EpiTraits<EPI>::kTma ? 4 : 5) : 6;
   static constexpr int SMEM = STAGES * STAGE_BYTES + OUT_BYTES + 1024 /*align*/ + 256 /*barriers*/;
-  static constexpr int TMEM_COLS = 2 * BN;
+  // two accumulators of BN columns; the allocation is a power of two
+  static constexpr int TMEM_COLS = (BN == 192) ? 512 : 2 * BN;
+  static_assert(SMEM <= 232448, "shared memory over the 227 KB per-CTA limit");
 };
 
 constexpr int kTileQueue = 4;  // depth of the producer -> MMA/epilogue tile-id ring
@@ -86,6 +92,62 @@ __device__ __forceinline__ float resid_at(const GemmEpilogue& ep, int row, int c
                  static_cast<size_t>(row) * ep.ldr + col);
 }
 
+// Load 32 consecutive bf16 values of one row as fp32; vectorised (4 x 16 B)
+// when the whole chunk is in range and 16-byte aligned.
+__device__ __forceinline__ void load_bf16_32(const __nv_bfloat16* src, float* f, int valid) {
+  if (valid >= 32 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+    const uint4* s4 = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint4 w = __ldg(s4 + j);
+      const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        f[8 * j + 2 * h] = __uint_as_float(u[h] << 16);
+        f[8 * j + 2 * h + 1] = __uint_as_float(u[h] & 0xffff0000u);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) f[i] = (i < valid) ? ld_bf16(src + i) : 0.f;
+  }
+}
+
+// Residual values at (row, col0 .. col0 + 31) as fp32 (bf16, or e4m3 with its
+// 1x128 block scale; a 32-column chunk never straddles a scale block).
+__device__ __forceinline__ void resid_32(const GemmEpilogue& ep, int row, int col0, float* f,
+                                         int valid) {
+  if (ep.resid_fp8) {
+    const uint8_t* src =
+        reinterpret_cast<const uint8_t*>(ep.resid) + static_cast<size_t>(row) * ep.ldr + col0;
+    const float s = ep.resid_scale[static_cast<size_t>(row) * ep.ld_resid_scale + (col0 >> 7)];
+    if (valid >= 32 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+      const uint4* s4 = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const uint4 w = __ldg(s4 + j);
+        const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+#pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            __nv_fp8_e4m3 q;
+            q.__x = static_cast<__nv_fp8_storage_t>((u[h] >> (8 * b)) & 0xffu);
+            f[16 * j + 4 * h + b] = static_cast<float>(q) * s;
+          }
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) f[i] = (i < valid) ? resid_at(ep, row, col0 + i) : 0.f;
+    }
+    return;
+  }
+  load_bf16_32(reinterpret_cast<const __nv_bfloat16*>(ep.resid) + static_cast<size_t>(row) * ep.ldr +
+                   col0,
+               f, valid);
+}
+
 // Store 32 consecutive bf16 values of one row; vectorised when the whole chunk
 // is in range and 16-byte aligned.
 __device__ __forceinline__ void store_bf16_32(__nv_bfloat16* dst, const float* f, int valid) {
@@ -107,10 +169,110 @@ __device__ __forceinline__ void store_bf16_32(__nv_bfloat16* dst, const float* f
   }
 }
 
+// Where the epilogue reads a tile's fp32 accumulator: TMEM, or, for the CTA
+// that finishes a K-split tail tile, the sum of the splits' partials in split
+// order (p0 + p1 + ... in that order whichever CTA finishes, so the result is
+// bitwise the same run to run).
+struct AccSrc {
+  uint32_t taddr;   // this warp's TMEM lane quarter of the accumulator
+  const float* ws;  // the tile's first partial ([kBM][BN] fp32), or nullptr
+  int ns;           // number of partials
+  int row;          // this thread's row of the tile
+};
+
+template <int BN>
+__device__ __forceinline__ void acc_ld32(const AccSrc& a, int c, float* f) {
+  if (a.ws == nullptr) {
+    uint32_t v[32];
+    tmem_ld32(a.taddr + c, v);
+    tmem_wait_ld();
+#pragma unroll
+    for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(v[i]);
+    return;
+  }
+  const float4* p = reinterpret_cast<const float4*>(a.ws + static_cast<size_t>(a.row) * BN + c);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float4 x = __ldcg(p + j);
+    f[4 * j] = x.x;
+    f[4 * j + 1] = x.y;
+    f[4 * j + 2] = x.z;
+    f[4 * j + 3] = x.w;
+  }
+#pragma unroll 1
+  for (int k = 1; k < a.ns; ++k) {
+    p += kBM * BN / 4;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 x = __ldcg(p + j);
+      f[4 * j] += x.x;
+      f[4 * j + 1] += x.y;
+      f[4 * j + 2] += x.z;
+      f[4 * j + 3] += x.w;
+    }
+  }
+}
+
+// A K-split tail unit's partial: this thread's accumulator row -> slot[row][*].
+template <int BN>
+__device__ __forceinline__ void write_partial(uint32_t taddr, float* slot, int row) {
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 32) {
+    uint32_t v[32];
+    tmem_ld32(taddr + c, v);
+    tmem_wait_ld();
+    float4* d = reinterpret_cast<float4*>(slot + static_cast<size_t>(row) * BN + c);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      __stcg(d + j, make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                                __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3])));
+  }
+}
+
+// Warm L2 with what the epilogue of a tile will read from global memory (the
+// fp32 gradient it folds into; the residual / pre-activation rows), issued
+// when the producer starts the tile, about one tile before the epilogue runs,
+// so the read-modify-write does not wait on DRAM latency chunk by chunk.
+template <int EPI, int BN>
+__device__ __forceinline__ void prefetch_epilogue_inputs(const GemmEpilogue& ep,
+                                                         const CUtensorMap* tmC, int mb, int nb,
+                                                         int M, int N) {
+  const int m0 = mb * kBM, n0 = nb * BN;
+  if constexpr (EPI == kEpiAccF32) {
+    if (ep.beta != 0.f)
+      for (int j = 0; j < BN; j += 32) tma_prefetch_l2_2d(tmC, n0 + j, m0);
+  } else if constexpr (EPI == kEpiResid || EPI == kEpiResidQ8 || EPI == kEpiDGelu) {
+    const void* base = (EPI == kEpiDGelu) ? ep.aux : ep.resid;
+    if (base == nullptr) return;
+    const int esize = (EPI != kEpiDGelu && ep.resid_fp8) ? 1 : 2;
+    const int ld = (EPI == kEpiDGelu) ? ep.ldaux : ep.ldr;
+    const uint32_t bytes = static_cast<uint32_t>(min(BN, N - n0) * esize) & ~15u;
+    if (bytes == 0) return;
+    const int rows = min(kBM, M - m0);
+    for (int r = 0; r < rows; ++r) {
+      const uint8_t* p = reinterpret_cast<const uint8_t*>(base) +
+                         (static_cast<size_t>(m0 + r) * ld + n0) * esize;
+      if ((reinterpret_cast<uintptr_t>(p) & 15) == 0) bulk_prefetch_l2(p, bytes);
+    }
+  }
+}
+
+// Work units: tiles [0, full) whole, then each tail tile in `ns` K-splits.
+struct Unit {
+  int tile, split, ns, kb0, kb1;
+};
+
+__device__ __forceinline__ Unit decode_unit(int u, int full, int ns, int kblocks) {
+  if (u < full) return {u, 0, 1, 0, kblocks};
+  const int v = u - full;
+  const int sp = v % ns;
+  return {full + v / ns, sp, ns, sp * kblocks / ns, (sp + 1) * kblocks / ns};
+}
+
 // Register epilogues (everything but the TMA-staged kinds). `taddr` is this
 // warp's TMEM lane quarter of the accumulator; `gm` this thread's row.
 template <int EPI, int BN>
-__device__ __forceinline__ void epilogue_tile_regs(uint32_t taddr, int gm, int nbase, int M, int N,
+__device__ __forceinline__ void epilogue_tile_regs(const AccSrc& acc, int gm, int nbase, int M, int N,
                                                    const GemmEpilogue& ep) {
   const bool row_ok = gm < M;
   if constexpr (EPI == kEpiResidQ8) {
@@ -123,15 +285,16 @@ __device__ __forceinline__ void epilogue_tile_regs(uint32_t taddr, int gm, int n
       float amax = 0.f;
 #pragma unroll 1
       for (int j = 0; j < 4; ++j) {
-        uint32_t v[32];
-        tmem_ld32(taddr + c + 32 * j, v);
-        tmem_wait_ld();
+        float v[32];
+        acc_ld32<BN>(acc, c + 32 * j, v);
         if (row_ok && n0 < N) {
+          float r[32];
+          resid_32(ep, gm, n0 + 32 * j, r, 32);
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const int n = n0 + 32 * j + i;
             const float b = ep.bias ? ep.bias[n] : 0.f;
-            amax = fmaxf(amax, fabsf(resid_at(ep, gm, n) + (__uint_as_float(v[i]) + b)));
+            amax = fmaxf(amax, fabsf(r[i] + (v[i] + b)));
           }
         }
       }
@@ -139,10 +302,11 @@ __device__ __forceinline__ void epilogue_tile_regs(uint32_t taddr, int gm, int n
       const float inv = 1.0f / scale;  // exact: scale is a power of two
 #pragma unroll 1
       for (int j = 0; j < 4; ++j) {
-        uint32_t v[32];
-        tmem_ld32(taddr + c + 32 * j, v);
-        tmem_wait_ld();
+        float v[32];
+        acc_ld32<BN>(acc, c + 32 * j, v);
         if (row_ok && n0 < N) {
+          float r[32];
+          resid_32(ep, gm, n0 + 32 * j, r, 32);
           uint32_t w[8];
 #pragma unroll
           for (int h = 0; h < 8; ++h) {
@@ -152,7 +316,7 @@ __device__ __forceinline__ void epilogue_tile_regs(uint32_t taddr, int gm, int n
               const int i = 4 * h + e;
               const int n = n0 + 32 * j + i;
               const float b = ep.bias ? ep.bias[n] : 0.f;
-              y[e] = (resid_at(ep, gm, n) + (__uint_as_float(v[i]) + b)) * inv;
+              y[e] = (r[i] + (v[i] + b)) * inv;
             }
             const __nv_fp8x2_storage_t lo =
                 __nv_cvt_float2_to_fp8x2(make_float2(y[0], y[1]), __NV_SATFINITE, __NV_E4M3);
@@ -171,15 +335,11 @@ __device__ __forceinline__ void epilogue_tile_regs(uint32_t taddr, int gm, int n
   } else {
 #pragma unroll 1
     for (int c = 0; c < BN; c += 32) {
-      uint32_t v[32];
-      tmem_ld32(taddr + c, v);
-      tmem_wait_ld();
+      float f[32];
+      acc_ld32<BN>(acc, c, f);
       const int n0 = nbase + c;
       if (!row_ok || n0 >= N) continue;
       const int valid = min(32, N - n0);
-      float f[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(v[i]);
       if constexpr (EPI == kEpiAccF32Peer) {
         // ZeRO-1 reduce-scatter from the epilogue: this replica's final partial
         // (its earlier microbatches, already folded in `out`, plus this tile)
@@ -224,15 +384,17 @@ __device__ __forceinline__ void epilogue_tile_regs(uint32_t taddr, int gm, int n
 #pragma unroll
         for (int i = 0; i < 32; ++i) f[i] = gelu_erf(f[i]);
       } else if constexpr (EPI == kEpiDGelu) {
-        const __nv_bfloat16* aux = reinterpret_cast<const __nv_bfloat16*>(ep.aux) +
-                                   static_cast<size_t>(gm) * ep.ldaux + n0;
+        float u[32];
+        load_bf16_32(reinterpret_cast<const __nv_bfloat16*>(ep.aux) +
+                         static_cast<size_t>(gm) * ep.ldaux + n0,
+                     u, valid);
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (i < valid) f[i] = f[i] * gelu_erf_grad(ld_bf16(aux + i));
+        for (int i = 0; i < 32; ++i) f[i] = f[i] * gelu_erf_grad(u[i]);
       } else if constexpr (EPI == kEpiResid) {
+        float r[32];
+        resid_32(ep, gm, n0, r, valid);
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (i < valid) f[i] = resid_at(ep, gm, n0 + i) + f[i];
+        for (int i = 0; i < 32; ++i) f[i] = r[i] + f[i];
       }
       __nv_bfloat16* dst =
           reinterpret_cast<__nv_bfloat16*>(ep.out) + static_cast<size_t>(gm) * ep.ldo + n0;
@@ -248,7 +410,7 @@ __device__ __forceinline__ void epilogue_tile_regs(uint32_t taddr, int gm, int n
 // tracks the bulk groups. Each output element receives exactly one store or
 // add per launch, so the fold stays deterministic.
 template <int EPI, int BN>
-__device__ __forceinline__ void epilogue_tile_tma(uint32_t taddr, int row, int m0, int nbase, int N,
+__device__ __forceinline__ void epilogue_tile_tma(const AccSrc& acc, int row, int m0, int nbase, int N,
                                                   const GemmEpilogue& ep, const CUtensorMap* tmC,
                                                   uint8_t* out_smem, bool leader, int& chunk) {
   constexpr int CW = (EPI == kEpiBf16) ? 64 : 32;
@@ -257,13 +419,7 @@ __device__ __forceinline__ void epilogue_tile_tma(uint32_t taddr, int row, int m
   for (int c = 0; c < BN; c += CW) {
     float f[CW];
 #pragma unroll
-    for (int j = 0; j < CW / 32; ++j) {
-      uint32_t v[32];
-      tmem_ld32(taddr + c + 32 * j, v);
-      tmem_wait_ld();
-#pragma unroll
-      for (int i = 0; i < 32; ++i) f[32 * j + i] = __uint_as_float(v[i]);
-    }
+    for (int j = 0; j < CW / 32; ++j) acc_ld32<BN>(acc, c + 32 * j, f + 32 * j);
     const int n0 = nbase + c;
     if (EPI != kEpiAccF32 && ep.bias != nullptr) {
 #pragma unroll
@@ -307,7 +463,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmC, const GemmEpilogue ep, int M,
-                        int N, int K, int* status, int* sched) {
+                        int N, int K, int* status, int* sched, int nfull, int ns, float* ws) {
   using Cfg = GemmCfg<BN, EPI>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -323,6 +479,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tq_empty = tq_full + kTileQueue;
   int* tile_ring = reinterpret_cast<int*>(tq_empty + kTileQueue);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tile_ring + kTileQueue);
+  int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -359,6 +516,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int num_n = (N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
   const int kblocks = (K + kBK - 1) / kBK;
+  // Units: tiles [0, nfull) whole, the other tiles each as `ns` K-splits (the
+  // tail of the last wave spread over all SMs; see decode_unit).
+  const int num_units = nfull + (num_tiles - nfull) * ns;
+  int* tail_cnt = sched + 2;
 
   // Tiles are claimed dynamically from sched[0]; the claimed id travels to the
   // MMA and epilogue roles through a small ring guarded by mbarriers; -1 ends.
@@ -374,7 +535,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int k = 0; ok; ++k) {
         int t = atomicAdd(&sched[0], 1);
-        if (t >= num_tiles) t = -1;
+        if (t >= num_units) t = -1;
         const int q = k % kTileQueue;
         if (!mbar_wait(&tq_empty[q], ((k / kTileQueue) & 1) ^ 1, status, kStatusTimeoutSmemEmpty)) {
           ok = false;
@@ -383,9 +544,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         tile_ring[q] = t;
         mbar_arrive(&tq_full[q]);
         if (t < 0) break;
+        const Unit un = decode_unit(t, nfull, ns, kblocks);
         int mb, nb;
-        tile_coords(t, num_m, num_n, mb, nb);
-        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+        tile_coords(un.tile, num_m, num_n, mb, nb);
+        if (un.split == 0) prefetch_epilogue_inputs<EPI, BN>(ep, &tmC, mb, nb, M, N);
+        for (int kb = un.kb0; kb < un.kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, status, kStatusTimeoutSmemEmpty)) {
@@ -432,7 +595,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&tempty[b], (use & 1) ^ 1, status, kStatusTimeoutTmemEmpty)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * BN);
-        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+        const Unit un = decode_unit(t, nfull, ns, kblocks);
+        for (int kb = un.kb0; kb < un.kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(&full[s], ph, status, kStatusTimeoutSmemFull)) {
@@ -448,7 +612,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                      : sdesc_sw128(a_addr + kk * 32, 16, 1024);
             const uint64_t bd = B_MN ? sdesc_sw128(b_addr + kk * 2048, 8192, 1024)
                                      : sdesc_sw128(b_addr + kk * 32, 16, 1024);
-            umma_f16(d_tmem, ad, bd, IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
+            umma_f16(d_tmem, ad, bd, IDESC, (kb > un.kb0 || kk > 0) ? 1u : 0u);
           }
           umma_commit(&empty[s]);
         }
@@ -468,20 +632,47 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&tq_empty[k % kTileQueue]);
       if (t < 0) break;
+      const Unit un = decode_unit(t, nfull, ns, kblocks);
       int mb, nb;
-      tile_coords(t, num_m, num_n, mb, nb);
+      tile_coords(un.tile, num_m, num_n, mb, nb);
       const int b = k & 1;
       const uint32_t use = static_cast<uint32_t>(k >> 1);
       if (!mbar_wait(&tfull[b], use & 1, status, kStatusTimeoutTmemFull)) break;
       tc_fence_after();
       const uint32_t taddr =
           tmem_base + static_cast<uint32_t>(b * BN) + (static_cast<uint32_t>(q * 32) << 16);
+      AccSrc acc{taddr, nullptr, 1, row};
+      if (un.ns > 1) {
+        // K-split tail unit: publish the partial; the CTA whose split lands
+        // last sums all of them in split order and runs the epilogue.
+        const int tail = un.tile - nfull;
+        float* tile_ws = ws + static_cast<size_t>(tail) * un.ns * kBM * BN;
+        write_partial<BN>(taddr, tile_ws + static_cast<size_t>(un.split) * kBM * BN, row);
+        __threadfence();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[b]);
+        named_bar_sync(2, 128);
+        if (warp == 2 && lane == 0) {
+          const int prev = atomicAdd(&tail_cnt[tail], 1);
+          const bool last = prev == un.ns - 1;
+          if (last) tail_cnt[tail] = 0;  // every split has arrived: ready for the next launch
+          __threadfence();
+          *reinterpret_cast<volatile int*>(last_flag) = last ? 1 : 0;
+        }
+        named_bar_sync(2, 128);
+        const bool last = *reinterpret_cast<volatile int*>(last_flag) != 0;
+        named_bar_sync(2, 128);  // the flag is read before the next unit rewrites it
+        if (!last) continue;
+        acc = AccSrc{0u, tile_ws, un.ns, row};
+      }
       if constexpr (EpiTraits<EPI>::kTma) {
-        epilogue_tile_tma<EPI, BN>(taddr, row, mb * kBM, nb * BN, N, ep, &tmC, out_smem, leader,
+        epilogue_tile_tma<EPI, BN>(acc, row, mb * kBM, nb * BN, N, ep, &tmC, out_smem, leader,
                                    chunk);
       } else {
-        epilogue_tile_regs<EPI, BN>(taddr, mb * kBM + row, nb * BN, M, N, ep);
+        epilogue_tile_regs<EPI, BN>(acc, mb * kBM + row, nb * BN, M, N, ep);
       }
+      if (un.ns > 1) continue;  // TMEM was released above
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[b]);
@@ -558,27 +749,70 @@ int num_sms_cached() {
   return sms[dev];
 }
 
-// Tile-scheduler counters: two ints per (device, stream), zeroed once; each
-// launch leaves them zeroed for the next launch on the same stream.
+// Per (device, stream) state, zeroed once; each launch leaves it zeroed for
+// the next launch on the same stream (launches on one stream are ordered):
+// [0] next unit, [1] CTAs done, [2 ..] arrivals per K-split tail tile. Plus a
+// lazily allocated workspace for the tail tiles' fp32 partials.
 constexpr int kSchedSlots = 256;
-int* sched_counters(cudaStream_t stream) {
+constexpr int kSchedInts = 256;      // >= 2 + the most tail tiles (one per SM)
+constexpr int kMaxTailUnits = 160;   // >= SMs: tail units fill at most one wave
+struct StreamState {
+  int* counters;
+  float* ws;  // kMaxTailUnits x [kBM][256] fp32, or nullptr
+};
+
+StreamState stream_state(cudaStream_t stream, bool want_ws) {
   static std::mutex mu;
   static int* base[64] = {nullptr};
   static cudaStream_t owner[64][kSchedSlots];
+  static float* wsp[64][kSchedSlots] = {{nullptr}};
   static int used[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return nullptr;
+  if (dev < 0 || dev >= 64) return {nullptr, nullptr};
   std::lock_guard<std::mutex> lock(mu);
   if (base[dev] == nullptr) {
-    if (cudaMalloc(&base[dev], kSchedSlots * 2 * sizeof(int)) != cudaSuccess) return nullptr;
-    if (cudaMemset(base[dev], 0, kSchedSlots * 2 * sizeof(int)) != cudaSuccess) return nullptr;
+    const size_t bytes = static_cast<size_t>(kSchedSlots) * kSchedInts * sizeof(int);
+    if (cudaMalloc(&base[dev], bytes) != cudaSuccess) return {nullptr, nullptr};
+    if (cudaMemset(base[dev], 0, bytes) != cudaSuccess) return {nullptr, nullptr};
   }
-  for (int i = 0; i < used[dev]; ++i)
-    if (owner[dev][i] == stream) return base[dev] + 2 * i;
-  if (used[dev] >= kSchedSlots) return nullptr;
-  owner[dev][used[dev]] = stream;
-  return base[dev] + 2 * (used[dev]++);
+  int i = 0;
+  while (i < used[dev] && owner[dev][i] != stream) ++i;
+  if (i == used[dev]) {
+    if (used[dev] >= kSchedSlots) return {nullptr, nullptr};
+    owner[dev][used[dev]++] = stream;
+  }
+  if (want_ws && wsp[dev][i] == nullptr) {
+    const size_t bytes = static_cast<size_t>(kMaxTailUnits) * kBM * 256 * sizeof(float);
+    if (cudaMalloc(&wsp[dev][i], bytes) != cudaSuccess) {
+      cudaGetLastError();  // clear: the launch runs without K-splits
+      wsp[dev][i] = nullptr;
+    }
+  }
+  return {base[dev] + static_cast<size_t>(i) * kSchedInts, wsp[dev][i]};
+}
+
+// K-split of a grid that fills less than one wave: the `tiles` tiles split
+// along K into ns = sms / tiles parts (each at least kMinSplitKb k-blocks), so
+// the launch uses ns times as many SMs. Returns ns (1: no split) and the number
+// of whole tiles in `full`.
+//
+// Only single partial waves split. Splitting the last wave of a multi-wave
+// grid measured slower on B200 (qkv projection 0.254 vs 0.237 ms, logits GEMM
+// 0.823 vs 0.761 ms): the dynamic tile counter already balances the CTAs to
+// within one tile, and a split tile ends with the CTA that claimed its last
+// split, which is one of the CTAs that finished their whole tiles last.
+constexpr int kMinSplitKb = 8;
+int split_plan(long tiles, int sms, int kblocks, int* full) {
+  *full = static_cast<int>(tiles);
+  if (tiles >= sms / 2) return 1;
+  const long r = tiles;
+  int ns = static_cast<int>(sms / r);
+  ns = std::min(ns, kblocks / kMinSplitKb);
+  ns = std::min(ns, 16);
+  if (ns < 2 || r * ns > kMaxTailUnits) return 1;
+  *full = static_cast<int>(tiles - r);
+  return ns;
 }
 
 // EWB_TRACE=1 prints each launch step to stderr (flushed), to localise host faults.
@@ -599,7 +833,7 @@ bool trace_on() {
   } while (0)
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
-int launch_cfg(const GemmArgs& g, cudaStream_t stream, int* sched) {
+int launch_cfg(const GemmArgs& g, cudaStream_t stream, int* sched, float* ws) {
   using Cfg = GemmCfg<BN, EPI>;
   EWB_TRACE("[gemm] BN=%d a_mn=%d b_mn=%d epi=%d M=%d N=%d K=%d lda=%d ldb=%d ldo=%d smem=%d\n",
             BN, (int)A_MN, (int)B_MN, EPI, g.M, g.N, g.K, g.lda, g.ldb, g.ep.ldo, Cfg::SMEM);
@@ -627,65 +861,84 @@ int launch_cfg(const GemmArgs& g, cudaStream_t stream, int* sched) {
     mc = ma;  // unused by register epilogues
   }
   if (!ok_a || !ok_b || !ok_c) return kGemmErrTensorMap;
-  const int tiles = ((g.M + kBM - 1) / kBM) * ((g.N + BN - 1) / BN);
-  const int grid = std::max(1, std::min(tiles, num_sms_cached()));
-  kern<<<grid, kThreads, Cfg::SMEM, stream>>>(ma, mbm, mc, g.ep, g.M, g.N, g.K, g.status, sched);
+  const int sms = num_sms_cached();
+  const long tiles = static_cast<long>((g.M + kBM - 1) / kBM) * ((g.N + BN - 1) / BN);
+  int full = static_cast<int>(tiles);
+  const int ns = (ws != nullptr && g.split) ? split_plan(tiles, sms, (g.K + kBK - 1) / kBK, &full) : 1;
+  const long units = full + (tiles - full) * ns;
+  const int grid = static_cast<int>(std::max(1L, std::min(units, static_cast<long>(sms))));
+  kern<<<grid, kThreads, Cfg::SMEM, stream>>>(ma, mbm, mc, g.ep, g.M, g.N, g.K, g.status, sched,
+                                              full, ns, ws);
   const cudaError_t err = cudaGetLastError();
-  EWB_TRACE("[gemm] launched grid=%d: %s\n", grid, cudaGetErrorString(err));
+  EWB_TRACE("[gemm] launched grid=%d ns=%d full=%d: %s\n", grid, ns, full, cudaGetErrorString(err));
   return err == cudaSuccess ? kGemmOk : kGemmErrLaunch;
 }
 
 template <int BN>
-int dispatch_bn(const GemmArgs& g, cudaStream_t s, int* sc) {
+int dispatch_bn(const GemmArgs& g, cudaStream_t s, int* sc, float* ws) {
   const int e = g.ep.kind;
   if (!g.a_mn && !g.b_mn) {
     switch (e) {
-      case kEpiBf16: return launch_cfg<BN, false, false, kEpiBf16>(g, s, sc);
-      case kEpiGelu: return launch_cfg<BN, false, false, kEpiGelu>(g, s, sc);
-      case kEpiResid: return launch_cfg<BN, false, false, kEpiResid>(g, s, sc);
-      case kEpiResidQ8: return launch_cfg<BN, false, false, kEpiResidQ8>(g, s, sc);
-      case kEpiF32: return launch_cfg<BN, false, false, kEpiF32>(g, s, sc);
-      case kEpiAccF32: return launch_cfg<BN, false, false, kEpiAccF32>(g, s, sc);
+      case kEpiBf16: return launch_cfg<BN, false, false, kEpiBf16>(g, s, sc, ws);
+      case kEpiGelu: return launch_cfg<BN, false, false, kEpiGelu>(g, s, sc, ws);
+      case kEpiResid: return launch_cfg<BN, false, false, kEpiResid>(g, s, sc, ws);
+      case kEpiResidQ8: return launch_cfg<BN, false, false, kEpiResidQ8>(g, s, sc, ws);
+      case kEpiF32: return launch_cfg<BN, false, false, kEpiF32>(g, s, sc, ws);
+      case kEpiAccF32: return launch_cfg<BN, false, false, kEpiAccF32>(g, s, sc, ws);
       default: break;
     }
   } else if (!g.a_mn && g.b_mn) {
     switch (e) {
-      case kEpiBf16: return launch_cfg<BN, false, true, kEpiBf16>(g, s, sc);
-      case kEpiDGelu: return launch_cfg<BN, false, true, kEpiDGelu>(g, s, sc);
-      case kEpiAccF32: return launch_cfg<BN, false, true, kEpiAccF32>(g, s, sc);
-      case kEpiF32: return launch_cfg<BN, false, true, kEpiF32>(g, s, sc);
+      case kEpiBf16: return launch_cfg<BN, false, true, kEpiBf16>(g, s, sc, ws);
+      case kEpiDGelu: return launch_cfg<BN, false, true, kEpiDGelu>(g, s, sc, ws);
+      case kEpiAccF32: return launch_cfg<BN, false, true, kEpiAccF32>(g, s, sc, ws);
+      case kEpiF32: return launch_cfg<BN, false, true, kEpiF32>(g, s, sc, ws);
       default: break;
     }
   } else if (g.a_mn && g.b_mn) {
     switch (e) {
-      case kEpiAccF32: return launch_cfg<BN, true, true, kEpiAccF32>(g, s, sc);
-      case kEpiAccF32Peer: return launch_cfg<BN, true, true, kEpiAccF32Peer>(g, s, sc);
-      case kEpiBf16: return launch_cfg<BN, true, true, kEpiBf16>(g, s, sc);
-      case kEpiF32: return launch_cfg<BN, true, true, kEpiF32>(g, s, sc);
+      case kEpiAccF32: return launch_cfg<BN, true, true, kEpiAccF32>(g, s, sc, ws);
+      case kEpiAccF32Peer: return launch_cfg<BN, true, true, kEpiAccF32Peer>(g, s, sc, ws);
+      case kEpiBf16: return launch_cfg<BN, true, true, kEpiBf16>(g, s, sc, ws);
+      case kEpiF32: return launch_cfg<BN, true, true, kEpiF32>(g, s, sc, ws);
       default: break;
     }
   }
   return kGemmErrUnsupported;
 }
 
-// Fraction of the last wave of a persistent grid that has work.
-double wave_efficiency(long tiles, int sms) {
-  const long waves = (tiles + sms - 1) / sms;
-  return static_cast<double>(tiles) / static_cast<double>(waves * sms);
-}
-
 }  // namespace
 
-int gemm_pick_bn(int M, int N) {
+int gemm_pick_bn(int M, int N, int K, bool split) {
+  const int kblocks = (K + kBK - 1) / kBK;
+  // Modelled time of a launch = whole waves x (time of one tile) / (the tile
+  // width's tensor rate). A 128x128 tile streams as many operand bytes per FLOP
+  // as the shared-memory port can feed (measured ~0.6 of the 128x256 tile's
+  // rate on B200); a 128x192 tile needs 83% of the port (rate taken as 0.92).
+  // The wave term is what picks 192 for the 5120-wide outputs of a 2048-row
+  // microbatch (3 full waves instead of 2.16).
   const int sms = num_sms_cached();
-  const long t256 = static_cast<long>((M + kBM - 1) / kBM) * ((N + 255) / 256);
-  const long t128 = static_cast<long>((M + kBM - 1) / kBM) * ((N + 127) / 128);
-  // A 128x128 tile streams as many operand bytes per FLOP as the shared-memory
-  // port can feed (measured ~0.6 of the 128x256 tile's rate on B200), so it
-  // only wins when the 128x256 grid leaves most of the last wave idle.
-  const double e256 = wave_efficiency(t256, sms) * (N >= 256 ? 1.0 : 0.5);
-  const double e128 = wave_efficiency(t128, sms) * 0.6;
-  return e128 > e256 ? 128 : 256;
+  const long mt = (M + kBM - 1) / kBM;
+  const int widths[3] = {256, 192, 128};
+  const double rate[3] = {1.0, 0.82, 0.6};
+  int best = 256;
+  double best_t = 0.0;
+  for (int i = 0; i < 3; ++i) {
+    const int bn = widths[i];
+    const long tiles = mt * ((N + bn - 1) / bn);
+    int full = 0;
+    const int ns = split ? split_plan(tiles, sms, kblocks, &full) : 1;
+    // waves of whole tiles, plus 1/ns of one for a K-split last wave
+    const double waves = ns > 1 ? static_cast<double>(full / sms) + 1.0 / ns + 0.05
+                                : static_cast<double>((tiles + sms - 1) / sms);
+    // columns computed per SM, including the padding of a partial last tile
+    const double t = waves * bn / rate[i];
+    if (i == 0 || t < best_t * 0.97) {
+      best = bn;
+      best_t = t;
+    }
+  }
+  return best;
 }
 
 int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
@@ -699,11 +952,13 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
       ((g.ep.kind == kEpiF32 || g.ep.kind == kEpiAccF32) && g.ep.ldo % 4))
     return kGemmErrAlign;
   int bn = g.bn;
-  if (g.ep.kind == kEpiResidQ8) bn = 256;
-  if (bn != 128 && bn != 256) bn = gemm_pick_bn(g.M, g.N);
-  int* sc = g.sched != nullptr ? g.sched : sched_counters(stream);
-  if (sc == nullptr) return kGemmErrLaunch;
-  return bn == 128 ? dispatch_bn<128>(g, stream, sc) : dispatch_bn<256>(g, stream, sc);
+  if (bn != 128 && bn != 192 && bn != 256) bn = gemm_pick_bn(g.M, g.N, g.K, g.split != 0);
+  if (g.ep.kind == kEpiResidQ8) bn = 256;  // a tile covers whole 128-column scale blocks
+  const StreamState st = stream_state(stream, g.split != 0);
+  if (st.counters == nullptr) return kGemmErrLaunch;
+  if (bn == 128) return dispatch_bn<128>(g, stream, st.counters, st.ws);
+  if (bn == 192) return dispatch_bn<192>(g, stream, st.counters, st.ws);
+  return dispatch_bn<256>(g, stream, st.counters, st.ws);
 }
 
 // Exported for the other tcgen05 kernels (attention): a bf16 2D tensor map

@@ -66,14 +66,14 @@ struct GemmArgs {
   int ldb;
   bool b_mn;  // false: B stored [N][ldb]; true: [K][ldb]
   int M, N, K;
-  int bn;  // 128 / 256, anything else = pick by wave efficiency
+  int bn;  // 128 / 192 / 256, anything else = pick by the wave model
   GemmEpilogue ep;
   int* status;  // device status word (may be null)
-  int* sched;  // two zeroed ints for the tile scheduler (null: per-stream pool)
+  int split;    // nonzero: the last wave's tiles may be split along K
 };
 
 int gemm_launch(const GemmArgs& args, cudaStream_t stream);
-int gemm_pick_bn(int M, int N);
+int gemm_pick_bn(int M, int N, int K, bool split);
 
 // bf16 2D tensor map with 128-byte swizzle (inner = contiguous extent in
 // elements, ld = row pitch in elements); false if the driver refuses it.

@@ -98,6 +98,7 @@ struct CeArgs {
   __nv_bfloat16* dlogits;
   int ldg;
   float grad_scale;
+  int* status;  // device status word for the bounded waits (may be null)
 };
 int cross_entropy(const CeArgs& a, cudaStream_t stream);
 // out[0] = sum(x[0..n)) / n, fixed-order tree (deterministic).

@@ -26,7 +26,7 @@ from elysium_wan_b200.models.params import plan_layout
 
 def stage_layout(cfg, span):
     specs = [s for e in range(*span) for s in entry_specs(cfg, e)]
-    _, index, nt, numel = plan_layout(specs)
+    _, index, nt, numel, _ = plan_layout(specs)
     return index, nt, numel
 
 

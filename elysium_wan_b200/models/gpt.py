@@ -255,16 +255,26 @@ class WExecutor:
         self.cuda = torch.device(device).type == "cuda" and enabled
         self.stream = torch.cuda.Stream(device=device) if self.cuda else None
 
-    def run(self, tasks: list):
+    def run(self, tasks: list, timing: bool = False):
+        """Enqueue `tasks`; with `timing`, returns (start, end) CUDA events
+        recorded around them on the side stream (the W work's device time)."""
         if not self.cuda:
             for t in tasks:
                 t.run()
-            return
+            return None
         self.stream.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(self.stream):
+            e0 = e1 = None
+            if timing:
+                e0 = torch.cuda.Event(enable_timing=True)
+                e0.record()
             for t in tasks:
                 t.record_stream(self.stream)
                 t.run()
+            if timing:
+                e1 = torch.cuda.Event(enable_timing=True)
+                e1.record()
+        return (e0, e1) if timing else None
 
     def join(self):
         if self.cuda:

@@ -41,15 +41,14 @@ class _Handler(socketserver.BaseRequestHandler):
                     return
                 if op == _PING:
                     s.sendall(_PING)
-                elif op == _UP:  # the client streams for n seconds; count and ack
+                elif op == _UP:  # the client streams until it closes its side; count and ack
                     (secs,) = struct.unpack("<d", _exact(s, 8))
-                    end = time.monotonic() + secs
                     got = 0
-                    s.settimeout(secs + 5)
-                    while time.monotonic() < end:
+                    s.settimeout(secs + 10)
+                    while True:
                         b = s.recv(_CHUNK)
                         if not b:
-                            return
+                            break
                         got += len(b)
                     s.sendall(struct.pack("<Q", got))
                     return

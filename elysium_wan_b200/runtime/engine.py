@@ -89,7 +89,11 @@ class StageEngine:
     def _run_w(self, tasks: list, mb: int):
         if self.zero1 is not None and hasattr(self.zero1, "mark"):
             self.zero1.mark(tasks, mb)
-        self.wexec.run(tasks)
+        # On the side stream the W op's device time is bracketed there (the
+        # compute stream only enqueues it), so busy counts the W GEMMs too.
+        ev = self.wexec.run(tasks, timing=self.timing)
+        if ev is not None:
+            self.events.append(("W", mb, ev[0], ev[1]))
 
     @property
     def first(self) -> bool:
@@ -240,7 +244,7 @@ class StageEngine:
                 self._run_w(wq.pop(mb), mb)
             if self.nvtx:
                 torch.cuda.nvtx.range_pop()
-            if ev:
+            if ev and not (op == "W" and self.wexec.cuda):
                 e1 = torch.cuda.Event(enable_timing=True)
                 e1.record()
                 self.events.append((op, mb, e0, e1))
@@ -337,7 +341,8 @@ class StageEngine:
         if not self.events:
             return []
         base = self.events[0][2]
-        return [(op, mb, base.elapsed_time(a), a.elapsed_time(b)) for op, mb, a, b in self.events]
+        out = [(op, mb, base.elapsed_time(a), a.elapsed_time(b)) for op, mb, a, b in self.events]
+        return sorted(out, key=lambda x: x[2])
 
     # ----------------------------------------------------------------- state
     def state_dict(self) -> dict:

@@ -4,7 +4,8 @@ Compute capture targets (one kernel, one to three launches, a few GB).
     python -m elysium_wan_b200.utils.profcase --op gemm_fwd [--iters 3]
 
 Ops: gemm_fwd (qkv projection), gemm_dx (fc1 input gradient), gemm_dw (fc1
-weight gradient fold), gemm_q8 (fc2 with the fp8 boundary epilogue),
+weight gradient fold), gemm_resid (out projection + residual), gemm_fc2 (fc2 +
+residual), gemm_dgelu (fc2 input gradient x GELU'), gemm_q8 (fc2 with the fp8 boundary epilogue),
 attn_fwd, attn_bwd, ln_fwd, ln_bwd, ce, adamw, embed_bwd, head_gemm (the 50257-way
 logits GEMM, fp32 out), head_fwd (LN + logits + CE of the head entry), head_bwd
 (its forward, backward and W).
@@ -21,6 +22,7 @@ import torch
 from elysium_wan_b200 import ops
 
 T, D, F, H, V = 2048, 5120, 20480, 40, 50257
+BN = 0  # GEMM tile width (0: the launcher's choice)
 
 
 def _bf(*shape, scale=1.0):
@@ -32,11 +34,28 @@ def build(op):
     if op == "gemm_fwd":
         x, w, b = _bf(T, D), _bf(3 * D, D, scale=0.02), torch.zeros(3 * D, device="cuda")
         out = torch.empty(T, 3 * D, dtype=torch.bfloat16, device="cuda")
-        return (lambda: ops.gemm(x, w, out, ops.EPI_BF16, bias=b)), 2.0 * T * 3 * D * D, None
+        return (lambda: ops.gemm(x, w, out, ops.EPI_BF16, bias=b, bn=BN)), 2.0 * T * 3 * D * D, None
     if op == "gemm_dx":
         dy, w = _bf(T, F), _bf(F, D, scale=0.02)
         out = torch.empty(T, D, dtype=torch.bfloat16, device="cuda")
-        return (lambda: ops.gemm(dy, w, out, ops.EPI_BF16, b_mn=True)), 2.0 * T * F * D, None
+        return (lambda: ops.gemm(dy, w, out, ops.EPI_BF16, b_mn=True, bn=BN)), 2.0 * T * F * D, None
+    if op == "gemm_resid":  # attention out projection + residual (N = 5120)
+        x, w, r = _bf(T, D), _bf(D, D, scale=0.02), _bf(T, D)
+        b = torch.zeros(D, device="cuda")
+        out = torch.empty(T, D, dtype=torch.bfloat16, device="cuda")
+        return (lambda: ops.gemm(x, w, out, ops.EPI_RESID, bias=b, resid=r, bn=BN)), \
+            2.0 * T * D * D, None
+    if op == "gemm_fc2":  # fc2 forward + residual (N = 5120, K = 20480)
+        g, w, r = _bf(T, F), _bf(D, F, scale=0.02), _bf(T, D)
+        b = torch.zeros(D, device="cuda")
+        out = torch.empty(T, D, dtype=torch.bfloat16, device="cuda")
+        return (lambda: ops.gemm(g, w, out, ops.EPI_RESID, bias=b, resid=r, bn=BN)), \
+            2.0 * T * F * D, None
+    if op == "gemm_dgelu":  # fc2 input gradient with the GELU derivative (N = 20480)
+        dy, w, u = _bf(T, D), _bf(D, F, scale=0.02), _bf(T, F)
+        out = torch.empty(T, F, dtype=torch.bfloat16, device="cuda")
+        return (lambda: ops.gemm(dy, w, out, ops.EPI_DGELU, b_mn=True, aux=u, bn=BN)), \
+            2.0 * T * F * D, None
     if op == "gemm_dw":
         dy, x = _bf(T, F), _bf(T, D)
         g = torch.zeros(F, D, device="cuda")
@@ -111,7 +130,13 @@ def main(argv=None):
     ap.add_argument("--op", required=True)
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--time", action="store_true", help="also print CUDA-event timing (no profiler)")
+    ap.add_argument("--bn", type=int, default=0, help="GEMM tile width 128/192/256 (0: auto)")
+    ap.add_argument("--no-split", action="store_true", help="no K-split of a GEMM's last wave")
     a = ap.parse_args(argv)
+    global BN
+    BN = a.bn
+    if a.no_split:
+        ops.ext().set_gemm_split(False)
     torch.manual_seed(0)
     fn, flops, nbytes = build(a.op)
     fn()
@@ -129,6 +154,10 @@ def main(argv=None):
             ts.append(e0.elapsed_time(e1))
         ms = sorted(ts)[len(ts) // 2]
         out = {"op": a.op, "ms": round(ms, 4)}
+        if a.bn:
+            out["bn"] = a.bn
+        if a.no_split:
+            out["split"] = False
         if flops:
             out["tflops"] = round(flops / ms / 1e9, 1)
         if nbytes:

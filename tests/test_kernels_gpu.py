@@ -31,7 +31,7 @@ GEMM_SHAPES = [(256, 512, 256), (128, 256, 64), (384, 640, 1024), (200, 264, 200
 
 
 @pytest.mark.parametrize("M,N,K", GEMM_SHAPES)
-@pytest.mark.parametrize("bn", [128, 256])
+@pytest.mark.parametrize("bn", [128, 192, 256])
 def test_gemm_forward_layouts(cuda, M, N, K, bn):
     torch.manual_seed(0)
     x = bf(M, K, dev=cuda)
@@ -88,6 +88,90 @@ def test_gemm_epilogues(cuda):
     uf = uu.float()
     gp = 0.5 * (1 + torch.erf(uf / math.sqrt(2))) + uf * torch.exp(-0.5 * uf * uf) / math.sqrt(2 * math.pi)
     assert rel_err(dg, (dy.float() @ wn.float()) * gp) < 8e-3
+
+
+@pytest.mark.parametrize("N", [5120, 520])
+@pytest.mark.parametrize("bn", [192, 256])
+def test_gemm_register_epilogues_widths(cuda, N, bn):
+    """Residual (bf16 and e4m3), GELU and GELU' epilogues at every tile width,
+    on the 5120-wide output that picks 192 and on a ragged width."""
+    torch.manual_seed(5)
+    M, K = 384, 256
+    x = bf(M, K, dev=cuda)
+    w = bf(N, K, dev=cuda, scale=0.05)
+    b = torch.randn(N, device=cuda)
+    acc = x.float() @ w.float().t() + b
+    r = bf(M, N, dev=cuda)
+    y = torch.empty(M, N, dtype=torch.bfloat16, device=cuda)
+    ops.gemm(x, w, y, ops.EPI_RESID, bias=b, resid=r, bn=bn)
+    assert rel_err(y, acc + r.float()) < 8e-3
+    if N % 128 == 0:
+        q, s = ops.quant_e4m3(r)
+        ops.gemm(x, w, y, ops.EPI_RESID, bias=b, resid=q, resid_scale=s, bn=bn)
+        assert rel_err(y, acc + ops.dequant_e4m3(q, s, torch.float32)) < 8e-3
+    g = torch.empty(M, N, dtype=torch.bfloat16, device=cuda)
+    u = torch.empty(M, N, dtype=torch.bfloat16, device=cuda)
+    ops.gemm(x, w, g, ops.EPI_GELU, bias=b, aux=u, bn=bn)
+    assert rel_err(u, acc) < 8e-3
+    assert rel_err(g, F.gelu(u.float())) < 8e-3
+    wt = w.t().contiguous()  # [K, N]: dX = dY W layout
+    uf = u.float()
+    gp = 0.5 * (1 + torch.erf(uf / math.sqrt(2))) + uf * torch.exp(-0.5 * uf * uf) / math.sqrt(2 * math.pi)
+    dg = torch.empty(M, N, dtype=torch.bfloat16, device=cuda)
+    ops.gemm(x, wt, dg, ops.EPI_DGELU, b_mn=True, aux=u, bn=bn)
+    assert rel_err(dg, (x.float() @ w.float().t()) * gp) < 8e-3
+
+
+def test_gemm_pick_bn(cuda):
+    ext = ops.ext()
+    # the 5120-wide outputs of a 2048-row microbatch take 192-wide tiles (3
+    # full waves instead of 2.16); the wider ones keep 256
+    assert ext.gemm_pick_bn(2048, 5120, 5120) == 192
+    assert ext.gemm_pick_bn(2048, 15360, 5120) == 256
+    assert ext.gemm_pick_bn(2048, 20480, 5120) == 256
+    # a single partial wave with a long K splits: 256-wide tiles then win
+    assert ext.gemm_pick_bn(256, 1024, 8192) == 256
+
+
+@pytest.mark.parametrize("bn", [192, 256])
+def test_gemm_k_split_tail(cuda, bn):
+    """16 tiles on 148 SMs: every tile is split 8 ways along K and the last
+    arriving split sums the partials in split order. Results match fp32 and
+    are bitwise reproducible; the fold and fp8 epilogues run on the sum."""
+    ext = ops.ext()
+    torch.manual_seed(6)
+    M, N, K = 512, 1024, 4096
+    x = bf(M, K, dev=cuda)
+    w = bf(N, K, dev=cuda, scale=0.05)
+    ref = x.float() @ w.float().t()
+    outs = []
+    for _ in range(2):
+        o = torch.empty(M, N, device=cuda)
+        ops.gemm(x, w, o, ops.EPI_F32, bn=bn)
+        outs.append(o)
+    assert rel_err(outs[0], ref) < 1e-5
+    assert torch.equal(outs[0], outs[1])
+    ext.set_gemm_split(False)
+    try:
+        o1 = torch.empty(M, N, device=cuda)
+        ops.gemm(x, w, o1, ops.EPI_F32, bn=bn)
+    finally:
+        ext.set_gemm_split(True)
+    assert rel_err(o1, ref) < 1e-5
+    # fold: dW layout (A, B MN-major), beta 0 then 1
+    xt, wt = x.t().contiguous(), w.t().contiguous()
+    g = torch.empty(M, N, device=cuda)
+    ops.gemm(xt, wt, g, ops.EPI_ACC_F32, a_mn=True, b_mn=True, beta=0.0, bn=bn)
+    ops.gemm(xt, wt, g, ops.EPI_ACC_F32, a_mn=True, b_mn=True, beta=1.0, bn=bn)
+    assert rel_err(g, 2 * ref) < 1e-5
+    # residual + bf16 out, and the fp8 quantising epilogue (always 256 wide)
+    b = torch.randn(N, device=cuda)
+    r = bf(M, N, dev=cuda)
+    y = torch.empty(M, N, dtype=torch.bfloat16, device=cuda)
+    ops.gemm(x, w, y, ops.EPI_RESID, bias=b, resid=r, bn=bn)
+    assert rel_err(y, ref + b + r.float()) < 8e-3
+    q, s = ops.linear_fwd(x, w, b, epi="resid_q8", resid=r)
+    assert rel_err(ops.dequant_e4m3(q, s, torch.float32), ref + b + r.float()) < 6e-2
 
 
 def test_gemm_weight_grad_fold_and_determinism(cuda):
