@@ -155,22 +155,6 @@ __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const 
       : "memory");
 }
 
-// L2 prefetch of one box of a tensor map (local memory; nothing lands in
-// shared memory and nothing signals completion).
-__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int x, int y) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(x), "r"(y)
-               : "memory");
-}
-
-// L2 prefetch of `bytes` (a multiple of 16) from a 16-byte aligned address.
-__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)),
-               "r"(bytes)
-               : "memory");
-}
-
 __device__ __forceinline__ void bulk_commit() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }

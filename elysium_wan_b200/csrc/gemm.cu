@@ -229,34 +229,6 @@ __device__ __forceinline__ void write_partial(uint32_t taddr, float* slot, int r
   }
 }
 
-// Warm L2 with what the epilogue of a tile will read from global memory (the
-// fp32 gradient it folds into; the residual / pre-activation rows), issued
-// when the producer starts the tile, about one tile before the epilogue runs,
-// so the read-modify-write does not wait on DRAM latency chunk by chunk.
-template <int EPI, int BN>
-__device__ __forceinline__ void prefetch_epilogue_inputs(const GemmEpilogue& ep,
-                                                         const CUtensorMap* tmC, int mb, int nb,
-                                                         int M, int N) {
-  const int m0 = mb * kBM, n0 = nb * BN;
-  if constexpr (EPI == kEpiAccF32) {
-    if (ep.beta != 0.f)
-      for (int j = 0; j < BN; j += 32) tma_prefetch_l2_2d(tmC, n0 + j, m0);
-  } else if constexpr (EPI == kEpiResid || EPI == kEpiResidQ8 || EPI == kEpiDGelu) {
-    const void* base = (EPI == kEpiDGelu) ? ep.aux : ep.resid;
-    if (base == nullptr) return;
-    const int esize = (EPI != kEpiDGelu && ep.resid_fp8) ? 1 : 2;
-    const int ld = (EPI == kEpiDGelu) ? ep.ldaux : ep.ldr;
-    const uint32_t bytes = static_cast<uint32_t>(min(BN, N - n0) * esize) & ~15u;
-    if (bytes == 0) return;
-    const int rows = min(kBM, M - m0);
-    for (int r = 0; r < rows; ++r) {
-      const uint8_t* p = reinterpret_cast<const uint8_t*>(base) +
-                         (static_cast<size_t>(m0 + r) * ld + n0) * esize;
-      if ((reinterpret_cast<uintptr_t>(p) & 15) == 0) bulk_prefetch_l2(p, bytes);
-    }
-  }
-}
-
 // Work units: tiles [0, full) whole, then each tail tile in `ns` K-splits.
 struct Unit {
   int tile, split, ns, kb0, kb1;
@@ -547,7 +519,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const Unit un = decode_unit(t, nfull, ns, kblocks);
         int mb, nb;
         tile_coords(un.tile, num_m, num_n, mb, nb);
-        if (un.split == 0) prefetch_epilogue_inputs<EPI, BN>(ep, &tmC, mb, nb, M, N);
         for (int kb = un.kb0; kb < un.kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;

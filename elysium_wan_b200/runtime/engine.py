@@ -25,6 +25,7 @@ from elysium_wan_b200.models.data import make_batch
 from elysium_wan_b200.models.gpt import Act, StageModel, WExecutor
 from elysium_wan_b200.parallel.p2p import dbg
 from elysium_wan_b200.runtime import optim
+from elysium_wan_b200.runtime.telemetry import parse_sim_slow
 
 
 class StageEngine:
@@ -61,6 +62,7 @@ class StageEngine:
         self.telemetry: list = []
         self._host_x = None
 
+        self.sim_slow = parse_sim_slow().get(stage, 1.0)
         side = os.environ.get("EWB_W_STREAM", "1") == "1"
         self.wexec = WExecutor(self.device, enabled=side)
         self.phase: dict = {}
@@ -198,6 +200,8 @@ class StageEngine:
                 if ev:
                     e0 = torch.cuda.Event(enable_timing=True)
                     e0.record()
+                else:
+                    e0 = time.perf_counter()
                 if self.nvtx:
                     torch.cuda.nvtx.range_push(f"{op}{mb}")
 
@@ -248,6 +252,14 @@ class StageEngine:
                 e1 = torch.cuda.Event(enable_timing=True)
                 e1.record()
                 self.events.append((op, mb, e0, e1))
+            elif not ev and e0 is not None:
+                # host device: the op ran synchronously; the timing-only seam
+                # stretches it by the stage's factor (never what it computes)
+                t1 = time.perf_counter()
+                if self.sim_slow > 1.0:
+                    time.sleep((self.sim_slow - 1.0) * (t1 - e0))
+                    t1 = time.perf_counter()
+                self.events.append((op, mb, e0, t1))
         dbg(f"stage {self.stage} ops done; waiting {len(sends)} sends")
         self.wexec.join()
         if ev:
@@ -341,7 +353,10 @@ class StageEngine:
         if not self.events:
             return []
         base = self.events[0][2]
-        out = [(op, mb, base.elapsed_time(a), a.elapsed_time(b)) for op, mb, a, b in self.events]
+        if isinstance(base, float):  # host clock (CPU stages)
+            out = [(op, mb, (a - base) * 1e3, (b - a) * 1e3) for op, mb, a, b in self.events]
+        else:
+            out = [(op, mb, base.elapsed_time(a), a.elapsed_time(b)) for op, mb, a, b in self.events]
         return sorted(out, key=lambda x: x[2])
 
     # ----------------------------------------------------------------- state

@@ -1,0 +1,124 @@
+"""Rebalance from telemetry: re-cut a running job's chain from the stage costs it
+measures, and spot a slot that has become slow.
+
+Reference behaviour: src/wantrain/coordinator/coordinator.py (`_maybe_rebalance`
+:2194, `_maybe_recut` :2299, `_watch_slow` :2406, `refined_partition` :3046,
+`recut_refusal` :3068, `stage_compute_ms` :3085, `slow_slots` :3091) and
+src/wantrain/scheduler/zero_bubble.py (`profiles_from_telemetry` :1008).
+
+Inputs are the per-step WT_TELEM summaries a stage prints
+(runtime/telemetry.summarize_step: {"ops": {"F"|"B"|"W": {"n", "med_ms"}}, ...}),
+collected per slot by the coordinator into a window of recent steps.
+
+- `profiles_from_telemetry(spec, windows)`: per stage and peer, the median over
+  the window of each op's per-step median, in seconds.
+- `refined_partition(spec, profiles, fits, min_gain)`: every stage's measured
+  rate (microbatches per second, summed over its peers) turns the model's
+  per-entry cost into that stage's speed (cost units per second); the exact
+  min-max partition DP (partition.assign_layers) then re-cuts the chain for
+  those speeds. The result is taken only when it shortens the slowest stage's
+  time per microbatch by at least `min_gain`.
+- `recut_pays(...)`: the saving over the remaining steps against the cost of a
+  restart.
+- `slow_slots(hist, base, ratio, runs)`: slots whose last `runs` compute
+  samples all exceed `ratio` x their own baseline.
+"""
+
+from __future__ import annotations
+
+import math
+import statistics
+
+from elysium_wan_b200.scheduler.partition import assign_layers, layer_costs
+
+OPS = ("F", "B", "W")
+
+
+def stage_compute_ms(summary: dict) -> float:
+    """A slot's compute per microbatch in one summary: F + B + W medians (ms)."""
+    ops = summary.get("ops") or {}
+    return float(sum((ops.get(k) or {}).get("med_ms", 0.0) for k in OPS))
+
+
+def profiles_from_telemetry(spec, windows: dict) -> list:
+    """profiles[stage][peer] = {"t_f", "t_b", "t_w"} in seconds. windows:
+    {(stage, peer): [summary, ...]}. A W that runs inside B (no W op of its
+    own in a summary) counts as 0. Raises ValueError naming a slot without F
+    or B samples."""
+    out = []
+    for r in range(spec.stages):
+        row = []
+        for q in range(spec.stage_widths[r]):
+            win = windows.get((r, q)) or []
+            prof = {}
+            for op in OPS:
+                xs = [float(s["ops"][op]["med_ms"]) for s in win
+                      if (s.get("ops") or {}).get(op, {}).get("n", 0) > 0]
+                if not xs:
+                    if op == "W":
+                        prof["t_w"] = 0.0
+                        continue
+                    raise ValueError(f"no {op} sample in the telemetry of slot ({r}, {q})")
+                if not all(math.isfinite(x) and x >= 0 for x in xs):
+                    raise ValueError(f"{op} med_ms of slot ({r}, {q}) must be finite and >= 0")
+                prof["t_" + op.lower()] = statistics.median(xs) / 1e3
+            row.append(prof)
+        out.append(row)
+    return out
+
+
+def stage_rates(profiles: list) -> list:
+    """Microbatches per second of each stage: its peers' rates added."""
+    return [sum(1.0 / max(1e-9, p["t_f"] + p["t_b"] + p["t_w"]) for p in row) for row in profiles]
+
+
+def refined_partition(spec, profiles: list, fits=None, min_gain: float = 0.05):
+    """-> (new partition, slowest stage before, after) in seconds per
+    microbatch, or None when the DP returns the same cut, nothing fits, or the
+    slowest stage shrinks by less than `min_gain`. fits(stage, lo, hi) -> bool."""
+    costs = layer_costs(spec.model)
+    rate = stage_rates(profiles)
+    speed = [sum(costs[a:b]) * r for (a, b), r in zip(spec.partition, rate)]
+    try:
+        new = [list(x) for x in assign_layers(costs, speed, fits)]
+    except ValueError:
+        return None
+    before = max(1.0 / r for r in rate)
+    after = max(sum(costs[a:b]) / s for (a, b), s in zip(new, speed))
+    if new == [list(x) for x in spec.partition] or after > (1.0 - min_gain) * before:
+        return None
+    return new, before, after
+
+
+def recut_pays(before_s: float, after_s: float, microbatches: int, remaining_steps: int,
+               cost_s: float) -> tuple[bool, float]:
+    """(worth it, seconds saved): the slowest stage sets the pipeline's pace, so
+    each remaining step saves (before - after) per microbatch."""
+    saving = (before_s - after_s) * microbatches * max(0, remaining_steps)
+    return saving > cost_s, saving
+
+
+def recut_refusal(spec) -> str | None:
+    """Why a running job cannot be re-cut, or None. The waves are converted
+    through the logical form (fault_tolerance/logical.py), which handles widths
+    and ZeRO-1 / pieces; it does not move a tied table between stages or MoE
+    routing state."""
+    if spec.stages < 2:
+        return "one stage"
+    if getattr(spec.model, "tie_embeddings", False):
+        return "a tied embedding"
+    if getattr(spec.model, "moe_experts", 0):
+        return "an MoE model"
+    return None
+
+
+def slow_slots(hist: dict, base: dict, ratio: float = 1.3, runs: int = 3) -> list:
+    """[(slot, latest / baseline)] for the slots whose last `runs` samples all
+    exceed `ratio` x their baseline. hist: slot -> [ms, ...]; base: slot -> ms."""
+    out = []
+    for slot, xs in hist.items():
+        b = base.get(slot)
+        tail = xs[len(xs) - runs:] if len(xs) >= runs else []
+        if b and tail and all(x > ratio * b for x in tail):
+            out.append((slot, round(xs[-1] / b, 3)))
+    return out
