@@ -44,7 +44,11 @@ def cmd_coordinator(a) -> int:
                             no_probe=a.no_probe, no_fit_check=a.no_fit_check, group_by=a.group_by,
                             allow_shared_hosts=a.allow_shared_hosts, any_region=a.any_region,
                             zb_mem_mode=a.zb_mem_mode, replacement_match=a.replacement_match,
-                            max_heals=a.max_heals, keep_workers=a.keep_workers)
+                            max_heals=a.max_heals, keep_workers=a.keep_workers,
+                            recut=not a.no_recut, recut_min_gain=a.recut_min_gain,
+                            recut_cost_s=a.recut_cost_s, max_replans=a.max_replans,
+                            watch_slow=not a.no_watch_slow, slow_ratio=a.slow_ratio,
+                            slow_runs=a.slow_runs)
     if a.wan_link:
         for item in a.wan_link:
             key, _, prof = item.partition("=")
@@ -229,6 +233,13 @@ def build_parser() -> argparse.ArgumentParser:
     c.add_argument("--max-heals", type=int, default=3)
     c.add_argument("--keep-workers", action="store_true")
     c.add_argument("--wan-link", action="append", help="regionA|regionB=60mbps:60ms")
+    c.add_argument("--no-recut", action="store_true", help="never re-cut from telemetry")
+    c.add_argument("--recut-min-gain", type=float, default=0.05)
+    c.add_argument("--recut-cost-s", type=float, default=60.0)
+    c.add_argument("--max-replans", type=int, default=2)
+    c.add_argument("--no-watch-slow", action="store_true", help="do not act on slow slots")
+    c.add_argument("--slow-ratio", type=float, default=1.3)
+    c.add_argument("--slow-runs", type=int, default=3)
     c.set_defaults(fn=cmd_coordinator)
 
     w = sub.add_parser("worker", help="worker agent: supervises one stage process")

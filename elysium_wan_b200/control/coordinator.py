@@ -22,17 +22,29 @@ and its message kinds:
     newest wave every slot holds (shipped CKPT files, sha256-checked), RESTORE
     that slot's wave to the spare, relaunch with resume=true.
   * stalled: restart in place from the common wave.
+  * rebalance (`_maybe_recut`, reference :2194-2400): each stage's WT_TELEM
+    summaries fill a per-slot window; at every new common wave the measured
+    F + B + W per microbatch re-cut the chain (scheduler/rebalance.py) when
+    the slowest stage shrinks by `recut_min_gain` and the saving over the
+    remaining steps beats `recut_cost_s`: ABORT, convert the common wave to
+    the new cut through the logical form (fault_tolerance/logical.py) under a
+    new tag, RESTORE every slot, relaunch.
+  * slow slot (`_watch_slow`, reference :2406): a slot whose compute per
+    microbatch stays above `slow_ratio` x its own baseline for `slow_runs`
+    summaries is healed onto a spare, or, with none, re-cut away from.
   * complete: RESULT losses of the last stage -> runs/<id>/losses.json and
     result.json.
 """
 
 from __future__ import annotations
 
+import collections
 import copy
 import hashlib
 import json
 import os
 import socket
+import statistics
 import threading
 import time
 import uuid
@@ -67,6 +79,16 @@ class CoordinatorConfig:
     wan_links: dict = field(default_factory=dict)  # {"regionA|regionB": {bw_mbps, latency_ms}}
     job_timeout_s: float = 3600.0
     min_workers: int = 0  # wait for at least this many (slots + spares) before placing
+    # rebalance from telemetry
+    recut: bool = True
+    recut_min_gain: float = 0.05      # the slowest stage must shrink by this fraction
+    recut_cost_s: float = 60.0        # what a re-cut costs (abort, convert, relaunch)
+    max_replans: int = 2
+    replan_min_summaries: int = 4     # per slot, in the current attempt
+    telem_window: int = 8
+    watch_slow: bool = True
+    slow_ratio: float = 1.3
+    slow_runs: int = 3
 
 
 @dataclass
@@ -128,6 +150,14 @@ class Coordinator:
         self._pending_ckpt: dict = {}
         self.link_memory = None
         self.link_results: dict = {}
+        # rebalance state (per run)
+        self.telem: dict = {}          # slot -> deque of this attempt's summaries
+        self.replans: list = []
+        self.replan_checked = -1
+        self.slot_base: dict = {}
+        self.slot_hist: dict = {}
+        self.slow_noted = None
+        self._next: tuple | None = None  # (kind, payload) decided by the monitor
 
     # ----------------------------------------------------------------- server
     def start(self):
@@ -251,6 +281,9 @@ class Coordinator:
                         self.store.commit_staged(os.path.dirname(rel))
             elif kind == "TELEM_STEP":
                 self.events.append(("telem", nid, hdr.get("telem")))
+                if slot is not None and current and isinstance(hdr.get("telem"), dict):
+                    self.telem.setdefault(
+                        slot, collections.deque(maxlen=self.cfg.telem_window)).append(hdr["telem"])
             elif kind == "LINK_RESULT":
                 self.link_results[(nid, hdr.get("target"))] = {k: v for k, v in hdr.items()
                                                               if k != "kind"}
@@ -369,6 +402,8 @@ class Coordinator:
                       f, indent=1)
         heals = restarts = 0
         resume_step = None
+        self.replans, self.replan_checked = [], -1
+        self.slot_base, self.slot_hist, self.slow_noted = {}, {}, None
         t_start = time.time()
         why = ""
         while True:
@@ -410,6 +445,29 @@ class Coordinator:
                 restarts += 1
                 resume_step = self._resume_point(spec)
                 self.events.append(("restart", None, {"step": resume_step, "why": verdict.why}))
+            elif verdict.kind == "recut":
+                new_spec, note = self._next[1]
+                got = self._apply_recut(spec, new_spec, note, run_dir)
+                if got is None:  # nothing to resume from: continue on the current cut
+                    resume_step = self._resume_point(spec)
+                else:
+                    spec, resume_step = got
+            elif verdict.kind == "slow_heal":
+                slot = verdict.slot
+                with self.lock:
+                    busy = set(self.slot_node.values())
+                    spares = [n for n in self.order if n not in busy and not self.nodes[n].dead
+                              and self.nodes[n].connected]
+                    cands = [self.nodes[n].info for n in spares]
+                old_nid = self.slot_node[slot]
+                rep = find_replacement(self.nodes[old_nid].info, cands, self.cfg.replacement_match)
+                resume_step = self._resume_point(spec)
+                if rep is not None:
+                    heals += 1
+                    self.slot_node[slot] = rep.node_id
+                    self._restore(spec, slot, rep.node_id, resume_step)
+                    self.events.append(("heal", slot, {"from": old_nid, "to": rep.node_id,
+                                                       "step": resume_step, "why": verdict.why}))
             else:
                 why = verdict.why
                 res = RunResult(False, self.run_id, None, self.attempt + 1, heals, restarts, why, run_dir)
@@ -418,9 +476,132 @@ class Coordinator:
         with open(os.path.join(run_dir, "result.json"), "w") as f:
             json.dump({"ok": res.ok, "run_id": res.run_id, "attempts": res.attempts, "heals": res.heals,
                        "restarts": res.restarts, "why": res.why, "losses": res.losses_path,
-                       "events": [list(map(str, e)) for e in self.events if e[0] in ("heal", "restart")]},
+                       "events": [list(map(str, e)) for e in self.events
+                                  if e[0] in ("heal", "restart", "recut")],
+                       "replans": self.replans},
                       f, indent=1)
         return res
+
+    # ------------------------------------------------------------ rebalance
+    def _windows(self) -> dict:
+        with self.lock:
+            return {slot: list(w) for slot, w in self.telem.items()}
+
+    def _maybe_rebalance(self, spec):
+        """Once per new common wave: ("recut", (new spec, note)) when the
+        measured stage costs call for another cut and it pays, else None."""
+        if not self.cfg.recut or os.environ.get("WANTRAIN_RECUT", "on") == "off":
+            return None
+        if len(self.replans) >= self.cfg.max_replans or self.store is None:
+            return None
+        windows = self._windows()
+        slots = spec.slots()
+        # the first summary of an attempt holds its warm-up
+        windows = {s: w[1:] for s, w in windows.items()}
+        if any(len(windows.get(s, ())) < self.cfg.replan_min_summaries for s in slots):
+            return None
+        step = self._resume_point(spec)
+        final = spec.steps
+        if step is None or step <= self.replan_checked or step >= final:
+            return None
+        self.replan_checked = step
+        return self._recut_plan(spec, windows, step, final)
+
+    def _recut_plan(self, spec, windows, step, final, why: str | None = None):
+        from elysium_wan_b200.scheduler import rebalance as rb
+
+        refusal = rb.recut_refusal(spec)
+        if refusal is not None:
+            self.events.append(("recut_refused", None, {"step": step, "why": refusal}))
+            return None
+        try:
+            profiles = rb.profiles_from_telemetry(spec, windows)
+        except ValueError as e:
+            self.events.append(("recut_skipped", None, {"step": step, "why": str(e)}))
+            return None
+        res = rb.refined_partition(spec, profiles, None, self.cfg.recut_min_gain)
+        if res is None:
+            return None
+        new_part, before, after = res
+        cost = float(os.environ.get("WANTRAIN_RECUT_COST_S", self.cfg.recut_cost_s))
+        pays, saving = rb.recut_pays(before, after, spec.microbatches, final - step, cost)
+        note = (f"re-cut {spec.partition} -> {new_part}: slowest stage {before * 1e3:.1f} -> "
+                f"~{after * 1e3:.1f} ms per microbatch, ~{saving:.1f} s saved over {final - step} "
+                f"steps against {cost:.1f} s" + (f" ({why})" if why else ""))
+        self.events.append(("recut_eval", None, {"step": step, "note": note, "pays": pays}))
+        if not pays:
+            return None
+        d = spec.to_dict()
+        cuts = sum(1 for r in self.replans if r.get("recut"))
+        d.update(partition=[list(x) for x in new_part], tag=f"{spec.tag.split('.cut')[0]}.cut{cuts + 1}",
+                 schedule_order=None, mb_owner=None, resume=False, resume_step=None)
+        new = JobSpec.from_dict(d)
+        new.finalize()
+        return "recut", (new, note)
+
+    def _watch_slow(self, spec):
+        """("slow", (slot, why)) for a slot that computes `slow_ratio` x its own
+        baseline per microbatch for `slow_runs` summaries in a row and has a
+        spare to move to; without a spare, a re-cut away from it (or None)."""
+        from elysium_wan_b200.scheduler import rebalance as rb
+
+        if not self.cfg.watch_slow or self.store is None:
+            return None
+        windows = self._windows()
+        for slot, win in windows.items():
+            hist = [rb.stage_compute_ms(x) for x in win[2:]]
+            if len(hist) >= self.cfg.slow_runs and slot not in self.slot_base:
+                self.slot_base[slot] = statistics.median(hist[: self.cfg.slow_runs])
+            if hist:
+                self.slot_hist[slot] = hist
+        slow = rb.slow_slots(self.slot_hist, self.slot_base, self.cfg.slow_ratio, self.cfg.slow_runs)
+        if not slow:
+            return None
+        slot, ratio = max(slow, key=lambda x: x[1])
+        why = f"slot {slot} computes {ratio:.2f}x its baseline per microbatch"
+        step = self._resume_point(spec)
+        if step is None or step >= spec.steps:
+            return None
+        with self.lock:
+            busy = set(self.slot_node.values())
+            spares = [n for n in self.order if n not in busy and not self.nodes[n].dead
+                      and self.nodes[n].connected]
+        if spares and sum(1 for e in self.events if e[0] == "heal") < self.cfg.max_heals:
+            self.slot_base, self.slot_hist, self.slow_noted = {}, {}, None
+            return "slow", (slot, why)
+        if self.slow_noted == (slot, step) or len(self.replans) >= self.cfg.max_replans:
+            return None
+        self.slow_noted = (slot, step)
+        recent = {s: w[-self.cfg.slow_runs:] for s, w in windows.items()}
+        got = self._recut_plan(spec, recent, step, spec.steps, why)
+        if got is not None:
+            self.slot_base, self.slot_hist, self.slow_noted = {}, {}, None
+        return got
+
+    def _apply_recut(self, old: JobSpec, new: JobSpec, note: str, run_dir: str):
+        """Abort, convert the common wave of every slot to `new`'s cut (a new
+        tag, in the coordinator's store), ship each slot its wave. -> (new spec,
+        resume step), or None when no common wave exists."""
+        from elysium_wan_b200.fault_tolerance import logical
+
+        step = self._resume_point(old)  # run_job has aborted every slot
+        if step is None:
+            self.replans.append({"recut": False, "why": "no common wave"})
+            return None
+        root = os.path.join(self.store.root, self.run_id)
+        v_old, v_new = copy.copy(old), copy.copy(new)
+        v_old.out_dir = v_new.out_dir = root
+        logical.convert(v_old, v_new, step)
+        rec = {"step": step, "recut": True, "from": old.partition, "to": new.partition,
+               "tag": new.tag, "note": note}
+        self.replans.append(rec)
+        self.events.append(("recut", None, rec))
+        with open(os.path.join(run_dir, "spec.json"), "w") as f:
+            f.write(new.to_json())
+        for s in new.slots():
+            self._restore(new, s, self.slot_node[s], step)
+        self._final_step = new.steps - 1
+        return new, step
 
     def _resume_point(self, spec) -> int | None:
         view = copy.copy(spec)
@@ -450,6 +631,9 @@ class Coordinator:
         with self.lock:
             self.results = {}
             self.slots = {}
+            self.telem = {}
+            # a slot's baseline belongs to the node that runs it in this attempt
+            self.slot_base, self.slot_hist, self.slow_noted = {}, {}, None
             for s in spec.slots():
                 nid = self.slot_node[s]
                 n = self.nodes[nid]
@@ -462,6 +646,8 @@ class Coordinator:
                 attempt=self.attempt, timeout=self.cfg.stage_timeout_s)
 
     def _monitor(self, spec, t_start):
+        from elysium_wan_b200.fault_tolerance.liveness import Verdict
+
         judge = LivenessJudge(final_step=spec.steps - 1, **self.cfg.liveness)
         while True:
             time.sleep(self.cfg.poll_s)
@@ -476,6 +662,13 @@ class Coordinator:
                     return v
                 if v.kind in ("convict", "stalled", "failed"):
                     return v
+            nxt = self._watch_slow(spec) or self._maybe_rebalance(spec)
+            if nxt is not None:
+                self._next = nxt
+                kind, payload = nxt
+                if kind == "recut":
+                    return Verdict("recut", None, payload[1])
+                return Verdict("slow_heal", payload[0], payload[1])
             if time.time() - t_start > self.cfg.job_timeout_s:
                 from elysium_wan_b200.fault_tolerance.liveness import Verdict
 

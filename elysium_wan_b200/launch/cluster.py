@@ -27,20 +27,23 @@ FAST_FT = dict(heartbeat_timeout_s=4.0, reconnect_grace_s=3.0, stall_floor_s=30.
 class LocalCluster:
     def __init__(self, workdir: str, regions: list, token: str = "demo-token", device: str = "cpu",
                  wan_links: dict | None = None, liveness: dict | None = None, max_heals: int = 3,
-                 stage_timeout_s: float = 30.0):
+                 stage_timeout_s: float = 30.0, coord: dict | None = None,
+                 worker_env: dict | None = None):
         self.workdir = os.path.abspath(workdir)
         os.makedirs(self.workdir, exist_ok=True)
         cfg = CoordinatorConfig(state_dir=os.path.join(self.workdir, "coordinator"), token=token,
                                 wait_workers_s=120.0, liveness=dict(FAST_FT, **(liveness or {})),
                                 wan_links=wan_links or {}, max_heals=max_heals,
                                 stage_timeout_s=stage_timeout_s, poll_s=0.2,
-                                min_workers=len(regions))
+                                min_workers=len(regions), **(coord or {}))
         self.coord = Coordinator("127.0.0.1", 0, cfg).start()
         self.token = token
         self.workers: list = []
         env = dict(os.environ)
         env["PYTHONPATH"] = ROOT + os.pathsep + env.get("PYTHONPATH", "")
         env["WANTRAIN_COORD_TOKEN"] = token
+        # worker_env: extra variables for every worker, or a list with one dict per worker
+        per = worker_env if isinstance(worker_env, list) else [worker_env or {}] * len(regions)
         for i, region in enumerate(regions):
             name = f"w{i}"
             log = open(os.path.join(self.workdir, f"{name}.log"), "w")
@@ -48,7 +51,7 @@ class LocalCluster:
                    f"127.0.0.1:{self.coord.port}", "--coordinator-id", self.coord.id, "--name", name,
                    "--workdir", os.path.join(self.workdir, name), "--device", device, "--region",
                    region, "--no-bench"]
-            p = subprocess.Popen(cmd, stdout=log, stderr=subprocess.STDOUT, env=env,
+            p = subprocess.Popen(cmd, stdout=log, stderr=subprocess.STDOUT, env={**env, **per[i]},
                                  start_new_session=True)
             self.workers.append((name, p, log))
 

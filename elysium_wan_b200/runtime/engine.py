@@ -62,7 +62,7 @@ class StageEngine:
         self.telemetry: list = []
         self._host_x = None
 
-        self.sim_slow = parse_sim_slow().get(stage, 1.0)
+        self.sim_slow = parse_sim_slow().get(stage, (1.0, 0))
         side = os.environ.get("EWB_W_STREAM", "1") == "1"
         self.wexec = WExecutor(self.device, enabled=side)
         self.phase: dict = {}
@@ -256,8 +256,9 @@ class StageEngine:
                 # host device: the op ran synchronously; the timing-only seam
                 # stretches it by the stage's factor (never what it computes)
                 t1 = time.perf_counter()
-                if self.sim_slow > 1.0:
-                    time.sleep((self.sim_slow - 1.0) * (t1 - e0))
+                factor, from_step = self.sim_slow
+                if factor > 1.0 and step >= from_step:
+                    time.sleep((factor - 1.0) * (t1 - e0))
                     t1 = time.perf_counter()
                 self.events.append((op, mb, e0, t1))
         dbg(f"stage {self.stage} ops done; waiting {len(sends)} sends")

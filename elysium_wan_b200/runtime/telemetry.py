@@ -39,10 +39,13 @@ def summarize_step(step, stage, peer, step_ms, op_times, bytes_sent, frames) -> 
 
 
 def parse_sim_slow(value: str | None = None) -> dict:
-    """WANTRAIN_SIM_SLOW="stage:factor,...": a timing-only seam (moves when, never what)."""
+    """WANTRAIN_SIM_SLOW="stage:factor[@from_step],...": a timing-only seam
+    (moves when, never what): the stage's ops take `factor` x their time from
+    `from_step` on (default 0). -> {stage: (factor, from_step)}."""
     value = value if value is not None else os.environ.get("WANTRAIN_SIM_SLOW", "")
     out = {}
     for part in filter(None, value.split(",")):
         k, _, v = part.partition(":")
-        out[int(k)] = float(v)
+        f, _, s = v.partition("@")
+        out[int(k)] = (float(f), int(s) if s else 0)
     return out

@@ -98,3 +98,81 @@ def test_coordinator_probes_pipeline_hops_into_link_memory(tmp_path):
             a.stop.set()
         co.stop()
         _t.sleep(0.2)
+
+
+def test_recut_from_telemetry_matches_oracle(tmp_path):
+    """Stage 1 runs 6x slower (the timing-only seam moves when, never what):
+    at a common wave the coordinator re-cuts the chain toward stage 0 from the
+    measured F/B/W, converts the wave to the new cut under a new tag, relaunches
+    every slot, and the 20 losses still equal the single-device oracle bit for
+    bit."""
+    cfg = make_config("toy", n_layer=6, vocab_size=97, d_model=64, n_head=4, seq_len=16)
+    spec = JobSpec(model=cfg, stages=2, microbatches=2, mb_size=2, steps=10, backend="gloo",
+                   tag="rc", ckpt_every=2)
+    cl = LocalCluster(str(tmp_path / "cl"), ["r0", "r0"],
+                      coord=dict(recut_cost_s=0.0, replan_min_summaries=2, watch_slow=False),
+                      worker_env={"WANTRAIN_SIM_SLOW": "1:6"})
+    try:
+        res = cl.run(Job(spec=spec))
+        replans = list(cl.coord.replans)
+    finally:
+        cl.close()
+    assert res.ok, res.why
+    assert replans and replans[0]["recut"], replans
+    assert replans[0]["to"][0][1] > replans[0]["from"][0][1], replans  # stage 0 took entries
+    ref = JobSpec.from_dict(spec.to_dict())
+    ref.out_dir = str(tmp_path / "oracle")
+    ref.finalize()
+    r = compare(run_baseline(ref, "reference"), res.losses_path)
+    assert r["ok"] and r["compared"] == 20, r
+
+
+def test_rebalance_rules():
+    from elysium_wan_b200.scheduler import rebalance as rb
+
+    cfg = make_config("toy", n_layer=6, vocab_size=97, d_model=64, n_head=4, seq_len=16)
+    spec = JobSpec(model=cfg, stages=2, microbatches=4, mb_size=1).finalize()
+    summ = lambda f, b, w: {"ops": {"F": {"n": 4, "med_ms": f}, "B": {"n": 4, "med_ms": b},  # noqa: E731
+                                    "W": {"n": 4, "med_ms": w}}}
+    even = {(0, 0): [summ(1, 2, 1)] * 3, (1, 0): [summ(1, 2, 1)] * 3}
+    prof = rb.profiles_from_telemetry(spec, even)
+    assert prof[0][0]["t_f"] == pytest.approx(1e-3)
+    # measured equal while the model says stage 1 is lighter: the cut moves toward stage 0
+    # only when that shortens the slowest stage by the gain
+    slow1 = {(0, 0): [summ(1, 2, 1)] * 3, (1, 0): [summ(6, 12, 6)] * 3}
+    new, before, after = rb.refined_partition(spec, rb.profiles_from_telemetry(spec, slow1))
+    assert new[0][1] > spec.partition[0][1] and after < before
+    assert rb.recut_pays(before, after, 4, 10, 0.0)[0]
+    assert not rb.recut_pays(before, after, 4, 0, 0.0)[0]
+    assert rb.stage_compute_ms(summ(1, 2, 3)) == 6
+    hist = {(0, 0): [10, 10, 14, 14, 14], (1, 0): [10, 14, 10, 14, 14]}
+    assert rb.slow_slots(hist, {(0, 0): 10, (1, 0): 10}, 1.3, 3) == [((0, 0), 1.4)]
+    with pytest.raises(ValueError):
+        rb.profiles_from_telemetry(spec, {(0, 0): [], (1, 0): [summ(1, 2, 1)]})
+    tied = make_config("toy", n_layer=2, tie_embeddings=True)
+    assert rb.recut_refusal(JobSpec(model=tied, stages=2).finalize()) == "a tied embedding"
+
+
+def test_slow_slot_moves_to_a_spare(tmp_path):
+    """From step 5 on, stage 1 computes 4x slower (timing-only seam). Its
+    compute per microbatch stays above 1.3x its own baseline for three
+    summaries, so the coordinator moves the slot to the spare and resumes from
+    the common wave; the losses equal the oracle."""
+    cfg = make_config("toy", n_layer=2, vocab_size=97, d_model=64, n_head=4, seq_len=16)
+    spec = JobSpec(model=cfg, stages=2, microbatches=2, mb_size=2, steps=12, backend="gloo",
+                   tag="slow", ckpt_every=2)
+    cl = LocalCluster(str(tmp_path / "cl"), ["r0", "r0", "r0"],
+                      coord=dict(recut=False, slow_runs=3, slow_ratio=1.3),
+                      worker_env={"WANTRAIN_SIM_SLOW": "1:4@5"})
+    try:
+        res = cl.run(Job(spec=spec))
+        heals = [e for e in cl.coord.events if e[0] == "heal"]
+    finally:
+        cl.close()
+    assert res.ok, res.why
+    assert len(heals) == 1 and heals[0][1] == (1, 0) and "baseline" in heals[0][2]["why"], heals
+    ref = JobSpec.from_dict(spec.to_dict())
+    ref.out_dir = str(tmp_path / "oracle")
+    ref.finalize()
+    r = compare(run_baseline(ref, "reference"), res.losses_path)
+    assert r["ok"] and r["compared"] == 24, r
