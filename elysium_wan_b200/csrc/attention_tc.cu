@@ -66,12 +66,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* sfull = bars + 9;   // [2]
   uint64_t* sfree = bars + 11;  // [2]
   uint64_t* pfull = bars + 13;  // [2]
-  uint64_t* ofull = bars + 15;
-  uint64_t* drain = bars + 16;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+  uint64_t* ofull = bars + 15;  // [2]: O += P_i V_i commits to ofull[i & 1]
+  uint64_t* drain = bars + 17;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
 
-  const int qb = gridDim.x - 1 - blockIdx.x;  // longest rows first
-  const int h = blockIdx.y, b = blockIdx.z;
+  // Longest rows first across all heads (blockIdx.x, the fastest launch
+  // dimension, walks the heads): the greedy CTA scheduler then ends within
+  // about one short tile of the ideal instead of one long tile.
+  const int qb = gridDim.y - 1 - blockIdx.y;
+  const int h = blockIdx.x, b = blockIdx.z;
   const int hk = h / (H / Hkv);
   const int dkv = Hkv * kTcHD;
   const int row0 = b * S;
@@ -88,8 +91,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&sfull[i], 1);
       mbar_init(&sfree[i], 4);
       mbar_init(&pfull[i], 4);
+      mbar_init(&ofull[i], 1);
     }
-    mbar_init(ofull, 1);
     mbar_init(drain, 1);
     fence_mbar_init();
     tma_prefetch_desc(&map_qk);
@@ -169,7 +172,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                      sdesc_sw128(v_addr + kb * kChunk + kk * 2048, 8192, 1024), IP,
                      (i > 0 || kb > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&vempty[s]);
-        umma_commit(ofull);
+        umma_commit(&ofull[s]);
         return true;
       };
       for (int j = 0; j < nblk && ok; ++j) {
@@ -239,12 +242,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       float mnew = m;
       if (__any_sync(0xffffffffu, mx > m + kRescale)) mnew = fmaxf(m, mx);
       const float alpha = (m == -INFINITY) ? 0.f : ex2f(m - mnew);
-      // P_j reuses the buffer of P_{j-2}; O is rescaled below: both need
-      // O += P_{j-1} V_{j-1} (and so every earlier MMA) complete.
-      if (j > 0 && !mbar_wait(ofull, (j - 1) & 1, status, kStatusTimeoutTmemFull)) {
+      // P_j reuses the buffer of P_{j-2}: O += P_{j-2} V_{j-2} must be
+      // complete. O += P_{j-1} V_{j-1} may still run while exp2 fills P_j;
+      // only a rescale of O (below) waits for it.
+      if (j > 1 && !mbar_wait(&ofull[s], ((j - 2) >> 1) & 1, status, kStatusTimeoutTmemFull)) {
         ok = false;
         break;
       }
+      const bool rescale = j > 0 && __any_sync(0xffffffffu, alpha != 1.0f);
       tc_fence_after();
       uint8_t* prow = smem + kOffP + s * kTile + r * 128;
       float rs = 0.f;
@@ -263,7 +268,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
       l = l * alpha + rs;
-      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+      if (rescale) {
+        if (!mbar_wait(&ofull[s ^ 1], ((j - 1) >> 1) & 1, status, kStatusTimeoutTmemFull)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
         const uint32_t o_t = tmem + 256 + lanes;
         uint32_t ov[32];
 #pragma unroll
@@ -283,7 +293,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (lane == 0) mbar_arrive(&pfull[s]);
       m = mnew;
     }
-    if (ok && mbar_wait(ofull, (nblk - 1) & 1, status, kStatusTimeoutTmemFull)) {
+    if (ok && mbar_wait(&ofull[(nblk - 1) & 1], ((nblk - 1) >> 1) & 1, status,
+                        kStatusTimeoutTmemFull)) {
       tc_fence_after();
       const float inv = 1.0f / l;
       const int qrow = qb * kTcBlk + r;
@@ -359,8 +370,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* drain = bars + 12;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
 
-  const int kb = blockIdx.x;  // earliest keys (most query blocks) first
-  const int hk = blockIdx.y, bz = blockIdx.z;
+  const int kb = blockIdx.y;  // earliest keys (most query blocks) first, across all kv heads
+  const int hk = blockIdx.x, bz = blockIdx.z;
   const int rep = H / Hkv, dkv = Hkv * kTcHD, ldq = d + 2 * dkv;
   const int row0 = bz * S;
   const int nq = S / 64, i0 = 2 * kb, nqs = nq - i0;
@@ -608,8 +619,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* dpfree = bars + 10;  // dP read
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
 
-  const int qb = gridDim.x - 1 - blockIdx.x;
-  const int h = blockIdx.y, bz = blockIdx.z;
+  const int qb = gridDim.y - 1 - blockIdx.y;  // longest rows first, across all heads
+  const int h = blockIdx.x, bz = blockIdx.z;
   const int hk = h / (H / Hkv);
   const int dkv = Hkv * kTcHD, ldq = d + 2 * dkv;
   const int row0 = bz * S;
@@ -848,7 +859,7 @@ int attention_fwd_tc(const AttnArgs& a, int* status, cudaStream_t stream) {
       return 2;
     attr = true;
   }
-  dim3 grid(a.S / kTcBlk, a.H, a.B);
+  dim3 grid(a.H, a.S / kTcBlk, a.B);
   attn_fwd_tc_kernel<<<grid, kTcThreads, kTcSmem, stream>>>(mqk, mv, a.o, a.lse, a.S, a.H, hkv,
                                                              a.d, a.scale * kLog2eTc, status);
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
@@ -882,9 +893,9 @@ int attention_bwd_tc(const AttnBwdArgs& a, int* status, cudaStream_t stream) {
     attr = true;
   }
   const float sl2 = a.scale * kLog2eTc;
-  attn_bwd_dkdv_tc_kernel<<<dim3(a.S / kTcBlk, hkv, a.B), kTcThreads, kBwSmem, stream>>>(
+  attn_bwd_dkdv_tc_kernel<<<dim3(hkv, a.S / kTcBlk, a.B), kTcThreads, kBwSmem, stream>>>(
       m_kv128, m_q64, m_do64, a.lse, a.Dbuf, a.dqkv, a.S, a.H, hkv, a.d, sl2, a.scale, status);
-  attn_bwd_dq_tc_kernel<<<dim3(a.S / kTcBlk, a.H, a.B), kTcThreads, kDqSmem, stream>>>(
+  attn_bwd_dq_tc_kernel<<<dim3(a.H, a.S / kTcBlk, a.B), kTcThreads, kDqSmem, stream>>>(
       m_q128, m_do128, m_kv64, a.lse, a.Dbuf, a.dqkv, a.S, a.H, hkv, a.d, sl2, a.scale, status);
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
