@@ -214,14 +214,28 @@ __global__ void __launch_bounds__(kLnThreads)
   }
 }
 
-// grad[c] (+)= sum over chunks, in chunk order, of part[chunk][c].
-__global__ void fold_partials_kernel(const float* __restrict__ part, int chunks, int d,
-                                     float* __restrict__ grad, int accumulate) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= d) return;
+// grad[c] (+)= sum over chunks of part[chunk][c] in a fixed tree: a CTA owns
+// 32 columns; warp w sums chunks w, w + 8, w + 16, ... in order (lane = column,
+// 128-byte rows), then the eight warp sums are added in warp order. 8 warps x
+// d / 32 CTAs instead of one serial chain per column over all chunks.
+constexpr int kFoldWarps = 8;
+__global__ void __launch_bounds__(kFoldWarps * 32)
+    fold_partials_kernel(const float* __restrict__ part, int chunks, int d,
+                         float* __restrict__ grad, int accumulate) {
+  __shared__ float red[kFoldWarps][32];
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  const int c = blockIdx.x * 32 + l;
   float s = 0.f;
-  for (int k = 0; k < chunks; ++k) s += part[static_cast<size_t>(k) * d + c];
-  grad[c] = accumulate ? grad[c] + s : s;
+  if (c < d)
+    for (int k = w; k < chunks; k += kFoldWarps) s += part[static_cast<size_t>(k) * d + c];
+  red[w][l] = s;
+  __syncthreads();
+  if (w == 0 && c < d) {
+    float t = red[0][l];
+#pragma unroll
+    for (int i = 1; i < kFoldWarps; ++i) t += red[i][l];
+    grad[c] = accumulate ? grad[c] + t : t;
+  }
 }
 
 }  // namespace
@@ -280,12 +294,12 @@ int layernorm_bwd(const LnBwdArgs& a, cudaStream_t stream) {
   }
 #undef EWB_LN_BWD
   if (cudaGetLastError() != cudaSuccess) return 2;
-  const int tb = 256;
-  fold_partials_kernel<<<(a.d + tb - 1) / tb, tb, 0, stream>>>(a.part_g, chunks, a.d, a.dgamma,
-                                                               a.accumulate);
+  const int fb = (a.d + 31) / 32;
+  fold_partials_kernel<<<fb, kFoldWarps * 32, 0, stream>>>(a.part_g, chunks, a.d, a.dgamma,
+                                                           a.accumulate);
   if (!a.rms)
-    fold_partials_kernel<<<(a.d + tb - 1) / tb, tb, 0, stream>>>(a.part_b, chunks, a.d, a.dbeta,
-                                                                 a.accumulate);
+    fold_partials_kernel<<<fb, kFoldWarps * 32, 0, stream>>>(a.part_b, chunks, a.d, a.dbeta,
+                                                             a.accumulate);
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
 
