@@ -137,6 +137,10 @@ def plan_spec(args, n: int, free_bytes: float | None):
     spec.optimizer = "adamw-host" if host_adam else "adamw"
     budget = cap - resident - (0 if host_adam else 8 * biggest) - slack
     spec.stage_widths = [1] * n
+    # Pipelined stages fold the weight gradients of microbatch pairs with one
+    # GEMM each (the W ops are deferred there anyway); one device runs W inline
+    # in B, where pairing would hold a microbatch's W inputs across the next B.
+    spec.w_pair = n > 1 and not getattr(args, "no_w_pair", False)
     from elysium_wan_b200.scheduler.planner import stage_memory_model
 
     spec.peer_weights = [[1.0]] * n
@@ -280,7 +284,8 @@ def run_ours(args) -> dict | None:
                    "global_batch": spec.microbatches * spec.mb_size, "seq_len": spec.model.seq_len,
                    "parallelism": f"pp{n}", "microbatches": spec.microbatches,
                    "schedule": "zero-bubble", "optimizer": spec.optimizer,
-                   "recompute": spec.recompute, "l2": "working set larger than L2 (no flush)"},
+                   "recompute": spec.recompute, "w_pair": spec.w_pair,
+                   "l2": "working set larger than L2 (no flush)"},
         "clocks": clocks,
         "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": spec.microbatches * 4},
@@ -308,6 +313,8 @@ def main(argv=None):
     # Diagnostics only (profiling on a shallower model of the same width): a
     # line printed with it is marked "diagnostic" and is not the benchmark.
     ap.add_argument("--n-layer", type=int, default=None)
+    ap.add_argument("--no-w-pair", action="store_true",
+                    help="fold every microbatch's weight gradient on its own")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")

@@ -85,7 +85,8 @@ void gemm_impl(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor out,
                c10::optional<at::Tensor> bias, c10::optional<at::Tensor> resid,
                c10::optional<at::Tensor> resid_scale, c10::optional<at::Tensor> aux,
                c10::optional<at::Tensor> scale_out, double beta, int64_t bn,
-               const ewb::PeerScatter* peer);
+               const ewb::PeerScatter* peer, c10::optional<at::Tensor> a2 = c10::nullopt,
+               c10::optional<at::Tensor> b2 = c10::nullopt);
 
 void gemm(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor out, int64_t epi,
           c10::optional<at::Tensor> bias, c10::optional<at::Tensor> resid,
@@ -94,11 +95,21 @@ void gemm(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor out, int6
   gemm_impl(a, a_mn, b, b_mn, out, epi, bias, resid, resid_scale, aux, scale_out, beta, bn, nullptr);
 }
 
+// Weight gradient of two microbatches in one launch (A, B and A2, B2 both
+// MN-major, [K][M] and [K][N]): out (+)= A^T B + A2^T B2, accumulated over
+// K + K2 in TMEM, then one fold into out.
+void gemm_pair(at::Tensor a, at::Tensor b, at::Tensor a2, at::Tensor b2, at::Tensor out,
+               double beta, int64_t bn) {
+  gemm_impl(a, true, b, true, out, ewb::kEpiAccF32, c10::nullopt, c10::nullopt, c10::nullopt,
+            c10::nullopt, c10::nullopt, beta, bn, nullptr, a2, b2);
+}
+
 // dW GEMM whose epilogue scatters (local partial + tile) into the ZeRO-1
 // owners' slots: slots = peer pointers (int64), lo = world+1 flat bounds.
+// Optional a2 / b2: a second microbatch folded by the same launch.
 void gemm_peer_scatter(at::Tensor a, at::Tensor b, at::Tensor out, std::vector<int64_t> slots,
                        std::vector<int64_t> lo, int64_t stride, int64_t flat_off, int64_t rank,
-                       int64_t bn) {
+                       int64_t bn, c10::optional<at::Tensor> a2, c10::optional<at::Tensor> b2) {
   TORCH_CHECK(slots.size() >= 1 && slots.size() <= ewb::kMaxPeers, "1..8 owners");
   TORCH_CHECK(lo.size() == slots.size() + 1, "lo must have world+1 bounds");
   ewb::PeerScatter ps{};
@@ -109,14 +120,15 @@ void gemm_peer_scatter(at::Tensor a, at::Tensor b, at::Tensor out, std::vector<i
   ps.rank = static_cast<int>(rank);
   ps.world = static_cast<int>(slots.size());
   gemm_impl(a, true, b, true, out, ewb::kEpiAccF32Peer, c10::nullopt, c10::nullopt, c10::nullopt,
-            c10::nullopt, c10::nullopt, 1.0, bn, &ps);
+            c10::nullopt, c10::nullopt, 1.0, bn, &ps, a2, b2);
 }
 
 void gemm_impl(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor out, int64_t epi,
                c10::optional<at::Tensor> bias, c10::optional<at::Tensor> resid,
                c10::optional<at::Tensor> resid_scale, c10::optional<at::Tensor> aux,
                c10::optional<at::Tensor> scale_out, double beta, int64_t bn,
-               const ewb::PeerScatter* peer) {
+               const ewb::PeerScatter* peer, c10::optional<at::Tensor> a2,
+               c10::optional<at::Tensor> b2) {
   check_2d_rowmajor(a, "a");
   check_2d_rowmajor(b, "b");
   check_2d_rowmajor(out, "out");
@@ -141,6 +153,23 @@ void gemm_impl(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor out,
   g.K = K;
   g.bn = bn;
   g.split = gemm_split_flag();
+  if (a2.has_value() && a2->defined()) {
+    TORCH_CHECK(b2.has_value() && b2->defined(), "gemm: a2 needs b2");
+    check_2d_rowmajor(*a2, "a2");
+    check_2d_rowmajor(*b2, "b2");
+    TORCH_CHECK(a2->scalar_type() == at::kBFloat16 && b2->scalar_type() == at::kBFloat16,
+                "gemm operands must be bf16");
+    const int M2 = a_mn ? a2->size(1) : a2->size(0);
+    const int K2 = a_mn ? a2->size(0) : a2->size(1);
+    const int N2 = b_mn ? b2->size(1) : b2->size(0);
+    const int K2b = b_mn ? b2->size(0) : b2->size(1);
+    TORCH_CHECK(M2 == M && N2 == N && K2 == K2b, "gemm: the second pair must match M, N and its K");
+    g.a2 = a2->data_ptr();
+    g.lda2 = a2->stride(0);
+    g.b2 = b2->data_ptr();
+    g.ldb2 = b2->stride(0);
+    g.K2 = K2;
+  }
   g.status = status_word(a.get_device());
   ewb::GemmEpilogue& e = g.ep;
   e.kind = static_cast<int>(epi);
@@ -611,6 +640,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_pick_bn", &gemm_pick_bn);
   m.def("set_gemm_split", &set_gemm_split);
   m.def("gemm_peer_scatter", &gemm_peer_scatter);
+  m.def("gemm_pair", &gemm_pair);
   m.def("zero1_push_partials", &zero1_push_partials);
   m.def("zero1_fold_slots", &zero1_fold_slots);
   m.def("zero1_adamw_push", &zero1_adamw_push);

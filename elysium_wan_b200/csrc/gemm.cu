@@ -436,8 +436,11 @@ template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
-                        const __grid_constant__ CUtensorMap tmC, const GemmEpilogue ep, int M,
-                        int N, int K, int* status, int* sched, int nfull, int ns, float* ws) {
+                        const __grid_constant__ CUtensorMap tmC,
+                        const __grid_constant__ CUtensorMap tmA2,
+                        const __grid_constant__ CUtensorMap tmB2, const GemmEpilogue ep, int M,
+                        int N, int K, int K2, int* status, int* sched, int nfull, int ns,
+                        float* ws) {
   using Cfg = GemmCfg<BN, EPI>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -475,6 +478,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (K2 > 0) {
+      tma_prefetch_desc(&tmA2);
+      tma_prefetch_desc(&tmB2);
+    }
     if (EpiTraits<EPI>::kTma) tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
@@ -489,7 +496,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int num_m = (M + kBM - 1) / kBM;
   const int num_n = (N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
-  const int kblocks = (K + kBK - 1) / kBK;
+  // K runs over one operand pair, or over two (A2, B2 after A, B: the weight
+  // gradients of two microbatches folded by one launch).
+  const int kb1 = (K + kBK - 1) / kBK;
+  const int kblocks = kb1 + (K2 + kBK - 1) / kBK;
   // Units: tiles [0, nfull) whole, the other tiles each as `ns` K-splits (the
   // tail of the last wave spread over all SMs; see decode_unit).
   const int num_units = nfull + (num_tiles - nfull) * ns;
@@ -531,18 +541,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sa = smem + s * Cfg::STAGE_BYTES;
           uint8_t* sb = sa + Cfg::A_BYTES;
           mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
+          const bool seg2 = kb >= kb1;
+          const CUtensorMap* mA = seg2 ? &tmA2 : &tmA;
+          const CUtensorMap* mB = seg2 ? &tmB2 : &tmB;
+          const int kc = (seg2 ? kb - kb1 : kb) * kBK;
           if constexpr (!A_MN) {
-            tma_load_2d(sa, &tmA, &full[s], kb * kBK, mb * kBM);
+            tma_load_2d(sa, mA, &full[s], kc, mb * kBM);
           } else {
-            tma_load_2d(sa, &tmA, &full[s], mb * kBM, kb * kBK);
-            tma_load_2d(sa + 8192, &tmA, &full[s], mb * kBM + 64, kb * kBK);
+            tma_load_2d(sa, mA, &full[s], mb * kBM, kc);
+            tma_load_2d(sa + 8192, mA, &full[s], mb * kBM + 64, kc);
           }
           if constexpr (!B_MN) {
-            tma_load_2d(sb, &tmB, &full[s], kb * kBK, nb * BN);
+            tma_load_2d(sb, mB, &full[s], kc, nb * BN);
           } else {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j)
-              tma_load_2d(sb + j * 8192, &tmB, &full[s], nb * BN + j * 64, kb * kBK);
+              tma_load_2d(sb + j * 8192, mB, &full[s], nb * BN + j * 64, kc);
           }
         }
       }
@@ -833,15 +847,24 @@ int launch_cfg(const GemmArgs& g, cudaStream_t stream, int* sched, float* ws) {
   } else {
     mc = ma;  // unused by register epilogues
   }
+  CUtensorMap ma2 = ma, mb2 = mbm;
+  if (g.K2 > 0) {
+    const bool ok_a2 = A_MN ? make_map_bf16(&ma2, g.a2, g.M, g.K2, g.lda2, 64, 64)
+                            : make_map_bf16(&ma2, g.a2, g.K2, g.M, g.lda2, 64, kBM);
+    const bool ok_b2 = B_MN ? make_map_bf16(&mb2, g.b2, g.N, g.K2, g.ldb2, 64, 64)
+                            : make_map_bf16(&mb2, g.b2, g.K2, g.N, g.ldb2, 64, BN);
+    if (!ok_a2 || !ok_b2) return kGemmErrTensorMap;
+  }
   if (!ok_a || !ok_b || !ok_c) return kGemmErrTensorMap;
   const int sms = num_sms_cached();
   const long tiles = static_cast<long>((g.M + kBM - 1) / kBM) * ((g.N + BN - 1) / BN);
   int full = static_cast<int>(tiles);
-  const int ns = (ws != nullptr && g.split) ? split_plan(tiles, sms, (g.K + kBK - 1) / kBK, &full) : 1;
+  const int kbt = (g.K + kBK - 1) / kBK + (g.K2 + kBK - 1) / kBK;
+  const int ns = (ws != nullptr && g.split) ? split_plan(tiles, sms, kbt, &full) : 1;
   const long units = full + (tiles - full) * ns;
   const int grid = static_cast<int>(std::max(1L, std::min(units, static_cast<long>(sms))));
-  kern<<<grid, kThreads, Cfg::SMEM, stream>>>(ma, mbm, mc, g.ep, g.M, g.N, g.K, g.status, sched,
-                                              full, ns, ws);
+  kern<<<grid, kThreads, Cfg::SMEM, stream>>>(ma, mbm, mc, ma2, mb2, g.ep, g.M, g.N, g.K, g.K2,
+                                              g.status, sched, full, ns, ws);
   const cudaError_t err = cudaGetLastError();
   EWB_TRACE("[gemm] launched grid=%d ns=%d full=%d: %s\n", grid, ns, full, cudaGetErrorString(err));
   return err == cudaSuccess ? kGemmOk : kGemmErrLaunch;
@@ -919,13 +942,17 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
   if ((reinterpret_cast<uintptr_t>(g.a) & 15) || (reinterpret_cast<uintptr_t>(g.b) & 15))
     return kGemmErrAlign;
   if ((g.lda % 8) || (g.ldb % 8)) return kGemmErrAlign;
+  if (g.K2 < 0) return kGemmErrShape;
+  if (g.K2 > 0 && ((reinterpret_cast<uintptr_t>(g.a2) & 15) ||
+                   (reinterpret_cast<uintptr_t>(g.b2) & 15) || (g.lda2 % 8) || (g.ldb2 % 8)))
+    return kGemmErrAlign;
   if (g.ep.kind == kEpiResidQ8 && (g.N % 128 || g.ep.ldo % 16)) return kGemmErrShape;
   if (reinterpret_cast<uintptr_t>(g.ep.out) & 15) return kGemmErrAlign;
   if ((g.ep.kind == kEpiBf16 && g.ep.ldo % 8) ||
       ((g.ep.kind == kEpiF32 || g.ep.kind == kEpiAccF32) && g.ep.ldo % 4))
     return kGemmErrAlign;
   int bn = g.bn;
-  if (bn != 128 && bn != 192 && bn != 256) bn = gemm_pick_bn(g.M, g.N, g.K, g.split != 0);
+  if (bn != 128 && bn != 192 && bn != 256) bn = gemm_pick_bn(g.M, g.N, g.K + g.K2, g.split != 0);
   if (g.ep.kind == kEpiResidQ8) bn = 256;  // a tile covers whole 128-column scale blocks
   const StreamState st = stream_state(stream, g.split != 0);
   if (st.counters == nullptr) return kGemmErrLaunch;

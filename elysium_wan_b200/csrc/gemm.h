@@ -69,7 +69,14 @@ struct GemmArgs {
   int bn;  // 128 / 192 / 256, anything else = pick by the wave model
   GemmEpilogue ep;
   int* status;  // device status word (may be null)
-  int split;    // nonzero: the last wave's tiles may be split along K
+  int split;    // nonzero: a partial single wave may be split along K
+  // Optional second operand pair over K2 more reduction steps (0: none):
+  // C (epi)= A B^T + A2 B2^T accumulated in one pass, same layouts as A / B.
+  const void* a2;
+  int lda2;
+  const void* b2;
+  int ldb2;
+  int K2;
 };
 
 int gemm_launch(const GemmArgs& args, cudaStream_t stream);

@@ -231,7 +231,7 @@ class WTask:
         if self.peer is not None:
             slots, lo, stride, flat_off, rank = self.peer
             ops.ext().gemm_peer_scatter(self.dy, self.x, self.w_grad, slots, lo, stride, flat_off,
-                                        rank, 0)
+                                        rank, 0, None, None)
         else:
             ops.linear_dw(self.dy, self.x, self.w_grad, accumulate=True)
         if self.b_grad is not None:
@@ -242,6 +242,57 @@ class WTask:
         """Keep the inputs' memory alive until `stream` has consumed them."""
         self.dy.record_stream(stream)
         self.x.record_stream(stream)
+
+
+class PairWTask:
+    """The W of one linear for two microbatches of a slot (its owned
+    microbatches 2k and 2k + 1): dW (+)= dY1^T X1 + dY2^T X2 in one GEMM over
+    both token sets, then the bias row sums in microbatch order. A ZeRO-1 peer
+    scatter on the second (the replica's last) runs on the paired GEMM too."""
+
+    __slots__ = ("t1", "t2")
+
+    def __init__(self, t1: WTask, t2: WTask):
+        self.t1, self.t2 = t1, t2
+
+    def run(self):
+        t1, t2 = self.t1, self.t2
+        if t2.peer is not None:
+            slots, lo, stride, flat_off, rank = t2.peer
+            ops.ext().gemm_peer_scatter(t1.dy, t1.x, t2.w_grad, slots, lo, stride, flat_off, rank,
+                                        0, t2.dy, t2.x)
+        else:
+            ops.linear_dw_pair(t1.dy, t1.x, t2.dy, t2.x, t2.w_grad, accumulate=True)
+        if t2.b_grad is not None:
+            ops.colsum(t1.dy, t2.b_grad, accumulate=True)
+            ops.colsum(t2.dy, t2.b_grad, accumulate=True)
+        t1.dy = t1.x = t2.dy = t2.x = None
+
+    def record_stream(self, stream):
+        self.t1.record_stream(stream)
+        self.t2.record_stream(stream)
+
+
+def pair_w_tasks(first: list, second: list) -> list:
+    """The W tasks of two microbatches of a slot, paired linear by linear where
+    both are plain dW tasks of the same gradient (same shapes); any other task
+    (adapters, expert GEMMs with different token counts, ...) runs unpaired in
+    microbatch order, which is the fold the oracle declares for it too."""
+    if len(first) != len(second):
+        return list(first) + list(second)
+    out, tail = [], []
+    for a, b in zip(first, second):
+        if (type(a) is WTask and type(b) is WTask and a.peer is None
+                and a.w_grad.data_ptr() == b.w_grad.data_ptr() and a.w_grad.shape == b.w_grad.shape
+                and a.dy.shape[1:] == b.dy.shape[1:] and a.x.shape[1:] == b.x.shape[1:]
+                and (a.b_grad is None) == (b.b_grad is None)):
+            out.append(PairWTask(a, b))
+        else:
+            out.append(a)
+            tail.append(b)
+    # unpaired second-microbatch tasks after every first-microbatch task: each
+    # gradient still folds microbatch 2k before 2k + 1
+    return out + tail
 
 
 class WExecutor:

@@ -146,6 +146,22 @@ def linear_dx(dy, w, *, gelu_u=None, out=None):
     return g
 
 
+def linear_dw_pair(dy1, x1, dy2, x2, grad, accumulate: bool):
+    """grad (+)= dY1^T X1 + dY2^T X2 as ONE reduction over the two microbatches'
+    tokens (K = T1 + T2), folded into grad once: half the fp32 read-modify-write
+    of two separate folds. The sum order differs from two folds, so a run pairs
+    its weight gradients only as its recipe declares (`w_pair`)."""
+    if _cuda(dy1):
+        ext().gemm_pair(dy1, x1, dy2, x2, grad, 1.0 if accumulate else 0.0, 0)
+        return grad
+    g = torch.cat([dy1.float(), dy2.float()]).t() @ torch.cat([x1.float(), x2.float()])
+    if accumulate:
+        grad.add_(g)
+    else:
+        grad.copy_(g)
+    return grad
+
+
 def linear_dw(dy, x, grad, accumulate: bool):
     """grad (+)= dY^T X (W pass): the deferred weight gradient, folded in call order."""
     if _cuda(dy):

@@ -22,7 +22,7 @@ import time
 import torch
 
 from elysium_wan_b200.models.data import make_batch
-from elysium_wan_b200.models.gpt import Act, StageModel, WExecutor
+from elysium_wan_b200.models.gpt import Act, StageModel, WExecutor, pair_w_tasks
 from elysium_wan_b200.parallel.p2p import dbg
 from elysium_wan_b200.runtime import optim
 from elysium_wan_b200.runtime.telemetry import parse_sim_slow
@@ -63,6 +63,8 @@ class StageEngine:
         self._host_x = None
 
         self.sim_slow = parse_sim_slow().get(stage, (1.0, 0))
+        self.w_pair = bool(spec.w_pair) and spec.stage_widths[stage] == 1
+        self._w_stash = None
         side = os.environ.get("EWB_W_STREAM", "1") == "1"
         self.wexec = WExecutor(self.device, enabled=side)
         self.phase: dict = {}
@@ -91,6 +93,17 @@ class StageEngine:
     def _run_w(self, tasks: list, mb: int):
         if self.zero1 is not None and hasattr(self.zero1, "mark"):
             self.zero1.mark(tasks, mb)
+        if self.w_pair:
+            # microbatch 2k waits for 2k + 1; the pair runs as one fold
+            if mb % 2 == 0 and mb + 1 < self.spec.microbatches:
+                self._w_stash = (mb, tasks)
+                return
+            if mb % 2 == 1:
+                first_mb, first = self._w_stash
+                if first_mb != mb - 1:
+                    raise RuntimeError(f"W of microbatch {mb} without that of {mb - 1}")
+                self._w_stash = None
+                tasks = pair_w_tasks(first, tasks)
         # On the side stream the W op's device time is bracketed there (the
         # compute stream only enqueues it), so busy counts the W GEMMs too.
         ev = self.wexec.run(tasks, timing=self.timing)
@@ -232,7 +245,8 @@ class StageEngine:
                         grad_q[b_mbs[bi]] = comm.irecv_grad(b_mbs[bi])
                 # A W that directly follows its own B runs layer by layer inside
                 # B, releasing each layer's W inputs at once (same fold order).
-                inline = idx + 1 < len(self.order) and self.order[idx + 1] == ("W", mb)
+                inline = (not self.w_pair and idx + 1 < len(self.order)
+                          and self.order[idx + 1] == ("W", mb))
                 tasks: list = []
                 mark()
                 dx = self.model.backward(st, dy, tasks, run_w_inline=inline,

@@ -90,6 +90,10 @@ class JobSpec:
     shard: str = "zero1"
     fold: str = "dp_tree"
     grad_sync: str = "fused"  # fused | nccl
+    # Width-1 stages fold the weight gradients of microbatches 2k and 2k + 1
+    # with one GEMM over both token sets (half the fp32 read-modify-write of
+    # the gradient); a recipe choice, so a pin.
+    w_pair: bool = False
     # ------------------------------------------------------------- output
     out_dir: str = "runs"
     tag: str = "run"
@@ -232,6 +236,8 @@ class JobSpec:
         }
         if self.optimizer != "adamw":
             pins["optimizer"] = self.optimizer
+        if self.w_pair:
+            pins["w_pair"] = True
         if self.dataset_sha256:
             pins["dataset_sha256"] = self.dataset_sha256
         if self.init_from:

@@ -4,7 +4,7 @@ Compute capture targets (one kernel, one to three launches, a few GB).
     python -m elysium_wan_b200.utils.profcase --op gemm_fwd [--iters 3]
 
 Ops: gemm_fwd (qkv projection), gemm_dx (fc1 input gradient), gemm_dw (fc1
-weight gradient fold), gemm_resid (out projection + residual), gemm_fc2 (fc2 +
+weight gradient fold), gemm_dw_pair (the same for two microbatches in one launch), gemm_resid (out projection + residual), gemm_fc2 (fc2 +
 residual), gemm_dgelu (fc2 input gradient x GELU'), gemm_q8 (fc2 with the fp8 boundary epilogue),
 attn_fwd, attn_bwd, ln_fwd, ln_bwd, ce, adamw, embed_bwd, head_gemm (the 50257-way
 logits GEMM, fp32 out), head_fwd (LN + logits + CE of the head entry), head_bwd
@@ -60,6 +60,11 @@ def build(op):
         dy, x = _bf(T, F), _bf(T, D)
         g = torch.zeros(F, D, device="cuda")
         return (lambda: ops.linear_dw(dy, x, g, accumulate=True)), 2.0 * T * F * D, None
+    if op == "gemm_dw_pair":  # the same fold for two microbatches in one launch
+        dy1, x1, dy2, x2 = _bf(T, F), _bf(T, D), _bf(T, F), _bf(T, D)
+        g = torch.zeros(F, D, device="cuda")
+        return (lambda: ops.linear_dw_pair(dy1, x1, dy2, x2, g, accumulate=True)), \
+            2.0 * 2 * T * F * D, None
     if op == "gemm_q8":
         g, w, r = _bf(T, F), _bf(D, F, scale=0.02), _bf(T, D)
         b = torch.zeros(D, device="cuda")

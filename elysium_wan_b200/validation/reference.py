@@ -22,7 +22,7 @@ import time
 import torch
 
 from elysium_wan_b200.models.data import make_batch
-from elysium_wan_b200.models.gpt import StageModel
+from elysium_wan_b200.models.gpt import StageModel, pair_w_tasks
 from elysium_wan_b200.parallel.zero1 import fold_tree, shard_bounds
 from elysium_wan_b200.runtime import optim
 from elysium_wan_b200.utils.determinism import float_hex, setup_determinism
@@ -39,6 +39,9 @@ class Oracle:
         for m in self.stages:
             init_from_spec(m, spec)
         self.widths = list(spec.stage_widths)
+        # the declared weight-gradient pairing of width-1 stages (spec.w_pair)
+        self.w_pair = [bool(spec.w_pair) and w == 1 for w in self.widths]
+        self.w_stash: list = [None] * len(self.widths)
         self.partials = []
         self.opts = []
         for r, m in enumerate(self.stages):
@@ -90,7 +93,15 @@ class Oracle:
                 tasks: list = []
                 dy = self.stages[r].backward(ctxs[r], dy, tasks)
                 tasks_all.append(tasks)
-            for tasks in tasks_all:
+            for k, tasks in enumerate(tasks_all):
+                r = len(self.stages) - 1 - k
+                if self.w_pair[r]:  # microbatch 2k waits for 2k + 1; one fold per pair
+                    if mb % 2 == 0 and mb + 1 < spec.microbatches:
+                        self.w_stash[r] = tasks
+                        continue
+                    if mb % 2 == 1:
+                        tasks = pair_w_tasks(self.w_stash[r], tasks)
+                        self.w_stash[r] = None
                 for tk in tasks:
                     tk.run()
             i = 0

@@ -174,6 +174,28 @@ def test_gemm_k_split_tail(cuda, bn):
     assert rel_err(ops.dequant_e4m3(q, s, torch.float32), ref + b + r.float()) < 6e-2
 
 
+@pytest.mark.parametrize("T2", [2048, 1000])
+def test_gemm_pair_weight_grad(cuda, T2):
+    """dW (+)= dY1^T X1 + dY2^T X2 in one launch (the second token set ragged
+    too): equal to fp32, reproducible, and the same function of its inputs
+    as the two folds up to fp32 rounding."""
+    torch.manual_seed(12)
+    T1, N, K = 2048, 1536, 512
+    dy1, x1 = bf(T1, N, dev=cuda), bf(T1, K, dev=cuda)
+    dy2, x2 = bf(T2, N, dev=cuda), bf(T2, K, dev=cuda)
+    g0 = torch.randn(N, K, device=cuda)
+    ref = g0 + dy1.float().t() @ x1.float() + dy2.float().t() @ x2.float()
+    g = g0.clone()
+    ops.linear_dw_pair(dy1, x1, dy2, x2, g, accumulate=True)
+    assert rel_err(g, ref) < 1e-5
+    g2 = g0.clone()
+    ops.linear_dw_pair(dy1, x1, dy2, x2, g2, accumulate=True)
+    assert torch.equal(g, g2)
+    g3 = torch.empty_like(g0)
+    ops.linear_dw_pair(dy1, x1, dy2, x2, g3, accumulate=False)
+    assert rel_err(g3, ref - g0) < 1e-5
+
+
 def test_gemm_weight_grad_fold_and_determinism(cuda):
     torch.manual_seed(2)
     T, N, K = 2048, 1536, 512

@@ -48,3 +48,18 @@ def test_zero1_wide_stage_bitwise_vs_oracle(tmp_path, widths, sync):
     r = run_and_compare(spec, timeout=240)
     assert r["ok"], r
     assert r["compared"] == 12
+
+
+@pytest.mark.parametrize("stages", [1, 2])
+def test_w_pair_bitwise_vs_oracle(tmp_path, stages):
+    """Paired weight-gradient folds (one GEMM for microbatches 2k and 2k + 1,
+    5 microbatches so the last runs alone) on the GPU kernels: the pipeline
+    equals the oracle, which pairs the same way."""
+    _need(stages)
+    cfg = make_config("gpt15b", n_layer=2, d_model=512, n_head=4, seq_len=256, vocab_size=4096,
+                      boundary_dtype="fp8_e4m3_b128")
+    spec = JobSpec(model=cfg, stages=stages, microbatches=5, mb_size=2, steps=2, device="cuda",
+                   backend="nccl", w_pair=True, out_dir=str(tmp_path), port_base=29990 + stages)
+    r = run_and_compare(spec, timeout=240)
+    assert r["ok"], r
+    assert r["compared"] == 10

@@ -22,6 +22,10 @@ def _cfg(**kw):
 
 CASES = {
     "chain2": dict(stages=2),
+    # Width-1 stages fold the W of microbatches 2k and 2k + 1 with one GEMM;
+    # 5 microbatches leave the last one unpaired; the wide stage does not pair.
+    "w_pair_chain3": dict(stages=3, w_pair=True, microbatches=5),
+    "w_pair_wide_1_2": dict(stages=2, stage_widths=[1, 2], w_pair=True),
     "chain3_fp8_recompute": dict(stages=3, recompute=True, model_kw=dict(boundary_dtype="fp8_e4m3_b128")),
     "wide_2_1": dict(stages=2, stage_widths=[2, 1]),
     "wide_1_2": dict(stages=2, stage_widths=[1, 2]),
@@ -53,11 +57,28 @@ def test_pipeline_bitwise_vs_oracle(tmp_path, name):
     kw = dict(CASES[name])
     mk = kw.pop("model_kw", {})
     port = 29700 + 17 * sorted(CASES).index(name) + (os.getpid() % 50) * 3
-    spec = JobSpec(model=_cfg(**mk), microbatches=4, mb_size=2, steps=2, out_dir=str(tmp_path),
+    m = kw.pop("microbatches", 4)
+    spec = JobSpec(model=_cfg(**mk), microbatches=m, mb_size=2, steps=2, out_dir=str(tmp_path),
                    port_base=port, backend="gloo", **kw)
     r = run_and_compare(spec, timeout=240)
     assert r["ok"], r
-    assert r["compared"] == 8
+    assert r["compared"] == 2 * m
+
+
+def test_w_pair_changes_the_fold_only_as_declared():
+    """Pairing is a declared recipe: the first forward is the same, the folded
+    gradients (another fp32 sum order) and so the updated weights are not,
+    and it is a pin."""
+    from elysium_wan_b200.validation.reference import Oracle
+
+    base = dict(model=_cfg(), stages=2, microbatches=4, mb_size=2, steps=2)
+    a = JobSpec(**base).finalize()
+    b = JobSpec(**base, w_pair=True).finalize()
+    oa, ob = Oracle(a), Oracle(b)
+    assert [v.hex() for _, v in oa.step(0)] == [v.hex() for _, v in ob.step(0)]
+    assert any(not torch.equal(x.store.master, y.store.master)
+               for x, y in zip(oa.stages, ob.stages))
+    assert "w_pair" in b.pins() and "w_pair" not in a.pins()
 
 
 def test_tied_embeddings_across_a_cut_equal_one_stage(tmp_path):
