@@ -393,12 +393,17 @@ class Coordinator:
         measured = {} if self.cfg.no_probe else self._probe_links(spec)
         self._links(spec)
         spec.finalize()
+        admission = self._admit(spec, slots)
+        if admission is not None and not admission["ok"]:
+            why = "admission refused: " + "; ".join(admission["reasons"])
+            return RunResult(False, self.run_id, None, 0, 0, 0, why, run_dir)
         self._final_step = spec.steps - 1
         with open(os.path.join(run_dir, "spec.json"), "w") as f:
             f.write(spec.to_json())
         with open(os.path.join(run_dir, "rationale.json"), "w") as f:
             json.dump({"placement": {f"{s[0]}:{s[1]}": self.slot_node[s] for s in slots},
-                       "spares": spares, "links": spec.links, "measured_links": measured},
+                       "spares": spares, "links": spec.links, "measured_links": measured,
+                       "admission": admission},
                       f, indent=1)
         heals = restarts = 0
         resume_step = None
@@ -481,6 +486,18 @@ class Coordinator:
                        "replans": self.replans},
                       f, indent=1)
         return res
+
+    def _admit(self, spec, slots) -> dict | None:
+        """Admission of a job with wide stages (scheduler/admission.py) on the
+        nodes placed in its slots; None when every stage has width 1."""
+        from elysium_wan_b200.scheduler import admission as ad
+
+        if all(w == 1 for w in spec.stage_widths):
+            return None
+        infos = [self.nodes[self.slot_node[s]].info for s in slots]
+        ok, reasons, pred = ad.admit(spec, ad.devices_from_nodes(infos))
+        return {"ok": ok, "reasons": [r.text() for r in reasons],
+                "exposed_s": {str(k): v["exposed_s"] for k, v in pred.items()}}
 
     # ------------------------------------------------------------ rebalance
     def _windows(self) -> dict:

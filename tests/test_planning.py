@@ -190,3 +190,39 @@ def test_link_probe_over_loopback_and_duplex_classes():
     assert links.classify_duplex(100, 100, 150) == "shared"
     em = links.Emulation("us", {"eu": {"rtt_ms": 120, "mbps": 500}})
     assert em.link_to("eu").rtt_ms == 120 and em.link_to("us").mbps == 0.0
+
+
+def test_wide_stage_admission_and_exchange_simulator():
+    from elysium_wan_b200.models.config import make_config
+    from elysium_wan_b200.runtime.spec import JobSpec
+    from elysium_wan_b200.scheduler import admission as ad
+
+    # the 0.6B config as 2 stages x 4 replicas on B200s: admitted, exposure tiny
+    cfg = make_config("gpt15b", n_layer=20, d_model=1536, n_head=12)
+    for shard in ("zero1", "pieces"):
+        spec = JobSpec(model=cfg, stages=2, stage_widths=[4, 4], microbatches=16, mb_size=4,
+                       shard=shard).finalize()
+        ok, reasons, pred = ad.admit(spec, [ad.Device(f"g{i}") for i in range(8)])
+        assert ok, [r.text() for r in reasons]
+        assert 0 <= pred[0]["exposed_s"] < 1e-3
+    # pieces moves the matrices as bf16: less all-gather than ZeRO-1, same reduce-scatter
+    t = ad.stage_terms(spec, 0)
+    rz, az = ad.exchange_bytes(t, 4, "zero1")
+    rp, ap = ad.exchange_bytes(t, 4, "pieces")
+    assert rz == rp and ap < az
+    assert ad.device_bytes(t, 4, "pieces", 1) < ad.device_bytes(t, 4, "zero1", 1)
+    # a slow link fails S1 (and S2), a small device fails MEM, mixed classes fail class
+    ok, reasons, _ = ad.admit(spec, [ad.Device(f"g{i}", link_Bps=1e9) for i in range(8)])
+    kinds = {r.kind for r in reasons}
+    assert not ok and {"S1", "S2"} <= kinds
+    ok, reasons, _ = ad.admit(spec, [ad.Device(f"g{i}", vram_bytes=8 * 2**30) for i in range(8)])
+    assert not ok and any(r.kind == "MEM" for r in reasons)
+    mixed = [ad.Device(f"g{i}") for i in range(7)] + [ad.Device("h", device_class="h100")]
+    ok, reasons, _ = ad.admit(spec, mixed)
+    assert not ok and reasons[0].kind == "class" and "h100" in reasons[0].text()
+    # need-first: with a link too slow to hide the exchange, the first unit the
+    # next forward needs gets its gather before later units' gradients
+    sim = ad.simulate_exchange([10, 10, 10, 10], 2, "zero1", link_Bps=1.0, c_mb=30.0)
+    assert sim["exposed_s"] > 0
+    ags = [u for k, u in sim["order"] if k == "ag"]
+    assert ags == sorted(ags)
