@@ -132,15 +132,21 @@ def plan_spec(args, n: int, free_bytes: float | None):
     biggest = max(numel(r) for r in range(n))
     cap = free_bytes if free_bytes else 178 * GiB
     resident = biggest * (4 + 4 + 2)
-    slack = 8 * GiB
     host_adam = resident + 8 * biggest > 0.80 * cap
     spec.optimizer = "adamw-host" if host_adam else "adamw"
+    # With the moments on the device the activations fill what is left; keep a
+    # tenth of the device free on top of the 8 GiB so the caching allocator
+    # does not run into its retry path near the cap (seen at 2 stages:
+    # 168.5 of 178 GiB, 18 retries per step).
+    slack = 8 * GiB + (0 if host_adam else 0.10 * cap)
     budget = cap - resident - (0 if host_adam else 8 * biggest) - slack
     spec.stage_widths = [1] * n
-    # Pipelined stages fold the weight gradients of microbatch pairs with one
-    # GEMM each (the W ops are deferred there anyway); one device runs W inline
-    # in B, where pairing would hold a microbatch's W inputs across the next B.
-    spec.w_pair = n > 1 and not getattr(args, "no_w_pair", False)
+    # Stages of at most 12 layers fold the weight gradients of microbatch pairs
+    # with one GEMM each (their W ops are deferred and memory is ample); one
+    # device runs W inline in B, and 24-layer stages are short of memory, where
+    # pairing would hold one more microbatch's W inputs (~0.34 GB per layer).
+    blocks = max(sum(1 for e in range(a, b) if 1 <= e <= cfg.n_layer) for a, b in spec.partition)
+    spec.w_pair = n > 1 and blocks <= 12 and not getattr(args, "no_w_pair", False)
     from elysium_wan_b200.scheduler.planner import stage_memory_model
 
     spec.peer_weights = [[1.0]] * n
