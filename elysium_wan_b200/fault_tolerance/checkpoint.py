@@ -129,7 +129,9 @@ def load_latest(spec, stage: int, peer: int, step: int | None = None):
             validate_wave(path)
         except ValueError:
             continue
-        state = torch.load(os.path.join(path, "state.pt"), weights_only=False)
+        # the restricted unpickler: tensors and plain containers only, so a
+        # wave shipped from another machine cannot run code when it is read
+        state = torch.load(os.path.join(path, "state.pt"), map_location="cpu", weights_only=True)
         diff = first_pin_difference(spec.pins(), state.get("pins", {}))
         if diff is not None:
             raise ValueError(f"wave {path} was written under another recipe: pin {diff!r} differs")

@@ -14,7 +14,8 @@ ZeRO-1 and pieces stages. Here the flat stores make the mapping mechanical:
   partition, widths and shard mode): a job can change its cut, its replica
   count and ZeRO-1 <-> pieces at a wave and continue bit for bit;
 - `save(state, dir)` / `load(dir)` keep the logical form on disk as three
-  safetensors files (params, exp_avg, exp_avg_sq) and a manifest with the
+  safetensors files (params, exp_avg, exp_avg_sq), the buffers / losses / RNG
+  in the safe object codec (transport/serial.py, no pickle), and a manifest with the
   step, the recipe pins that do not name a topology, and a sha256 per file
   and per 16 MiB chunk; `load` verifies every chunk.
 """
@@ -32,6 +33,7 @@ from elysium_wan_b200.fault_tolerance import checkpoint as ckpt
 from elysium_wan_b200.models.gpt import entry_specs
 from elysium_wan_b200.models.params import plan_layout, shard_ranges
 from elysium_wan_b200.parallel.zero1 import shard_bounds
+from elysium_wan_b200.transport import serial
 
 CHUNK = 16 << 20
 _TOPOLOGY_PINS = ("partition", "zero1_widths", "device_types", "stage_widths")
@@ -175,10 +177,10 @@ def save(state: dict, out: str) -> str:
         save_file({k: v.contiguous() for k, v in state[key].items()}, path)
         files[os.path.basename(path)] = {"sha256": ckpt._sha256(path), "chunks": _chunks(path),
                                          "size": os.path.getsize(path)}
-    extra = os.path.join(out, "extra.pt")
-    torch.save({"buffers": state["buffers"], "losses": state["losses"], "rng": state["rng"]}, extra)
-    files["extra.pt"] = {"sha256": ckpt._sha256(extra), "chunks": _chunks(extra),
-                         "size": os.path.getsize(extra)}
+    extra = os.path.join(out, "extra.ewbs")  # safe object codec: no pickle
+    serial.save({"buffers": state["buffers"], "losses": state["losses"], "rng": state["rng"]}, extra)
+    files["extra.ewbs"] = {"sha256": ckpt._sha256(extra), "chunks": _chunks(extra),
+                           "size": os.path.getsize(extra)}
     man = {"step": state["step"], "t": state["t"], "pins": state["pins"], "chunk": CHUNK,
            "files": files}
     with open(os.path.join(out, "manifest.json"), "w") as f:
@@ -196,7 +198,7 @@ def load(src: str) -> dict:
         path = os.path.join(src, name)
         if os.path.getsize(path) != ent["size"] or _chunks(path) != ent["chunks"]:
             raise ValueError(f"{path}: a chunk does not match the manifest")
-    extra = torch.load(os.path.join(src, "extra.pt"), weights_only=False)
+    extra = serial.load(os.path.join(src, "extra.ewbs"))
     return {"step": man["step"], "t": man["t"], "pins": man["pins"],
             "params": load_state(os.path.join(src, "params.safetensors")),
             "exp_avg": load_state(os.path.join(src, "exp_avg.safetensors")),

@@ -181,3 +181,31 @@ def test_socket_tuning_plan_and_apply():
     rep = tuning.tune(s)  # never raises; reports what holds
     assert set(rep) == {"cc", "sndbuf", "rcvbuf", "pace"}
     s.close()
+
+
+def test_safe_object_codec_roundtrip_and_no_pickle():
+    import math
+    import pickle
+
+    import torch
+
+    from elysium_wan_b200.transport import serial
+
+    obj = {"step": 3, "params": torch.randn(10), "names": ["a", "b"],
+           "opt": {"t": 2, "m": torch.zeros(3, dtype=torch.bfloat16)},
+           "losses": {0: 1.5, 1: float("inf")}, "rng": torch.get_rng_state(),
+           "tup": (1, "x", None), "b": b"\x00\x01", "nan": float("nan"), "e": torch.empty(0, 4),
+           "f8": torch.randn(8).to(torch.float8_e4m3fn)}
+    o = serial.loads(serial.dumps(obj))
+    assert torch.equal(o["params"], obj["params"]) and o["names"] == ["a", "b"]
+    assert o["opt"]["m"].dtype == torch.bfloat16 and o["losses"] == {0: 1.5, 1: float("inf")}
+    assert torch.equal(o["rng"], obj["rng"]) and o["tup"] == (1, "x", None) and o["b"] == b"\x00\x01"
+    assert math.isnan(o["nan"]) and o["e"].shape == (0, 4)
+    assert torch.equal(o["f8"].view(torch.uint8), obj["f8"].view(torch.uint8))
+    # the same bytes for the same object (exact, deterministic)
+    assert serial.dumps(obj["opt"]) == serial.dumps(obj["opt"])
+    # a pickle is refused, not executed
+    with pytest.raises(ValueError):
+        serial.loads(pickle.dumps({"x": 1}))
+    with pytest.raises(TypeError):
+        serial.dumps({"f": object()})
