@@ -4,9 +4,10 @@ Field names follow the reference's GPTConfig (src/wantrain/model/gpt.py:47-253)
 so a job JSON written for wantrain loads unchanged. The block is the reference's
 generalized decoder (src/wantrain/model/arch.py): norm layernorm | rmsnorm,
 mlp gelu | swiglu, pos learned | rope, grouped-query attention (n_kv_head),
-bias on/off, tied embeddings, and the exact MoE block (moe_* fields). Knobs
-this engine does not build (arch "hf", user models) are accepted in the JSON
-and refused with a clear message at build time.
+bias on/off, tied embeddings, and the exact MoE block (moe_* fields). User
+models (arch "user": the operator's own flat layer list, models/user.py) run
+on the host path. Arch "hf" (transformers module trees) is accepted in the
+JSON and refused with a clear message at build time.
 """
 
 from __future__ import annotations
@@ -58,6 +59,10 @@ class GPTConfig:
     moe_d_ff: int | None = None
     moe_shared_d_ff: int = 0
     moe_shared_gate: str = "sigmoid"  # sigmoid | none
+    # arch "user": a Python file defining build(cfg) -> n_layer + 2 modules
+    # (token ids -> ... -> logits), pinned by its sha256
+    user_model: str = ""
+    user_model_sha256: str = ""
     moe_layers: list | None = None  # 0-based block indices; None = every block
     moe_router_dtype: str = "compute"  # compute | fp32
     moe_router_bias: bool = False
@@ -130,10 +135,17 @@ class GPTConfig:
             raise ValueError(f"boundary_dtype {self.boundary_dtype!r} not in {BOUNDARY_DTYPES}")
         if self.d_model % self.n_head:
             raise ValueError("d_model must be divisible by n_head")
-        if self.arch != "builtin":
+        if self.arch == "user":
+            if not self.user_model:
+                raise ValueError("arch 'user' needs user_model (a Python file defining build(cfg))")
+            if self.compute_dtype != "fp32" or self.boundary_dtype != "fp32":
+                raise ValueError("user models run in fp32 with fp32 boundaries (the host path)")
+            if self.lora_rank or self.moe_experts or self.tie_embeddings:
+                raise ValueError("LoRA, MoE and tied embeddings are built-in decoder knobs")
+        elif self.arch != "builtin":
             raise NotImplementedError(
-                f"arch {self.arch!r}: this engine builds the built-in decoder family only "
-                f"(GPT and Llama-style knobs, MoE); HF module trees and user models are not built")
+                f"arch {self.arch!r}: this engine builds the built-in decoder family and user "
+                f"models (arch 'user'); HF module trees are not built")
         for name, allowed in (("norm", ("layernorm", "rmsnorm")), ("mlp", ("gelu", "swiglu")),
                               ("pos", ("learned", "rope")),
                               ("lora_targets", ("attn", "attn_mlp", "all"))):

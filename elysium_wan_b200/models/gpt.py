@@ -93,6 +93,10 @@ def entry_specs(cfg: GPTConfig, e: int) -> list[ParamSpec]:
     `{linear}.B.weight` (out x r, zeros), declared after the entry's base
     tensors so the base init is the same as without LoRA (reference:
     src/wantrain/model/lora.py)."""
+    if cfg.arch == "user":
+        from elysium_wan_b200.models import user
+
+        return user.entry_specs(cfg, e)
     base = _base_specs(cfg, e)
     if not cfg.lora_rank:
         return base
@@ -333,6 +337,7 @@ class WExecutor:
 
 
 class Embed:
+    is_embed, is_head = True, False
     def __init__(self, cfg, store: ParamStore, e: int):
         self.cfg, self.s, self.e = cfg, store, e
         self.has_pos = cfg.pos == "learned"
@@ -508,6 +513,7 @@ class Block:
 
 
 class Head:
+    is_embed, is_head = False, True
     def __init__(self, cfg, store: ParamStore, e: int):
         self.cfg, self.s, self.e = cfg, store, e
         self.n = lambda k: f"{e}.{k}"
@@ -592,9 +598,16 @@ class StageModel:
             raise NotImplementedError("LoRA over MoE blocks is not built")
         if cfg.lora_rank and self.device.type == "cuda" and cfg.lora_rank % 8:
             raise ValueError("lora_rank must be a multiple of 8 on the GPU kernels")
+        if cfg.arch == "user" and self.device.type != "cpu":
+            raise ValueError("user models run on the host path (device cpu)")
         self.store = ParamStore(specs, self.device, work_dtype=work, shard=shard)
-        init_params(self.store, seed, entry_of, cfg.init_std, cfg.n_layer, cfg.init_scheme,
-                    first_of_entry={"0.tok.weight": 0} if self.tied and self.lo > 0 else None)
+        if cfg.arch == "user":
+            from elysium_wan_b200.models import user
+
+            user.copy_initial(self.store, cfg, span, seed)
+        else:
+            init_params(self.store, seed, entry_of, cfg.init_std, cfg.n_layer, cfg.init_scheme,
+                        first_of_entry={"0.tok.weight": 0} if self.tied and self.lo > 0 else None)
         # The head's gradient of a tied table accumulates apart from the
         # embedding's (its own fold, microbatch order); before the optimizer the
         # table's gradient becomes (embedding part) + (head part) on every cut.
@@ -605,6 +618,13 @@ class StageModel:
                          for n in self.store.names() if n.endswith(".A.weight")]
         self.after_step()
         self.layers = []
+        if cfg.arch == "user":
+            from elysium_wan_b200.models import user
+
+            mods = user.stage_modules(cfg, span, seed)
+            self.layers = [user.UserLayer(cfg, self.store, e, m)
+                           for e, m in zip(range(self.lo, self.hi), mods)]
+            return
         for e in range(self.lo, self.hi):
             if e == 0:
                 self.layers.append(Embed(cfg, self.store, e))
@@ -686,11 +706,11 @@ class StageModel:
         for layer in self.layers:
             ctx: dict = {}
             x_in = h
-            if isinstance(layer, Head):
+            if getattr(layer, "is_head", False):
                 h = layer.forward(h, ctx, targets)
             else:
                 h = layer.forward(h, ctx)
-            if keep == "all" or isinstance(layer, (Head, Embed)):
+            if keep == "all" or getattr(layer, "is_head", False) or getattr(layer, "is_embed", False):
                 saved.append(("ctx", ctx))
             else:
                 ctx.clear()

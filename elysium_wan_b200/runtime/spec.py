@@ -179,12 +179,30 @@ class JobSpec:
                 (self.stage_widths[0] != 1 or self.stage_widths[-1] != 1):
             raise NotImplementedError("a tied table across a cut needs width-1 first and last "
                                       "stages")
+        if self.model.arch == "user":
+            self._check_user_model()
         if self.schedule_order is None:
             self.schedule_order = default_schedule(self)
         self._check_schedule_order()
         if self.resume_step is not None and not self.resume:
             raise ValueError("resume_step needs resume")
         return self
+
+    def _check_user_model(self):
+        """The structural contract of a user model (validation/model_contract.py):
+        deterministic build under one seed, stateless deterministic layers."""
+        from elysium_wan_b200.models.user import _source
+        from elysium_wan_b200.validation.model_contract import validate
+
+        raw = _source(self.model)  # checks the sha256 pin
+        target = self.model.to_dict()
+        target["example"] = [[i % self.model.vocab_size for i in range(self.model.seq_len)]]
+        r = validate(raw.decode(), target)
+        if not r["ok"]:
+            raise ValueError("user model breaks the contract: " + "; ".join(r["errors"]))
+        if r["layers"] != self.model.n_entries:
+            raise ValueError(f"user model has {r['layers']} layers, the spec declares "
+                             f"{self.model.n_entries} (n_layer + 2)")
 
     def reschedule(self) -> "JobSpec":
         self.mb_owner = None

@@ -9,7 +9,25 @@ from __future__ import annotations
 import torch
 
 
-def validate(source: str, target: dict) -> dict:
+class _Target(dict):
+    """A dict target read by attribute too (build(cfg) may use cfg.d_model)."""
+
+    def __getattr__(self, k):
+        try:
+            return self[k]
+        except KeyError as e:
+            raise AttributeError(k) from e
+
+
+def validate(source: str, target) -> dict:
+    """target: a dict (or a config object; its fields are read) with an
+    optional "example" input for the per-layer checks."""
+    if not isinstance(target, dict):
+        example = getattr(target, "example", None)
+        target = dict(target.to_dict()) if hasattr(target, "to_dict") else dict(vars(target))
+        if example is not None:
+            target["example"] = example
+    target = _Target(target)
     errors = []
     ns: dict = {}
     try:

@@ -136,3 +136,59 @@ def test_pieces_layout_holds_one_range_and_resumes(tmp_path):
     with open(b) as f:
         lb = {(r["step"], r["mb"]): r["loss_hex"] for r in json.load(f)["losses"]}
     assert all(lb[k] == v for k, v in la.items() if k[0] == 2)
+
+
+def _user_cfg(n_layer=4):
+    import hashlib
+
+    src = os.path.join(os.path.dirname(os.path.abspath(__file__)), "data", "user_mlp_model.py")
+    sha = hashlib.sha256(open(src, "rb").read()).hexdigest()
+    return make_config("toy", n_layer=n_layer, vocab_size=97, d_model=64, n_head=4, seq_len=16,
+                       arch="user", user_model=src, user_model_sha256=sha)
+
+
+@pytest.mark.parametrize("stages,widths", [(2, None), (3, [1, 2, 1])])
+def test_user_model_pipeline_bitwise_vs_oracle(tmp_path, stages, widths):
+    """arch "user": the operator's own flat module list (sha256-pinned source)
+    cut over stages, a wide stage among them, equals the oracle bit for bit."""
+    port = 35500 + stages * 13 + (os.getpid() % 200) * 7
+    kw = {"stage_widths": widths} if widths else {}
+    spec = JobSpec(model=_user_cfg(), stages=stages, microbatches=4, mb_size=2, steps=2,
+                   out_dir=str(tmp_path), port_base=port, backend="gloo", **kw)
+    r = run_and_compare(spec, timeout=240)
+    assert r["ok"], r
+    assert r["compared"] == 8
+
+
+def test_user_model_source_is_pinned(tmp_path):
+    from elysium_wan_b200.models.gpt import StageModel
+
+    cfg = _user_cfg()
+    bad = make_config("toy", n_layer=4, vocab_size=97, d_model=64, n_head=4, seq_len=16,
+                      arch="user", user_model=cfg.user_model, user_model_sha256="0" * 64)
+    with pytest.raises(ValueError, match="does not match"):
+        StageModel(bad, (0, bad.n_entries), "cpu", 1)
+    wrong_depth = make_config("toy", n_layer=4, vocab_size=97, d_model=64, n_head=4, seq_len=16,
+                              arch="user", user_model=cfg.user_model)
+    m = StageModel(wrong_depth, (0, 2), "cpu", 1)  # no sha pinned: accepted, builds 6 entries
+    assert len(m.layers) == 2
+
+
+def test_user_model_contract_refuses_a_stateful_layer(tmp_path):
+    src = tmp_path / "bad_model.py"
+    src.write_text(
+        "import torch\nfrom torch import nn\n"
+        "class E(nn.Module):\n"
+        "    def __init__(s, c):\n        super().__init__(); s.t = nn.Embedding(c.vocab_size, c.d_model)\n"
+        "    def forward(s, i):\n        return s.t(i)\n"
+        "class Noisy(nn.Module):\n"
+        "    def __init__(s, c):\n        super().__init__(); s.l = nn.Linear(c.d_model, c.d_model); s.n = 0\n"
+        "    def forward(s, x):\n        s.n += 1\n        return s.l(x) * s.n\n"
+        "class H(nn.Module):\n"
+        "    def __init__(s, c):\n        super().__init__(); s.o = nn.Linear(c.d_model, c.vocab_size)\n"
+        "    def forward(s, x):\n        return s.o(x)\n"
+        "def build(c):\n    return [E(c), Noisy(c), H(c)]\n")
+    cfg = make_config("toy", n_layer=1, vocab_size=97, d_model=64, n_head=4, seq_len=16,
+                      arch="user", user_model=str(src))
+    with pytest.raises(ValueError, match="contract"):
+        JobSpec(model=cfg, stages=1, microbatches=2, mb_size=1).finalize()
