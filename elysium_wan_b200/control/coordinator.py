@@ -12,7 +12,10 @@ and its message kinds:
     (scheduler/fleetplan.py). Workers are placed in rank order grouped by
     region; the rest are spares. Hops between regions get the worker's WAN
     link profile (the CPU/gloo configuration emulates it in the transport).
-  * fit-check (FIT) and profile (PROFILE) are optional round trips.
+  * profile (PROFILE): every slot times F, B and W of one microbatch on its
+    own node; the zero-bubble schedule and the peers' ownership weights are
+    solved from those costs, and a cut the job did not pin is refined by the
+    measured stage rates (reference :1591-1700). fit-check (FIT) is optional.
   * launch: ASSIGN to every slot, last rank first, with a fresh rendezvous
     port per attempt (a heal relaunches every slot, so NCCL / gloo groups are
     always new).
@@ -68,6 +71,8 @@ class CoordinatorConfig:
     max_restarts: int = 2
     no_probe: bool = True
     no_fit_check: bool = True
+    profile: bool = True   # measure F/B/W per slot before launch and solve the schedule from them
+    profile_timeout_s: float = 300.0
     group_by: str = "region"
     allow_shared_hosts: bool = True
     any_region: bool = True
@@ -150,8 +155,10 @@ class Coordinator:
         self._pending_ckpt: dict = {}
         self.link_memory = None
         self.link_results: dict = {}
+        self.replies: dict = {}  # (result kind, node id) -> fields
         # rebalance state (per run)
         self.telem: dict = {}          # slot -> deque of this attempt's summaries
+        self.telem_all: dict = {}      # slot -> compute ms of every summary of this attempt
         self.replans: list = []
         self.replan_checked = -1
         self.slot_base: dict = {}
@@ -284,6 +291,13 @@ class Coordinator:
                 if slot is not None and current and isinstance(hdr.get("telem"), dict):
                     self.telem.setdefault(
                         slot, collections.deque(maxlen=self.cfg.telem_window)).append(hdr["telem"])
+                    # every summary's compute of this attempt, in arrival order:
+                    # the slow-slot baseline must not depend on when the monitor polls
+                    from elysium_wan_b200.scheduler.rebalance import stage_compute_ms
+
+                    self.telem_all.setdefault(slot, []).append(stage_compute_ms(hdr["telem"]))
+            elif kind in ("PROFILE_RESULT", "FIT_RESULT"):
+                self.replies[(kind, nid)] = {k: v for k, v in hdr.items() if k != "kind"}
             elif kind == "LINK_RESULT":
                 self.link_results[(nid, hdr.get("target"))] = {k: v for k, v in hdr.items()
                                                               if k != "kind"}
@@ -378,6 +392,7 @@ class Coordinator:
 
     def run_job(self, job: Job) -> RunResult:
         spec = self._spec_for(job)
+        cut_given = spec.partition is not None
         spec.zb_mem_mode = spec.zb_mem_mode or self.cfg.zb_mem_mode
         spec.finalize()
         self.run_id = time.strftime("%Y%m%d-%H%M%S") + "-" + uuid.uuid4().hex[:6]
@@ -393,17 +408,24 @@ class Coordinator:
         measured = {} if self.cfg.no_probe else self._probe_links(spec)
         self._links(spec)
         spec.finalize()
+        schedule = None
+        if spec.stages > 1 and self.cfg.profile and not spec.resume:
+            schedule = self._zero_bubble(spec, slots, refine=not cut_given)
         admission = self._admit(spec, slots)
         if admission is not None and not admission["ok"]:
             why = "admission refused: " + "; ".join(admission["reasons"])
             return RunResult(False, self.run_id, None, 0, 0, 0, why, run_dir)
+        if not self.cfg.no_fit_check:
+            fits, why = self._fit_check(spec, slots)
+            if not fits:
+                return RunResult(False, self.run_id, None, 0, 0, 0, why, run_dir)
         self._final_step = spec.steps - 1
         with open(os.path.join(run_dir, "spec.json"), "w") as f:
             f.write(spec.to_json())
         with open(os.path.join(run_dir, "rationale.json"), "w") as f:
             json.dump({"placement": {f"{s[0]}:{s[1]}": self.slot_node[s] for s in slots},
                        "spares": spares, "links": spec.links, "measured_links": measured,
-                       "admission": admission},
+                       "admission": admission, "schedule": schedule},
                       f, indent=1)
         heals = restarts = 0
         resume_step = None
@@ -487,6 +509,91 @@ class Coordinator:
                       f, indent=1)
         return res
 
+    def _ask_slots(self, kind: str, result: str, spec, slots, timeout: float) -> dict:
+        """Send `kind` (PROFILE / FIT) for every slot to its node at once and
+        collect the `result` replies. -> {slot: fields}; a missing reply is
+        {"ok": False, "why": "timeout"}."""
+        with self.lock:
+            for s in slots:
+                self.replies.pop((result, self.slot_node[s]), None)
+        body = spec.to_dict()
+        for s in slots:
+            self.nodes[self.slot_node[s]].ch.send(kind, spec=body, stage=s[0], peer=s[1])
+        t0 = time.time()
+        while time.time() - t0 < timeout:
+            with self.lock:
+                if all((result, self.slot_node[s]) in self.replies for s in slots):
+                    break
+            time.sleep(0.05)
+        with self.lock:
+            return {s: self.replies.get((result, self.slot_node[s]), {"ok": False, "why": "timeout"})
+                    for s in slots}
+
+    def _zero_bubble(self, spec, slots, refine: bool) -> dict:
+        """Profile every slot on its own node (F, B, W of one microbatch),
+        re-cut by the measured stage rates when the job did not pin a cut and
+        it shortens the slowest stage by 5% (reference: coordinator.py:1591-
+        1700), then solve the zero-bubble schedule and the peers' ownership
+        weights from the measured costs. A failed profile keeps the analytic
+        schedule."""
+        from elysium_wan_b200.scheduler import rebalance as rb
+
+        def profile():
+            got = self._ask_slots("PROFILE", "PROFILE_RESULT", spec, slots,
+                                  self.cfg.profile_timeout_s)
+            bad = [f"{s}: {r.get('why')}" for s, r in got.items() if not r.get("ok")]
+            if bad:
+                raise RuntimeError("; ".join(bad))
+            out = []
+            for r in range(spec.stages):
+                out.append([{"t_f": got[(r, p)]["F"], "t_b": got[(r, p)]["B"],
+                             "t_w": got[(r, p)]["W"]} for p in range(spec.stage_widths[r])])
+            return out
+
+        refined = None
+        try:
+            profiles = profile()
+            if refine:
+                res = rb.refined_partition(spec, profiles, None, 0.05)
+                if res is not None:
+                    refined = {"from": spec.partition, "to": res[0]}
+                    spec.partition = res[0]
+                    spec.stage_costs = None
+                    spec.reschedule()
+                    profiles = profile()
+        except RuntimeError as e:
+            self.events.append(("profile_failed", None, {"why": str(e)}))
+            return {"source": "analytic", "reason": str(e)}
+        # each peer's weight is its measured rate; the stage's cost per
+        # microbatch is its peers' combined rate
+        weights = [[1.0 / max(1e-9, p["t_f"] + p["t_b"] + p["t_w"]) for p in row]
+                   for row in profiles]
+        costs = []
+        for row, wr in zip(profiles, weights):
+            share = sum(wr)
+            costs.append([sum(p[k] * w for p, w in zip(row, wr)) / share / len(row)
+                          for k in ("t_f", "t_b", "t_w")])
+        spec.stage_costs = costs
+        spec.peer_weights = [[w / max(wr) for w in wr] for wr in weights]
+        spec.mb_owner = None
+        spec.schedule_order = None
+        spec.finalize()
+        return {"source": "profiled", "partition_refined": refined,
+                "costs_ms": [[round(x * 1e3, 3) for x in c] for c in costs],
+                "peer_weights": [[round(w, 3) for w in row] for row in spec.peer_weights]}
+
+    def _fit_check(self, spec, slots):
+        """Every slot builds its real slice on its node and holds the
+        schedule's peak in-flight microbatches (resources/fit.py)."""
+        got = self._ask_slots("FIT", "FIT_RESULT", spec, slots, self.cfg.profile_timeout_s)
+        for s in slots:
+            r = got[s]
+            if not r.get("ok"):
+                return False, f"fit of slot {s} failed: {r.get('why')}"
+            if not r.get("fits"):
+                return False, f"slot {s} does not fit: peak {r.get('peak_bytes')} bytes"
+        return True, ""
+
     def _admit(self, spec, slots) -> dict | None:
         """Admission of a job with wide stages (scheduler/admission.py) on the
         nodes placed in its slots; None when every stage has width 1."""
@@ -565,8 +672,10 @@ class Coordinator:
         if not self.cfg.watch_slow or self.store is None:
             return None
         windows = self._windows()
-        for slot, win in windows.items():
-            hist = [rb.stage_compute_ms(x) for x in win[2:]]
+        with self.lock:
+            series = {slot: list(v) for slot, v in self.telem_all.items()}
+        for slot, xs in series.items():
+            hist = xs[2:]  # the attempt's first two summaries hold its warm-up
             if len(hist) >= self.cfg.slow_runs and slot not in self.slot_base:
                 self.slot_base[slot] = statistics.median(hist[: self.cfg.slow_runs])
             if hist:
@@ -649,6 +758,7 @@ class Coordinator:
             self.results = {}
             self.slots = {}
             self.telem = {}
+            self.telem_all = {}
             # a slot's baseline belongs to the node that runs it in this attempt
             self.slot_base, self.slot_hist, self.slow_noted = {}, {}, None
             for s in spec.slots():

@@ -61,6 +61,13 @@ def test_cluster_run_matches_oracle(tmp_path):
     finally:
         cl.close()
     assert res.ok, res.why
+    # every slot was profiled on its worker and the schedule solved from the measured costs
+    import json
+    import os
+
+    with open(os.path.join(res.run_dir, "rationale.json")) as f:
+        sched = json.load(f)["schedule"]
+    assert sched["source"] == "profiled" and len(sched["costs_ms"]) == 2, sched
     ref = JobSpec.from_dict(spec.to_dict())
     ref.out_dir = str(tmp_path / "oracle")
     ref.finalize()
