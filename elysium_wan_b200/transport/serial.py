@@ -32,18 +32,22 @@ _DTYPES = {str(d).replace("torch.", ""): d for d in (
     torch.int16, torch.int32, torch.int64, torch.bool, torch.float8_e4m3fn, torch.float8_e5m2)}
 
 
+_RESERVED = {"__t__", "__b__", "__tuple__", "__f__", "__d__"}
+
+
 def _enc(obj, blobs: list):
     if isinstance(obj, torch.Tensor):
         t = obj.detach().to("cpu").contiguous()
-        blobs.append(t.view(torch.uint8).reshape(-1).numpy().tobytes() if t.numel() else b"")
+        blobs.append(t.reshape(-1).view(torch.uint8).numpy().tobytes() if t.numel() else b"")
         return {"__t__": len(blobs) - 1, "dtype": str(t.dtype).replace("torch.", ""),
                 "shape": list(t.shape)}
     if isinstance(obj, (bytes, bytearray)):
         blobs.append(bytes(obj))
         return {"__b__": len(blobs) - 1}
     if isinstance(obj, dict):
-        if not all(isinstance(k, str) for k in obj):
-            # integer keys (stage indices, ...) travel as ["__k__", key, value] pairs
+        if not all(isinstance(k, str) for k in obj) or _RESERVED & set(obj):
+            # non-string keys (stage indices, ...) and keys that would read as a
+            # marker travel as {"__d__": [[key, value], ...]}
             return {"__d__": [[_enc(k, blobs), _enc(v, blobs)] for k, v in obj.items()]}
         return {k: _enc(v, blobs) for k, v in obj.items()}
     if isinstance(obj, tuple):

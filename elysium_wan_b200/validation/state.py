@@ -38,19 +38,42 @@ def store_entries(store, m=None, v=None, lo=0) -> dict:
 def reference_manifest(oracle) -> dict:
     params = {}
     for r, m in enumerate(oracle.stages):
-        ents = store_entries(m.store)
-        from elysium_wan_b200.parallel.zero1 import shard_bounds
-
-        bounds = shard_bounds(m.store.nt, oracle.widths[r]) if oracle.widths[r] > 1 else [(0, m.store.nt)]
-        for (lo, hi), o in zip(bounds, oracle.opts[r]):
-            mm, vv = o.m, o.v
-            sub = store_entries(m.store, mm, vv, lo)
-            for k, e in sub.items():
-                if "exp_avg" in e:
-                    ents[k].update(e)
-        params.update(ents)
+        # the shards' moments in order cover [0, nt): join them so a tensor
+        # that straddles a shard boundary gets its moments too
+        mm = torch.cat([o.m.reshape(-1).cpu() for o in oracle.opts[r]])
+        vv = torch.cat([o.v.reshape(-1).cpu() for o in oracle.opts[r]])
+        params.update(store_entries(m.store, mm, vv, 0))
     return {"params": params, "step": oracle.opts[0][0].t,
             "losses": {f"{s}:{mb}": float(v).hex() for s, mb, v in oracle.losses}}
+
+
+def distributed_manifest(spec, step: int | None = None) -> dict:
+    """The same manifest for a distributed run, read from its checkpoint waves
+    at `step` (default: the newest wave every slot holds) through the logical
+    form, whatever the cut, the widths and the ZeRO-1 / pieces layout."""
+    from elysium_wan_b200.fault_tolerance import logical
+
+    st = logical.gather(spec, step)
+    params = {}
+    for name, t in st["params"].items():
+        ent = {"param": _sha(t)}
+        if name in st["exp_avg"]:
+            ent["exp_avg"] = _sha(st["exp_avg"][name])
+            ent["exp_avg_sq"] = _sha(st["exp_avg_sq"][name])
+        params[name] = ent
+    return {"params": params, "step": st["t"],
+            "losses": {f"{s}:{mb}": float(v).hex() for (s, mb), v in _loss_items(st["losses"])}}
+
+
+def _loss_items(losses):
+    out = []
+    for k, v in (losses or {}).items():
+        if isinstance(k, (tuple, list)):
+            out.append(((int(k[0]), int(k[1])), v))
+        elif isinstance(k, str) and ":" in k:
+            a, b = k.split(":")
+            out.append(((int(a), int(b)), v))
+    return out
 
 
 def write_manifest(path: str, man: dict):

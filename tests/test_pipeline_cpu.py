@@ -192,3 +192,28 @@ def test_user_model_contract_refuses_a_stateful_layer(tmp_path):
                       arch="user", user_model=str(src))
     with pytest.raises(ValueError, match="contract"):
         JobSpec(model=cfg, stages=1, microbatches=2, mb_size=1).finalize()
+
+
+@pytest.mark.parametrize("shard", ["zero1", "pieces"])
+def test_final_training_state_is_byte_identical_to_the_oracle(tmp_path, shard):
+    """Beyond the losses: every fp32 master weight, AdamW moment and the step
+    count of the pipeline's final waves (read back through the logical form)
+    hash to the oracle's manifest."""
+    import json
+
+    from elysium_wan_b200.validation.state import diff_manifests, distributed_manifest
+
+    port = 36200 + 31 * (shard == "pieces") + (os.getpid() % 200) * 7
+    spec = JobSpec(model=_cfg(), stages=2, stage_widths=[1, 2], shard=shard, microbatches=4,
+                   mb_size=2, steps=2, ckpt_every=2, out_dir=str(tmp_path), port_base=port,
+                   backend="gloo")
+    r = run_and_compare(spec, timeout=240)
+    assert r["ok"], r
+    spec.finalize()
+    got = distributed_manifest(spec, 2)
+    with open(tmp_path / "reference_state.json") as f:
+        ref = json.load(f)
+    assert diff_manifests(ref, got) == []
+    assert len(got["params"]) == len(ref["params"]) > 10
+    assert all("exp_avg" in e for e in got["params"].values())
+    assert got["losses"] == {k: v for k, v in ref["losses"].items() if k.startswith(("0:", "1:"))}
