@@ -209,3 +209,98 @@ def test_safe_object_codec_roundtrip_and_no_pickle():
         serial.loads(pickle.dumps({"x": 1}))
     with pytest.raises(TypeError):
         serial.dumps({"f": object()})
+
+
+class _TearingProxy:
+    """A TCP relay that forwards each direction in random 1..2048-byte pieces
+    with random pauses and a few 50 ms stalls: torn reads and stalls on the
+    data plane, never a changed or lost byte."""
+
+    def __init__(self, target_port: int, seed: int = 0):
+        import random
+
+        self.target = target_port
+        self.rng = random.Random(seed)
+        self.lsock = socket.socket()
+        self.lsock.setsockopt(socket.SOL_SOCKET, socket.SO_REUSEADDR, 1)
+        self.lsock.bind(("127.0.0.1", 0))
+        self.lsock.listen(16)
+        self.port = self.lsock.getsockname()[1]
+        self.stop = threading.Event()
+        self.forwarded = 0
+        threading.Thread(target=self._accept, daemon=True).start()
+
+    def _accept(self):
+        import time as _t
+
+        while not self.stop.is_set():
+            try:
+                c, _ = self.lsock.accept()
+            except OSError:
+                return
+            for _ in range(200):  # the target may not listen yet
+                try:
+                    u = socket.create_connection(("127.0.0.1", self.target))
+                    break
+                except OSError:
+                    _t.sleep(0.05)
+            else:
+                c.close()
+                continue
+            for a, b in ((c, u), (u, c)):
+                threading.Thread(target=self._pump, args=(a, b), daemon=True).start()
+
+    def _pump(self, src, dst):
+        import time as _t
+
+        try:
+            while True:
+                data = src.recv(65536)
+                if not data:
+                    break
+                i = 0
+                while i < len(data):
+                    n = self.rng.randint(1, 2048)
+                    dst.sendall(data[i:i + n])
+                    self.forwarded += len(data[i:i + n])
+                    i += n
+                    r = self.rng.random()
+                    if r < 0.002:
+                        _t.sleep(0.05)
+                    elif r < 0.05:
+                        _t.sleep(0.0005)
+            dst.shutdown(socket.SHUT_WR)
+        except OSError:
+            pass
+
+    def close(self):
+        self.stop.set()
+        self.lsock.close()
+
+
+def test_pipeline_through_a_tearing_proxy_is_bitwise(tmp_path, monkeypatch):
+    """Stage 0 reaches stage 1 only through a relay that tears every write
+    into random pieces and stalls at random: frames, fragments, sealed records
+    and the pipeline's losses stay exactly the oracle's."""
+    from elysium_wan_b200.launch.local import run_and_compare
+    from elysium_wan_b200.models.config import make_config
+    from elysium_wan_b200.runtime.spec import JobSpec
+
+    monkeypatch.setenv("ELYSIUM_PEER_KEY", str(tmp_path / "peer.key"))
+    cfg = make_config("toy", n_layer=4, vocab_size=97, d_model=128, n_head=4, seq_len=16,
+                      boundary_dtype="bf16")
+    base = 32000 + (os.getpid() % 200) * 10
+    s1_port = base + 1
+    proxy = _TearingProxy(s1_port, seed=7)
+    try:
+        spec = JobSpec(model=cfg, stages=2, microbatches=4, mb_size=2, steps=2,
+                       out_dir=str(tmp_path), port_base=base + 5, backend="tcp",
+                       wire_codec="planes", p2p_streams=2,
+                       endpoints=[[["127.0.0.1", base, base]],
+                                  [["127.0.0.1", proxy.port, s1_port]]])
+        r = run_and_compare(spec, timeout=300)
+    finally:
+        proxy.close()
+    assert r["ok"], r
+    assert r["compared"] == 8
+    assert proxy.forwarded > 0
