@@ -22,6 +22,8 @@ def _cfg(**kw):
 
 CASES = {
     "chain2": dict(stages=2),
+    # AdamW moments in host memory (streamed through the device on a GPU)
+    "host_adamw_wide_1_2": dict(stages=2, stage_widths=[1, 2], optimizer="adamw-host"),
     # Width-1 stages fold the W of microbatches 2k and 2k + 1 with one GEMM;
     # 5 microbatches leave the last one unpaired; the wide stage does not pair.
     "w_pair_chain3": dict(stages=3, w_pair=True, microbatches=5),
