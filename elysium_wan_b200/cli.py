@@ -128,10 +128,21 @@ def cmd_plan(a) -> int:
     with open(a.fleet) as f:
         d = json.load(f)
     fleet = [NodeInfo.from_caps(n.get("name", f"n{i}"), n) for i, n in enumerate(d.get("nodes", []))]
-    spec = build_spec(d["plan"], d.get("stages"), fleet).finalize()
+    stages = d.get("stages") or d["plan"].get("stages")
+    if stages is None and fleet:
+        # plan mode: depth, widths, layout and microbatches chosen from the fleet
+        from elysium_wan_b200.scheduler.fleetplan import plan_job
+
+        try:
+            spec, rationale = plan_job(d["plan"], fleet)
+        except ValueError as e:
+            print(f"WT_PLAN_REFUSED {json.dumps({'why': str(e)})}")
+            return 1
+    else:
+        spec, rationale = build_spec(d["plan"], stages, fleet).finalize(), None
     with open(a.out, "w") as f:
         f.write(spec.to_json())
-    print(f"WT_PLAN {json.dumps({'stages': spec.stages, 'partition': spec.partition})}")
+    print(f"WT_PLAN {json.dumps({'stages': spec.stages, 'partition': spec.partition, 'stage_widths': spec.stage_widths, 'shard': spec.shard, 'microbatches': spec.microbatches, 'rationale': rationale})}")
     return 0
 
 

@@ -156,6 +156,7 @@ class Coordinator:
         self.link_memory = None
         self.link_results: dict = {}
         self.replies: dict = {}  # (result kind, node id) -> fields
+        self.plan_rationale: dict | None = None
         # rebalance state (per run)
         self.telem: dict = {}          # slot -> deque of this attempt's summaries
         self.telem_all: dict = {}      # slot -> compute ms of every summary of this attempt
@@ -318,10 +319,14 @@ class Coordinator:
     def _spec_for(self, job: Job) -> JobSpec:
         if job.spec is not None:
             return job.spec
-        from elysium_wan_b200.scheduler.fleetplan import build_spec
+        from elysium_wan_b200.scheduler.fleetplan import build_spec, plan_job
 
         with self.lock:
-            fleet = [self.nodes[n].info for n in self.order]
+            fleet = [self.nodes[n].info for n in self.order if not self.nodes[n].dead]
+        if job.stages is None and "stages" not in job.plan:
+            # plan mode: depth, widths, layout and microbatches from the fleet
+            spec, self.plan_rationale = plan_job(job.plan, fleet)
+            return spec
         return build_spec(job.plan, job.stages, fleet)
 
     def _place(self, spec: JobSpec, live: list) -> list:
@@ -391,6 +396,9 @@ class Coordinator:
         spec.links = links
 
     def run_job(self, job: Job) -> RunResult:
+        if job.spec is None and job.stages is None and "stages" not in (job.plan or {}):
+            # plan mode plans on the fleet: let the expected workers register first
+            self.wait_for_workers(max(1, self.cfg.min_workers), self.cfg.wait_workers_s)
         spec = self._spec_for(job)
         cut_given = spec.partition is not None
         spec.zb_mem_mode = spec.zb_mem_mode or self.cfg.zb_mem_mode
@@ -425,7 +433,8 @@ class Coordinator:
         with open(os.path.join(run_dir, "rationale.json"), "w") as f:
             json.dump({"placement": {f"{s[0]}:{s[1]}": self.slot_node[s] for s in slots},
                        "spares": spares, "links": spec.links, "measured_links": measured,
-                       "admission": admission, "schedule": schedule},
+                       "admission": admission, "schedule": schedule,
+                       "plan": self.plan_rationale},
                       f, indent=1)
         heals = restarts = 0
         resume_step = None

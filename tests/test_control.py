@@ -183,3 +183,32 @@ def test_slow_slot_moves_to_a_spare(tmp_path):
     ref.finalize()
     r = compare(run_baseline(ref, "reference"), res.losses_path)
     assert r["ok"] and r["compared"] == 24, r
+
+
+def test_plan_mode_job_through_the_coordinator(tmp_path):
+    """A {plan} job without a stage count: the coordinator plans depth, width
+    and layout from the registered fleet (here: one stage, two ZeRO-1
+    replicas), records the rationale, and the run equals the oracle."""
+    import json
+    import os
+
+    plan = {"preset": "toy", "n_layer": 2, "vocab_size": 97, "d_model": 64, "n_head": 4,
+            "seq_len": 16, "microbatches": 2, "mb_size": 2, "steps": 2, "backend": "gloo"}
+    cl = LocalCluster(str(tmp_path / "cl"), ["r0", "r0"])
+    try:
+        res = cl.run(Job(plan=plan))
+    finally:
+        cl.close()
+    assert res.ok, res.why
+    with open(os.path.join(res.run_dir, "rationale.json")) as f:
+        rat = json.load(f)
+    assert rat["plan"]["depth"]["stages"] == 1 and rat["plan"]["width"]["layout"] == "zero1"
+    with open(os.path.join(res.run_dir, "spec.json")) as f:
+        ran = JobSpec.from_dict(json.load(f))
+    assert ran.stage_widths == [2]
+    ref = JobSpec.from_dict(ran.to_dict())
+    ref.out_dir = str(tmp_path / "oracle")
+    ref.resume, ref.resume_step = False, None
+    ref.finalize()
+    r = compare(run_baseline(ref, "reference"), res.losses_path)
+    assert r["ok"] and r["compared"] == 4, r

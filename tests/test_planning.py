@@ -226,3 +226,40 @@ def test_wide_stage_admission_and_exchange_simulator():
     assert sim["exposed_s"] > 0
     ags = [u for k, u in sim["order"] if k == "ag"]
     assert ags == sorted(ags)
+
+
+def _fleet(n, vram=178, device="cuda:0", cls="b200"):
+    from elysium_wan_b200.resources.node import NodeInfo
+
+    return [NodeInfo(node_id=f"n{i}", name=f"g{i}", device=device, device_class=cls,
+                     vram_gb=vram, tflops_bf16=1400.0 if device.startswith("cuda") else None)
+            for i in range(n)]
+
+
+def test_plan_mode_depth_width_layout_and_microbatches():
+    from elysium_wan_b200.scheduler import admission as ad
+    from elysium_wan_b200.scheduler.fleetplan import plan_job
+
+    # 15.8B on 8 B200s: the fewest stages that hold the state, two ZeRO-1 replicas each
+    spec, rat = plan_job({"preset": "gpt15b"}, _fleet(8))
+    assert spec.stages == 3 and spec.stage_widths == [2, 2, 2] and spec.shard == "zero1"
+    assert rat["width"]["spares"] == 2 and spec.optimizer == "adamw"
+    assert max(rat["depth"]["stage_gib"]) <= rat["depth"]["device_budget_gib"]
+    assert spec.microbatches % 2 == 0 and spec.microbatches >= 2
+    ok, reasons, _ = ad.admit(spec, ad.devices_from_nodes(_fleet(6)))
+    assert ok, [r.text() for r in reasons]
+    # a depth the plan pins is kept
+    spec, rat = plan_job({"preset": "gpt15b", "stages": 8}, _fleet(8))
+    assert spec.stages == 8 and rat["depth"]["given"]
+    # the 0.6B model fits one device: one stage, eight replicas
+    spec, _ = plan_job({"preset": "gpt15b", "n_layer": 20, "d_model": 1536, "n_head": 12},
+                       _fleet(8))
+    assert spec.stages == 1 and spec.stage_widths == [8]
+    # small devices push the moments to the host before giving up
+    spec, rat = plan_job({"preset": "gpt15b", "n_layer": 4, "d_model": 1024, "n_head": 8},
+                         _fleet(1, vram=5))
+    assert spec.optimizer == "adamw-host"
+    with pytest.raises(ValueError, match="no depth"):
+        plan_job({"preset": "gpt15b"}, _fleet(2, vram=8))
+    with pytest.raises(ValueError, match="mixed"):
+        plan_job({"preset": "toy"}, _fleet(1) + _fleet(1, device="cpu", cls="cpu"))
