@@ -157,6 +157,7 @@ class Coordinator:
         self.link_results: dict = {}
         self.replies: dict = {}  # (result kind, node id) -> fields
         self.plan_rationale: dict | None = None
+        self.run_dir: str | None = None
         # rebalance state (per run)
         self.telem: dict = {}          # slot -> deque of this attempt's summaries
         self.telem_all: dict = {}      # slot -> compute ms of every summary of this attempt
@@ -297,6 +298,13 @@ class Coordinator:
                     from elysium_wan_b200.scheduler.rebalance import stage_compute_ms
 
                     self.telem_all.setdefault(slot, []).append(stage_compute_ms(hdr["telem"]))
+                    if self.run_dir:
+                        try:
+                            with open(os.path.join(self.run_dir, "telem_steps.jsonl"), "a") as f:
+                                f.write(json.dumps({"slot": list(slot), "attempt": self.attempt,
+                                                    "telem": hdr["telem"]}) + "\n")
+                        except OSError:
+                            pass
             elif kind in ("PROFILE_RESULT", "FIT_RESULT"):
                 self.replies[(kind, nid)] = {k: v for k, v in hdr.items() if k != "kind"}
             elif kind == "LINK_RESULT":
@@ -406,6 +414,7 @@ class Coordinator:
         self.run_id = time.strftime("%Y%m%d-%H%M%S") + "-" + uuid.uuid4().hex[:6]
         run_dir = os.path.join(self.cfg.state_dir, "runs", self.run_id)
         os.makedirs(run_dir, exist_ok=True)
+        self.run_dir = run_dir
         self.store = ckpt.CheckpointStore(os.path.join(self.cfg.state_dir, "store"))
         live = self.wait_for_workers(max(spec.world_size, self.cfg.min_workers),
                                      self.cfg.wait_workers_s)

@@ -137,7 +137,8 @@ def run_stage(spec, stage: int, peer: int, timeout_s: float = 600.0) -> int:
                 stream.flush()
             _print("WT_METRIC", {"step": step, "mb": mb, "loss": v})
         summary = summarize_step(step, stage, peer, dt * 1e3, eng.op_times_ms(),
-                                 comm.bytes_sent if comm else 0, comm.frames if comm else 0)
+                                 comm.bytes_sent if comm else 0, comm.frames if comm else 0,
+                                 eng.phase_ms().get("opt_ms"))
         _print("WT_TELEM", summary)
         tel.write(json.dumps({"step": step, "events": [[o, m, round(a, 4), round(d, 4)]
                                                         for o, m, a, d in eng.op_times_ms()]})

@@ -1,8 +1,12 @@
 """Per-step telemetry summary (reference: src/wantrain/runtime/telemetry.py:38-98).
 
-WT_TELEM {v, step, rank, peer, step_ms, ops{F,B,W:{n, med_ms}}, busy_ms,
-busy_frac, hops{frames, bytes}} capped at 4096 bytes. Op durations are CUDA
-event times on the compute stream; busy = union of op intervals.
+WT_TELEM {v, step, rank, peer, step_ms, emit_us, ops{F,B,W[,OPT]:{n, med_ms}},
+stall_ms, busy_ms, busy_frac, hops{frames, bytes}, recv{n, med_ms, max_ms}}
+capped at 4096 bytes (the reference's keys; busy_ms / busy_frac are added).
+Op durations are CUDA-event times (host clock on a CPU stage); W on a GPU
+stage is bracketed on the side stream that runs it. busy = union of the op
+intervals; stall_ms = the part of the ops' span with no op running; recv =
+the gaps before F and B ops (each starts once its input has arrived).
 """
 
 from __future__ import annotations
@@ -12,12 +16,24 @@ import os
 import statistics
 
 
-def summarize_step(step, stage, peer, step_ms, op_times, bytes_sent, frames) -> dict:
+def summarize_step(step, stage, peer, step_ms, op_times, bytes_sent, frames,
+                   opt_ms: float | None = None) -> dict:
+    import time as _time
+
+    t_emit = _time.perf_counter()
     ops = {}
     for op in ("F", "B", "W"):
         ds = [d for o, _, _, d in op_times if o == op]
         if ds:
             ops[op] = {"n": len(ds), "med_ms": round(statistics.median(ds), 4)}
+    if opt_ms is not None:
+        ops["OPT"] = {"n": 1, "med_ms": round(float(opt_ms), 4)}
+    # waits for inputs: the gap before each F / B since the previous op ended
+    gaps, last_end = [], None
+    for o, _, s0, d in sorted(op_times, key=lambda x: x[2]):
+        if last_end is not None and o in ("F", "B") and s0 > last_end:
+            gaps.append(s0 - last_end)
+        last_end = s0 + d if last_end is None else max(last_end, s0 + d)
     busy = 0.0
     end = -1.0
     for _, _, s, d in sorted(op_times, key=lambda x: x[2]):
@@ -29,9 +45,13 @@ def summarize_step(step, stage, peer, step_ms, op_times, bytes_sent, frames) -> 
         end = max(end, e)
     span = (max(s + d for _, _, s, d in op_times) - min(s for _, _, s, _ in op_times)) if op_times else 0.0
     out = {"v": 1, "step": step, "rank": stage, "peer": peer, "step_ms": round(step_ms, 3),
-           "ops": ops, "busy_ms": round(busy, 3),
+           "emit_us": 0, "ops": ops, "stall_ms": round(max(0.0, span - busy), 3),
+           "busy_ms": round(busy, 3),
            "busy_frac": round(busy / span, 4) if span > 0 else None,
-           "hops": {"frames": frames, "bytes": bytes_sent}}
+           "hops": {"frames": frames, "bytes": bytes_sent},
+           "recv": {"n": len(gaps), "med_ms": round(statistics.median(gaps), 4) if gaps else 0.0,
+                    "max_ms": round(max(gaps), 4) if gaps else 0.0}}
+    out["emit_us"] = int((_time.perf_counter() - t_emit) * 1e6)
     s = json.dumps(out)
     if len(s) > 4096:
         out.pop("ops")

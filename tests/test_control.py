@@ -68,6 +68,12 @@ def test_cluster_run_matches_oracle(tmp_path):
     with open(os.path.join(res.run_dir, "rationale.json")) as f:
         sched = json.load(f)["schedule"]
     assert sched["source"] == "profiled" and len(sched["costs_ms"]) == 2, sched
+    # every stage's per-step summary, in the reference's WT_TELEM keys, kept in the run dir
+    with open(os.path.join(res.run_dir, "telem_steps.jsonl")) as f:
+        tel = [json.loads(line) for line in f]
+    assert {tuple(t["slot"]) for t in tel} == {(0, 0), (1, 0)} and len(tel) == 6
+    assert {"v", "step", "rank", "peer", "step_ms", "emit_us", "ops", "stall_ms", "hops",
+            "recv"} <= set(tel[0]["telem"])
     ref = JobSpec.from_dict(spec.to_dict())
     ref.out_dir = str(tmp_path / "oracle")
     ref.finalize()
