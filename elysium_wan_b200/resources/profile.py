@@ -49,3 +49,29 @@ def profile_stage(spec, stage: int, device: str = "cpu", reps: int = 3) -> dict:
             ts["B"].append(t2 - t1)
             ts["W"].append(t3 - t2)
     return {k: statistics.median(v) for k, v in ts.items()}
+
+
+def main(argv=None) -> int:
+    """python -m elysium_wan_b200.resources.profile --spec s.json --stage R
+    [--device cuda] [--reps 3]: prints one WT_PROFILE {stage, F, B, W} line
+    (seconds per microbatch)."""
+    import argparse
+    import json
+
+    from elysium_wan_b200.runtime.spec import JobSpec
+
+    ap = argparse.ArgumentParser(prog="profile")
+    ap.add_argument("--spec", required=True)
+    ap.add_argument("--stage", type=int, required=True)
+    ap.add_argument("--device", default="cpu")
+    ap.add_argument("--reps", type=int, default=3)
+    a = ap.parse_args(argv)
+    spec = JobSpec.load(a.spec).finalize()
+    r = profile_stage(spec, a.stage, a.device, a.reps)
+    print("WT_PROFILE " + json.dumps({"stage": a.stage, **{k: round(v, 6) for k, v in r.items()}}),
+          flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -139,6 +139,9 @@ def run_stage(spec, stage: int, peer: int, timeout_s: float = 600.0) -> int:
         summary = summarize_step(step, stage, peer, dt * 1e3, eng.op_times_ms(),
                                  comm.bytes_sent if comm else 0, comm.frames if comm else 0,
                                  eng.phase_ms().get("opt_ms"))
+        if "ops" not in summary:
+            print(f"WT_WARN telemetry summary of step {step} exceeded 4096 bytes: its per-op "
+                  f"medians were dropped", flush=True)
         _print("WT_TELEM", summary)
         tel.write(json.dumps({"step": step, "events": [[o, m, round(a, 4), round(d, 4)]
                                                         for o, m, a, d in eng.op_times_ms()]})
