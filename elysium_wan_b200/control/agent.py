@@ -93,7 +93,8 @@ class WorkerAgent:
                  probe_port: int | None = None):
         host, _, port = coordinator.rpartition(":")
         self.addr = (host or "127.0.0.1", int(port))
-        self.coordinator_id = coordinator_id
+        # the coordinator this agent trusts: the flag, else $WANTRAIN_COORD_ID
+        self.coordinator_id = coordinator_id or os.environ.get("WANTRAIN_COORD_ID", "")
         self.token = token if token is not None else os.environ.get("WANTRAIN_COORD_TOKEN", "")
         self.name = name or f"worker-{os.getpid()}"
         self.workdir = os.path.abspath(workdir)
@@ -123,6 +124,10 @@ class WorkerAgent:
         from elysium_wan_b200.resources.probe import measure
 
         caps = measure(self.device, bench=not self.no_bench)
+        if os.environ.get("WANTRAIN_DEVICE_CLASS"):
+            # an operator-chosen device class (e.g. an architecture class for a
+            # fleet of different boards that compute alike)
+            caps["device_class"] = os.environ["WANTRAIN_DEVICE_CLASS"]
         caps.update(self.declare)
         caps.update(name=self.name, region=self.region, host=self.advertise_host,
                     wan_profile=self.wan_profile, pid=os.getpid(), probe_port=self.probe_port)

@@ -46,8 +46,9 @@ def peer_id(pub_bytes: bytes) -> str:
 
 
 def default_key_path() -> str:
-    return os.environ.get("ELYSIUM_PEER_KEY",
-                          os.path.join(os.path.expanduser("~"), ".elysium", "peer_key"))
+    """ELYSIUM_PEER_KEY, or the reference's WANTRAIN_PEER_KEY, else ~/.elysium/peer_key."""
+    return os.environ.get("ELYSIUM_PEER_KEY") or os.environ.get(
+        "WANTRAIN_PEER_KEY", os.path.join(os.path.expanduser("~"), ".elysium", "peer_key"))
 
 
 def load_or_create_key(path: str | None = None) -> Ed25519PrivateKey:
