@@ -46,7 +46,8 @@ def cmd_coordinator(a) -> int:
                             zb_mem_mode=a.zb_mem_mode, replacement_match=a.replacement_match,
                             max_heals=a.max_heals, keep_workers=a.keep_workers,
                             profile=not a.no_profile,
-                            recut=not a.no_recut, recut_min_gain=a.recut_min_gain,
+                            recut=not a.no_recut, replan=not a.no_replan,
+                            recut_min_gain=a.recut_min_gain,
                             recut_cost_s=a.recut_cost_s, max_replans=a.max_replans,
                             watch_slow=not a.no_watch_slow, slow_ratio=a.slow_ratio,
                             slow_runs=a.slow_runs)
@@ -248,6 +249,8 @@ def build_parser() -> argparse.ArgumentParser:
     c.add_argument("--no-profile", action="store_true",
                    help="keep the analytic schedule (no F/B/W profile of the slots before launch)")
     c.add_argument("--no-recut", action="store_true", help="never re-cut from telemetry")
+    c.add_argument("--no-replan", action="store_true",
+                   help="never re-solve the zero-bubble order from telemetry")
     c.add_argument("--recut-min-gain", type=float, default=0.05)
     c.add_argument("--recut-cost-s", type=float, default=60.0)
     c.add_argument("--max-replans", type=int, default=2)

@@ -32,6 +32,10 @@ and its message kinds:
     remaining steps beats `recut_cost_s`: ABORT, convert the common wave to
     the new cut through the logical form (fault_tolerance/logical.py) under a
     new tag, RESTORE every slot, relaunch.
+  * re-plan (`_reschedule_plan`, reference :2194 via zero_bubble.replan):
+    when no re-cut pays, the zero-bubble order is re-solved from the same
+    measured costs and the run relaunches from the wave with it (the cut and
+    the ownership stay, so no bit changes).
   * slow slot (`_watch_slow`, reference :2406): a slot whose compute per
     microbatch stays above `slow_ratio` x its own baseline for `slow_runs`
     summaries is healed onto a spare, or, with none, re-cut away from.
@@ -90,6 +94,9 @@ class CoordinatorConfig:
     recut_cost_s: float = 60.0        # what a re-cut costs (abort, convert, relaunch)
     max_replans: int = 2
     replan_min_summaries: int = 4     # per slot, in the current attempt
+    replan: bool = True               # re-solve the zero-bubble order from telemetry
+    replan_min_gain: float = 0.10     # a re-solved order must be this much shorter ...
+    replan_cost_s: float = 30.0       # ... and save twice this over the remaining steps
     telem_window: int = 8
     watch_slow: bool = True
     slow_ratio: float = 1.3
@@ -497,6 +504,14 @@ class Coordinator:
                     resume_step = self._resume_point(spec)
                 else:
                     spec, resume_step = got
+            elif verdict.kind == "reschedule":
+                spec, note = self._next[1]
+                resume_step = self._resume_point(spec)
+                rec = {"step": resume_step, "reschedule": True, "note": note}
+                self.replans.append(rec)
+                self.events.append(("reschedule", None, rec))
+                with open(os.path.join(run_dir, "spec.json"), "w") as f:
+                    f.write(spec.to_json())
             elif verdict.kind == "slow_heal":
                 slot = verdict.slot
                 with self.lock:
@@ -522,7 +537,7 @@ class Coordinator:
             json.dump({"ok": res.ok, "run_id": res.run_id, "attempts": res.attempts, "heals": res.heals,
                        "restarts": res.restarts, "why": res.why, "losses": res.losses_path,
                        "events": [list(map(str, e)) for e in self.events
-                                  if e[0] in ("heal", "restart", "recut")],
+                                  if e[0] in ("heal", "restart", "recut", "reschedule")],
                        "replans": self.replans},
                       f, indent=1)
         return res
@@ -632,7 +647,8 @@ class Coordinator:
     def _maybe_rebalance(self, spec):
         """Once per new common wave: ("recut", (new spec, note)) when the
         measured stage costs call for another cut and it pays, else None."""
-        if not self.cfg.recut or os.environ.get("WANTRAIN_RECUT", "on") == "off":
+        recut = self.cfg.recut and os.environ.get("WANTRAIN_RECUT", "on") != "off"
+        if not (recut or self.cfg.replan):
             return None
         if len(self.replans) >= self.cfg.max_replans or self.store is None:
             return None
@@ -647,7 +663,40 @@ class Coordinator:
         if step is None or step <= self.replan_checked or step >= final:
             return None
         self.replan_checked = step
-        return self._recut_plan(spec, windows, step, final)
+        got = self._recut_plan(spec, windows, step, final) if recut else None
+        if got is None and self.cfg.replan:
+            got = self._reschedule_plan(spec, windows, step, final)
+        return got
+
+    def _reschedule_plan(self, spec, windows, step, final):
+        """The order half of a re-plan: the zero-bubble order re-solved from the
+        window's measured F / B / W (the cut and the ownership stay, so no bit
+        changes), applied when it is `replan_min_gain` shorter and saves more
+        than twice `replan_cost_s` over the remaining steps."""
+        from elysium_wan_b200.scheduler import rebalance as rb
+
+        try:
+            profiles = rb.profiles_from_telemetry(spec, windows)
+            res = rb.replan_schedule(spec, profiles, self.cfg.replan_min_gain)
+        except ValueError as e:
+            self.events.append(("reschedule_skipped", None, {"step": step, "why": str(e)}))
+            return None
+        if res is None:
+            return None
+        order, cur, new = res
+        cost = float(os.environ.get("WANTRAIN_REPLAN_COST_S", self.cfg.replan_cost_s))
+        gain = (cur - new) * max(0, final - step)
+        note = (f"re-solved order: {cur * 1e3:.1f} -> {new * 1e3:.1f} ms per step predicted, "
+                f"{gain:.1f} s over {final - step} steps against 2 x {cost:.1f} s")
+        self.events.append(("reschedule_eval", None, {"step": step, "note": note}))
+        if gain <= 2 * cost:
+            return None
+        d = spec.to_dict()
+        d.update(schedule_order=order, stage_costs=rb.stage_costs_from_profiles(
+            profiles, spec.peer_weights), resume=False, resume_step=None)
+        nspec = JobSpec.from_dict(d)
+        nspec.finalize()
+        return "reschedule", (nspec, note)
 
     def _recut_plan(self, spec, windows, step, final, why: str | None = None):
         from elysium_wan_b200.scheduler import rebalance as rb
@@ -811,8 +860,8 @@ class Coordinator:
             if nxt is not None:
                 self._next = nxt
                 kind, payload = nxt
-                if kind == "recut":
-                    return Verdict("recut", None, payload[1])
+                if kind in ("recut", "reschedule"):
+                    return Verdict(kind, None, payload[1])
                 return Verdict("slow_heal", payload[0], payload[1])
             if time.time() - t_start > self.cfg.job_timeout_s:
                 from elysium_wan_b200.fault_tolerance.liveness import Verdict

@@ -122,3 +122,42 @@ def slow_slots(hist: dict, base: dict, ratio: float = 1.3, runs: int = 3) -> lis
         if b and tail and all(x > ratio * b for x in tail):
             out.append((slot, round(xs[-1] / b, 3)))
     return out
+
+
+def stage_costs_from_profiles(profiles: list, peer_weights: list | None = None) -> list:
+    """[F, B, W] seconds per stage: each peer's measured ops weighted by its
+    share of the stage's microbatches (its ownership weight)."""
+    out = []
+    for r, row in enumerate(profiles):
+        wr = (peer_weights[r] if peer_weights else None) or [1.0] * len(row)
+        tot = sum(wr)
+        out.append([sum(p[k] * w for p, w in zip(row, wr)) / tot / len(row)
+                    for k in ("t_f", "t_b", "t_w")])
+    return out
+
+
+def replan_schedule(spec, profiles: list, min_gain: float = 0.10):
+    """Re-solve the zero-bubble order from measured costs (reference:
+    scheduler/zero_bubble.py:1079 `replan`, its order half). Ownership and
+    the cut stay, so the run's bits do not change. -> (new schedule_order,
+    predicted s/step now, predicted after) when the new order is at least
+    `min_gain` shorter under the same measured costs, else None."""
+    import copy
+
+    from elysium_wan_b200.scheduler.planner import default_schedule, zb_config
+    from elysium_wan_b200.scheduler.zero_bubble import simulate_slots
+
+    s2 = copy.deepcopy(spec)
+    s2.stage_costs = stage_costs_from_profiles(profiles, spec.peer_weights)
+    cfg = zb_config(s2)
+
+    def makespan(order):
+        slots = [[[(op, int(mb)) for op, mb in o] for o in per_stage] for per_stage in order]
+        return simulate_slots(cfg, slots, spec.peer_weights)[1]
+
+    cur = makespan(spec.schedule_order)
+    new_order = default_schedule(s2)
+    new = makespan(new_order)
+    if new > (1.0 - min_gain) * cur:
+        return None
+    return new_order, cur, new

@@ -123,7 +123,8 @@ def test_recut_from_telemetry_matches_oracle(tmp_path):
     spec = JobSpec(model=cfg, stages=2, microbatches=2, mb_size=2, steps=10, backend="gloo",
                    tag="rc", ckpt_every=2, partition=[[0, 4], [4, 8]])
     cl = LocalCluster(str(tmp_path / "cl"), ["r0", "r0"],
-                      coord=dict(recut_cost_s=0.0, replan_min_summaries=2, watch_slow=False),
+                      coord=dict(recut_cost_s=0.0, replan_min_summaries=2, watch_slow=False,
+                                 replan=False),
                       worker_env={"WANTRAIN_SIM_SLOW": "1:6"})
     try:
         res = cl.run(Job(spec=spec))
@@ -177,7 +178,7 @@ def test_slow_slot_moves_to_a_spare(tmp_path):
     spec = JobSpec(model=cfg, stages=2, microbatches=2, mb_size=2, steps=20, backend="gloo",
                    tag="slow", ckpt_every=2, partition=[[0, 2], [2, 4]])
     cl = LocalCluster(str(tmp_path / "cl"), ["r0", "r0", "r0"],
-                      coord=dict(recut=False, slow_runs=3, slow_ratio=2.0),
+                      coord=dict(recut=False, replan=False, slow_runs=3, slow_ratio=2.0),
                       worker_env={"WANTRAIN_SIM_SLOW": "1:20@5"})
     try:
         res = cl.run(Job(spec=spec))
@@ -220,3 +221,33 @@ def test_plan_mode_job_through_the_coordinator(tmp_path):
     ref.finalize()
     r = compare(run_baseline(ref, "reference"), res.losses_path)
     assert r["ok"] and r["compared"] == 4, r
+
+
+def test_reschedule_from_telemetry_matches_oracle(tmp_path):
+    """A job launched with a GPipe-like order (all F, then all B, then all W):
+    at a common wave the coordinator re-solves the zero-bubble order from the
+    measured F / B / W, relaunches from the wave with it, and the losses stay
+    the oracle's (an order never changes a bit)."""
+    cfg = make_config("toy", n_layer=4, vocab_size=97, d_model=64, n_head=4, seq_len=16)
+    M, S = 6, 3
+    naive = [[[["F", m] for m in range(M)] + [["B", m] for m in range(M)]
+              + [["W", m] for m in range(M)]] for _ in range(S)]
+    spec = JobSpec(model=cfg, stages=S, microbatches=M, mb_size=1, steps=10, backend="gloo",
+                   tag="rs", ckpt_every=2, partition=[[0, 2], [2, 4], [4, 6]],
+                   schedule_order=naive)
+    cl = LocalCluster(str(tmp_path / "cl"), ["r0", "r0", "r0"],
+                      coord=dict(profile=False, recut=False, watch_slow=False,
+                                 replan_cost_s=0.0, replan_min_gain=0.02,
+                                 replan_min_summaries=2))
+    try:
+        res = cl.run(Job(spec=spec))
+        replans = list(cl.coord.replans)
+    finally:
+        cl.close()
+    assert res.ok, res.why
+    assert replans and replans[0].get("reschedule"), replans
+    ref = JobSpec.from_dict(spec.to_dict())
+    ref.out_dir = str(tmp_path / "oracle")
+    ref.finalize()
+    r = compare(run_baseline(ref, "reference"), res.losses_path)
+    assert r["ok"] and r["compared"] == M * 10, r
