@@ -26,7 +26,6 @@ send, a host->device copy after the receive).
 from __future__ import annotations
 
 import collections
-import os
 import queue
 import socket
 import threading
