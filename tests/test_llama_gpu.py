@@ -8,7 +8,6 @@ wrong pair, position or sign, the SwiGLU derivative were wrong, or the GPU
 model diverged from the CPU restatement beyond bf16 rounding.
 """
 
-import math
 
 import pytest
 import torch
