@@ -5,8 +5,9 @@ dials the coordinator, answers the CHALLENGE with an HMAC'd HELLO carrying its
 measured capabilities, heartbeats every second, and supervises one stage
 subprocess (`python -m elysium_wan_b200.runtime.stage_main`). It turns the
 stage's WT_* stdout markers into PROGRESS / TELEM_STEP messages, ships every
-checkpoint wave to the coordinator (CKPT, files with sha256), reports EXIT
-{rc, done_marker, log tail} and, from the last stage, RESULT {losses}. It
+checkpoint wave to the coordinator (CKPT, files with sha256), ships the stage's
+per-step telemetry file (TELEMETRY) and reports EXIT {rc, done_marker, log
+tail} and, from the last stage, RESULT {losses}. It
 obeys ABORT (kill the stage's process group), RESTORE (write shipped wave
 files), RELEASE and SHUTDOWN, and reconnects with backoff when the control
 connection drops.
@@ -297,9 +298,18 @@ class WorkerAgent:
         rc = proc.wait()
         if self.stage is not proc:
             return
+        spec = a["spec"]
+        tel = os.path.join(a["dir"], f"{spec['tag']}_rank{a['stage']}p{a['peer']}_telemetry.jsonl")
+        if os.path.exists(tel) and self.ch is not None:
+            # the stage's per-step telemetry file, whole, before EXIT so the
+            # coordinator has it when it sees the stage finish (reference:
+            # worker/agent.py:1053-1067)
+            try:
+                self.ch.send_file("TELEMETRY", tel, run_id=a["run_id"], attempt=a["attempt"])
+            except OSError:
+                pass
         self.send("EXIT", rc=rc, done_marker=proc.done_marker, tail="\n".join(proc.tail[-20:]),
                   run_id=a["run_id"], attempt=a["attempt"], stage=a["stage"], peer=a["peer"])
-        spec = a["spec"]
         if rc == 0 and a["stage"] == spec["stages"] - 1:
             p = os.path.join(a["dir"], f"{spec['tag']}_losses_r{a['stage']}p{a['peer']}.json")
             if os.path.exists(p):

@@ -295,6 +295,18 @@ class Coordinator:
                     self.store.stage_part(rel, body)
                     if hdr.get("last"):
                         self.store.commit_staged(os.path.dirname(rel))
+            elif kind == "TELEMETRY" and slot is not None and current and self.run_dir:
+                # rank and peer come from the connection's slot, never from the
+                # message (reference: coordinator/coordinator.py:594-604)
+                if hashlib.sha256(body).hexdigest() == hdr.get("sha256"):
+                    r, q = slot
+                    path = os.path.join(self.run_dir, f"telemetry_r{r}p{q}_a{self.attempt}.jsonl")
+                    try:
+                        with open(path + ".part", "wb") as f:
+                            f.write(body)
+                        os.replace(path + ".part", path)
+                    except OSError:
+                        pass
             elif kind == "TELEM_STEP":
                 self.events.append(("telem", nid, hdr.get("telem")))
                 if slot is not None and current and isinstance(hdr.get("telem"), dict):

@@ -74,6 +74,12 @@ def test_cluster_run_matches_oracle(tmp_path):
     assert {tuple(t["slot"]) for t in tel} == {(0, 0), (1, 0)} and len(tel) == 6
     assert {"v", "step", "rank", "peer", "step_ms", "emit_us", "ops", "stall_ms", "hops",
             "recv"} <= set(tel[0]["telem"])
+    # each stage's whole telemetry file, shipped as TELEMETRY when it exits and
+    # named by the connection's slot
+    for r, q in ((0, 0), (1, 0)):
+        with open(os.path.join(res.run_dir, f"telemetry_r{r}p{q}_a0.jsonl")) as f:
+            rows = [json.loads(line) for line in f if line.strip()]
+        assert [x["step"] for x in rows] == [0, 1, 2] and all(x["events"] for x in rows), rows
     ref = JobSpec.from_dict(spec.to_dict())
     ref.out_dir = str(tmp_path / "oracle")
     ref.finalize()
