@@ -4,7 +4,8 @@ Reference: WorkerAgent (src/wantrain/worker/agent.py:403-1301). The agent
 dials the coordinator, answers the CHALLENGE with an HMAC'd HELLO carrying its
 measured capabilities, heartbeats every second, and supervises one stage
 subprocess (`python -m elysium_wan_b200.runtime.stage_main`). It turns the
-stage's WT_* stdout markers into PROGRESS / TELEM_STEP messages, ships every
+stage's WT_* stdout markers into PROGRESS / TELEM_STEP messages, answers
+PROBE (a row of the link matrix) and MEASURE (one path in full), ships every
 checkpoint wave to the coordinator (CKPT, files with sha256), ships the stage's
 per-step telemetry file (TELEMETRY) and reports EXIT {rc, done_marker, log
 tail} and, from the last stage, RESULT {losses}. It
@@ -103,6 +104,10 @@ class WorkerAgent:
         self.device = device
         self.region = region
         self.wan_profile = wan_profile
+        from elysium_wan_b200.resources.links import load_emulation
+
+        # the region-pair link model this worker's probes are shaped by (WAN emulation)
+        self.emu = load_emulation(region, wan_profile)
         self.declare = declare or {}
         self.no_bench = no_bench
         self.advertise_host = advertise_host
@@ -199,25 +204,47 @@ class WorkerAgent:
             handler(hdr, body)
 
     def _on_probe(self, hdr, body):
-        self.send("PROBE_RESULT", caps=self._caps())
+        """PROBE {targets: [[host, port, region], ...], self_index}: one row of
+        the coordinator's probe matrix (round trip and upload rate to every
+        other worker, shaped by this worker's WAN emulation). Without targets:
+        this worker's capabilities again. Runs in a thread: the control
+        channel keeps serving (heartbeats) meanwhile."""
+        if "targets" not in hdr:
+            self.send("PROBE_RESULT", caps=self._caps())
+            return
+        from elysium_wan_b200.resources.links import probe_row
+
+        def run():
+            try:
+                row = probe_row(hdr["targets"], int(hdr["self_index"]),
+                                secs=float(hdr.get("secs", 0.25)), flows=int(hdr.get("flows", 1)),
+                                emu=self.emu)
+                self.send("PROBE_RESULT", ok=True, row=row)
+            except Exception as e:
+                self.send("PROBE_RESULT", ok=False, why=repr(e))
+
+        threading.Thread(target=run, daemon=True).start()
 
     def _on_measure(self, hdr, body):
-        from elysium_wan_b200.resources.probe import measure
+        """MEASURE {host, port, region, target}: the full measurement of one
+        path to another worker's probe server (round trip, up, down, both at
+        once, duplex). Without a host: this device's capabilities with the
+        matmul bench."""
+        if "host" not in hdr:
+            from elysium_wan_b200.resources.probe import measure
 
-        self.send("MEASURE_RESULT", caps=measure(self.device, bench=True))
-
-    def _on_link_probe(self, hdr, body):
-        """Measure the path to another worker's probe server (in a thread: the
-        control channel keeps serving meanwhile)."""
+            self.send("MEASURE_RESULT", caps=measure(self.device, bench=True))
+            return
         from elysium_wan_b200.resources.links import measure_pair
 
         def run():
             try:
                 r = measure_pair(hdr["host"], int(hdr["port"]), flows=int(hdr.get("flows", 2)),
-                                 secs=float(hdr.get("secs", 0.5)))
-                self.send("LINK_RESULT", ok=True, target=hdr.get("target"), **r)
+                                 secs=float(hdr.get("secs", 0.5)), emu=self.emu,
+                                 region=hdr.get("region"))
+                self.send("MEASURE_RESULT", ok=True, target=hdr.get("target"), **r)
             except Exception as e:
-                self.send("LINK_RESULT", ok=False, target=hdr.get("target"), why=repr(e))
+                self.send("MEASURE_RESULT", ok=False, target=hdr.get("target"), why=repr(e))
 
         threading.Thread(target=run, daemon=True).start()
 
@@ -337,8 +364,11 @@ class WorkerAgent:
             self.send("RESTORE_ACK", ok=True, rel=hdr["rel"])
 
     def _on_release(self, hdr, body):
+        """RELEASE {run_id}: the job is over; stop any stage and drop the
+        assignment, so this worker is idle for the next job."""
         self._kill_stage()
-        self.send("RELEASE_ACK", ok=True)
+        self.assign = None
+        self.send("RELEASE_ACK", ok=True, run_id=hdr.get("run_id"))
 
     def _on_shutdown(self, hdr, body):
         self._kill_stage()

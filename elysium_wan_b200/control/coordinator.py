@@ -12,6 +12,13 @@ and its message kinds:
     (scheduler/fleetplan.py). Workers are placed in rank order grouped by
     region; the rest are spares. Hops between regions get the worker's WAN
     link profile (the CPU/gloo configuration emulates it in the transport).
+  * route (PROBE, MEASURE; with probing on): each worker in turn measures a
+    row of the link matrix (round trip and upload rate to every other
+    worker); a chain of 3+ single-peer stages is ordered through it for the
+    fastest slowest hop, then the least total round trip
+    (scheduler/routing.py). Each chosen hop is then measured in full; a hop
+    far below its probe re-routes with the measured figures (reference
+    :813-950). The matrix and the order go to rationale.json.
   * profile (PROFILE): every slot times F, B and W of one microbatch on its
     own node; the zero-bubble schedule and the peers' ownership weights are
     solved from those costs, and a cut the job did not pin is refined by the
@@ -40,7 +47,8 @@ and its message kinds:
     microbatch stays above `slow_ratio` x its own baseline for `slow_runs`
     summaries is healed onto a spare, or, with none, re-cut away from.
   * complete: RESULT losses of the last stage -> runs/<id>/losses.json and
-    result.json.
+    result.json; every slot's worker gets RELEASE (idle for the next job) and
+    its stage's telemetry file arrives as TELEMETRY before its EXIT.
 """
 
 from __future__ import annotations
@@ -49,6 +57,7 @@ import collections
 import copy
 import hashlib
 import json
+import math
 import os
 import socket
 import statistics
@@ -74,6 +83,9 @@ class CoordinatorConfig:
     max_heals: int = 3
     max_restarts: int = 2
     no_probe: bool = True
+    route: bool = True     # with probing on: order a chain of 3+ workers through the probe matrix
+    probe_secs: float = 0.25  # upload seconds per pair in a probe-matrix row
+    probe_disagree: float = 0.5  # a full measurement below this x its probe re-routes
     no_fit_check: bool = True
     profile: bool = True   # measure F/B/W per slot before launch and solve the schedule from them
     profile_timeout_s: float = 300.0
@@ -324,9 +336,9 @@ class Coordinator:
                                                     "telem": hdr["telem"]}) + "\n")
                         except OSError:
                             pass
-            elif kind in ("PROFILE_RESULT", "FIT_RESULT"):
+            elif kind in ("PROFILE_RESULT", "FIT_RESULT", "PROBE_RESULT", "RELEASE_ACK"):
                 self.replies[(kind, nid)] = {k: v for k, v in hdr.items() if k != "kind"}
-            elif kind == "LINK_RESULT":
+            elif kind == "MEASURE_RESULT" and "target" in hdr:
                 self.link_results[(nid, hdr.get("target"))] = {k: v for k, v in hdr.items()
                                                               if k != "kind"}
             else:
@@ -392,7 +404,8 @@ class Coordinator:
             port = bi.caps.get("probe_port")
             if not port:
                 continue
-            self.nodes[a].ch.send("LINK_PROBE", host=bi.host, port=int(port), target=b)
+            self.nodes[a].ch.send("MEASURE", host=bi.host, port=int(port), region=bi.region,
+                                  target=b)
             asked.append((j, a, b))
         out = {}
         end = time.time() + timeout
@@ -408,6 +421,94 @@ class Coordinator:
                                                  self.run_id or "probe")
                 out[f"{j}->{j + 1}"] = r
         return out
+
+    def _probe_matrix(self, nids: list, timeout: float = 60.0):
+        """(rtt, bw) over `nids`, symmetric: each worker in turn measures its
+        round trip and upload rate to every other one's probe server (one row
+        at a time: concurrent bulk probes would measure each other), then each
+        pair takes its slower direction (reference: coordinator.py:813-857).
+        None when a worker has no probe server or a row does not come back."""
+        from elysium_wan_b200.scheduler.routing import symmetrize
+
+        infos = [self.nodes[n].info for n in nids]
+        if not all(i.caps.get("probe_port") for i in infos):
+            return None
+        targets = [[i.host, int(i.caps["probe_port"]), i.region] for i in infos]
+        rtt, bw = [], []
+        for k, nid in enumerate(nids):
+            with self.lock:
+                self.replies.pop(("PROBE_RESULT", nid), None)
+            self.nodes[nid].ch.send("PROBE", targets=targets, self_index=k,
+                                    secs=self.cfg.probe_secs)
+            end = time.time() + timeout
+            while ("PROBE_RESULT", nid) not in self.replies and time.time() < end:
+                time.sleep(0.05)
+            r = self.replies.get(("PROBE_RESULT", nid))
+            if not r or not r.get("ok"):
+                return None
+            rtt.append(r["row"]["rtt_ms"])
+            bw.append(r["row"]["bw_mbps"])
+        return symmetrize(rtt, bw)
+
+    def _route_chain(self, spec: JobSpec, live: list):
+        """Order the chain's workers through the probed link matrix (max
+        bottleneck rate, then min total round trip; scheduler/routing.py).
+        Only a chain of single-peer stages over three or more workers is
+        routed, and only an order clearly better than the placement's
+        (`route_gain`) replaces it. -> (live, note or None)."""
+        from elysium_wan_b200.scheduler.routing import chain_key, order_chain, route_gain
+
+        n = spec.world_size
+        if spec.stages < 3 or n != spec.stages or len(live) < n:
+            return live, None
+        chosen = live[:n]
+        m = self._probe_matrix(chosen)
+        if m is None:
+            return live, None
+        rtt, bw = m
+        order = order_chain(rtt, bw)
+        ident = list(range(n))
+        moved = order != ident and route_gain(ident, order, bw, rtt)
+        note = {"probe_bw_mbps": [[None if not math.isfinite(x) else round(x, 1) for x in row]
+                                  for row in bw],
+                "probe_rtt_ms": [[None if not math.isfinite(x) else round(x, 3) for x in row]
+                                 for row in rtt],
+                "placed": [self.nodes[x].info.name for x in chosen],
+                "order": [self.nodes[chosen[i]].info.name for i in (order if moved else ident)],
+                "bottleneck_mbps": chain_key(order if moved else ident, bw, rtt)[0],
+                "rerouted": moved, "matrix": (rtt, bw), "nids": chosen}
+        if moved:
+            live = [chosen[i] for i in order] + live[n:]
+        return live, note
+
+    def _reroute_on_disagreement(self, spec: JobSpec, route: dict, measured: dict):
+        """A hop whose full measurement is far below its probe (the probe was
+        misled: a burst allowance, a shaper that kicks in late) re-routes the
+        chain with the measured figures in the matrix (reference:
+        coordinator.py:871-920). -> the new order (indices into the routed
+        workers), or None when nothing changes."""
+        from elysium_wan_b200.scheduler.routing import order_chain, route_gain
+
+        rtt, bw = route["matrix"]
+        chosen = route["nids"]
+        cur = [chosen.index(self.slot_node[(j, 0)]) for j in range(spec.stages)]
+        misled = False
+        for j in range(spec.stages - 1):
+            h = measured.get(f"{j}->{j + 1}")
+            if h is None:
+                continue
+            a, b = cur[j], cur[j + 1]
+            got = min(h["up_mbps"], h["down_mbps"])
+            if bw[a][b] > 0 and got < self.cfg.probe_disagree * bw[a][b]:
+                misled = True
+            bw[a][b] = bw[b][a] = got
+            rtt[a][b] = rtt[b][a] = h["rtt_ms"]
+        if not misled:
+            return None
+        order = order_chain(rtt, bw)
+        if order == cur or not route_gain(cur, order, bw, rtt):
+            return None
+        return order
 
     def _links(self, spec: JobSpec):
         links = []
@@ -440,8 +541,24 @@ class Coordinator:
         live = self._place(spec, live)
         slots = spec.slots()
         self.slot_node = {s: live[i] for i, s in enumerate(slots)}
-        spares = live[len(slots):]
+        route = None
+        if not self.cfg.no_probe and self.cfg.route:
+            live, route = self._route_chain(spec, live)
+            self.slot_node = {s: live[i] for i, s in enumerate(slots)}
         measured = {} if self.cfg.no_probe else self._probe_links(spec)
+        for _ in range(2):  # a misled probe re-routes (twice at most), then re-measures
+            order = None if route is None else self._reroute_on_disagreement(spec, route, measured)
+            if order is None:
+                break
+            live = [route["nids"][i] for i in order] + live[spec.world_size:]
+            self.slot_node = {s: live[i] for i, s in enumerate(slots)}
+            route.update(order=[self.nodes[x].info.name for x in live[:spec.world_size]],
+                         rerouted=True, remeasured=route.get("remeasured", 0) + 1)
+            measured = self._probe_links(spec)
+        spares = live[len(slots):]
+        if route is not None:
+            route.pop("matrix", None)
+            route.pop("nids", None)
         self._links(spec)
         spec.finalize()
         schedule = None
@@ -461,7 +578,7 @@ class Coordinator:
         with open(os.path.join(run_dir, "rationale.json"), "w") as f:
             json.dump({"placement": {f"{s[0]}:{s[1]}": self.slot_node[s] for s in slots},
                        "spares": spares, "links": spec.links, "measured_links": measured,
-                       "admission": admission, "schedule": schedule,
+                       "admission": admission, "schedule": schedule, "route": route,
                        "plan": self.plan_rationale},
                       f, indent=1)
         heals = restarts = 0
@@ -545,14 +662,36 @@ class Coordinator:
                 res = RunResult(False, self.run_id, None, self.attempt + 1, heals, restarts, why, run_dir)
                 break
             self.attempt += 1
+        released = self._release_all()
         with open(os.path.join(run_dir, "result.json"), "w") as f:
             json.dump({"ok": res.ok, "run_id": res.run_id, "attempts": res.attempts, "heals": res.heals,
                        "restarts": res.restarts, "why": res.why, "losses": res.losses_path,
                        "events": [list(map(str, e)) for e in self.events
                                   if e[0] in ("heal", "restart", "recut", "reschedule")],
-                       "replans": self.replans},
+                       "replans": self.replans, "released": released},
                       f, indent=1)
         return res
+
+    def _release_all(self, timeout: float = 10.0) -> list:
+        """RELEASE every worker that held a slot (its stage is stopped and its
+        assignment dropped, so it is idle for the next job; reference:
+        coordinator.py:1895-1905). -> names of the workers that acknowledged."""
+        with self.lock:
+            nids = [n for n in dict.fromkeys(self.slot_node.values())
+                    if self.nodes[n].connected and not self.nodes[n].dead]
+            for n in nids:
+                self.replies.pop(("RELEASE_ACK", n), None)
+        asked = []
+        for n in nids:
+            try:
+                self.nodes[n].ch.send("RELEASE", run_id=self.run_id)
+                asked.append(n)
+            except OSError:
+                pass
+        end = time.time() + timeout
+        while time.time() < end and not all(("RELEASE_ACK", n) in self.replies for n in asked):
+            time.sleep(0.05)
+        return [self.nodes[n].info.name for n in asked if ("RELEASE_ACK", n) in self.replies]
 
     def _ask_slots(self, kind: str, result: str, spec, slots, timeout: float) -> dict:
         """Send `kind` (PROFILE / FIT) for every slot to its node at once and

@@ -160,13 +160,19 @@ def classify_duplex(up: float, down: float, both: float) -> str:
 
 
 def measure_pair(host: str, port: int, flows: int = 4, secs: float = 1.0,
-                 timeout: float = 5.0) -> dict:
-    """{rtt_ms, up_mbps, down_mbps, both_mbps, duplex} to an echo server."""
+                 timeout: float = 5.0, emu: Emulation | None = None,
+                 region: str | None = None) -> dict:
+    """{rtt_ms, up_mbps, down_mbps, both_mbps, duplex} to an echo server
+    (shaped by `emu` toward `region` when an emulation is given)."""
     r = rtt_ms(host, port, timeout=timeout)
     up = _rate([lambda o, i: _up(host, port, secs, o, i, timeout)] * flows, secs)
     down = _rate([lambda o, i: _down(host, port, secs, o, i, timeout)] * flows, secs)
     both = _rate([lambda o, i: _up(host, port, secs, o, i, timeout)] * flows
                  + [lambda o, i: _down(host, port, secs, o, i, timeout)] * flows, secs)
+    if emu is not None and emu.enabled:
+        r, up = emu.shape(region, r, up)
+        _, down = emu.shape(region, r, down)
+        _, both = emu.shape(region, r, both)
     return {"rtt_ms": round(r, 3), "up_mbps": round(up, 1), "down_mbps": round(down, 1),
             "both_mbps": round(both, 1), "duplex": classify_duplex(up, down, both),
             "flows": flows}
@@ -199,15 +205,89 @@ class Link:
 
 @dataclass
 class Emulation:
-    """Experiment regions: this node's region and the (rtt, rate) to others."""
+    """Experiment regions: this node's region and the (rtt, rate) to others.
+
+    `links` maps another region to {"rtt_ms", "mbps"}. A worker's
+    `--wan-profile` file uses the reference's region-pair form instead
+    ({"intra": {...}, "inter": {...}, "pairs": {"A|B": {...}}}, reference:
+    src/wantrain/resources/links.py:44-66); `from_profile` reads it. A rate of
+    0 means not shaped."""
 
     region: str
     links: dict = field(default_factory=dict)  # region -> {"rtt_ms", "mbps"}
     enabled: bool = True
     default: Link = field(default_factory=lambda: Link(0.0, 0.0))
+    pairs: dict = field(default_factory=dict)  # "A|B" (sorted) -> {"rtt_ms", "mbps"}
+    intra: Link | None = None
+
+    @staticmethod
+    def from_profile(region: str, prof: dict | None) -> "Emulation":
+        prof = prof or {}
+
+        def link(d):
+            return Link(float(d.get("rtt_ms", 0.0)), float(d.get("mbps", 0.0)))
+
+        return Emulation(region, enabled=bool(prof),
+                         default=link(prof.get("inter") or {}),
+                         pairs=dict(prof.get("pairs") or {}),
+                         intra=link(prof["intra"]) if prof.get("intra") else None)
 
     def link_to(self, region: str) -> Link:
+        ent = self.pairs.get("|".join(sorted((self.region or "", region or ""))))
+        if ent is not None:
+            return Link(float(ent.get("rtt_ms", 0.0)), float(ent.get("mbps", 0.0)))
         if region == self.region:
-            return Link(0.0, 0.0)
+            return self.intra or Link(0.0, 0.0)
         ent = self.links.get(region)
         return Link(float(ent["rtt_ms"]), float(ent["mbps"])) if ent else self.default
+
+    def shape(self, region: str, rtt: float, mbps: float) -> tuple[float, float]:
+        """A measured (rtt, rate) as the emulated path would show it: the
+        round trip at least the emulated one, the rate at most the emulated one."""
+        lk = self.link_to(region)
+        return max(rtt, lk.rtt_ms), (min(mbps, lk.mbps) if lk.mbps > 0 else mbps)
+
+
+def load_emulation(region: str, wan_profile: str | None) -> Emulation | None:
+    """A worker's `--wan-profile`: a path to the JSON region-pair model, or the
+    JSON itself. None when there is none."""
+    import json
+    import os
+
+    if not wan_profile:
+        return None
+    s = wan_profile.strip()
+    if not s.startswith("{"):
+        if not os.path.exists(s):
+            return None
+        with open(s) as f:
+            s = f.read()
+    return Emulation.from_profile(region, json.loads(s))
+
+
+def probe_row(targets: list, self_index: int, secs: float = 0.25, flows: int = 1,
+              emu: Emulation | None = None, timeout: float = 5.0) -> dict:
+    """One row of the probe matrix: this node's round trip and upload rate to
+    every target [host, port, region]. Unreachable targets give None; the own
+    index gives rtt 0 and rate None (reference: the PROBE request,
+    src/wantrain/worker/agent.py:649-658)."""
+    rtts, rates = [], []
+    for j, t in enumerate(targets):
+        host, port = t[0], int(t[1])
+        region = t[2] if len(t) > 2 else None
+        if j == self_index:
+            rtts.append(0.0)
+            rates.append(None)
+            continue
+        try:
+            r = rtt_ms(host, port, n=5, timeout=timeout)
+            b = _rate([lambda o, i: _up(host, port, secs, o, i, timeout)] * flows, secs)
+        except OSError:
+            rtts.append(None)
+            rates.append(None)
+            continue
+        if emu is not None and emu.enabled:
+            r, b = emu.shape(region, r, b)
+        rtts.append(round(r, 3))
+        rates.append(round(b, 1))
+    return {"rtt_ms": rtts, "bw_mbps": rates}

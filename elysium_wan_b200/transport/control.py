@@ -9,7 +9,7 @@ mac gets REJECT and the connection is closed. The token comes from --token or
 WANTRAIN_COORD_TOKEN.
 
 Message kinds (public surface):
-  agent -> coordinator: HELLO, HEARTBEAT, PROGRESS, TELEM_STEP, EXIT, CKPT,
+  agent -> coordinator: HELLO, HEARTBEAT, PROGRESS, TELEM_STEP, TELEMETRY, EXIT, CKPT,
                         RESULT, *_ACK, *_RESULT
   coordinator -> agent: CHALLENGE, WELCOME, REJECT, ASSIGN, PROFILE, FIT,
                         MEASURE, PROBE, ABORT, RESTORE, RELEASE, SHUTDOWN

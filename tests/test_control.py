@@ -74,6 +74,9 @@ def test_cluster_run_matches_oracle(tmp_path):
     assert {tuple(t["slot"]) for t in tel} == {(0, 0), (1, 0)} and len(tel) == 6
     assert {"v", "step", "rank", "peer", "step_ms", "emit_us", "ops", "stall_ms", "hops",
             "recv"} <= set(tel[0]["telem"])
+    # both workers were released at the end (idle for the next job)
+    with open(os.path.join(res.run_dir, "result.json")) as f:
+        assert sorted(json.load(f)["released"]) == ["w0", "w1"]
     # each stage's whole telemetry file, shipped as TELEMETRY when it exits and
     # named by the connection's slot
     for r, q in ((0, 0), (1, 0)):
@@ -112,6 +115,49 @@ def test_coordinator_probes_pipeline_hops_into_link_memory(tmp_path):
         got = co._probe_links(spec, timeout=30)
         assert "0->1" in got and got["0->1"]["rtt_ms"] > 0
         assert co.link_memory.path("127.0.0.1", "127.0.0.1") is not None
+    finally:
+        for a in agents:
+            a.stop.set()
+        co.stop()
+        _t.sleep(0.2)
+
+
+def test_coordinator_routes_the_chain_around_a_slow_pair(tmp_path):
+    """Three workers in regions a, b, c whose emulated a-b path is 5 Mbps: the
+    probe matrix shows it, the chain is ordered a-c-b (no slow hop), and a
+    full measurement far below its probe re-routes with the measured rate."""
+    import json as _json
+    import threading
+    import time as _t
+
+    from elysium_wan_b200.control.agent import WorkerAgent
+    from elysium_wan_b200.control.coordinator import Coordinator, CoordinatorConfig
+
+    prof = _json.dumps({"pairs": {"a|b": {"mbps": 5, "rtt_ms": 60}}})
+    co = Coordinator(port=0, cfg=CoordinatorConfig(state_dir=str(tmp_path / "co"), no_probe=False,
+                                                   probe_secs=0.05))
+    co.start()
+    agents = [WorkerAgent(f"127.0.0.1:{co.port}", name=f"w{i}", workdir=str(tmp_path / f"w{i}"),
+                          region=r, wan_profile=prof, probe_port=0)
+              for i, r in enumerate("abc")]
+    for a in agents:
+        threading.Thread(target=a.run, daemon=True).start()
+    try:
+        live = sorted(co.wait_for_workers(3, 30), key=lambda n: co.nodes[n].info.name)
+        spec = JobSpec(model=make_config("toy", n_layer=3), stages=3, microbatches=3,
+                       mb_size=1).finalize()
+        got, note = co._route_chain(spec, live)
+        assert note["rerouted"] and note["order"] == ["w0", "w2", "w1"], note
+        assert note["probe_bw_mbps"][0][1] <= 5.0 and note["bottleneck_mbps"] > 5.0
+        assert [co.nodes[n].info.name for n in got] == ["w0", "w2", "w1"]
+        # a hop whose full measurement is far below its probe re-routes
+        co.slot_node = {(j, 0): got[j] for j in range(3)}
+        fake = {"0->1": {"up_mbps": 1.0, "down_mbps": 1.0, "rtt_ms": 300.0},
+                "1->2": {"up_mbps": 1e4, "down_mbps": 1e4, "rtt_ms": 0.1}}
+        order = co._reroute_on_disagreement(spec, note, fake)
+        assert order is not None and order != [0, 2, 1]
+        assert co._reroute_on_disagreement(
+            spec, note, {"0->1": {"up_mbps": 1e9, "down_mbps": 1e9, "rtt_ms": 0.1}}) is None
     finally:
         for a in agents:
             a.stop.set()

@@ -263,3 +263,64 @@ def test_plan_mode_depth_width_layout_and_microbatches():
         plan_job({"preset": "gpt15b"}, _fleet(2, vram=8))
     with pytest.raises(ValueError, match="mixed"):
         plan_job({"preset": "toy"}, _fleet(1) + _fleet(1, device="cpu", cls="cpu"))
+
+
+def test_chain_routing_is_exact_and_routes_around_slow_pairs():
+    """order_chain equals brute force over every ordering on random matrices
+    (bottleneck first, then total RTT); best_chain reports 0 when no order
+    connects every node; the heuristic beyond EXACT_MAX returns a valid order
+    no worse than the identity; route_gain ignores noise."""
+    import itertools
+    import random
+
+    from elysium_wan_b200.scheduler import routing as R
+
+    rng = random.Random(7)
+    for _ in range(150):
+        n = rng.randint(3, 7)
+        bw = [[0.0] * n for _ in range(n)]
+        rtt = [[0.0] * n for _ in range(n)]
+        for i in range(n):
+            for j in range(i + 1, n):
+                bw[i][j] = bw[j][i] = rng.choice([0, 10, 50, 100, 100, 500, 1000])
+                rtt[i][j] = rtt[j][i] = rng.choice([1, 5, 20, 80, 150])
+        got = R.order_chain(rtt, bw)
+        assert sorted(got) == list(range(n)) and got[0] < got[-1]
+        best = max(R.chain_key(list(p), bw, rtt) for p in itertools.permutations(range(n)))
+        assert R.chain_key(got, bw, rtt) == best
+    # a slow a-b pair: the chain goes a-c-b
+    assert R.best_chain(3, [(0, 1, 5), (1, 2, 900), (0, 2, 800)]) == ([0, 2, 1], 800.0)
+    assert R.best_chain(4, [(0, 1, 100), (1, 2, 100)])[1] == 0.0
+    # one direction unreachable: symmetrize takes the slower direction
+    r2, b2 = R.symmetrize([[0, 1], [None, 0]], [[None, 100], [50, None]])
+    assert b2[0][1] == b2[1][0] == 50 and r2[0][1] == float("inf")
+    n = R.EXACT_MAX + 3
+    bw = [[0.0] * n for _ in range(n)]
+    for i in range(n):
+        for j in range(i + 1, n):
+            bw[i][j] = bw[j][i] = rng.choice([10, 100, 1000])
+    got = R.order_chain(None, bw)
+    assert sorted(got) == list(range(n))
+    assert R.chain_key(got, bw) >= R.chain_key(list(range(n)), bw)
+    bw3 = [[0, 100, 100], [100, 0, 105], [100, 105, 0]]
+    assert not R.route_gain([0, 1, 2], [0, 2, 1], bw3, None)
+    assert R.route_gain([0, 1, 2], [0, 2, 1], [[0, 5, 100], [5, 0, 100], [100, 100, 0]], None)
+
+
+def test_emulation_profile_shapes_probes():
+    from elysium_wan_b200.resources import links
+
+    em = links.Emulation.from_profile("a", {"inter": {"mbps": 100, "rtt_ms": 40},
+                                            "intra": {"mbps": 0, "rtt_ms": 1},
+                                            "pairs": {"a|b": {"mbps": 5, "rtt_ms": 200}}})
+    assert em.shape("b", 0.2, 9000.0) == (200.0, 5.0)
+    assert em.shape("c", 0.2, 9000.0) == (40.0, 100.0)
+    assert em.shape("a", 0.2, 9000.0) == (1.0, 9000.0)  # rate 0: not shaped
+    srv, port = links.serve_echo("127.0.0.1", 0)
+    try:
+        row = links.probe_row([["127.0.0.1", port, "a"], ["127.0.0.1", port, "b"]], 0,
+                              secs=0.05, emu=em)
+    finally:
+        srv.shutdown()
+    assert row["rtt_ms"][0] == 0.0 and row["bw_mbps"][0] is None
+    assert row["rtt_ms"][1] >= 200.0 and row["bw_mbps"][1] <= 5.0
