@@ -265,13 +265,18 @@ def build_parser() -> argparse.ArgumentParser:
     w.add_argument("--advertise-host", default="127.0.0.1")
     w.add_argument("--data-port", type=int, default=29000)
     w.add_argument("--listen-port", type=int, default=None)
-    w.add_argument("--probe-port", type=int, default=None)
+    w.add_argument("--probe-port", type=int, default=None,
+                   help="serve link probes on this port (the coordinator's probe matrix and "
+                        "chain routing need one on every worker)")
     w.add_argument("--probe-listen-port", type=int, default=None)
     w.add_argument("--name", default=None)
     w.add_argument("--workdir", default="worker")
     w.add_argument("--device", default="cpu")
     w.add_argument("--region", default="default")
-    w.add_argument("--wan-profile", default=None)
+    w.add_argument("--wan-profile", default=None,
+                   help="region-pair link model for this worker's probes: a JSON file (or the "
+                        "JSON itself) {\"intra\": {...}, \"inter\": {...}, \"pairs\": "
+                        "{\"A|B\": {\"mbps\": .., \"rtt_ms\": ..}}}")
     w.add_argument("--declare", default=None)
     w.add_argument("--no-bench", action="store_true")
     w.set_defaults(fn=cmd_worker)
