@@ -167,6 +167,12 @@ def run_stage(spec, stage: int, peer: int, timeout_s: float = 600.0) -> int:
     if eng.last:
         with open(loss_path(spec, stage, peer), "w") as f:
             json.dump({"losses": loss_records(eng.losses)}, f, indent=1)
+        if spec.stage_widths[-1] == 1:
+            # a single last peer also writes the reference's file name
+            # (src/wantrain/runtime/stage.py:3558-3571); wide last stages are
+            # merged by the launcher or the coordinator
+            with open(os.path.join(spec.out_dir, f"{spec.tag}_losses.json"), "w") as f:
+                json.dump({"losses": loss_records(eng.losses)}, f, indent=1)
     if comm is not None:
         comm.close()
     if spec.world_size > 1:
