@@ -28,7 +28,7 @@ class LocalCluster:
     def __init__(self, workdir: str, regions: list, token: str = "demo-token", device: str = "cpu",
                  wan_links: dict | None = None, liveness: dict | None = None, max_heals: int = 3,
                  stage_timeout_s: float = 30.0, coord: dict | None = None,
-                 worker_env: dict | None = None):
+                 worker_env: dict | None = None, worker_args: list | None = None):
         self.workdir = os.path.abspath(workdir)
         os.makedirs(self.workdir, exist_ok=True)
         cfg = CoordinatorConfig(state_dir=os.path.join(self.workdir, "coordinator"), token=token,
@@ -42,7 +42,8 @@ class LocalCluster:
         env = dict(os.environ)
         env["PYTHONPATH"] = ROOT + os.pathsep + env.get("PYTHONPATH", "")
         env["WANTRAIN_COORD_TOKEN"] = token
-        # worker_env: extra variables for every worker, or a list with one dict per worker
+        # worker_env: extra variables for every worker, or a list with one dict per worker;
+        # worker_args: one list of extra `wantrain worker` flags per worker
         per = worker_env if isinstance(worker_env, list) else [worker_env or {}] * len(regions)
         for i, region in enumerate(regions):
             name = f"w{i}"
@@ -50,7 +51,7 @@ class LocalCluster:
             cmd = [sys.executable, "-m", "elysium_wan_b200", "worker", "--coordinator",
                    f"127.0.0.1:{self.coord.port}", "--coordinator-id", self.coord.id, "--name", name,
                    "--workdir", os.path.join(self.workdir, name), "--device", device, "--region",
-                   region, "--no-bench"]
+                   region, "--no-bench"] + list((worker_args or [[]] * len(regions))[i])
             p = subprocess.Popen(cmd, stdout=log, stderr=subprocess.STDOUT, env={**env, **per[i]},
                                  start_new_session=True)
             self.workers.append((name, p, log))

@@ -165,6 +165,40 @@ def test_coordinator_routes_the_chain_around_a_slow_pair(tmp_path):
         _t.sleep(0.2)
 
 
+def test_routed_job_matches_oracle(tmp_path):
+    """A 3-stage job over workers in regions a, b, c with probe servers and an
+    emulated 5 Mbps a-b path: the coordinator's probe matrix routes the chain
+    a-c-b, measures each chosen hop in full, and the losses still equal the
+    single-device oracle bit for bit (placement never changes a bit)."""
+    import json
+    import os
+
+    prof = json.dumps({"pairs": {"a|b": {"mbps": 5, "rtt_ms": 60}}})
+    cfg = make_config("toy", n_layer=3, vocab_size=97, d_model=64, n_head=4, seq_len=16)
+    spec = JobSpec(model=cfg, stages=3, microbatches=3, mb_size=2, steps=2, backend="gloo",
+                   tag="rt")
+    cl = LocalCluster(str(tmp_path / "cl"), ["a", "b", "c"],
+                      coord=dict(no_probe=False, probe_secs=0.05, profile=False),
+                      worker_args=[["--probe-port", "0", "--wan-profile", prof]] * 3)
+    try:
+        res = cl.run(Job(spec=spec))
+    finally:
+        cl.close()
+    assert res.ok, res.why
+    with open(os.path.join(res.run_dir, "rationale.json")) as f:
+        rat = json.load(f)
+    route = rat["route"]
+    # the a-b pair is never a hop: w2 (region c) sits in the middle
+    assert route["order"][1] == "w2" and route["bottleneck_mbps"] > 5.0, route
+    assert route["rerouted"] == (route["placed"][1] != "w2"), route
+    assert set(rat["measured_links"]) == {"0->1", "1->2"}
+    ref = JobSpec.from_dict(spec.to_dict())
+    ref.out_dir = str(tmp_path / "oracle")
+    ref.finalize()
+    r = compare(run_baseline(ref, "reference"), res.losses_path)
+    assert r["ok"] and r["compared"] == 6, r
+
+
 def test_recut_from_telemetry_matches_oracle(tmp_path):
     """Stage 1 runs 6x slower (the timing-only seam moves when, never what):
     at a common wave the coordinator re-cuts the chain toward stage 0 from the
