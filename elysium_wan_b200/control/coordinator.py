@@ -481,6 +481,24 @@ class Coordinator:
             live = [chosen[i] for i in order] + live[n:]
         return live, note
 
+    def _memory_order(self, spec: JobSpec, live: list) -> list:
+        """An unrouted chain on cards of different memory: the rank that needs
+        the most (live activation graphs, the embedding on rank 0, logits and
+        head on the last) takes the largest card (reference:
+        coordinator.py:1023-1026 via placement.memory_order). Equal cards keep
+        the placement's order."""
+        from elysium_wan_b200.scheduler.placement import memory_order
+
+        n = spec.world_size
+        infos = [self.nodes[x].info for x in live[:n]]
+        mems = [i.memory_bytes() for i in infos]
+        if len(infos) < n or not all(mems) or min(mems) == max(mems):
+            return live
+        mo = memory_order(spec, infos)
+        if mo is None:
+            return live
+        return [live[i] for i in mo] + live[n:]
+
     def _reroute_on_disagreement(self, spec: JobSpec, route: dict, measured: dict):
         """A hop whose full measurement is far below its probe (the probe was
         misled: a burst allowance, a shaper that kicks in late) re-routes the
@@ -544,6 +562,9 @@ class Coordinator:
         route = None
         if not self.cfg.no_probe and self.cfg.route:
             live, route = self._route_chain(spec, live)
+            self.slot_node = {s: live[i] for i, s in enumerate(slots)}
+        if route is None and spec.stages > 1 and spec.world_size == spec.stages:
+            live = self._memory_order(spec, live)
             self.slot_node = {s: live[i] for i, s in enumerate(slots)}
         measured = {} if self.cfg.no_probe else self._probe_links(spec)
         for _ in range(2):  # a misled probe re-routes (twice at most), then re-measures

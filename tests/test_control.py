@@ -337,3 +337,30 @@ def test_reschedule_from_telemetry_matches_oracle(tmp_path):
     ref.finalize()
     r = compare(run_baseline(ref, "reference"), res.losses_path)
     assert r["ok"] and r["compared"] == M * 10, r
+
+
+def test_unrouted_chain_gives_the_hungriest_rank_the_largest_card(tmp_path):
+    """Without probing, a chain on cards of different memory is ordered so the
+    rank needing the most memory gets the largest card; equal cards keep the
+    placement's order."""
+    from elysium_wan_b200.control.coordinator import Coordinator, CoordinatorConfig, _Node
+    from elysium_wan_b200.resources.node import NodeInfo
+    from elysium_wan_b200.scheduler.placement import rank_memory_weights
+
+    co = Coordinator(port=0, cfg=CoordinatorConfig(state_dir=str(tmp_path / "co")))
+    try:
+        spec = JobSpec(model=make_config("toy", n_layer=4), stages=3, microbatches=3,
+                       mb_size=1).finalize()
+        need = rank_memory_weights(spec)
+        for k, gb in enumerate([40, 180, 80]):
+            co.nodes[f"n{k}"] = _Node(NodeInfo.from_caps(f"n{k}", {"vram_gb": gb}), None)
+        live = ["n0", "n1", "n2"]
+        got = co._memory_order(spec, live)
+        mem = {"n0": 40, "n1": 180, "n2": 80}
+        hungriest = max(range(3), key=lambda r: (need[r], -r))
+        assert mem[got[hungriest]] == 180, (need, got)
+        for k in range(3):
+            co.nodes[f"n{k}"] = _Node(NodeInfo.from_caps(f"n{k}", {"vram_gb": 80}), None)
+        assert co._memory_order(spec, live) == live
+    finally:
+        co.nodes.clear()  # never started: no socket, and the fake nodes have no channel
