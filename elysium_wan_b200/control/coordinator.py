@@ -404,8 +404,11 @@ class Coordinator:
             port = bi.caps.get("probe_port")
             if not port:
                 continue
+            # measured with the data plane's own flow count: a hop's rate over
+            # one flow says little about `p2p_streams` flows (reference:
+            # coordinator.py:1013-1017)
             self.nodes[a].ch.send("MEASURE", host=bi.host, port=int(port), region=bi.region,
-                                  target=b)
+                                  target=b, flows=max(1, int(spec.p2p_streams or 1)))
             asked.append((j, a, b))
         out = {}
         end = time.time() + timeout
@@ -422,7 +425,7 @@ class Coordinator:
                 out[f"{j}->{j + 1}"] = r
         return out
 
-    def _probe_matrix(self, nids: list, timeout: float = 60.0):
+    def _probe_matrix(self, nids: list, timeout: float = 60.0, flows: int = 1):
         """(rtt, bw) over `nids`, symmetric: each worker in turn measures its
         round trip and upload rate to every other one's probe server (one row
         at a time: concurrent bulk probes would measure each other), then each
@@ -439,7 +442,7 @@ class Coordinator:
             with self.lock:
                 self.replies.pop(("PROBE_RESULT", nid), None)
             self.nodes[nid].ch.send("PROBE", targets=targets, self_index=k,
-                                    secs=self.cfg.probe_secs)
+                                    secs=self.cfg.probe_secs, flows=flows)
             end = time.time() + timeout
             while ("PROBE_RESULT", nid) not in self.replies and time.time() < end:
                 time.sleep(0.05)
@@ -462,7 +465,7 @@ class Coordinator:
         if spec.stages < 3 or n != spec.stages or len(live) < n:
             return live, None
         chosen = live[:n]
-        m = self._probe_matrix(chosen)
+        m = self._probe_matrix(chosen, flows=max(1, int(spec.p2p_streams or 1)))
         if m is None:
             return live, None
         rtt, bw = m
