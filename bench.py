@@ -102,72 +102,118 @@ class ClockSampler:
                 "samples": len(mhz)}
 
 
+# model preset, microbatches x sequences per step, pipeline
+# depth at 8 GPUs (the rest of the GPUs are ZeRO-1 replicas of each stage).
+CONFIGS = {
+    "15.8b": dict(model="gpt15b", microbatches=64, mb_size=1, stages=None, recompute=None,
+                  metric=METRIC, shape="48L d5120 40h MLP20480 seq2048 vocab50257, fp8 e4m3 1x128 boundaries"),
+    "0.6b": dict(model="gpt0_6b", microbatches=16, mb_size=4, stages=2, recompute=None,
+                 metric="tokens/s (max over ranks) 0.6B GPT PP x ZeRO-1",
+                 shape="20L d1536 12h MLP6144 seq2048 vocab50257, bf16 boundaries"),
+    "2.8b": dict(model="gpt2_8b", microbatches=32, mb_size=2, stages=4, recompute=None,
+                 metric="tokens/s (max over ranks) 2.8B GPT PP x ZeRO-1",
+                 shape="32L d2560 32h MLP10240 seq2048 vocab50257, bf16 boundaries"),
+    "25.1b": dict(model="gpt25b", microbatches=32, mb_size=1, stages=4, recompute=True,
+                  metric="tokens/s (max over ranks) 25.1B GPT PP x ZeRO-1",
+                  shape="60L d5888 46h MLP23552 seq2048 vocab50257, fp8 e4m3 1x128 boundaries, recompute"),
+}
+
+
+def layout(args, n: int) -> list:
+    """Stage widths for N GPUs: --widths when given, else the config's depth
+    (capped by N) with the remaining GPUs as ZeRO-1 replicas of every stage."""
+    if args.widths:
+        w = [int(x) for x in args.widths.split(",")]
+        if sum(w) != n:
+            raise SystemExit(f"--widths {args.widths} uses {sum(w)} GPUs, not {n}")
+        return w
+    depth = CONFIGS[args.config]["stages"]
+    if depth is None:
+        return [1] * n
+    stages = min(depth, n)
+    if n % stages:
+        raise SystemExit(f"{n} GPUs do not split into {stages} stages of equal width")
+    return [n // stages] * stages
+
+
+def _numel(cfg, a: int, b: int) -> int:
+    from elysium_wan_b200.models.gpt import entry_specs
+
+    tot = 0
+    for e in range(a, b):
+        for s in entry_specs(cfg, e):
+            k = 1
+            for x in s.shape:
+                k *= x
+            tot += k
+    return tot
+
+
 def plan_spec(args, n: int, free_bytes: float | None):
-    """The 15.8B spec at N stages, with the per-stage memory plan."""
+    """The benchmark spec on N GPUs, with the per-slot memory plan."""
     from elysium_wan_b200.models.config import make_config
     from elysium_wan_b200.runtime.spec import JobSpec
     from elysium_wan_b200.scheduler import partition as part
 
     over = {"n_layer": args.n_layer} if getattr(args, "n_layer", None) else {}
     cfg = make_config(args.model, **over)
-    spec = JobSpec(model=cfg, stages=n, microbatches=args.microbatches, mb_size=args.mb_size,
-                   steps=args.warmup + args.steps, device="cuda", backend="nccl",
-                   init_seed=1234, data_seed=5678, lr=1e-4, out_dir=tempfile.gettempdir(),
-                   tag="bench")
-    spec.partition = part.even_blocks_partition(cfg, n)
-    # Largest stage decides the plan (all ranks must agree on the spec).
-    from elysium_wan_b200.models.gpt import entry_specs
-
-    def numel(stage):
-        a, b = spec.partition[stage]
-        tot = 0
-        for e in range(a, b):
-            for s in entry_specs(cfg, e):
-                k = 1
-                for x in s.shape:
-                    k *= x
-                tot += k
-        return tot
-
-    biggest = max(numel(r) for r in range(n))
+    widths = layout(args, n)
+    stages = len(widths)
+    spec = JobSpec(model=cfg, stages=stages, stage_widths=widths, microbatches=args.microbatches,
+                   mb_size=args.mb_size, steps=args.warmup + args.steps, device="cuda",
+                   backend="nccl", grad_sync=args.grad_sync, init_seed=1234, data_seed=5678,
+                   lr=1e-4, out_dir=tempfile.gettempdir(), tag="bench")
+    # Cost-aware contiguous cut (exact min-max DP over the per-entry FLOP
+    # model: block h(72h + 12s), head 6hV, embedding 3h).
+    spec.partition = part.proportional_partition(cfg, [float(w) for w in widths])
+    # Largest slot decides the plan (all ranks must agree on the spec).
+    biggest = max(_numel(cfg, a, b) for a, b in spec.partition)
+    wmin = min(widths)
     cap = free_bytes if free_bytes else 178 * GiB
-    resident = biggest * (4 + 4 + 2)
-    host_adam = resident + 8 * biggest > 0.80 * cap
+    # fp32 master + fp32 gradient + bf16 working copy on every replica; a
+    # replica of a wide stage also holds the fused path's fp32 exchange slots
+    # (one stage-sized buffer) and its shard of the moments.
+    resident = biggest * (4 + 4 + 2) + (4 * biggest if wmin > 1 else 0)
+    moments = 8 * biggest / wmin
+    host_adam = resident + moments > 0.80 * cap
     spec.optimizer = "adamw-host" if host_adam else "adamw"
     # With the moments on the device the activations fill what is left; keep a
     # tenth of the device free on top of the 8 GiB so the caching allocator
     # does not run into its retry path near the cap (seen at 2 stages:
     # 168.5 of 178 GiB, 18 retries per step).
     slack = 8 * GiB + (0 if host_adam else 0.10 * cap)
-    budget = cap - resident - (0 if host_adam else 8 * biggest) - slack
-    spec.stage_widths = [1] * n
-    # Stages of at most 12 layers fold the weight gradients of microbatch pairs
-    # with one GEMM each (their W ops are deferred and memory is ample); one
-    # device runs W inline in B, and 24-layer stages are short of memory, where
-    # pairing would hold one more microbatch's W inputs (~0.34 GB per layer).
+    budget = cap - resident - (0 if host_adam else moments) - slack
+    # Width-1 stages of at most 12 layers fold the weight gradients of
+    # microbatch pairs with one GEMM each (their W ops are deferred and memory
+    # is ample); one device runs W inline in B, and 24-layer stages are short of
+    # memory, where pairing would hold one more microbatch's W inputs.
     blocks = max(sum(1 for e in range(a, b) if 1 <= e <= cfg.n_layer) for a, b in spec.partition)
-    spec.w_pair = n > 1 and blocks <= 12 and not getattr(args, "no_w_pair", False)
+    spec.w_pair = stages > 1 and wmin == 1 and blocks <= 12 and not getattr(args, "no_w_pair", False)
     from elysium_wan_b200.scheduler.planner import stage_memory_model
 
-    spec.peer_weights = [[1.0]] * n
-    spec.recompute = False
+    spec.peer_weights = [[1.0] * w for w in widths]
+    forced = CONFIGS[args.config]["recompute"]
+    spec.recompute = bool(forced)
     if n == 1:
         # Single device: F, B, W per microbatch (W inline in B); recompute if one
         # microbatch's activations do not fit.
-        f, _, _ = stage_memory_model(spec, 0)
-        spec.recompute = f > budget
+        if not forced:
+            f, _, _ = stage_memory_model(spec, 0)
+            spec.recompute = f > budget
+        spec.mb_owner = [[0] * spec.microbatches]
         spec.schedule_order = [[sum(([["F", mb], ["B", mb], ["W", mb]]
                                      for mb in range(spec.microbatches)), [])]]
     else:
         from elysium_wan_b200.scheduler.planner import default_schedule
 
         spec.zb_mem_mode = "auto"
-        spec.mb_owner = [[0] * spec.microbatches for _ in range(n)]
+        spec.mb_owner = None
+        spec.finalize()  # ownership (IWRR over each stage's replicas)
         try:
-            spec.schedule_order = default_schedule(spec, [budget] * n)
+            spec.schedule_order = default_schedule(spec, [budget] * stages)
         except ValueError:  # one microbatch does not fit without recompute
             spec.recompute = True
-            spec.schedule_order = default_schedule(spec, [budget] * n)
+            spec.schedule_order = default_schedule(spec, [budget] * stages)
     spec.finalize()
     return spec
 
@@ -198,9 +244,10 @@ def run_ours(args) -> dict | None:
     os.environ.setdefault("EWB_W_STREAM", "0" if spec.optimizer == "adamw-host" else "1")
     setup_determinism(spec.init_seed)
     init_group(spec, rank, timeout_s=float(os.environ.get("EWB_PG_TIMEOUT_S", "600")))
-    eng = StageEngine(spec, rank, 0, None, dev)
+    stage, peer = spec.slot_of(rank)
+    eng = StageEngine(spec, stage, peer, None, dev)
     eng.warm_kernels()
-    comm = PipeComm(spec, rank, 0, dev) if world > 1 else None
+    comm = PipeComm(spec, stage, peer, dev) if world > 1 else None
     eng.attach_comm(comm)
     torch.cuda.synchronize()
 
@@ -280,15 +327,21 @@ def run_ours(args) -> dict | None:
     value = tokens * args.steps / (dev_ms / 1e3)
     e2e = tokens * args.steps / (wall_ms / 1e3)
     h2d = spec.microbatches * spec.mb_size * spec.model.seq_len * 8 * 2
+    conf = CONFIGS[args.config]
+    widths = spec.stage_widths
+    par = f"pp{spec.stages}" + (f"xdp{widths[0]}" if len(set(widths)) == 1 and widths[0] > 1
+                                else ("" if max(widths) == 1 else " widths " + ",".join(map(str, widths))))
     return {
-        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": n,
+        "metric": conf["metric"], "value": round(value, 1), "unit": "tokens/s", "n_gpus": n,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 3),
         "higher_is_better": True, "scaling": "strong",
         "vs_baseline": round(value / BASELINE_TOK_S, 3), "dtype": "bf16",
         "data": "synthetic (seeded uniform token ids, random-init weights)",
-        "config": {"model": f"{args.model} (48L d5120 40h MLP20480 seq2048 vocab50257, fp8 e4m3 1x128 boundaries)",
+        "config": {"model": f"{args.model} ({conf['shape']})",
                    "global_batch": spec.microbatches * spec.mb_size, "seq_len": spec.model.seq_len,
-                   "parallelism": f"pp{n}", "microbatches": spec.microbatches,
+                   "parallelism": par, "partition": spec.partition,
+                   "grad_sync": spec.grad_sync if max(widths) > 1 else None,
+                   "microbatches": spec.microbatches,
                    "schedule": "zero-bubble", "optimizer": spec.optimizer,
                    "recompute": spec.recompute, "w_pair": spec.w_pair,
                    "l2": "working set larger than L2 (no flush)"},
@@ -304,6 +357,7 @@ def run_ours(args) -> dict | None:
 def run_reference(args) -> dict:
     from elysium_wan_b200.utils.refbench import run_reference_arm
 
+    args.ref_widths = layout(args, args.gpus)
     return run_reference_arm(args)
 
 
@@ -313,9 +367,15 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--model", default="gpt15b")
-    ap.add_argument("--microbatches", type=int, default=64)
-    ap.add_argument("--mb-size", type=int, default=1)
+    ap.add_argument("--config", default="15.8b", choices=sorted(CONFIGS),
+                    help="BASELINE config (the headline is 15.8b)")
+    ap.add_argument("--widths", default=None,
+                    help="comma-separated replicas per stage (default: the config's layout)")
+    ap.add_argument("--grad-sync", default="fused", choices=["fused", "nccl"],
+                    help="ZeRO-1 gradient/parameter exchange of wide stages: fused into the "
+                         "kernels over NVLink peer memory, or NCCL collectives")
+    ap.add_argument("--microbatches", type=int, default=None)
+    ap.add_argument("--mb-size", type=int, default=None)
     # Diagnostics only (profiling on a shallower model of the same width): a
     # line printed with it is marked "diagnostic" and is not the benchmark.
     ap.add_argument("--n-layer", type=int, default=None)
@@ -324,12 +384,22 @@ def main(argv=None):
     args = ap.parse_args(argv)
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
+    conf = CONFIGS[args.config]
+    args.model = conf["model"]
+    args.metric = conf["metric"]
+    reduced = args.microbatches not in (None, conf["microbatches"]) or \
+        args.mb_size not in (None, conf["mb_size"])
+    args.microbatches = args.microbatches or conf["microbatches"]
+    args.mb_size = args.mb_size or conf["mb_size"]
+    ref_model = {"15.8b": "gpt15b", "0.6b": "gpt0p6b", "2.8b": "gpt2p8b", "25.1b": "gpt25b"}
+    args.ref_model = ref_model[args.config]
+    args.widths_list = [int(x) for x in args.widths.split(",")] if args.widths else None
     if args.impl == "reference":
         out = run_reference(args)
     else:
         out = run_ours(args)
     if out is not None:
-        if args.n_layer or args.microbatches != 64 or args.mb_size != 1:
+        if args.n_layer or reduced:
             out["diagnostic"] = "reduced config: not the benchmark"
         print(json.dumps(out), flush=True)
 

@@ -16,8 +16,10 @@ connection drops.
 
 from __future__ import annotations
 
+import hashlib
 import json
 import os
+import shutil
 import signal
 import subprocess
 import sys
@@ -25,6 +27,7 @@ import threading
 import time
 import traceback
 
+from elysium_wan_b200.fault_tolerance import checkpoint as ckpt
 from elysium_wan_b200.transport.control import Channel, control_dial, token_mac
 
 ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
@@ -270,6 +273,8 @@ class WorkerAgent:
             self.send("PROFILE_RESULT", ok=False, why=repr(e))
 
     def _run_dir(self, run_id: str) -> str:
+        if not ckpt.safe_name(run_id):
+            raise ValueError(f"refused run id {run_id!r}")
         d = os.path.join(self.workdir, run_id)
         os.makedirs(d, exist_ok=True)
         return d
@@ -314,11 +319,14 @@ class WorkerAgent:
             self.send("METRIC", metric=json.loads(rest), attempt=a.get("attempt"))
 
     def _ship_wave(self, wave_dir: str, a: dict):
-        """Send every file of a committed wave (wave.json last) to the coordinator."""
-        rel = os.path.relpath(wave_dir, a["dir"])
+        """Send every file of a committed wave (wave.json last) to the
+        coordinator, which files it under the slot of this connection."""
+        step = ckpt._step_of(os.path.basename(os.path.normpath(wave_dir)))
+        if step is None:
+            return
         names = sorted(os.listdir(wave_dir), key=lambda n: n == "wave.json")
         for n in names:
-            self.ch and self.ch.send_file("CKPT", os.path.join(wave_dir, n), rel=os.path.join(rel, n),
+            self.ch and self.ch.send_file("CKPT", os.path.join(wave_dir, n), step=step, name=n,
                                           run_id=a["run_id"], last=(n == "wave.json"))
 
     def _supervise(self, proc: StageProcess, a: dict):
@@ -355,13 +363,37 @@ class WorkerAgent:
         self.send("ABORT_ACK", ok=True)
 
     def _on_restore(self, hdr, body):
-        d = self._run_dir(hdr["run_id"])
-        p = os.path.join(d, hdr["rel"])
-        os.makedirs(os.path.dirname(p), exist_ok=True)
-        with open(p, "wb") as f:
+        """RESTORE: one file of a wave for this worker's next slot. The path is
+        built here from checked parts (plain run id, tag and file name; integer
+        slot and step), under <run dir>/waves/<tag>/r<R>p<P>/; the files land in
+        a staging directory that is validated and renamed into place when the
+        last one (wave.json) arrives."""
+        run_id, tag, name = hdr.get("run_id"), hdr.get("tag"), hdr.get("name")
+        stage, peer, step = hdr.get("stage"), hdr.get("peer"), hdr.get("step")
+        ok = all(ckpt.safe_name(x) for x in (run_id, tag, name)) and \
+            all(type(v) is int and v >= 0 for v in (stage, peer, step)) and \
+            hashlib.sha256(body).hexdigest() == hdr.get("sha256")
+        if not ok:
+            self.send("RESTORE_ACK", ok=False, why="refused: malformed restore part")
+            return
+        d = self._run_dir(run_id)
+        final = ckpt.wave_dir(d, tag, stage, peer, step)
+        staging = final + ".restore"
+        os.makedirs(staging, exist_ok=True)
+        with open(os.path.join(staging, name), "wb") as f:
             f.write(body)
-        if hdr.get("last"):
-            self.send("RESTORE_ACK", ok=True, rel=hdr["rel"])
+        if not hdr.get("last"):
+            return
+        try:
+            ckpt.validate_wave(staging)
+        except ValueError as e:
+            shutil.rmtree(staging, ignore_errors=True)
+            self.send("RESTORE_ACK", ok=False, why=str(e), step=step)
+            return
+        if os.path.isdir(final):
+            shutil.rmtree(final, ignore_errors=True)
+        os.rename(staging, final)
+        self.send("RESTORE_ACK", ok=True, step=step)
 
     def _on_release(self, hdr, body):
         """RELEASE {run_id}: the job is over; stop any stage and drop the

@@ -302,11 +302,19 @@ class Coordinator:
             elif kind == "RESULT" and hdr.get("attempt") == self.attempt:
                 self.results[(hdr["stage"], hdr["peer"])] = hdr["losses"]
             elif kind == "CKPT" and self.store is not None and hdr.get("run_id") == self.run_id:
-                if hashlib.sha256(body).hexdigest() == hdr.get("sha256"):
-                    rel = os.path.join(self.run_id, hdr["rel"])
-                    self.store.stage_part(rel, body)
-                    if hdr.get("last"):
-                        self.store.commit_staged(os.path.dirname(rel))
+                # The wave belongs to the slot of the connection that sent it;
+                # only a validated integer step and a plain file name are taken
+                # from the message (reference: checkpoint.py:727-745).
+                if slot is not None and hashlib.sha256(body).hexdigest() == hdr.get("sha256"):
+                    r, q = slot
+                    try:
+                        self.store.stage_part(self.run_id, r, q, hdr.get("step"), hdr.get("name"),
+                                              body)
+                        if hdr.get("last"):
+                            self.store.commit_staged(self.run_id, self.ckpt_tag, r, q,
+                                                     hdr.get("step"))
+                    except (ValueError, OSError) as e:
+                        self.events.append(("ckpt_refused", nid, str(e)))
             elif kind == "TELEMETRY" and slot is not None and current and self.run_dir:
                 # rank and peer come from the connection's slot, never from the
                 # message (reference: coordinator/coordinator.py:594-604)
@@ -557,6 +565,7 @@ class Coordinator:
         os.makedirs(run_dir, exist_ok=True)
         self.run_dir = run_dir
         self.store = ckpt.CheckpointStore(os.path.join(self.cfg.state_dir, "store"))
+        self.ckpt_tag = spec.tag
         live = self.wait_for_workers(max(spec.world_size, self.cfg.min_workers),
                                      self.cfg.wait_workers_s)
         live = self._place(spec, live)
@@ -977,18 +986,23 @@ class Coordinator:
         return ckpt.common_step(view)
 
     def _restore(self, spec, slot, nid, step):
-        """Ship the slot's wave at `step` from the store to its new worker."""
+        """Ship the slot's wave at `step` from the store to its new worker.
+        The wave is validated first (a step that does not validate is refused),
+        and pinned so that pruning cannot remove it while it is shipped."""
         if step is None:
             return
         stage, peer = slot
-        rel_dir = os.path.relpath(ckpt.wave_dir("", spec.tag, stage, peer, step), "")
-        src = os.path.join(self.store.root, self.run_id, rel_dir)
+        self.store.pinned.add(step)
+        src = ckpt.wave_dir(os.path.join(self.store.root, self.run_id), spec.tag, stage, peer, step)
+        meta = ckpt.validate_wave(src)  # raises ValueError: no heal from a damaged wave
         ch = self.nodes[nid].ch
-        names = sorted(os.listdir(src), key=lambda n: n == "wave.json")
+        names = sorted(meta["files"]) + ["wave.json"]
         for n in names:
             with open(os.path.join(src, n), "rb") as f:
-                ch.send("RESTORE", f.read(), run_id=self.run_id, rel=os.path.join(rel_dir, n),
-                        last=(n == "wave.json"))
+                data = f.read()
+            ch.send("RESTORE", data, run_id=self.run_id, tag=spec.tag, stage=stage, peer=peer,
+                    step=step, name=n, last=(n == "wave.json"),
+                    sha256=hashlib.sha256(data).hexdigest())
 
     def _launch(self, spec: JobSpec, resume_step):
         a = copy.deepcopy(spec)

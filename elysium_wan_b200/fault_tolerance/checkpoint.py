@@ -81,17 +81,28 @@ def commit_wave(spec, stage: int, peer: int, step: int, state: dict, replace: bo
     return final
 
 
+def _step_of(name: str) -> int | None:
+    """N of a committed wave directory name "step-<N:08d>", else None."""
+    if not name.startswith("step-"):
+        return None
+    digits = name[5:]
+    if not digits.isdigit() or len(digits) < 8:
+        return None
+    return int(digits)
+
+
 def list_waves(out_dir: str, tag: str, stage: int, peer: int) -> list:
+    """Steps of the slot's committed waves: directories named step-<N> that
+    hold a wave.json (a wave is renamed into place only once it is whole, so a
+    directory without wave.json is never a wave)."""
     d = slot_dir(out_dir, tag, stage, peer)
     if not os.path.isdir(d):
         return []
     out = []
     for name in os.listdir(d):
-        if name.startswith("step-") and not name.endswith((".staging", ".replaced")):
-            try:
-                out.append(int(name[5:]))
-            except ValueError:
-                pass
+        n = _step_of(name)
+        if n is not None and os.path.isfile(os.path.join(d, name, "wave.json")):
+            out.append(n)
     return sorted(out)
 
 
@@ -151,41 +162,89 @@ def common_step(spec) -> int | None:
     return max(common) if common else None
 
 
+def safe_name(name) -> bool:
+    """A plain file or directory name: no separator, no parent reference, no
+    NUL, not hidden, not empty. Names arriving in control messages are used
+    only if they pass."""
+    return (isinstance(name, str) and 0 < len(name) <= 255 and "/" not in name
+            and "\\" not in name and "\0" not in name and name not in (".", "..")
+            and not name.startswith("."))
+
+
 class CheckpointStore:
-    """Coordinator-side store of shipped waves: files arrive under
-    <root>/<run>/waves/..., are verified, and the common step across slots is
-    the heal point (reference CheckpointStore, checkpoint.py:656-900)."""
+    """Coordinator-side store of shipped waves (reference CheckpointStore,
+    src/wantrain/fault_tolerance/checkpoint.py:656-900).
+
+    Parts arrive per slot into a staging area outside every wave directory,
+    <root>/<run>/.incoming/r<R>p<P>/step-<N>/, keyed by the slot of the
+    connection that sent them (never by a path from the message). When the last
+    part (wave.json) arrives the staged directory is validated (every listed
+    file's size and sha256, and the wave's own step, stage and peer) and only
+    then renamed into <root>/<run>/waves/<tag>/r<R>p<P>/step-<N>, so a wave in
+    the store is always whole: a slot that dies half-way through shipping
+    leaves nothing that the resume point can pick. The heal pins its resume
+    step so that pruning never removes the wave being restored."""
 
     def __init__(self, root: str):
         self.root = root
+        self.pinned: set = set()
         os.makedirs(root, exist_ok=True)
 
-    def stage_part(self, rel_path: str, data: bytes) -> str:
-        p = os.path.join(self.root, rel_path + ".part")
-        os.makedirs(os.path.dirname(p), exist_ok=True)
-        with open(p, "wb") as f:
+    def _incoming(self, run_id: str, stage: int, peer: int, step: int) -> str:
+        return os.path.join(self.root, run_id, ".incoming", f"r{stage}p{peer}", f"step-{step:08d}")
+
+    @staticmethod
+    def _check(run_id, stage, peer, step, name=None):
+        if not safe_name(run_id):
+            raise ValueError(f"bad run id {run_id!r}")
+        for v in (stage, peer, step):
+            if type(v) is not int or v < 0:
+                raise ValueError(f"bad slot or step {v!r}")
+        if name is not None and not safe_name(name):
+            raise ValueError(f"bad part name {name!r}")
+
+    def stage_part(self, run_id: str, stage: int, peer: int, step: int, name: str,
+                   data: bytes) -> str:
+        """Write one shipped file of the slot's wave at `step` into staging."""
+        self._check(run_id, stage, peer, step, name)
+        d = self._incoming(run_id, stage, peer, step)
+        os.makedirs(d, exist_ok=True)
+        p = os.path.join(d, name)
+        with open(p + ".part", "wb") as f:
             f.write(data)
+        os.replace(p + ".part", p)
         return p
 
-    def commit_staged(self, rel_dir: str) -> bool:
-        d = os.path.join(self.root, rel_dir)
+    def commit_staged(self, run_id: str, tag: str, stage: int, peer: int, step: int) -> bool:
+        """Validate the staged wave and rename it into place (False, and the
+        staging removed, if it does not validate)."""
+        self._check(run_id, stage, peer, step)
+        if not safe_name(tag):
+            raise ValueError(f"bad tag {tag!r}")
+        d = self._incoming(run_id, stage, peer, step)
         if not os.path.isdir(d):
             return False
-        for name in os.listdir(d):
-            if name.endswith(".part"):
-                os.replace(os.path.join(d, name), os.path.join(d, name[:-5]))
         try:
-            validate_wave(d)
-        except ValueError:
+            meta = validate_wave(d)
+            if (meta.get("step"), meta.get("stage"), meta.get("peer")) != (step, stage, peer):
+                raise ValueError("wave.json names another slot or step")
+        except (ValueError, KeyError, OSError, json.JSONDecodeError):
             shutil.rmtree(d, ignore_errors=True)
             return False
-        # Keep the newest WAVE_KEEP waves of this slot, like the workers do.
-        slot = os.path.dirname(d)
-        steps = sorted(int(x[5:]) for x in os.listdir(slot)
-                       if x.startswith("step-") and not x.endswith(".part") and x[5:].isdigit())
-        for old in steps[:-WAVE_KEEP]:
-            shutil.rmtree(os.path.join(slot, f"step-{old:08d}"), ignore_errors=True)
+        final = wave_dir(os.path.join(self.root, run_id), tag, stage, peer, step)
+        os.makedirs(os.path.dirname(final), exist_ok=True)
+        if os.path.isdir(final):  # waves are immutable: the first whole copy stays
+            shutil.rmtree(d, ignore_errors=True)
+        else:
+            os.rename(d, final)
+        self._prune(os.path.dirname(final))
         return True
+
+    def _prune(self, slot: str):
+        steps = sorted(n for n in (_step_of(x) for x in os.listdir(slot)) if n is not None)
+        for old in steps[:-WAVE_KEEP]:
+            if old not in self.pinned:
+                shutil.rmtree(os.path.join(slot, f"step-{old:08d}"), ignore_errors=True)
 
     def common_step(self, spec) -> int | None:
         from copy import copy

@@ -8,7 +8,10 @@ from __future__ import annotations
 
 def find_replacement(dead, candidates: list, match: str = "any", dead_hosts: set | None = None):
     dead_hosts = dead_hosts or set()
-    pool = [c for c in candidates if c.alive and c.host not in dead_hosts or c.host == "127.0.0.1"]
+    # A dead spare never qualifies. Hosts remembered as dead are skipped, except
+    # the loopback host, which every worker of a one-machine fleet shares.
+    pool = [c for c in candidates
+            if c.alive and (c.host not in dead_hosts or c.host == "127.0.0.1")]
     pool = [c for c in pool if c.node_id != dead.node_id]
     if not pool:
         return None

@@ -42,7 +42,18 @@ def measure(spec, stage: int, device: str = "cpu") -> dict:
             out, st = eng.model.forward(inp, t.to(dev) if eng.last else None,
                                         keep="inputs" if eng.recompute else "all")
             saved.append(st)
-        eng.opt.step()
+        opt = eng.opt
+        if opt is None:
+            # A wide stage: one replica's ZeRO-1 shard of the moments.
+            from elysium_wan_b200.parallel.zero1 import shard_bounds
+            from elysium_wan_b200.runtime import optim
+
+            st_ = eng.store
+            lo, hi = shard_bounds(st_.nt, eng.width)[0]
+            opt = optim.build(spec.optimizer, st_.master[lo:hi], st_.grad[lo:hi],
+                              st_.work[lo:hi] if st_.work is not None else None, spec.lr,
+                              spec.adamw)
+        opt.step()
     except torch.cuda.OutOfMemoryError:
         ok = False
     peak = torch.cuda.max_memory_allocated(dev) if dev.type == "cuda" else 0

@@ -49,10 +49,12 @@ class StageEngine:
         # The optimizer covers the trainable region [0, nt) (all of it unless
         # LoRA froze the base).
         # (The pieces layout builds its two range optimizers when the comm attaches.)
-        self.opt = None if self.pieces else optim.build(
+        # A wide stage's ZeRO-1 layer builds the optimizer of its own shard when
+        # the comm attaches (whole-stage moments would double its memory).
+        self.width = spec.stage_widths[stage]
+        self.opt = None if (self.pieces or self.width > 1) else optim.build(
             spec.optimizer, st.master[:st.nt], st.grad,
             st.work[:st.nt] if st.work is not None else None, spec.lr, spec.adamw)
-        self.width = spec.stage_widths[stage]
         self.step_done = 0
         self.losses: list = []  # (step, mb, float)
         self.events: list = []  # per-op (op, mb, start_event, end_event)

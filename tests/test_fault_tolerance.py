@@ -154,6 +154,78 @@ def test_replacement_prefers_same_class_and_region():
     assert find_replacement(dead, [cands[2]], match="device") is None
 
 
+def test_replacement_never_picks_a_dead_spare_even_on_loopback():
+    """A spare whose node is not alive is refused whatever its host (the
+    loopback exemption only lifts the dead-host memory)."""
+    dead = NodeInfo("n0", "w0", host="127.0.0.1", device_class="b200")
+    gone = NodeInfo("n1", "w1", host="127.0.0.1", device_class="b200")
+    gone.alive = False
+    live = NodeInfo("n2", "w2", host="127.0.0.1", device_class="b200")
+    assert find_replacement(dead, [gone]) is None
+    assert find_replacement(dead, [gone, live], dead_hosts={"127.0.0.1"}).node_id == "n2"
+    remote = NodeInfo("n3", "w3", host="10.0.0.7", device_class="b200")
+    assert find_replacement(dead, [remote], dead_hosts={"10.0.0.7"}) is None
+
+
+def _wave_parts(tmp_path, spec, stage, peer, step):
+    """The files of a committed worker wave: {name: bytes}."""
+    d = ckpt.commit_wave(spec, stage, peer, step, {"step": step})
+    return {n: open(os.path.join(d, n), "rb").read() for n in os.listdir(d)}
+
+
+def test_store_keeps_half_shipped_waves_out_of_the_resume_point(tmp_path):
+    """A slot that dies after shipping state.pt but before wave.json leaves
+    nothing in the store's wave tree: the common step stays the previous
+    whole wave, and only a validated wave is renamed into place."""
+    spec = _spec(tmp_path / "w")
+    store = ckpt.CheckpointStore(str(tmp_path / "store"))
+    run = "run1"
+    for step in (2, 4):
+        for r in (0, 1):
+            parts = _wave_parts(tmp_path, spec, r, 0, step)
+            names = sorted(parts, key=lambda n: n == "wave.json")
+            for n in names:
+                if step == 4 and r == 1 and n == "wave.json":
+                    break  # slot 1 dies before its last part of step 4
+                store.stage_part(run, r, 0, step, n, parts[n])
+                if n == "wave.json":
+                    assert store.commit_staged(run, spec.tag, r, 0, step)
+    view = _spec(tmp_path / "store" / run)
+    assert ckpt.list_waves(view.out_dir, spec.tag, 1, 0) == [2]
+    assert ckpt.common_step(view) == 2
+    # a wave whose wave.json names another step is refused and dropped
+    parts = _wave_parts(tmp_path, spec, 0, 0, 6)
+    for n in sorted(parts, key=lambda n: n == "wave.json"):
+        store.stage_part(run, 1, 0, 6, n, parts[n])
+    assert not store.commit_staged(run, spec.tag, 1, 0, 6)
+    assert ckpt.list_waves(view.out_dir, spec.tag, 1, 0) == [2]
+
+
+@pytest.mark.parametrize("name", ["../../x", "/etc/passwd", "a/b", "..", ".hidden", "", "x\0y"])
+def test_store_refuses_part_names_that_leave_the_slot(tmp_path, name):
+    store = ckpt.CheckpointStore(str(tmp_path / "store"))
+    with pytest.raises(ValueError):
+        store.stage_part("run1", 0, 0, 2, name, b"data")
+    with pytest.raises(ValueError):
+        store.stage_part("../run", 0, 0, 2, "state.pt", b"data")
+    with pytest.raises(ValueError):
+        store.stage_part("run1", 0, 0, -1, "state.pt", b"data")
+    assert not os.path.exists(tmp_path / "x") and not os.path.exists(tmp_path / "run")
+
+
+def test_store_pins_the_restored_wave_against_pruning(tmp_path):
+    spec = _spec(tmp_path / "w")
+    store = ckpt.CheckpointStore(str(tmp_path / "store"))
+    store.pinned.add(2)
+    for step in (2, 4, 6, 8, 10):
+        parts = _wave_parts(tmp_path, spec, 0, 0, step)
+        for n in sorted(parts, key=lambda n: n == "wave.json"):
+            store.stage_part("run1", 0, 0, step, n, parts[n])
+        assert store.commit_staged("run1", spec.tag, 0, 0, step)
+    view = _spec(tmp_path / "store" / "run1")
+    assert ckpt.list_waves(view.out_dir, spec.tag, 0, 0) == [2, 6, 8, 10]
+
+
 def test_recut_resume_continues_the_run_bitwise(tmp_path):
     """Waves of a 2-stage run at step 2, re-cut to a 3-stage partition, resume
     to step 4: every loss equals the uninterrupted run's."""
