@@ -1,76 +1,112 @@
-"""Link memory: what earlier runs measured on the path between two machines,
-and which machines recently proved dead.
+"""Memory across runs: how the network path between two machines measured, and
+which machines recently failed.
 
-Parity: src/wantrain/scheduler/linkmemory.py (`PathRecord` :52, `verdict`
-:66, `LinkMemory` :92 with `record_path`, `path`, `record_dead`,
-`dead_keys`). A slow path is ranked down and named, never refused; a dead
-host is remembered for a TTL because it fails against every peer. Stored as
-two JSON files under the coordinator's state directory (atomic replace).
+Behaviour of the reference's link memory (src/wantrain/scheduler/linkmemory.py
+:52-176, semantics only): a path is graded from its readings -- good when
+every reading clears the bandwidth floor, variable when only some do, slow
+when none does or its round trip is too long -- and a slow path is ranked
+down and named by node selection, never refused; a machine that failed is
+avoided for a time-to-live, because a dead host fails against every peer; a
+run counts once per path however often its measurement is replayed.
+
+Structure here: the memory is a journal of readings. Each path keeps one
+`Reading` per run (the newest runs, at most `KEEP_RUNS`), and everything the
+selector asks for (latest rate, slowest and fastest run, the grade) is
+derived from that list when asked. Failed machines are `Sighting`s that
+expire by age when read. Both live in one JSON document under the
+coordinator's state directory, rewritten through a temporary file in the same
+directory and an atomic rename.
 """
 
 from __future__ import annotations
 
+import ipaddress
 import json
 import os
-import re
+import tempfile
 import threading
 import time
 from dataclasses import asdict, dataclass, field
 
-SLOW_PATH_MBPS = 100.0
-SLOW_PATH_RTT_MS = 80.0
-DEAD_HOST_TTL_S = 6 * 3600.0
-PENALTY = {"good": 0, "variable": 1, "slow": 2}
+FLOOR_MBPS = 100.0  # a reading below this rate is slow
+MAX_RTT_MS = 80.0  # a path whose latest round trip is longer is slow
+DEAD_TTL_S = 6 * 3600.0  # how long a failed machine is avoided
+KEEP_RUNS = 50  # readings kept per path
+GRADE_RANK = {"good": 0, "variable": 1, "slow": 2}  # selection sorts by this
+FILE_NAME = "links.json"
 
 
-def path_key(a: str, b: str) -> str:
-    return "|".join(sorted((a, b)))
+def _ends(a: str, b: str) -> tuple:
+    return tuple(sorted((a, b)))
 
 
-def subnet24(ip: str | None) -> str | None:
-    m = re.fullmatch(r"(\d{1,3}\.\d{1,3}\.\d{1,3})\.\d{1,3}", (ip or "").strip())
-    return m.group(1) if m else None
-
-
-def shares_subnet(ips) -> str | None:
-    """The /24 two of the addresses share, if any (one LAN, or two forwards
-    through one gateway): reported with the selection, not scored."""
-    seen = set()
-    for n in (subnet24(i) for i in ips):
-        if n is None:
+def shares_subnet(addresses) -> str | None:
+    """The /24 network that two of the IPv4 addresses share (one LAN, or two
+    port forwards through one gateway), else None. Reported with a
+    selection, not scored."""
+    nets = set()
+    for a in addresses:
+        try:
+            ip = ipaddress.IPv4Address((a or "").strip())
+        except ValueError:
             continue
-        if n in seen:
-            return n
-        seen.add(n)
+        net = str(ipaddress.IPv4Network(f"{ip}/24", strict=False).network_address)[:-2]
+        if net in nets:
+            return net
+        nets.add(net)
     return None
 
 
-@dataclass
-class PathRecord:
-    a: str
-    b: str
-    mbps: float  # slower direction of the latest reading
-    rtt_ms: float
-    measured_at: float
+@dataclass(frozen=True)
+class Reading:
     run_id: str
-    samples: int = 1
-    run_ids: list = field(default_factory=list)
-    worst_mbps: float = 0.0
-    best_mbps: float = 0.0
-
-
-def verdict(p: PathRecord | None) -> str | None:
-    """good (every reading clears the floor), variable (some do), slow (none
-    does, or the round trip is too long); None when never measured."""
-    if p is None:
-        return None
-    if p.rtt_ms > SLOW_PATH_RTT_MS or p.best_mbps < SLOW_PATH_MBPS:
-        return "slow"
-    return "variable" if p.worst_mbps < SLOW_PATH_MBPS else "good"
+    mbps: float  # slower direction
+    rtt_ms: float
+    at: float
 
 
 @dataclass
-class DeadHost:
+class PathHistory:
+    ends: tuple
+    readings: list = field(default_factory=list)  # oldest first, one per run
+
+    @property
+    def samples(self) -> int:
+        return len(self.readings)
+
+    @property
+    def latest(self) -> Reading:
+        return self.readings[-1]
+
+    @property
+    def mbps(self) -> float:
+        return self.latest.mbps
+
+    @property
+    def rtt_ms(self) -> float:
+        return self.latest.rtt_ms
+
+    @property
+    def slowest_mbps(self) -> float:
+        return min(r.mbps for r in self.readings)
+
+    @property
+    def fastest_mbps(self) -> float:
+        return max(r.mbps for r in self.readings)
+
+    def grade(self) -> str:
+        if self.rtt_ms > MAX_RTT_MS or self.fastest_mbps < FLOOR_MBPS:
+            return "slow"
+        return "good" if self.slowest_mbps >= FLOOR_MBPS else "variable"
+
+
+def verdict(history: PathHistory | None) -> str | None:
+    """The grade of a remembered path; None for a path never measured."""
+    return None if history is None or not history.readings else history.grade()
+
+
+@dataclass(frozen=True)
+class Sighting:
     node_key: str
     host: str | None
     reason: str
@@ -79,69 +115,77 @@ class DeadHost:
 
 
 class LinkMemory:
-    def __init__(self, state_dir: str | None = None, dead_ttl_s: float = DEAD_HOST_TTL_S):
+    def __init__(self, state_dir: str | None = None, dead_ttl_s: float = DEAD_TTL_S):
         self.state_dir = state_dir
         self.dead_ttl_s = dead_ttl_s
         self._lock = threading.Lock()
-        self._paths: dict[str, PathRecord] = {}
-        self._dead: dict[str, DeadHost] = {}
+        self._paths: dict = {}  # ends -> PathHistory
+        self._dead: dict = {}  # node_key -> Sighting
         if state_dir:
             os.makedirs(state_dir, exist_ok=True)
-            for r in self._load("link-memory.json"):
-                p = PathRecord(**r)
-                self._paths[path_key(p.a, p.b)] = p
-            for r in self._load("dead-hosts.json"):
-                d = DeadHost(**r)
-                self._dead[d.node_key] = d
+            self._read()
 
-    def _load(self, name) -> list:
+    # ------------------------------------------------------------ storage
+    def _read(self):
         try:
-            with open(os.path.join(self.state_dir, name)) as f:
-                rows = json.load(f)
-            return rows if isinstance(rows, list) else []
-        except (OSError, ValueError, TypeError):
-            return []
+            with open(os.path.join(self.state_dir, FILE_NAME)) as f:
+                doc = json.load(f)
+        except (OSError, ValueError):
+            return
+        for row in doc.get("paths", []) if isinstance(doc, dict) else []:
+            try:
+                h = PathHistory(_ends(*row["ends"]), [Reading(**r) for r in row["readings"]])
+            except (KeyError, TypeError, ValueError):
+                continue
+            if h.readings:
+                self._paths[h.ends] = h
+        for row in doc.get("dead", []) if isinstance(doc, dict) else []:
+            try:
+                s = Sighting(**row)
+            except TypeError:
+                continue
+            self._dead[s.node_key] = s
 
-    def _save(self, name, rows):
+    def _write(self):
         if not self.state_dir:
             return
-        path = os.path.join(self.state_dir, name)
-        tmp = f"{path}.{os.getpid()}.tmp"
-        with open(tmp, "w") as f:
-            json.dump(rows, f, indent=1)
-        os.replace(tmp, path)
+        doc = {"paths": [{"ends": list(h.ends), "readings": [asdict(r) for r in h.readings]}
+                         for h in self._paths.values()],
+               "dead": [asdict(s) for s in self._dead.values()]}
+        fd, tmp = tempfile.mkstemp(prefix=".links-", dir=self.state_dir)
+        with os.fdopen(fd, "w") as f:
+            json.dump(doc, f)
+        os.replace(tmp, os.path.join(self.state_dir, FILE_NAME))
 
-    def record_path(self, a: str, b: str, mbps: float, rtt_ms: float, run_id: str) -> PathRecord:
-        """One reading per run per path (a replay does not count twice); the
-        range of readings rides along with the latest."""
-        a, b = sorted((a, b))
+    # ------------------------------------------------------------ paths
+    def record_path(self, a: str, b: str, mbps: float, rtt_ms: float, run_id: str) -> PathHistory:
+        """Add this run's reading of the path (a second reading from the same
+        run is ignored)."""
         with self._lock:
-            key = path_key(a, b)
-            prev = self._paths.get(key)
-            ids = list(prev.run_ids) if prev else []
-            if prev and run_id in ids:
-                return prev
-            ids = (ids + [run_id])[-50:]
-            rec = PathRecord(a, b, float(mbps), float(rtt_ms), time.time(), run_id, len(ids), ids,
-                             min(prev.worst_mbps, mbps) if prev else mbps,
-                             max(prev.best_mbps, mbps) if prev else mbps)
-            self._paths[key] = rec
-            self._save("link-memory.json", [asdict(p) for p in self._paths.values()])
-            return rec
+            h = self._paths.setdefault(_ends(a, b), PathHistory(_ends(a, b)))
+            if any(r.run_id == run_id for r in h.readings):
+                return h
+            h.readings = (h.readings + [Reading(run_id, float(mbps), float(rtt_ms), time.time())])
+            h.readings = h.readings[-KEEP_RUNS:]
+            self._write()
+            return h
 
-    def path(self, a: str, b: str) -> PathRecord | None:
-        return self._paths.get(path_key(a, b))
+    def path(self, a: str, b: str) -> PathHistory | None:
+        return self._paths.get(_ends(a, b))
 
     def paths(self) -> dict:
         return dict(self._paths)
 
+    # ------------------------------------------------------------ failed machines
+    def _live_sightings(self, now: float) -> dict:
+        return {k: s for k, s in self._dead.items() if now - s.at < self.dead_ttl_s}
+
     def record_dead(self, node_key: str, reason: str, run_id: str, host: str | None = None):
-        now = time.time()
         with self._lock:
-            self._dead = {k: d for k, d in self._dead.items() if now - d.at < self.dead_ttl_s}
-            self._dead[node_key] = DeadHost(node_key, host, reason[:300], now, run_id)
-            self._save("dead-hosts.json", [asdict(d) for d in self._dead.values()])
+            now = time.time()
+            self._dead = self._live_sightings(now)
+            self._dead[node_key] = Sighting(node_key, host, reason[:300], now, run_id)
+            self._write()
 
     def dead_keys(self) -> set:
-        now = time.time()
-        return {k for k, d in self._dead.items() if now - d.at < self.dead_ttl_s}
+        return set(self._live_sightings(time.time()))

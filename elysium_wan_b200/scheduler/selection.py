@@ -19,7 +19,7 @@ from __future__ import annotations
 import re
 from dataclasses import dataclass, field
 
-from elysium_wan_b200.scheduler.linkmemory import PENALTY, LinkMemory, shares_subnet, verdict
+from elysium_wan_b200.scheduler.linkmemory import GRADE_RANK, LinkMemory, shares_subnet, verdict
 
 MIN_UPLINK_MBPS = 200.0
 
@@ -87,7 +87,7 @@ def _hop(a, b, memory):
 
 
 def _penalty(fleet, memory) -> int:
-    return max([PENALTY[v] for v in (_hop(a, b, memory) for a, b in zip(fleet, fleet[1:])) if v]
+    return max([GRADE_RANK[v] for v in (_hop(a, b, memory) for a, b in zip(fleet, fleet[1:])) if v]
                or [0])
 
 
@@ -210,12 +210,12 @@ def select_nodes(pool, n: int, policy: SelectionPolicy | None = None,
     worst = None
     for a, b in zip(chosen, chosen[1:]):
         p = memory.path(a.host, b.host) if memory else None
-        if p and (worst is None or p.worst_mbps < worst.worst_mbps):
+        if p and (worst is None or p.slowest_mbps < worst.slowest_mbps):
             worst = p
     if worst is not None:
         v = verdict(worst)
         notes.append(f"{'WARNING: ' if v != 'good' else ''}a hop was measured at "
-                     f"{worst.worst_mbps:.0f}-{worst.best_mbps:.0f} Mbps, RTT {worst.rtt_ms:.0f} ms "
+                     f"{worst.slowest_mbps:.0f}-{worst.fastest_mbps:.0f} Mbps, RTT {worst.rtt_ms:.0f} ms "
                      f"({v})")
     net = shares_subnet({x.host for x in chosen})
     if net and worst is None:

@@ -174,7 +174,9 @@ def run_reference_arm(args) -> dict | None:
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     n = args.gpus
-    wait_s = float(os.environ.get("EWB_REF_TIMEOUT_S", "3000"))
+    # The run is stopped at this deadline (seconds from its launch), under the
+    # driver's per-run limit; the timed steps finished by then are reported.
+    wait_s = float(os.environ.get("EWB_REF_TIMEOUT_S", "780"))
     if not os.path.isdir(os.path.join(REF, "wantrain")):
         out = unavailable("the reference is not laid out in baseline/_ref")
         _rendezvous(world, wait_s + 600)
@@ -190,8 +192,10 @@ def run_reference_arm(args) -> dict | None:
     if widths is not None and sum(widths) != n:
         _rendezvous(world, wait_s + 600)
         return unavailable(f"stage widths {widths} do not use {n} GPUs")
-    scratch = os.environ.get("EWB_REF_LOGDIR") or tempfile.mkdtemp(prefix="refbench-")
-    os.makedirs(scratch, exist_ok=True)
+    # The reference's out_dir (its stage logs, and the start of its final
+    # checkpoint before the run is stopped) is a scratch directory; with
+    # EWB_REF_LOGDIR set, only the logs are copied there afterwards.
+    scratch = tempfile.mkdtemp(prefix="refbench-")
     kw = reference_spec_kwargs(model, n, widths, args.warmup + args.steps, args.microbatches,
                                args.mb_size, args.n_layer, scratch)
     kw["timeout_s"] = wait_s
@@ -213,7 +217,7 @@ def run_reference_arm(args) -> dict | None:
                          start_new_session=True)
     timed = list(range(args.warmup, args.warmup + args.steps))
     # Timing per slot; the step time of a stage is the slowest of its peers.
-    result = None
+    result, partial = None, False
     try:
         while True:
             done = p.poll() is not None
@@ -225,6 +229,10 @@ def run_reference_arm(args) -> dict | None:
             if done:
                 break
             if time.time() - t0 > wait_s:
+                # Out of time: keep the timed steps that every stage finished.
+                got = [t for t in timed if all(t in st for st in per_slot.values())]
+                if got:
+                    timed, result, partial = got, per_slot, True
                 break
             time.sleep(2.0)
     finally:
@@ -234,18 +242,18 @@ def run_reference_arm(args) -> dict | None:
     err = _errors(scratch, "refbench", slots)
     if result is None:
         why = "timed out" if p.returncode is None or wall > wait_s else f"exited (rc {p.returncode})"
-        out = unavailable(f"the reference run {why} before every stage reported the timed steps: "
-                          + (err or "no error line in the stage logs"))
+        out = unavailable(f"the reference run {why} before every stage reported a timed step "
+                          f"({wall:.0f} s): " + (err or "no error line in the stage logs"))
     else:
         ms = max(sum(st[t] for t in timed) for st in result.values())
         S = 2048
         tokens = kw["spec"]["microbatches"] * kw["spec"]["mb_size"] * S
-        value = tokens * args.steps / (ms / 1e3)
+        value = tokens * len(timed) / (ms / 1e3)
         m = kw["model"]
         layout = "x".join(str(w) for w in kw["spec"]["stage_widths"])
         out = {"impl": "reference", "metric": args.metric, "value": round(value, 1),
-               "unit": "tokens/s", "n_gpus": n, "steps": args.steps, "warmup": args.warmup,
-               "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
+               "unit": "tokens/s", "n_gpus": n, "steps": len(timed), "warmup": args.warmup,
+               "ms_per_step": round(ms / len(timed), 3), "higher_is_better": True,
                "scaling": "strong", "vs_baseline": round(value / 3344.0, 3), "dtype": "bf16",
                "data": "synthetic (seeded uniform token ids, random-init weights)",
                "config": {"model": f"reference GPTConfig {m['n_layer']}L d{m['d_model']} "
@@ -262,10 +270,20 @@ def run_reference_arm(args) -> dict | None:
                "wall_s": round(wall, 1),
                "note": "the run is stopped once every stage has reported the timed steps "
                        "(its final checkpoint is not part of the measured work)"}
+        if partial:
+            out["steps_requested"] = args.steps
+            out["partial"] = (f"the reference needed more than {wait_s:.0f} s for {args.warmup} "
+                              f"warm-up and {args.steps} timed steps; its rate is over the "
+                              f"{len(timed)} timed steps every stage finished")
         if args.n_layer:
             out["diagnostic"] = "reduced config: not the benchmark"
-    if not os.environ.get("EWB_REF_LOGDIR"):
-        shutil.rmtree(scratch, ignore_errors=True)
+    keep = os.environ.get("EWB_REF_LOGDIR")
+    if keep:
+        os.makedirs(keep, exist_ok=True)
+        for name in os.listdir(scratch):
+            if name.endswith((".log", ".json")) and os.path.getsize(os.path.join(scratch, name)) < (8 << 20):
+                shutil.copy(os.path.join(scratch, name), os.path.join(keep, name))
+    shutil.rmtree(scratch, ignore_errors=True)
     _rendezvous(world, 600)
     return out
 

@@ -345,13 +345,13 @@ def test_unrouted_chain_gives_the_hungriest_rank_the_largest_card(tmp_path):
     placement's order."""
     from elysium_wan_b200.control.coordinator import Coordinator, CoordinatorConfig, _Node
     from elysium_wan_b200.resources.node import NodeInfo
-    from elysium_wan_b200.scheduler.placement import rank_memory_weights
+    from elysium_wan_b200.scheduler.placement import rank_memory_need
 
     co = Coordinator(port=0, cfg=CoordinatorConfig(state_dir=str(tmp_path / "co")))
     try:
         spec = JobSpec(model=make_config("toy", n_layer=4), stages=3, microbatches=3,
                        mb_size=1).finalize()
-        need = rank_memory_weights(spec)
+        need = rank_memory_need(spec)
         for k, gb in enumerate([40, 180, 80]):
             co.nodes[f"n{k}"] = _Node(NodeInfo.from_caps(f"n{k}", {"vram_gb": gb}), None)
         live = ["n0", "n1", "n2"]

@@ -99,6 +99,66 @@ def test_everyone_alive_but_no_progress_is_stalled():
     assert j.judge(ss, NOW).kind == "stalled"
 
 
+def test_stage_reported_gone_convicts_after_the_exit_report_grace():
+    """S2 without an exit report: the agent says its stage process is gone;
+    the judge waits the exit-report grace for an explaining EXIT, then
+    convicts that slot."""
+    j = LivenessJudge(exit_report_grace_s=5)
+    ss = slots()
+    ss[1].stage_alive = False
+    assert j.judge(ss, NOW).kind == "ok"
+    assert j.judge(ss, NOW + 4).kind == "ok"
+    v = j.judge(ss, NOW + 6)
+    assert v.kind == "convict" and v.slot == (1, 0)
+    ss[1].stage_alive = True  # it came back: the memory is dropped
+    assert j.judge(ss, NOW + 7).kind == "ok"
+
+
+def test_stall_limit_follows_the_median_step():
+    """S4 after the first steps: the limit is max(floor, steps x median step)."""
+    j = LivenessJudge(stall_floor_s=10, stall_steps=4, heartbeat_timeout_s=1e9)
+    ss = slots()
+    for st in ss:
+        for k in range(5):
+            st.add_progress(k, NOW + 3.0 * k, None)  # 3 s per step
+    last = NOW + 12.0
+    assert j.judge(ss, last + 11).kind == "ok"  # under 4 x 3 = 12 s
+    assert j.judge(ss, last + 13).kind == "stalled"
+
+
+def test_shutdown_quiet_is_bounded():
+    """After every slot reached the final step, quiet is not a stall, but a
+    shutdown that takes longer than the limit fails the job."""
+    j = LivenessJudge(final_step=3, shutdown_limit_s=50, heartbeat_timeout_s=1e9, stall_floor_s=1)
+    ss = slots()
+    for st in ss:
+        for k in range(4):
+            st.add_progress(k, NOW + k, 3)
+    ss[0].exit_code, ss[0].done_marker = 0, True
+    assert j.judge(ss, NOW + 3 + 40).kind == "ok"
+    v = j.judge(ss, NOW + 3 + 60)
+    assert v.kind == "failed" and "shutdown" in v.why
+
+
+def test_several_silent_suspects_wait_instead_of_convicting():
+    j = LivenessJudge(heartbeat_timeout_s=10, first_step_timeout_s=100, strike_gap_s=1)
+    ss = slots(started_at=NOW - 500)
+    ss[0].last_heartbeat = ss[2].last_heartbeat = NOW - 30
+    v = j.judge(ss, NOW)
+    assert v.kind == "suspect" and v.slot is None and set(v.slots) == {(0, 0), (2, 0)}
+    assert j.judge(ss, NOW + 5).kind == "suspect"
+
+
+def test_rule_table_is_walked_in_order():
+    """The decision table names every verdict path; its last rule always holds."""
+    from elysium_wan_b200.fault_tolerance.liveness import RULES
+
+    names = [r.name for r in RULES]
+    assert names[0] == "nothing launched" and names[-1] == "everyone alive, no progress"
+    assert names.index("S1/S2 against one slot") < names.index("connection down inside the grace")
+    assert names.index("a stage raised its own error") < names.index("no S3/S4 suspects")
+
+
 def test_progress_must_increase_within_attempt():
     st = SlotState(slot=(0, 0), node_id="n", start_step=4)
     assert not st.add_progress(3, 1.0, 10)

@@ -11,7 +11,7 @@ from elysium_wan_b200.resources.node import NodeInfo
 from elysium_wan_b200.runtime.spec import JobSpec
 from elysium_wan_b200.scheduler import autoconfig, production, shape, solve
 from elysium_wan_b200.scheduler.linkmemory import LinkMemory, verdict
-from elysium_wan_b200.scheduler.placement import memory_order, place, rank_memory_weights
+from elysium_wan_b200.scheduler.placement import memory_order, place, rank_memory_need
 from elysium_wan_b200.scheduler.selection import SelectionPolicy, select_nodes
 
 
@@ -102,7 +102,7 @@ def _nodes(n, vram=(180,), tf=1000.0, cls="cuda:B200", region="r0"):
 
 def test_memory_order_gives_rank0_the_biggest_card():
     spec = JobSpec(model=make_config("gpt0_6b"), stages=4, microbatches=8, mb_size=1)
-    w = rank_memory_weights(spec)
+    w = rank_memory_need(spec)
     assert w[0] == max(w[:-1])
     nodes = _nodes(4, vram=(80, 180, 96, 141))
     order = memory_order(spec, nodes)
