@@ -246,6 +246,7 @@ def run_ours(args) -> dict | None:
     init_group(spec, rank, timeout_s=float(os.environ.get("EWB_PG_TIMEOUT_S", "600")))
     stage, peer = spec.slot_of(rank)
     eng = StageEngine(spec, stage, peer, None, dev)
+    eng.log = lambda line: print(f"[bench] rank {rank}: {line}", file=sys.stderr, flush=True)
     eng.warm_kernels()
     comm = PipeComm(spec, stage, peer, dev) if world > 1 else None
     eng.attach_comm(comm)

@@ -302,6 +302,13 @@ class WorkerAgent:
         self.assign = dict(hdr, spec_path=sp, dir=d)
         log = os.path.join(d, f"stage-a{attempt}-r{stage}p{peer}.log")
         self.stage = StageProcess(cmd, env, self._on_stage_line, log)
+        # The stage's process id (its own process group), for host-side fault
+        # injection by test harnesses.
+        try:
+            with open(os.path.join(self.workdir, "stage.pid"), "w") as f:
+                f.write(str(self.stage.p.pid))
+        except OSError:
+            pass
         self.send("ASSIGN_ACK", ok=True, run_id=run_id, attempt=attempt)
         threading.Thread(target=self._supervise, args=(self.stage, dict(self.assign)), daemon=True).start()
 

@@ -242,9 +242,11 @@ class Coordinator:
             nid = hdr.get("node_id")
             if nid and nid in self.nodes and not self.nodes[nid].dead:
                 n = self.nodes[nid]
+                down = None if n.disconnected_at is None else time.time() - n.disconnected_at
                 n.ch, n.connected, n.disconnected_at = ch, True, None
                 n.last_heartbeat = time.time()
                 self._sync_slot(nid)
+                self.events.append(("reconnected", nid, {"after_s": down}))
                 return nid
             caps = hdr.get("caps", {})
             nid = f"n{len(self.order)}-{caps.get('name', 'worker')}"

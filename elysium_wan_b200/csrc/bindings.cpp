@@ -563,6 +563,24 @@ void cast_bf16(at::Tensor x, at::Tensor y) {
 
 int64_t launch_count() { return g_launches.load(); }
 
+// A bounded device wait that nothing releases (or that is released before it
+// starts, release=true): returns {completed, waited ns}; a timeout records its
+// code in the device status word and the kernel returns normally.
+std::vector<int64_t> wait_probe(int64_t mode, bool release, int64_t limit_ns) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  auto opts = at::TensorOptions().device(at::kCUDA, dev);
+  at::Tensor flag = at::zeros({1}, opts.dtype(at::kInt));
+  at::Tensor out = at::zeros({2}, opts.dtype(at::kLong));
+  ok(ewb::wait_probe(static_cast<int>(mode), release ? 1 : 0, flag.data_ptr<int>(),
+                     static_cast<unsigned long long>(limit_ns), status_word(dev),
+                     reinterpret_cast<long long*>(out.data_ptr<int64_t>()), cur_stream()),
+     "wait_probe");
+  count(1);
+  at::Tensor h = out.cpu();
+  return {h[0].item<int64_t>(), h[1].item<int64_t>()};
+}
+
 void zero1_push_partials(at::Tensor partial, at::Tensor ranges, std::vector<int64_t> slots,
                          std::vector<int64_t> lo, int64_t stride, int64_t rank) {
   c10::cuda::CUDAGuard guard(partial.device());
@@ -665,6 +683,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("launch_count", &launch_count);
   m.def("install_segv_backtrace", &install_segv_backtrace);
   m.def("status_read_clear", &status_read_clear);
+  m.def("wait_probe", &wait_probe);
   m.attr("EPI_BF16") = static_cast<int>(ewb::kEpiBf16);
   m.attr("EPI_GELU") = static_cast<int>(ewb::kEpiGelu);
   m.attr("EPI_RESID") = static_cast<int>(ewb::kEpiResid);

@@ -90,8 +90,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Wait for the phase with the given parity to complete. Returns false when the
-// global-time limit ran out or another role of this launch already failed.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
+// global-time limit (limit_ns, kWaitLimitNs unless a caller passes its own) ran
+// out or another role of this launch already failed.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   while (true) {
@@ -99,11 +101,28 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(bar, parity)) return true;
     if (status_failed(status)) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       record_status(status, code);
       return false;
     }
   }
+}
+
+// Wait until the int at `flag` (global memory, written by another CTA, kernel
+// or GPU) equals `want`, with the same bound and status record as mbar_wait.
+__device__ __forceinline__ bool flag_wait(const int* flag, int want, int* status, int code,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
+  const volatile int* f = reinterpret_cast<const volatile int*>(flag);
+  const unsigned long long t0 = globaltimer_ns();
+  while (*f != want) {
+    if (status_failed(status)) return false;
+    if (globaltimer_ns() - t0 > limit_ns) {
+      record_status(status, code);
+      return false;
+    }
+    __nanosleep(256);
+  }
+  return true;
 }
 
 // ---------------------------------------------------------------- TMA (local memory only)

@@ -150,6 +150,10 @@ int quant_e4m3_rows(const __nv_bfloat16* x, int T, int d, uint8_t* q, float* sca
 int dequant_e4m3_rows(const uint8_t* q, const float* scale, int T, int d, __nv_bfloat16* y,
                       cudaStream_t stream);
 int cast_f32_bf16(const float* x, __nv_bfloat16* y, int64_t n, cudaStream_t stream);
+// One bounded wait (mode 0: mbarrier phase, 1: global flag) with a caller
+// limit; completes only if `release`. out[2]: {completed, waited ns}.
+int wait_probe(int mode, int release, int* flag, unsigned long long limit_ns, int* status,
+               long long* out, cudaStream_t stream);
 
 // ---------------------------------------------------------------- ZeRO-1 over peer memory
 int zero1_push_partials(const float* partial, const long long* ranges_dev, int nranges,

@@ -73,7 +73,35 @@ __global__ void cast_kernel(const float* __restrict__ x, __nv_bfloat16* __restri
     y[i] = __float2bfloat16_rn(x[i]);
 }
 
+// The bounded waits in one launch: an mbarrier phase (mode 0) or a global
+// flag (mode 1) that completes only if `release` is set, waited on with the
+// caller's limit. out[0] = 1 if the wait completed, 0 if it gave up;
+// out[1] = nanoseconds spent waiting.
+__global__ void wait_probe_kernel(int mode, int release, int* flag, unsigned long long limit_ns,
+                                  int* status, long long* out) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x != 0) return;
+  mbar_init(&bar, 1);
+  fence_mbar_init();
+  if (release) {
+    if (mode == 0) mbar_arrive(&bar);
+    else atomicExch(flag, 1);
+  }
+  const unsigned long long t0 = globaltimer_ns();
+  const bool ok = mode == 0 ? mbar_wait(&bar, 0, status, kStatusTimeoutSmemFull, limit_ns)
+                            : flag_wait(flag, 1, status, kStatusTimeoutPeer, limit_ns);
+  out[0] = ok ? 1 : 0;
+  out[1] = static_cast<long long>(globaltimer_ns() - t0);
+}
+
 }  // namespace
+
+int wait_probe(int mode, int release, int* flag, unsigned long long limit_ns, int* status,
+               long long* out, cudaStream_t stream) {
+  if (mode != 0 && mode != 1) return 1;
+  wait_probe_kernel<<<1, 32, 0, stream>>>(mode, release, flag, limit_ns, status, out);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
 
 int colsum_part_rows(int T) { return (T + kColRows - 1) / kColRows; }
 

@@ -78,6 +78,40 @@ class LocalCluster:
             if n == name and p.poll() is None:
                 os.killpg(p.pid, signal.SIGSTOP)
 
+    def _stage_pid(self, name: str) -> int | None:
+        try:
+            with open(os.path.join(self.workdir, name, "stage.pid")) as f:
+                return int(f.read().strip())
+        except (OSError, ValueError):
+            return None
+
+    def kill_stage(self, name: str):
+        """SIGKILL the worker's stage process group; the agent survives and
+        reports the exit (no done marker): a stage killed from outside."""
+        pid = self._stage_pid(name)
+        if pid:
+            try:
+                os.killpg(pid, signal.SIGKILL)
+            except ProcessLookupError:
+                pass
+
+    def freeze_stage(self, name: str):
+        """SIGSTOP the worker's stage: alive and heartbeating (its agent runs),
+        but no progress anywhere."""
+        pid = self._stage_pid(name)
+        if pid:
+            try:
+                os.killpg(pid, signal.SIGSTOP)
+            except ProcessLookupError:
+                pass
+
+    def sever_control(self, name: str):
+        """Close the coordinator's side of a worker's control connection (a
+        control-plane blip); the agent dials back with its node id."""
+        nid = self.node_of(name)
+        if nid is not None:
+            self.coord.nodes[nid].ch.close()
+
     def run(self, job):
         return self.coord.run_job(job)
 

@@ -70,6 +70,8 @@ class StageEngine:
         side = os.environ.get("EWB_W_STREAM", "1") == "1"
         self.wexec = WExecutor(self.device, enabled=side)
         self.phase: dict = {}
+        # Marker lines (WT_*) go to stdout, where a stage's agent reads them.
+        self.log = lambda line: print(line, flush=True)
         self.zero1 = None
         if comm is not None:
             self.attach_comm(comm)
@@ -290,6 +292,7 @@ class StageEngine:
         if self.zero1 is not None:
             self.zero1.sync_and_step()
         else:
+            self._promote_moments()
             self.opt.step()
         self._tied_relay()
         self.model.after_step()
@@ -307,6 +310,25 @@ class StageEngine:
             for mb, v in out:
                 self.losses.append((step, mb, v))
         return out
+
+    def _promote_moments(self):
+        """Before the third optimizer step of a stage whose AdamW moments live
+        in host memory, move as long a prefix of them onto the device as the
+        first two steps' peak leaves room for (the card's memory less the peak
+        reserved by the caching allocator and a margin of 3% of the card, at
+        least 2 GiB). WANTRAIN_OPT_RESIDENT=off keeps every moment on the host.
+        The update is the same kernel on the same values, so bits do not change
+        (reference: _promote_moments, src/wantrain/runtime/stage.py:3124)."""
+        self._opt_steps = getattr(self, "_opt_steps", 0) + 1
+        if self._opt_steps != 3 or not isinstance(self.opt, optim.HostAdamW) or \
+                self.device.type != "cuda" or os.environ.get("WANTRAIN_OPT_RESIDENT") == "off":
+            return
+        total = torch.cuda.get_device_properties(self.device).total_memory
+        peak = torch.cuda.max_memory_reserved(self.device)
+        room = total - peak - max(2 << 30, int(0.03 * total))
+        moved = self.opt.promote(room) if room > 0 else 0
+        self.log(f"WT_OPT resident bytes={moved} elements={self.opt.resident}/"
+                 f"{self.opt.p.numel()} room={room} peak={peak}")
 
     def _tied_fold(self):
         """Tied embeddings: the table's gradient becomes (embedding part) +

@@ -43,7 +43,15 @@ class DeviceAdamW:
 
 class HostAdamW(DeviceAdamW):
     """Moments in pinned host memory, streamed through two device staging
-    buffers: chunk i computes while chunk i+1 loads and chunk i-1 stores."""
+    buffers: chunk i computes while chunk i+1 loads and chunk i-1 stores.
+
+    Partial residency (`promote`): the moments of the first `resident`
+    elements can move to the device when memory allows; those elements update
+    in place with one kernel launch and only the rest cross PCIe. The same
+    kernel runs on the same values wherever the moments live, so the bits do
+    not change (reference: HostAdamW.promote, src/wantrain/runtime/optim.py:208,
+    which moves whole parameters; here the resident part is a prefix of the
+    flat store)."""
 
     def __init__(self, master, grad, work, lr, adamw: dict, chunk: int = HOST_CHUNK):
         self.p, self.g, self.work = master, grad, work
@@ -57,6 +65,8 @@ class HostAdamW(DeviceAdamW):
         self.m = torch.zeros(n, dtype=torch.float32, pin_memory=pin)
         self.v = torch.zeros(n, dtype=torch.float32, pin_memory=pin)
         self.chunk = min(chunk, n)
+        self.resident = 0  # elements whose moments live on the device
+        self.m_dev = self.v_dev = None
         if pin:
             dev = master.device
             self.stage = [(torch.empty(self.chunk, device=dev), torch.empty(self.chunk, device=dev))
@@ -66,6 +76,36 @@ class HostAdamW(DeviceAdamW):
             self.copy = torch.cuda.Stream(device=dev)
             self.copy_out = torch.cuda.Stream(device=dev)
 
+    def promote(self, budget_bytes: int) -> int:
+        """Move the moments of a longer prefix onto the device, within
+        `budget_bytes` more device memory (8 bytes per element). -> bytes moved."""
+        if not self.p.is_cuda:
+            return 0
+        n = self.p.numel()
+        want = min(n, self.resident + max(0, int(budget_bytes)) // 8)
+        if want < n:
+            want -= want % 64
+        if want <= self.resident:
+            return 0
+        old = self.resident
+        dev = self.p.device
+        m_dev = torch.empty(want, dtype=torch.float32, device=dev)
+        v_dev = torch.empty(want, dtype=torch.float32, device=dev)
+        if old:
+            m_dev[:old].copy_(self.m_dev)
+            v_dev[:old].copy_(self.v_dev)
+        m_dev[old:].copy_(self.m[old:want])
+        v_dev[old:].copy_(self.v[old:want])
+        torch.cuda.synchronize(dev)
+        self.m_dev, self.v_dev, self.resident = m_dev, v_dev, want
+        return 8 * (want - old)
+
+    def _sync_host(self):
+        """The device-resident prefix back into the host copies (the state)."""
+        if self.resident:
+            self.m[:self.resident].copy_(self.m_dev)
+            self.v[:self.resident].copy_(self.v_dev)
+
     def step(self):
         self.t += 1
         if not self.p.is_cuda:
@@ -73,11 +113,18 @@ class HostAdamW(DeviceAdamW):
                       self.eps, self.wd, self.t)
             return
         n = self.p.numel()
+        R = self.resident
+        if R:
+            work = self.work[:R] if self.work is not None else None
+            ops.adamw(self.p[:R], self.m_dev, self.v_dev, self.g[:R], work, self.lr, self.b1,
+                      self.b2, self.eps, self.wd, self.t)
+        if R >= n:
+            return
         comp = torch.cuda.current_stream(self.p.device)
         loaded = [torch.cuda.Event(), torch.cuda.Event()]
         computed = [torch.cuda.Event(), torch.cuda.Event()]
         stored = [None, None]
-        starts = list(range(0, n, self.chunk))
+        starts = list(range(R, n, self.chunk))
 
         def load(i):
             b = i % 2
@@ -114,12 +161,16 @@ class HostAdamW(DeviceAdamW):
                 comp.wait_event(ev)
 
     def state_dict(self):
+        self._sync_host()
         return {"t": self.t, "m": self.m.clone(), "v": self.v.clone()}
 
     def load_state_dict(self, sd):
         self.t = int(sd["t"])
         self.m.copy_(sd["m"])
         self.v.copy_(sd["v"])
+        if self.resident:
+            self.m_dev.copy_(self.m[:self.resident])
+            self.v_dev.copy_(self.v[:self.resident])
 
 
 def build(name: str, master, grad, work, lr, adamw: dict):

@@ -348,6 +348,37 @@ def test_adamw(cuda):
     assert torch.equal(pb, p.to(torch.bfloat16))
 
 
+def test_host_adamw_partial_residency_is_bitwise(cuda):
+    """Host-resident moments streamed in chunks, with a prefix promoted to the
+    device after two steps, give the same bits as device moments."""
+    from elysium_wan_b200.runtime.optim import DeviceAdamW, HostAdamW
+
+    torch.manual_seed(10)
+    n = 300_001
+    hp = dict(betas=[0.9, 0.95], eps=1e-8, weight_decay=0.1)
+    p0 = torch.randn(n, device=cuda)
+    grads = [torch.randn(n, device=cuda) for _ in range(5)]
+    a_p, b_p = p0.clone(), p0.clone()
+    a_w = torch.empty(n, dtype=torch.bfloat16, device=cuda)
+    b_w = torch.empty_like(a_w)
+    a_g, b_g = torch.empty(n, device=cuda), torch.empty(n, device=cuda)
+    dev = DeviceAdamW(a_p, a_g, a_w, 1e-3, hp)
+    host = HostAdamW(b_p, b_g, b_w, 1e-3, hp, chunk=65_536)
+    for k, g in enumerate(grads):
+        if k == 2:
+            assert host.promote(8 * 100_000) == 8 * 99_968  # rounded down to 64 elements
+        if k == 3:
+            host.promote(8 * 50_000)  # grows the prefix
+        a_g.copy_(g)
+        b_g.copy_(g)
+        dev.step()
+        host.step()
+    torch.cuda.synchronize()
+    assert torch.equal(a_p, b_p) and torch.equal(a_w, b_w)
+    sd = host.state_dict()
+    assert torch.equal(sd["m"], dev.m.cpu()) and torch.equal(sd["v"], dev.v.cpu())
+
+
 def test_colsum_and_fp8(cuda):
     torch.manual_seed(9)
     x = bf(3000, 777, dev=cuda)
