@@ -226,6 +226,66 @@ void gemm_impl(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor out,
   count(1);
 }
 
+// Fused head + cross-entropy, the GEMM half: logits of h [T][d] x W [V][d]
+// never stored; per 256-wide vocabulary tile each row leaves (max, sum exp) in
+// part [T][nt][2], the target logit in tgt_logit [T], and fp16 exp(x - tile
+// max) in buf [T][ld] (a 2-byte buffer the finalize turns into the bf16
+// gradient in place).
+void gemm_lse(at::Tensor h, at::Tensor w, at::Tensor buf, int64_t V, at::Tensor targets,
+              at::Tensor part, at::Tensor tgt_logit) {
+  check_2d_rowmajor(h, "h");
+  check_2d_rowmajor(w, "w");
+  check_2d_rowmajor(buf, "buf");
+  TORCH_CHECK(h.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16,
+              "gemm operands must be bf16");
+  TORCH_CHECK(buf.element_size() == 2 && buf.size(0) == h.size(0) && buf.size(1) >= V,
+              "buf must be a 2-byte [T][>= V] buffer");
+  TORCH_CHECK(w.size(0) == V && w.size(1) == h.size(1), "w must be [V][d]");
+  TORCH_CHECK(targets.scalar_type() == at::kLong && targets.numel() == h.size(0), "targets int64 [T]");
+  TORCH_CHECK(part.scalar_type() == at::kFloat && part.is_contiguous() && part.dim() == 3 &&
+                  part.size(0) == h.size(0) && part.size(1) == (V + 255) / 256 && part.size(2) == 2,
+              "part must be fp32 [T][ceil(V/256)][2]");
+  TORCH_CHECK(tgt_logit.scalar_type() == at::kFloat && tgt_logit.numel() == h.size(0),
+              "tgt_logit fp32 [T]");
+  c10::cuda::CUDAGuard guard(h.device());
+  ewb::GemmArgs g{};
+  g.a = h.data_ptr();
+  g.lda = h.stride(0);
+  g.b = w.data_ptr();
+  g.ldb = w.stride(0);
+  g.M = h.size(0);
+  g.N = static_cast<int>(V);
+  g.K = h.size(1);
+  g.bn = 256;
+  g.split = gemm_split_flag();
+  g.status = status_word(h.get_device());
+  ewb::GemmEpilogue& e = g.ep;
+  e.kind = ewb::kEpiLse;
+  e.out = buf.data_ptr();
+  e.ldo = buf.stride(0);
+  e.targets = reinterpret_cast<const long long*>(targets.data_ptr<int64_t>());
+  e.lse_part = part.data_ptr<float>();
+  e.ld_part = part.size(1);
+  e.tgt_logit = tgt_logit.data_ptr<float>();
+  ok(ewb::gemm_launch(g, cur_stream()), "gemm_lse");
+  count(1);
+}
+
+void ce_lse_finalize(at::Tensor part, at::Tensor tgt_logit, at::Tensor targets, int64_t V,
+                     at::Tensor buf, double grad_scale, at::Tensor loss_rows) {
+  check_2d_rowmajor(buf, "buf");
+  TORCH_CHECK(buf.is_contiguous() && buf.element_size() == 2, "buf: dense 2-byte [T][ld]");
+  TORCH_CHECK(part.scalar_type() == at::kFloat && part.is_contiguous(), "part fp32");
+  c10::cuda::CUDAGuard guard(buf.device());
+  ok(ewb::ce_lse_finalize(part.data_ptr<float>(), part.size(1), part.size(1),
+                          tgt_logit.data_ptr<float>(), targets.data_ptr<int64_t>(), buf.size(0),
+                          static_cast<int>(V), buf.data_ptr(), buf.size(1),
+                          static_cast<float>(grad_scale), loss_rows.data_ptr<float>(),
+                          cur_stream()),
+     "ce_lse_finalize");
+  count(1);
+}
+
 int64_t gemm_pick_bn(int64_t M, int64_t N, int64_t K) {
   return ewb::gemm_pick_bn(M, N, K, gemm_split_flag() != 0);
 }
@@ -659,6 +719,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_gemm_split", &set_gemm_split);
   m.def("gemm_peer_scatter", &gemm_peer_scatter);
   m.def("gemm_pair", &gemm_pair);
+  m.def("gemm_lse", &gemm_lse);
+  m.def("ce_lse_finalize", &ce_lse_finalize);
   m.def("zero1_push_partials", &zero1_push_partials);
   m.def("zero1_fold_slots", &zero1_fold_slots);
   m.def("zero1_adamw_push", &zero1_adamw_push);

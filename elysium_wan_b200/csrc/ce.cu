@@ -190,7 +190,98 @@ __global__ void __launch_bounds__(1024) mean_kernel(const float* __restrict__ x,
   }
 }
 
+// Fused head + cross-entropy, second half (the first is the kEpiLse epilogue
+// of the logits GEMM, which leaves per 256-wide vocabulary tile k of a row its
+// max m_k and sum s_k of exp(x - m_k), the fp32 target logit, and fp16
+// e = exp(x - m_k) in the gradient buffer). One CTA per row:
+//   LSE  = M + log(sum_k s_k exp(m_k - M)),  M = max_k m_k  (fixed trees)
+//   loss = LSE - x[target]
+//   grad = (e * exp(m_k - LSE) - onehot) * grad_scale, rounded once to bf16 and
+//          written over e in place; columns V .. ld are zeroed.
+// The fp32 logits never exist in memory.
+constexpr int kFinThreads = 256;
+constexpr int kFinMaxTiles = 1024;  // vocabularies up to 256K
+
+__device__ __forceinline__ float block_reduce_fin(float v, float* red, bool is_max) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float u = __shfl_xor_sync(0xffffffffu, v, o);
+    v = is_max ? fmaxf(v, u) : v + u;
+  }
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    v = l < kFinThreads / 32 ? red[l] : (is_max ? -INFINITY : 0.f);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float u = __shfl_xor_sync(0xffffffffu, v, o);
+      v = is_max ? fmaxf(v, u) : v + u;
+    }
+    if (l == 0) red[32] = v;
+  }
+  __syncthreads();
+  return red[32];
+}
+
+__global__ void __launch_bounds__(kFinThreads)
+    ce_lse_finalize_kernel(const float2* __restrict__ part, int nt, int ld_part,
+                           const float* __restrict__ tgt_logit, const int64_t* __restrict__ targets,
+                           int V, uint16_t* __restrict__ buf, int ld, float grad_scale,
+                           float* __restrict__ loss_rows) {
+  __shared__ float fac[kFinMaxTiles];
+  __shared__ float red[33];
+  const int row = blockIdx.x;
+  const float2* pr = part + static_cast<size_t>(row) * ld_part;
+  float m = -INFINITY;
+  for (int k = threadIdx.x; k < nt; k += kFinThreads) m = fmaxf(m, pr[k].x);
+  const float M = block_reduce_fin(m, red, true);
+  float s = 0.f;
+  for (int k = threadIdx.x; k < nt; k += kFinThreads) {
+    const float2 p = pr[k];
+    s += p.y * expf(p.x - M);
+  }
+  const float S = block_reduce_fin(s, red, false);
+  const float lse = M + logf(S);
+  const int64_t tgt = targets[row];
+  if (threadIdx.x == 0) loss_rows[row] = lse - tgt_logit[row];
+  for (int k = threadIdx.x; k < nt; k += kFinThreads) fac[k] = expf(pr[k].x - lse);
+  __syncthreads();
+  uint16_t* g = buf + static_cast<size_t>(row) * ld;
+  // 8 columns (16 bytes) per thread and iteration; ld is a multiple of 8 and
+  // a 256-wide tile holds whole groups of 8.
+  for (int j = threadIdx.x * 8; j < ld; j += kFinThreads * 8) {
+    uint4 w = *reinterpret_cast<const uint4*>(g + j);
+    uint32_t u[4] = {w.x, w.y, w.z, w.w};
+    const float f = j < V ? fac[j >> 8] : 0.f;
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const __half2 e = *reinterpret_cast<const __half2*>(&u[h]);
+      const float2 ef = __half22float2(e);
+      const int c0 = j + 2 * h;
+      float d0 = 0.f, d1 = 0.f;
+      if (c0 < V) d0 = (ef.x * f - (c0 == tgt ? 1.0f : 0.0f)) * grad_scale;
+      if (c0 + 1 < V) d1 = (ef.y * f - (c0 + 1 == tgt ? 1.0f : 0.0f)) * grad_scale;
+      u[h] = pack_bf16x2(d0, d1);
+    }
+    *reinterpret_cast<uint4*>(g + j) = make_uint4(u[0], u[1], u[2], u[3]);
+  }
+}
+
 }  // namespace
+
+int ce_lse_finalize(const float* part, int nt, int ld_part, const float* tgt_logit,
+                    const int64_t* targets, int T, int V, void* buf, int ld, float grad_scale,
+                    float* loss_rows, cudaStream_t stream) {
+  if (T <= 0 || V <= 0 || nt != (V + 255) / 256 || nt > kFinMaxTiles || ld_part < nt ||
+      ld < V || ld % 8 || (reinterpret_cast<uintptr_t>(buf) & 15))
+    return 1;
+  ce_lse_finalize_kernel<<<T, kFinThreads, 0, stream>>>(
+      reinterpret_cast<const float2*>(part), nt, ld_part, tgt_logit, targets, V,
+      reinterpret_cast<uint16_t*>(buf), ld, grad_scale, loss_rows);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
 
 int cross_entropy(const CeArgs& a, cudaStream_t stream) {
   if (a.T <= 0 || a.V <= 0 || a.ldl < a.V || (a.dlogits && a.ldg < a.V)) return 1;

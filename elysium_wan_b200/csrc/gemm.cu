@@ -248,7 +248,63 @@ template <int EPI, int BN>
 __device__ __forceinline__ void epilogue_tile_regs(const AccSrc& acc, int gm, int nbase, int M, int N,
                                                    const GemmEpilogue& ep) {
   const bool row_ok = gm < M;
-  if constexpr (EPI == kEpiResidQ8) {
+  if constexpr (EPI == kEpiLse) {
+    // Fused head + cross-entropy, first half: this row's part of one 256-wide
+    // vocabulary tile. Two passes over TMEM: the tile max m, then e = exp(x - m)
+    // stored as fp16 (the finalize kernel turns it into the gradient in place)
+    // and summed in column order; (m, sum) goes to the partials, and the tile
+    // that holds the row's target also records the target's fp32 logit.
+    // Every lane runs both passes (tcgen05.ld is warp-collective); a row past
+    // M only skips its stores.
+    const long long tgt = row_ok ? ep.targets[gm] : -1;
+    float mx = -INFINITY;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      float f[32];
+      acc_ld32<BN>(acc, c, f);
+      const int n0 = nbase + c;
+      const int valid = (row_ok && n0 < N) ? min(32, N - n0) : 0;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        if (i < valid) mx = fmaxf(mx, f[i]);
+        if (n0 + i == tgt && i < valid) ep.tgt_logit[gm] = f[i];
+      }
+    }
+    float sum = 0.f;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      float f[32];
+      acc_ld32<BN>(acc, c, f);
+      const int n0 = nbase + c;
+      if (!row_ok || n0 >= N) continue;
+      const int valid = min(32, N - n0);
+      uint32_t w[16];
+#pragma unroll
+      for (int h = 0; h < 16; ++h) {
+        const float e0 = (2 * h < valid) ? expf(f[2 * h] - mx) : 0.f;
+        const float e1 = (2 * h + 1 < valid) ? expf(f[2 * h + 1] - mx) : 0.f;
+        sum += e0;
+        sum += e1;
+        const __half2 hv = __floats2half2_rn(e0, e1);
+        w[h] = *reinterpret_cast<const uint32_t*>(&hv);
+      }
+      __half* dst = reinterpret_cast<__half*>(ep.out) + static_cast<size_t>(gm) * ep.ldo + n0;
+      if (valid == 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+        uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) d4[j] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+      } else {
+#pragma unroll
+        for (int h = 0; h < 16; ++h) {
+          if (2 * h < valid) dst[2 * h] = __ushort_as_half(static_cast<unsigned short>(w[h] & 0xffffu));
+          if (2 * h + 1 < valid) dst[2 * h + 1] = __ushort_as_half(static_cast<unsigned short>(w[h] >> 16));
+        }
+      }
+    }
+    if (row_ok)
+      reinterpret_cast<float2*>(ep.lse_part)[static_cast<size_t>(gm) * ep.ld_part + nbase / BN] =
+          make_float2(mx, sum);
+  } else if constexpr (EPI == kEpiResidQ8) {
     // fp8 e4m3 with one power-of-two scale per 128 columns of a row, in two
     // passes over TMEM (amax, then quantise) so no 128-value array is held.
     const int nblk = ep.ld_scale_out;
@@ -881,6 +937,9 @@ int dispatch_bn(const GemmArgs& g, cudaStream_t s, int* sc, float* ws) {
       case kEpiResidQ8: return launch_cfg<BN, false, false, kEpiResidQ8>(g, s, sc, ws);
       case kEpiF32: return launch_cfg<BN, false, false, kEpiF32>(g, s, sc, ws);
       case kEpiAccF32: return launch_cfg<BN, false, false, kEpiAccF32>(g, s, sc, ws);
+      case kEpiLse:
+        if constexpr (BN == 256) return launch_cfg<BN, false, false, kEpiLse>(g, s, sc, ws);
+        break;
       default: break;
     }
   } else if (!g.a_mn && g.b_mn) {
@@ -954,6 +1013,13 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
   int bn = g.bn;
   if (bn != 128 && bn != 192 && bn != 256) bn = gemm_pick_bn(g.M, g.N, g.K + g.K2, g.split != 0);
   if (g.ep.kind == kEpiResidQ8) bn = 256;  // a tile covers whole 128-column scale blocks
+  if (g.ep.kind == kEpiLse) {
+    // the partials are indexed by 256-wide vocabulary tile
+    if (g.ep.targets == nullptr || g.ep.lse_part == nullptr || g.ep.tgt_logit == nullptr ||
+        g.ep.ld_part < (g.N + 255) / 256 || g.ep.ldo % 8 || g.a_mn || g.b_mn)
+      return kGemmErrShape;
+    bn = 256;
+  }
   const StreamState st = stream_state(stream, g.split != 0);
   if (st.counters == nullptr) return kGemmErrLaunch;
   if (bn == 128) return dispatch_bn<128>(g, stream, st.counters, st.ws);

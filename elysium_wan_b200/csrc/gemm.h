@@ -15,6 +15,8 @@ enum GemmEpilogueKind : int {
   kEpiDGelu = 5,    // out bf16 = acc * gelu'(aux)
   kEpiF32 = 6,      // out f32 = acc (+ bias)
   kEpiAccF32Peer = 7,  // owner slot (peer memory) = out (local f32 partial) + acc: ZeRO-1 RS
+  kEpiLse = 8,  // logits tile -> per-row (tile max, sum exp) partials, target logit,
+                // out fp16 = exp(acc - tile max); the logits themselves are never stored
 };
 
 constexpr int kMaxPeers = 8;
@@ -56,6 +58,12 @@ struct GemmEpilogue {
   int ld_scale_out;
   float beta;
   PeerScatter peer;  // kEpiAccF32Peer only
+  // kEpiLse only (tiles are 256 wide): targets[M] (int64), lse_part[M][ld_part]
+  // float2 (tile max, sum of exp over the tile), tgt_logit[M] fp32.
+  const long long* targets;
+  float* lse_part;
+  int ld_part;
+  float* tgt_logit;
 };
 
 struct GemmArgs {

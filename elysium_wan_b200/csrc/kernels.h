@@ -101,6 +101,12 @@ struct CeArgs {
   int* status;  // device status word for the bounded waits (may be null)
 };
 int cross_entropy(const CeArgs& a, cudaStream_t stream);
+// Second half of the fused head + cross-entropy (after the kEpiLse logits
+// GEMM): per-row LSE from the 256-wide tile partials, loss rows, and the bf16
+// gradient written over the fp16 exp(x - tile max) values in `buf` ([T][ld]).
+int ce_lse_finalize(const float* part, int nt, int ld_part, const float* tgt_logit,
+                    const int64_t* targets, int T, int V, void* buf, int ld, float grad_scale,
+                    float* loss_rows, cudaStream_t stream);
 // out[0] = sum(x[0..n)) / n, fixed-order tree (deterministic).
 int mean_reduce(const float* x, int n, float* out, cudaStream_t stream);
 

@@ -8,10 +8,10 @@
 // format with one power-of-two scale per 128 columns: the dequantisation is the
 // prologue of this kernel (the next stage's first op after a stage cut).
 //
-// Backward: one CTA per chunk of rows. Each thread owns the same columns in
-// every row of its chunk, so dgamma/dbeta partial sums accumulate in registers
-// and are written once per chunk; a second kernel folds the chunk partials in
-// chunk order into the fp32 gradients. No atomics anywhere.
+// Backward: dx with one warp per row (warp-shuffle row sums, no block
+// barrier); dgamma/dbeta as per-chunk column partials (each thread owns 8
+// columns over the chunk's rows, summed in row order) that a third kernel
+// folds in chunk order into the fp32 gradients. No atomics anywhere.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -127,90 +127,109 @@ __global__ void __launch_bounds__(kLnThreads)
 }
 
 // dx = rstd * (g - mean(g) - xhat * mean(g * xhat)) (+ dres), g = dy * gamma.
-// Partial dgamma = sum dy * xhat and dbeta = sum dy over the rows of the chunk.
 // RMSNorm (RMS = true): mean = 0 and no centring of g, dx = rstd * (g - xhat * mean(g * xhat)).
-template <int S, bool RMS>
-__global__ void __launch_bounds__(kLnThreads)
-    layernorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, int lddy, const void* __restrict__ x,
-                         const float* __restrict__ xs, int x_fp8, int ldx, int ldxs,
-                         const float* __restrict__ mean, const float* __restrict__ rstd,
-                         const float* __restrict__ gamma, const __nv_bfloat16* __restrict__ dres,
-                         int lddres, __nv_bfloat16* __restrict__ dx, int lddx,
-                         float* __restrict__ part_g, float* __restrict__ part_b, int rows, int d,
-                         int rows_per_chunk) {
-  __shared__ float red[4];
-  const int chunk = blockIdx.x;
-  const int r0 = chunk * rows_per_chunk;
-  const int r1 = min(rows, r0 + rows_per_chunk);
-  float pg[S][8];
-  float pb[S][8];
-#pragma unroll
-  for (int j = 0; j < S; ++j)
+//
+// One warp per row: lane l owns columns 256 j + 8 l (16-byte loads), the two
+// row sums are per-lane sums in column order then a fixed butterfly, so no
+// block barrier stands between the loads; the second pass re-reads the row
+// from cache. Eight rows per CTA.
+constexpr int kLnBwdWarps = 8;
+
+template <bool RMS>
+__global__ void __launch_bounds__(kLnBwdWarps * 32)
+    layernorm_bwd_dx_kernel(const __nv_bfloat16* __restrict__ dy, int lddy, const void* __restrict__ x,
+                            const float* __restrict__ xs, int x_fp8, int ldx, int ldxs,
+                            const float* __restrict__ mean, const float* __restrict__ rstd,
+                            const float* __restrict__ gamma, const __nv_bfloat16* __restrict__ dres,
+                            int lddres, __nv_bfloat16* __restrict__ dx, int lddx, int rows, int d) {
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kLnBwdWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const float mu = RMS ? 0.f : mean[row];
+  const float rs = rstd[row];
+  float s1 = 0.f, s2 = 0.f;
+#pragma unroll 4
+  for (int col = lane * 8; col < d; col += 256) {
+    float xv[8], dv[8], gm[8];
+    load8(x, xs, x_fp8, ldx, ldxs, row, col, xv);
+    load8(dy, nullptr, 0, lddy, 0, row, col, dv);
+    load8_f32(gamma + col, gm);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      pg[j][i] = 0.f;
-      pb[j][i] = 0.f;
-    }
-  for (int row = r0; row < r1; ++row) {
-    const float mu = mean[row];
-    const float rs = rstd[row];
-    float s1 = 0.f, s2 = 0.f;
-#pragma unroll
-    for (int j = 0; j < S; ++j) {
-      const int col = j * 1024 + threadIdx.x * 8;
-      if (col < d) {
-        float xv[8], dv[8], gm[8];
-        load8(x, xs, x_fp8, ldx, ldxs, row, col, xv);
-        load8(dy, nullptr, 0, lddy, 0, row, col, dv);
-        load8_f32(gamma + col, gm);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float xh = (xv[i] - mu) * rs;
-          const float g = dv[i] * gm[i];
-          s1 += g;
-          s2 += g * xh;
-          pg[j][i] += dv[i] * xh;
-          pb[j][i] += dv[i];
-        }
-      }
-    }
-    const float m1 = RMS ? 0.f : block_sum_128(s1, red) / static_cast<float>(d);
-    const float m2 = block_sum_128(s2, red) / static_cast<float>(d);
-    // Second pass re-reads the row (L1/L2 resident) instead of holding it.
-#pragma unroll
-    for (int j = 0; j < S; ++j) {
-      const int col = j * 1024 + threadIdx.x * 8;
-      if (col < d) {
-        float xv[8], dv[8], o[8], gm[8];
-        load8(x, xs, x_fp8, ldx, ldxs, row, col, xv);
-        load8(dy, nullptr, 0, lddy, 0, row, col, dv);
-        load8_f32(gamma + col, gm);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float xh = (xv[i] - mu) * rs;
-          const float g = dv[i] * gm[i];
-          o[i] = rs * (g - m1 - xh * m2);
-        }
-        if (dres != nullptr) {
-          float rv[8];
-          load8(dres, nullptr, 0, lddres, 0, row, col, rv);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) o[i] += rv[i];
-        }
-        store8_bf16(dx + static_cast<size_t>(row) * lddx + col, o);
-      }
+      const float g = dv[i] * gm[i];
+      s1 += g;
+      s2 += g * ((xv[i] - mu) * rs);
     }
   }
 #pragma unroll
-  for (int j = 0; j < S; ++j) {
-    const int col = j * 1024 + threadIdx.x * 8;
-    if (col < d) {
+  for (int o = 16; o > 0; o >>= 1) {
+    s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+    s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+  }
+  const float m1 = RMS ? 0.f : s1 / static_cast<float>(d);
+  const float m2 = s2 / static_cast<float>(d);
+#pragma unroll 4
+  for (int col = lane * 8; col < d; col += 256) {
+    float xv[8], dv[8], gm[8], o[8];
+    load8(x, xs, x_fp8, ldx, ldxs, row, col, xv);
+    load8(dy, nullptr, 0, lddy, 0, row, col, dv);
+    load8_f32(gamma + col, gm);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        part_g[static_cast<size_t>(chunk) * d + col + i] = pg[j][i];
-        if (!RMS) part_b[static_cast<size_t>(chunk) * d + col + i] = pb[j][i];
-      }
+    for (int i = 0; i < 8; ++i) {
+      const float xh = (xv[i] - mu) * rs;
+      o[i] = rs * (dv[i] * gm[i] - m1 - xh * m2);
     }
+    if (dres != nullptr) {
+      float rv[8];
+      load8(dres, nullptr, 0, lddres, 0, row, col, rv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] += rv[i];
+    }
+    store8_bf16(dx + static_cast<size_t>(row) * lddx + col, o);
+  }
+}
+
+// dgamma / dbeta partial sums of one chunk of rows: thread t of CTA (bx, chunk)
+// owns columns 1024 bx + 8 t and sums dy * xhat and dy over the chunk's rows
+// in row order; the chunks are folded in chunk order by fold_partials_kernel.
+template <bool RMS>
+__global__ void __launch_bounds__(kLnThreads)
+    layernorm_bwd_param_kernel(const __nv_bfloat16* __restrict__ dy, int lddy,
+                               const void* __restrict__ x, const float* __restrict__ xs, int x_fp8,
+                               int ldx, int ldxs, const float* __restrict__ mean,
+                               const float* __restrict__ rstd, float* __restrict__ part_g,
+                               float* __restrict__ part_b, int rows, int d, int rows_per_chunk) {
+  const int col = blockIdx.x * 1024 + threadIdx.x * 8;
+  const int chunk = blockIdx.y;
+  if (col >= d) return;
+  const int r0 = chunk * rows_per_chunk;
+  const int r1 = min(rows, r0 + rows_per_chunk);
+  float pg[8], pb[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    pg[i] = 0.f;
+    pb[i] = 0.f;
+  }
+#pragma unroll 4
+  for (int row = r0; row < r1; ++row) {
+    float xv[8], dv[8];
+    load8(x, xs, x_fp8, ldx, ldxs, row, col, xv);
+    load8(dy, nullptr, 0, lddy, 0, row, col, dv);
+    const float mu = RMS ? 0.f : __ldg(mean + row);
+    const float rs = __ldg(rstd + row);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      pg[i] += dv[i] * ((xv[i] - mu) * rs);
+      pb[i] += dv[i];
+    }
+  }
+  float4* g4 = reinterpret_cast<float4*>(part_g + static_cast<size_t>(chunk) * d + col);
+  g4[0] = make_float4(pg[0], pg[1], pg[2], pg[3]);
+  g4[1] = make_float4(pg[4], pg[5], pg[6], pg[7]);
+  if (!RMS) {
+    float4* b4 = reinterpret_cast<float4*>(part_b + static_cast<size_t>(chunk) * d + col);
+    b4[0] = make_float4(pb[0], pb[1], pb[2], pb[3]);
+    b4[1] = make_float4(pb[4], pb[5], pb[6], pb[7]);
   }
 }
 
@@ -265,34 +284,34 @@ int layernorm_fwd(const LnArgs& a, cudaStream_t stream) {
 }
 
 int layernorm_bwd_rows_per_chunk(int rows) {
-  // Enough chunks to fill the GPU twice, few enough that the fold stays cheap.
-  int rpc = (rows + 295) / 296;
+  // At most 64 chunks of rows for the dgamma / dbeta partials (d / 1024 x 64
+  // CTAs of 128 threads: enough to fill the GPU, and a cheap fold).
+  int rpc = (rows + 63) / 64;
   return rpc < 1 ? 1 : rpc;
 }
 
 int layernorm_bwd(const LnBwdArgs& a, cudaStream_t stream) {
   if (a.d % 8 || a.d > 1024 * kLnMaxSlices || (a.x_fp8 && a.d % 128)) return 1;
   const int rpc = a.rows_per_chunk;
+  if (rpc < 1) return 1;
   const int chunks = (a.rows + rpc - 1) / rpc;
-  const int S = (a.d + 1023) / 1024;
-#define EWB_LN_BWD(SS)                                                                        \
-  (a.rms ? layernorm_bwd_kernel<SS, true><<<chunks, kLnThreads, 0, stream>>>(                  \
-               a.dy, a.lddy, a.x, a.x_scale, a.x_fp8, a.ldx, a.ldxs, a.mean, a.rstd, a.gamma,  \
-               a.dres, a.lddres, a.dx, a.lddx, a.part_g, a.part_b, a.rows, a.d, rpc)          \
-         : layernorm_bwd_kernel<SS, false><<<chunks, kLnThreads, 0, stream>>>(                 \
-               a.dy, a.lddy, a.x, a.x_scale, a.x_fp8, a.ldx, a.ldxs, a.mean, a.rstd, a.gamma,  \
-               a.dres, a.lddres, a.dx, a.lddx, a.part_g, a.part_b, a.rows, a.d, rpc))
-  switch (S) {
-    case 1: EWB_LN_BWD(1); break;
-    case 2: EWB_LN_BWD(2); break;
-    case 3: EWB_LN_BWD(3); break;
-    case 4: EWB_LN_BWD(4); break;
-    case 5: EWB_LN_BWD(5); break;
-    case 6: EWB_LN_BWD(6); break;
-    case 7: EWB_LN_BWD(7); break;
-    default: EWB_LN_BWD(8); break;
+  const int dx_grid = (a.rows + kLnBwdWarps - 1) / kLnBwdWarps;
+  const dim3 pgrid((a.d + 1023) / 1024, chunks);
+  if (a.rms) {
+    layernorm_bwd_dx_kernel<true><<<dx_grid, kLnBwdWarps * 32, 0, stream>>>(
+        a.dy, a.lddy, a.x, a.x_scale, a.x_fp8, a.ldx, a.ldxs, a.mean, a.rstd, a.gamma, a.dres,
+        a.lddres, a.dx, a.lddx, a.rows, a.d);
+    layernorm_bwd_param_kernel<true><<<pgrid, kLnThreads, 0, stream>>>(
+        a.dy, a.lddy, a.x, a.x_scale, a.x_fp8, a.ldx, a.ldxs, a.mean, a.rstd, a.part_g, a.part_b,
+        a.rows, a.d, rpc);
+  } else {
+    layernorm_bwd_dx_kernel<false><<<dx_grid, kLnBwdWarps * 32, 0, stream>>>(
+        a.dy, a.lddy, a.x, a.x_scale, a.x_fp8, a.ldx, a.ldxs, a.mean, a.rstd, a.gamma, a.dres,
+        a.lddres, a.dx, a.lddx, a.rows, a.d);
+    layernorm_bwd_param_kernel<false><<<pgrid, kLnThreads, 0, stream>>>(
+        a.dy, a.lddy, a.x, a.x_scale, a.x_fp8, a.ldx, a.ldxs, a.mean, a.rstd, a.part_g, a.part_b,
+        a.rows, a.d, rpc);
   }
-#undef EWB_LN_BWD
   if (cudaGetLastError() != cudaSuccess) return 2;
   const int fb = (a.d + 31) / 32;
   fold_partials_kernel<<<fb, kFoldWarps * 32, 0, stream>>>(a.part_g, chunks, a.d, a.dgamma,

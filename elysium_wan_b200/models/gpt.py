@@ -530,13 +530,12 @@ class Head:
         beta = None if self.rms else s.p(n("ln_f.bias"))
         h, m, r = ops.layernorm_fwd(x.x, x.scale, s.p(n("ln_f.weight")), beta, c.norm_eps)
         if h.is_cuda:
-            ld = (V + 7) // 8 * 8
-            logits = torch.empty((T, ld), dtype=torch.float32, device=h.device)[:, :V]
-            ops.gemm(h, s.w(self.out), logits, ops.EPI_F32)
+            # fused logits GEMM + cross-entropy: no fp32 logits in memory
+            loss, dl = ops.head_ce(h, s.w(self.out), targets, V, 1.0 / T)
         else:
             logits = ops.linear_fwd(h, s.w(self.out), epi="f32")
-        loss, dl = ops.cross_entropy(logits, V, targets.reshape(-1), 1.0 / T)
-        del logits
+            loss, dl = ops.cross_entropy(logits, V, targets.reshape(-1), 1.0 / T)
+            del logits
         ctx.update(x=x, h=h, m=m, r=r, dl=dl)
         return loss
 

@@ -408,6 +408,33 @@ def cross_entropy(logits, V, targets, grad_scale, want_grad=True, ld_grad=None):
     return loss, dl
 
 
+def head_ce(h, w, targets, V, grad_scale):
+    """Fused head logits + mean cross-entropy on the GPU: (loss scalar tensor,
+    dlogits bf16 [T][ld], ld = V rounded up to 8, pad columns zero).
+
+    The logits GEMM's epilogue keeps, per row and 256-wide vocabulary tile,
+    the tile max and the sum of exp(x - max) (and the target's logit), and
+    writes exp(x - tile max) in fp16 where the gradient will go; a second
+    kernel combines the tiles' partials in a fixed order into the row's
+    log-sum-exp and loss and turns those values into the bf16 gradient in
+    place. The fp32 logits are never stored (reference op: logits.float()
+    then F.cross_entropy, src/wantrain/model/gpt.py:410-418,556-557)."""
+    T = h.shape[0]
+    ld = (V + 7) // 8 * 8
+    nt = (V + 255) // 256
+    dev = h.device
+    buf = torch.empty((T, ld), dtype=torch.bfloat16, device=dev)
+    part = torch.empty((T, nt, 2), dtype=torch.float32, device=dev)
+    tgt_logit = torch.empty(T, dtype=torch.float32, device=dev)
+    targets = targets.reshape(-1).contiguous()
+    ext().gemm_lse(h, w, buf[:, :V], V, targets, part, tgt_logit)
+    rows = torch.empty(T, dtype=torch.float32, device=dev)
+    ext().ce_lse_finalize(part, tgt_logit, targets, V, buf, grad_scale, rows)
+    loss = torch.empty(1, dtype=torch.float32, device=dev)
+    ext().mean_reduce(rows, loss)
+    return loss[0], buf
+
+
 # ----------------------------------------------------------------------------- embedding
 def embed_fwd(idx, wte, wpe, S, fp8: bool, out_dtype=torch.bfloat16):
     """x = wte[idx] (+ wpe[pos] when learned positions); bf16, or (e4m3,

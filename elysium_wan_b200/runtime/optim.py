@@ -125,6 +125,11 @@ class HostAdamW(DeviceAdamW):
         computed = [torch.cuda.Event(), torch.cuda.Event()]
         stored = [None, None]
         starts = list(range(R, n, self.chunk))
+        # The loads read host moments that the previous step's stores wrote on
+        # the other copy stream; the compute stream waited for those stores at
+        # the end of that step, so ordering the loads after it orders them
+        # after the stores.
+        self.copy.wait_stream(comp)
 
         def load(i):
             b = i % 2

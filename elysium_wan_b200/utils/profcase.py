@@ -7,7 +7,8 @@ Ops: gemm_fwd (qkv projection), gemm_dx (fc1 input gradient), gemm_dw (fc1
 weight gradient fold), gemm_dw_pair (the same for two microbatches in one launch), gemm_resid (out projection + residual), gemm_fc2 (fc2 +
 residual), gemm_dgelu (fc2 input gradient x GELU'), gemm_q8 (fc2 with the fp8 boundary epilogue),
 attn_fwd, attn_bwd, ln_fwd, ln_bwd, ce, adamw, embed_bwd, head_gemm (the 50257-way
-logits GEMM, fp32 out), head_fwd (LN + logits + CE of the head entry), head_bwd
+logits GEMM, fp32 out), head_lse (the fused logits GEMM + cross-entropy: LSE epilogue and
+finalize), head_fwd (LN + fused logits / CE of the head entry), head_bwd
 (its forward, backward and W).
 """
 
@@ -111,6 +112,10 @@ def build(op):
             for t in wq:
                 t.run()
         return fb, 3 * 2.0 * T * V * D, None
+    if op == "head_lse":  # the fused head: logits GEMM with the LSE epilogue, then finalize
+        h, w = _bf(T, D), _bf(V, D, scale=0.02)
+        tgt = torch.randint(0, V, (T,), device="cuda")
+        return (lambda: ops.head_ce(h, w, tgt, V, 1.0 / T)), 2.0 * T * V * D, None
     if op == "ce":
         ld = (V + 7) // 8 * 8
         logits = torch.randn(T, ld, device="cuda")[:, :V]

@@ -307,6 +307,32 @@ def test_cross_entropy(cuda, V):
     assert torch.equal(loss, loss2) and torch.equal(dl, dl2)
 
 
+@pytest.mark.parametrize("T,V,d", [(333, 50257, 512), (256, 1001, 256), (130, 300, 128)])
+def test_fused_head_cross_entropy(cuda, T, V, d):
+    """The fused head (logits GEMM with the log-sum-exp epilogue, then the
+    finalize kernel) against fp32 PyTorch logits + F.cross_entropy: loss and
+    gradient, ragged rows (T % 128) and vocabularies (V % 256, V % 8), and the
+    same bits on a second run."""
+    torch.manual_seed(11)
+    h = (torch.randn(T, d, device=cuda) * 0.5).to(torch.bfloat16)
+    w = (torch.randn(V, d, device=cuda) * 0.1).to(torch.bfloat16)
+    tgt = torch.randint(0, V, (T,), device=cuda)
+    tgt[0], tgt[1] = V - 1, 0  # the last and the first column as targets
+    loss, dl = ops.head_ce(h, w, tgt, V, 1.0 / T)
+    lr = (h.float() @ w.float().t()).requires_grad_(True)
+    ref = F.cross_entropy(lr, tgt)
+    ref.backward()
+    torch.cuda.synchronize()
+    assert abs(loss.item() - ref.item()) < 2e-5 * abs(ref.item())
+    assert dl.dtype == torch.bfloat16 and dl.shape == (T, (V + 7) // 8 * 8)
+    assert rel_err(dl[:, :V], lr.grad) < 1e-2
+    if dl.shape[1] > V:
+        assert dl[:, V:].abs().max().item() == 0
+    loss2, dl2 = ops.head_ce(h, w, tgt, V, 1.0 / T)
+    assert torch.equal(loss, loss2) and torch.equal(dl, dl2)
+    assert ops.ext().status_read_clear() == 0
+
+
 @pytest.mark.parametrize("fp8", [False, True])
 def test_embedding(cuda, fp8):
     torch.manual_seed(7)
