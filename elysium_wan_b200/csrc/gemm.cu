@@ -22,8 +22,14 @@
 // The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
 // of tile i overlaps the main loop of tile i+1.
 //
-// Determinism: each output tile is produced by exactly one CTA with a fixed
-// k order, so results do not depend on the grid size or on scheduling.
+// A second kernel runs the same GEMM on pairs of SMs (tcgen05 cta_group::2,
+// 256-row tiles, see gemm_pair_kernel); the launcher picks single or pair
+// tiles per shape with a wave model (measured on B200: the pair tiles are
+// 6-19% faster on the forward and weight-gradient shapes of the 15.8B layer).
+//
+// Determinism: each output tile is produced by exactly one CTA (or CTA pair)
+// with a fixed k order, so results do not depend on the grid size or on
+// scheduling; a given shape always takes the same kernel and tile width.
 #include "common.cuh"
 #include "gemm.h"
 
@@ -742,6 +748,286 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------- CTA-pair kernel
+// The same GEMM on pairs of SMs (a cluster of two CTAs, tcgen05 cta_group::2):
+// one pair computes a 256 x BN tile; CTA r of the pair holds rows 128 r ..
+// 128 r + 127 of the tile (its A half) and columns BN/2 r .. of B (its B half)
+// in its own shared memory, and its 128 rows of the fp32 accumulator in its
+// own TMEM. The leader (rank 0) issues every MMA; the hardware reads both
+// CTAs' operand halves, so each SM streams 2/3 of the operand bytes per FLOP of
+// the single-CTA 128 x 256 tile. Both CTAs' TMA loads complete on the leader's
+// stage barrier (no multicast: each CTA loads only its own halves); the
+// leader's MMA commits release both CTAs' stages and accumulators; both CTAs'
+// epilogue warps free an accumulator by arriving on the leader's barrier.
+// Tiles are assigned statically (pair p takes tiles p, p + pairs, ...), so the
+// two CTAs and their roles walk the same sequence without exchanging ids.
+template <int BN, int EPI>
+struct PairCfg {
+  static constexpr int A_BYTES = kBM * kBK * 2;
+  static constexpr int B_BYTES = (BN / 2) * kBK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int OUT_BUFS = EpiTraits<EPI>::kTma ? 2 : 0;
+  static constexpr int OUT_BYTES = OUT_BUFS * 16384;
+  static constexpr int STAGES = (227 * 1024 - OUT_BYTES - 1536) / STAGE_BYTES > 8
+                                    ? 8
+                                    : (227 * 1024 - OUT_BYTES - 1536) / STAGE_BYTES;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + OUT_BYTES + 1024 + 512;
+  static constexpr int TMEM_COLS = (BN == 192) ? 512 : 2 * BN;
+  static_assert(SMEM <= 232448, "shared memory over the 227 KB per-CTA limit");
+  static_assert(BN == 128 || BN == 192 || BN == 256, "pair tiles are 256 x {128, 192, 256}");
+};
+
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t num_clusters_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmC, const GemmEpilogue ep, int M, int N,
+                     int K, int* status, int* sched) {
+  using Cfg = PairCfg<BN, EPI>;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* out_smem = smem + STAGES * Cfg::STAGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(out_smem + Cfg::OUT_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint64_t* tq_full = drain + 1;
+  uint64_t* tq_empty = tq_full + kTileQueue;
+  int* tile_ring = reinterpret_cast<int*>(tq_empty + kTileQueue);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tile_ring + kTileQueue);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool lead = rank == 0;
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 8);  // four epilogue warps in each CTA
+    }
+    mbar_init(drain, 1);
+    for (int q = 0; q < kTileQueue; ++q) {
+      mbar_init(&tq_full[q], 1);
+      // the leader's ring slot is free again once every reader of both CTAs
+      // took the id: its MMA thread and four epilogue warps, the peer's
+      // producer and four epilogue warps
+      mbar_init(&tq_empty[q], 10);
+    }
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if (EpiTraits<EPI>::kTma) tma_prefetch_desc(&tmC);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers exist before any cross-CTA arrive
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_m = (M + 2 * kBM - 1) / (2 * kBM);
+  const int num_n = (N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int kblocks = (K + kBK - 1) / kBK;
+
+  // Tiles are claimed dynamically by the leader's producer (a pair that
+  // starts late takes fewer tiles) and published to both CTAs' roles through
+  // a ring in each CTA's shared memory; -1 ends.
+  auto next_tile = [&](int k) -> int {
+    const int q = k % kTileQueue;
+    if (!mbar_wait_cluster(&tq_full[q], (k / kTileQueue) & 1, status, kStatusTimeoutSmemFull))
+      return -1;
+    return *reinterpret_cast<volatile int*>(&tile_ring[q]);
+  };
+  auto took_tile = [&](int k) {
+    mbar_arrive_cluster(peer_smem(smem_u32(&tq_empty[k % kTileQueue]), 0));
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int k = 0; ok; ++k) {
+        int t;
+        if (lead) {
+          t = atomicAdd(&sched[0], 1);
+          if (t >= num_tiles) t = -1;
+          const int q = k % kTileQueue;
+          if (!mbar_wait(&tq_empty[q], ((k / kTileQueue) & 1) ^ 1, status,
+                         kStatusTimeoutSmemEmpty)) {
+            ok = false;
+            t = -1;
+          }
+          // publish to this CTA and to the peer (store, then release-arrive)
+          tile_ring[q] = t;
+          const uint32_t peer_slot = peer_smem(smem_u32(&tile_ring[q]), 1);
+          asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(peer_slot), "r"(t) : "memory");
+          mbar_arrive(&tq_full[q]);
+          mbar_arrive_cluster(peer_smem(smem_u32(&tq_full[q]), 1));
+        } else {
+          t = next_tile(k);
+          took_tile(k);
+        }
+        if (t < 0) break;
+        int mb, nb;
+        tile_coords(t, num_m, num_n, mb, nb);
+        const int m0 = mb * 2 * kBM + static_cast<int>(rank) * kBM;
+        const int n0 = nb * BN + static_cast<int>(rank) * (BN / 2);
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, status, kStatusTimeoutSmemEmpty)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + s * Cfg::STAGE_BYTES;
+          uint8_t* sb = sa + Cfg::A_BYTES;
+          // the leader's stage barrier counts both CTAs' bytes
+          if (lead) mbar_arrive_expect_tx(&full[s], 2 * Cfg::STAGE_BYTES);
+          const uint32_t lbar = peer_smem(smem_u32(&full[s]), 0);
+          const int kc = kb * kBK;
+          if constexpr (!A_MN) {
+            tma_load_2d_pair(sa, &tmA, lbar, kc, m0);
+          } else {
+            tma_load_2d_pair(sa, &tmA, lbar, m0, kc);
+            tma_load_2d_pair(sa + 8192, &tmA, lbar, m0 + 64, kc);
+          }
+          if constexpr (!B_MN) {
+            tma_load_2d_pair(sb, &tmB, lbar, kc, n0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 128; ++j)
+              tma_load_2d_pair(sb + j * 8192, &tmB, lbar, n0 + j * 64, kc);
+          }
+        }
+      }
+      // Drain after a failure: the stages armed last must land before exit.
+      if (!ok && lead) {
+        for (int j = 0; j < STAGES && j < it; ++j) {
+          const int i2 = it - 1 - j;
+          mbar_wait(&full[i2 % STAGES], (i2 / STAGES) & 1, nullptr, kStatusTimeoutDrain);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lead && lane == 0) {
+      constexpr uint32_t IDESC = idesc_bf16_f32(2 * kBM, BN, A_MN, B_MN);
+      int it = 0;
+      bool ok = true;
+      for (int k = 0; ok; ++k) {
+        const int t = next_tile(k);
+        took_tile(k);
+        if (t < 0) break;
+        const int b = k & 1;
+        const uint32_t use = static_cast<uint32_t>(k >> 1);
+        if (!mbar_wait(&tempty[b], (use & 1) ^ 1, status, kStatusTimeoutTmemEmpty)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * BN);
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, status, kStatusTimeoutSmemFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + s * Cfg::STAGE_BYTES);
+          const uint32_t b_addr = a_addr + Cfg::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t ad = A_MN ? sdesc_sw128(a_addr + kk * 2048, 8192, 1024)
+                                     : sdesc_sw128(a_addr + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sdesc_sw128(b_addr + kk * 2048, 8192, 1024)
+                                     : sdesc_sw128(b_addr + kk * 32, 16, 1024);
+            umma_f16_pair(d_tmem, ad, bd, IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          // this stage is free again in both CTAs once these MMAs complete
+          umma_commit_pair(peer_smem(smem_u32(&empty[s]), 0));
+          umma_commit_pair(peer_smem(smem_u32(&empty[s]), 1));
+        }
+        if (ok) {
+          umma_commit_pair(peer_smem(smem_u32(&tfull[b]), 0));
+          umma_commit_pair(peer_smem(smem_u32(&tfull[b]), 1));
+        }
+      }
+      umma_commit_pair(peer_smem(smem_u32(drain), 0));
+      mbar_wait(drain, 0, nullptr, kStatusTimeoutDrain);
+    }
+  } else {
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const bool leader_thread = (warp == 2 && lane == 0);
+    int chunk = 0;
+    for (int k = 0;; ++k) {
+      const int t = next_tile(k);
+      __syncwarp();
+      if (lane == 0) took_tile(k);
+      if (t < 0) break;
+      int mb, nb;
+      tile_coords(t, num_m, num_n, mb, nb);
+      const int b = k & 1;
+      const uint32_t use = static_cast<uint32_t>(k >> 1);
+      if (!mbar_wait(&tfull[b], use & 1, status, kStatusTimeoutTmemFull)) break;
+      tc_fence_after();
+      const uint32_t taddr =
+          tmem_base + static_cast<uint32_t>(b * BN) + (static_cast<uint32_t>(q * 32) << 16);
+      const AccSrc acc{taddr, nullptr, 1, row};
+      const int m0 = mb * 2 * kBM + static_cast<int>(rank) * kBM;
+      if constexpr (EpiTraits<EPI>::kTma) {
+        epilogue_tile_tma<EPI, BN>(acc, row, m0, nb * BN, N, ep, &tmC, out_smem, leader_thread,
+                                   chunk);
+      } else {
+        epilogue_tile_regs<EPI, BN>(acc, m0 + row, nb * BN, M, N, ep);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(peer_smem(smem_u32(&tempty[b]), 0));
+    }
+    if (EpiTraits<EPI>::kTma && leader_thread) bulk_wait<0>();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // no CTA leaves while its pair may still touch its memory
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+  }
+  // The last CTA to finish resets the tile counter for the next launch on
+  // this stream (launches on one stream are ordered).
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int done = atomicAdd(&sched[1], 1);
+    if (done == static_cast<int>(gridDim.x) - 1) {
+      sched[0] = 0;
+      sched[1] = 0;
+      __threadfence();
+    }
+  }
+}
+
 // ---------------------------------------------------------------- host side
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -926,6 +1212,89 @@ int launch_cfg(const GemmArgs& g, cudaStream_t stream, int* sched, float* ws) {
   return err == cudaSuccess ? kGemmOk : kGemmErrLaunch;
 }
 
+template <int BN, bool A_MN, bool B_MN, int EPI>
+int launch_pair(const GemmArgs& g, cudaStream_t stream) {
+  using Cfg = PairCfg<BN, EPI>;
+  auto kern = gemm_pair_kernel<BN, A_MN, B_MN, EPI>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM) !=
+        cudaSuccess)
+      return kGemmErrLaunch;
+    attr_set[dev & 63] = true;
+  }
+  CUtensorMap ma, mbm, mc;
+  const bool ok_a = A_MN ? make_map_bf16(&ma, g.a, g.M, g.K, g.lda, 64, 64)
+                         : make_map_bf16(&ma, g.a, g.K, g.M, g.lda, 64, kBM);
+  const bool ok_b = B_MN ? make_map_bf16(&mbm, g.b, g.N, g.K, g.ldb, 64, 64)
+                         : make_map_bf16(&mbm, g.b, g.K, g.N, g.ldb, 64, BN / 2);
+  bool ok_c = true;
+  if constexpr (EPI == kEpiBf16) {
+    ok_c = make_map_bf16(&mc, g.ep.out, g.N, g.M, g.ep.ldo, 64, kBM);
+  } else if constexpr (EPI == kEpiF32 || EPI == kEpiAccF32) {
+    ok_c = make_map(&mc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, g.ep.out, g.N, g.M, g.ep.ldo, 32, kBM);
+  } else {
+    mc = ma;
+  }
+  if (!ok_a || !ok_b || !ok_c) return kGemmErrTensorMap;
+  const int sms = num_sms_cached() & ~1;
+  const long tiles = static_cast<long>((g.M + 2 * kBM - 1) / (2 * kBM)) * ((g.N + BN - 1) / BN);
+  const int grid = static_cast<int>(std::max(2L, std::min(2 * tiles, static_cast<long>(sms))));
+  EWB_TRACE("[gemm-pair] BN=%d a_mn=%d b_mn=%d epi=%d M=%d N=%d K=%d grid=%d smem=%d\n", BN,
+            (int)A_MN, (int)B_MN, EPI, g.M, g.N, g.K, grid, Cfg::SMEM);
+  const StreamState st = stream_state(stream, false);
+  if (st.counters == nullptr) return kGemmErrLaunch;
+  kern<<<grid, kThreads, Cfg::SMEM, stream>>>(ma, mbm, mc, g.ep, g.M, g.N, g.K, g.status,
+                                              st.counters);
+  const cudaError_t err = cudaGetLastError();
+  return err == cudaSuccess ? kGemmOk : kGemmErrLaunch;
+}
+
+template <int BN>
+int dispatch_pair(const GemmArgs& g, cudaStream_t s) {
+  const int e = g.ep.kind;
+  // an MN-major B half is whole 64-column swizzle panels: not with 192
+  if (BN == 192 && g.b_mn) return kGemmErrUnsupported;
+  if (!g.a_mn && !g.b_mn) {
+    switch (e) {
+      case kEpiBf16: return launch_pair<BN, false, false, kEpiBf16>(g, s);
+      case kEpiGelu: return launch_pair<BN, false, false, kEpiGelu>(g, s);
+      case kEpiResid: return launch_pair<BN, false, false, kEpiResid>(g, s);
+      case kEpiResidQ8:
+        if constexpr (BN == 256) return launch_pair<BN, false, false, kEpiResidQ8>(g, s);
+        break;
+      case kEpiF32: return launch_pair<BN, false, false, kEpiF32>(g, s);
+      case kEpiLse:
+        if constexpr (BN == 256) return launch_pair<BN, false, false, kEpiLse>(g, s);
+        break;
+      default: break;
+    }
+  } else if (!g.a_mn && g.b_mn) {
+    switch (e) {
+      case kEpiBf16:
+        if constexpr (BN != 192) return launch_pair<BN, false, true, kEpiBf16>(g, s);
+        break;
+      case kEpiDGelu:
+        if constexpr (BN != 192) return launch_pair<BN, false, true, kEpiDGelu>(g, s);
+        break;
+      default: break;
+    }
+  } else if (g.a_mn && g.b_mn) {
+    switch (e) {
+      case kEpiAccF32:
+        if constexpr (BN != 192) return launch_pair<BN, true, true, kEpiAccF32>(g, s);
+        break;
+      case kEpiAccF32Peer:
+        if constexpr (BN != 192) return launch_pair<BN, true, true, kEpiAccF32Peer>(g, s);
+        break;
+      default: break;
+    }
+  }
+  return kGemmErrUnsupported;
+}
+
 template <int BN>
 int dispatch_bn(const GemmArgs& g, cudaStream_t s, int* sc, float* ws) {
   const int e = g.ep.kind;
@@ -996,6 +1365,53 @@ int gemm_pick_bn(int M, int N, int K, bool split) {
   return best;
 }
 
+int& gemm_pair_mode() {
+  static int mode = [] {
+    const char* e = std::getenv("EWB_GEMM_PAIR");
+    return e == nullptr ? 2 : std::atoi(e);
+  }();
+  return mode;
+}
+
+void set_gemm_pair_mode(int mode) { gemm_pair_mode() = mode; }
+
+// Tile width of a CTA-pair launch (0: single-CTA tiles model faster). Same
+// wave model as gemm_pick_bn: a pair tile is 256 rows and occupies two SMs;
+// its rate relative to the single-CTA 128 x 256 tile is kPairRate.
+constexpr double kPairRate = 1.08;
+int gemm_pick_pair_bn(int M, int N, int K, int single_bn, bool split, bool b_mn) {
+  const int sms = num_sms_cached();
+  const int pairs = sms / 2;
+  const double rate1[3] = {1.0, 0.82, 0.6};
+  const int widths[3] = {256, 192, 128};
+  double best1 = 0.0;
+  for (int i = 0; i < 3; ++i) {
+    if (widths[i] != single_bn) continue;
+    const long tiles = static_cast<long>((M + kBM - 1) / kBM) * ((N + widths[i] - 1) / widths[i]);
+    int full = 0;
+    const int ns = split ? split_plan(tiles, sms, (K + kBK - 1) / kBK, &full) : 1;
+    const double waves = ns > 1 ? static_cast<double>(full / sms) + 1.0 / ns + 0.05
+                                : static_cast<double>((tiles + sms - 1) / sms);
+    best1 = waves * widths[i] / rate1[i];
+  }
+  int best = 0;
+  double best_t = best1;
+  const int pw[3] = {256, 192, 128};
+  const double prate[3] = {kPairRate, kPairRate * 0.92, kPairRate * 0.75};
+  for (int i = 0; i < 3; ++i) {
+    if (pw[i] == 192 && b_mn) continue;
+    const long tiles = static_cast<long>((M + 2 * kBM - 1) / (2 * kBM)) * ((N + pw[i] - 1) / pw[i]);
+    const double waves = static_cast<double>((tiles + pairs - 1) / pairs);
+    // a pair tile is two single-CTA tiles of work per SM pair
+    const double t = waves * pw[i] / prate[i];
+    if (t < best_t * 0.97) {
+      best = pw[i];
+      best_t = t;
+    }
+  }
+  return best;
+}
+
 int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
   if (g.M <= 0 || g.N <= 0 || g.K <= 0) return kGemmErrShape;
   if ((reinterpret_cast<uintptr_t>(g.a) & 15) || (reinterpret_cast<uintptr_t>(g.b) & 15))
@@ -1019,6 +1435,24 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
         g.ep.ld_part < (g.N + 255) / 256 || g.ep.ldo % 8 || g.a_mn || g.b_mn)
       return kGemmErrShape;
     bn = 256;
+  }
+  // CTA pairs: whole operand pairs only (no second pair, no K-split), tiles
+  // of 256 rows; gemm_pair_mode() 0 = never, 1 = always when supported,
+  // 2 = when the wave model prefers it.
+  if (g.K2 == 0 && gemm_pair_mode() != 0) {
+    int pbn = 0;
+    if (gemm_pair_mode() == 1) {
+      pbn = (g.ep.kind == kEpiResidQ8 || g.ep.kind == kEpiLse) ? 256 : (g.N <= 128 ? 128 : 256);
+    } else {
+      pbn = gemm_pick_pair_bn(g.M, g.N, g.K, bn, g.split != 0, g.b_mn);
+      if ((g.ep.kind == kEpiResidQ8 || g.ep.kind == kEpiLse) && pbn != 256) pbn = 0;
+    }
+    if (pbn == 256 || pbn == 192 || pbn == 128) {
+      const int rc = pbn == 256   ? dispatch_pair<256>(g, stream)
+                     : pbn == 192 ? dispatch_pair<192>(g, stream)
+                                  : dispatch_pair<128>(g, stream);
+      if (rc != kGemmErrUnsupported) return rc;
+    }
   }
   const StreamState st = stream_state(stream, g.split != 0);
   if (st.counters == nullptr) return kGemmErrLaunch;

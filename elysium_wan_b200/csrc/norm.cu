@@ -129,36 +129,82 @@ __global__ void __launch_bounds__(kLnThreads)
 // dx = rstd * (g - mean(g) - xhat * mean(g * xhat)) (+ dres), g = dy * gamma.
 // RMSNorm (RMS = true): mean = 0 and no centring of g, dx = rstd * (g - xhat * mean(g * xhat)).
 //
-// One warp per row: lane l owns columns 256 j + 8 l (16-byte loads), the two
-// row sums are per-lane sums in column order then a fixed butterfly, so no
-// block barrier stands between the loads; the second pass re-reads the row
-// from cache. Eight rows per CTA.
+// Two warps per row (four rows per CTA of eight warps): thread t of the row's
+// 64 owns columns 512 j + 8 t (16-byte loads). Its share of x and dy is loaded
+// once into registers (raw 16-byte words, so the whole row is in flight at
+// once); the two row sums are per-thread sums in column order, a fixed warp
+// butterfly, then the two warps' sums added in warp order through shared
+// memory; dx is computed from the registers. NS = the most 512-column slices a
+// row may have (d <= 512 NS).
 constexpr int kLnBwdWarps = 8;
 
-template <bool RMS>
+__device__ __forceinline__ void unpack8(const uint4& w, const float* xs_row, int x_fp8, int col,
+                                        float* v) {
+  if (x_fp8) {
+    const float s = xs_row[col >> 7];
+    const uint8_t* b = reinterpret_cast<const uint8_t*>(&w);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      __nv_fp8_e4m3 q;
+      q.__x = b[i];
+      v[i] = static_cast<float>(q) * s;
+    }
+  } else {
+    const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&w);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __bfloat162float(b[i]);
+  }
+}
+
+template <int NS, bool RMS>
 __global__ void __launch_bounds__(kLnBwdWarps * 32)
     layernorm_bwd_dx_kernel(const __nv_bfloat16* __restrict__ dy, int lddy, const void* __restrict__ x,
                             const float* __restrict__ xs, int x_fp8, int ldx, int ldxs,
                             const float* __restrict__ mean, const float* __restrict__ rstd,
                             const float* __restrict__ gamma, const __nv_bfloat16* __restrict__ dres,
                             int lddres, __nv_bfloat16* __restrict__ dx, int lddx, int rows, int d) {
+  __shared__ float red[kLnBwdWarps][2];
   const int lane = threadIdx.x & 31;
-  const int row = blockIdx.x * kLnBwdWarps + (threadIdx.x >> 5);
-  if (row >= rows) return;
-  const float mu = RMS ? 0.f : mean[row];
-  const float rs = rstd[row];
-  float s1 = 0.f, s2 = 0.f;
-#pragma unroll 4
-  for (int col = lane * 8; col < d; col += 256) {
-    float xv[8], dv[8], gm[8];
-    load8(x, xs, x_fp8, ldx, ldxs, row, col, xv);
-    load8(dy, nullptr, 0, lddy, 0, row, col, dv);
-    load8_f32(gamma + col, gm);
+  const int warp = threadIdx.x >> 5;
+  const int half = warp & 1;
+  const int t = half * 32 + lane;  // thread index within the row's 64
+  const int row = blockIdx.x * (kLnBwdWarps / 2) + (warp >> 1);
+  const bool live = row < rows;
+  uint4 xw[NS], dw[NS];
+  const uint8_t* xrow = reinterpret_cast<const uint8_t*>(x) +
+                        static_cast<size_t>(live ? row : 0) * ldx * (x_fp8 ? 1 : 2);
+  const __nv_bfloat16* dyrow = dy + static_cast<size_t>(live ? row : 0) * lddy;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float g = dv[i] * gm[i];
-      s1 += g;
-      s2 += g * ((xv[i] - mu) * rs);
+  for (int j = 0; j < NS; ++j) {
+    const int col = j * 512 + t * 8;
+    if (live && col < d) {
+      if (x_fp8) {
+        const uint2 r = __ldg(reinterpret_cast<const uint2*>(xrow + col));
+        xw[j] = make_uint4(r.x, r.y, 0u, 0u);
+      } else {
+        xw[j] = __ldg(reinterpret_cast<const uint4*>(xrow + 2 * col));
+      }
+      dw[j] = __ldg(reinterpret_cast<const uint4*>(dyrow + col));
+    }
+  }
+  const float* xs_row = (x_fp8 && live) ? xs + static_cast<size_t>(row) * ldxs : nullptr;
+  const float mu = (RMS || !live) ? 0.f : mean[row];
+  const float rs = live ? rstd[row] : 0.f;
+  float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+  for (int j = 0; j < NS; ++j) {
+    const int col = j * 512 + t * 8;
+    if (live && col < d) {
+      float xv[8], dv[8], gm[8];
+      unpack8(xw[j], xs_row, x_fp8, col, xv);
+      unpack8(dw[j], nullptr, 0, col, dv);
+      load8_f32(gamma + col, gm);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float g = dv[i] * gm[i];
+        s1 += g;
+        s2 += g * ((xv[i] - mu) * rs);
+      }
     }
   }
 #pragma unroll
@@ -166,26 +212,38 @@ __global__ void __launch_bounds__(kLnBwdWarps * 32)
     s1 += __shfl_xor_sync(0xffffffffu, s1, o);
     s2 += __shfl_xor_sync(0xffffffffu, s2, o);
   }
+  if (lane == 0) {
+    red[warp][0] = s1;
+    red[warp][1] = s2;
+  }
+  __syncthreads();
+  if (!live) return;
+  const int w0 = warp & ~1;
+  s1 = red[w0][0] + red[w0 + 1][0];
+  s2 = red[w0][1] + red[w0 + 1][1];
   const float m1 = RMS ? 0.f : s1 / static_cast<float>(d);
   const float m2 = s2 / static_cast<float>(d);
-#pragma unroll 4
-  for (int col = lane * 8; col < d; col += 256) {
-    float xv[8], dv[8], gm[8], o[8];
-    load8(x, xs, x_fp8, ldx, ldxs, row, col, xv);
-    load8(dy, nullptr, 0, lddy, 0, row, col, dv);
-    load8_f32(gamma + col, gm);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float xh = (xv[i] - mu) * rs;
-      o[i] = rs * (dv[i] * gm[i] - m1 - xh * m2);
-    }
-    if (dres != nullptr) {
-      float rv[8];
-      load8(dres, nullptr, 0, lddres, 0, row, col, rv);
+  for (int j = 0; j < NS; ++j) {
+    const int col = j * 512 + t * 8;
+    if (col < d) {
+      float xv[8], dv[8], gm[8], o[8];
+      unpack8(xw[j], xs_row, x_fp8, col, xv);
+      unpack8(dw[j], nullptr, 0, col, dv);
+      load8_f32(gamma + col, gm);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] += rv[i];
+      for (int i = 0; i < 8; ++i) {
+        const float xh = (xv[i] - mu) * rs;
+        o[i] = rs * (dv[i] * gm[i] - m1 - xh * m2);
+      }
+      if (dres != nullptr) {
+        float rv[8];
+        load8(dres, nullptr, 0, lddres, 0, row, col, rv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] += rv[i];
+      }
+      store8_bf16(dx + static_cast<size_t>(row) * lddx + col, o);
     }
-    store8_bf16(dx + static_cast<size_t>(row) * lddx + col, o);
   }
 }
 
@@ -210,17 +268,41 @@ __global__ void __launch_bounds__(kLnThreads)
     pg[i] = 0.f;
     pb[i] = 0.f;
   }
-#pragma unroll 4
-  for (int row = r0; row < r1; ++row) {
-    float xv[8], dv[8];
-    load8(x, xs, x_fp8, ldx, ldxs, row, col, xv);
-    load8(dy, nullptr, 0, lddy, 0, row, col, dv);
-    const float mu = RMS ? 0.f : __ldg(mean + row);
-    const float rs = __ldg(rstd + row);
+  // eight rows' raw 16-byte loads in flight per thread, then their sums in
+  // row order
+  const size_t xb = x_fp8 ? 1 : 2;
+  for (int rb = r0; rb < r1; rb += 8) {
+    uint4 xw[8], dw[8];
+    float mu[8], rs[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      pg[i] += dv[i] * ((xv[i] - mu) * rs);
-      pb[i] += dv[i];
+    for (int k = 0; k < 8; ++k) {
+      const int row = rb + k;
+      if (row < r1) {
+        const uint8_t* xp = reinterpret_cast<const uint8_t*>(x) + (static_cast<size_t>(row) * ldx + col) * xb;
+        if (x_fp8) {
+          const uint2 r = __ldg(reinterpret_cast<const uint2*>(xp));
+          xw[k] = make_uint4(r.x, r.y, 0u, 0u);
+        } else {
+          xw[k] = __ldg(reinterpret_cast<const uint4*>(xp));
+        }
+        dw[k] = __ldg(reinterpret_cast<const uint4*>(dy + static_cast<size_t>(row) * lddy + col));
+        mu[k] = RMS ? 0.f : __ldg(mean + row);
+        rs[k] = __ldg(rstd + row);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int row = rb + k;
+      if (row < r1) {
+        float xv[8], dv[8];
+        unpack8(xw[k], x_fp8 ? xs + static_cast<size_t>(row) * ldxs : nullptr, x_fp8, col, xv);
+        unpack8(dw[k], nullptr, 0, col, dv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          pg[i] += dv[i] * ((xv[i] - mu[k]) * rs[k]);
+          pb[i] += dv[i];
+        }
+      }
     }
   }
   float4* g4 = reinterpret_cast<float4*>(part_g + static_cast<size_t>(chunk) * d + col);
@@ -284,10 +366,10 @@ int layernorm_fwd(const LnArgs& a, cudaStream_t stream) {
 }
 
 int layernorm_bwd_rows_per_chunk(int rows) {
-  // At most 64 chunks of rows for the dgamma / dbeta partials (d / 1024 x 64
-  // CTAs of 128 threads: enough to fill the GPU, and a cheap fold).
-  int rpc = (rows + 63) / 64;
-  return rpc < 1 ? 1 : rpc;
+  // Chunks of 16 rows (at most 256 chunks) for the dgamma / dbeta partials:
+  // d / 1024 x chunks CTAs of 128 threads, two batches of eight rows each.
+  int rpc = rows > 256 * 16 ? (rows + 255) / 256 : 16;
+  return rpc;
 }
 
 int layernorm_bwd(const LnBwdArgs& a, cudaStream_t stream) {
@@ -295,23 +377,34 @@ int layernorm_bwd(const LnBwdArgs& a, cudaStream_t stream) {
   const int rpc = a.rows_per_chunk;
   if (rpc < 1) return 1;
   const int chunks = (a.rows + rpc - 1) / rpc;
-  const int dx_grid = (a.rows + kLnBwdWarps - 1) / kLnBwdWarps;
+  const int dx_grid = (a.rows + kLnBwdWarps / 2 - 1) / (kLnBwdWarps / 2);
   const dim3 pgrid((a.d + 1023) / 1024, chunks);
+  const int ns = (a.d + 511) / 512;
+#define EWB_LN_DX(NSV, R)                                                                     \
+  layernorm_bwd_dx_kernel<NSV, R><<<dx_grid, kLnBwdWarps * 32, 0, stream>>>(                   \
+      a.dy, a.lddy, a.x, a.x_scale, a.x_fp8, a.ldx, a.ldxs, a.mean, a.rstd, a.gamma, a.dres,     \
+      a.lddres, a.dx, a.lddx, a.rows, a.d)
+#define EWB_LN_DX_NS(R)                     \
+  if (ns <= 2) EWB_LN_DX(2, R);             \
+  else if (ns <= 4) EWB_LN_DX(4, R);        \
+  else if (ns <= 6) EWB_LN_DX(6, R);        \
+  else if (ns <= 8) EWB_LN_DX(8, R);        \
+  else if (ns <= 10) EWB_LN_DX(10, R);      \
+  else if (ns <= 12) EWB_LN_DX(12, R);      \
+  else EWB_LN_DX(16, R)
   if (a.rms) {
-    layernorm_bwd_dx_kernel<true><<<dx_grid, kLnBwdWarps * 32, 0, stream>>>(
-        a.dy, a.lddy, a.x, a.x_scale, a.x_fp8, a.ldx, a.ldxs, a.mean, a.rstd, a.gamma, a.dres,
-        a.lddres, a.dx, a.lddx, a.rows, a.d);
+    EWB_LN_DX_NS(true);
     layernorm_bwd_param_kernel<true><<<pgrid, kLnThreads, 0, stream>>>(
         a.dy, a.lddy, a.x, a.x_scale, a.x_fp8, a.ldx, a.ldxs, a.mean, a.rstd, a.part_g, a.part_b,
         a.rows, a.d, rpc);
   } else {
-    layernorm_bwd_dx_kernel<false><<<dx_grid, kLnBwdWarps * 32, 0, stream>>>(
-        a.dy, a.lddy, a.x, a.x_scale, a.x_fp8, a.ldx, a.ldxs, a.mean, a.rstd, a.gamma, a.dres,
-        a.lddres, a.dx, a.lddx, a.rows, a.d);
+    EWB_LN_DX_NS(false);
     layernorm_bwd_param_kernel<false><<<pgrid, kLnThreads, 0, stream>>>(
         a.dy, a.lddy, a.x, a.x_scale, a.x_fp8, a.ldx, a.ldxs, a.mean, a.rstd, a.part_g, a.part_b,
         a.rows, a.d, rpc);
   }
+#undef EWB_LN_DX_NS
+#undef EWB_LN_DX
   if (cudaGetLastError() != cudaSuccess) return 2;
   const int fb = (a.d + 31) / 32;
   fold_partials_kernel<<<fb, kFoldWarps * 32, 0, stream>>>(a.part_g, chunks, a.d, a.dgamma,

@@ -78,6 +78,15 @@ def build(op):
             return (lambda: ops.attention_fwd(qkv, 1, T, H, D // H)), flops_f, None
         do = _bf(T, D)
         return (lambda: ops.attention_bwd(qkv, o, do, lse, 1, T, H, D // H)), 2.5 * flops_f, None
+    if op in ("ln_fwd1", "ln_bwd1"):  # one microbatch (2048 rows)
+        x = _bf(T, D)
+        gam, bet = torch.ones(D, device="cuda"), torch.zeros(D, device="cuda")
+        if op == "ln_fwd1":
+            return (lambda: ops.layernorm_fwd(x, None, gam, bet)), None, T * D * 4
+        y, m, r = ops.layernorm_fwd(x, None, gam, bet)
+        dy = _bf(T, D)
+        dg, db = torch.zeros(D, device="cuda"), torch.zeros(D, device="cuda")
+        return (lambda: ops.layernorm_bwd(dy, x, None, m, r, gam, dy, dg, db, True)), None, T * D * 8
     if op in ("ln_fwd", "ln_bwd"):
         x = _bf(8 * T, D)
         gam, bet = torch.ones(D, device="cuda"), torch.zeros(D, device="cuda")

@@ -1,0 +1,148 @@
+"""The CTA-pair GEMM (tcgen05 cta_group::2: one 256-row tile on two SMs)
+against fp32 PyTorch and against the single-CTA kernel, for every operand
+layout (forward, B-pass dX, W-pass dW) and epilogue, ragged shapes included,
+and run twice for determinism.
+
+Would fail if the pair's operand halves, the leader's stage barriers, the
+cross-CTA commits or the two CTAs' epilogue rows were wrong (wrong values,
+or a bounded wait recording a timeout in the device status word).
+"""
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from elysium_wan_b200 import ops
+
+pytestmark = pytest.mark.gpu
+
+
+def bf(*shape, dev, scale=1.0):
+    return (torch.randn(*shape, device=dev) * scale).to(torch.bfloat16)
+
+
+def rel_err(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).norm() / (b.norm() + 1e-12)).item()
+
+
+@pytest.fixture
+def pair(cuda):
+    ext = ops.ext()
+    assert ext.status_read_clear() == 0
+    ext.set_gemm_pair(1)
+    try:
+        yield cuda
+    finally:
+        ext.set_gemm_pair(2)  # the default: pairs where the wave model prefers them
+    torch.cuda.synchronize()
+    assert ext.status_read_clear() == 0
+
+
+def test_pair_gemm_smallest_case(pair):
+    torch.manual_seed(0)
+    x, w = bf(256, 128, dev=pair), bf(256, 128, dev=pair)
+    out = torch.empty(256, 256, dtype=torch.float32, device=pair)
+    ops.gemm(x, w, out, ops.EPI_F32)
+    torch.cuda.synchronize()
+    assert ops.ext().status_read_clear() == 0
+    assert rel_err(out, x.float() @ w.float().t()) < 1e-5
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 512, 256), (200, 264, 200), (1000, 1536, 512),
+                                   (2048, 640, 1024), (512, 128, 192)])
+def test_pair_gemm_layouts(pair, M, N, K):
+    torch.manual_seed(1)
+    x, w = bf(M, K, dev=pair), bf(N, K, dev=pair)
+    ref = x.float() @ w.float().t()
+    out = torch.empty(M, N, dtype=torch.float32, device=pair)
+    ops.gemm(x, w, out, ops.EPI_F32)
+    assert rel_err(out, ref) < 1e-5
+    wt = w.t().contiguous()
+    y = torch.empty(M, N, dtype=torch.bfloat16, device=pair)
+    ops.gemm(x, wt, y, ops.EPI_BF16, b_mn=True)
+    assert rel_err(y, ref) < 1e-2
+    xt = x.t().contiguous()
+    acc = torch.empty(M, N, dtype=torch.float32, device=pair)
+    ops.gemm(xt, wt, acc, ops.EPI_ACC_F32, a_mn=True, b_mn=True, beta=0.0)
+    assert rel_err(acc, ref) < 1e-5
+    ops.gemm(xt, wt, acc, ops.EPI_ACC_F32, a_mn=True, b_mn=True, beta=1.0)
+    assert rel_err(acc, 2 * ref) < 1e-5
+    again = torch.empty_like(out)
+    ops.gemm(x, w, again, ops.EPI_F32)
+    assert torch.equal(out, again)
+
+
+def test_pair_gemm_epilogues_match_single_cta(pair):
+    """bias, GELU (+ pre-activation), residual, fp8 boundary quantise and
+    dGELU through the pair kernel agree with the single-CTA kernel."""
+    torch.manual_seed(2)
+    M, N, K = 512, 768, 384
+    x, w = bf(M, K, dev=pair), bf(N, K, dev=pair, scale=0.05)
+    b = torch.randn(N, device=pair)
+    r = bf(M, N, dev=pair)
+
+    def both(fn):
+        ops.ext().set_gemm_pair(1)
+        a = fn()
+        ops.ext().set_gemm_pair(0)  # single-CTA tiles only
+        s = fn()
+        ops.ext().set_gemm_pair(1)
+        return a, s
+
+    def gelu():
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=pair)
+        aux = torch.empty(M, N, dtype=torch.bfloat16, device=pair)
+        ops.gemm(x, w, out, ops.EPI_GELU, bias=b, aux=aux)
+        return torch.cat([out.float(), aux.float()])
+
+    def resid():
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=pair)
+        ops.gemm(x, w, out, ops.EPI_RESID, bias=b, resid=r)
+        return out.float()
+
+    def q8():
+        out = torch.empty(M, N, dtype=torch.float8_e4m3fn, device=pair)
+        sc = torch.empty(M, N // 128, dtype=torch.float32, device=pair)
+        ops.gemm(x, w, out, ops.EPI_RESID_Q8, bias=b, resid=r, scale_out=sc)
+        return out.float() * sc.repeat_interleave(128, dim=1)
+
+    def dgelu():
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=pair)
+        ops.gemm(x, w.t().contiguous(), out, ops.EPI_DGELU, b_mn=True, aux=r)
+        return out.float()
+
+    for fn in (gelu, resid, q8, dgelu):
+        a, s = both(fn)
+        assert rel_err(a, s) < 1e-2, fn.__name__
+    ref = F.gelu(x.float() @ w.float().t() + b)
+    a, _ = both(gelu)
+    assert rel_err(a[:M], ref) < 1e-2
+
+
+def test_pair_fused_head_cross_entropy(pair):
+    torch.manual_seed(3)
+    T, V, d = 333, 1001, 256
+    h = (torch.randn(T, d, device=pair) * 0.5).to(torch.bfloat16)
+    w = (torch.randn(V, d, device=pair) * 0.1).to(torch.bfloat16)
+    tgt = torch.randint(0, V, (T,), device=pair)
+    loss, dl = ops.head_ce(h, w, tgt, V, 1.0 / T)
+    lr = (h.float() @ w.float().t()).requires_grad_(True)
+    ref = F.cross_entropy(lr, tgt)
+    ref.backward()
+    assert abs(loss.item() - ref.item()) < 2e-5 * abs(ref.item())
+    assert rel_err(dl[:, :V], lr.grad) < 1e-2
+
+
+def test_pair_gemm_auto_choice_wide_outputs(pair):
+    """Mode 2 lets the wave model choose per shape (pair 256 / 192 / 128 or a
+    single-CTA tile); the 5120-wide outputs of a 2048-row microbatch take
+    192-wide pair tiles when B is K-major."""
+    torch.manual_seed(4)
+    ops.ext().set_gemm_pair(2)
+    for M, N, K, b_mn in [(2048, 5120, 512, False), (2048, 5120, 512, True), (4096, 1536, 256, False)]:
+        x, w = bf(M, K, dev=pair), bf(N, K, dev=pair)
+        ref = x.float() @ w.float().t()
+        out = torch.empty(M, N, dtype=torch.float32, device=pair)
+        ops.gemm(x, w.t().contiguous() if b_mn else w, out, ops.EPI_F32, b_mn=b_mn)
+        assert rel_err(out, ref) < 1e-5, (M, N, K, b_mn)
