@@ -2,7 +2,7 @@
 //
 // Everything here is hand-written inline PTX for Blackwell (sm_100a):
 //   * mbarrier init / arrive / expect-tx / bounded try-wait,
-//   * TMA tiled 2D loads (cp.async.bulk.tensor, never with cluster multicast),
+//   * TMA tiled 2D loads of this GPU's own memory, one CTA's box each (no broadcast form),
 //   * tcgen05 TMEM alloc / dealloc, the kind::f16 MMA with a shared-memory
 //     descriptor pair, commit-to-mbarrier, and tcgen05.ld of 32 lanes x 32 bits.
 //
@@ -360,7 +360,7 @@ __device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
 
 // 2D tiled load into this CTA's shared memory whose completion (transaction
 // bytes) is signalled on the leader CTA's mbarrier `leader_bar` (a
-// shared::cluster address). No multicast: each CTA loads its own half.
+// shared::cluster address). No broadcast: each CTA loads its own half.
 __device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map,
                                                  uint32_t leader_bar, int x, int y) {
   asm volatile(

@@ -14,7 +14,7 @@
 //
 // Structure: a persistent kernel, one CTA per SM, 6 warps.
 //   warp 0      TMA producer: 128B-swizzled boxes of A and B into a ring of
-//               shared-memory stages (local memory only, no multicast).
+//               shared-memory stages (local memory only, no broadcast).
 //   warp 1      TMEM allocator + MMA issuer: one elected thread issues
 //               tcgen05.mma (M=128, N=BN, K=16) and commits to mbarriers.
 //   warps 2-5   epilogue: tcgen05.ld of the fp32 accumulator (each warp owns
@@ -756,7 +756,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // own TMEM. The leader (rank 0) issues every MMA; the hardware reads both
 // CTAs' operand halves, so each SM streams 2/3 of the operand bytes per FLOP of
 // the single-CTA 128 x 256 tile. Both CTAs' TMA loads complete on the leader's
-// stage barrier (no multicast: each CTA loads only its own halves); the
+// stage barrier (no broadcast: each CTA loads only its own halves); the
 // leader's MMA commits release both CTAs' stages and accumulators; both CTAs'
 // epilogue warps free an accumulator by arriving on the leader's barrier.
 // Tiles are assigned statically (pair p takes tiles p, p + pairs, ...), so the

@@ -63,3 +63,18 @@ def test_w_pair_bitwise_vs_oracle(tmp_path, stages):
     r = run_and_compare(spec, timeout=240)
     assert r["ok"], r
     assert r["compared"] == 10
+
+
+def test_gpt2p8b_shape_4x2_zero1_320_losses_bitwise(tmp_path):
+    """The 2.8B GPT's layer shape (d 2560, 32 heads of 80, MLP 10240, seq 2048,
+    vocab 50257, bf16) at reduced depth as BASELINE's 4 stages x 2 ZeRO-1
+    replicas with the fused gradient exchange: 32 microbatches of 2 sequences
+    for 10 steps, all 320 losses equal to the single-GPU oracle bit for bit."""
+    _need(8)
+    cfg = make_config("gpt2_8b", n_layer=4)
+    spec = JobSpec(model=cfg, stages=4, stage_widths=[2, 2, 2, 2], microbatches=32, mb_size=2,
+                   steps=10, device="cuda", backend="nccl", grad_sync="fused", lr=1e-4,
+                   out_dir=str(tmp_path), port_base=29940)
+    r = run_and_compare(spec, timeout=900)
+    assert r["ok"], r
+    assert r["compared"] == 320
