@@ -236,30 +236,41 @@ def _fleet(n, vram=178, device="cuda:0", cls="b200"):
             for i in range(n)]
 
 
-def test_plan_mode_depth_width_layout_and_microbatches():
+def test_plan_mode_prices_every_candidate_and_takes_the_fastest():
+    """Plan mode enumerates (depth, moments on device / host, recompute), fits
+    the largest microbatch, admits wide stages, prices each candidate's step
+    and returns the fastest fitting one with the whole table."""
     from elysium_wan_b200.scheduler import admission as ad
     from elysium_wan_b200.scheduler.fleetplan import plan_job
 
-    # 15.8B on 8 B200s: the fewest stages that hold the state, two ZeRO-1 replicas each
     spec, rat = plan_job({"preset": "gpt15b"}, _fleet(8))
-    assert spec.stages == 3 and spec.stage_widths == [2, 2, 2] and spec.shard == "zero1"
-    assert rat["width"]["spares"] == 2 and spec.optimizer == "adamw"
-    assert max(rat["depth"]["stage_gib"]) <= rat["depth"]["device_budget_gib"]
-    assert spec.microbatches % 2 == 0 and spec.microbatches >= 2
-    ok, reasons, _ = ad.admit(spec, ad.devices_from_nodes(_fleet(6)))
-    assert ok, [r.text() for r in reasons]
-    # a depth the plan pins is kept
-    spec, rat = plan_job({"preset": "gpt15b", "stages": 8}, _fleet(8))
-    assert spec.stages == 8 and rat["depth"]["given"]
-    # the 0.6B model fits one device: one stage, eight replicas
+    priced = [r for r in rat["candidates"] if "tokens_per_s" in r]
+    assert priced and len(priced) + sum(1 for r in rat["candidates"] if r.get("refused")) == \
+        len(rat["candidates"])
+    best = max(r["tokens_per_s"] for r in priced)
+    assert rat["price"]["tokens_per_s"] == pytest.approx(best)
+    assert spec.stages == rat["depth"]["stages"] and sum(spec.stage_widths) <= 8
+    assert rat["width"]["spares"] == 8 - sum(spec.stage_widths)
+    assert spec.mb_size >= 1 and spec.microbatches % max(spec.stage_widths) == 0
+    # the winner fits: its heaviest stage within the device budget
+    if max(spec.stage_widths) > 1:
+        ok, reasons, _ = ad.admit(spec, ad.devices_from_nodes(_fleet(sum(spec.stage_widths))))
+        assert ok, [r.text() for r in reasons]
+    # a depth the plan pins is kept, and so are its microbatches and size
+    spec, rat = plan_job({"preset": "gpt15b", "stages": 8, "microbatches": 64, "mb_size": 1},
+                         _fleet(8))
+    assert spec.stages == 8 and rat["depth"]["given"] and spec.microbatches == 64
+    assert rat["mb_size"]["given"] and spec.mb_size == 1
+    assert all(r["stages"] == 8 for r in rat["candidates"])
+    # a model that fits one device: wide stages win over a pipeline
     spec, _ = plan_job({"preset": "gpt15b", "n_layer": 20, "d_model": 1536, "n_head": 12},
                        _fleet(8))
-    assert spec.stages == 1 and spec.stage_widths == [8]
-    # small devices push the moments to the host before giving up
-    spec, rat = plan_job({"preset": "gpt15b", "n_layer": 4, "d_model": 1024, "n_head": 8},
-                         _fleet(1, vram=5))
-    assert spec.optimizer == "adamw-host"
-    with pytest.raises(ValueError, match="no depth"):
+    assert max(spec.stage_widths) > 1 and spec.shard == "zero1"
+    # small devices: host moments or recompute before giving up
+    spec, rat = plan_job({"preset": "gpt15b", "n_layer": 8, "d_model": 2048, "n_head": 16},
+                         _fleet(1, vram=8))
+    assert spec.optimizer == "adamw-host" or spec.recompute
+    with pytest.raises(ValueError, match="no candidate"):
         plan_job({"preset": "gpt15b"}, _fleet(2, vram=8))
     with pytest.raises(ValueError, match="mixed"):
         plan_job({"preset": "toy"}, _fleet(1) + _fleet(1, device="cpu", cls="cpu"))
