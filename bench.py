@@ -214,6 +214,11 @@ def plan_spec(args, n: int, free_bytes: float | None):
         except ValueError:  # one microbatch does not fit without recompute
             spec.recompute = True
             spec.schedule_order = default_schedule(spec, [budget] * stages)
+        if spec.recompute:
+            # stages whose in-flight activations fit keep F's tensors
+            from elysium_wan_b200.scheduler.zero_bubble import selective_recompute
+
+            spec.recompute_stages = selective_recompute(spec, budget_bytes=[budget] * stages)
     spec.finalize()
     return spec
 

@@ -14,6 +14,7 @@ both produce the same bits, so it is not a pin).
 from __future__ import annotations
 
 import json
+import os
 from dataclasses import asdict, dataclass, field
 from typing import Any
 
@@ -184,6 +185,13 @@ class JobSpec:
         if self.schedule_order is None:
             self.schedule_order = default_schedule(self)
         self._check_schedule_order()
+        if self.recompute and self.recompute_stages is None and \
+                os.environ.get("WANTRAIN_SELECTIVE_RECOMPUTE") == "on":
+            from elysium_wan_b200.scheduler.zero_bubble import selective_recompute
+
+            sel = selective_recompute(self)
+            if sel is not None:
+                self.recompute_stages = sel
         if self.resume_step is not None and not self.resume:
             raise ValueError("resume_step needs resume")
         return self

@@ -448,3 +448,49 @@ def slot_orders(stage_order: list, owners: list, width: int) -> list:
     for op, mb in stage_order:
         out[owners[mb]].append((op, mb))
     return out
+
+
+def in_flight_peak(order) -> int:
+    """Most microbatches one slot's order holds between an F and its B."""
+    live = peak = 0
+    for op, _mb in order:
+        if op == F:
+            live += 1
+            peak = max(peak, live)
+        elif op == B:
+            live -= 1
+    return peak
+
+
+def selective_recompute(spec, force=frozenset(), budget_bytes: list | None = None) -> list | None:
+    """Per stage, whether it recomputes under a recomputing spec (None when
+    nothing changes).
+
+    Without `budget_bytes` (the reference's rule, selective_recompute in
+    src/wantrain/scheduler/zero_bubble.py:607, RUNTIME-I25): a stage
+    recomputes only where some slot's order holds more than one microbatch
+    between an F and its B, or it is in `force`.
+
+    This engine recomputes layer by layer (B re-runs one layer's forward just
+    before that layer's backward), so even one microbatch in flight needs less
+    memory recomputed. With `budget_bytes` (activation bytes each stage may
+    hold) the rule is memory's: a stage keeps F's saved tensors when its
+    in-flight peak of them fits its budget, else it recomputes. The math is the
+    same either way, so the bits are too."""
+    if not spec.recompute or spec.schedule_order is None:
+        return None
+    out = []
+    for r, slots in enumerate(spec.schedule_order):
+        peak = max((in_flight_peak([(op, mb) for op, mb in order]) for order in slots),
+                   default=0)
+        if budget_bytes is None:
+            need = peak > 1
+        else:
+            from elysium_wan_b200.scheduler.planner import act_bytes
+
+            a, b = spec.partition[r]
+            blocks = sum(1 for e in range(a, b) if 1 <= e <= spec.model.n_layer)
+            m = act_bytes(spec.model, spec.mb_size, spec.device_for(r))
+            need = peak * blocks * (m["saved"] + m["boundary"]) > budget_bytes[r]
+        out.append(need or r in force)
+    return None if all(out) else out

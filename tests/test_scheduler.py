@@ -96,3 +96,25 @@ def test_even_partition_baseline_cut():
     p = part.even_blocks_partition(cfg, 8)
     assert p[0] == [0, 7] and p[-1] == [43, 50]
     assert all(b - a == 6 for a, b in p[1:-1])
+
+
+def test_selective_recompute_rules():
+    """The in-flight rule (recompute only where an order holds more than one
+    microbatch between F and B; the last stage never does) and the memory
+    rule (keep F's tensors where the in-flight peak of them fits)."""
+    from elysium_wan_b200.models.config import make_config
+    from elysium_wan_b200.runtime.spec import JobSpec
+    from elysium_wan_b200.scheduler.zero_bubble import in_flight_peak, selective_recompute
+
+    spec = JobSpec(model=make_config("toy", n_layer=4), stages=4, microbatches=8, mb_size=1,
+                   recompute=True).finalize()
+    peaks = [in_flight_peak(o[0]) for o in spec.schedule_order]
+    assert peaks[-1] == 1 and peaks[0] > 1
+    sel = selective_recompute(spec)
+    assert sel == [p > 1 for p in peaks] and sel[-1] is False
+    assert selective_recompute(spec, force={3}) is None  # every stage then recomputes
+    big = selective_recompute(spec, budget_bytes=[1e18] * 4)
+    assert big == [False] * 4
+    assert selective_recompute(spec, budget_bytes=[0.0] * 4) is None
+    spec.recompute = False
+    assert selective_recompute(spec) is None
