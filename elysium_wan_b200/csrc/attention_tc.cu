@@ -8,20 +8,25 @@
 // shapes and the backward.
 //
 // One CTA owns 128 query rows of one (batch, head) and walks the causal key
-// blocks of 128. Six warps:
+// blocks of 128. Ten warps:
 //   warp 0     TMA producer: Q once, then K and V tiles into a 2-stage ring;
 //   warp 1     MMA issuer (one thread): S_j = Q K_j^T into one of two TMEM
 //              S buffers, then O += P_{j-1} V_{j-1} into the TMEM O
 //              accumulator; S_{j+1} is issued before P_j exists, so the
 //              tensor core works while the softmax warps do;
-//   warps 2-5  softmax, one query row per thread (warp w reads TMEM lanes
-//              32 (w % 4) .. +31): the S row is read once into registers (its
-//              TMEM buffer is released at once), row max and exp2, P rounded
-//              to bf16 and written into shared memory in the 128-byte-swizzled
-//              K-major layout the MMA reads, the running O rescaled in TMEM
-//              only when the row max grows by more than 2^8 (P and l use the
-//              same stale max, so O / l is unchanged), and the final O / l
-//              written out.
+//   warps 2-9  softmax in two warpgroups: warpgroup g owns key columns
+//              64 g .. 64 g + 63 of every row, one query row per thread (warp
+//              w reads TMEM lanes 32 (w % 4) .. +31, so each lane quarter has
+//              one warp of each group). Its half of the S row is read once
+//              into registers (the TMEM buffer is released at once), the two
+//              halves' maxima meet through shared memory (a 64-thread named
+//              barrier per lane quarter), exp2 of the half row, P rounded to
+//              bf16 and written into its 64-column chunk of shared memory in the
+//              128-byte-swizzled K-major layout the MMA reads, the running O
+//              (its 64 columns) rescaled in TMEM only when the row max grows by
+//              more than 2^8 (P and l use the same stale max, so O / l is
+//              unchanged), and its half of the final O / l written out; the
+//              row sum l is kept per half and added once at the end.
 // TMEM: S0 | S1 | O = 384 of 512 columns. Shared memory: Q 32 KB, K 2 x 32 KB,
 // V 2 x 32 KB, P 2 x 32 KB (224 KB). Every mbarrier wait is bounded (a
 // status word records a timeout and every role returns).
@@ -39,7 +44,9 @@ constexpr uint32_t kTile = 32768;  // one 128 x 128 bf16 tile (two 64-column chu
 constexpr uint32_t kChunk = 16384;
 constexpr uint32_t kOffQ = 0, kOffK = kTile, kOffV = 3 * kTile, kOffP = 5 * kTile;
 constexpr uint32_t kOffBar = 7 * kTile;
-constexpr int kTcSmem = 7 * kTile + 256 + 1024;
+constexpr uint32_t kOffXch = 7 * kTile + 256;  // [2 groups][128 rows] fp32 exchange
+constexpr int kTcSmem = 7 * kTile + 256 + 1024 + 1024;
+constexpr int kTcFwdThreads = 320;
 constexpr float kLog2eTc = 1.4426950408889634f;
 constexpr float kRescale = 8.0f;  // log2 of the largest P the lazy rescale allows
 
@@ -49,7 +56,7 @@ __device__ __forceinline__ float ex2f(float x) {
   return y;
 }
 
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(kTcFwdThreads, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qk,
                        const __grid_constant__ CUtensorMap map_v, __nv_bfloat16* __restrict__ o,
                        float* __restrict__ lse2, int S, int H, int Hkv, int d, float scale_log2,
@@ -89,8 +96,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&vfull[i], 1);
       mbar_init(&vempty[i], 1);
       mbar_init(&sfull[i], 1);
-      mbar_init(&sfree[i], 4);
-      mbar_init(&pfull[i], 4);
+      mbar_init(&sfree[i], 8);
+      mbar_init(&pfull[i], 8);
       mbar_init(&ofull[i], 1);
     }
     mbar_init(drain, 1);
@@ -205,40 +212,53 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   } else {
     const int wq = warp & 3;
+    const int g = (warp - 2) >> 2;  // column half of this warpgroup
+    const int c0 = g * 64;
     const int r = wq * 32 + lane;  // query row within the tile = TMEM lane
     const uint32_t lanes = static_cast<uint32_t>(wq * 32) << 16;
+    float* xch = reinterpret_cast<float*>(smem + kOffXch);  // [2][128]
+    const int bar_id = 1 + wq;  // the two warps of this lane quarter
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nblk; ++j) {
       const int s = j & 1;
       const uint32_t ph = (j >> 1) & 1;
-      if (!mbar_wait(&sfull[s], ph, status, kStatusTimeoutTmemFull)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const uint32_t s_t = tmem + s * 128 + lanes;
-      const bool diag = (j == qb);
-      // The whole S row in registers: four loads in flight, one wait.
-      uint32_t v[128];
-#pragma unroll
-      for (int c = 0; c < 8; ++c) tmem_ld16(s_t + c * 16, v + c * 16);
-      tmem_wait_ld();
+      if (ok && !mbar_wait(&sfull[s], ph, status, kStatusTimeoutTmemFull)) ok = false;
+      uint32_t v[64];
       float mx = -INFINITY;
+      if (ok) {
+        tc_fence_after();
+        const uint32_t s_t = tmem + s * 128 + c0 + lanes;
+        const bool diag = (j == qb);
 #pragma unroll
-      for (int i = 0; i < 128; ++i) {
-        float x = __uint_as_float(v[i]) * scale_log2;
-        if (diag && i > r) x = -INFINITY;
-        v[i] = __float_as_uint(x);
-        mx = fmaxf(mx, x);
+        for (int c = 0; c < 4; ++c) tmem_ld16(s_t + c * 16, v + c * 16);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          float x = __uint_as_float(v[i]) * scale_log2;
+          if (diag && c0 + i > r) x = -INFINITY;
+          v[i] = __float_as_uint(x);
+          mx = fmaxf(mx, x);
+        }
+        // this half of S is in registers: the buffer can take S_{j+2}
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sfree[s]);
       }
-      // S is in registers now: its TMEM buffer can take S_{j+2}.
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sfree[s]);
+      // The row max over both halves. Every warp passes the same sequence of
+      // named barriers whatever happens (a failed wait only skips work), so the
+      // two warps of a quarter can never meet at different barriers.
+      xch[g * 128 + r] = ok ? mx : INFINITY;
+      named_bar_sync(bar_id, 64);
+      const float other = xch[(g ^ 1) * 128 + r];
+      named_bar_sync(bar_id, 64);
+      if (other == INFINITY) ok = false;
+      if (!ok) continue;
+      mx = fmaxf(mx, other);
       // Lazy rescaling: the running max moves only when it grows by more than
       // kRescale (log2 units); P and l use the same stale max, so O / l is the
-      // same quantity (P <= 2^kRescale, well inside bf16 and fp32 range).
+      // same quantity (P <= 2^kRescale, well inside bf16 and fp32 range). The
+      // two warps of a quarter see the same rows, so they decide alike.
       float mnew = m;
       if (__any_sync(0xffffffffu, mx > m + kRescale)) mnew = fmaxf(m, mx);
       const float alpha = (m == -INFINITY) ? 0.f : ex2f(m - mnew);
@@ -247,14 +267,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       // only a rescale of O (below) waits for it.
       if (j > 1 && !mbar_wait(&ofull[s], ((j - 2) >> 1) & 1, status, kStatusTimeoutTmemFull)) {
         ok = false;
-        break;
+        continue;
       }
       const bool rescale = j > 0 && __any_sync(0xffffffffu, alpha != 1.0f);
       tc_fence_after();
-      uint8_t* prow = smem + kOffP + s * kTile + r * 128;
+      uint8_t* prow = smem + kOffP + s * kTile + g * kChunk + r * 128;
       float rs = 0.f;
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {  // 8 keys per 16-byte unit
+      for (int c = 0; c < 8; ++c) {  // 8 keys per 16-byte unit
         uint32_t pk[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -263,21 +283,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           rs += p0 + p1;
           pk[i] = pack_bf16x2(p0, p1);
         }
-        const int unit = c & 7;
-        *reinterpret_cast<uint4*>(prow + (c >> 3) * kChunk + ((unit ^ (r & 7)) << 4)) =
+        *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) =
             make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
       l = l * alpha + rs;
       if (rescale) {
         if (!mbar_wait(&ofull[s ^ 1], ((j - 1) >> 1) & 1, status, kStatusTimeoutTmemFull)) {
           ok = false;
-          break;
+          continue;
         }
         tc_fence_after();
-        const uint32_t o_t = tmem + 256 + lanes;
+        const uint32_t o_t = tmem + 256 + c0 + lanes;
         uint32_t ov[32];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
           tmem_ld32(o_t + c * 32, ov);
           tmem_wait_ld();
 #pragma unroll
@@ -293,16 +312,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (lane == 0) mbar_arrive(&pfull[s]);
       m = mnew;
     }
-    if (ok && mbar_wait(&ofull[(nblk - 1) & 1], ((nblk - 1) >> 1) & 1, status,
-                        kStatusTimeoutTmemFull)) {
+    // the row sum over both halves (both warps of the quarter get here)
+    xch[g * 128 + r] = ok ? l : -1.0f;
+    named_bar_sync(bar_id, 64);
+    const float l_other = xch[(g ^ 1) * 128 + r];
+    if (ok && l_other >= 0.f &&
+        mbar_wait(&ofull[(nblk - 1) & 1], ((nblk - 1) >> 1) & 1, status,
+                  kStatusTimeoutTmemFull)) {
       tc_fence_after();
+      l = g == 0 ? l + l_other : l_other + l;  // the same sum in both halves
       const float inv = 1.0f / l;
       const int qrow = qb * kTcBlk + r;
-      __nv_bfloat16* orow = o + (static_cast<size_t>(row0) + qrow) * d + h * kTcHD;
-      const uint32_t o_t = tmem + 256 + lanes;
+      __nv_bfloat16* orow = o + (static_cast<size_t>(row0) + qrow) * d + h * kTcHD + c0;
+      const uint32_t o_t = tmem + 256 + c0 + lanes;
       uint32_t v[32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         tmem_ld32(o_t + c * 32, v);
         tmem_wait_ld();
 #pragma unroll
@@ -315,7 +340,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           *reinterpret_cast<uint4*>(orow + c * 32 + t * 8) = w4;
         }
       }
-      lse2[(static_cast<size_t>(b) * H + h) * S + qrow] = m + log2f(l);
+      if (g == 0) lse2[(static_cast<size_t>(b) * H + h) * S + qrow] = m + log2f(l);
     }
   }
 
@@ -349,7 +374,9 @@ constexpr uint32_t kBwOffL = 131072, kBwOffD = 131584, kBwOffP = 135168, kBwOffS
 constexpr uint32_t kBwOffBar = 200704;
 constexpr int kBwSmem = 200704 + 256 + 1024;
 
-__global__ void __launch_bounds__(kTcThreads, 1)
+constexpr int kBwThreads = 320;  // producer, MMA issuer, two warpgroups of four softmax warps
+
+__global__ void __launch_bounds__(kBwThreads, 1)
     attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap map_kv,
                             const __grid_constant__ CUtensorMap map_q,
                             const __grid_constant__ CUtensorMap map_do,
@@ -384,8 +411,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&qfull[i], 1);
       mbar_init(&done[i], 1);
       mbar_init(&sfull[i], 1);
-      mbar_init(&sfree[i], 4);
-      mbar_init(&pfull[i], 4);
+      mbar_init(&sfree[i], 8);
+      mbar_init(&pfull[i], 8);
     }
     mbar_init(fin, 1);
     mbar_init(drain, 1);
@@ -490,6 +517,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   } else {
     const int wq = warp & 3;
+    const int g = (warp - 2) >> 2;  // this warpgroup's half of the 64 query columns
+    const int q0 = g * 32;
     const int r = wq * 32 + lane;  // key row within the block = TMEM lane
     const int kpos = kb * kTcBlk + r;
     const uint32_t lanes = static_cast<uint32_t>(wq * 32) << 16;
@@ -504,11 +533,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         break;
       }
       tc_fence_after();
-      uint32_t sv[64], pv[64];
+      uint32_t sv[32], pv[32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        tmem_ld16(tmem + sb * 64 + lanes + c * 16, sv + c * 16);
-        tmem_ld16(tmem + 128 + sb * 64 + lanes + c * 16, pv + c * 16);
+      for (int c = 0; c < 2; ++c) {
+        tmem_ld16(tmem + sb * 64 + q0 + lanes + c * 16, sv + c * 16);
+        tmem_ld16(tmem + 128 + sb * 64 + q0 + lanes + c * 16, pv + c * 16);
       }
       tmem_wait_ld();
       tc_fence_before();
@@ -524,18 +553,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       uint8_t* prow = smem + kBwOffP + sb * 16384 + r * 128;
       uint8_t* srow = smem + kBwOffS + sb * 16384 + r * 128;
 #pragma unroll
-      for (int u8 = 0; u8 < 8; ++u8) {
+      for (int u4 = 0; u4 < 4; ++u4) {
+        const int u8 = g * 4 + u4;  // 16-byte unit of the 64-query row
         uint32_t pk[4], dk[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           float pp[2], dd[2];
 #pragma unroll
           for (int z = 0; z < 2; ++z) {
-            const int q = u8 * 8 + 2 * e + z;
-            float p = ex2f(__uint_as_float(sv[q]) * scale_log2 - Ls[q]);
+            const int ql = u4 * 8 + 2 * e + z;  // within this half
+            const int q = q0 + ql;
+            float p = ex2f(__uint_as_float(sv[ql]) * scale_log2 - Ls[q]);
             if (kpos > i * 64 + q) p = 0.f;
             pp[z] = p;
-            dd[z] = p * (__uint_as_float(pv[q]) - Ds[q]);
+            dd[z] = p * (__uint_as_float(pv[ql]) - Ds[q]);
           }
           pk[e] = pack_bf16x2(pp[0], pp[1]);
           dk[e] = pack_bf16x2(dd[0], dd[1]);
@@ -554,8 +585,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       __nv_bfloat16* dk_row = dqkv + (static_cast<size_t>(row0) + kpos) * ldq + d + hk * kTcHD;
       __nv_bfloat16* dv_row = dk_row + dkv;
       uint32_t v[32];
-#pragma unroll
-      for (int g = 0; g < 2; ++g) {
+      {  // warpgroup 0 writes dV, warpgroup 1 dK
         __nv_bfloat16* out = g ? dk_row : dv_row;
         const float mul = g ? scale : 1.0f;
 #pragma unroll
@@ -597,7 +627,7 @@ constexpr uint32_t kDqOffQ = 0, kDqOffDO = 32768, kDqOffK = 65536, kDqOffV = 131
 constexpr uint32_t kDqOffS = 196608, kDqOffBar = 229376;
 constexpr int kDqSmem = 229376 + 256 + 1024;
 
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(kBwThreads, 1)
     attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap map_q128,
                           const __grid_constant__ CUtensorMap map_do128,
                           const __grid_constant__ CUtensorMap map_kv64,
@@ -634,9 +664,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&kempty[i], 1);
     }
     mbar_init(sfull, 1);
-    mbar_init(sfree, 4);
-    mbar_init(dpfree, 4);
-    mbar_init(pfull, 4);
+    mbar_init(sfree, 8);
+    mbar_init(dpfree, 8);
+    mbar_init(pfull, 8);
     mbar_init(dsfree, 1);
     mbar_init(drain, 1);
     fence_mbar_init();
@@ -753,6 +783,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   } else {
     const int wq = warp & 3;
+    const int g = (warp - 2) >> 2;  // this warpgroup's half of the 128 key columns
+    const int k0 = g * 64;
     const int r = wq * 32 + lane;
     const int qrow = qb * kTcBlk + r;
     const uint32_t lanes = static_cast<uint32_t>(wq * 32) << 16;
@@ -765,18 +797,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         break;
       }
       tc_fence_after();
-      uint32_t sv[128];
+      uint32_t sv[64];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) tmem_ld16(tmem + lanes + c * 16, sv + c * 16);
+      for (int c = 0; c < 4; ++c) tmem_ld16(tmem + lanes + k0 + c * 16, sv + c * 16);
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(sfree);
       const bool diag = (j == qb);
 #pragma unroll
-      for (int k = 0; k < 128; ++k) {
+      for (int k = 0; k < 64; ++k) {
         float p = ex2f(__uint_as_float(sv[k]) * scale_log2 - lr);
-        if (diag && k > r) p = 0.f;
+        if (diag && k0 + k > r) p = 0.f;
         sv[k] = __float_as_uint(p);
       }
       uint32_t dp[32];
@@ -785,10 +817,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         ok = false;
         break;
       }
-      uint8_t* srow = smem + kDqOffS + r * 128;
+      uint8_t* srow = smem + kDqOffS + g * kChunk + r * 128;  // this half's 64-key chunk
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        tmem_ld32(tmem + 128 + lanes + c * 32, dp);
+      for (int c = 0; c < 2; ++c) {
+        tmem_ld32(tmem + 128 + lanes + k0 + c * 32, dp);
         tmem_wait_ld();
 #pragma unroll
         for (int t4 = 0; t4 < 4; ++t4) {
@@ -800,8 +832,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                 __uint_as_float(sv[k + 1]) *
                                     (__uint_as_float(dp[t4 * 8 + 2 * e + 1]) - dr));
           }
-          const int unit = (c & 1) * 4 + t4;
-          *reinterpret_cast<uint4*>(srow + (c >> 1) * kChunk + ((unit ^ (r & 7)) << 4)) =
+          const int unit = c * 4 + t4;
+          *reinterpret_cast<uint4*>(srow + ((unit ^ (r & 7)) << 4)) =
               make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
       }
@@ -814,11 +846,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     if (ok && mbar_wait(dsfree, (nblk - 1) & 1, status, kStatusTimeoutTmemFull)) {
       tc_fence_after();
-      __nv_bfloat16* out = dqkv + (static_cast<size_t>(row0) + qrow) * ldq + h * kTcHD;
+      __nv_bfloat16* out = dqkv + (static_cast<size_t>(row0) + qrow) * ldq + h * kTcHD + k0;
       uint32_t v[32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        tmem_ld32(tmem + 256 + lanes + c * 32, v);
+      for (int c = 0; c < 2; ++c) {  // this warpgroup's 64 of the 128 columns
+        tmem_ld32(tmem + 256 + lanes + k0 + c * 32, v);
         tmem_wait_ld();
 #pragma unroll
         for (int t4 = 0; t4 < 4; ++t4) {
@@ -860,8 +892,8 @@ int attention_fwd_tc(const AttnArgs& a, int* status, cudaStream_t stream) {
     attr = true;
   }
   dim3 grid(a.H, a.S / kTcBlk, a.B);
-  attn_fwd_tc_kernel<<<grid, kTcThreads, kTcSmem, stream>>>(mqk, mv, a.o, a.lse, a.S, a.H, hkv,
-                                                             a.d, a.scale * kLog2eTc, status);
+  attn_fwd_tc_kernel<<<grid, kTcFwdThreads, kTcSmem, stream>>>(mqk, mv, a.o, a.lse, a.S, a.H, hkv,
+                                                                a.d, a.scale * kLog2eTc, status);
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
 
@@ -893,9 +925,9 @@ int attention_bwd_tc(const AttnBwdArgs& a, int* status, cudaStream_t stream) {
     attr = true;
   }
   const float sl2 = a.scale * kLog2eTc;
-  attn_bwd_dkdv_tc_kernel<<<dim3(hkv, a.S / kTcBlk, a.B), kTcThreads, kBwSmem, stream>>>(
+  attn_bwd_dkdv_tc_kernel<<<dim3(hkv, a.S / kTcBlk, a.B), kBwThreads, kBwSmem, stream>>>(
       m_kv128, m_q64, m_do64, a.lse, a.Dbuf, a.dqkv, a.S, a.H, hkv, a.d, sl2, a.scale, status);
-  attn_bwd_dq_tc_kernel<<<dim3(a.H, a.S / kTcBlk, a.B), kTcThreads, kDqSmem, stream>>>(
+  attn_bwd_dq_tc_kernel<<<dim3(a.H, a.S / kTcBlk, a.B), kBwThreads, kDqSmem, stream>>>(
       m_q128, m_do128, m_kv64, a.lse, a.Dbuf, a.dqkv, a.S, a.H, hkv, a.d, sl2, a.scale, status);
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }

@@ -285,6 +285,27 @@ def test_attention(cuda, hd, S):
     assert torch.equal(dqkv, dqkv2)
 
 
+def test_attention_tcgen05_long_rows(cuda):
+    """The tensor-core attention (head size 128) over 8 causal key blocks:
+    both softmax warpgroups, the lazy rescale and the double-buffered S and P
+    run many times per tile; fp32 SDPA reference; same bits twice."""
+    torch.manual_seed(12)
+    B, H, hd, S = 1, 4, 128, 1024
+    d = H * hd
+    qkv = bf(B * S, 3 * d, dev=cuda, scale=2.0)
+    o, lse = ops.attention_fwd(qkv, B, S, H, hd)
+    q, k, v = qkv.float().view(B, S, 3, H, hd).permute(2, 0, 3, 1, 4)
+    ref = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+    assert rel_err(o, ref.transpose(1, 2).reshape(B * S, d)) < 1e-2
+    att = (q @ k.transpose(-2, -1)) / math.sqrt(hd)
+    att = att.masked_fill(torch.triu(torch.ones(S, S, dtype=torch.bool, device=cuda), 1),
+                          float("-inf"))
+    assert rel_err(lse, torch.logsumexp(att, -1) / math.log(2)) < 1e-5
+    o2, lse2 = ops.attention_fwd(qkv, B, S, H, hd)
+    assert torch.equal(o, o2) and torch.equal(lse, lse2)
+    assert ops.ext().status_read_clear() == 0
+
+
 @pytest.mark.parametrize("V", [50257, 1001, 70001])
 def test_cross_entropy(cuda, V):
     """50257 and 1001 take the shared-memory row path (1001: a ragged last
