@@ -28,7 +28,8 @@ class LocalCluster:
     def __init__(self, workdir: str, regions: list, token: str = "demo-token", device: str = "cpu",
                  wan_links: dict | None = None, liveness: dict | None = None, max_heals: int = 3,
                  stage_timeout_s: float = 30.0, coord: dict | None = None,
-                 worker_env: dict | None = None, worker_args: list | None = None):
+                 worker_env: dict | None = None, worker_args: list | None = None,
+                 sequential: bool = False):
         self.workdir = os.path.abspath(workdir)
         os.makedirs(self.workdir, exist_ok=True)
         cfg = CoordinatorConfig(state_dir=os.path.join(self.workdir, "coordinator"), token=token,
@@ -55,6 +56,12 @@ class LocalCluster:
             p = subprocess.Popen(cmd, stdout=log, stderr=subprocess.STDOUT, env={**env, **per[i]},
                                  start_new_session=True)
             self.workers.append((name, p, log))
+            if sequential:
+                # registration order = list order (placement takes workers in
+                # that order; the last ones are the spares)
+                deadline = time.time() + 120.0
+                while len(self.coord.nodes) < i + 1 and time.time() < deadline and p.poll() is None:
+                    time.sleep(0.1)
 
     def node_of(self, name: str):
         for nid, n in self.coord.nodes.items():

@@ -63,6 +63,13 @@ def loss_path(spec, stage, peer) -> str:
     return os.path.join(spec.out_dir, f"{spec.tag}_losses_r{stage}p{peer}.json")
 
 
+def _leaves_after(step: int, spec) -> bool:
+    """EWB_TEST_LEAVE_AFTER_STEP=N (a failure-injection seam for tests, set on
+    one worker): the first attempt's stage process exits right after step N."""
+    v = os.environ.get("EWB_TEST_LEAVE_AFTER_STEP")
+    return v is not None and not spec.resume and step == int(v)
+
+
 def run_stage(spec, stage: int, peer: int, timeout_s: float = 600.0) -> int:
     from elysium_wan_b200.fault_tolerance import checkpoint as ckpt
     from elysium_wan_b200.parallel.p2p import PipeComm
@@ -159,6 +166,12 @@ def run_stage(spec, stage: int, peer: int, timeout_s: float = 600.0) -> int:
             path = ckpt.commit_wave(spec, stage, peer, step + 1, eng.state_dict())
             _print("WT_WAVE", {"step": step + 1, "dir": path})
         _print("WT_STEP", {"step": step, "ms": round(dt * 1e3, 3)})
+        if _leaves_after(step, spec):
+            # Test seam: this process leaves between steps (its kernels and
+            # collectives are complete), without a done marker, as a rank whose
+            # machine went away would.
+            sys.stdout.flush()
+            os._exit(17)
     tel.close()
     n_run = spec.steps - start
     _print("WT_TIMING", {"steps": n_run, "total_s": round(time.perf_counter() - t_run, 3),
