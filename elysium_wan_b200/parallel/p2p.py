@@ -253,6 +253,11 @@ class PipeComm:
             w.wait()
         return bufs
 
+    @staticmethod
+    def ready(handle) -> bool:
+        """Whether a posted receive has completed (never blocks)."""
+        return all(w.is_completed() for w in handle[1])
+
     def as_act(self, bufs) -> Act:
         if self.fp8:
             return Act(bufs[0].view(torch.float8_e4m3fn), bufs[1])

@@ -66,6 +66,15 @@ class StageEngine:
 
         self.sim_slow = parse_sim_slow().get(stage, (1.0, 0))
         self.w_pair = bool(spec.w_pair) and spec.stage_widths[stage] == 1
+        # W fill (reference RUNTIME-I27, src/wantrain/runtime/stage.py:3353-3373):
+        # on host devices a receive that is late runs deferred W tasks, one
+        # layer's at a time, instead of idling; on a GPU the side stream
+        # already overlaps W with the wait.
+        self.fill_w = bool(spec.schedule_fill) and self.device.type != "cuda" and not self.w_pair
+        self.w_filled = 0  # W tasks run while a receive was pending (last step)
+        self._w_seq: list = []
+        self._w_pos = 0
+        self._w_done: set = set()
         self._w_stash = None
         side = os.environ.get("EWB_W_STREAM", "1") == "1"
         self.wexec = WExecutor(self.device, enabled=side)
@@ -93,6 +102,33 @@ class StageEngine:
                 from elysium_wan_b200.parallel.zero1 import Zero1
 
                 self.zero1 = Zero1(self, comm)
+
+    def _await(self, handle, wq: dict, step: int):
+        """Wait for a receive. While it is pending (host devices), run the
+        deferred W tasks of the next W op in the order, one task (one layer's
+        weight gradients) at a time, once its B is done: W work still runs in
+        the order's sequence, so every parameter folds its contributions in the
+        same order and no bit changes; the W op itself later runs what is
+        left."""
+        comm = self.comm
+        if self.fill_w and hasattr(comm, "ready"):
+            seq = self._w_seq
+            while not comm.ready(handle):
+                while self._w_pos < len(seq) and seq[self._w_pos] in self._w_done:
+                    self._w_pos += 1
+                if self._w_pos == len(seq):
+                    break
+                mb = seq[self._w_pos]
+                tasks = wq.get(mb)
+                if not tasks:  # its B has not run yet
+                    break
+                t0 = time.perf_counter()
+                tasks.pop(0).run()
+                if not tasks:
+                    self._w_done.add(mb)
+                self.w_filled += 1
+                self.events.append(("W", mb, t0, time.perf_counter()))
+        return comm.wait(handle)
 
     def _run_w(self, tasks: list, mb: int):
         if self.zero1 is not None and hasattr(self.zero1, "mark"):
@@ -203,6 +239,10 @@ class StageEngine:
         ev = self.timing
         self.events = []
         inline_done: set = set()
+        self.w_filled = 0
+        self._w_seq = [m for o, m in self.order if o == "W"]
+        self._w_pos = 0
+        self._w_done: set = set()
         keep = "inputs" if self.recompute else "all"
         for idx, (op, mb) in enumerate(self.order):
             if op == "W" and mb in inline_done:
@@ -226,7 +266,7 @@ class StageEngine:
                 if self.first:
                     inp = batches[mb][0]
                 else:
-                    inp = comm.as_act(comm.wait(act_q.pop(mb)))
+                    inp = comm.as_act(self._await(act_q.pop(mb), wq, step))
                 fi += 1
                 if not self.first and fi < len(f_mbs):
                     act_q[f_mbs[fi]] = comm.irecv_act(f_mbs[fi])
@@ -243,7 +283,7 @@ class StageEngine:
                 if self.last:
                     dy = None
                 else:
-                    dy = comm.wait(grad_q.pop(mb))[0]
+                    dy = self._await(grad_q.pop(mb), wq, step)[0]
                     bi += 1
                     if bi < len(b_mbs):
                         grad_q[b_mbs[bi]] = comm.irecv_grad(b_mbs[bi])
@@ -257,13 +297,15 @@ class StageEngine:
                                          w_exec=lambda ts, m=mb: self._run_w(ts, m))
                 if inline:
                     inline_done.add(mb)
+                    self._w_done.add(mb)
                 else:
                     wq[mb] = tasks
                 if not self.first:
                     sends += comm.send_grad(mb, dx)
             else:  # W
                 mark()
-                self._run_w(wq.pop(mb), mb)
+                self._run_w(wq.pop(mb, []), mb)
+                self._w_done.add(mb)
             if self.nvtx:
                 torch.cuda.nvtx.range_pop()
             if ev and not (op == "W" and self.wexec.cuda):

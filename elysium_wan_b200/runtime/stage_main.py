@@ -150,6 +150,8 @@ def run_stage(spec, stage: int, peer: int, timeout_s: float = 600.0) -> int:
             print(f"WT_WARN telemetry summary of step {step} exceeded 4096 bytes: its per-op "
                   f"medians were dropped", flush=True)
         _print("WT_TELEM", summary)
+        if eng.w_filled:
+            _print("WT_WFILL", {"step": step, "tasks": eng.w_filled})
         tel.write(json.dumps({"step": step, "events": [[o, m, round(a, 4), round(d, 4)]
                                                         for o, m, a, d in eng.op_times_ms()]})
                   + "\n")

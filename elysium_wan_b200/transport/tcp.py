@@ -331,6 +331,11 @@ class TcpPipeComm:
     def irecv_grad(self, mb: int):
         return (BWD, mb)
 
+    def ready(self, handle) -> bool:
+        """Whether the frame a receive waits for has arrived (never blocks)."""
+        with self.inbox.cv:
+            return bool(self.inbox.q[handle]) or self.inbox.err is not None
+
     def wait(self, handle):
         f = self.inbox.get(handle, self.timeout)
         t = f.tensor()

@@ -304,3 +304,32 @@ def test_pipeline_through_a_tearing_proxy_is_bitwise(tmp_path, monkeypatch):
     assert r["ok"], r
     assert r["compared"] == 8
     assert proxy.forwarded > 0
+
+
+def test_late_receive_fills_with_deferred_w_bitwise(tmp_path, monkeypatch):
+    """A slow hop makes receives late; the stage runs deferred W tasks while it
+    waits (the order's W sequence kept) and every loss still equals the
+    oracle bit for bit."""
+    import glob
+    import json as _json
+
+    from elysium_wan_b200.launch.local import run_and_compare
+    from elysium_wan_b200.models.config import make_config
+    from elysium_wan_b200.runtime.spec import JobSpec
+
+    monkeypatch.setenv("ELYSIUM_PEER_KEY", str(tmp_path / "peer.key"))
+    cfg = make_config("toy", n_layer=6, vocab_size=97, d_model=128, n_head=4, seq_len=16,
+                      boundary_dtype="bf16")
+    port = 33000 + (os.getpid() % 200) * 10
+    spec = JobSpec(model=cfg, stages=3, microbatches=6, mb_size=2, steps=2,
+                   out_dir=str(tmp_path), port_base=port, backend="tcp", wire_codec="planes",
+                   links=[{"latency_ms": 40.0, "bw_mbps": 0.0}] * 3)
+    r = run_and_compare(spec, timeout=300)
+    assert r["ok"], r
+    assert r["compared"] == 12
+    filled = 0
+    for path in glob.glob(os.path.join(str(tmp_path), "*_r*p*.log")):
+        for line in open(path):
+            if line.startswith("WT_WFILL"):
+                filled += _json.loads(line.split(" ", 1)[1])["tasks"]
+    assert filled > 0
