@@ -10,7 +10,8 @@ the W inputs (dY, X pairs) that B hands over, and the boundary tensor.
 from __future__ import annotations
 
 from elysium_wan_b200.scheduler import partition as part
-from elysium_wan_b200.scheduler.zero_bubble import ZBConfig, comm_seconds, slot_orders, zero_bubble
+from elysium_wan_b200.scheduler.zero_bubble import (ZBConfig, comm_seconds, simulate_slots,
+                                                    slot_orders, stage_peak, zero_bubble)
 
 _BOUNDARY_BYTES = {"fp32": 4, "bf16": 2, "fp8_e4m3_b128": 1}
 
@@ -95,9 +96,65 @@ def default_schedule(spec, budget_bytes: list | None = None) -> list:
             two_p = [2 * spec.stages * unit] * spec.stages
             cfg = cfg.with_budget([min(a, b) for a, b in zip(budget_bytes, two_p)])
             mode = "given"
-    sched = zero_bubble(cfg, mode if mode in ("1p", "2p", "given") else "2p")
-    out = []
-    for r in range(spec.stages):
-        out.append([[[op, mb] for op, mb in o]
-                    for o in slot_orders(sched.orders[r], spec.mb_owner[r], spec.stage_widths[r])])
+    mode = mode if mode in ("1p", "2p", "given") else "2p"
+    sched = zero_bubble(cfg, mode)
+    split = [slot_orders(sched.orders[r], spec.mb_owner[r], spec.stage_widths[r])
+             for r in range(spec.stages)]
+    if any(w > 1 for w in spec.stage_widths):
+        lanes = lane_orders(spec, cfg, mode, budget_bytes)
+        if lanes:
+            mixed = [lanes.get(r, split[r]) for r in range(spec.stages)]
+            try:
+                _, ms_split = simulate_slots(cfg, split, spec.peer_weights)
+                _, ms_lanes = simulate_slots(cfg, mixed, spec.peer_weights)
+            except ValueError:  # a lane waits on an op another slot orders later
+                ms_lanes = ms_split = 0.0
+            if ms_lanes < ms_split * (1.0 - 1e-9):
+                split = mixed
+    return [[[[op, mb] for op, mb in o] for o in orders] for orders in split]
+
+
+def lane_orders(spec, cfg: ZBConfig, mode: str, budget_bytes: list | None = None) -> dict:
+    """{stage: [order per peer]} for the wide stages, each peer's order solved
+    as a pipeline of its own (reference: _lane_orders / bridge_orders,
+    src/wantrain/scheduler/zero_bubble.py:715-870, semantics only).
+
+    A peer of a wide stage runs whole microbatches, the ones it owns. Seen
+    from those microbatches the job is a pipeline in which every stage gives
+    them the peer's share of its throughput, so each op costs the aggregate
+    stage cost x (sum of the stage's weights / the peer's weight); the
+    zero-bubble solve of that lane, mapped onto the owned microbatches, is the
+    peer's order. Each solve keeps the device budget of one GPU, which the
+    stage-level solve has to share among all the stage's microbatches. A
+    stage whose lanes cannot all be solved, or whose lane order would not fit
+    its budget, keeps the stage-level split. default_schedule keeps the lanes
+    only when the slot simulation finds them faster."""
+    out = {}
+    for s in range(spec.stages):
+        weights = spec.peer_weights[s]
+        if len(weights) == 1:
+            continue
+        total = float(sum(weights))
+        per: list | None = []
+        for q, wq in enumerate(weights):
+            own = [mb for mb, o in enumerate(spec.mb_owner[s]) if o == q]
+            if not own:
+                per.append([])
+                continue
+            k = total / wq
+            lane = ZBConfig(cfg.n_stages, len(own), [c * k for c in cfg.cost_f],
+                            [c * k for c in cfg.cost_b], [c * k for c in cfg.cost_w], cfg.comm,
+                            cfg.mem_f, cfg.mem_b, cfg.mem_w, max_mem=cfg.max_mem)
+            try:
+                lane_sched = zero_bubble(lane, mode)
+            except ValueError:
+                per = None
+                break
+            order = [(op, own[i]) for op, i in lane_sched.orders[s]]
+            if budget_bytes and stage_peak(cfg, s, order) > budget_bytes[s] * (1 + 1e-9):
+                per = None
+                break
+            per.append(order)
+        if per is not None:
+            out[s] = per
     return out

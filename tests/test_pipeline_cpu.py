@@ -30,6 +30,10 @@ CASES = {
     "w_pair_wide_1_2": dict(stages=2, stage_widths=[1, 2], w_pair=True),
     "chain3_fp8_recompute": dict(stages=3, recompute=True, model_kw=dict(boundary_dtype="fp8_e4m3_b128")),
     "wide_2_1": dict(stages=2, stage_widths=[2, 1]),
+    # Uneven peers: each peer of the wide stages runs its own lane order
+    # (solved per peer, chosen because the slot simulation finds it faster).
+    "lanes_2_2": dict(stages=2, stage_widths=[2, 2], peer_weights=[[1.0, 2.0], [1.0, 2.0]],
+                      microbatches=6, zb_mem_mode="2p"),
     "wide_1_2": dict(stages=2, stage_widths=[1, 2]),
     # Llama block (RMSNorm, GQA, RoPE, SwiGLU, no bias) cut over 2 stages.
     "llama_chain2": dict(stages=2, model_kw=dict(norm="rmsnorm", mlp="swiglu", pos="rope",
