@@ -305,7 +305,9 @@ def run_ours(args) -> dict | None:
         print("[bench] rank %d: %s" % (rank, json.dumps(
             {"busy_frac": busy, "busy_ms": summ["busy_ms"], "ops": summ.get("ops"),
              "phases": eng.phase_ms()})), file=sys.stderr, flush=True)
-    vec = torch.tensor([dev_ms, wall_ms, float(launches), busy or 0.0, busy or 2.0],
+    ph = eng.phase_ms()
+    vec = torch.tensor([dev_ms, wall_ms, float(launches), busy or 0.0, busy or 2.0,
+                        ph.get("ops_ms", 0.0), ph.get("opt_ms", 0.0)],
                        dtype=torch.float64, device=dev)
     if world > 1:
         mx = vec.clone()
@@ -317,8 +319,10 @@ def run_ours(args) -> dict | None:
         dev_ms, wall_ms = mx[0].item(), mx[1].item()
         launches = int(sm[2].item())
         busy_min = mn[4].item()
+        ops_ms, opt_ms = mx[5].item(), mx[6].item()
     else:
         busy_min = busy
+        ops_ms, opt_ms = ph.get("ops_ms", 0.0), ph.get("opt_ms", 0.0)
     st = ops.ext().status_read_clear()
     losses = [v for _, _, v in eng.losses[-spec.microbatches:]] if eng.last else []
     if comm is not None:
@@ -356,6 +360,12 @@ def run_ours(args) -> dict | None:
                 "d2h_bytes_per_step": spec.microbatches * 4},
         "gpu_launches": launches,
         "busy_frac_min_over_stages": None if busy_min is None else round(busy_min, 4),
+        # The last timed step split at its last op (max over ranks): the F/B/W
+        # span and the optimizer / parameter-exchange phase after it, and the
+        # tokens/s of the F/B/W span alone (comparable across N whatever the
+        # optimizer placement, e.g. host moments at N = 1).
+        "phases": {"ops_ms": round(ops_ms, 2), "opt_ms": round(opt_ms, 2),
+                   "ops_only_tokens_per_s": round(tokens / (ops_ms / 1e3), 1) if ops_ms else None},
         "last_losses": losses[:4],
     }
 

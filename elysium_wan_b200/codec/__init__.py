@@ -8,8 +8,8 @@ planes compressed on parallel threads with the interpreter lock released.
 
 - planes: any dtype, exact bytes split into byte planes (most significant
   first) and compressed; one-byte dtypes go as one interleaved blob.
-- e4m3_b128 (this engine's fp8 boundary): the e4m3 codes and their fp32
-  1x128 block scales in one payload (wire dtype id 34).
+- e4m3_b128 / e5m2_b128 (this engine's fp8 boundaries): the fp8 codes and
+  their fp32 1x128 block scales in one payload (wire dtype ids 34 / 35).
 - fp8_planes: e4m3 codes split into sign+exponent / mantissa nibble planes.
 - f32_planes: fp32 bytes in plane-major order, one compressed blob.
 
@@ -27,6 +27,9 @@ DT = {0: torch.float32, 1: torch.bfloat16, 2: torch.float16, 3: torch.float8_e4m
       4: torch.float8_e5m2, 5: torch.int64}
 ID = {v: k for k, v in DT.items()}
 E4M3_B128_ID = 34
+E5M2_B128_ID = 35
+Q8_B128 = {E4M3_B128_ID: torch.float8_e4m3fn, E5M2_B128_ID: torch.float8_e5m2}
+_Q8_B128_ID = {v: k for k, v in Q8_B128.items()}
 
 _IVIEW = {1: torch.uint8, 2: torch.int16, 4: torch.int32, 8: torch.int64}
 
@@ -59,25 +62,30 @@ def planes_encode(t: torch.Tensor, level: int = 1) -> tuple[bytes, tuple]:
 
 def planes_decode(payload: bytes, shape) -> torch.Tensor:
     did = payload[0]
-    if did == E4M3_B128_ID:
-        raise ValueError("an e4m3_b128 payload decodes with e4m3_b128_decode")
+    if did in Q8_B128:
+        raise ValueError("an fp8 b128 payload decodes with q8_b128_decode")
     dtype = DT[did]
     esz = torch.empty(0, dtype=dtype).element_size()
     _, _, raw = wire().planes_decode(payload, esz)
     return _tensor_of(raw, dtype, shape)
 
 
-def e4m3_b128_encode(codes: torch.Tensor, scales: torch.Tensor, level: int = 1):
-    """(e4m3 [T, d], fp32 scales [T, d / 128]) -> (payload, shape of codes)."""
-    return (wire().pair_encode(_bytes_of(codes), _bytes_of(scales.float()), 4, E4M3_B128_ID,
-                               level), tuple(codes.shape))
+def q8_b128_encode(codes: torch.Tensor, scales: torch.Tensor, level: int = 1):
+    """(fp8 codes [T, d] (e4m3 or e5m2), fp32 scales [T, d / 128]) ->
+    (payload, shape of codes); the payload's dtype id names the format."""
+    return (wire().pair_encode(_bytes_of(codes), _bytes_of(scales.float()), 4,
+                               _Q8_B128_ID[codes.dtype], level), tuple(codes.shape))
 
 
-def e4m3_b128_decode(payload: bytes, shape):
-    _, a, b = wire().pair_decode(payload, 4)
-    codes = _tensor_of(a, torch.float8_e4m3fn, shape)
+def q8_b128_decode(payload: bytes, shape):
+    did, a, b = wire().pair_decode(payload, 4)
+    codes = _tensor_of(a, Q8_B128[did], shape)
     scales = _tensor_of(b, torch.float32, (shape[0], shape[1] // 128))
     return codes, scales
+
+
+e4m3_b128_encode = q8_b128_encode
+e4m3_b128_decode = q8_b128_decode
 
 
 def fp8_planes_encode(t: torch.Tensor, level: int = 1) -> tuple[bytes, tuple]:

@@ -39,7 +39,6 @@ namespace {
 
 constexpr int kTcHD = 128;
 constexpr int kTcBlk = 128;
-constexpr int kTcThreads = 192;
 constexpr uint32_t kTile = 32768;  // one 128 x 128 bf16 tile (two 64-column chunks)
 constexpr uint32_t kChunk = 16384;
 constexpr uint32_t kOffQ = 0, kOffK = kTile, kOffV = 3 * kTile, kOffP = 5 * kTile;

@@ -88,6 +88,17 @@ void gemm_impl(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor out,
                const ewb::PeerScatter* peer, c10::optional<at::Tensor> a2 = c10::nullopt,
                c10::optional<at::Tensor> b2 = c10::nullopt);
 
+// The boundary format a tensor's dtype names (BoundaryFmt in common.cuh).
+int boundary_fmt(const at::Tensor& t, const char* what) {
+  switch (t.scalar_type()) {
+    case at::kBFloat16: return ewb::kFmtBf16;
+    case at::kFloat8_e4m3fn: return ewb::kFmtE4m3;
+    case at::kFloat8_e5m2: return ewb::kFmtE5m2;
+    case at::kHalf: return ewb::kFmtF16;
+    default: TORCH_CHECK(false, what, " must be bf16, fp16, e4m3 or e5m2"); return -1;
+  }
+}
+
 void gemm(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor out, int64_t epi,
           c10::optional<at::Tensor> bias, c10::optional<at::Tensor> resid,
           c10::optional<at::Tensor> resid_scale, c10::optional<at::Tensor> aux,
@@ -182,13 +193,11 @@ void gemm_impl(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor out,
     check_2d_rowmajor(*resid, "resid");
     e.resid = resid->data_ptr();
     e.ldr = resid->stride(0);
-    e.resid_fp8 = resid->scalar_type() == at::kFloat8_e4m3fn ? 1 : 0;
-    if (e.resid_fp8) {
+    e.resid_fmt = boundary_fmt(*resid, "resid");
+    if (ewb::fmt_q8(e.resid_fmt)) {
       TORCH_CHECK(resid_scale.has_value() && resid_scale->defined(), "fp8 resid needs scales");
       e.resid_scale = resid_scale->data_ptr<float>();
       e.ld_resid_scale = resid_scale->stride(0);
-    } else {
-      TORCH_CHECK(resid->scalar_type() == at::kBFloat16, "resid must be bf16 or e4m3");
     }
   }
   if (aux.has_value() && aux->defined()) {
@@ -205,9 +214,13 @@ void gemm_impl(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor out,
   switch (e.kind) {
     case ewb::kEpiBf16:
     case ewb::kEpiGelu:
-    case ewb::kEpiResid:
     case ewb::kEpiDGelu:
       TORCH_CHECK(out.scalar_type() == at::kBFloat16, "out must be bf16 for this epilogue");
+      break;
+    case ewb::kEpiResid:
+      TORCH_CHECK(out.scalar_type() == at::kBFloat16 || out.scalar_type() == at::kHalf,
+                  "out must be bf16 or fp16 for the residual epilogue");
+      e.out_fmt = boundary_fmt(out, "out");
       break;
     case ewb::kEpiAccF32:
     case ewb::kEpiF32:
@@ -215,7 +228,8 @@ void gemm_impl(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor out,
       TORCH_CHECK(out.scalar_type() == at::kFloat, "out must be fp32 for this epilogue");
       break;
     case ewb::kEpiResidQ8:
-      TORCH_CHECK(out.scalar_type() == at::kFloat8_e4m3fn, "out must be e4m3");
+      e.out_fmt = boundary_fmt(out, "out");
+      TORCH_CHECK(ewb::fmt_q8(e.out_fmt), "out must be e4m3 or e5m2");
       TORCH_CHECK(e.scale_out != nullptr, "scale_out required");
       break;
     default: TORCH_CHECK(false, "unknown epilogue ", epi);
@@ -299,14 +313,12 @@ void layernorm_fwd(at::Tensor x, c10::optional<at::Tensor> x_scale, at::Tensor g
   c10::cuda::CUDAGuard guard(x.device());
   ewb::LnArgs a{};
   a.x = x.data_ptr();
-  a.x_fp8 = x.scalar_type() == at::kFloat8_e4m3fn;
+  a.x_fmt = boundary_fmt(x, "x");
   a.ldx = x.stride(0);
-  if (a.x_fp8) {
-    TORCH_CHECK(x_scale.has_value(), "fp8 input needs scales");
+  if (ewb::fmt_q8(a.x_fmt)) {
+    TORCH_CHECK(x_scale.has_value() && x_scale->defined(), "fp8 input needs scales");
     a.x_scale = x_scale->data_ptr<float>();
     a.ldxs = x_scale->stride(0);
-  } else {
-    TORCH_CHECK(x.scalar_type() == at::kBFloat16, "x must be bf16 or e4m3");
   }
   a.gamma = gamma.data_ptr<float>();
   a.rms = !(beta.has_value() && beta->defined());
@@ -339,9 +351,10 @@ void layernorm_bwd(at::Tensor dy, at::Tensor x, c10::optional<at::Tensor> x_scal
   a.dy = reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr());
   a.lddy = dy.stride(0);
   a.x = x.data_ptr();
-  a.x_fp8 = x.scalar_type() == at::kFloat8_e4m3fn;
+  a.x_fmt = boundary_fmt(x, "x");
   a.ldx = x.stride(0);
-  if (a.x_fp8) {
+  if (ewb::fmt_q8(a.x_fmt)) {
+    TORCH_CHECK(x_scale.has_value() && x_scale->defined(), "fp8 input needs scales");
     a.x_scale = x_scale->data_ptr<float>();
     a.ldxs = x_scale->stride(0);
   }
@@ -516,9 +529,9 @@ void mean_reduce(at::Tensor x, at::Tensor out) {
   count(1);
 }
 
+// out's dtype names the boundary format (fp8 outputs also fill out_scale).
 void embed_fwd(at::Tensor idx, at::Tensor wte, c10::optional<at::Tensor> wpe, int64_t S,
-               c10::optional<at::Tensor> out_bf16, c10::optional<at::Tensor> out_q8,
-               c10::optional<at::Tensor> out_scale) {
+               at::Tensor out, c10::optional<at::Tensor> out_scale) {
   c10::cuda::CUDAGuard guard(idx.device());
   ewb::EmbedArgs a{};
   a.idx = idx.data_ptr<int64_t>();
@@ -527,10 +540,12 @@ void embed_fwd(at::Tensor idx, at::Tensor wte, c10::optional<at::Tensor> wpe, in
   a.T = idx.numel();
   a.S = S;
   a.d = wte.size(1);
-  a.out_bf16 = ptr_or_null<__nv_bfloat16>(out_bf16);
-  a.out_q8 = ptr_or_null<uint8_t>(out_q8);
+  check_2d_rowmajor(out, "out");
+  TORCH_CHECK(out.stride(0) == a.d, "out must be contiguous [T][d]");
+  a.out = out.data_ptr();
+  a.out_fmt = boundary_fmt(out, "out");
   a.out_scale = ptr_or_null<float>(out_scale);
-  TORCH_CHECK((a.out_bf16 != nullptr) != (a.out_q8 != nullptr), "exactly one output format");
+  TORCH_CHECK(!ewb::fmt_q8(a.out_fmt) || a.out_scale != nullptr, "fp8 output needs out_scale");
   ok(ewb::embed_fwd(a, cur_stream()), "embed_fwd");
   count(1);
 }
@@ -592,23 +607,25 @@ void colsum(at::Tensor x, at::Tensor part, at::Tensor grad, bool accumulate) {
   count(2);
 }
 
-void quant_e4m3(at::Tensor x, at::Tensor q, at::Tensor scale) {
+// fp8 with 1x128 scales; q's dtype (e4m3 / e5m2) names the format.
+void quant_q8(at::Tensor x, at::Tensor q, at::Tensor scale) {
   TORCH_CHECK(x.is_contiguous() && q.is_contiguous() && scale.is_contiguous(), "contiguous");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16, "x must be bf16");
   c10::cuda::CUDAGuard guard(x.device());
-  ok(ewb::quant_e4m3_rows(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.size(0),
-                          x.size(1), reinterpret_cast<uint8_t*>(q.data_ptr()),
-                          scale.data_ptr<float>(), cur_stream()),
-     "quant_e4m3");
+  ok(ewb::quant_q8_rows(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.size(0), x.size(1),
+                        boundary_fmt(q, "q"), reinterpret_cast<uint8_t*>(q.data_ptr()),
+                        scale.data_ptr<float>(), cur_stream()),
+     "quant_q8");
   count(1);
 }
 
-void dequant_e4m3(at::Tensor q, at::Tensor scale, at::Tensor y) {
+void dequant_q8(at::Tensor q, at::Tensor scale, at::Tensor y) {
   TORCH_CHECK(y.is_contiguous() && q.is_contiguous() && scale.is_contiguous(), "contiguous");
   c10::cuda::CUDAGuard guard(q.device());
-  ok(ewb::dequant_e4m3_rows(reinterpret_cast<const uint8_t*>(q.data_ptr()),
-                            scale.data_ptr<float>(), q.size(0), q.size(1),
-                            reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), cur_stream()),
-     "dequant_e4m3");
+  ok(ewb::dequant_q8_rows(reinterpret_cast<const uint8_t*>(q.data_ptr()), scale.data_ptr<float>(),
+                          q.size(0), q.size(1), boundary_fmt(q, "q"),
+                          reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), cur_stream()),
+     "dequant_q8");
   count(1);
 }
 
@@ -740,8 +757,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw", &adamw);
   m.def("colsum", &colsum);
   m.def("colsum_chunks", &colsum_chunks);
-  m.def("quant_e4m3", &quant_e4m3);
-  m.def("dequant_e4m3", &dequant_e4m3);
+  m.def("quant_q8", &quant_q8);
+  m.def("dequant_q8", &dequant_q8);
   m.def("cast_bf16", &cast_bf16);
   m.def("launch_count", &launch_count);
   m.def("install_segv_backtrace", &install_segv_backtrace);

@@ -18,6 +18,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "boundary.h"
+
 namespace ewb {
 
 // ---------------------------------------------------------------- status word
@@ -434,6 +436,53 @@ __device__ __forceinline__ float e4m3_block_scale(float amax) {
   int e;
   frexpf(amax, &e);
   return ldexpf(1.0f, e - 8);
+}
+
+// 1x128 block scale of either fp8 format: 2^(e - 8) for e4m3 (|x| / scale <
+// 256 <= 448) and 2^(e - 15) for e5m2 (|x| / scale < 32768 <= 57344).
+__device__ __forceinline__ float q8_block_scale(float amax, int fmt) {
+  if (!(amax > 0.0f) || !isfinite(amax)) return 1.0f;
+  int e;
+  frexpf(amax, &e);
+  return ldexpf(1.0f, e - (fmt == kFmtE5m2 ? 15 : 8));
+}
+
+// Two fp32 values (already divided by the block scale) as two fp8 bytes.
+__device__ __forceinline__ uint32_t q8x2(float a, float b, int fmt) {
+  return static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(
+      make_float2(a, b), __NV_SATFINITE, fmt == kFmtE5m2 ? __NV_E5M2 : __NV_E4M3));
+}
+
+__device__ __forceinline__ float q8_value(uint8_t byte, int fmt) {
+  const __half_raw h =
+      __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(byte), fmt == kFmtE5m2 ? __NV_E5M2 : __NV_E4M3);
+  return __half2float(__half(h));
+}
+
+// Eight boundary elements packed in 16 bytes (bf16 / fp16) or 8 bytes (fp8,
+// the low half of w) as fp32; `scale` multiplies fp8 values.
+__device__ __forceinline__ void unpack8_fmt(const uint4& w, int fmt, float scale, float* v) {
+  if (fmt_q8(fmt)) {
+    const uint8_t* b = reinterpret_cast<const uint8_t*>(&w);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = q8_value(b[i], fmt) * scale;
+  } else if (fmt == kFmtF16) {
+    const __half* h = reinterpret_cast<const __half*>(&w);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __half2float(h[i]);
+  } else {
+    const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[2 * i] = __uint_as_float(u[i] << 16);
+      v[2 * i + 1] = __uint_as_float(u[i] & 0xffff0000u);
+    }
+  }
+}
+
+__device__ __forceinline__ uint32_t pack_f16x2(float a, float b) {
+  __half2 v = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {

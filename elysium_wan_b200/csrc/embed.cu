@@ -2,8 +2,9 @@
 //
 // Reference op: Embed (src/wantrain/model/gpt.py:320-338): x = wte[idx] +
 // wpe[pos], cast to the compute dtype, then the boundary narrowing. Forward
-// reads the fp32 master tables directly and writes either bf16 or the fp8
-// e4m3 1x128 boundary format (the quantisation is this kernel's epilogue).
+// reads the fp32 master tables directly and writes the boundary format: bf16,
+// fp16, or fp8 (e4m3 / e5m2) with 1x128 scales (the quantisation is this
+// kernel's epilogue).
 //
 // Backward without atomics: one CTA ranks every position by (token, position),
 // so equal tokens form runs in position order; a second kernel gives each run
@@ -17,8 +18,7 @@ namespace {
 
 __global__ void __launch_bounds__(128)
     embed_fwd_kernel(const int64_t* __restrict__ idx, const float* __restrict__ wte,
-                     const float* __restrict__ wpe, int S, int d,
-                     __nv_bfloat16* __restrict__ out_bf16, uint8_t* __restrict__ out_q8,
+                     const float* __restrict__ wpe, int S, int d, void* __restrict__ out, int fmt,
                      float* __restrict__ out_scale) {
   const int t = blockIdx.x;
   const int64_t tok = idx[t];
@@ -31,35 +31,35 @@ __global__ void __launch_bounds__(128)
     const bool ok = c < d;
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[i] = ok ? er[c + i] + (pr != nullptr ? pr[c + i] : 0.f) : 0.f;
-    if (out_q8 != nullptr) {
+    if (fmt_q8(fmt)) {
       // 16 consecutive threads cover one 128-column block.
       float amax = 0.f;
 #pragma unroll
       for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
 #pragma unroll
       for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-      const float scale = e4m3_block_scale(amax);
+      const float scale = q8_block_scale(amax, fmt);
       const float inv = 1.0f / scale;
       if (ok) {
         uint32_t w[2];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(
-              make_float2(v[4 * h] * inv, v[4 * h + 1] * inv), __NV_SATFINITE, __NV_E4M3);
-          const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(
-              make_float2(v[4 * h + 2] * inv, v[4 * h + 3] * inv), __NV_SATFINITE, __NV_E4M3);
-          w[h] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
-        }
-        *reinterpret_cast<uint2*>(out_q8 + static_cast<size_t>(t) * d + c) = make_uint2(w[0], w[1]);
+        for (int h = 0; h < 2; ++h)
+          w[h] = q8x2(v[4 * h] * inv, v[4 * h + 1] * inv, fmt) |
+                 (q8x2(v[4 * h + 2] * inv, v[4 * h + 3] * inv, fmt) << 16);
+        *reinterpret_cast<uint2*>(static_cast<uint8_t*>(out) + static_cast<size_t>(t) * d + c) =
+            make_uint2(w[0], w[1]);
         if ((threadIdx.x & 15) == 0) out_scale[static_cast<size_t>(t) * (d / 128) + c / 128] = scale;
       }
     } else if (ok) {
       uint4 w;
-      w.x = pack_bf16x2(v[0], v[1]);
-      w.y = pack_bf16x2(v[2], v[3]);
-      w.z = pack_bf16x2(v[4], v[5]);
-      w.w = pack_bf16x2(v[6], v[7]);
-      *reinterpret_cast<uint4*>(out_bf16 + static_cast<size_t>(t) * d + c) = w;
+      if (fmt == kFmtF16) {
+        w = make_uint4(pack_f16x2(v[0], v[1]), pack_f16x2(v[2], v[3]), pack_f16x2(v[4], v[5]),
+                       pack_f16x2(v[6], v[7]));
+      } else {
+        w = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
+                       pack_bf16x2(v[6], v[7]));
+      }
+      *reinterpret_cast<uint4*>(static_cast<uint8_t*>(out) + (static_cast<size_t>(t) * d + c) * 2) = w;
     }
   }
 }
@@ -135,8 +135,10 @@ __global__ void __launch_bounds__(256)
 }  // namespace
 
 int embed_fwd(const EmbedArgs& a, cudaStream_t stream) {
-  if (a.d % 8 || (a.out_q8 && a.d % 128) || a.T % a.S) return 1;
-  embed_fwd_kernel<<<a.T, 128, 0, stream>>>(a.idx, a.wte, a.wpe, a.S, a.d, a.out_bf16, a.out_q8,
+  if (a.d % 8 || (fmt_q8(a.out_fmt) && (a.d % 128 || a.out_scale == nullptr)) || a.T % a.S ||
+      a.out_fmt < kFmtBf16 || a.out_fmt > kFmtF16)
+    return 1;
+  embed_fwd_kernel<<<a.T, 128, 0, stream>>>(a.idx, a.wte, a.wpe, a.S, a.d, a.out, a.out_fmt,
                                             a.out_scale);
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }

@@ -87,16 +87,16 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb
 
 __device__ __forceinline__ float ld_bf16(const __nv_bfloat16* p) { return __bfloat162float(*p); }
 
-// Residual value (bf16, or fp8 e4m3 with a 1x128 block scale) at (row, col).
+// Residual value (boundary format resid_fmt: bf16, fp16, or fp8 with a 1x128
+// block scale) at (row, col).
 __device__ __forceinline__ float resid_at(const GemmEpilogue& ep, int row, int col) {
-  if (ep.resid_fp8) {
-    const __nv_fp8_e4m3 q =
-        reinterpret_cast<const __nv_fp8_e4m3*>(ep.resid)[static_cast<size_t>(row) * ep.ldr + col];
+  const size_t i = static_cast<size_t>(row) * ep.ldr + col;
+  if (fmt_q8(ep.resid_fmt)) {
     const float s = ep.resid_scale[static_cast<size_t>(row) * ep.ld_resid_scale + (col >> 7)];
-    return static_cast<float>(q) * s;
+    return q8_value(reinterpret_cast<const uint8_t*>(ep.resid)[i], ep.resid_fmt) * s;
   }
-  return ld_bf16(reinterpret_cast<const __nv_bfloat16*>(ep.resid) +
-                 static_cast<size_t>(row) * ep.ldr + col);
+  if (ep.resid_fmt == kFmtF16) return __half2float(reinterpret_cast<const __half*>(ep.resid)[i]);
+  return ld_bf16(reinterpret_cast<const __nv_bfloat16*>(ep.resid) + i);
 }
 
 // Load 32 consecutive bf16 values of one row as fp32; vectorised (4 x 16 B)
@@ -120,39 +120,55 @@ __device__ __forceinline__ void load_bf16_32(const __nv_bfloat16* src, float* f,
   }
 }
 
-// Residual values at (row, col0 .. col0 + 31) as fp32 (bf16, or e4m3 with its
-// 1x128 block scale; a 32-column chunk never straddles a scale block).
+// Residual values at (row, col0 .. col0 + 31) as fp32 (any boundary format; a
+// 32-column chunk never straddles an fp8 scale block).
 __device__ __forceinline__ void resid_32(const GemmEpilogue& ep, int row, int col0, float* f,
                                          int valid) {
-  if (ep.resid_fp8) {
-    const uint8_t* src =
-        reinterpret_cast<const uint8_t*>(ep.resid) + static_cast<size_t>(row) * ep.ldr + col0;
-    const float s = ep.resid_scale[static_cast<size_t>(row) * ep.ld_resid_scale + (col0 >> 7)];
-    if (valid >= 32 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
-      const uint4* s4 = reinterpret_cast<const uint4*>(src);
+  const int fmt = ep.resid_fmt;
+  if (fmt == kFmtBf16) {
+    load_bf16_32(reinterpret_cast<const __nv_bfloat16*>(ep.resid) + static_cast<size_t>(row) * ep.ldr +
+                     col0,
+                 f, valid);
+    return;
+  }
+  const int eb = fmt_bytes(fmt);
+  const uint8_t* src =
+      reinterpret_cast<const uint8_t*>(ep.resid) + (static_cast<size_t>(row) * ep.ldr + col0) * eb;
+  if (valid >= 32 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+    const float s = fmt_q8(fmt)
+                        ? ep.resid_scale[static_cast<size_t>(row) * ep.ld_resid_scale + (col0 >> 7)]
+                        : 1.f;
+    const uint4* s4 = reinterpret_cast<const uint4*>(src);
+    if (eb == 1) {
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
         const uint4 w = __ldg(s4 + j);
-        const uint32_t u[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-        for (int h = 0; h < 4; ++h) {
-#pragma unroll
-          for (int b = 0; b < 4; ++b) {
-            __nv_fp8_e4m3 q;
-            q.__x = static_cast<__nv_fp8_storage_t>((u[h] >> (8 * b)) & 0xffu);
-            f[16 * j + 4 * h + b] = static_cast<float>(q) * s;
-          }
-        }
+        unpack8_fmt(make_uint4(w.x, w.y, 0u, 0u), fmt, s, f + 16 * j);
+        unpack8_fmt(make_uint4(w.z, w.w, 0u, 0u), fmt, s, f + 16 * j + 8);
       }
     } else {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) f[i] = (i < valid) ? resid_at(ep, row, col0 + i) : 0.f;
+      for (int j = 0; j < 4; ++j) unpack8_fmt(__ldg(s4 + j), fmt, s, f + 8 * j);
     }
-    return;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) f[i] = (i < valid) ? resid_at(ep, row, col0 + i) : 0.f;
   }
-  load_bf16_32(reinterpret_cast<const __nv_bfloat16*>(ep.resid) + static_cast<size_t>(row) * ep.ldr +
-                   col0,
-               f, valid);
+}
+
+// Store 32 consecutive fp16 values of one row (the fp16 boundary format).
+__device__ __forceinline__ void store_f16_32(__half* dst, const float* f, int valid) {
+  if (valid >= 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      d4[j] = make_uint4(pack_f16x2(f[8 * j + 0], f[8 * j + 1]), pack_f16x2(f[8 * j + 2], f[8 * j + 3]),
+                         pack_f16x2(f[8 * j + 4], f[8 * j + 5]), pack_f16x2(f[8 * j + 6], f[8 * j + 7]));
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (i < valid) dst[i] = __float2half_rn(f[i]);
+  }
 }
 
 // Store 32 consecutive bf16 values of one row; vectorised when the whole chunk
@@ -311,8 +327,9 @@ __device__ __forceinline__ void epilogue_tile_regs(const AccSrc& acc, int gm, in
       reinterpret_cast<float2*>(ep.lse_part)[static_cast<size_t>(gm) * ep.ld_part + nbase / BN] =
           make_float2(mx, sum);
   } else if constexpr (EPI == kEpiResidQ8) {
-    // fp8 e4m3 with one power-of-two scale per 128 columns of a row, in two
-    // passes over TMEM (amax, then quantise) so no 128-value array is held.
+    // fp8 (e4m3 or e5m2, out_fmt) with one power-of-two scale per 128 columns
+    // of a row, in two passes over TMEM (amax, then quantise) so no 128-value
+    // array is held.
     const int nblk = ep.ld_scale_out;
 #pragma unroll 1
     for (int c = 0; c < BN; c += 128) {
@@ -333,7 +350,7 @@ __device__ __forceinline__ void epilogue_tile_regs(const AccSrc& acc, int gm, in
           }
         }
       }
-      const float scale = e4m3_block_scale(amax);
+      const float scale = q8_block_scale(amax, ep.out_fmt);
       const float inv = 1.0f / scale;  // exact: scale is a power of two
 #pragma unroll 1
       for (int j = 0; j < 4; ++j) {
@@ -353,11 +370,7 @@ __device__ __forceinline__ void epilogue_tile_regs(const AccSrc& acc, int gm, in
               const float b = ep.bias ? ep.bias[n] : 0.f;
               y[e] = (r[i] + (v[i] + b)) * inv;
             }
-            const __nv_fp8x2_storage_t lo =
-                __nv_cvt_float2_to_fp8x2(make_float2(y[0], y[1]), __NV_SATFINITE, __NV_E4M3);
-            const __nv_fp8x2_storage_t hi =
-                __nv_cvt_float2_to_fp8x2(make_float2(y[2], y[3]), __NV_SATFINITE, __NV_E4M3);
-            w[h] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+            w[h] = q8x2(y[0], y[1], ep.out_fmt) | (q8x2(y[2], y[3], ep.out_fmt) << 16);
           }
           uint4* d4 = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(ep.out) +
                                                static_cast<size_t>(gm) * ep.ldo + n0 + 32 * j);
@@ -430,6 +443,11 @@ __device__ __forceinline__ void epilogue_tile_regs(const AccSrc& acc, int gm, in
         resid_32(ep, gm, n0, r, valid);
 #pragma unroll
         for (int i = 0; i < 32; ++i) f[i] = r[i] + f[i];
+        if (ep.out_fmt == kFmtF16) {
+          store_f16_32(reinterpret_cast<__half*>(ep.out) + static_cast<size_t>(gm) * ep.ldo + n0, f,
+                       valid);
+          continue;
+        }
       }
       __nv_bfloat16* dst =
           reinterpret_cast<__nv_bfloat16*>(ep.out) + static_cast<size_t>(gm) * ep.ldo + n0;
@@ -776,18 +794,6 @@ struct PairCfg {
   static_assert(SMEM <= 232448, "shared memory over the 227 KB per-CTA limit");
   static_assert(BN == 128 || BN == 192 || BN == 256, "pair tiles are 256 x {128, 192, 256}");
 };
-
-__device__ __forceinline__ uint32_t cluster_id_x() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
-  return r;
-}
-
-__device__ __forceinline__ uint32_t num_clusters_x() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
-  return r;
-}
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
@@ -1421,7 +1427,13 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
   if (g.K2 > 0 && ((reinterpret_cast<uintptr_t>(g.a2) & 15) ||
                    (reinterpret_cast<uintptr_t>(g.b2) & 15) || (g.lda2 % 8) || (g.ldb2 % 8)))
     return kGemmErrAlign;
-  if (g.ep.kind == kEpiResidQ8 && (g.N % 128 || g.ep.ldo % 16)) return kGemmErrShape;
+  if (g.ep.kind == kEpiResidQ8 && (g.N % 128 || g.ep.ldo % 16 || !fmt_q8(g.ep.out_fmt)))
+    return kGemmErrShape;
+  if (g.ep.kind == kEpiResid && g.ep.out_fmt != kFmtBf16 && g.ep.out_fmt != kFmtF16) return kGemmErrShape;
+  if ((g.ep.kind == kEpiResid || g.ep.kind == kEpiResidQ8) &&
+      (g.ep.resid_fmt < kFmtBf16 || g.ep.resid_fmt > kFmtF16 ||
+       (fmt_q8(g.ep.resid_fmt) && g.ep.resid_scale == nullptr)))
+    return kGemmErrShape;
   if (reinterpret_cast<uintptr_t>(g.ep.out) & 15) return kGemmErrAlign;
   if ((g.ep.kind == kEpiBf16 && g.ep.ldo % 8) ||
       ((g.ep.kind == kEpiF32 || g.ep.kind == kEpiAccF32) && g.ep.ldo % 4))

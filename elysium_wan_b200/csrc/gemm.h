@@ -2,6 +2,8 @@
 // headers, so the launcher can be reached from any host code.
 #pragma once
 
+#include "boundary.h"
+
 #include <cuda_runtime.h>
 
 namespace ewb {
@@ -9,8 +11,8 @@ namespace ewb {
 enum GemmEpilogueKind : int {
   kEpiBf16 = 0,     // out bf16 = acc (+ bias)
   kEpiGelu = 1,     // aux bf16 = acc + bias; out bf16 = gelu(aux)
-  kEpiResid = 2,    // out bf16 = resid + acc (+ bias)            (resid bf16 or fp8+scale)
-  kEpiResidQ8 = 3,  // out e4m3 + 1x128 scales = quant(resid + acc (+ bias))
+  kEpiResid = 2,    // out bf16 / fp16 (out_fmt) = resid + acc (+ bias)  (resid: any boundary fmt)
+  kEpiResidQ8 = 3,  // out e4m3 / e5m2 (out_fmt) + 1x128 scales = quant(resid + acc (+ bias))
   kEpiAccF32 = 4,   // out f32 = (beta != 0 ? out : 0) + acc     (ordered gradient fold)
   kEpiDGelu = 5,    // out bf16 = acc * gelu'(aux)
   kEpiF32 = 6,      // out f32 = acc (+ bias)
@@ -47,10 +49,11 @@ struct GemmEpilogue {
   void* out;
   int ldo;
   const float* bias;  // fp32 [N] or null
-  const void* resid;  // bf16 or e4m3 [M][ldr]
+  const void* resid;  // [M][ldr] in boundary format resid_fmt (BoundaryFmt, common.cuh)
   int ldr;
-  int resid_fp8;
-  const float* resid_scale;  // [M][ld_resid_scale] when resid_fp8
+  int resid_fmt;
+  const float* resid_scale;  // [M][ld_resid_scale] when resid_fmt is an fp8 format
+  int out_fmt;  // kEpiResid: 0 bf16 / 3 fp16; kEpiResidQ8: 1 e4m3 / 2 e5m2
   int ld_resid_scale;
   void* aux;  // bf16 [M][ldaux]
   int ldaux;

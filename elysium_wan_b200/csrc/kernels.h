@@ -4,6 +4,8 @@
 // error.
 #pragma once
 
+#include "boundary.h"
+
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -12,9 +14,9 @@ namespace ewb {
 
 // ---------------------------------------------------------------- LayerNorm
 struct LnArgs {
-  const void* x;  // bf16 [rows][ldx] or e4m3 [rows][ldx]
-  const float* x_scale;  // e4m3 block scales [rows][ldxs]
-  int x_fp8, ldx, ldxs;
+  const void* x;  // [rows][ldx] in boundary format x_fmt (BoundaryFmt)
+  const float* x_scale;  // fp8 block scales [rows][ldxs]
+  int x_fmt, ldx, ldxs;
   const float* gamma;
   const float* beta;
   __nv_bfloat16* y;
@@ -32,7 +34,7 @@ struct LnBwdArgs {
   int lddy;
   const void* x;
   const float* x_scale;
-  int x_fp8, ldx, ldxs;
+  int x_fmt, ldx, ldxs;
   const float* mean;
   const float* rstd;
   const float* gamma;
@@ -116,8 +118,8 @@ struct EmbedArgs {
   const float* wte;  // [V][d] fp32 master
   const float* wpe;  // [S][d]
   int T, S, d;
-  __nv_bfloat16* out_bf16;  // either bf16 out...
-  uint8_t* out_q8;  // ...or e4m3 + 1x128 scales
+  void* out;  // [T][d] in boundary format out_fmt (bf16, fp16, or fp8 + 1x128 scales)
+  int out_fmt;
   float* out_scale;
 };
 int embed_fwd(const EmbedArgs& a, cudaStream_t stream);
@@ -150,11 +152,12 @@ int adamw_step(const AdamWArgs& a, cudaStream_t stream);
 int colsum_bf16(const __nv_bfloat16* x, int T, int N, int ld, float* part, float* grad,
                 int accumulate, cudaStream_t stream);
 int colsum_part_rows(int T);
-// e4m3 with 1x128 power-of-two scales, standalone (tests, boundary tooling).
-int quant_e4m3_rows(const __nv_bfloat16* x, int T, int d, uint8_t* q, float* scale,
+// fp8 (fmt kFmtE4m3 / kFmtE5m2) with 1x128 power-of-two scales, standalone
+// (tests, boundary tooling).
+int quant_q8_rows(const __nv_bfloat16* x, int T, int d, int fmt, uint8_t* q, float* scale,
+                  cudaStream_t stream);
+int dequant_q8_rows(const uint8_t* q, const float* scale, int T, int d, int fmt, __nv_bfloat16* y,
                     cudaStream_t stream);
-int dequant_e4m3_rows(const uint8_t* q, const float* scale, int T, int d, __nv_bfloat16* y,
-                      cudaStream_t stream);
 int cast_f32_bf16(const float* x, __nv_bfloat16* y, int64_t n, cudaStream_t stream);
 // One bounded wait (mode 0: mbarrier phase, 1: global flag) with a caller
 // limit; completes only if `release`. out[2]: {completed, waited ns}.

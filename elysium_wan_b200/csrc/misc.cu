@@ -1,5 +1,5 @@
 // Small deterministic helpers: bias-gradient column sums, standalone fp8
-// e4m3 1x128 quantise / dequantise, fp32 -> bf16 cast.
+// (e4m3 / e5m2) 1x128 quantise / dequantise, fp32 -> bf16 cast.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -31,7 +31,7 @@ __global__ void __launch_bounds__(256)
 }
 
 // One warp per 128-column block of a row.
-__global__ void quant_kernel(const __nv_bfloat16* __restrict__ x, int T, int d,
+__global__ void quant_kernel(const __nv_bfloat16* __restrict__ x, int T, int d, int fmt,
                              uint8_t* __restrict__ q, float* __restrict__ scale) {
   const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int l = threadIdx.x & 31;
@@ -45,26 +45,20 @@ __global__ void quant_kernel(const __nv_bfloat16* __restrict__ x, int T, int d,
   float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  const float s = e4m3_block_scale(amax);
+  const float s = q8_block_scale(amax, fmt);
   const float inv = 1.0f / s;
-  const __nv_fp8x2_storage_t lo =
-      __nv_cvt_float2_to_fp8x2(make_float2(v[0] * inv, v[1] * inv), __NV_SATFINITE, __NV_E4M3);
-  const __nv_fp8x2_storage_t hi =
-      __nv_cvt_float2_to_fp8x2(make_float2(v[2] * inv, v[3] * inv), __NV_SATFINITE, __NV_E4M3);
   *reinterpret_cast<uint32_t*>(q + static_cast<size_t>(row) * d + blk * 128 + 4 * l) =
-      static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+      q8x2(v[0] * inv, v[1] * inv, fmt) | (q8x2(v[2] * inv, v[3] * inv, fmt) << 16);
   if (l == 0) scale[static_cast<size_t>(row) * nb + blk] = s;
 }
 
 __global__ void dequant_kernel(const uint8_t* __restrict__ q, const float* __restrict__ scale,
-                               int64_t n, int d, __nv_bfloat16* __restrict__ y) {
+                               int64_t n, int d, int fmt, __nv_bfloat16* __restrict__ y) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const int64_t row = i / d;
   const int col = static_cast<int>(i % d);
-  __nv_fp8_e4m3 v;
-  v.__x = q[i];
-  y[i] = __float2bfloat16_rn(static_cast<float>(v) * scale[row * (d / 128) + col / 128]);
+  y[i] = __float2bfloat16_rn(q8_value(q[i], fmt) * scale[row * (d / 128) + col / 128]);
 }
 
 __global__ void cast_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, int64_t n) {
@@ -115,19 +109,19 @@ int colsum_bf16(const __nv_bfloat16* x, int T, int N, int ld, float* part, float
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
 
-int quant_e4m3_rows(const __nv_bfloat16* x, int T, int d, uint8_t* q, float* scale,
-                    cudaStream_t stream) {
-  if (d % 128) return 1;
+int quant_q8_rows(const __nv_bfloat16* x, int T, int d, int fmt, uint8_t* q, float* scale,
+                  cudaStream_t stream) {
+  if (d % 128 || !fmt_q8(fmt)) return 1;
   const int warps = T * (d / 128);
-  quant_kernel<<<(warps * 32 + 255) / 256, 256, 0, stream>>>(x, T, d, q, scale);
+  quant_kernel<<<(warps * 32 + 255) / 256, 256, 0, stream>>>(x, T, d, fmt, q, scale);
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
 
-int dequant_e4m3_rows(const uint8_t* q, const float* scale, int T, int d, __nv_bfloat16* y,
-                      cudaStream_t stream) {
-  if (d % 128) return 1;
+int dequant_q8_rows(const uint8_t* q, const float* scale, int T, int d, int fmt, __nv_bfloat16* y,
+                    cudaStream_t stream) {
+  if (d % 128 || !fmt_q8(fmt)) return 1;
   const int64_t n = static_cast<int64_t>(T) * d;
-  dequant_kernel<<<static_cast<int>((n + 255) / 256), 256, 0, stream>>>(q, scale, n, d, y);
+  dequant_kernel<<<static_cast<int>((n + 255) / 256), 256, 0, stream>>>(q, scale, n, d, fmt, y);
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
 

@@ -49,10 +49,13 @@ enum {
 
 // dx = LayerNorm backward of dy (+ dres when non-null); dgamma / dbeta get the
 // row sums of dy * xhat and dy (added to their contents when accumulate != 0).
-// x is bf16 (x_fp8 = 0) or e4m3 with one fp32 scale per 128 columns (x_fp8 = 1,
-// scales in x_scale with row stride ldxs). dy, dres and dx are bf16. mean and
+// x_fp8 names x's format: 0 bf16, 1 e4m3 or 2 e5m2 with one fp32 scale per
+// 128 columns (scales in x_scale with row stride ldxs), 3 fp16. dy, dres and dx are bf16. mean and
 // rstd are the forward's per-row statistics. Leading dimensions are in
 // elements. stream is a cudaStream_t (null for the legacy default stream).
+// The scratch address is looked up once per device and cached; the cache does
+// not survive cudaDeviceReset (call this entry point only in a context that
+// has not been reset since its first call).
 int ewb_layernorm_bwd_noalloc(const void* dy, int lddy, const void* x, const float* x_scale,
                               int x_fp8, int ldx, int ldxs, const float* mean, const float* rstd,
                               const float* gamma, const void* dres, int lddres, void* dx, int lddx,

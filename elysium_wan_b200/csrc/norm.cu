@@ -4,9 +4,10 @@
 // Forward: one CTA of 128 threads per row; the row is held in registers as
 // fp32 (8 contiguous elements per thread per 1024-column slice), mean and
 // variance are two-pass over the registers with a fixed reduction tree, so the
-// result is deterministic. The input is either bf16 or the fp8 e4m3 boundary
-// format with one power-of-two scale per 128 columns: the dequantisation is the
-// prologue of this kernel (the next stage's first op after a stage cut).
+// result is deterministic. The input is any boundary format: bf16, fp16, or
+// fp8 (e4m3 / e5m2) with one power-of-two scale per 128 columns; the
+// conversion is the prologue of this kernel (the next stage's first op after a
+// stage cut).
 //
 // Backward: dx with one warp per row (warp-shuffle row sums, no block
 // barrier); dgamma/dbeta as per-chunk column partials (each thread owns 8
@@ -31,27 +32,18 @@ __device__ __forceinline__ float block_sum_128(float v, float* red) {
   return (red[0] + red[1]) + (red[2] + red[3]);
 }
 
-// Load 8 contiguous input elements (bf16 or e4m3 + block scale) as fp32.
-__device__ __forceinline__ void load8(const void* x, const float* xs, int x_fp8, int ld, int lds,
+// Load 8 contiguous input elements of a boundary format (bf16, fp16, or
+// e4m3 / e5m2 with a 1x128 block scale) as fp32.
+__device__ __forceinline__ void load8(const void* x, const float* xs, int fmt, int ld, int lds,
                                       int row, int col, float* v) {
-  if (x_fp8) {
+  if (fmt_q8(fmt)) {
     const uint8_t* p = reinterpret_cast<const uint8_t*>(x) + static_cast<size_t>(row) * ld + col;
     const uint2 raw = *reinterpret_cast<const uint2*>(p);
     const float s = xs[static_cast<size_t>(row) * lds + (col >> 7)];
-    const uint8_t* b = reinterpret_cast<const uint8_t*>(&raw);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      __nv_fp8_e4m3 q;
-      q.__x = b[i];
-      v[i] = static_cast<float>(q) * s;
-    }
+    unpack8_fmt(make_uint4(raw.x, raw.y, 0u, 0u), fmt, s, v);
   } else {
-    const __nv_bfloat16* p =
-        reinterpret_cast<const __nv_bfloat16*>(x) + static_cast<size_t>(row) * ld + col;
-    const uint4 raw = *reinterpret_cast<const uint4*>(p);
-    const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&raw);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = __bfloat162float(b[i]);
+    const uint8_t* p = reinterpret_cast<const uint8_t*>(x) + (static_cast<size_t>(row) * ld + col) * 2;
+    unpack8_fmt(*reinterpret_cast<const uint4*>(p), fmt, 1.f, v);
   }
 }
 
@@ -74,7 +66,7 @@ __device__ __forceinline__ void store8_bf16(__nv_bfloat16* p, const float* v) {
 
 template <int S, bool RMS>
 __global__ void __launch_bounds__(kLnThreads)
-    layernorm_fwd_kernel(const void* __restrict__ x, const float* __restrict__ xs, int x_fp8,
+    layernorm_fwd_kernel(const void* __restrict__ x, const float* __restrict__ xs, int x_fmt,
                          int ldx, int ldxs, const float* __restrict__ gamma,
                          const float* __restrict__ beta, __nv_bfloat16* __restrict__ y, int ldy,
                          float* __restrict__ mean_out, float* __restrict__ rstd_out, int d,
@@ -87,7 +79,7 @@ __global__ void __launch_bounds__(kLnThreads)
   for (int j = 0; j < S; ++j) {
     const int col = j * 1024 + threadIdx.x * 8;
     if (col < d) {
-      load8(x, xs, x_fp8, ldx, ldxs, row, col, v[j]);
+      load8(x, xs, x_fmt, ldx, ldxs, row, col, v[j]);
 #pragma unroll
       for (int i = 0; i < 8; ++i) s += v[j][i];
     }
@@ -138,28 +130,15 @@ __global__ void __launch_bounds__(kLnThreads)
 // row may have (d <= 512 NS).
 constexpr int kLnBwdWarps = 8;
 
-__device__ __forceinline__ void unpack8(const uint4& w, const float* xs_row, int x_fp8, int col,
+__device__ __forceinline__ void unpack8(const uint4& w, const float* xs_row, int fmt, int col,
                                         float* v) {
-  if (x_fp8) {
-    const float s = xs_row[col >> 7];
-    const uint8_t* b = reinterpret_cast<const uint8_t*>(&w);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      __nv_fp8_e4m3 q;
-      q.__x = b[i];
-      v[i] = static_cast<float>(q) * s;
-    }
-  } else {
-    const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&w);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = __bfloat162float(b[i]);
-  }
+  unpack8_fmt(w, fmt, fmt_q8(fmt) ? xs_row[col >> 7] : 1.f, v);
 }
 
 template <int NS, bool RMS>
 __global__ void __launch_bounds__(kLnBwdWarps * 32)
     layernorm_bwd_dx_kernel(const __nv_bfloat16* __restrict__ dy, int lddy, const void* __restrict__ x,
-                            const float* __restrict__ xs, int x_fp8, int ldx, int ldxs,
+                            const float* __restrict__ xs, int x_fmt, int ldx, int ldxs,
                             const float* __restrict__ mean, const float* __restrict__ rstd,
                             const float* __restrict__ gamma, const __nv_bfloat16* __restrict__ dres,
                             int lddres, __nv_bfloat16* __restrict__ dx, int lddx, int rows, int d) {
@@ -172,13 +151,13 @@ __global__ void __launch_bounds__(kLnBwdWarps * 32)
   const bool live = row < rows;
   uint4 xw[NS], dw[NS];
   const uint8_t* xrow = reinterpret_cast<const uint8_t*>(x) +
-                        static_cast<size_t>(live ? row : 0) * ldx * (x_fp8 ? 1 : 2);
+                        static_cast<size_t>(live ? row : 0) * ldx * fmt_bytes(x_fmt);
   const __nv_bfloat16* dyrow = dy + static_cast<size_t>(live ? row : 0) * lddy;
 #pragma unroll
   for (int j = 0; j < NS; ++j) {
     const int col = j * 512 + t * 8;
     if (live && col < d) {
-      if (x_fp8) {
+      if (fmt_q8(x_fmt)) {
         const uint2 r = __ldg(reinterpret_cast<const uint2*>(xrow + col));
         xw[j] = make_uint4(r.x, r.y, 0u, 0u);
       } else {
@@ -187,7 +166,7 @@ __global__ void __launch_bounds__(kLnBwdWarps * 32)
       dw[j] = __ldg(reinterpret_cast<const uint4*>(dyrow + col));
     }
   }
-  const float* xs_row = (x_fp8 && live) ? xs + static_cast<size_t>(row) * ldxs : nullptr;
+  const float* xs_row = (fmt_q8(x_fmt) && live) ? xs + static_cast<size_t>(row) * ldxs : nullptr;
   const float mu = (RMS || !live) ? 0.f : mean[row];
   const float rs = live ? rstd[row] : 0.f;
   float s1 = 0.f, s2 = 0.f;
@@ -196,7 +175,7 @@ __global__ void __launch_bounds__(kLnBwdWarps * 32)
     const int col = j * 512 + t * 8;
     if (live && col < d) {
       float xv[8], dv[8], gm[8];
-      unpack8(xw[j], xs_row, x_fp8, col, xv);
+      unpack8(xw[j], xs_row, x_fmt, col, xv);
       unpack8(dw[j], nullptr, 0, col, dv);
       load8_f32(gamma + col, gm);
 #pragma unroll
@@ -228,7 +207,7 @@ __global__ void __launch_bounds__(kLnBwdWarps * 32)
     const int col = j * 512 + t * 8;
     if (col < d) {
       float xv[8], dv[8], gm[8], o[8];
-      unpack8(xw[j], xs_row, x_fp8, col, xv);
+      unpack8(xw[j], xs_row, x_fmt, col, xv);
       unpack8(dw[j], nullptr, 0, col, dv);
       load8_f32(gamma + col, gm);
 #pragma unroll
@@ -253,7 +232,7 @@ __global__ void __launch_bounds__(kLnBwdWarps * 32)
 template <bool RMS>
 __global__ void __launch_bounds__(kLnThreads)
     layernorm_bwd_param_kernel(const __nv_bfloat16* __restrict__ dy, int lddy,
-                               const void* __restrict__ x, const float* __restrict__ xs, int x_fp8,
+                               const void* __restrict__ x, const float* __restrict__ xs, int x_fmt,
                                int ldx, int ldxs, const float* __restrict__ mean,
                                const float* __restrict__ rstd, float* __restrict__ part_g,
                                float* __restrict__ part_b, int rows, int d, int rows_per_chunk) {
@@ -270,7 +249,7 @@ __global__ void __launch_bounds__(kLnThreads)
   }
   // eight rows' raw 16-byte loads in flight per thread, then their sums in
   // row order
-  const size_t xb = x_fp8 ? 1 : 2;
+  const size_t xb = fmt_bytes(x_fmt);
   for (int rb = r0; rb < r1; rb += 8) {
     uint4 xw[8], dw[8];
     float mu[8], rs[8];
@@ -279,7 +258,7 @@ __global__ void __launch_bounds__(kLnThreads)
       const int row = rb + k;
       if (row < r1) {
         const uint8_t* xp = reinterpret_cast<const uint8_t*>(x) + (static_cast<size_t>(row) * ldx + col) * xb;
-        if (x_fp8) {
+        if (fmt_q8(x_fmt)) {
           const uint2 r = __ldg(reinterpret_cast<const uint2*>(xp));
           xw[k] = make_uint4(r.x, r.y, 0u, 0u);
         } else {
@@ -295,7 +274,7 @@ __global__ void __launch_bounds__(kLnThreads)
       const int row = rb + k;
       if (row < r1) {
         float xv[8], dv[8];
-        unpack8(xw[k], x_fp8 ? xs + static_cast<size_t>(row) * ldxs : nullptr, x_fp8, col, xv);
+        unpack8(xw[k], fmt_q8(x_fmt) ? xs + static_cast<size_t>(row) * ldxs : nullptr, x_fmt, col, xv);
         unpack8(dw[k], nullptr, 0, col, dv);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -342,14 +321,15 @@ __global__ void __launch_bounds__(kFoldWarps * 32)
 }  // namespace
 
 int layernorm_fwd(const LnArgs& a, cudaStream_t stream) {
-  if (a.d % 8 || a.d > 1024 * kLnMaxSlices || (a.x_fp8 && a.d % 128)) return 1;
+  if (a.d % 8 || a.d > 1024 * kLnMaxSlices || (fmt_q8(a.x_fmt) && a.d % 128) ||
+      a.x_fmt < kFmtBf16 || a.x_fmt > kFmtF16) return 1;
   const int S = (a.d + 1023) / 1024;
 #define EWB_LN_FWD(SS)                                                                       \
   (a.rms ? layernorm_fwd_kernel<SS, true><<<a.rows, kLnThreads, 0, stream>>>(                 \
-               a.x, a.x_scale, a.x_fp8, a.ldx, a.ldxs, a.gamma, a.beta, a.y, a.ldy, a.mean,   \
+               a.x, a.x_scale, a.x_fmt, a.ldx, a.ldxs, a.gamma, a.beta, a.y, a.ldy, a.mean,   \
                a.rstd, a.d, a.eps)                                                            \
          : layernorm_fwd_kernel<SS, false><<<a.rows, kLnThreads, 0, stream>>>(                \
-               a.x, a.x_scale, a.x_fp8, a.ldx, a.ldxs, a.gamma, a.beta, a.y, a.ldy, a.mean,   \
+               a.x, a.x_scale, a.x_fmt, a.ldx, a.ldxs, a.gamma, a.beta, a.y, a.ldy, a.mean,   \
                a.rstd, a.d, a.eps))
   switch (S) {
     case 1: EWB_LN_FWD(1); break;
@@ -373,7 +353,8 @@ int layernorm_bwd_rows_per_chunk(int rows) {
 }
 
 int layernorm_bwd(const LnBwdArgs& a, cudaStream_t stream) {
-  if (a.d % 8 || a.d > 1024 * kLnMaxSlices || (a.x_fp8 && a.d % 128)) return 1;
+  if (a.d % 8 || a.d > 1024 * kLnMaxSlices || (fmt_q8(a.x_fmt) && a.d % 128) ||
+      a.x_fmt < kFmtBf16 || a.x_fmt > kFmtF16) return 1;
   const int rpc = a.rows_per_chunk;
   if (rpc < 1) return 1;
   const int chunks = (a.rows + rpc - 1) / rpc;
@@ -382,7 +363,7 @@ int layernorm_bwd(const LnBwdArgs& a, cudaStream_t stream) {
   const int ns = (a.d + 511) / 512;
 #define EWB_LN_DX(NSV, R)                                                                     \
   layernorm_bwd_dx_kernel<NSV, R><<<dx_grid, kLnBwdWarps * 32, 0, stream>>>(                   \
-      a.dy, a.lddy, a.x, a.x_scale, a.x_fp8, a.ldx, a.ldxs, a.mean, a.rstd, a.gamma, a.dres,     \
+      a.dy, a.lddy, a.x, a.x_scale, a.x_fmt, a.ldx, a.ldxs, a.mean, a.rstd, a.gamma, a.dres,     \
       a.lddres, a.dx, a.lddx, a.rows, a.d)
 #define EWB_LN_DX_NS(R)                     \
   if (ns <= 2) EWB_LN_DX(2, R);             \
@@ -395,12 +376,12 @@ int layernorm_bwd(const LnBwdArgs& a, cudaStream_t stream) {
   if (a.rms) {
     EWB_LN_DX_NS(true);
     layernorm_bwd_param_kernel<true><<<pgrid, kLnThreads, 0, stream>>>(
-        a.dy, a.lddy, a.x, a.x_scale, a.x_fp8, a.ldx, a.ldxs, a.mean, a.rstd, a.part_g, a.part_b,
+        a.dy, a.lddy, a.x, a.x_scale, a.x_fmt, a.ldx, a.ldxs, a.mean, a.rstd, a.part_g, a.part_b,
         a.rows, a.d, rpc);
   } else {
     EWB_LN_DX_NS(false);
     layernorm_bwd_param_kernel<false><<<pgrid, kLnThreads, 0, stream>>>(
-        a.dy, a.lddy, a.x, a.x_scale, a.x_fp8, a.ldx, a.ldxs, a.mean, a.rstd, a.part_g, a.part_b,
+        a.dy, a.lddy, a.x, a.x_scale, a.x_fmt, a.ldx, a.ldxs, a.mean, a.rstd, a.part_g, a.part_b,
         a.rows, a.d, rpc);
   }
 #undef EWB_LN_DX_NS
@@ -458,14 +439,15 @@ float* noalloc_scratch(int* err) {
 }  // namespace
 
 extern "C" int ewb_layernorm_bwd_noalloc(const void* dy, int lddy, const void* x,
-                                         const float* x_scale, int x_fp8, int ldx, int ldxs,
+                                         const float* x_scale, int x_fmt, int ldx, int ldxs,
                                          const float* mean, const float* rstd, const float* gamma,
                                          const void* dres, int lddres, void* dx, int lddx,
                                          float* dgamma, float* dbeta, int accumulate, int rows,
                                          int d, void* stream) {
   if (dy == nullptr || x == nullptr || mean == nullptr || rstd == nullptr || gamma == nullptr ||
       dx == nullptr || dgamma == nullptr || dbeta == nullptr || rows <= 0 || d <= 0 || d % 8 ||
-      (x_fp8 && (x_scale == nullptr || d % 128)))
+      x_fmt < ewb::kFmtBf16 || x_fmt > ewb::kFmtF16 ||
+      (ewb::fmt_q8(x_fmt) && (x_scale == nullptr || d % 128)))
     return EWB_NOALLOC_ERR_ARGUMENT;
   if (d > EWB_NOALLOC_LN_MAX_D) return EWB_NOALLOC_ERR_TOO_LARGE;
   int err = EWB_NOALLOC_OK;
@@ -476,7 +458,7 @@ extern "C" int ewb_layernorm_bwd_noalloc(const void* dy, int lddy, const void* x
   a.lddy = lddy;
   a.x = x;
   a.x_scale = x_scale;
-  a.x_fp8 = x_fp8;
+  a.x_fmt = x_fmt;
   a.ldx = ldx;
   a.ldxs = ldxs;
   a.mean = mean;

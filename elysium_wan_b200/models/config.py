@@ -16,10 +16,15 @@ import dataclasses
 import math
 from dataclasses import dataclass, field
 
-# Precision recipes (reference: src/wantrain/model/precision.py:18-162).
+# Precision recipes (reference: src/wantrain/model/precision.py:18-162; the
+# table with classification and capability gates is models/precision.py).
 COMPUTE_DTYPES = ("fp32", "bf16")
-BOUNDARY_DTYPES = ("fp32", "bf16", "fp8_e4m3_b128")
-RECIPE_BYTES = {"fp32": 4, "bf16": 2, "fp8_e4m3_b128": 1}
+BOUNDARY_DTYPES = ("fp32", "bf16", "fp16", "fp8_e5m2_b128", "fp8_e4m3_b128")
+RECIPE_BYTES = {"fp32": 4, "bf16": 2, "fp16": 2, "fp8_e5m2_b128": 1, "fp8_e4m3_b128": 1}
+# The reference's fp8 boundary names scale per token; this engine scales the
+# same formats per 1x128 block of a row (a finer scale, the layout the fused
+# GEMM epilogue writes), and reads the reference's names as these.
+BOUNDARY_ALIASES = {"fp8_e4m3": "fp8_e4m3_b128", "fp8_e5m2": "fp8_e5m2_b128"}
 
 
 @dataclass
@@ -126,9 +131,10 @@ class GPTConfig:
         return self.n_layer + 2
 
     def fp8_boundary(self) -> bool:
-        return self.boundary_dtype == "fp8_e4m3_b128"
+        return self.boundary_dtype in ("fp8_e4m3_b128", "fp8_e5m2_b128")
 
     def validate(self) -> "GPTConfig":
+        self.boundary_dtype = BOUNDARY_ALIASES.get(self.boundary_dtype, self.boundary_dtype)
         if self.compute_dtype not in COMPUTE_DTYPES:
             raise ValueError(f"compute_dtype {self.compute_dtype!r} not in {COMPUTE_DTYPES}")
         if self.boundary_dtype not in BOUNDARY_DTYPES:
@@ -160,7 +166,7 @@ class GPTConfig:
         if self.lora_rank < 0:
             raise ValueError("lora_rank must be >= 0")
         if self.fp8_boundary() and self.d_model % 128:
-            raise ValueError("fp8_e4m3_b128 boundaries need d_model % 128 == 0")
+            raise ValueError(f"{self.boundary_dtype} boundaries need d_model % 128 == 0")
         check_moe(self)
         return self
 

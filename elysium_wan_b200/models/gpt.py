@@ -14,12 +14,15 @@ gradients, which the reference also computes in B) and W is a list of GEMM
 tasks that fold dW into fp32 gradients in the order they are run.
 
 Boundary recipe: every entry boundary (the input of each block and of the
-head) carries the config's boundary dtype. With fp8_e4m3_b128 the block
-output is quantised in the epilogue of the fc2 GEMM (e4m3, one power-of-two
-scale per 128 elements of a row) and dequantised in the prologue of the next
-LayerNorm / as the residual of the next proj GEMM; gradients stay bf16 and
-pass the quantiser unchanged (straight-through). The recipe is the same at
-every boundary, so a run does not depend on where the model is cut.
+head) carries the config's boundary dtype. With an fp8 recipe
+(fp8_e4m3_b128 / fp8_e5m2_b128) the block output is quantised in the
+epilogue of the fc2 GEMM (one power-of-two scale per 128 elements of a row)
+and dequantised in the prologue of the next LayerNorm / as the residual of
+the next proj GEMM; with fp16 the same epilogue writes fp16 and the same two
+readers widen it; gradients stay in the compute dtype and pass the boundary
+unchanged (straight-through). The recipe is the same at every boundary
+(the embedding's output included), so a run does not depend on where the
+model is cut.
 """
 
 from __future__ import annotations
@@ -33,8 +36,8 @@ from .params import ParamSpec, ParamStore, init_params
 
 
 class Act:
-    """A boundary activation: a dense tensor, or an e4m3 payload with its
-    1x128 scales."""
+    """A boundary activation: a dense tensor (bf16 / fp16 on the GPU, fp32 on
+    the host path), or an fp8 payload (e4m3 / e5m2) with its 1x128 scales."""
 
     __slots__ = ("x", "scale")
 
@@ -347,9 +350,9 @@ class Embed:
         ctx["tokens"] = tokens
         wpe = self.s.p(f"{self.e}.pos.weight") if self.has_pos else None
         out = ops.embed_fwd(tokens, self.s.p(f"{self.e}.tok.weight"), wpe, c.seq_len,
-                            c.fp8_boundary(),
-                            out_dtype=torch.float32 if not tokens.is_cuda else torch.bfloat16)
-        return Act(*out) if isinstance(out, tuple) else Act(out)
+                            ops.q8_dtype(c.boundary_dtype),
+                            out_dtype=ops.act_dtype(c.boundary_dtype, tokens.is_cuda))
+        return Act(*out) if isinstance(out, tuple) else _boundary_out(c, out)
 
     def backward(self, ctx: dict, dy: torch.Tensor, wq: list):
         dwte = self.s.g(f"{self.e}.tok.weight")
@@ -360,11 +363,15 @@ class Embed:
         return None
 
 
+_HOST_ROUND = {"bf16": torch.bfloat16, "fp16": torch.float16}
+
+
 def _boundary_out(cfg, y) -> Act:
-    """The block output in the boundary dtype (bf16 rounding on the CPU
-    plumbing path when the boundary is bf16)."""
-    if not y.is_cuda and cfg.boundary_dtype == "bf16":
-        y = y.to(torch.bfloat16).float()
+    """A dense entry output in the boundary dtype: on the GPU the producing
+    kernel already wrote it; the host path keeps fp32 holding the recipe's
+    rounding (bf16 or fp16)."""
+    if not y.is_cuda and cfg.boundary_dtype in _HOST_ROUND:
+        y = y.to(_HOST_ROUND[cfg.boundary_dtype]).float()
     return Act(y)
 
 
@@ -457,12 +464,15 @@ class Block:
                             resid=x.x, resid_scale=x.scale)
         h2, m2, r2 = self._norm(x2, None, "ln2")
         ctx.update(x=x, h1=h1, m1=m1, r1=r1, qkv=qkv, o=o, lse=lse, x2=x2, h2=h2, m2=m2, r2=r2)
-        q8 = c.fp8_boundary()
+        q8 = ops.q8_dtype(c.boundary_dtype)
+        out_dt = ops.act_dtype(c.boundary_dtype, x2.is_cuda)
         if self.mlp == "moe":
             y = self.moe.forward(h2, ctx)
             out = ops.residual_add(x2, y)  # x2 + y in the compute dtype
-            if q8:
-                return Act(*ops.quant_e4m3(out))
+            if q8 is not None:
+                return Act(*ops.quant_q8(out, q8))
+            if out.is_cuda and out.dtype != out_dt:
+                out = out.to(out_dt)
             return _boundary_out(c, out)
         if self.mlp == "gelu":
             g, u = ops.linear_fwd(h2, self._w(self.up_w), self._bp(self.up_b), epi="gelu")
@@ -473,10 +483,10 @@ class Block:
             hin = ops.swiglu_fwd(gu)
             ctx.update(gu=gu, g=hin)
         bdn = self._bp([self.dn_b])
-        if q8:
-            q, sc = ops.linear_fwd(hin, s.w(self.dn_w), bdn, epi="resid_q8", resid=x2)
+        if q8 is not None:
+            q, sc = ops.linear_fwd(hin, s.w(self.dn_w), bdn, epi="resid_q8", resid=x2, q8=q8)
             return Act(q, sc)
-        y = ops.linear_fwd(hin, s.w(self.dn_w), bdn, epi="resid", resid=x2)
+        y = ops.linear_fwd(hin, s.w(self.dn_w), bdn, epi="resid", resid=x2, out_dtype=out_dt)
         return _boundary_out(c, y)
 
     def backward(self, ctx: dict, dy: torch.Tensor, wq: list) -> torch.Tensor:

@@ -23,6 +23,28 @@ import torch.nn.functional as F
 from ._ext import ext, launch_count  # noqa: F401
 
 E4M3 = torch.float8_e4m3fn
+E5M2 = torch.float8_e5m2
+# fp8 boundary formats: torch dtype, exponent offset of the 1x128 block scale
+# (scale = 2^(e - offset) with amax = f 2^e, f in [0.5, 1), so |x| / scale <
+# 2^offset stays inside the format: 256 <= 448 for e4m3, 32768 <= 57344 for
+# e5m2) and the largest finite value.
+Q8_FORMATS = {"fp8_e4m3_b128": (E4M3, 8, 448.0), "fp8_e5m2_b128": (E5M2, 15, 57344.0)}
+_Q8_BY_DTYPE = {dt: (off, mx) for dt, off, mx in Q8_FORMATS.values()}
+
+
+def q8_dtype(boundary: str):
+    """The fp8 dtype of an fp8 boundary recipe, else None."""
+    f = Q8_FORMATS.get(boundary)
+    return f[0] if f else None
+
+
+def act_dtype(boundary: str, cuda: bool):
+    """dtype of a dense boundary activation: fp16 for the fp16 recipe and bf16
+    otherwise on the GPU; fp32 (holding the recipe's rounded values) on the
+    host path. Gradients stay in the compute dtype whatever the recipe."""
+    if not cuda:
+        return torch.float32
+    return torch.float16 if boundary == "fp16" else torch.bfloat16
 
 # Epilogue kinds of the GEMM (mirrors csrc/gemm.h).
 EPI_BF16, EPI_GELU, EPI_RESID, EPI_RESID_Q8, EPI_ACC_F32, EPI_DGELU, EPI_F32 = range(7)
@@ -33,35 +55,49 @@ def _cuda(t: torch.Tensor) -> bool:
 
 
 # ----------------------------------------------------------------------------- fp8 boundary
-def e4m3_block_scale_ref(amax: torch.Tensor) -> torch.Tensor:
-    """Power-of-two scale 2^(e-8) with amax = f * 2^e, f in [0.5, 1); 1 where amax == 0."""
+def q8_block_scale_ref(amax: torch.Tensor, dtype=E4M3) -> torch.Tensor:
+    """Power-of-two scale 2^(e - offset) with amax = f * 2^e, f in [0.5, 1); 1
+    where amax == 0 (offset 8 for e4m3, 15 for e5m2)."""
+    off, _ = _Q8_BY_DTYPE[dtype]
     _, e = torch.frexp(amax)
-    s = torch.ldexp(torch.ones_like(amax), e - 8)
+    s = torch.ldexp(torch.ones_like(amax), e - off)
     return torch.where(amax > 0, s, torch.ones_like(amax))
 
 
-def quant_e4m3(x: torch.Tensor):
-    """1x128 block-scaled e4m3: returns (q [T,d] e4m3, scale [T,d/128] fp32)."""
+def e4m3_block_scale_ref(amax: torch.Tensor) -> torch.Tensor:
+    return q8_block_scale_ref(amax, E4M3)
+
+
+def quant_q8(x: torch.Tensor, dtype=E4M3):
+    """1x128 block-scaled fp8 (e4m3 or e5m2): returns (q [T,d], scale [T,d/128] fp32)."""
     T, d = x.shape
     assert d % 128 == 0, "fp8 boundary needs d_model % 128 == 0"
     if _cuda(x):
-        q = torch.empty((T, d), dtype=E4M3, device=x.device)
+        q = torch.empty((T, d), dtype=dtype, device=x.device)
         s = torch.empty((T, d // 128), dtype=torch.float32, device=x.device)
-        ext().quant_e4m3(x.contiguous(), q, s)
+        ext().quant_q8(x.to(torch.bfloat16).contiguous(), q, s)
         return q, s
+    _, mx = _Q8_BY_DTYPE[dtype]
     xf = x.float().view(T, d // 128, 128)
-    s = e4m3_block_scale_ref(xf.abs().amax(dim=2))
-    q = (xf / s[..., None]).clamp(-448, 448).to(E4M3).view(T, d)
+    s = q8_block_scale_ref(xf.abs().amax(dim=2), dtype)
+    q = (xf / s[..., None]).clamp(-mx, mx).to(dtype).view(T, d)
     return q, s
 
 
-def dequant_e4m3(q: torch.Tensor, s: torch.Tensor, dtype=torch.bfloat16) -> torch.Tensor:
+def quant_e4m3(x: torch.Tensor):
+    return quant_q8(x, E4M3)
+
+
+def dequant_q8(q: torch.Tensor, s: torch.Tensor, dtype=torch.bfloat16) -> torch.Tensor:
     T, d = q.shape
     if _cuda(q) and dtype == torch.bfloat16:
         y = torch.empty((T, d), dtype=torch.bfloat16, device=q.device)
-        ext().dequant_e4m3(q.contiguous(), s.contiguous(), y)
+        ext().dequant_q8(q.contiguous(), s.contiguous(), y)
         return y
     return (q.float().view(T, d // 128, 128) * s[..., None]).view(T, d).to(dtype)
+
+
+dequant_e4m3 = dequant_q8
 
 
 # ----------------------------------------------------------------------------- GEMM
@@ -77,16 +113,18 @@ def gemm(a, b, out, epi=EPI_BF16, *, a_mn=False, b_mn=False, bias=None, resid=No
 
 
 def _resid_value(resid, resid_scale):
-    if resid.dtype == E4M3:
-        return dequant_e4m3(resid, resid_scale, torch.float32)
+    if resid.dtype in _Q8_BY_DTYPE:
+        return dequant_q8(resid, resid_scale, torch.float32)
     return resid.float()
 
 
-def linear_fwd(x, w, bias=None, *, epi="none", resid=None, resid_scale=None, out=None):
+def linear_fwd(x, w, bias=None, *, epi="none", resid=None, resid_scale=None, out=None,
+               q8=E4M3, out_dtype=torch.bfloat16):
     """Y = X W^T (+ b) with a fused epilogue.
 
     epi: "none" -> Y; "gelu" -> (gelu(U), U) with U = XW^T+b kept for the
-    backward; "resid" -> resid + XW^T + b; "resid_q8" -> e4m3 + scales of that.
+    backward; "resid" -> resid + XW^T + b (out_dtype bf16 or fp16 on the GPU);
+    "resid_q8" -> fp8 (q8: e4m3 or e5m2) + 1x128 scales of that.
     """
     T = x.shape[0]
     N = w.shape[0]
@@ -101,10 +139,10 @@ def linear_fwd(x, w, bias=None, *, epi="none", resid=None, resid_scale=None, out
             gemm(x, w, g, EPI_GELU, bias=bias, aux=u)
             return g, u
         if epi == "resid":
-            out = out if out is not None else torch.empty((T, N), dtype=torch.bfloat16, device=dev)
+            out = out if out is not None else torch.empty((T, N), dtype=out_dtype, device=dev)
             return gemm(x, w, out, EPI_RESID, bias=bias, resid=resid, resid_scale=resid_scale)
         if epi == "resid_q8":
-            q = torch.empty((T, N), dtype=E4M3, device=dev)
+            q = torch.empty((T, N), dtype=q8, device=dev)
             s = torch.empty((T, N // 128), dtype=torch.float32, device=dev)
             gemm(x, w, q, EPI_RESID_Q8, bias=bias, resid=resid, resid_scale=resid_scale,
                  scale_out=s)
@@ -124,7 +162,7 @@ def linear_fwd(x, w, bias=None, *, epi="none", resid=None, resid_scale=None, out
     if epi == "resid":
         return _resid_value(resid, resid_scale) + y
     if epi == "resid_q8":
-        return quant_e4m3(_resid_value(resid, resid_scale) + y)
+        return quant_q8(_resid_value(resid, resid_scale) + y, q8)
     raise ValueError(epi)
 
 
@@ -436,26 +474,27 @@ def head_ce(h, w, targets, V, grad_scale):
 
 
 # ----------------------------------------------------------------------------- embedding
-def embed_fwd(idx, wte, wpe, S, fp8: bool, out_dtype=torch.bfloat16):
-    """x = wte[idx] (+ wpe[pos] when learned positions); bf16, or (e4m3,
-    scales) when fp8."""
+def embed_fwd(idx, wte, wpe, S, q8=None, out_dtype=torch.bfloat16):
+    """x = wte[idx] (+ wpe[pos] when learned positions) in a boundary format:
+    (fp8, scales) when q8 names an fp8 dtype, else a dense out_dtype tensor
+    (bf16 / fp16 on the GPU)."""
     T = idx.numel()
     d = wte.shape[1]
     if _cuda(idx):
-        if fp8:
-            q = torch.empty((T, d), dtype=E4M3, device=idx.device)
+        if q8 is not None:
+            q = torch.empty((T, d), dtype=q8, device=idx.device)
             s = torch.empty((T, d // 128), dtype=torch.float32, device=idx.device)
-            ext().embed_fwd(idx, wte, wpe, S, None, q, s)
+            ext().embed_fwd(idx, wte, wpe, S, q, s)
             return q, s
-        x = torch.empty((T, d), dtype=torch.bfloat16, device=idx.device)
-        ext().embed_fwd(idx, wte, wpe, S, x, None, None)
+        x = torch.empty((T, d), dtype=out_dtype, device=idx.device)
+        ext().embed_fwd(idx, wte, wpe, S, x, None)
         return x
     flat = idx.reshape(-1)
     x = wte[flat]
     if wpe is not None:
         x = x + wpe[torch.arange(T) % S]
-    if fp8:
-        return quant_e4m3(x)
+    if q8 is not None:
+        return quant_q8(x, q8)
     return x.to(out_dtype)
 
 

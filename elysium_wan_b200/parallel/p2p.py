@@ -125,8 +125,12 @@ class PipeComm:
         self.T = spec.mb_size * cfg.seq_len
         self.d = cfg.d_model
         self.cuda = self.device.type == "cuda"
-        self.fp8 = cfg.fp8_boundary()
-        self.act_dtype = torch.bfloat16 if self.cuda else torch.float32
+        from elysium_wan_b200 import ops
+
+        self.q8 = ops.q8_dtype(cfg.boundary_dtype)  # fp8 boundary: its dtype, else None
+        self.fp8 = self.q8 is not None
+        self.act_dtype = ops.act_dtype(cfg.boundary_dtype, self.cuda)  # dense boundary activations
+        self.grad_dtype = torch.bfloat16 if self.cuda else torch.float32  # boundary gradients
         link = spec.links[stage] if stage < len(spec.links) else {}
         back = spec.links[stage - 1] if stage > 0 and stage - 1 < len(spec.links) else {}
         self.shim_next = _Shim(link) if not self.cuda else None
@@ -202,7 +206,7 @@ class PipeComm:
         return [torch.empty((self.T, self.d), dtype=self.act_dtype, device=self.device)]
 
     def _grad_buffer(self):
-        return torch.empty((self.T, self.d), dtype=self.act_dtype, device=self.device)
+        return torch.empty((self.T, self.d), dtype=self.grad_dtype, device=self.device)
 
     # ----------------------------------------------------------------- sends
     def _send(self, tensors, dst, group, shim):
@@ -230,7 +234,7 @@ class PipeComm:
 
     def send_grad(self, mb: int, g: torch.Tensor):
         dbg(f"rank {self.rank} send grad mb {mb} -> {self.prev_rank(mb)}")
-        g = g.to(self.act_dtype).contiguous()
+        g = g.to(self.grad_dtype).contiguous()
         return self._send([g], self.prev_rank(mb), self.g_grad_out, self.shim_prev)
 
     # ----------------------------------------------------------------- receives
@@ -260,7 +264,7 @@ class PipeComm:
 
     def as_act(self, bufs) -> Act:
         if self.fp8:
-            return Act(bufs[0].view(torch.float8_e4m3fn), bufs[1])
+            return Act(bufs[0].view(self.q8), bufs[1])
         return Act(bufs[0])
 
     def tied_send(self, t):

@@ -201,9 +201,11 @@ class StageEngine:
         else:
             from elysium_wan_b200 import ops
 
-            dt = torch.bfloat16 if self.device.type == "cuda" else torch.float32
-            z = torch.zeros((T, s.model.d_model), dtype=dt, device=self.device)
-            inp = Act(*ops.quant_e4m3(z)) if s.model.fp8_boundary() else Act(z)
+            cuda = self.device.type == "cuda"
+            z = torch.zeros((T, s.model.d_model), dtype=ops.act_dtype(s.model.boundary_dtype, cuda),
+                            device=self.device)
+            q8 = ops.q8_dtype(s.model.boundary_dtype)
+            inp = Act(*ops.quant_q8(z, q8)) if q8 is not None else Act(z)
         out, st = self.model.forward(inp, x if self.last else None)
         dt = torch.bfloat16 if self.device.type == "cuda" else torch.float32
         dy = None if self.last else torch.zeros((T, s.model.d_model), dtype=dt, device=self.device)

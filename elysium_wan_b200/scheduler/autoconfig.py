@@ -13,8 +13,9 @@ stage's memory. Policies:
 - "max_throughput": the rung with the highest wire ceiling that clears the
   margin.
 
-Rungs are this engine's boundary dtypes: fp32, bf16 and the 1x128
-block-scaled e4m3 (one byte per value plus one fp32 scale per 128 values).
+Rungs are this engine's boundary formats (models/precision.py): fp32, bf16,
+fp16 and the 1x128 block-scaled e5m2 and e4m3 (one byte per value plus one
+fp32 scale per 128 values); "lossless" is the table's representability rule.
 Memory is priced with this engine's model (`planner.act_bytes`: saved bf16
 activations, deferred-W inputs and boundary buffers), not the reference's
 fp32 autograd graph.
@@ -22,10 +23,11 @@ fp32 autograd graph.
 
 from __future__ import annotations
 
+from elysium_wan_b200.models import precision
+
 # widest first
-LADDER = ["fp32", "bf16", "fp8_e4m3_b128"]
-_BYTES = {"fp32": 4.0, "bf16": 2.0, "fp8_e4m3_b128": 1.0 + 4.0 / 128}
-_COMPUTE_BYTES = {"fp32": 4.0, "bf16": 2.0}
+LADDER = list(precision.LADDER)
+_BYTES = {name: f.wire_bytes for name, f in precision.FORMATS.items()}
 BYTES_PER_PARAM_ADAM = 16
 BYTES_PER_PARAM_HOST_ADAM = 8
 BYTES_PER_PARAM_FROZEN = 2  # a frozen bf16 working copy (LoRA base)
@@ -51,9 +53,9 @@ def floor_mbps(d_model: int, seq_len: int, mb_size: int, boundary: str, window_s
 
 
 def lossless(compute_dtype: str, boundary: str) -> bool:
-    """A boundary at least as wide as the compute dtype carries its values
-    exactly (a bf16 activation fits fp32 and bf16 bit for bit)."""
-    return _BYTES[boundary] >= _COMPUTE_BYTES.get(compute_dtype, 4.0) and boundary != "fp8_e4m3_b128"
+    """The boundary holds every compute value exactly (a bf16 activation fits
+    fp32 and bf16 bit for bit; fp16's exponent and the fp8 rungs do not)."""
+    return precision.represents(boundary, compute_dtype)
 
 
 def stage_memory_bytes(cfg, params_stage: int, n_layers_stage: int, mb_size: int,
@@ -99,7 +101,7 @@ def evaluate(cfg, params_stage: int, n_layers_stage: int, mb_size: int, live_gra
             tokens_per_s_ceiling=round(tokens_per_s_ceiling(cfg.d_model, b, link_mbps, wire_ratio)),
             stage_mem_gb=round(mem["total"] / 2**30, 2),
             fits_memory=mem["total"] <= mem_budget_bytes,
-            needs_scale=b == "fp8_e4m3_b128"))
+            needs_scale=precision.fmt(b).needs_scale))
     return rows
 
 

@@ -13,7 +13,7 @@ from elysium_wan_b200.scheduler import partition as part
 from elysium_wan_b200.scheduler.zero_bubble import (ZBConfig, comm_seconds, simulate_slots,
                                                     slot_orders, stage_peak, zero_bubble)
 
-_BOUNDARY_BYTES = {"fp32": 4, "bf16": 2, "fp8_e4m3_b128": 1}
+_BOUNDARY_BYTES = {"fp32": 4, "bf16": 2, "fp16": 2, "fp8_e5m2_b128": 1, "fp8_e4m3_b128": 1}
 
 
 def act_bytes(cfg, spec_mb_size: int, device: str) -> dict:

@@ -36,7 +36,8 @@ import math
 from dataclasses import dataclass
 
 VOCAB = 50257
-BOUNDARY_BYTES = {"fp8_e4m3_b128": 1.0 + 4.0 / 128, "bf16": 2.0, "fp32": 4.0}
+BOUNDARY_BYTES = {"fp8_e4m3_b128": 1.0 + 4.0 / 128, "fp8_e5m2_b128": 1.0 + 4.0 / 128,
+                  "fp16": 2.0, "bf16": 2.0, "fp32": 4.0}
 
 
 @dataclass(frozen=True)

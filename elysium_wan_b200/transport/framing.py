@@ -57,13 +57,13 @@ class Frame:
     frag_cnt: int = 1
 
     def tensor(self):
-        """The payload as a tensor (an e4m3_b128 PLANES payload gives the
+        """The payload as a tensor (an fp8 b128 PLANES payload gives the
         (codes, scales) pair)."""
         if self.codec == OBJ:
             raise ValueError("control frame has no tensor")
         if self.codec == PLANES:
-            if self.payload and self.payload[0] == codec.E4M3_B128_ID:
-                return codec.e4m3_b128_decode(self.payload, self.shape)
+            if self.payload and self.payload[0] in codec.Q8_B128:
+                return codec.q8_b128_decode(self.payload, self.shape)
             return codec.planes_decode(self.payload, self.shape)
         if self.codec == FP8_PLANES:
             return codec.fp8_planes_decode(self.payload, self.shape)
@@ -84,9 +84,9 @@ def encode_tensor(t, wire_codec: str = "raw", level: int = 1):
     """(codec id, payload, shape) of a tensor under a spec's wire_codec.
     raw: exact bytes (fp32 / int64 as RAW, other dtypes as uncompressed
     PLANES); planes: byte planes + zlib; f32_planes / fp8_planes as named.
-    A (codes, scales) pair is this engine's e4m3_b128 boundary."""
+    A (codes, scales) pair is this engine's fp8 b128 boundary."""
     if isinstance(t, tuple):
-        payload, shape = codec.e4m3_b128_encode(t[0], t[1], 0 if wire_codec == "raw" else level)
+        payload, shape = codec.q8_b128_encode(t[0], t[1], 0 if wire_codec == "raw" else level)
         return PLANES, payload, shape
     if wire_codec == "raw":
         if t.dtype == torch.float32:

@@ -165,8 +165,12 @@ class TcpPipeComm:
         cfg = spec.model
         self.T, self.d = spec.mb_size * cfg.seq_len, cfg.d_model
         self.cuda = self.device.type == "cuda"
-        self.fp8 = cfg.fp8_boundary()
-        self.act_dtype = torch.bfloat16 if self.cuda else torch.float32
+        from elysium_wan_b200 import ops
+
+        self.q8 = ops.q8_dtype(cfg.boundary_dtype)  # fp8 boundary: its dtype, else None
+        self.fp8 = self.q8 is not None
+        self.act_dtype = ops.act_dtype(cfg.boundary_dtype, self.cuda)  # dense boundary activations
+        self.grad_dtype = torch.bfloat16 if self.cuda else torch.float32  # boundary gradients
         self.key = identity.load_or_create_key(key_path)
         self.trusted = spec.trusted_peers
         self.inbox = _Inbox()
@@ -312,7 +316,7 @@ class TcpPipeComm:
 
     def send_grad(self, mb: int, g: torch.Tensor):
         self._enqueue(self.prev_links[self.prev_peer(mb)], BWD, mb,
-                      [self._host(g.to(self.act_dtype))])
+                      [self._host(g.to(self.grad_dtype))])
         return []
 
     def _enqueue(self, link, ftype, mb, tensors):
@@ -345,7 +349,7 @@ class TcpPipeComm:
 
     def as_act(self, bufs) -> Act:
         if self.fp8:
-            return Act(bufs[0].view(torch.float8_e4m3fn), bufs[1])
+            return Act(bufs[0].view(self.q8), bufs[1])
         return Act(bufs[0])
 
     def tied_send(self, t):

@@ -131,7 +131,7 @@ def build(op):
         tgt = torch.randint(0, V, (T,), device="cuda")
         return (lambda: ops.cross_entropy(logits, V, tgt, 1.0 / T)), None, T * V * 6
     if op == "adamw":
-        n = 1 << 28
+        n = 1 << 26  # 64 M parameters: 1.2 GB of state, ten times L2
         p, g = torch.randn(n, device="cuda"), torch.randn(n, device="cuda")
         m, v = torch.zeros(n, device="cuda"), torch.zeros(n, device="cuda")
         pb = torch.empty(n, dtype=torch.bfloat16, device="cuda")

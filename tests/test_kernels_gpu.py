@@ -70,7 +70,7 @@ def test_gemm_epilogues(cuda):
     y = ops.linear_fwd(x, w, b, epi="resid", resid=r)
     assert rel_err(y, acc + r.float()) < 8e-3
     q, s = ops.linear_fwd(x, w, b, epi="resid_q8", resid=r)
-    deq = ops.dequant_e4m3(q, s, torch.float32)
+    deq = ops.dequant_q8(q, s, torch.float32)
     assert rel_err(deq, acc + r.float()) < 6e-2
     qr, sr = ops.quant_e4m3((acc + r.float()).to(torch.bfloat16))
     # same scales as quantising the bf16-free fp32 sum up to bf16 rounding of the input
@@ -108,7 +108,7 @@ def test_gemm_register_epilogues_widths(cuda, N, bn):
     if N % 128 == 0:
         q, s = ops.quant_e4m3(r)
         ops.gemm(x, w, y, ops.EPI_RESID, bias=b, resid=q, resid_scale=s, bn=bn)
-        assert rel_err(y, acc + ops.dequant_e4m3(q, s, torch.float32)) < 8e-3
+        assert rel_err(y, acc + ops.dequant_q8(q, s, torch.float32)) < 8e-3
     g = torch.empty(M, N, dtype=torch.bfloat16, device=cuda)
     u = torch.empty(M, N, dtype=torch.bfloat16, device=cuda)
     ops.gemm(x, w, g, ops.EPI_GELU, bias=b, aux=u, bn=bn)
@@ -171,7 +171,7 @@ def test_gemm_k_split_tail(cuda, bn):
     ops.gemm(x, w, y, ops.EPI_RESID, bias=b, resid=r, bn=bn)
     assert rel_err(y, ref + b + r.float()) < 8e-3
     q, s = ops.linear_fwd(x, w, b, epi="resid_q8", resid=r)
-    assert rel_err(ops.dequant_e4m3(q, s, torch.float32), ref + b + r.float()) < 6e-2
+    assert rel_err(ops.dequant_q8(q, s, torch.float32), ref + b + r.float()) < 6e-2
 
 
 @pytest.mark.parametrize("T2", [2048, 1000])
@@ -233,7 +233,7 @@ def test_layernorm(cuda, d, fp8):
     xin = x
     if fp8:
         xin, xs = ops.quant_e4m3(x)
-        xf = ops.dequant_e4m3(xin, xs, torch.float32)
+        xf = ops.dequant_q8(xin, xs, torch.float32)
     else:
         xf = x.float()
     gamma = torch.randn(d, device=cuda)
@@ -354,17 +354,28 @@ def test_fused_head_cross_entropy(cuda, T, V, d):
     assert ops.ext().status_read_clear() == 0
 
 
-@pytest.mark.parametrize("fp8", [False, True])
-def test_embedding(cuda, fp8):
+@pytest.mark.parametrize("fmt", ["bf16", "fp16", "fp8_e4m3_b128", "fp8_e5m2_b128"])
+def test_embedding(cuda, fmt):
     torch.manual_seed(7)
     V, S, d, B = 1000, 128, 256, 4
     wte = torch.randn(V, d, device=cuda)
     wpe = torch.randn(S, d, device=cuda)
     idx = torch.randint(0, 50, (B, S), device=cuda)  # many repeats
-    out = ops.embed_fwd(idx, wte, wpe, S, fp8)
+    q8 = ops.q8_dtype(fmt)
+    out = ops.embed_fwd(idx, wte, wpe, S, q8, out_dtype=ops.act_dtype(fmt, True))
     ref = wte[idx.view(-1)] + wpe[torch.arange(B * S, device=cuda) % S]
-    got = ops.dequant_e4m3(*out, torch.float32) if fp8 else out.float()
-    assert rel_err(got, ref) < (6e-2 if fp8 else 8e-3)
+    # bit for bit the host restatement of the same boundary recipe
+    host = ops.embed_fwd(idx.cpu(), wte.cpu(), wpe.cpu(), S, q8,
+                         out_dtype=ops.act_dtype(fmt, True))
+    if q8 is not None:
+        assert out[0].dtype == q8
+        assert torch.equal(out[0].cpu().view(torch.uint8), host[0].view(torch.uint8))
+        assert torch.equal(out[1].cpu(), host[1])
+        got = ops.dequant_q8(*out, torch.float32)
+    else:
+        assert out.dtype == host.dtype and torch.equal(out.cpu(), host)
+        got = out.float()
+    assert rel_err(got, ref) < (0.13 if fmt == "fp8_e5m2_b128" else 6e-2 if q8 else 8e-3)
     dx = bf(B * S, d, dev=cuda)
     dwte = torch.zeros(V, d, device=cuda)
     dwpe = torch.zeros(S, d, device=cuda)

@@ -22,13 +22,16 @@ def _need(n):
         pytest.skip(f"needs {n} GPUs")
 
 
-@pytest.mark.parametrize("stages,boundary", [(2, "fp8_e4m3_b128"), (2, "bf16"), (4, "fp8_e4m3_b128")])
+@pytest.mark.parametrize("stages,boundary", [(2, "fp8_e4m3_b128"), (2, "bf16"), (4, "fp8_e4m3_b128"),
+                                             (1, "fp16"), (1, "fp8_e5m2_b128"), (2, "fp16"),
+                                             (2, "fp8_e5m2_b128")])
 def test_nccl_pipeline_bitwise_vs_oracle(tmp_path, stages, boundary):
     _need(stages)
     cfg = make_config("gpt15b", n_layer=max(4, stages), d_model=512, n_head=4, seq_len=256, vocab_size=4096,
                       boundary_dtype=boundary)
     spec = JobSpec(model=cfg, stages=stages, microbatches=6, mb_size=2, steps=2, device="cuda",
-                   backend="nccl", out_dir=str(tmp_path), port_base=29950 + stages)
+                   backend="nccl", out_dir=str(tmp_path),
+                   port_base=29950 + 7 * stages + len(boundary))
     r = run_and_compare(spec, timeout=240)
     assert r["ok"], r
     assert r["compared"] == 12

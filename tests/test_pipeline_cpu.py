@@ -29,6 +29,10 @@ CASES = {
     "w_pair_chain3": dict(stages=3, w_pair=True, microbatches=5),
     "w_pair_wide_1_2": dict(stages=2, stage_widths=[1, 2], w_pair=True),
     "chain3_fp8_recompute": dict(stages=3, recompute=True, model_kw=dict(boundary_dtype="fp8_e4m3_b128")),
+    # The other boundary rungs: fp16 (host path rounds to fp16 at every entry
+    # boundary) and block-scaled e5m2, the latter on a wide stage.
+    "chain2_fp16": dict(stages=2, model_kw=dict(boundary_dtype="fp16")),
+    "e5m2_wide_1_2": dict(stages=2, stage_widths=[1, 2], model_kw=dict(boundary_dtype="fp8_e5m2_b128")),
     "wide_2_1": dict(stages=2, stage_widths=[2, 1]),
     # Uneven peers: each peer of the wide stages runs its own lane order
     # (solved per peer, chosen because the slot simulation finds it faster).
