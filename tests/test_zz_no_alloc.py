@@ -33,10 +33,15 @@ def _fn():
     return f
 
 
-def _call(f, dy, x, mean, rstd, gamma, dres, dx, dg, db, accumulate):
+# x's format code (the x_fp8 argument): 0 bf16, 1 e4m3 + 1x128 scales, 2 e5m2 + scales, 3 fp16
+FMT = {torch.bfloat16: 0, torch.float8_e4m3fn: 1, torch.float8_e5m2: 2, torch.float16: 3}
+
+
+def _call(f, dy, x, mean, rstd, gamma, dres, dx, dg, db, accumulate, xs=None):
     rows, d = x.shape
     stream = torch.cuda.current_stream().cuda_stream
-    return f(dy.data_ptr(), dy.stride(0), x.data_ptr(), None, 0, x.stride(0), 0, mean.data_ptr(),
+    return f(dy.data_ptr(), dy.stride(0), x.data_ptr(), None if xs is None else xs.data_ptr(),
+             FMT[x.dtype], x.stride(0), 0 if xs is None else xs.stride(0), mean.data_ptr(),
              rstd.data_ptr(), gamma.data_ptr(), dres.data_ptr(), dres.stride(0), dx.data_ptr(),
              dx.stride(0), dg.data_ptr(), db.data_ptr(), 1 if accumulate else 0, rows, d, stream)
 
@@ -87,3 +92,46 @@ def test_noalloc_rejects_rows_wider_than_its_scratch():
     out = torch.empty_like(x)
     rc = _call(f, x, x, stats, stats, g, x, out, g.clone(), g.clone(), accumulate=False)
     assert rc == ERR_TOO_LARGE
+
+
+@pytest.mark.parametrize("fmt,rows,d", [("e4m3", 300, 1536), ("e5m2", 40, 1024), ("fp16", 17, 768),
+                                        ("bf16", 63, 512)])
+def test_noalloc_accumulates_every_format_without_allocating(fmt, rows, d):
+    """accumulate=1 on preset dgamma / dbeta, x in each boundary format, row
+    counts below the 64 scratch chunks; a warmed call changes neither the
+    caching allocator's count nor the device's free memory."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    torch.manual_seed(13)
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    f = _fn()
+    xb = (torch.randn(rows, d, device=dev) * 2).to(torch.bfloat16)
+    xs = None
+    if fmt in ("e4m3", "e5m2"):
+        x, xs = ops.quant_q8(xb, ops.E4M3 if fmt == "e4m3" else ops.E5M2)
+    elif fmt == "fp16":
+        x = xb.to(torch.float16)
+    else:
+        x = xb
+    gamma, beta = torch.randn(d, device=dev), torch.randn(d, device=dev)
+    _, mean, rstd = ops.layernorm_fwd(x, xs, gamma, beta)
+    dy = torch.randn(rows, d, device=dev).to(torch.bfloat16)
+    dres = torch.randn(rows, d, device=dev).to(torch.bfloat16)
+    g0, b0 = torch.randn(d, device=dev), torch.randn(d, device=dev)
+    dg_ref, db_ref = g0.clone(), b0.clone()
+    dx_ref = ops.layernorm_bwd(dy, x, xs, mean, rstd, gamma, dres, dg_ref, db_ref, accumulate=True)
+    dx = torch.empty_like(dx_ref)
+    dg, db = g0.clone(), b0.clone()
+    assert _call(f, dy, x, mean, rstd, gamma, dres, dx, dg, db, True, xs) == 0  # warm
+    torch.cuda.synchronize()
+    dg, db = g0.clone(), b0.clone()
+    torch.cuda.synchronize()
+    alloc0, free0 = torch.cuda.memory_allocated(dev), torch.cuda.mem_get_info(dev)[0]
+    rc = _call(f, dy, x, mean, rstd, gamma, dres, dx, dg, db, True, xs)
+    torch.cuda.synchronize()
+    assert rc == 0
+    assert torch.cuda.memory_allocated(dev) == alloc0
+    assert torch.cuda.mem_get_info(dev)[0] == free0
+    assert torch.equal(dx, dx_ref)
+    assert rel(dg, dg_ref) < 1e-5 and rel(db, db_ref) < 1e-5
