@@ -118,7 +118,7 @@ __global__ void __launch_bounds__(kTcFwdThreads, 1)
       uint8_t* sq = smem + kOffQ;
       mbar_arrive_expect_tx(qfull, kTile);
       for (int c = 0; c < 2; ++c)
-        tma_load_2d(sq + c * kChunk, &map_qk, qfull, h * kTcHD + c * 64, row0 + qb * kTcBlk);
+        tma_load_2d(sq + c * kChunk, &map_qk, qfull, h * kTcHD + c * 64, row0 + qb * kTcBlk, status);
       int issued = 0;
       bool ok = true;
       for (int j = 0; j < nblk && ok; ++j) {
@@ -133,7 +133,7 @@ __global__ void __launch_bounds__(kTcFwdThreads, 1)
         mbar_arrive_expect_tx(&kfull[s], kTile);
         for (int c = 0; c < 2; ++c)
           tma_load_2d(sk + c * kChunk, &map_qk, &kfull[s], d + hk * kTcHD + c * 64,
-                      row0 + j * kTcBlk);
+                      row0 + j * kTcBlk, status);
         if (!mbar_wait(&vempty[s], ph, status, kStatusTimeoutSmemEmpty)) {
           ok = false;
           issued = 2 * j + 1;
@@ -143,7 +143,7 @@ __global__ void __launch_bounds__(kTcFwdThreads, 1)
         for (int kb = 0; kb < 2; ++kb)
           for (int c = 0; c < 2; ++c)
             tma_load_2d(sv + kb * kChunk + c * 8192, &map_v, &vfull[s],
-                        d + dkv + hk * kTcHD + c * 64, row0 + j * kTcBlk + kb * 64);
+                        d + dkv + hk * kTcHD + c * 64, row0 + j * kTcBlk + kb * 64, status);
         issued = 2 * j + 2;
       }
       // Drain: loads already issued must land before this CTA's memory goes away.
@@ -434,9 +434,9 @@ __global__ void __launch_bounds__(kBwThreads, 1)
       mbar_arrive_expect_tx(kvfull, 2 * kTile);
       for (int c = 0; c < 2; ++c) {
         tma_load_2d(smem + kBwOffK + c * kChunk, &map_kv, kvfull, d + hk * kTcHD + c * 64,
-                    row0 + kb * kTcBlk);
+                    row0 + kb * kTcBlk, status);
         tma_load_2d(smem + kBwOffV + c * kChunk, &map_kv, kvfull, d + dkv + hk * kTcHD + c * 64,
-                    row0 + kb * kTcBlk);
+                    row0 + kb * kTcBlk, status);
       }
       int issued = 0;
       for (int t = 0; t < steps; ++t) {
@@ -446,9 +446,9 @@ __global__ void __launch_bounds__(kBwThreads, 1)
         mbar_arrive_expect_tx(&qfull[sb], 2 * 16384 + 512);
         for (int c = 0; c < 2; ++c) {
           tma_load_2d(smem + kBwOffQ + sb * 16384 + c * 8192, &map_q, &qfull[sb],
-                      h * kTcHD + c * 64, row0 + i * 64);
+                      h * kTcHD + c * 64, row0 + i * 64, status);
           tma_load_2d(smem + kBwOffDO + sb * 16384 + c * 8192, &map_do, &qfull[sb],
-                      h * kTcHD + c * 64, row0 + i * 64);
+                      h * kTcHD + c * 64, row0 + i * 64, status);
         }
         const size_t li = (static_cast<size_t>(bz) * H + h) * S + i * 64;
         bulk_load(smem + kBwOffL + sb * 256, lse2 + li, 256, &qfull[sb]);
@@ -687,9 +687,9 @@ __global__ void __launch_bounds__(kBwThreads, 1)
       mbar_arrive_expect_tx(qfull, 2 * kTile);
       for (int c = 0; c < 2; ++c) {
         tma_load_2d(smem + kDqOffQ + c * kChunk, &map_q128, qfull, h * kTcHD + c * 64,
-                    row0 + qb * kTcBlk);
+                    row0 + qb * kTcBlk, status);
         tma_load_2d(smem + kDqOffDO + c * kChunk, &map_do128, qfull, h * kTcHD + c * 64,
-                    row0 + qb * kTcBlk);
+                    row0 + qb * kTcBlk, status);
       }
       int issued = 0;
       for (int j = 0; j < nblk; ++j) {
@@ -700,9 +700,9 @@ __global__ void __launch_bounds__(kBwThreads, 1)
           for (int c = 0; c < 2; ++c) {
             const int y = row0 + j * kTcBlk + kh * 64;
             tma_load_2d(smem + kDqOffK + sb * kTile + kh * kChunk + c * 8192, &map_kv64,
-                        &kfull[sb], d + hk * kTcHD + c * 64, y);
+                        &kfull[sb], d + hk * kTcHD + c * 64, y, status);
             tma_load_2d(smem + kDqOffV + sb * kTile + kh * kChunk + c * 8192, &map_kv64,
-                        &kfull[sb], d + dkv + hk * kTcHD + c * 64, y);
+                        &kfull[sb], d + dkv + hk * kTcHD + c * 64, y, status);
           }
         issued = j + 1;
       }

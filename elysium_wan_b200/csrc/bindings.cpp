@@ -16,6 +16,7 @@
 #include <atomic>
 #include <cstdlib>
 #include <string>
+#include <vector>
 
 #include "gemm.h"
 #include "kernels.h"
@@ -53,8 +54,9 @@ int* status_word(int dev) {
   if (dev < 0 || dev >= 64) return nullptr;
   if (words[dev] == nullptr) {
     int* p = nullptr;
-    TORCH_CHECK(cudaMalloc(&p, sizeof(int)) == cudaSuccess, "status word allocation failed");
-    TORCH_CHECK(cudaMemset(p, 0, sizeof(int)) == cudaSuccess, "status word init failed");
+    // the 32-byte status record: status word, failing site, two 64-bit values
+    TORCH_CHECK(cudaMalloc(&p, 32) == cudaSuccess, "status word allocation failed");
+    TORCH_CHECK(cudaMemset(p, 0, 32) == cudaSuccess, "status word init failed");
     words[dev] = p;
   }
   return words[dev];
@@ -295,7 +297,7 @@ void ce_lse_finalize(at::Tensor part, at::Tensor tgt_logit, at::Tensor targets, 
                           tgt_logit.data_ptr<float>(), targets.data_ptr<int64_t>(), buf.size(0),
                           static_cast<int>(V), buf.data_ptr(), buf.size(1),
                           static_cast<float>(grad_scale), loss_rows.data_ptr<float>(),
-                          cur_stream()),
+                          status_word(buf.get_device()), cur_stream()),
      "ce_lse_finalize");
   count(1);
 }
@@ -540,6 +542,8 @@ void embed_fwd(at::Tensor idx, at::Tensor wte, c10::optional<at::Tensor> wpe, in
   a.T = idx.numel();
   a.S = S;
   a.d = wte.size(1);
+  a.V = wte.size(0);
+  a.status = status_word(idx.get_device());
   check_2d_rowmajor(out, "out");
   TORCH_CHECK(out.stride(0) == a.d, "out must be contiguous [T][d]");
   a.out = out.data_ptr();
@@ -563,6 +567,7 @@ void embed_bwd(at::Tensor idx, at::Tensor dx, int64_t S, at::Tensor order, at::T
   a.order = order.data_ptr<int>();
   a.dwte = dwte.data_ptr<float>();
   a.dwpe = ptr_or_null<float>(dwpe);
+  a.status = status_word(idx.get_device());
   ok(ewb::embed_bwd(a, cur_stream()), "embed_bwd");
   count(3);
 }
@@ -723,8 +728,20 @@ int64_t status_read_clear() {
   int v = 0;
   TORCH_CHECK(cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess,
               "status read failed");
-  if (v != 0) cudaMemset(p, 0, sizeof(int));
+  if (v != 0) cudaMemset(p, 0, 32);
   return v;
+}
+
+// The status record of the current device without clearing it (synchronises):
+// [status, site, a, b] (site and values name the first failed check).
+std::vector<int64_t> status_record() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int* p = status_word(dev);
+  int32_t w[8] = {0};
+  TORCH_CHECK(cudaMemcpy(w, p, 32, cudaMemcpyDeviceToHost) == cudaSuccess, "status read failed");
+  const long long* q = reinterpret_cast<const long long*>(w);
+  return {w[0], w[1], q[1], q[2]};
 }
 
 }  // namespace
@@ -763,6 +780,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("launch_count", &launch_count);
   m.def("install_segv_backtrace", &install_segv_backtrace);
   m.def("status_read_clear", &status_read_clear);
+  m.def("status_record", &status_record);
+#ifdef EWB_KCHECK
+  m.attr("KCHECK") = true;
+#else
+  m.attr("KCHECK") = false;
+#endif
   m.def("wait_probe", &wait_probe);
   m.attr("EPI_BF16") = static_cast<int>(ewb::kEpiBf16);
   m.attr("EPI_GELU") = static_cast<int>(ewb::kEpiGelu);

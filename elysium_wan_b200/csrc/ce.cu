@@ -31,7 +31,7 @@ __device__ __forceinline__ void lse_combine(float& m, float& s, float m2, float 
 __global__ void __launch_bounds__(kCeThreads)
     ce_kernel(const float* __restrict__ logits, int ldl, const int64_t* __restrict__ targets,
               int V, float* __restrict__ loss_rows, __nv_bfloat16* __restrict__ dlogits, int ldg,
-              float grad_scale) {
+              float grad_scale, int* status) {
   __shared__ float sm_m[kCeThreads / 32];
   __shared__ float sm_s[kCeThreads / 32];
   const int row = blockIdx.x;
@@ -62,7 +62,13 @@ __global__ void __launch_bounds__(kCeThreads)
   for (int k = 1; k < kCeThreads / 32; ++k) lse_combine(M, Ssum, sm_m[k], sm_s[k]);
   const float lse = M + logf(Ssum);
   const int64_t tgt = targets[row];
-  if (threadIdx.x == 0) loss_rows[row] = lse - x[tgt];
+  // A target outside the vocabulary is reported (status record) and gives a
+  // NaN loss instead of a read outside the row.
+  const bool tgt_ok = tgt >= 0 && tgt < V;
+  if (threadIdx.x == 0) {
+    if (!tgt_ok) record_check(status, kStatusBadArgument, kSiteCeTarget, row, tgt);
+    loss_rows[row] = tgt_ok ? lse - x[tgt] : __int_as_float(0x7fc00000);
+  }
   if (dlogits != nullptr) {
     __nv_bfloat16* g = dlogits + static_cast<size_t>(row) * ldg;
     for (int j = threadIdx.x; j < ldg; j += kCeThreads) {
@@ -155,7 +161,13 @@ __global__ void __launch_bounds__(kCeSmemThreads, 1)
   const float S = block_reduce(s, red, false);
   const float lse = M + logf(S);
   const int64_t tgt = targets[row];
-  if (threadIdx.x == 0) loss_rows[row] = lse - x[tgt];
+  // A target outside the vocabulary is reported (status record) and gives a
+  // NaN loss instead of a read outside the row.
+  const bool tgt_ok = tgt >= 0 && tgt < V;
+  if (threadIdx.x == 0) {
+    if (!tgt_ok) record_check(status, kStatusBadArgument, kSiteCeTarget, row, tgt);
+    loss_rows[row] = tgt_ok ? lse - x[tgt] : __int_as_float(0x7fc00000);
+  }
   if (dlogits == nullptr) return;
   const float inv = 1.0f / S;
   __nv_bfloat16* g = dlogits + static_cast<size_t>(row) * ldg;
@@ -229,7 +241,7 @@ __global__ void __launch_bounds__(kFinThreads)
     ce_lse_finalize_kernel(const float2* __restrict__ part, int nt, int ld_part,
                            const float* __restrict__ tgt_logit, const int64_t* __restrict__ targets,
                            int V, uint16_t* __restrict__ buf, int ld, float grad_scale,
-                           float* __restrict__ loss_rows) {
+                           float* __restrict__ loss_rows, int* status) {
   __shared__ float fac[kFinMaxTiles];
   __shared__ float red[33];
   const int row = blockIdx.x;
@@ -245,7 +257,11 @@ __global__ void __launch_bounds__(kFinThreads)
   const float S = block_reduce_fin(s, red, false);
   const float lse = M + logf(S);
   const int64_t tgt = targets[row];
-  if (threadIdx.x == 0) loss_rows[row] = lse - tgt_logit[row];
+  if (threadIdx.x == 0) {
+    const bool tgt_ok = tgt >= 0 && tgt < V;
+    if (!tgt_ok) record_check(status, kStatusBadArgument, kSiteCeTarget, row, tgt);
+    loss_rows[row] = tgt_ok ? lse - tgt_logit[row] : __int_as_float(0x7fc00000);
+  }
   for (int k = threadIdx.x; k < nt; k += kFinThreads) fac[k] = expf(pr[k].x - lse);
   __syncthreads();
   uint16_t* g = buf + static_cast<size_t>(row) * ld;
@@ -273,13 +289,13 @@ __global__ void __launch_bounds__(kFinThreads)
 
 int ce_lse_finalize(const float* part, int nt, int ld_part, const float* tgt_logit,
                     const int64_t* targets, int T, int V, void* buf, int ld, float grad_scale,
-                    float* loss_rows, cudaStream_t stream) {
+                    float* loss_rows, int* status, cudaStream_t stream) {
   if (T <= 0 || V <= 0 || nt != (V + 255) / 256 || nt > kFinMaxTiles || ld_part < nt ||
       ld < V || ld % 8 || (reinterpret_cast<uintptr_t>(buf) & 15))
     return 1;
   ce_lse_finalize_kernel<<<T, kFinThreads, 0, stream>>>(
       reinterpret_cast<const float2*>(part), nt, ld_part, tgt_logit, targets, V,
-      reinterpret_cast<uint16_t*>(buf), ld, grad_scale, loss_rows);
+      reinterpret_cast<uint16_t*>(buf), ld, grad_scale, loss_rows, status);
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
 
@@ -310,7 +326,7 @@ int cross_entropy(const CeArgs& a, cudaStream_t stream) {
                                                           a.grad_scale, row_bytes, a.status);
   } else {
     ce_kernel<<<a.T, kCeThreads, 0, stream>>>(a.logits, a.ldl, a.targets, a.V, a.loss_rows,
-                                              a.dlogits, a.ldg, a.grad_scale);
+                                              a.dlogits, a.ldg, a.grad_scale, a.status);
   }
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }

@@ -32,6 +32,15 @@ enum StatusCode : int {
   kStatusTimeoutPeer = 5,
   kStatusBadArgument = 6,
   kStatusTimeoutDrain = 7,
+  kStatusBoundsCheck = 8,  // a check of a bounds-checked build (EWB_KCHECK) failed
+};
+
+// Where a check failed (the status record's site word).
+enum CheckSite : int {
+  kSiteNone = 0,
+  kSiteEmbedToken = 1,   // a token id outside [0, V): a = position, b = id
+  kSiteCeTarget = 2,     // a target outside [0, V): a = row, b = target
+  kSiteTmaInnerX = 3,    // a tiled TMA load whose inner coordinate is not 16-byte aligned: a = x, b = y
 };
 
 // Two seconds: long enough for any legitimate wait inside one kernel (a GEMM
@@ -51,6 +60,33 @@ __device__ __forceinline__ void record_status(int* status, int code) {
 
 __device__ __forceinline__ bool status_failed(const int* status) {
   return status != nullptr && *reinterpret_cast<const volatile int*>(status) != 0;
+}
+
+// The status record is 32 bytes: the status word, the failing site, and two
+// 64-bit values naming the failing index (first failure wins).
+__device__ __forceinline__ void record_check(int* status, int code, int site, long long a,
+                                             long long b) {
+  if (status != nullptr && atomicCAS(status, 0, code) == 0) {
+    status[1] = site;
+    reinterpret_cast<long long*>(status)[1] = a;
+    reinterpret_cast<long long*>(status)[2] = b;
+  }
+}
+
+// Bounds-checked builds (-DEWB_KCHECK): `ok` false records the site and the
+// two values and returns false so the caller skips the access. In a regular
+// build the check compiles away (always true).
+#ifdef EWB_KCHECK
+constexpr bool kKcheck = true;
+#else
+constexpr bool kKcheck = false;
+#endif
+__device__ __forceinline__ bool kcheck(int* status, bool ok, int site, long long a, long long b) {
+  if (kKcheck && !ok) {
+    record_check(status, kStatusBoundsCheck, site, a, b);
+    return false;
+  }
+  return true;
 }
 
 // ---------------------------------------------------------------- smem / mbarrier
@@ -135,8 +171,14 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
 
 // 2D tiled load of one box into this CTA's shared memory; completion is
 // signalled as transaction bytes on `bar`. x is the innermost coordinate.
+// Every tiled load of this library reads a 2-byte map, so its inner
+// coordinate x must be a multiple of 8 (16 bytes); a bounds-checked build
+// records a violation (site kSiteTmaInnerX) and skips the copy, so the waiting
+// consumer's bounded wait expires instead of the GPU raising an illegal
+// instruction.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
-                                            int x, int y) {
+                                            int x, int y, int* status = nullptr) {
+  if (!kcheck(status, (x & 7) == 0, kSiteTmaInnerX, x, y)) return;
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
@@ -364,7 +406,9 @@ __device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
 // bytes) is signalled on the leader CTA's mbarrier `leader_bar` (a
 // shared::cluster address). No broadcast: each CTA loads its own half.
 __device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map,
-                                                 uint32_t leader_bar, int x, int y) {
+                                                 uint32_t leader_bar, int x, int y,
+                                                 int* status = nullptr) {
+  if (!kcheck(status, (x & 7) == 0, kSiteTmaInnerX, x, y)) return;
   asm volatile(
       "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),

@@ -18,11 +18,17 @@ namespace {
 
 __global__ void __launch_bounds__(128)
     embed_fwd_kernel(const int64_t* __restrict__ idx, const float* __restrict__ wte,
-                     const float* __restrict__ wpe, int S, int d, void* __restrict__ out, int fmt,
-                     float* __restrict__ out_scale) {
+                     const float* __restrict__ wpe, int S, int d, int V, void* __restrict__ out,
+                     int fmt, float* __restrict__ out_scale, int* status) {
   const int t = blockIdx.x;
-  const int64_t tok = idx[t];
+  int64_t tok = idx[t];
   const int pos = t % S;
+  // A token id outside the table is reported (status record) and reads row 0
+  // instead of memory outside the table.
+  if (tok < 0 || tok >= V) {
+    if (threadIdx.x == 0) record_check(status, kStatusBadArgument, kSiteEmbedToken, t, tok);
+    tok = 0;
+  }
   const float* er = wte + static_cast<size_t>(tok) * d;
   const float* pr = wpe != nullptr ? wpe + static_cast<size_t>(pos) * d : nullptr;  // rope: none
   for (int c0 = 0; c0 < d; c0 += 1024) {
@@ -87,11 +93,16 @@ __global__ void __launch_bounds__(kRankPer) embed_rank_kernel(const int64_t* __r
 
 __global__ void __launch_bounds__(256)
     embed_wte_bwd_kernel(const int64_t* __restrict__ idx, const __nv_bfloat16* __restrict__ dx,
-                         const int* __restrict__ order, int T, int d, float* __restrict__ dwte) {
+                         const int* __restrict__ order, int T, int d, int V, float* __restrict__ dwte,
+                         int* status) {
   const int i = blockIdx.x;
   const int t0 = order[i];
   const int64_t tok = idx[t0];
   if (i > 0 && idx[order[i - 1]] == tok) return;  // not a run head
+  if (tok < 0 || tok >= V) {  // reported, never written outside the table
+    if (threadIdx.x == 0) record_check(status, kStatusBadArgument, kSiteEmbedToken, t0, tok);
+    return;
+  }
   int end = i + 1;
   while (end < T && idx[order[end]] == tok) ++end;
   float* g = dwte + static_cast<size_t>(tok) * d;
@@ -135,11 +146,11 @@ __global__ void __launch_bounds__(256)
 }  // namespace
 
 int embed_fwd(const EmbedArgs& a, cudaStream_t stream) {
-  if (a.d % 8 || (fmt_q8(a.out_fmt) && (a.d % 128 || a.out_scale == nullptr)) || a.T % a.S ||
+  if (a.d % 8 || a.V <= 0 || (fmt_q8(a.out_fmt) && (a.d % 128 || a.out_scale == nullptr)) || a.T % a.S ||
       a.out_fmt < kFmtBf16 || a.out_fmt > kFmtF16)
     return 1;
-  embed_fwd_kernel<<<a.T, 128, 0, stream>>>(a.idx, a.wte, a.wpe, a.S, a.d, a.out, a.out_fmt,
-                                            a.out_scale);
+  embed_fwd_kernel<<<a.T, 128, 0, stream>>>(a.idx, a.wte, a.wpe, a.S, a.d, a.V, a.out, a.out_fmt,
+                                            a.out_scale, a.status);
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
 
@@ -147,7 +158,8 @@ int embed_bwd(const EmbedBwdArgs& a, cudaStream_t stream) {
   if (a.T > 16384 || a.T % a.S) return 1;
   embed_rank_kernel<<<(a.T + kRankPer - 1) / kRankPer, kRankPer, a.T * sizeof(int), stream>>>(
       a.idx, a.T, a.order);
-  embed_wte_bwd_kernel<<<a.T, 256, 0, stream>>>(a.idx, a.dx, a.order, a.T, a.d, a.dwte);
+  embed_wte_bwd_kernel<<<a.T, 256, 0, stream>>>(a.idx, a.dx, a.order, a.T, a.d, a.V, a.dwte,
+                                                a.status);
   if (a.dwpe != nullptr) embed_wpe_bwd_kernel<<<a.S, 256, 0, stream>>>(a.dx, a.T, a.S, a.d, a.dwpe);
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }

@@ -626,17 +626,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           const CUtensorMap* mB = seg2 ? &tmB2 : &tmB;
           const int kc = (seg2 ? kb - kb1 : kb) * kBK;
           if constexpr (!A_MN) {
-            tma_load_2d(sa, mA, &full[s], kc, mb * kBM);
+            tma_load_2d(sa, mA, &full[s], kc, mb * kBM, status);
           } else {
-            tma_load_2d(sa, mA, &full[s], mb * kBM, kc);
-            tma_load_2d(sa + 8192, mA, &full[s], mb * kBM + 64, kc);
+            tma_load_2d(sa, mA, &full[s], mb * kBM, kc, status);
+            tma_load_2d(sa + 8192, mA, &full[s], mb * kBM + 64, kc, status);
           }
           if constexpr (!B_MN) {
-            tma_load_2d(sb, mB, &full[s], kc, nb * BN);
+            tma_load_2d(sb, mB, &full[s], kc, nb * BN, status);
           } else {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j)
-              tma_load_2d(sb + j * 8192, mB, &full[s], nb * BN + j * 64, kc);
+              tma_load_2d(sb + j * 8192, mB, &full[s], nb * BN + j * 64, kc, status);
           }
         }
       }
@@ -915,17 +915,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint32_t lbar = peer_smem(smem_u32(&full[s]), 0);
           const int kc = kb * kBK;
           if constexpr (!A_MN) {
-            tma_load_2d_pair(sa, &tmA, lbar, kc, m0);
+            tma_load_2d_pair(sa, &tmA, lbar, kc, m0, status);
           } else {
-            tma_load_2d_pair(sa, &tmA, lbar, m0, kc);
-            tma_load_2d_pair(sa + 8192, &tmA, lbar, m0 + 64, kc);
+            tma_load_2d_pair(sa, &tmA, lbar, m0, kc, status);
+            tma_load_2d_pair(sa + 8192, &tmA, lbar, m0 + 64, kc, status);
           }
           if constexpr (!B_MN) {
-            tma_load_2d_pair(sb, &tmB, lbar, kc, n0);
+            tma_load_2d_pair(sb, &tmB, lbar, kc, n0, status);
           } else {
 #pragma unroll
             for (int j = 0; j < BN / 128; ++j)
-              tma_load_2d_pair(sb + j * 8192, &tmB, lbar, n0 + j * 64, kc);
+              tma_load_2d_pair(sb + j * 8192, &tmB, lbar, n0 + j * 64, kc, status);
           }
         }
       }

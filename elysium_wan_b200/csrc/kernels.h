@@ -108,7 +108,7 @@ int cross_entropy(const CeArgs& a, cudaStream_t stream);
 // gradient written over the fp16 exp(x - tile max) values in `buf` ([T][ld]).
 int ce_lse_finalize(const float* part, int nt, int ld_part, const float* tgt_logit,
                     const int64_t* targets, int T, int V, void* buf, int ld, float grad_scale,
-                    float* loss_rows, cudaStream_t stream);
+                    float* loss_rows, int* status, cudaStream_t stream);
 // out[0] = sum(x[0..n)) / n, fixed-order tree (deterministic).
 int mean_reduce(const float* x, int n, float* out, cudaStream_t stream);
 
@@ -117,10 +117,11 @@ struct EmbedArgs {
   const int64_t* idx;  // [B*S]
   const float* wte;  // [V][d] fp32 master
   const float* wpe;  // [S][d]
-  int T, S, d;
+  int T, S, d, V;
   void* out;  // [T][d] in boundary format out_fmt (bf16, fp16, or fp8 + 1x128 scales)
   int out_fmt;
   float* out_scale;
+  int* status;  // status record: a token id outside [0, V) is reported here
 };
 int embed_fwd(const EmbedArgs& a, cudaStream_t stream);
 
@@ -131,6 +132,7 @@ struct EmbedBwdArgs {
   int* order;  // [T] scratch: positions sorted by (token, position)
   float* dwte;  // [V][d] fp32 gradient (accumulated)
   float* dwpe;  // [S][d]
+  int* status;  // status record: a token id outside [0, V) is reported here
 };
 int embed_bwd(const EmbedBwdArgs& a, cudaStream_t stream);
 

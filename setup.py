@@ -35,15 +35,27 @@ NVCC = [
     "-U__CUDA_NO_BFLOAT16_CONVERSIONS__", "-U__CUDA_NO_BFLOAT16_OPERATORS__",
 ]
 
+
+def kernels(name: str, defines: list) -> CUDAExtension:
+    return CUDAExtension(
+        name=name,
+        sources=[os.path.join(CSRC, "bindings.cpp")] + [os.path.join(CSRC, f) for f in CU],
+        include_dirs=[os.path.join(HERE, CSRC)],
+        extra_compile_args={"cxx": ["-O3", "-std=c++17"] + defines, "nvcc": NVCC + defines},
+    )
+
+
+# EWB_KCHECK=1 builds `_C_kcheck` instead: the same kernels with bounds checks
+# (-DEWB_KCHECK) that record the failing site in the status record and skip
+# the access; `EWB_KCHECK=1` at run time loads it instead of `_C`. Build it in
+# its own temporary directory so the two flag sets do not rebuild each other:
+#     EWB_KCHECK=1 python setup.py build_ext --inplace --build-temp build/kcheck
+KCHECK = os.environ.get("EWB_KCHECK", "0") == "1"
+
 setup(
     name="elysium_wan_b200",
-    ext_modules=[
-        CUDAExtension(
-            name="elysium_wan_b200._C",
-            sources=[os.path.join(CSRC, "bindings.cpp")] + [os.path.join(CSRC, f) for f in CU],
-            include_dirs=[os.path.join(HERE, CSRC)],
-            extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC},
-        ),
+    ext_modules=[kernels("elysium_wan_b200._C_kcheck", ["-DEWB_KCHECK"])] if KCHECK else [
+        kernels("elysium_wan_b200._C", []),
         Extension(
             name="elysium_wan_b200._wire",
             sources=[os.path.join(CSRC, "wire", "wire.cpp")],
