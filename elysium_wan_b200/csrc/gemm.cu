@@ -799,7 +799,7 @@ template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, const GemmEpilogue ep, int M, int N,
-                     int K, int* status, int* sched) {
+                     int K, int* status, int* sched, int nfull, int ns, float* ws) {
   using Cfg = PairCfg<BN, EPI>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -815,6 +815,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   uint64_t* tq_empty = tq_full + kTileQueue;
   int* tile_ring = reinterpret_cast<int*>(tq_empty + kTileQueue);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tile_ring + kTileQueue);
+  int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  int* tail_cnt = sched + 2;  // arrivals per (tail tile, CTA rank)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -857,10 +859,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int num_n = (N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
   const int kblocks = (K + kBK - 1) / kBK;
+  // Units: tiles [0, nfull) whole, then each tail tile as `ns` K-splits (the
+  // last partial wave spread over every pair; ns = 1: no split).
+  const int num_units = nfull + (num_tiles - nfull) * ns;
 
-  // Tiles are claimed dynamically by the leader's producer (a pair that
-  // starts late takes fewer tiles) and published to both CTAs' roles through
-  // a ring in each CTA's shared memory; -1 ends.
+  // Units are claimed dynamically by the leader's producer (a pair that
+  // starts late takes fewer) and published to both CTAs' roles through a ring
+  // in each CTA's shared memory; -1 ends.
   auto next_tile = [&](int k) -> int {
     const int q = k % kTileQueue;
     if (!mbar_wait_cluster(&tq_full[q], (k / kTileQueue) & 1, status, kStatusTimeoutSmemFull))
@@ -879,7 +884,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         int t;
         if (lead) {
           t = atomicAdd(&sched[0], 1);
-          if (t >= num_tiles) t = -1;
+          if (t >= num_units) t = -1;
           const int q = k % kTileQueue;
           if (!mbar_wait(&tq_empty[q], ((k / kTileQueue) & 1) ^ 1, status,
                          kStatusTimeoutSmemEmpty)) {
@@ -897,11 +902,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           took_tile(k);
         }
         if (t < 0) break;
+        const Unit un = decode_unit(t, nfull, ns, kblocks);
         int mb, nb;
-        tile_coords(t, num_m, num_n, mb, nb);
+        tile_coords(un.tile, num_m, num_n, mb, nb);
         const int m0 = mb * 2 * kBM + static_cast<int>(rank) * kBM;
         const int n0 = nb * BN + static_cast<int>(rank) * (BN / 2);
-        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+        for (int kb = un.kb0; kb < un.kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, status, kStatusTimeoutSmemEmpty)) {
@@ -946,12 +952,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int t = next_tile(k);
         took_tile(k);
         if (t < 0) break;
+        const Unit un = decode_unit(t, nfull, ns, kblocks);
         const int b = k & 1;
         const uint32_t use = static_cast<uint32_t>(k >> 1);
         if (!mbar_wait(&tempty[b], (use & 1) ^ 1, status, kStatusTimeoutTmemEmpty)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * BN);
-        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+        for (int kb = un.kb0; kb < un.kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(&full[s], ph, status, kStatusTimeoutSmemFull)) {
@@ -967,7 +974,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                      : sdesc_sw128(a_addr + kk * 32, 16, 1024);
             const uint64_t bd = B_MN ? sdesc_sw128(b_addr + kk * 2048, 8192, 1024)
                                      : sdesc_sw128(b_addr + kk * 32, 16, 1024);
-            umma_f16_pair(d_tmem, ad, bd, IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
+            umma_f16_pair(d_tmem, ad, bd, IDESC, (kb > un.kb0 || kk > 0) ? 1u : 0u);
           }
           // this stage is free again in both CTAs once these MMAs complete
           umma_commit_pair(peer_smem(smem_u32(&empty[s]), 0));
@@ -991,15 +998,43 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) took_tile(k);
       if (t < 0) break;
+      const Unit un = decode_unit(t, nfull, ns, kblocks);
       int mb, nb;
-      tile_coords(t, num_m, num_n, mb, nb);
+      tile_coords(un.tile, num_m, num_n, mb, nb);
       const int b = k & 1;
       const uint32_t use = static_cast<uint32_t>(k >> 1);
       if (!mbar_wait(&tfull[b], use & 1, status, kStatusTimeoutTmemFull)) break;
       tc_fence_after();
       const uint32_t taddr =
           tmem_base + static_cast<uint32_t>(b * BN) + (static_cast<uint32_t>(q * 32) << 16);
-      const AccSrc acc{taddr, nullptr, 1, row};
+      AccSrc acc{taddr, nullptr, 1, row};
+      if (un.ns > 1) {
+        // K-split tail unit: this CTA's half-tile partial goes to the
+        // workspace and the accumulator is released; the CTA whose split of
+        // this half lands last sums all of them in split order and runs the
+        // epilogue (the same sum whichever CTA finishes last).
+        const int tail = un.tile - nfull;
+        const int slot = tail * 2 + static_cast<int>(rank);
+        float* tile_ws = ws + static_cast<size_t>(slot) * un.ns * kBM * BN;
+        write_partial<BN>(taddr, tile_ws + static_cast<size_t>(un.split) * kBM * BN, row);
+        __threadfence();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(peer_smem(smem_u32(&tempty[b]), 0));
+        named_bar_sync(2, 128);
+        if (warp == 2 && lane == 0) {
+          const int prev = atomicAdd(&tail_cnt[slot], 1);
+          const bool last = prev == un.ns - 1;
+          if (last) tail_cnt[slot] = 0;  // every split arrived: ready for the next launch
+          __threadfence();
+          *reinterpret_cast<volatile int*>(last_flag) = last ? 1 : 0;
+        }
+        named_bar_sync(2, 128);
+        const bool last = *reinterpret_cast<volatile int*>(last_flag) != 0;
+        named_bar_sync(2, 128);  // the flag is read before the next unit rewrites it
+        if (!last) continue;
+        acc = AccSrc{0u, tile_ws, un.ns, row};
+      }
       const int m0 = mb * 2 * kBM + static_cast<int>(rank) * kBM;
       if constexpr (EpiTraits<EPI>::kTma) {
         epilogue_tile_tma<EPI, BN>(acc, row, m0, nb * BN, N, ep, &tmC, out_smem, leader_thread,
@@ -1007,6 +1042,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       } else {
         epilogue_tile_regs<EPI, BN>(acc, m0 + row, nb * BN, M, N, ep);
       }
+      if (un.ns > 1) continue;  // the accumulator was released above
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(peer_smem(smem_u32(&tempty[b]), 0));
@@ -1150,6 +1186,29 @@ int split_plan(long tiles, int sms, int kblocks, int* full) {
   return ns;
 }
 
+// K-split of the pair kernel's last partial wave: when the tiles leave a
+// tail of r <= pairs / 4 tiles after their whole waves (or the whole grid is
+// that small), each tail tile splits along K into ns = pairs / r parts, so the
+// tail takes about 1 / ns of a tile instead of a whole tile while most pairs
+// idle. A 2048 x 5120 output is 160 pair tiles of 256 x 256: two waves of 74
+// pairs and a tail of 12 tiles, which would otherwise hold the launch for a
+// third tile time (72 % of the machine busy). The whole tiles are claimed
+// first, so the split units start when every pair finishes its whole tiles.
+// Returns ns (1: no split) and the number of whole tiles in `full`.
+int pair_split_plan(bool allow, long tiles, int pairs, int kblocks, int bn, int* full) {
+  *full = static_cast<int>(tiles);
+  if (!allow || pairs < 2) return 1;
+  const long r = tiles >= pairs ? tiles % pairs : tiles;
+  if (r == 0 || 4 * r > pairs) return 1;
+  int ns = static_cast<int>(pairs / r);
+  ns = std::min(ns, kblocks / kMinSplitKb);
+  ns = std::min(ns, 16);
+  // workspace: r tiles x ns splits x 2 CTAs x [kBM][bn] fp32
+  if (ns < 2 || r * ns * 2 * bn > static_cast<long>(kMaxTailUnits) * 256) return 1;
+  *full = static_cast<int>(tiles - r);
+  return ns;
+}
+
 // EWB_TRACE=1 prints each launch step to stderr (flushed), to localise host faults.
 bool trace_on() {
   static int on = -1;
@@ -1250,10 +1309,15 @@ int launch_pair(const GemmArgs& g, cudaStream_t stream) {
   const int grid = static_cast<int>(std::max(2L, std::min(2 * tiles, static_cast<long>(sms))));
   EWB_TRACE("[gemm-pair] BN=%d a_mn=%d b_mn=%d epi=%d M=%d N=%d K=%d grid=%d smem=%d\n", BN,
             (int)A_MN, (int)B_MN, EPI, g.M, g.N, g.K, grid, Cfg::SMEM);
-  const StreamState st = stream_state(stream, false);
+  const int kblocks = (g.K + kBK - 1) / kBK;
+  int nfull = static_cast<int>(tiles);
+  const int ns = pair_split_plan(g.split != 0, tiles, sms / 2, kblocks, BN, &nfull);
+  const StreamState st = stream_state(stream, ns > 1);
   if (st.counters == nullptr) return kGemmErrLaunch;
+  const bool split = ns > 1 && st.ws != nullptr;
   kern<<<grid, kThreads, Cfg::SMEM, stream>>>(ma, mbm, mc, g.ep, g.M, g.N, g.K, g.status,
-                                              st.counters);
+                                              st.counters, split ? nfull : static_cast<int>(tiles),
+                                              split ? ns : 1, st.ws);
   const cudaError_t err = cudaGetLastError();
   return err == cudaSuccess ? kGemmOk : kGemmErrLaunch;
 }
@@ -1407,7 +1471,10 @@ int gemm_pick_pair_bn(int M, int N, int K, int single_bn, bool split, bool b_mn)
   for (int i = 0; i < 3; ++i) {
     if (pw[i] == 192 && b_mn) continue;
     const long tiles = static_cast<long>((M + 2 * kBM - 1) / (2 * kBM)) * ((N + pw[i] - 1) / pw[i]);
-    const double waves = static_cast<double>((tiles + pairs - 1) / pairs);
+    int full = 0;
+    const int ns = pair_split_plan(split, tiles, pairs, (K + kBK - 1) / kBK, pw[i], &full);
+    const double waves = ns > 1 ? static_cast<double>(full / pairs) + 1.0 / ns + 0.05
+                                : static_cast<double>((tiles + pairs - 1) / pairs);
     // a pair tile is two single-CTA tiles of work per SM pair
     const double t = waves * pw[i] / prate[i];
     if (t < best_t * 0.97) {
@@ -1448,9 +1515,9 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
       return kGemmErrShape;
     bn = 256;
   }
-  // CTA pairs: whole operand pairs only (no second pair, no K-split), tiles
-  // of 256 rows; gemm_pair_mode() 0 = never, 1 = always when supported,
-  // 2 = when the wave model prefers it.
+  // CTA pairs: whole operand pairs only (no second pair), tiles of 256 rows,
+  // a small last wave split along K (pair_split_plan); gemm_pair_mode() 0 =
+  // never, 1 = always when supported, 2 = when the wave model prefers it.
   if (g.K2 == 0 && gemm_pair_mode() != 0) {
     int pbn = 0;
     if (gemm_pair_mode() == 1) {

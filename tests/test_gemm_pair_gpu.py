@@ -146,3 +146,55 @@ def test_pair_gemm_auto_choice_wide_outputs(pair):
         out = torch.empty(M, N, dtype=torch.float32, device=pair)
         ops.gemm(x, w.t().contiguous() if b_mn else w, out, ops.EPI_F32, b_mn=b_mn)
         assert rel_err(out, ref) < 1e-5, (M, N, K, b_mn)
+
+
+@pytest.mark.parametrize("M,N,K", [(2048, 5120, 2048), (512, 1024, 4096)])
+@pytest.mark.parametrize("kind", ["f32", "bf16", "dx", "dw_fold", "resid"])
+def test_pair_tail_split(pair, M, N, K, kind):
+    """Grids whose last wave is a small tail (160 tiles on 74 pairs: 12 left)
+    or small altogether split those tiles along K over every pair; the result
+    equals fp32, is the same run to run, and equals the unsplit launch up to
+    fp32 summation order."""
+    torch.manual_seed(7)
+    ext = ops.ext()
+    x, w = bf(M, K, dev=pair), bf(N, K, dev=pair, scale=0.05)
+    b = torch.randn(N, device=pair)
+
+    def run():
+        if kind == "f32":
+            out = torch.empty(M, N, device=pair)
+            ops.gemm(x, w, out, ops.EPI_F32)
+            return out, x.float() @ w.float().t(), 1e-5
+        if kind == "bf16":
+            out = torch.empty(M, N, dtype=torch.bfloat16, device=pair)
+            ops.gemm(x, w, out, ops.EPI_BF16, bias=b)
+            return out, x.float() @ w.float().t() + b, 8e-3
+        if kind == "dx":  # dX = dY W with W [K_out, N_in] read MN-major
+            wt = w.t().contiguous()  # [K, N]
+            out = torch.empty(M, N, dtype=torch.bfloat16, device=pair)
+            ops.gemm(x, wt, out, ops.EPI_BF16, b_mn=True)
+            return out, x.float() @ wt.float(), 8e-3
+        if kind == "dw_fold":  # dW [M_out, N] += dY^T X, both MN-major
+            dy, xx = bf(K, M, dev=pair), bf(K, N, dev=pair)
+            g0 = torch.randn(M, N, device=pair)
+            out = g0.clone()
+            ops.gemm(dy, xx, out, ops.EPI_ACC_F32, a_mn=True, b_mn=True, beta=1.0)
+            return out, g0 + dy.float().t() @ xx.float(), 1e-5
+        r = bf(M, N, dev=pair)
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=pair)
+        ops.gemm(x, w, out, ops.EPI_RESID, bias=b, resid=r)
+        return out, x.float() @ w.float().t() + b + r.float(), 8e-3
+
+    torch.manual_seed(8)
+    a, ref, tol = run()
+    torch.manual_seed(8)
+    a2, _, _ = run()
+    assert rel_err(a, ref) < tol
+    assert torch.equal(a, a2)
+    ext.set_gemm_split(False)
+    try:
+        torch.manual_seed(8)
+        c, _, _ = run()
+    finally:
+        ext.set_gemm_split(True)
+    assert rel_err(a, c) < (1e-6 if a.dtype == torch.float32 else 8e-3)
