@@ -197,4 +197,4 @@ def test_pair_tail_split(pair, M, N, K, kind):
         c, _, _ = run()
     finally:
         ext.set_gemm_split(True)
-    assert rel_err(a, c) < (1e-6 if a.dtype == torch.float32 else 8e-3)
+    assert rel_err(a, c) < (1e-5 if a.dtype == torch.float32 else 8e-3)
