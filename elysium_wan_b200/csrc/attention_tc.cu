@@ -55,25 +55,6 @@ __device__ __forceinline__ float ex2f(float x) {
   return y;
 }
 
-// 2^x for x <= 0 on the FMA and integer pipes, so that half of each row's
-// exponentials leave the MUFU pipe, which bounds the softmax otherwise.
-// Range reduction x = j + f: adding 1.5 * 2^23 rounds x to the integer j in
-// the low mantissa bits (exactly, for |x| < 2^22), and f = x - j lies in
-// [-0.5, 0.5]. 2^f is a cubic fitted on [-0.5, 0.5] for the least largest
-// relative error (Lawson's iteratively reweighted least squares; 7.5e-5 in
-// fp32 Horner form, well under the 2^-9 of the bf16 P it feeds). j goes into
-// the exponent field by an integer add. Below -126 the result is 0, as the
-// flush-to-zero MUFU instruction gives there.
-__device__ __forceinline__ float ex2_poly(float x) {
-  const float t = x + 12582912.0f;  // 1.5 * 2^23
-  const float jf = t - 12582912.0f;
-  const float f = x - jf;
-  const float p = fmaf(fmaf(fmaf(0.05517132f, f, 0.24261054f), f, 0.69326097f), f, 0.99992812f);
-  const int j = __float_as_int(t) - 0x4B400000;
-  const float y = __int_as_float(__float_as_int(p) + (j << 23));
-  return x < -126.0f ? 0.0f : y;
-}
-
 __global__ void __launch_bounds__(kTcFwdThreads, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qk,
                        const __grid_constant__ CUtensorMap map_v, __nv_bfloat16* __restrict__ o,
@@ -297,7 +278,7 @@ __global__ void __launch_bounds__(kTcFwdThreads, 1)
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const float p0 = ex2f(__uint_as_float(v[c * 8 + 2 * i]) - mnew);
-          const float p1 = ex2_poly(__uint_as_float(v[c * 8 + 2 * i + 1]) - mnew);
+          const float p1 = ex2f(__uint_as_float(v[c * 8 + 2 * i + 1]) - mnew);
           rs += p0 + p1;
           pk[i] = pack_bf16x2(p0, p1);
         }
@@ -581,8 +562,7 @@ __global__ void __launch_bounds__(kBwThreads, 1)
           for (int z = 0; z < 2; ++z) {
             const int ql = u4 * 8 + 2 * e + z;  // within this half
             const int q = q0 + ql;
-            const float xa = __uint_as_float(sv[ql]) * scale_log2 - Ls[q];
-            float p = z ? ex2_poly(xa) : ex2f(xa);
+            float p = ex2f(__uint_as_float(sv[ql]) * scale_log2 - Ls[q]);
             if (kpos > i * 64 + q) p = 0.f;
             pp[z] = p;
             dd[z] = p * (__uint_as_float(pv[ql]) - Ds[q]);
@@ -826,8 +806,7 @@ __global__ void __launch_bounds__(kBwThreads, 1)
       const bool diag = (j == qb);
 #pragma unroll
       for (int k = 0; k < 64; ++k) {
-        const float xa = __uint_as_float(sv[k]) * scale_log2 - lr;
-        float p = (k & 1) ? ex2_poly(xa) : ex2f(xa);
+        float p = ex2f(__uint_as_float(sv[k]) * scale_log2 - lr);
         if (diag && k0 + k > r) p = 0.f;
         sv[k] = __float_as_uint(p);
       }

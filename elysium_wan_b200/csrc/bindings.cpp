@@ -752,6 +752,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_pick_bn", &gemm_pick_bn);
   m.def("set_gemm_split", &set_gemm_split);
   m.def("set_gemm_pair", [](int64_t mode) { ewb::set_gemm_pair_mode(static_cast<int>(mode)); });
+  m.def("set_gemm_pair_split", [](bool on) { ewb::set_gemm_pair_split(on); });
   m.def("gemm_peer_scatter", &gemm_peer_scatter);
   m.def("gemm_pair", &gemm_pair);
   m.def("gemm_lse", &gemm_lse);

@@ -1195,9 +1195,24 @@ int split_plan(long tiles, int sms, int kblocks, int* full) {
 // third tile time (72 % of the machine busy). The whole tiles are claimed
 // first, so the split units start when every pair finishes its whole tiles.
 // Returns ns (1: no split) and the number of whole tiles in `full`.
+//
+// Off unless EWB_GEMM_PAIR_SPLIT=1: measured on B200 it made the launches it
+// touched slower (5120-wide projection 0.162 vs 0.098 ms, qkv weight
+// gradient 0.397 vs 0.272 ms). Each thread writes and re-reads its whole
+// accumulator row of every partial (1 KB strided rows, uncoalesced), and the
+// last arrival's fixup sits on the launch's critical path.
+int& pair_split_flag() {
+  static int on = [] {
+    const char* e = std::getenv("EWB_GEMM_PAIR_SPLIT");
+    return (e != nullptr && e[0] == '1') ? 1 : 0;
+  }();
+  return on;
+}
+bool pair_split_enabled() { return pair_split_flag() != 0; }
+
 int pair_split_plan(bool allow, long tiles, int pairs, int kblocks, int bn, int* full) {
   *full = static_cast<int>(tiles);
-  if (!allow || pairs < 2) return 1;
+  if (!allow || !pair_split_enabled() || pairs < 2) return 1;
   const long r = tiles >= pairs ? tiles % pairs : tiles;
   if (r == 0 || 4 * r > pairs) return 1;
   int ns = static_cast<int>(pairs / r);
@@ -1442,6 +1457,8 @@ int& gemm_pair_mode() {
   }();
   return mode;
 }
+
+void set_gemm_pair_split(bool on) { pair_split_flag() = on ? 1 : 0; }
 
 void set_gemm_pair_mode(int mode) { gemm_pair_mode() = mode; }
 

@@ -94,6 +94,8 @@ int gemm_launch(const GemmArgs& args, cudaStream_t stream);
 int gemm_pick_bn(int M, int N, int K, bool split);
 // CTA-pair (cta_group::2) tiles: 0 = never, 1 = whenever supported, 2 = when
 // the wave model prefers them (initial value from EWB_GEMM_PAIR, default 2).
+// K-split of the pair kernel's small last wave (off by default; EWB_GEMM_PAIR_SPLIT=1).
+void set_gemm_pair_split(bool on);
 void set_gemm_pair_mode(int mode);
 
 // bf16 2D tensor map with 128-byte swizzle (inner = contiguous extent in

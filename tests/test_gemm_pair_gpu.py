@@ -157,6 +157,7 @@ def test_pair_tail_split(pair, M, N, K, kind):
     fp32 summation order."""
     torch.manual_seed(7)
     ext = ops.ext()
+    ext.set_gemm_pair_split(True)  # off by default (measured slower); its bits are still tested
     x, w = bf(M, K, dev=pair), bf(N, K, dev=pair, scale=0.05)
     b = torch.randn(N, device=pair)
 
@@ -197,4 +198,5 @@ def test_pair_tail_split(pair, M, N, K, kind):
         c, _, _ = run()
     finally:
         ext.set_gemm_split(True)
+        ext.set_gemm_pair_split(False)
     assert rel_err(a, c) < (1e-5 if a.dtype == torch.float32 else 8e-3)
