@@ -52,6 +52,9 @@ constexpr int kGroupM = 16;
 template <int EPI>
 struct EpiTraits {
   static constexpr bool kTma = (EPI == kEpiBf16 || EPI == kEpiF32 || EPI == kEpiAccF32);
+  // shared-memory staging: TMA epilogues, and the peer scatter (rows regrouped
+  // so each warp stores whole 128-byte row segments)
+  static constexpr bool kStage = kTma || EPI == kEpiAccF32Peer;
 };
 
 // Tile widths: 256 (the default), 192 (an output 5120 wide splits into 27
@@ -64,9 +67,9 @@ struct GemmCfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   // Two 16 KB staging buffers for the TMA epilogues. (Four buffers with three
   // operand stages made the 256-wide gradient fold slower: 0.409 vs 0.372 ms.)
-  static constexpr int OUT_BUFS = EpiTraits<EPI>::kTma ? 2 : 0;
+  static constexpr int OUT_BUFS = EpiTraits<EPI>::kStage ? 2 : 0;
   static constexpr int OUT_BYTES = OUT_BUFS * 16384;
-  static constexpr int STAGES = (BN == 256) ? 4 : (BN == 192) ? (EpiTraits<EPI>::kTma ? 4 : 5) : 6;
+  static constexpr int STAGES = (BN == 256) ? 4 : (BN == 192) ? (EpiTraits<EPI>::kStage ? 4 : 5) : 6;
   static constexpr int SMEM = STAGES * STAGE_BYTES + OUT_BYTES + 1024 /*align*/ + 256 /*barriers*/;
   // two accumulators of BN columns; the allocation is a power of two
   static constexpr int TMEM_COLS = (BN == 192) ? 512 : 2 * BN;
@@ -456,6 +459,66 @@ __device__ __forceinline__ void epilogue_tile_regs(const AccSrc& acc, int gm, in
   }
 }
 
+// ZeRO-1 reduce-scatter from the epilogue (kEpiAccF32Peer): this replica's
+// final partial of a tile (its earlier microbatches, already folded in `out`,
+// plus the accumulator) goes straight into the owning replica's slot over
+// NVLink. A thread holds one accumulator row, so storing from registers
+// would send 32 rows' 16-byte pieces per warp instruction; instead each warp
+// parks its 32 rows x 32 columns in shared memory (rows padded to 36 floats)
+// and then writes them out row segment by row segment: 8 lanes cover one
+// row's 128 contiguous bytes, a warp instruction four rows, for both the
+// local partial it reads and the peer slot it writes.
+template <int BN>
+__device__ __forceinline__ void epilogue_tile_peer(const AccSrc& acc, int row, int m0, int nbase,
+                                                   int M, int N, const GemmEpilogue& ep,
+                                                   uint8_t* out_smem) {
+  const int warp_q = row >> 5, lane = row & 31;
+  float* stage = reinterpret_cast<float*>(out_smem) + warp_q * (32 * 36);
+  const PeerScatter& ps = ep.peer;
+  const int sub = lane >> 3;      // which of 4 rows this lane serves per pass
+  const int c4 = (lane & 7) * 4;  // its 4 columns within the 32-column chunk
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 32) {
+    float f[32];
+    acc_ld32<BN>(acc, c, f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      *reinterpret_cast<float4*>(stage + lane * 36 + 4 * j) =
+          make_float4(f[4 * j], f[4 * j + 1], f[4 * j + 2], f[4 * j + 3]);
+    __syncwarp();
+    const int n = nbase + c + c4;
+#pragma unroll 1
+    for (int pass = 0; pass < 8; ++pass) {
+      const int lr = pass * 4 + sub;  // row within this warp's 32
+      const int gm = m0 + warp_q * 32 + lr;
+      if (gm < M && n < N) {
+        const float4 a = *reinterpret_cast<const float4*>(stage + lr * 36 + c4);
+        const float* lp = reinterpret_cast<const float*>(ep.out) + static_cast<size_t>(gm) * ep.ldo + n;
+        const long long f0 = ps.flat_off + static_cast<long long>(gm) * ep.ldo + n;
+        int k = 0;
+        while (k + 1 < ps.world && f0 >= ps.shard_lo[k + 1]) ++k;
+        const int valid = min(4, N - n);
+        const bool one_owner = (k + 1 >= ps.world) || (f0 + valid <= ps.shard_lo[k + 1]);
+        float* dst = ps.slots[k] + static_cast<long long>(ps.rank) * ps.slot_stride + (f0 - ps.shard_lo[k]);
+        if (one_owner && valid == 4 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0 &&
+            (reinterpret_cast<uintptr_t>(lp) & 15) == 0) {
+          const float4 l4 = __ldcs(reinterpret_cast<const float4*>(lp));
+          *reinterpret_cast<float4*>(dst) = make_float4(l4.x + a.x, l4.y + a.y, l4.z + a.z, l4.w + a.w);
+        } else {
+          const float av[4] = {a.x, a.y, a.z, a.w};
+          for (int i = 0; i < valid; ++i) {
+            const long long fi = f0 + i;
+            while (k + 1 < ps.world && fi >= ps.shard_lo[k + 1]) ++k;
+            ps.slots[k][static_cast<long long>(ps.rank) * ps.slot_stride + (fi - ps.shard_lo[k])] =
+                lp[i] + av[i];
+          }
+        }
+      }
+    }
+    __syncwarp();  // the next chunk overwrites this warp's staging rows
+  }
+}
+
 // TMA-staged epilogue: each 128-byte-wide column chunk of the tile (32 fp32 or
 // 64 bf16 columns x 128 rows) goes TMEM -> registers -> 128B-swizzled shared
 // memory -> one bulk tensor store (or fp32 reduce-add for the gradient fold).
@@ -733,7 +796,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!last) continue;
         acc = AccSrc{0u, tile_ws, un.ns, row};
       }
-      if constexpr (EpiTraits<EPI>::kTma) {
+      if constexpr (EPI == kEpiAccF32Peer) {
+        epilogue_tile_peer<BN>(acc, row, mb * kBM, nb * BN, M, N, ep, out_smem);
+      } else if constexpr (EpiTraits<EPI>::kTma) {
         epilogue_tile_tma<EPI, BN>(acc, row, mb * kBM, nb * BN, N, ep, &tmC, out_smem, leader,
                                    chunk);
       } else {
@@ -784,7 +849,7 @@ struct PairCfg {
   static constexpr int A_BYTES = kBM * kBK * 2;
   static constexpr int B_BYTES = (BN / 2) * kBK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int OUT_BUFS = EpiTraits<EPI>::kTma ? 2 : 0;
+  static constexpr int OUT_BUFS = EpiTraits<EPI>::kStage ? 2 : 0;
   static constexpr int OUT_BYTES = OUT_BUFS * 16384;
   static constexpr int STAGES = (227 * 1024 - OUT_BYTES - 1536) / STAGE_BYTES > 8
                                     ? 8
@@ -1036,7 +1101,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         acc = AccSrc{0u, tile_ws, un.ns, row};
       }
       const int m0 = mb * 2 * kBM + static_cast<int>(rank) * kBM;
-      if constexpr (EpiTraits<EPI>::kTma) {
+      if constexpr (EPI == kEpiAccF32Peer) {
+        epilogue_tile_peer<BN>(acc, row, m0, nb * BN, M, N, ep, out_smem);
+      } else if constexpr (EpiTraits<EPI>::kTma) {
         epilogue_tile_tma<EPI, BN>(acc, row, m0, nb * BN, N, ep, &tmC, out_smem, leader_thread,
                                    chunk);
       } else {
