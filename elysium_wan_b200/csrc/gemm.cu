@@ -487,32 +487,53 @@ __device__ __forceinline__ void epilogue_tile_peer(const AccSrc& acc, int row, i
           make_float4(f[4 * j], f[4 * j + 1], f[4 * j + 2], f[4 * j + 3]);
     __syncwarp();
     const int n = nbase + c + c4;
-#pragma unroll 1
+    // All eight rows' local-partial loads go out before any store, so their
+    // latencies overlap instead of adding up pass by pass.
+    float4 l4[8];
+    float* dst[8];
+    unsigned fast = 0u, live = 0u;
+#pragma unroll
     for (int pass = 0; pass < 8; ++pass) {
-      const int lr = pass * 4 + sub;  // row within this warp's 32
-      const int gm = m0 + warp_q * 32 + lr;
+      const int gm = m0 + warp_q * 32 + pass * 4 + sub;
+      dst[pass] = nullptr;
       if (gm < M && n < N) {
-        const float4 a = *reinterpret_cast<const float4*>(stage + lr * 36 + c4);
+        live |= 1u << pass;
         const float* lp = reinterpret_cast<const float*>(ep.out) + static_cast<size_t>(gm) * ep.ldo + n;
         const long long f0 = ps.flat_off + static_cast<long long>(gm) * ep.ldo + n;
         int k = 0;
         while (k + 1 < ps.world && f0 >= ps.shard_lo[k + 1]) ++k;
-        const int valid = min(4, N - n);
-        const bool one_owner = (k + 1 >= ps.world) || (f0 + valid <= ps.shard_lo[k + 1]);
-        float* dst = ps.slots[k] + static_cast<long long>(ps.rank) * ps.slot_stride + (f0 - ps.shard_lo[k]);
-        if (one_owner && valid == 4 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0 &&
+        const bool one_owner = (k + 1 >= ps.world) || (f0 + 4 <= ps.shard_lo[k + 1]);
+        float* d = ps.slots[k] + static_cast<long long>(ps.rank) * ps.slot_stride + (f0 - ps.shard_lo[k]);
+        if (one_owner && n + 4 <= N && (reinterpret_cast<uintptr_t>(d) & 15) == 0 &&
             (reinterpret_cast<uintptr_t>(lp) & 15) == 0) {
-          const float4 l4 = __ldcs(reinterpret_cast<const float4*>(lp));
-          *reinterpret_cast<float4*>(dst) = make_float4(l4.x + a.x, l4.y + a.y, l4.z + a.z, l4.w + a.w);
-        } else {
-          const float av[4] = {a.x, a.y, a.z, a.w};
-          for (int i = 0; i < valid; ++i) {
-            const long long fi = f0 + i;
-            while (k + 1 < ps.world && fi >= ps.shard_lo[k + 1]) ++k;
-            ps.slots[k][static_cast<long long>(ps.rank) * ps.slot_stride + (fi - ps.shard_lo[k])] =
-                lp[i] + av[i];
-          }
+          fast |= 1u << pass;
+          dst[pass] = d;
+          l4[pass] = __ldcs(reinterpret_cast<const float4*>(lp));
         }
+      }
+    }
+#pragma unroll
+    for (int pass = 0; pass < 8; ++pass) {
+      if (!(live & (1u << pass))) continue;
+      const int lr = pass * 4 + sub;  // row within this warp's 32
+      const float4 a = *reinterpret_cast<const float4*>(stage + lr * 36 + c4);
+      if (fast & (1u << pass)) {
+        *reinterpret_cast<float4*>(dst[pass]) =
+            make_float4(l4[pass].x + a.x, l4[pass].y + a.y, l4[pass].z + a.z, l4[pass].w + a.w);
+        continue;
+      }
+      // ragged edge or a shard boundary inside these four columns
+      const int gm = m0 + warp_q * 32 + lr;
+      const float* lp = reinterpret_cast<const float*>(ep.out) + static_cast<size_t>(gm) * ep.ldo + n;
+      const long long f0 = ps.flat_off + static_cast<long long>(gm) * ep.ldo + n;
+      const int valid = min(4, N - n);
+      const float av[4] = {a.x, a.y, a.z, a.w};
+      int k = 0;
+      for (int q = 0; q < valid; ++q) {
+        const long long fi = f0 + q;
+        while (k + 1 < ps.world && fi >= ps.shard_lo[k + 1]) ++k;
+        ps.slots[k][static_cast<long long>(ps.rank) * ps.slot_stride + (fi - ps.shard_lo[k])] =
+            lp[q] + av[q];
       }
     }
     __syncwarp();  // the next chunk overwrites this warp's staging rows
