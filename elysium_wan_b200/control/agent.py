@@ -297,6 +297,13 @@ class WorkerAgent:
         env.update(PINNED_ENV)
         env.setdefault("CUDA_MODULE_LOADING", "EAGER")
         env["PYTHONPATH"] = ROOT + os.pathsep + env.get("PYTHONPATH", "")
+        # Shared WAN budgets of this run and attempt: every stage process on
+        # this host paces through the same bucket files (a host-wide path, so
+        # agents of one host share them; a new attempt starts fresh buckets).
+        import tempfile
+
+        env["EWB_PACER_DIR"] = os.path.join(tempfile.gettempdir(), f"ewb-pacers-{os.getuid()}",
+                                            f"{run_id}-a{attempt}")
         cmd = [sys.executable, "-m", "elysium_wan_b200.runtime.stage_main", "--spec", sp,
                "--rank", str(stage), "--peer", str(peer), "--timeout", str(hdr.get("timeout", 120))]
         self.assign = dict(hdr, spec_path=sp, dir=d)

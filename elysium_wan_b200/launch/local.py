@@ -47,6 +47,8 @@ def run_local(spec, timeout: float = 1800.0, log_dir: str | None = None, extra_e
     # Load every kernel at context creation: a module loaded lazily while an
     # NCCL receive is pending can wait on that receive (cross-rank deadlock).
     env.setdefault("CUDA_MODULE_LOADING", "EAGER")
+    # shared WAN budgets (NIC, uplink) of this run live in one directory
+    env["EWB_PACER_DIR"] = os.path.join(os.path.abspath(spec.out_dir), ".pacers")
     if extra_env:
         env.update(extra_env)
     procs = []

@@ -42,11 +42,15 @@ class _Shim:
     """Sender-side WAN emulation for one outgoing link: a FIFO worker thread
     that sleeps latency + bytes/rate (+ jitter) and then sends."""
 
-    def __init__(self, link: dict):
+    def __init__(self, link: dict, tag: str = "run"):
+        from elysium_wan_b200.transport.pacer import link_buckets
+
         self.lat = float(link.get("latency_ms", 0.0)) / 1000.0
         self.rate = float(link.get("bw_mbps", 0.0)) * 1e6 / 8.0
         self.jit = float(link.get("jitter_ms", 0.0)) / 1000.0
         self.rng = random.Random(int(link.get("jitter_seed", 0)))
+        # shared budgets (a NIC, a site pair's uplink) this link's frames cross
+        self.budgets = link_buckets(link, tag)
         self.q: queue.Queue = queue.Queue()
         self.busy_until = 0.0
         self.err: Exception | None = None
@@ -55,7 +59,7 @@ class _Shim:
 
     @property
     def active(self) -> bool:
-        return self.lat > 0 or self.rate > 0
+        return self.lat > 0 or self.rate > 0 or bool(self.budgets)
 
     def submit(self, fn, nbytes: int):
         self.q.put((fn, nbytes, time.monotonic()))
@@ -69,7 +73,12 @@ class _Shim:
             try:
                 start = max(self.busy_until, t_in)
                 ser = nbytes / self.rate if self.rate > 0 else 0.0
-                self.busy_until = start + ser
+                end = start + ser
+                # the frame crosses every shared budget at once: it has left
+                # when the slowest of them has carried it
+                for b in self.budgets:
+                    end = max(end, b.reserve(nbytes))
+                self.busy_until = end
                 jit = self.rng.uniform(0, self.jit) if self.jit > 0 else 0.0
                 due = self.busy_until + self.lat + jit
                 d = due - time.monotonic()
@@ -133,8 +142,10 @@ class PipeComm:
         self.grad_dtype = torch.bfloat16 if self.cuda else torch.float32  # boundary gradients
         link = spec.links[stage] if stage < len(spec.links) else {}
         back = spec.links[stage - 1] if stage > 0 and stage - 1 < len(spec.links) else {}
-        self.shim_next = _Shim(link) if not self.cuda else None
-        self.shim_prev = _Shim(back) if not self.cuda else None
+        from elysium_wan_b200.transport.pacer import reverse_link
+
+        self.shim_next = _Shim(link, spec.tag) if not self.cuda else None
+        self.shim_prev = _Shim(reverse_link(back), spec.tag) if not self.cuda else None
         self.bytes_sent = 0
         self.frames = 0
         if world > 1:

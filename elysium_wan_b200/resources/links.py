@@ -219,6 +219,11 @@ class Emulation:
     default: Link = field(default_factory=lambda: Link(0.0, 0.0))
     pairs: dict = field(default_factory=dict)  # "A|B" (sorted) -> {"rtt_ms", "mbps"}
     intra: Link | None = None
+    # Shared-pacer mode (this engine's profile keys "nic_mbps" and "shared"):
+    # the node's NIC rate shared by all its connections, and whether flows
+    # between two regions share one uplink per direction.
+    nic_mbps: float = 0.0
+    shared: bool = False
 
     @staticmethod
     def from_profile(region: str, prof: dict | None) -> "Emulation":
@@ -230,7 +235,9 @@ class Emulation:
         return Emulation(region, enabled=bool(prof),
                          default=link(prof.get("inter") or {}),
                          pairs=dict(prof.get("pairs") or {}),
-                         intra=link(prof["intra"]) if prof.get("intra") else None)
+                         intra=link(prof["intra"]) if prof.get("intra") else None,
+                         nic_mbps=float(prof.get("nic_mbps") or 0.0),
+                         shared=bool(prof.get("shared", False)))
 
     def link_to(self, region: str) -> Link:
         ent = self.pairs.get("|".join(sorted((self.region or "", region or ""))))

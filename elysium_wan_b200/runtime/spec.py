@@ -33,6 +33,14 @@ class LinkCfg:
     bw_mbps: float = 0.0
     jitter_ms: float = 0.0
     jitter_seed: int = 0
+    # Shared budgets (transport/pacer.py), off when the key is empty: the
+    # sender's NIC, the site pair's uplink in this direction, the receiver's NIC.
+    egress_key: str = ""
+    egress_mbps: float = 0.0
+    uplink_key: str = ""
+    uplink_mbps: float = 0.0
+    ingress_key: str = ""
+    ingress_mbps: float = 0.0
 
 
 @dataclass

@@ -76,9 +76,22 @@ def memory_order(spec: JobSpec, nodes) -> list | None:
 
 
 def _hop(src, dst, emulations):
-    """Shim settings of the hop src -> dst from src's emulation profile."""
-    link = emulations[src.node_id].link_to(dst.region)
-    return asdict(LinkCfg(latency_ms=link.rtt_ms / 2.0, bw_mbps=link.mbps))
+    """Shim settings of the hop src -> dst from src's emulation profile; in
+    shared-pacer mode also the budgets its frames share with other flows: the
+    sender's and the receiver's NIC, and the uplink from src's region to
+    dst's when they differ."""
+    em = emulations[src.node_id]
+    link = em.link_to(dst.region)
+    cfg = LinkCfg(latency_ms=link.rtt_ms / 2.0, bw_mbps=link.mbps)
+    if em.shared:
+        dem = emulations.get(dst.node_id)
+        if em.nic_mbps > 0:
+            cfg.egress_key, cfg.egress_mbps = src.node_id, em.nic_mbps
+        if dem is not None and dem.nic_mbps > 0:
+            cfg.ingress_key, cfg.ingress_mbps = dst.node_id, dem.nic_mbps
+        if src.region != dst.region and link.mbps > 0:
+            cfg.uplink_key, cfg.uplink_mbps = f"{src.region}>{dst.region}", link.mbps
+    return asdict(cfg)
 
 
 def emulated_links(groups, emulations) -> list | None:

@@ -35,6 +35,7 @@ import torch
 import torch.distributed as dist
 
 from elysium_wan_b200.models.gpt import Act
+from elysium_wan_b200.transport.pacer import reverse_link
 from elysium_wan_b200.transport import framing
 from elysium_wan_b200.transport.framing import BWD, END, FWD, HELLO
 
@@ -85,7 +86,7 @@ class _Link:
         self.comm, self.socks = comm, socks
         self.q: queue.Queue = queue.Queue()
         self.err: Exception | None = None
-        self.shim = _Shim(link_cfg or {})
+        self.shim = _Shim(link_cfg or {}, comm.spec.tag)
         self.t = threading.Thread(target=self._loop, daemon=True)
         self.t.start()
 
@@ -258,7 +259,7 @@ class TcpPipeComm:
             back = spec.links[self.stage - 1] if self.stage - 1 < len(spec.links) else {}
             for p in range(spec.stage_widths[self.stage - 1]):
                 socks = [accepted[p][f] for f in range(flows)]
-                self.prev_links[p] = _Link(self, socks, back)
+                self.prev_links[p] = _Link(self, socks, reverse_link(back))
                 for sc in socks:
                     self._start_reader(sc)
 

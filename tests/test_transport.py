@@ -333,3 +333,82 @@ def test_late_receive_fills_with_deferred_w_bitwise(tmp_path, monkeypatch):
             if line.startswith("WT_WFILL"):
                 filled += _json.loads(line.split(" ", 1)[1])["tasks"]
     assert filled > 0
+
+
+def _bucket_worker(path, n, nbytes, q):
+    import time as _t
+
+    from elysium_wan_b200.transport.pacer import HostBucket
+
+    b = HostBucket(100.0, path, burst_ms=0.0)
+    t0 = _t.monotonic()
+    end = 0.0
+    for _ in range(n):
+        end = b.reserve(nbytes)
+        d = end - _t.monotonic()
+        if d > 0:
+            _t.sleep(d)
+    q.put((t0, _t.monotonic()))
+
+
+def test_host_bucket_is_shared_by_processes(tmp_path):
+    """Two processes pacing through one 100 Mbit/s bucket take twice as long as
+    one: 2 x 10 frames of 125 kB at 10 ms each need >= 0.2 s together."""
+    import multiprocessing as mp
+    import time as _t
+
+    path = str(tmp_path / "nic.bucket")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_bucket_worker, args=(path, 10, 125_000, q)) for _ in range(2)]
+    for p in ps:
+        p.start()
+    spans = [q.get(timeout=60) for _ in ps]
+    for p in ps:
+        p.join(30)
+    start, end = min(s for s, _ in spans), max(e for _, e in spans)
+    assert end - start >= 0.19
+    # a bucket at another rate refuses the same file
+    from elysium_wan_b200.transport.pacer import HostBucket
+
+    with pytest.raises(ValueError):
+        HostBucket(50.0, path)
+    _t.sleep(0)
+
+
+def test_shared_budgets_pace_but_never_change_bits(tmp_path):
+    """A wide next stage: stage 0 sends to two replicas through one shared
+    egress budget (its NIC) and an uplink budget; losses stay bitwise."""
+    from elysium_wan_b200.launch.local import run_and_compare
+    from elysium_wan_b200.models.config import make_config
+    from elysium_wan_b200.runtime.spec import JobSpec
+
+    cfg = make_config("toy", n_layer=4, vocab_size=97, d_model=128, n_head=4, seq_len=16)
+    port = 34000 + (os.getpid() % 200) * 10
+    link = {"latency_ms": 2.0, "bw_mbps": 400.0, "egress_key": "node0", "egress_mbps": 200.0,
+            "uplink_key": "r0>r1", "uplink_mbps": 300.0}
+    spec = JobSpec(model=cfg, stages=2, stage_widths=[1, 2], microbatches=4, mb_size=2, steps=2,
+                   out_dir=str(tmp_path), port_base=port, backend="gloo", links=[link, {}])
+    r = run_and_compare(spec, timeout=300)
+    assert r["ok"], r
+    assert os.listdir(os.path.join(str(tmp_path), ".pacers"))
+
+
+def test_emulated_links_carry_shared_budgets():
+    from elysium_wan_b200.resources.links import Emulation
+    from elysium_wan_b200.scheduler.placement import emulated_links
+
+    class N:
+        def __init__(self, i, region):
+            self.node_id, self.region = f"n{i}", region
+
+    prof = {"inter": {"rtt_ms": 40.0, "mbps": 500.0}, "nic_mbps": 1000.0, "shared": True}
+    groups = [[N(0, "a")], [N(1, "b")]]
+    ems = {"n0": Emulation.from_profile("a", prof), "n1": Emulation.from_profile("b", prof)}
+    links = emulated_links(groups, ems)
+    assert links[0]["egress_key"] == "n0" and links[0]["egress_mbps"] == 1000.0
+    assert links[0]["ingress_key"] == "n1" and links[0]["uplink_key"] == "a>b"
+    assert links[0]["uplink_mbps"] == 500.0 and links[0]["latency_ms"] == 20.0
+    off = {"n0": Emulation.from_profile("a", {"inter": prof["inter"]}),
+           "n1": Emulation.from_profile("b", {"inter": prof["inter"]})}
+    assert emulated_links(groups, off)[0]["egress_key"] == ""
