@@ -111,7 +111,8 @@ class StageEngine:
         same order and no bit changes; the W op itself later runs what is
         left."""
         comm = self.comm
-        if self.fill_w and hasattr(comm, "ready"):
+        marks = self.zero1 is not None and hasattr(self.zero1, "mark")  # W routed by the exchange
+        if self.fill_w and not marks and hasattr(comm, "ready"):
             seq = self._w_seq
             while not comm.ready(handle):
                 while self._w_pos < len(seq) and seq[self._w_pos] in self._w_done:
