@@ -175,6 +175,10 @@ def plan_spec(args, n: int, free_bytes: float | None):
     # (one stage-sized buffer) and its shard of the moments.
     resident = biggest * (4 + 4 + 2) + (4 * biggest if wmin > 1 else 0)
     moments = 8 * biggest / wmin
+    if resident + 8 * GiB > cap:
+        raise SystemExit(f"{args.config} on {n} GPU(s): the largest stage's weights and gradients "
+                         f"({resident / GiB:.0f} GiB) do not fit a {cap / GiB:.0f} GiB device; "
+                         f"use more GPUs")
     host_adam = resident + moments > 0.80 * cap
     spec.optimizer = "adamw-host" if host_adam else "adamw"
     # With the moments on the device the activations fill what is left; keep a
