@@ -249,8 +249,7 @@ class TcpPipeComm:
                     socks.append(sc)
                 link = spec.links[self.stage] if self.stage < len(spec.links) else {}
                 self.next_links[q] = _Link(self, socks, link)
-                for sc in socks:
-                    self._start_reader(sc)
+                self._start_readers(socks)
         if t_acc:
             t_acc.join(self.timeout + 5)
             lsock.close()
@@ -260,8 +259,7 @@ class TcpPipeComm:
             for p in range(spec.stage_widths[self.stage - 1]):
                 socks = [accepted[p][f] for f in range(flows)]
                 self.prev_links[p] = _Link(self, socks, reverse_link(back))
-                for sc in socks:
-                    self._start_reader(sc)
+                self._start_readers(socks)
 
     def _dial(self, host, port):
         from elysium_wan_b200.transport import tuning
@@ -277,24 +275,29 @@ class TcpPipeComm:
                     raise
                 time.sleep(0.05)
 
-    def _start_reader(self, sock):
+    def _start_readers(self, socks):
+        """One reader thread per flow of a link. A frame's fragments travel on
+        different flows (one each), so the link's flows share one reassembler."""
         re = framing.Reassembler()
+        lock = threading.Lock()
 
-        def loop():
+        def loop(sock):
             try:
                 while True:
                     f = framing.recv_frame(sock)
                     if f.type == END:
                         return
-                    whole = re.push(f)
+                    with lock:
+                        whole = re.push(f)
                     if whole is not None:
                         self.inbox.put((whole.type, whole.mb), whole)
             except Exception as e:
                 self.inbox.fail(e)
 
-        t = threading.Thread(target=loop, daemon=True)
-        t.start()
-        self.readers.append(t)
+        for sock in socks:
+            t = threading.Thread(target=loop, args=(sock,), daemon=True)
+            t.start()
+            self.readers.append(t)
 
     # ----------------------------------------------------------------- routing
     def next_peer(self, mb: int) -> int:

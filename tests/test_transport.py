@@ -412,3 +412,21 @@ def test_emulated_links_carry_shared_budgets():
     off = {"n0": Emulation.from_profile("a", {"inter": prof["inter"]}),
            "n1": Emulation.from_profile("b", {"inter": prof["inter"]})}
     assert emulated_links(groups, off)[0]["egress_key"] == ""
+
+
+def test_multi_flow_fragments_reassemble_across_flows(tmp_path, monkeypatch):
+    """Boundaries large enough to be cut into one fragment per flow (4 flows,
+    256 kB fp32 boundaries): each frame's fragments arrive on different
+    sockets and must reassemble into one frame; losses stay bitwise."""
+    from elysium_wan_b200.launch.local import run_and_compare
+    from elysium_wan_b200.models.config import make_config
+    from elysium_wan_b200.runtime.spec import JobSpec
+
+    monkeypatch.setenv("ELYSIUM_PEER_KEY", str(tmp_path / "peer.key"))
+    cfg = make_config("toy", n_layer=2, vocab_size=97, d_model=512, n_head=4, seq_len=64)
+    port = 35000 + (os.getpid() % 200) * 10
+    spec = JobSpec(model=cfg, stages=2, microbatches=2, mb_size=2, steps=2, out_dir=str(tmp_path),
+                   port_base=port, backend="tcp", wire_codec="planes", p2p_streams=4)
+    r = run_and_compare(spec, timeout=180)
+    assert r["ok"], r
+    assert r["compared"] == 4
