@@ -28,7 +28,7 @@ import time
 import traceback
 
 from elysium_wan_b200.fault_tolerance import checkpoint as ckpt
-from elysium_wan_b200.transport.control import Channel, control_dial, token_mac
+from elysium_wan_b200.transport.control import Channel, body_sha256, control_dial, token_mac, write_body
 
 ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
@@ -197,14 +197,22 @@ class WorkerAgent:
 
     # ----------------------------------------------------------------- messages
     def _serve(self):
+        from elysium_wan_b200.transport.control import Spilled
+
         while not self.stop.is_set():
+            # restored checkpoint parts stream into the workdir's filesystem
+            self.ch.spill_dir = os.path.join(self.workdir, ".spill")
             hdr, body = self.ch.recv()
             kind = hdr["kind"]
             handler = getattr(self, f"_on_{kind.lower()}", None)
-            if handler is None:
-                self.send(f"{kind}_ACK", ok=False, why="unknown message")
-                continue
-            handler(hdr, body)
+            try:
+                if handler is None:
+                    self.send(f"{kind}_ACK", ok=False, why="unknown message")
+                    continue
+                handler(hdr, body)
+            finally:
+                if isinstance(body, Spilled):
+                    body.discard()
 
     def _on_probe(self, hdr, body):
         """PROBE {targets: [[host, port, region], ...], self_index}: one row of
@@ -386,7 +394,7 @@ class WorkerAgent:
         stage, peer, step = hdr.get("stage"), hdr.get("peer"), hdr.get("step")
         ok = all(ckpt.safe_name(x) for x in (run_id, tag, name)) and \
             all(type(v) is int and v >= 0 for v in (stage, peer, step)) and \
-            hashlib.sha256(body).hexdigest() == hdr.get("sha256")
+            body_sha256(body) == hdr.get("sha256")
         if not ok:
             self.send("RESTORE_ACK", ok=False, why="refused: malformed restore part")
             return
@@ -394,8 +402,7 @@ class WorkerAgent:
         final = ckpt.wave_dir(d, tag, stage, peer, step)
         staging = final + ".restore"
         os.makedirs(staging, exist_ok=True)
-        with open(os.path.join(staging, name), "wb") as f:
-            f.write(body)
+        write_body(body, os.path.join(staging, name))
         if not hdr.get("last"):
             return
         try:

@@ -71,7 +71,8 @@ from elysium_wan_b200.fault_tolerance.liveness import LivenessJudge, SlotState
 from elysium_wan_b200.fault_tolerance.replacement import find_replacement
 from elysium_wan_b200.resources.node import NodeInfo, mixed_fleet
 from elysium_wan_b200.runtime.spec import JobSpec
-from elysium_wan_b200.transport.control import Channel, check_mac, control_listen, new_nonce
+from elysium_wan_b200.transport.control import (Channel, Spilled, body_sha256, check_mac,
+                                                control_listen, new_nonce, write_body)
 
 
 @dataclass
@@ -270,6 +271,8 @@ class Coordinator:
 
     def _conn_loop(self, nid: str, ch: Channel):
         while not self.stop_ev.is_set():
+            # large bodies (checkpoint parts) stream into the store's filesystem
+            ch.spill_dir = os.path.join(self.store.root, ".spill") if self.store is not None else None
             try:
                 hdr, body = ch.recv()
             except (OSError, ConnectionError, ValueError):
@@ -280,9 +283,13 @@ class Coordinator:
                         n.disconnected_at = time.time()
                         self._sync_slot(nid)
                 return
-            self._dispatch(nid, hdr, body)
+            try:
+                self._dispatch(nid, hdr, body)
+            finally:
+                if isinstance(body, Spilled):
+                    body.discard()  # a body nobody took
 
-    def _dispatch(self, nid: str, hdr: dict, body: bytes):
+    def _dispatch(self, nid: str, hdr: dict, body):
         kind = hdr["kind"]
         with self.lock:
             n = self.nodes[nid]
@@ -307,7 +314,7 @@ class Coordinator:
                 # The wave belongs to the slot of the connection that sent it;
                 # only a validated integer step and a plain file name are taken
                 # from the message (reference: checkpoint.py:727-745).
-                if slot is not None and hashlib.sha256(body).hexdigest() == hdr.get("sha256"):
+                if slot is not None and body_sha256(body) == hdr.get("sha256"):
                     r, q = slot
                     try:
                         self.store.stage_part(self.run_id, r, q, hdr.get("step"), hdr.get("name"),
@@ -320,13 +327,11 @@ class Coordinator:
             elif kind == "TELEMETRY" and slot is not None and current and self.run_dir:
                 # rank and peer come from the connection's slot, never from the
                 # message (reference: coordinator/coordinator.py:594-604)
-                if hashlib.sha256(body).hexdigest() == hdr.get("sha256"):
+                if body_sha256(body) == hdr.get("sha256"):
                     r, q = slot
                     path = os.path.join(self.run_dir, f"telemetry_r{r}p{q}_a{self.attempt}.jsonl")
                     try:
-                        with open(path + ".part", "wb") as f:
-                            f.write(body)
-                        os.replace(path + ".part", path)
+                        write_body(body, path)
                     except OSError:
                         pass
             elif kind == "TELEM_STEP":
@@ -1000,11 +1005,13 @@ class Coordinator:
         ch = self.nodes[nid].ch
         names = sorted(meta["files"]) + ["wave.json"]
         for n in names:
-            with open(os.path.join(src, n), "rb") as f:
-                data = f.read()
-            ch.send("RESTORE", data, run_id=self.run_id, tag=spec.tag, stage=stage, peer=peer,
-                    step=step, name=n, last=(n == "wave.json"),
-                    sha256=hashlib.sha256(data).hexdigest())
+            # streamed from disk; the wave's own manifest already holds each
+            # file's sha256 (validated above), wave.json's is computed
+            sha = meta["files"][n]["sha256"] if n in meta["files"] else None
+            extra = {"sha256": sha} if sha else {}
+            ch.send_file("RESTORE", os.path.join(src, n), run_id=self.run_id, tag=spec.tag,
+                         stage=stage, peer=peer, step=step, name=n, last=(n == "wave.json"),
+                         **extra)
 
     def _launch(self, spec: JobSpec, resume_step):
         a = copy.deepcopy(spec)

@@ -203,16 +203,17 @@ class CheckpointStore:
         if name is not None and not safe_name(name):
             raise ValueError(f"bad part name {name!r}")
 
-    def stage_part(self, run_id: str, stage: int, peer: int, step: int, name: str,
-                   data: bytes) -> str:
-        """Write one shipped file of the slot's wave at `step` into staging."""
+    def stage_part(self, run_id: str, stage: int, peer: int, step: int, name: str, data) -> str:
+        """Write one shipped file of the slot's wave at `step` into staging
+        (`data`: bytes, or a body the control channel streamed to a file,
+        which is renamed into place)."""
+        from elysium_wan_b200.transport.control import write_body
+
         self._check(run_id, stage, peer, step, name)
         d = self._incoming(run_id, stage, peer, step)
         os.makedirs(d, exist_ok=True)
         p = os.path.join(d, name)
-        with open(p + ".part", "wb") as f:
-            f.write(data)
-        os.replace(p + ".part", p)
+        write_body(data, p)
         return p
 
     def commit_staged(self, run_id: str, tag: str, stage: int, peer: int, step: int) -> bool:

@@ -27,6 +27,47 @@ import threading
 
 MAX_HEADER = 16 << 20
 MAX_BODY = 1 << 40
+SPILL_MIN = 64 << 20  # bodies this large go to a file as they arrive (when the channel has a spill dir)
+_CHUNK = 4 << 20
+
+
+class Spilled:
+    """A message body the receiver streamed into a file as it arrived, with
+    its sha256 computed on the way (a checkpoint part of gigabytes never sits
+    in memory). `move_to` renames it into place (same filesystem)."""
+
+    def __init__(self, path: str, size: int, sha256: str):
+        self.path, self.size, self.sha256 = path, size, sha256
+
+    def __len__(self):
+        return self.size
+
+    def read(self) -> bytes:
+        with open(self.path, "rb") as f:
+            return f.read()
+
+    def move_to(self, dst: str):
+        os.replace(self.path, dst)
+
+    def discard(self):
+        try:
+            os.unlink(self.path)
+        except FileNotFoundError:
+            pass
+
+
+def body_sha256(body) -> str:
+    return body.sha256 if isinstance(body, Spilled) else hashlib.sha256(body).hexdigest()
+
+
+def write_body(body, dst: str):
+    """Put a received body at dst (through dst + '.part', renamed when whole)."""
+    if isinstance(body, Spilled):
+        body.move_to(dst)
+        return
+    with open(dst + ".part", "wb") as f:
+        f.write(body)
+    os.replace(dst + ".part", dst)
 
 
 def token_mac(token: str, nonce: str, coordinator_id: str) -> str:
@@ -50,10 +91,12 @@ def _recv_exact(sock: socket.socket, n: int) -> bytes:
 class Channel:
     """A framed, thread-safe (for sends) message channel over one socket."""
 
-    def __init__(self, sock: socket.socket):
+    def __init__(self, sock: socket.socket, spill_dir: str | None = None):
         self.sock = sock
         self.lock = threading.Lock()
         self.closed = False
+        self.spill_dir = spill_dir  # where large bodies are streamed (None: in memory)
+        self.spill_min = int(os.environ.get("EWB_CONTROL_SPILL_MIN", SPILL_MIN))
         try:
             sock.setsockopt(socket.IPPROTO_TCP, socket.TCP_NODELAY, 1)
         except OSError:
@@ -67,12 +110,28 @@ class Channel:
                 self.sock.sendall(body)
 
     def send_file(self, kind: str, path: str, **fields):
-        with open(path, "rb") as f:
-            data = f.read()
-        fields.setdefault("sha256", hashlib.sha256(data).hexdigest())
-        self.send(kind, data, **fields)
+        """Send a file as the body, streamed from disk in 4 MiB pieces (its
+        sha256 from a first pass over the file unless given)."""
+        size = os.path.getsize(path)
+        if "sha256" not in fields:
+            h = hashlib.sha256()
+            with open(path, "rb") as f:
+                for piece in iter(lambda: f.read(_CHUNK), b""):
+                    h.update(piece)
+            fields["sha256"] = h.hexdigest()
+        hdr = json.dumps(dict(fields, kind=kind)).encode()
+        with self.lock, open(path, "rb") as f:
+            self.sock.sendall(struct.pack(">I", len(hdr)) + hdr + struct.pack(">Q", size))
+            sent = 0
+            for piece in iter(lambda: f.read(_CHUNK), b""):
+                self.sock.sendall(piece)
+                sent += len(piece)
+            if sent != size:
+                raise ConnectionError(f"{path} changed size while being sent")
 
-    def recv(self) -> tuple[dict, bytes]:
+    def recv(self) -> tuple:
+        """(header, body): body is bytes, or a Spilled file for bodies of at
+        least SPILL_MIN bytes when the channel has a spill directory."""
         (n,) = struct.unpack(">I", _recv_exact(self.sock, 4))
         if n > MAX_HEADER:
             raise ValueError(f"control header of {n} bytes refused")
@@ -80,8 +139,34 @@ class Channel:
         (m,) = struct.unpack(">Q", _recv_exact(self.sock, 8))
         if m > MAX_BODY:
             raise ValueError("control body too large")
+        if m and m >= self.spill_min and self.spill_dir:
+            return hdr, self._spill(m)
         body = _recv_exact(self.sock, m) if m else b""
         return hdr, body
+
+    def _spill(self, m: int) -> Spilled:
+        import tempfile
+
+        os.makedirs(self.spill_dir, exist_ok=True)
+        fd, path = tempfile.mkstemp(prefix="body-", dir=self.spill_dir)
+        h = hashlib.sha256()
+        left = m
+        try:
+            with os.fdopen(fd, "wb") as f:
+                while left:
+                    piece = self.sock.recv(min(left, _CHUNK))
+                    if not piece:
+                        raise ConnectionError("control connection closed")
+                    h.update(piece)
+                    f.write(piece)
+                    left -= len(piece)
+        except BaseException:
+            try:
+                os.unlink(path)
+            except FileNotFoundError:
+                pass
+            raise
+        return Spilled(path, m, h.hexdigest())
 
     def close(self):
         self.closed = True

@@ -364,3 +364,37 @@ def test_unrouted_chain_gives_the_hungriest_rank_the_largest_card(tmp_path):
         assert co._memory_order(spec, live) == live
     finally:
         co.nodes.clear()  # never started: no socket, and the fake nodes have no channel
+
+
+def test_control_channel_streams_large_bodies_to_disk(tmp_path):
+    """A file body at least spill_min long is streamed from disk by the sender
+    and into a file by the receiver (sha256 computed on the way), then renamed
+    into place; small bodies stay in memory."""
+    import os
+    import socket
+    import threading
+
+    from elysium_wan_b200.transport.control import Channel, Spilled, body_sha256, write_body
+
+    a, b = socket.socketpair()
+    tx, rx = Channel(a), Channel(b, spill_dir=str(tmp_path / "spill"))
+    rx.spill_min = 1 << 16
+    src = tmp_path / "state.pt"
+    payload = os.urandom(3 << 20)
+    src.write_bytes(payload)
+    t = threading.Thread(target=lambda: (tx.send_file("CKPT", str(src), name="state.pt"),
+                                         tx.send("HEARTBEAT", b"x" * 10)))
+    t.start()
+    hdr, body = rx.recv()
+    assert hdr["kind"] == "CKPT" and isinstance(body, Spilled) and len(body) == len(payload)
+    import hashlib
+
+    assert body_sha256(body) == hdr["sha256"] == hashlib.sha256(payload).hexdigest()
+    dst = tmp_path / "placed.pt"
+    write_body(body, str(dst))
+    assert dst.read_bytes() == payload and not os.path.exists(body.path)
+    hdr2, small = rx.recv()
+    assert hdr2["kind"] == "HEARTBEAT" and small == b"x" * 10
+    t.join(10)
+    a.close()
+    b.close()
