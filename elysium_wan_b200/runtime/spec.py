@@ -88,6 +88,12 @@ class JobSpec:
     port_base: int = 29000
     host: str = "127.0.0.1"
     p2p_streams: int = 1
+    # TCP sender fragment sizing (reference field names): a frame is cut into
+    # fragments spread over the flows; with adapt_budget_ms > 0 the fragment
+    # size halves (not below frag_min_bytes) while a fragment takes longer
+    # than the budget to send and doubles back after 8 frames well under it.
+    adapt_budget_ms: float = 0.0
+    frag_min_bytes: int = 4096
     endpoints: list | None = None
     trusted_peers: list | None = None
     slot_peers: list | None = None

@@ -84,6 +84,8 @@ class _Link:
         from elysium_wan_b200.parallel.p2p import _Shim
 
         self.comm, self.socks = comm, socks
+        self.frag_size = 0  # 0: one fragment per flow; else the adapted fragment size
+        self.clean = 0
         self.q: queue.Queue = queue.Queue()
         self.err: Exception | None = None
         self.shim = _Shim(link_cfg or {}, comm.spec.tag)
@@ -97,11 +99,38 @@ class _Link:
         c = self.comm
         payload_t = tensors if len(tensors) > 1 else tensors[0]
         codec_id, payload, shape = framing.encode_tensor(payload_t, c.wire_codec)
-        frags = framing.fragments(payload, len(self.socks))
+        if self.frag_size:
+            # adapted size: fragments taken round-robin by the flows
+            n = max(1, -(-len(payload) // self.frag_size))
+            frags = [payload[i * self.frag_size:(i + 1) * self.frag_size] for i in range(n)] or [b""]
+        else:
+            frags = framing.fragments(payload, len(self.socks))
+        t0 = time.monotonic()
         for i, part in enumerate(frags):
-            framing.send_frame(self.socks[i], ftype, step, mb, part, chunk=c.peer,
+            framing.send_frame(self.socks[i % len(self.socks)], ftype, step, mb, part, chunk=c.peer,
                                codec_id=codec_id, shape=shape, frag_idx=i, frag_cnt=len(frags))
+        self._adapt((time.monotonic() - t0) / len(frags), len(frags[0]), len(payload))
         return len(payload)
+
+    def _adapt(self, per_frag_s: float, size: int, total: int):
+        """Fragment-size adaptation (reference: the sender loop of
+        src/wantrain/runtime/stage.py:2032-2105, semantics only): a fragment
+        slower than the budget halves the size, down to frag_min_bytes; eight
+        frames in a row under a quarter of it double the size back, up to
+        whole frames (the flows' default split)."""
+        spec = self.comm.spec
+        budget = float(spec.adapt_budget_ms) / 1e3
+        if budget <= 0 or total <= 0:
+            return
+        floor = max(1, int(spec.frag_min_bytes))
+        if per_frag_s > budget and size > floor:
+            self.frag_size = max(floor, size // 2)
+            self.clean = 0
+        elif per_frag_s < budget / 4 and self.frag_size:
+            self.clean += 1
+            if self.clean >= 8:
+                self.frag_size = self.frag_size * 2 if self.frag_size * 2 < total else 0
+                self.clean = 0
 
     def _loop(self):
         while True:

@@ -430,3 +430,41 @@ def test_multi_flow_fragments_reassemble_across_flows(tmp_path, monkeypatch):
     r = run_and_compare(spec, timeout=180)
     assert r["ok"], r
     assert r["compared"] == 4
+
+
+def test_adaptive_fragments_shrink_and_stay_bitwise(tmp_path, monkeypatch):
+    """With a tiny send budget every fragment is 'too slow', so the sender
+    halves its fragment size down to the floor: a 256 kB boundary then goes
+    as many small fragments round-robin over 2 flows, and the losses are
+    still bitwise equal to the oracle."""
+    from elysium_wan_b200.launch.local import run_and_compare
+    from elysium_wan_b200.models.config import make_config
+    from elysium_wan_b200.runtime.spec import JobSpec
+
+    monkeypatch.setenv("ELYSIUM_PEER_KEY", str(tmp_path / "peer.key"))
+    cfg = make_config("toy", n_layer=2, vocab_size=97, d_model=512, n_head=4, seq_len=64)
+    port = 36000 + (os.getpid() % 200) * 10
+    spec = JobSpec(model=cfg, stages=2, microbatches=4, mb_size=2, steps=2, out_dir=str(tmp_path),
+                   port_base=port, backend="tcp", wire_codec="planes", p2p_streams=2,
+                   adapt_budget_ms=1e-6, frag_min_bytes=16384)
+    r = run_and_compare(spec, timeout=240)
+    assert r["ok"], r
+    assert r["compared"] == 8
+
+
+def test_fragment_size_adaptation_rule():
+    from types import SimpleNamespace
+
+    from elysium_wan_b200.transport.tcp import _Link
+
+    link = _Link.__new__(_Link)
+    link.comm = SimpleNamespace(spec=SimpleNamespace(adapt_budget_ms=5.0, frag_min_bytes=4096))
+    link.frag_size, link.clean = 0, 0
+    link._adapt(0.010, 1 << 20, 1 << 20)  # 10 ms > 5 ms: halve
+    assert link.frag_size == 1 << 19
+    for _ in range(20):
+        link._adapt(0.010, link.frag_size, 1 << 20)
+    assert link.frag_size == 4096  # the floor
+    for _ in range(8):
+        link._adapt(0.0001, link.frag_size, 1 << 20)  # well under a quarter: double after 8
+    assert link.frag_size == 8192
