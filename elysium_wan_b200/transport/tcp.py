@@ -97,7 +97,8 @@ class _Link:
 
     def _send_frame(self, ftype, step, mb, tensors):
         c = self.comm
-        payload_t = tensors if len(tensors) > 1 else tensors[0]
+        # an fp8 boundary is the (codes, scales) pair: one frame, one payload
+        payload_t = tuple(tensors) if len(tensors) > 1 else tensors[0]
         codec_id, payload, shape = framing.encode_tensor(payload_t, c.wire_codec)
         if self.frag_size:
             # adapted size: fragments taken round-robin by the flows

@@ -468,3 +468,25 @@ def test_fragment_size_adaptation_rule():
     for _ in range(8):
         link._adapt(0.0001, link.frag_size, 1 << 20)  # well under a quarter: double after 8
     assert link.frag_size == 8192
+
+
+@pytest.mark.parametrize("boundary", ["fp8_e4m3_b128", "fp8_e5m2_b128"])
+def test_fp8_boundaries_over_tcp_wide_shaped_multiflow(tmp_path, monkeypatch, boundary):
+    """The fp8 boundary pair (codes + 1x128 scales) as one frame over the
+    sealed TCP plane: 3 stages with a wide middle stage, 3 flows per hop,
+    adaptive fragments, a shaped link with a shared egress budget; bitwise."""
+    from elysium_wan_b200.launch.local import run_and_compare
+    from elysium_wan_b200.models.config import make_config
+    from elysium_wan_b200.runtime.spec import JobSpec
+
+    monkeypatch.setenv("ELYSIUM_PEER_KEY", str(tmp_path / "peer.key"))
+    cfg = make_config("toy", n_layer=4, vocab_size=97, d_model=512, n_head=4, seq_len=64,
+                      boundary_dtype=boundary)
+    link = {"latency_ms": 3.0, "bw_mbps": 800.0, "egress_key": "n0", "egress_mbps": 600.0}
+    port = 38000 + (os.getpid() % 200) * 10 + len(boundary)
+    spec = JobSpec(model=cfg, stages=3, stage_widths=[1, 2, 1], microbatches=6, mb_size=2, steps=2,
+                   out_dir=str(tmp_path), port_base=port, backend="tcp", wire_codec="planes",
+                   p2p_streams=3, adapt_budget_ms=0.5, frag_min_bytes=16384, links=[link, link, {}])
+    r = run_and_compare(spec, timeout=300)
+    assert r["ok"], r
+    assert r["compared"] == 12
