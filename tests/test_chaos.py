@@ -183,3 +183,26 @@ def test_wide_stage_peer_death_heals_every_shard(tmp_path):
     heal = [e for e in cl.coord.events if e[0] == "heal"][0]
     assert heal[1] == (0, 1)
     _oracle_ok(spec, res, tmp_path)
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("boundary", ["fp8_e4m3_b128", "fp16"])
+def test_heal_over_tcp_with_format_boundaries(tmp_path, monkeypatch, boundary):
+    """The TCP data plane (sealed multi-flow links, planes codec) in a heal: a
+    replica of the wide second stage dies, its slot moves to the spare, every
+    stage re-dials its links, and the run stays exact with fp8 (codes + block
+    scales travelling as one frame) and fp16 boundaries."""
+    monkeypatch.setenv("ELYSIUM_PEER_KEY", str(tmp_path / "peer.key"))
+    cfg = make_config("toy", n_layer=4, vocab_size=97, d_model=256, n_head=4, seq_len=32,
+                      boundary_dtype=boundary)
+    spec = JobSpec(model=cfg, stages=2, stage_widths=[1, 2], microbatches=4, mb_size=2, steps=8,
+                   backend="tcp", wire_codec="planes", p2p_streams=2, ckpt_every=2, tag="chaos")
+    cl = LocalCluster(str(tmp_path / "cl"), ["a"] * 4)
+    fired = _at_step(cl, 3, lambda: cl.kill_worker(cl.worker_of_slot((1, 1))) or True)
+    try:
+        res = cl.run(Job(spec=spec))
+    finally:
+        cl.close()
+    assert fired and res.ok, res.why
+    assert res.heals == 1
+    _oracle_ok(spec, res, tmp_path)
