@@ -31,7 +31,7 @@ import torch
 
 from elysium_wan_b200.fault_tolerance import checkpoint as ckpt
 from elysium_wan_b200.models.gpt import entry_specs
-from elysium_wan_b200.models.params import plan_layout, shard_ranges
+from elysium_wan_b200.models.params import pieces_held, plan_layout, shard_ranges
 from elysium_wan_b200.parallel.zero1 import shard_bounds
 from elysium_wan_b200.transport import serial
 
@@ -75,10 +75,12 @@ def gather(spec, step: int | None = None) -> dict:
             opt = st["opt"]
             if pieces:
                 rb = shard_ranges(nr, w)[p]
-                mb = [(nr + a, nr + b) for a, b in shard_ranges(nt - nr, w)][p]
-                held = st["params"]
-                flat_p[:nr] = held[:nr]
-                flat_p[mb[0]:mb[1]] = held[nr:]
+                held = pieces_held(nr, nt, numel, w, p)
+                mb = held[1]
+                base = 0
+                for lo, hi in held:
+                    flat_p[lo:hi] = st["params"][base: base + hi - lo]
+                    base += hi - lo
                 for (lo, hi), key in ((rb, "r"), (mb, "m")):
                     flat_m[lo:hi] = opt[key]["m"].reshape(-1)
                     flat_v[lo:hi] = opt[key]["v"].reshape(-1)
@@ -134,8 +136,9 @@ def scatter(state: dict, spec, step: int | None = None):
         for p in range(w):
             if pieces:
                 rb = shard_ranges(nr, w)[p]
-                mb = [(nr + x, nr + y) for x, y in shard_ranges(nt - nr, w)][p]
-                params = torch.cat([flat_p[:nr], flat_p[mb[0]:mb[1]]])
+                held = pieces_held(nr, nt, numel, w, p)
+                mb = held[1]
+                params = torch.cat([flat_p[lo:hi] for lo, hi in held])
                 opt = {"t": state["t"], "pieces": {"k": p, "w": w},
                        "r": {"t": state["t"], "m": flat_m[rb[0]:rb[1]].clone(),
                              "v": flat_v[rb[0]:rb[1]].clone()},

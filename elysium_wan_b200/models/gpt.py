@@ -107,14 +107,16 @@ def entry_specs(cfg: GPTConfig, e: int) -> list[ParamSpec]:
     out, adapters = [], []
     for sp in base:
         out.append(ParamSpec(sp.name, sp.shape, sp.init, sp.fan_in, sp.matrix, sp.pack,
-                             frozen=True))
+                             frozen=True, replicate=sp.replicate))
         stem = sp.name[:-len(".weight")] if sp.name.endswith(".weight") else None
         if sp.matrix and stem and stem.split(".")[-1] in want:
             o, i = sp.shape
+            # the merge W + s B A reads the adapters' fp32 masters: a pieces
+            # stage keeps them whole on every replica
             adapters += [ParamSpec(f"{stem}.A.weight", (cfg.lora_rank, i), "lora_a", fan_in=i,
-                                   matrix=True),
+                                   matrix=True, replicate=True),
                          ParamSpec(f"{stem}.B.weight", (o, cfg.lora_rank), "zeros", fan_in=cfg.lora_rank,
-                                   matrix=True)]
+                                   matrix=True, replicate=True)]
     return out + adapters
 
 

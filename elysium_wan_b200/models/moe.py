@@ -54,7 +54,10 @@ def moe_specs(cfg, e: int) -> list[ParamSpec]:
     d, E, f = cfg.d_model, cfg.moe_experts, cfg.moe_width
     p = f"{e}.mlp"
     clamped = cfg.moe_expert == "swiglu_clamped"
-    out = [ParamSpec(f"{p}.router.weight", (E, d), "normal", fan_in=d, matrix=True)]
+    # the router's fp32 master is read directly (fp32 router logits), so a
+    # pieces stage keeps it whole on every replica
+    out = [ParamSpec(f"{p}.router.weight", (E, d), "normal", fan_in=d, matrix=True,
+                     replicate=True)]
     if cfg.moe_router_bias:
         out.append(ParamSpec(f"{p}.router.bias", (E,), "bias", fan_in=d))
 

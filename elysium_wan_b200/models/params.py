@@ -31,17 +31,21 @@ class ParamSpec:
     matrix: bool = False  # read by a GEMM (needs the bf16 working copy)
     pack: bool = False  # the next tensor follows with no alignment gap (read as one operand)
     frozen: bool = False  # not trained: no gradient, no optimizer state (LoRA base)
+    # pieces layout: every replica holds this matrix's fp32 master whole (a
+    # kernel reads it in fp32, or another tensor is computed from it)
+    replicate: bool = False
 
 
 def plan_layout(specs: list[ParamSpec], replicated_first: bool = False):
     """(ordered specs, {name: (offset, shape)}, nt, numel, nr) of a flat store:
     trainable tensors first, each on an ALIGN boundary unless its predecessor
     packs it, frozen tensors after nt. With `replicated_first` (the pieces
-    layout) the trainable non-matrix tensors (norms, biases, tables) come
-    before the matrices; nr is where the matrices start."""
+    layout) the trainable tensors every replica holds whole (norms, biases,
+    tables, and matrices marked `replicate`) come before the sharded
+    matrices; nr is where the sharded matrices start."""
     train = [s for s in specs if not s.frozen]
     if replicated_first:
-        train = [s for s in train if not s.matrix] + [s for s in train if s.matrix]
+        train = [s for s in train if not _sharded(s)] + [s for s in train if _sharded(s)]
     ordered = train + [s for s in specs if s.frozen]
     index: dict[str, tuple[int, tuple]] = {}
     off, nt, nr = 0, None, None
@@ -50,7 +54,7 @@ def plan_layout(specs: list[ParamSpec], replicated_first: bool = False):
             off = (off + ALIGN - 1) // ALIGN * ALIGN
             nt = max(off, ALIGN)
             off = nt
-        if replicated_first and s.matrix and not s.frozen and nr is None:
+        if replicated_first and _sharded(s) and nr is None:
             off = (off + ALIGN - 1) // ALIGN * ALIGN
             nr = off
         index[s.name] = (off, tuple(s.shape))
@@ -59,6 +63,21 @@ def plan_layout(specs: list[ParamSpec], replicated_first: bool = False):
     numel = max(off, ALIGN)
     nt = numel if nt is None else nt
     return ordered, index, nt, numel, (nt if nr is None else nr)
+
+
+def _sharded(s: ParamSpec) -> bool:
+    """Whether the pieces layout splits this tensor's fp32 master over the
+    replicas (a trainable matrix nobody reads in fp32)."""
+    return s.matrix and not s.frozen and not s.replicate
+
+
+def pieces_held(nr: int, nt: int, numel: int, w: int, k: int) -> list:
+    """[(flat lo, flat hi)] of the store that replica k of a width-w pieces
+    stage holds in fp32, in the order its master buffer keeps them: the
+    replicated region [0, nr), its range of the sharded matrices, and the
+    frozen region [nt, numel) (not trained, read by every replica)."""
+    lo, hi = [(nr + a, nr + b) for a, b in shard_ranges(nt - nr, w)][k]
+    return [(0, nr), (lo, hi), (nt, numel)]
 
 
 def shard_ranges(n: int, w: int) -> list:
@@ -73,8 +92,9 @@ class ParamStore:
     optimizer cover only [0, nt).
 
     `shard=(k, w)` is the pieces layout of replica k of a width-w stage: the
-    non-matrix tensors [0, nr) keep a full fp32 master, the matrices [nr, nt)
-    keep only their k-th contiguous range [mlo, mhi) in fp32 (the bf16 working
+    replicated tensors [0, nr) keep a full fp32 master, the sharded matrices
+    [nr, nt) keep only their k-th contiguous range [mlo, mhi) in fp32, and the
+    frozen tensors [nt, numel) are held whole after them (the bf16 working
     copy stays whole; the replicas all-gather it after every step)."""
 
     def __init__(self, specs: list[ParamSpec], device: torch.device, work_dtype=None,
@@ -86,15 +106,15 @@ class ParamStore:
         self.frozen = {s.name for s in self.specs if s.frozen}
         self.shard = shard
         if shard is not None:
-            if self.frozen:
-                raise NotImplementedError("the pieces layout holds no frozen tensors")
             k, w = shard
             self.mbounds = [(self.nr + lo, self.nr + hi)
                             for lo, hi in shard_ranges(self.nt - self.nr, w)]
-            self.mlo, self.mhi = self.mbounds[k]
-            held = self.nr + (self.mhi - self.mlo)
+            self.held = pieces_held(self.nr, self.nt, self.numel, w, k)
+            self.mlo, self.mhi = self.held[1]
+            held = sum(hi - lo for lo, hi in self.held)
         else:
             self.mlo = self.mhi = self.nr
+            self.held = [(0, self.numel)]
             held = self.numel
         self.master = torch.zeros(held, dtype=torch.float32, device=self.device)
         self.grad = torch.zeros(self.nt, dtype=torch.float32, device=self.device)
@@ -112,17 +132,18 @@ class ParamStore:
         return buf[off: off + math.prod(shape)].view(shape)
 
     def p(self, name):
-        """fp32 master view (in the pieces layout: a non-matrix tensor, or a
-        matrix that lies wholly inside this replica's range)."""
+        """fp32 master view (in the pieces layout: a replicated or frozen
+        tensor, or a matrix that lies wholly inside this replica's range)."""
         if self.shard is None:
             return self._view(self.master, name)
         off, shape = self.index[name]
         n = math.prod(shape)
-        if off + n <= self.nr:
-            return self.master[off: off + n].view(shape)
-        if self.mlo <= off and off + n <= self.mhi:
-            o = self.nr + off - self.mlo
-            return self.master[o: o + n].view(shape)
+        base = 0
+        for lo, hi in self.held:
+            if lo <= off and off + n <= hi:
+                o = base + off - lo
+                return self.master[o: o + n].view(shape)
+            base += hi - lo
         raise KeyError(f"{name}: its fp32 master is held by another replica (pieces layout)")
 
     def holds(self, name) -> bool:
@@ -134,10 +155,11 @@ class ParamStore:
 
     def master_ranges(self) -> list:
         """[(flat lo, flat hi, master view)] of what this store holds in fp32."""
-        if self.shard is None:
-            return [(0, self.numel, self.master)]
-        return [(0, self.nr, self.master[:self.nr]),
-                (self.mlo, self.mhi, self.master[self.nr:])]
+        out, base = [], 0
+        for lo, hi in self.held:
+            out.append((lo, hi, self.master[base: base + hi - lo]))
+            base += hi - lo
+        return out
 
     def set_initial(self, name, value):
         """Initial values of one tensor: the held part of the fp32 master and

@@ -80,7 +80,10 @@ def entry_specs(cfg, e: int) -> list:
     from elysium_wan_b200.models.params import ParamSpec
 
     mod = build_layers(cfg, 0)[e]
-    return [ParamSpec(f"{e}.{n}", tuple(p.shape), "user", fan_in=1, matrix=p.dim() >= 2)
+    # the module computes on views of the fp32 masters, so a pieces stage keeps
+    # every one of them whole on each replica (each still steps only its range)
+    return [ParamSpec(f"{e}.{n}", tuple(p.shape), "user", fan_in=1, matrix=p.dim() >= 2,
+                      replicate=True)
             for n, p in mod.named_parameters()]
 
 

@@ -3,13 +3,16 @@
 Reference behaviour: src/wantrain/runtime/pieces.py and stage.py:846-1130
 (each replica owns a piece of every tensor: its fp32 master, AdamW moments
 and gradient fold; per-unit update and gather). Here the store's pieces
-layout (models/params.py) puts the non-matrix tensors (norms, biases,
-embedding tables) first and the matrices after them; replica k holds:
+layout (models/params.py) puts the replicated tensors (norms, biases,
+embedding tables, and the small matrices read in fp32: an fp32 MoE router,
+LoRA adapters, which the merged weight is computed from) first and the
+sharded matrices after them; replica k holds:
 
-- the fp32 master of the non-matrix region in full (its kernels read fp32),
+- the fp32 master of the replicated region in full (its kernels read fp32),
   but steps only its k-th range of it;
-- the fp32 master and the AdamW moments of only its k-th range of the matrix
-  region (the bulk of the parameters);
+- the fp32 master and the AdamW moments of only its k-th range of the
+  sharded region (the bulk of the parameters);
+- the frozen tensors (a LoRA base) whole, untouched by the exchange;
 - the whole bf16 working copy, which the GEMMs read.
 
 A step: the replicas' fp32 gradient partials (each replica folds its own
@@ -56,7 +59,7 @@ class Pieces:
         self.opt_r = optim.build(spec.optimizer, st.master[self.r_lo:self.r_hi], self.g[:n_r],
                                  work[self.r_lo:self.r_hi] if work is not None else None,
                                  spec.lr, spec.adamw)
-        self.opt_m = optim.build(spec.optimizer, st.master[st.nr:], self.g[n_r:],
+        self.opt_m = optim.build(spec.optimizer, st.master[st.nr:st.nr + n_m], self.g[n_r:],
                                  work[self.m_lo:self.m_hi] if work is not None else None,
                                  spec.lr, spec.adamw)
         engine.opt = self
@@ -87,8 +90,8 @@ class Pieces:
                 if q != self.k:
                     st.master[l:h] = out[q * per: q * per + h - l]
         # matrix ranges as the working copy (bf16 on the GPU)
-        if st.work is not None:
-            per = max(h - l for l, h in self.mb)
+        per = max(h - l for l, h in self.mb)
+        if st.work is not None and per > 0:
             mine = torch.zeros(per, dtype=st.work.dtype, device=st.work.device)
             mine[: self.m_hi - self.m_lo] = st.work[self.m_lo:self.m_hi]
             out = torch.empty(self.w * per, dtype=st.work.dtype, device=st.work.device)
@@ -96,9 +99,9 @@ class Pieces:
             for q, (l, h) in enumerate(self.mb):
                 if q != self.k:
                     st.work[l:h] = out[q * per: q * per + h - l]
-            # non-matrix working copy follows the fp32 master
-            if st.nr > 0:
-                st.work[:st.nr].copy_(st.master[:st.nr])
+        # the replicated region's working copy follows its fp32 master
+        if st.work is not None and st.nr > 0:
+            st.work[:st.nr].copy_(st.master[:st.nr])
 
     def sync_and_step(self):
         self._reduce_scatter()

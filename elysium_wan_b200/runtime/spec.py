@@ -156,8 +156,6 @@ class JobSpec:
             raise ValueError(f"fold {self.fold!r} is not one of {FOLDS}")
         if self.shard not in ("zero1", "pieces"):
             raise ValueError(f"shard {self.shard!r} is not one of ('zero1', 'pieces')")
-        if self.shard == "pieces" and (self.model.lora_rank or self.model.moe_experts):
-            raise NotImplementedError("the pieces layout does not combine with LoRA or MoE")
         if self.partition is None:
             try:
                 self.partition = part.even_blocks_partition(self.model, self.stages)

@@ -110,7 +110,7 @@ def stage_terms(spec, stage: int) -> StageTerms:
                 continue
             trainable += n
             n_unit += n
-            if not s.matrix:
+            if not s.matrix or s.replicate:  # held whole by every pieces replica
                 nonmatrix += n
         units.append(n_unit)
     T = spec.mb_size * cfg.seq_len

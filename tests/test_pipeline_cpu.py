@@ -52,6 +52,17 @@ CASES = {
     "lora_wide_1_2": dict(stages=2, stage_widths=[1, 2],
                           model_kw=dict(norm="rmsnorm", mlp="swiglu", pos="rope", bias=False,
                                         n_kv_head=2, lora_rank=8, lora_targets="attn_mlp")),
+    # Pieces under LoRA (the frozen base held whole by every replica, the
+    # adapters replicated for the merge) and under MoE (the fp32 router
+    # replicated, the experts sharded).
+    "pieces_lora_1_2": dict(stages=2, stage_widths=[1, 2], shard="pieces",
+                            model_kw=dict(norm="rmsnorm", mlp="swiglu", pos="rope", bias=False,
+                                          n_kv_head=2, lora_rank=8, lora_targets="attn")),
+    "pieces_moe_2_1": dict(stages=2, stage_widths=[2, 1], shard="pieces",
+                           model_kw=dict(norm="rmsnorm", mlp="swiglu", pos="rope", bias=False,
+                                         moe_experts=4, moe_top_k=2, moe_d_ff=64,
+                                         moe_shared_d_ff=64, moe_select="score_bias",
+                                         moe_bias_rate=0.01, moe_lbl_coef=0.01)),
     # MoE block with a selection bias that moves every step, recompute, a
     # wide second stage (counts summed over its replicas).
     "moe_wide_1_2": dict(stages=2, stage_widths=[1, 2], recompute=True,
@@ -157,12 +168,15 @@ def _user_cfg(n_layer=4):
                        arch="user", user_model=src, user_model_sha256=sha)
 
 
-@pytest.mark.parametrize("stages,widths", [(2, None), (3, [1, 2, 1])])
-def test_user_model_pipeline_bitwise_vs_oracle(tmp_path, stages, widths):
+@pytest.mark.parametrize("stages,widths,shard", [(2, None, "zero1"), (3, [1, 2, 1], "zero1"),
+                                                (2, [2, 1], "pieces")])
+def test_user_model_pipeline_bitwise_vs_oracle(tmp_path, stages, widths, shard):
     """arch "user": the operator's own flat module list (sha256-pinned source)
-    cut over stages, a wide stage among them, equals the oracle bit for bit."""
-    port = 35500 + stages * 13 + (os.getpid() % 200) * 7
-    kw = {"stage_widths": widths} if widths else {}
+    cut over stages, a wide stage among them (ZeRO-1, or pieces: every
+    replica keeps the fp32 masters the module computes on), equals the oracle
+    bit for bit."""
+    port = 35500 + stages * 13 + 5 * (shard == "pieces") + (os.getpid() % 200) * 7
+    kw = {"stage_widths": widths, "shard": shard} if widths else {}
     spec = JobSpec(model=_user_cfg(), stages=stages, microbatches=4, mb_size=2, steps=2,
                    out_dir=str(tmp_path), port_base=port, backend="gloo", **kw)
     r = run_and_compare(spec, timeout=240)
