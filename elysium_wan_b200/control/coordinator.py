@@ -674,9 +674,17 @@ class Coordinator:
                 else:
                     spec, resume_step = got
             elif verdict.kind == "reschedule":
-                spec, note = self._next[1]
+                new_spec, note = self._next[1]
                 resume_step = self._resume_point(spec)
-                rec = {"step": resume_step, "reschedule": True, "note": note}
+                if new_spec.mb_owner != spec.mb_owner and resume_step:
+                    # the steps before the resume point ran under the old table
+                    new_spec.ownership_log = list(spec.ownership_log) + \
+                        [[resume_step, spec.mb_owner]]
+                    new_spec.finalize()
+                spec = new_spec
+                rec = {"step": resume_step, "reschedule": True, "note": note,
+                       "owner_changed": bool(spec.ownership_log and
+                                             spec.ownership_log[-1][0] == resume_step)}
                 self.replans.append(rec)
                 self.events.append(("reschedule", None, rec))
                 with open(os.path.join(run_dir, "spec.json"), "w") as f:
@@ -860,15 +868,28 @@ class Coordinator:
         return got
 
     def _reschedule_plan(self, spec, windows, step, final):
-        """The order half of a re-plan: the zero-bubble order re-solved from the
-        window's measured F / B / W (the cut and the ownership stay, so no bit
-        changes), applied when it is `replan_min_gain` shorter and saves more
-        than twice `replan_cost_s` over the remaining steps."""
+        """A re-plan from the window's measured F / B / W, the cut kept: on a
+        chain of width-1 stages the zero-bubble order is re-solved (no bit
+        changes); with a wide stage the ownership is re-solved too (each
+        peer's share of the microbatches from its measured rate,
+        `rebalance.replan_ownership`), and the run records the old table in
+        `ownership_log` from the resume step on. Applied when it is
+        `replan_min_gain` shorter and saves more than twice `replan_cost_s`
+        over the remaining steps."""
         from elysium_wan_b200.scheduler import rebalance as rb
 
+        owners = None
         try:
             profiles = rb.profiles_from_telemetry(spec, windows)
-            res = rb.replan_schedule(spec, profiles, self.cfg.replan_min_gain)
+            if any(w > 1 for w in spec.stage_widths):
+                got = rb.replan_ownership(spec, profiles, self.cfg.replan_min_gain)
+                self.events.append(("replan_eval", None, {"step": step, "why": got["why"]}))
+                res = None
+                if got["decision"]:
+                    res = got["schedule_order"], got["pred_cur_s"], got["pred_new_s"]
+                    owners = got
+            else:
+                res = rb.replan_schedule(spec, profiles, self.cfg.replan_min_gain)
         except ValueError as e:
             self.events.append(("reschedule_skipped", None, {"step": step, "why": str(e)}))
             return None
@@ -885,6 +906,11 @@ class Coordinator:
         d = spec.to_dict()
         d.update(schedule_order=order, stage_costs=rb.stage_costs_from_profiles(
             profiles, spec.peer_weights), resume=False, resume_step=None)
+        if owners is not None:
+            d.update(peer_weights=owners["peer_weights"], mb_owner=owners["mb_owner"],
+                     stage_costs=owners["stage_costs"])
+            if owners["owner_changed"]:
+                note += f"; peer weights {spec.peer_weights} -> {owners['peer_weights']}"
         nspec = JobSpec.from_dict(d)
         nspec.finalize()
         return "reschedule", (nspec, note)

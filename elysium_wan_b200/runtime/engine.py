@@ -64,7 +64,8 @@ class StageEngine:
         self.telemetry: list = []
         self._host_x = None
 
-        self.sim_slow = parse_sim_slow().get(stage, (1.0, 0))
+        slow = parse_sim_slow()
+        self.sim_slow = slow.get((stage, peer), slow.get(stage, (1.0, 0)))
         self.w_pair = bool(spec.w_pair) and spec.stage_widths[stage] == 1
         # W fill (reference RUNTIME-I27, src/wantrain/runtime/stage.py:3353-3373):
         # on host devices a receive that is late runs deferred W tasks, one

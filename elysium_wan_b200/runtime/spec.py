@@ -77,6 +77,12 @@ class JobSpec:
     partition: list | None = None
     peer_weights: list | None = None
     mb_owner: list | None = None
+    # The ownership earlier steps ran under, oldest first: [until_step,
+    # mb_owner] means steps before until_step used that mb_owner (a re-plan
+    # moved microbatches between the replicas of a wide stage at a wave). The
+    # declared dp_tree fold of a step follows the ownership it ran under, so
+    # the oracle reads it (`owner_at`).
+    ownership_log: list = field(default_factory=list)
     stream_grads: bool = False
     # ------------------------------------------------------------- schedule
     schedule_order: list | None = None
@@ -131,6 +137,13 @@ class JobSpec:
     def owned(self, rank: int, peer: int) -> list:
         """Microbatches slot (stage `rank`, `peer`) computes, ascending."""
         return [mb for mb, p in enumerate(self.mb_owner[rank]) if p == peer]
+
+    def owner_at(self, step: int) -> list:
+        """The mb_owner table step `step` ran (or runs) under."""
+        for until, owners in self.ownership_log:
+            if step < int(until):
+                return owners
+        return self.mb_owner
 
     def device_for(self, stage: int, peer: int = 0) -> str:
         if self.devices is not None:
@@ -188,6 +201,16 @@ class JobSpec:
         for r, row in enumerate(self.mb_owner):
             if len(row) != self.microbatches or not all(0 <= p < self.stage_widths[r] for p in row):
                 raise ValueError(f"mb_owner[{r}] must map every microbatch to a peer of stage {r}")
+        last = 0
+        for entry in self.ownership_log:
+            until, owners = int(entry[0]), entry[1]
+            if until <= last or len(owners) != self.stages or any(
+                    len(row) != self.microbatches or
+                    not all(0 <= int(p) < self.stage_widths[r] for p in row)
+                    for r, row in enumerate(owners)):
+                raise ValueError("ownership_log entries are [until_step, mb_owner] with rising "
+                                 "steps and tables of this spec's shape")
+            last = until
         if self.model.tie_embeddings and self.stages > 1 and \
                 (self.stage_widths[0] != 1 or self.stage_widths[-1] != 1):
             raise NotImplementedError("a tied table across a cut needs width-1 first and last "

@@ -12,6 +12,7 @@ the gaps before F and B ops (each starts once its input has arrived).
 from __future__ import annotations
 
 import json
+import math
 import os
 import statistics
 
@@ -59,13 +60,29 @@ def summarize_step(step, stage, peer, step_ms, op_times, bytes_sent, frames,
 
 
 def parse_sim_slow(value: str | None = None) -> dict:
-    """WANTRAIN_SIM_SLOW="stage:factor[@from_step],...": a timing-only seam
-    (moves when, never what): the stage's ops take `factor` x their time from
-    `from_step` on (default 0). -> {stage: (factor, from_step)}."""
+    """WANTRAIN_SIM_SLOW, a timing-only seam (moves when, never what): the
+    named stage's ops take `factor` x their time from `from_step` on (default
+    0). Comma-separated parts, each either "stage:factor[@from_step]" (every
+    peer of the stage) or the reference's one-slot form
+    "rank:peer:factor[:from_step]" (src/wantrain/runtime/telemetry.py:81).
+    -> {stage or (stage, peer): (factor, from_step)}."""
     value = value if value is not None else os.environ.get("WANTRAIN_SIM_SLOW", "")
     out = {}
     for part in filter(None, value.split(",")):
-        k, _, v = part.partition(":")
-        f, _, s = v.partition("@")
-        out[int(k)] = (float(f), int(s) if s else 0)
+        f = part.split(":")
+        try:
+            if len(f) == 2:
+                fac, _, st = f[1].partition("@")
+                key, factor, start = int(f[0]), float(fac), int(st) if st else 0
+            elif len(f) in (3, 4):
+                key, factor = (int(f[0]), int(f[1])), float(f[2])
+                start = int(f[3]) if len(f) == 4 else 0
+            else:
+                raise ValueError
+        except ValueError:
+            raise ValueError(f"WANTRAIN_SIM_SLOW={value!r}: expected stage:factor[@from_step] "
+                             "or rank:peer:factor[:from_step]") from None
+        if not (math.isfinite(factor) and factor >= 1.0) or start < 0:
+            raise ValueError(f"WANTRAIN_SIM_SLOW={value!r}: a finite factor >= 1, from_step >= 0")
+        out[key] = (factor, start)
     return out

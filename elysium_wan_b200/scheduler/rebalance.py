@@ -161,3 +161,91 @@ def replan_schedule(spec, profiles: list, min_gain: float = 0.10):
     if new > (1.0 - min_gain) * cur:
         return None
     return new_order, cur, new
+
+
+def measured_model(profiles: list) -> tuple[list, list]:
+    """(speeds, costs) of a window: speeds[stage][peer] is the peer's measured
+    rate (microbatches per second over F + B + W), costs[stage] the [F, B, W]
+    seconds under which `simulate_slots` gives peer q of a stage an op time of
+    cost x sum(speeds) / speeds[q], the peer's measured time (exactly so when
+    a stage's peers differ by one factor; otherwise the op mix is averaged)."""
+    speeds, costs = [], []
+    for row in profiles:
+        w = [1.0 / max(1e-9, p["t_f"] + p["t_b"] + p["t_w"]) for p in row]
+        speeds.append(w)
+        costs.append([sum(p[k] * wq for p, wq in zip(row, w)) / len(row) / sum(w)
+                      for k in ("t_f", "t_b", "t_w")])
+    return speeds, costs
+
+
+def _with_one_each(n: int, weights: list) -> list:
+    """Weights under which IWRR leaves no peer without a microbatch: a peer
+    that gets none has its weight doubled until it does."""
+    from elysium_wan_b200.scheduler.zero_bubble import iwrr
+
+    w = list(weights)
+    for _ in range(64):
+        got = set(iwrr(n, w))
+        if len(got) == len(w):
+            return w
+        for q in range(len(w)):
+            if q not in got:
+                w[q] *= 2.0
+    raise ValueError("cannot give every peer a microbatch")
+
+
+def replan_ownership(spec, profiles: list, min_gain: float = 0.10) -> dict:
+    """Re-solve a job's ownership and order from measured per-peer costs
+    (reference: scheduler/zero_bubble.py:1079 `replan`, both halves). Each
+    wide stage's peer weights become its peers' measured rates (every peer
+    keeps at least one microbatch, so the next window measures it again), the
+    microbatches are re-dealt by IWRR and the zero-bubble order re-solved.
+    Both predictions run the same measured model (`measured_model`), so a
+    bias of the profile cancels. Only peer_weights, mb_owner and
+    schedule_order change. Unlike the reference's per-microbatch fold, this
+    engine's declared `dp_tree` fold sums each replica's own microbatches
+    first, so moving microbatches moves bits: the caller records the old table
+    in the spec's `ownership_log` from the resume step on, and the oracle
+    follows it.
+
+    -> {"decision", "pred_cur_s", "pred_new_s", "peer_weights", "mb_owner",
+    "schedule_order", "stage_costs", "owner_changed", "why"}."""
+    import copy
+
+    from elysium_wan_b200.scheduler.planner import zb_config
+    from elysium_wan_b200.scheduler.zero_bubble import simulate_slots
+
+    if not 0.0 <= min_gain < 1.0:
+        raise ValueError(f"min_gain must be in [0, 1), got {min_gain}")
+    speeds, costs = measured_model(profiles)
+    cur = copy.deepcopy(spec)
+    cur.stage_costs = costs
+    cfg = zb_config(cur)
+
+    def predict(order):
+        slots = [[[(op, int(mb)) for op, mb in o] for o in per_stage] for per_stage in order]
+        return simulate_slots(cfg, slots, speeds)[1]
+
+    pred_cur = predict(spec.schedule_order)
+    new = copy.deepcopy(spec)
+    new.stage_costs = costs
+    new.peer_weights = [[round(x / max(row), 4) for x in _with_one_each(spec.microbatches, row)]
+                        if len(row) > 1 else [1.0] for row in speeds]
+    new.mb_owner, new.schedule_order = None, None
+    new.finalize()
+    pred_new = predict(new.schedule_order)
+    owner_changed = new.mb_owner != spec.mb_owner
+    order_changed = new.schedule_order != spec.schedule_order
+    gain_ok = pred_new <= (1.0 - min_gain) * pred_cur
+    decision = gain_ok and (owner_changed or order_changed)
+    if decision:
+        why = f"predicted {pred_cur:.6g} s -> {pred_new:.6g} s per step"
+    elif not (owner_changed or order_changed):
+        why = "the re-solve gives the current ownership and order"
+    else:
+        why = (f"predicted {pred_cur:.6g} s -> {pred_new:.6g} s per step, below the "
+               f"{min_gain:.0%} threshold")
+    return {"decision": decision, "pred_cur_s": pred_cur, "pred_new_s": pred_new,
+            "peer_weights": new.peer_weights, "mb_owner": new.mb_owner,
+            "schedule_order": new.schedule_order, "stage_costs": costs,
+            "owner_changed": owner_changed, "why": why}

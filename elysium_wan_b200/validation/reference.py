@@ -3,7 +3,8 @@
 Reference: run_baseline (src/wantrain/validation/reference.py:189-362). Here
 the oracle builds one StageModel per pipeline stage on ONE device and runs the
 microbatches through them in index order; per stage it keeps one fp32 partial
-gradient per ZeRO-1 replica (the replica that owns the microbatch) and folds
+gradient per ZeRO-1 replica (the replica that owns the microbatch at that
+step: `spec.owner_at`, which follows a re-plan's ownership changes) and folds
 the partials in rank order before AdamW, which is the declared `dp_tree` fold
 of the distributed run. Cutting the model into stages changes no value (the
 boundary recipe is applied at every block boundary), so a stage-count change
@@ -71,6 +72,7 @@ class Oracle:
                 for p in part:
                     p.zero_()
         out = []
+        owners = spec.owner_at(step)  # a re-plan may have moved microbatches between replicas
         for mb in range(spec.microbatches):
             x, t = make_batch(spec.data_seed, step, mb, spec.mb_size, spec.model.seq_len,
                               spec.model.vocab_size, dataset=spec.dataset_path,
@@ -81,7 +83,7 @@ class Oracle:
             for r, m in enumerate(self.stages):
                 if self.partials[r] is not None:
                     saved_grads.append(m.store.grad)
-                    m.store.grad = self.partials[r][spec.mb_owner[r][mb]]
+                    m.store.grad = self.partials[r][owners[r][mb]]
             ctxs, h = [], x
             for m in self.stages:
                 h, c = m.forward(h, t if m.last else None)

@@ -339,6 +339,84 @@ def test_reschedule_from_telemetry_matches_oracle(tmp_path):
     assert r["ok"] and r["compared"] == M * 10, r
 
 
+def test_ownership_replan_from_telemetry_matches_oracle(tmp_path):
+    """One replica of a wide stage computes 4x slower from step 2 on (the
+    reference's one-slot form of the timing-only seam). At a common wave the
+    coordinator re-solves the stage's peer weights from the measured rates,
+    re-deals the microbatches (the slow replica keeps at least one), re-solves
+    the order and relaunches from the wave; the spec records the table the
+    earlier steps ran under, and the losses equal the oracle that follows it."""
+    import json
+    import os
+
+    cfg = make_config("toy", n_layer=4, vocab_size=97, d_model=64, n_head=4, seq_len=16)
+    spec = JobSpec(model=cfg, stages=2, stage_widths=[1, 2], microbatches=8, mb_size=1,
+                   steps=10, backend="gloo", tag="ow", ckpt_every=2, partition=[[0, 3], [3, 6]])
+    cl = LocalCluster(str(tmp_path / "cl"), ["r0", "r0", "r0"],
+                      coord=dict(profile=False, recut=False, watch_slow=False,
+                                 replan_cost_s=0.0, replan_min_gain=0.1,
+                                 replan_min_summaries=2),
+                      worker_env={"WANTRAIN_SIM_SLOW": "1:1:4:2"})
+    try:
+        res = cl.run(Job(spec=spec))
+        replans = list(cl.coord.replans)
+    finally:
+        cl.close()
+    assert res.ok, res.why
+    assert replans and replans[0].get("owner_changed"), replans
+    with open(os.path.join(res.run_dir, "spec.json")) as f:
+        ran = JobSpec.from_dict(json.load(f))
+    assert ran.ownership_log and ran.ownership_log[0][1] == spec.finalize().mb_owner
+    fast, slow = ran.peer_weights[1]
+    assert slow < fast and ran.owned(1, 1) and len(ran.owned(1, 0)) > len(ran.owned(1, 1))
+    ref = JobSpec.from_dict(ran.to_dict())
+    ref.out_dir = str(tmp_path / "oracle")
+    ref.resume, ref.resume_step = False, None
+    ref.finalize()
+    r = compare(run_baseline(ref, "reference"), res.losses_path)
+    assert r["ok"] and r["compared"] == 80, r
+    # the oracle of the launch ownership alone differs after the re-plan
+    plain = JobSpec.from_dict(spec.to_dict())
+    plain.out_dir = str(tmp_path / "oracle_plain")
+    plain.finalize()
+    assert not compare(run_baseline(plain, "reference"), res.losses_path)["ok"]
+
+
+def test_ownership_log_and_sim_slow_rules():
+    from elysium_wan_b200.runtime.telemetry import parse_sim_slow
+    from elysium_wan_b200.scheduler import rebalance as rb
+
+    assert parse_sim_slow("1:3") == {1: (3.0, 0)}
+    assert parse_sim_slow("1:2@5,0:1:4:2") == {1: (2.0, 5), (0, 1): (4.0, 2)}
+    for bad in ("1", "1:0.5", "a:2", "1:1:2:3:4"):
+        with pytest.raises(ValueError):
+            parse_sim_slow(bad)
+    cfg = make_config("toy", n_layer=4, vocab_size=97, d_model=64, n_head=4, seq_len=16)
+    spec = JobSpec(model=cfg, stages=2, stage_widths=[1, 2], microbatches=8, mb_size=1).finalize()
+    old = spec.mb_owner
+    summ = lambda f, b, w: {"ops": {"F": {"n": 4, "med_ms": f}, "B": {"n": 4, "med_ms": b},  # noqa: E731
+                                    "W": {"n": 4, "med_ms": w}}}
+    even = {(0, 0): [summ(1, 2, 1)] * 3, (1, 0): [summ(1, 2, 1)] * 3, (1, 1): [summ(1, 2, 1)] * 3}
+    r = rb.replan_ownership(spec, rb.profiles_from_telemetry(spec, even))
+    assert not r["owner_changed"] and not r["decision"]
+    # one replica 8x slower: it keeps one microbatch (IWRR alone would give it none)
+    slow = dict(even)
+    slow[(1, 1)] = [summ(8, 16, 8)] * 3
+    r = rb.replan_ownership(spec, rb.profiles_from_telemetry(spec, slow))
+    assert r["decision"] and r["owner_changed"] and r["pred_new_s"] < r["pred_cur_s"]
+    assert r["mb_owner"][1].count(1) >= 1 and r["mb_owner"][1].count(0) > r["mb_owner"][1].count(1)
+    assert r["mb_owner"][0] == old[0]
+    # the log: steps before 4 ran under the launch table
+    spec.ownership_log = [[4, old]]
+    spec.mb_owner = r["mb_owner"]
+    spec.schedule_order = r["schedule_order"]
+    spec.finalize()
+    assert spec.owner_at(3) == old and spec.owner_at(4) == r["mb_owner"]
+    spec.ownership_log = [[4, old], [2, old]]
+    with pytest.raises(ValueError):
+        spec.finalize()
+
+
 def test_unrouted_chain_gives_the_hungriest_rank_the_largest_card(tmp_path):
     """Without probing, a chain on cards of different memory is ordered so the
     rank needing the most memory gets the largest card; equal cards keep the
