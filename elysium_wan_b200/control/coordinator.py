@@ -71,6 +71,13 @@ from elysium_wan_b200.fault_tolerance.liveness import LivenessJudge, SlotState
 from elysium_wan_b200.fault_tolerance.replacement import find_replacement
 from elysium_wan_b200.resources.node import NodeInfo, mixed_fleet
 from elysium_wan_b200.runtime.spec import JobSpec
+
+# The fit loop (`Coordinator._fit_loop`): remedies tried before a job that does
+# not fit is refused, and how far an overshooting stage's planning memory
+# drops per unit of excess (the analytic model misses by a per-layer amount,
+# so one re-cut usually clears it).
+FIT_ATTEMPTS = 4
+MEM_FEEDBACK = 1.25
 from elysium_wan_b200.transport.control import (Channel, Spilled, body_sha256, check_mac,
                                                 control_listen, new_nonce, write_body)
 
@@ -144,6 +151,10 @@ class _Node:
         self.last_heartbeat = time.time()
         self.stage_alive = None
         self.dead = False
+
+
+def _size(n: float) -> str:
+    return f"{n / 2**30:.2f} GiB" if n >= 2**30 else f"{n / 2**20:.1f} MiB"
 
 
 def _free_port() -> int:
@@ -608,8 +619,9 @@ class Coordinator:
         if admission is not None and not admission["ok"]:
             why = "admission refused: " + "; ".join(admission["reasons"])
             return RunResult(False, self.run_id, None, 0, 0, 0, why, run_dir)
+        fit_notes = None
         if not self.cfg.no_fit_check:
-            fits, why = self._fit_check(spec, slots)
+            fits, why, fit_notes = self._fit_loop(spec, slots, cut_given)
             if not fits:
                 return RunResult(False, self.run_id, None, 0, 0, 0, why, run_dir)
         self._final_step = spec.steps - 1
@@ -619,7 +631,7 @@ class Coordinator:
             json.dump({"placement": {f"{s[0]}:{s[1]}": self.slot_node[s] for s in slots},
                        "spares": spares, "links": spec.links, "measured_links": measured,
                        "admission": admission, "schedule": schedule, "route": route,
-                       "plan": self.plan_rationale},
+                       "plan": self.plan_rationale, "fit": fit_notes},
                       f, indent=1)
         heals = restarts = 0
         resume_step = None
@@ -816,15 +828,114 @@ class Coordinator:
 
     def _fit_check(self, spec, slots):
         """Every slot builds its real slice on its node and holds the
-        schedule's peak in-flight microbatches (resources/fit.py)."""
+        schedule's peak in-flight microbatches (resources/fit.py). -> (why a
+        fit could not run or None, {stage: overshoot}) where an overshoot is
+        the worst slot's {"peak", "budget", "base", "oom"} in bytes: a peak
+        above the node's memory less its reserve, or an out-of-memory fit
+        (whose demand is unknown: the peak counts as the whole device)."""
+        from elysium_wan_b200.scheduler.admission import vram_reserve
+
         got = self._ask_slots("FIT", "FIT_RESULT", spec, slots, self.cfg.profile_timeout_s)
+        over: dict = {}
         for s in slots:
             r = got[s]
             if not r.get("ok"):
-                return False, f"fit of slot {s} failed: {r.get('why')}"
-            if not r.get("fits"):
-                return False, f"slot {s} does not fit: peak {r.get('peak_bytes')} bytes"
-        return True, ""
+                return f"fit of slot {s} failed: {r.get('why')}", {}
+            mem = self.nodes[self.slot_node[s]].info.memory_bytes()
+            budget = mem - vram_reserve(mem) if mem else None
+            oom = not r.get("fits")
+            peak = float(r.get("peak_bytes") or 0)
+            if oom:
+                peak = max(peak, mem or 0.0)
+            if not oom and (budget is None or peak <= budget):
+                continue
+            if budget is None:
+                return f"slot {s} does not fit: peak {int(peak)} bytes", {}
+            prev = over.get(s[0])
+            if prev is None or peak - budget > prev["peak"] - prev["budget"]:
+                over[s[0]] = {"peak": peak, "budget": budget,
+                              "base": float(r.get("base_bytes") or 0), "oom": oom}
+        return None, over
+
+    def _fit_loop(self, spec, slots, cut_given: bool):
+        """The fit check with feedback (reference behaviour: coordinator.py
+        :1500-1570, FIT_ATTEMPTS, `calibrated_budget`, `shrink_for_overshoot`).
+        The memory models are analytic, the fit is measured; a stage that
+        overshoots its node's budget is answered in this order, one remedy per
+        attempt, the fit measured again after each:
+
+        1. a stage that keeps F's tensors recomputes them instead;
+        2. the schedule's activation budget of the stage is calibrated: the
+           model's in-flight activations are scaled by what the fit really
+           held beyond the stage's resident state, and the zero-bubble order
+           is solved again under the budget that leaves (fewer microbatches
+           in flight there; the cut keeps its balance);
+        3. unless the job pinned its cut, the stage plans with less memory
+           (its budget less MEM_FEEDBACK x the excess) and the chain is cut
+           again by the memory model, moving layers off it.
+
+        -> (fits, why, notes)."""
+        from elysium_wan_b200.scheduler import rebalance as rb
+        from elysium_wan_b200.scheduler.planner import default_schedule
+
+        notes: list = []
+        caps: dict = {}
+        shrunk: dict = {}
+        why = ""
+        for attempt in range(FIT_ATTEMPTS):
+            bad, over = self._fit_check(spec, slots)
+            if bad:
+                return False, bad, notes
+            if not over:
+                return True, "", notes
+            why = "; ".join(f"stage {r} peaks at {_size(o['peak'])} of a {_size(o['budget'])} "
+                            "budget" for r, o in sorted(over.items()))
+            if attempt == FIT_ATTEMPTS - 1:
+                break
+            keep = [r for r in sorted(over) if not spec.recomputes(r)]
+            if keep:
+                spec.recompute_stages = [spec.recomputes(r) or r in keep
+                                         for r in range(spec.stages)]
+                spec.reschedule()
+                notes.append(f"{why}: stages {keep} recompute")
+                continue
+            fresh = [r for r in sorted(over) if r not in caps]
+            if fresh:
+                for r in fresh:
+                    o = over[r]
+                    caps[r] = rb.calibrated_budget(spec, r, o["peak"], o["budget"], o["base"],
+                                                   oom=o["oom"], feedback=MEM_FEEDBACK)
+                spec.schedule_order = default_schedule(spec, rb.budget_list(spec, caps))
+                spec.finalize()
+                notes.append(f"{why}: the schedule holds at most " + ", ".join(
+                    f"{_size(caps[r])} of activations on stage {r}" for r in fresh))
+                continue
+            if cut_given:
+                break
+            for r, o in over.items():
+                shrunk[r] = max(0.0, min(shrunk.get(r, o["budget"]),
+                                         o["budget"] - MEM_FEEDBACK * (o["peak"] - o["budget"])))
+            budgets = [shrunk.get(r, self._stage_budget(r)) for r in range(spec.stages)]
+            new = rb.memory_partition(spec, budgets)
+            if new is None:
+                break
+            notes.append(f"{why}: re-cut {spec.partition} -> {new}")
+            spec.partition, caps = new, {}
+            spec.stage_costs = None
+            spec.reschedule()
+        return False, f"does not fit after {len(notes)} remedies: {why}", notes
+
+    def _stage_budget(self, r: int) -> float:
+        """The smallest memory budget among stage r's nodes (inf when unknown)."""
+        from elysium_wan_b200.scheduler.admission import vram_reserve
+
+        out = math.inf
+        for (st, _p), nid in self.slot_node.items():
+            if st == r:
+                mem = self.nodes[nid].info.memory_bytes()
+                if mem:
+                    out = min(out, mem - vram_reserve(mem))
+        return out
 
     def _admit(self, spec, slots) -> dict | None:
         """Admission of a job with wide stages (scheduler/admission.py) on the

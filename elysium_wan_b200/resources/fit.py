@@ -23,6 +23,25 @@ def measure(spec, stage: int, device: str = "cpu") -> dict:
     if dev.type == "cuda":
         torch.cuda.reset_peak_memory_stats(dev)
     eng = StageEngine(spec, stage, 0, None, dev)
+    opt = eng.opt
+    if eng.pieces:
+        # the two range optimizers of replica 0 of a pieces stage
+        from elysium_wan_b200.parallel.pieces import Pieces
+
+        pc = Pieces(eng, None)
+        opt = _Both(pc.opt_r, pc.opt_m)
+    elif opt is None:
+        # A wide stage: one replica's ZeRO-1 shard of the moments.
+        from elysium_wan_b200.parallel.zero1 import shard_bounds
+        from elysium_wan_b200.runtime import optim
+
+        st_ = eng.store
+        lo, hi = shard_bounds(st_.nt, eng.width)[0]
+        opt = optim.build(spec.optimizer, st_.master[lo:hi], st_.grad[lo:hi],
+                          st_.work[lo:hi] if st_.work is not None else None, spec.lr,
+                          spec.adamw)
+    # what the stage holds before any microbatch: parameters, gradients, moments
+    base = torch.cuda.memory_allocated(dev) if dev.type == "cuda" else 0
     k = peak_pending(spec.schedule_order[stage][0])
     ok = True
     try:
@@ -42,19 +61,18 @@ def measure(spec, stage: int, device: str = "cpu") -> dict:
             out, st = eng.model.forward(inp, t.to(dev) if eng.last else None,
                                         keep="inputs" if eng.recompute else "all")
             saved.append(st)
-        opt = eng.opt
-        if opt is None:
-            # A wide stage: one replica's ZeRO-1 shard of the moments.
-            from elysium_wan_b200.parallel.zero1 import shard_bounds
-            from elysium_wan_b200.runtime import optim
-
-            st_ = eng.store
-            lo, hi = shard_bounds(st_.nt, eng.width)[0]
-            opt = optim.build(spec.optimizer, st_.master[lo:hi], st_.grad[lo:hi],
-                              st_.work[lo:hi] if st_.work is not None else None, spec.lr,
-                              spec.adamw)
         opt.step()
     except torch.cuda.OutOfMemoryError:
         ok = False
     peak = torch.cuda.max_memory_allocated(dev) if dev.type == "cuda" else 0
-    return {"fits": ok, "peak_bytes": int(peak), "in_flight": k, "params": int(eng.store.numel)}
+    return {"fits": ok, "peak_bytes": int(peak), "base_bytes": int(base), "in_flight": k,
+            "params": int(eng.store.numel)}
+
+
+class _Both:
+    def __init__(self, *opts):
+        self.opts = opts
+
+    def step(self):
+        for o in self.opts:
+            o.step()

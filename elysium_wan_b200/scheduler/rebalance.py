@@ -249,3 +249,72 @@ def replan_ownership(spec, profiles: list, min_gain: float = 0.10) -> dict:
             "peer_weights": new.peer_weights, "mb_owner": new.mb_owner,
             "schedule_order": new.schedule_order, "stage_costs": costs,
             "owner_changed": owner_changed, "why": why}
+
+
+# ------------------------------------------------------------- fit feedback
+def order_peak(order, deltas: dict) -> float:
+    """Peak activation bytes an order holds (F adds deltas["F"], B and W
+    their own, usually negative, deltas)."""
+    m = peak = 0.0
+    for op, _mb in order:
+        m += deltas[op]
+        peak = max(peak, m)
+    return peak
+
+
+def calibrated_budget(spec, stage: int, peak: float, budget: float, base: float,
+                      oom: bool = False, feedback: float = 1.25) -> float:
+    """The activation budget, in the memory model's bytes, under which
+    `stage`'s schedule fits after a measured overshoot (reference behaviour:
+    `calibrated_budget`, src/wantrain/coordinator/coordinator.py:3100-3136).
+    The fit held `peak` bytes of which `base` were resident before any
+    microbatch; the model expected the order's in-flight peak. The ratio of
+    the two activation figures (times `feedback` again for an out-of-memory
+    fit, whose demand is unknown) scales the room the budget leaves. Never
+    below one microbatch's F and B."""
+    from elysium_wan_b200.scheduler.planner import stage_memory_model
+
+    mf, mb, mw = stage_memory_model(spec, stage)
+    modeled = max(order_peak(o, {"F": mf, "B": mb, "W": mw}) for o in spec.schedule_order[stage])
+    factor = max(1.0, (peak - base) / max(1.0, modeled)) * (feedback if oom else 1.0)
+    return max(mf, mf + mb, (budget - base) / factor)
+
+
+def budget_list(spec, caps: dict) -> list:
+    """Per-stage schedule budgets: the calibrated caps, no cap elsewhere."""
+    return [float(caps.get(r, math.inf)) for r in range(spec.stages)]
+
+
+def memory_partition(spec, budgets: list) -> list | None:
+    """A cut that every stage's memory allows: the min-max cost partition
+    (the model's per-entry costs; a wide stage's replicas add their weights'
+    throughput) among the cuts in which each stage's resident state (its
+    layout's parameters, gradients and moments) plus the zero-bubble warm-up's
+    (stages - r) microbatches of F activations fits `budgets[r]`. None when no
+    cut fits or the answer is the current cut."""
+    import copy
+
+    from elysium_wan_b200.scheduler import admission as ad
+    from elysium_wan_b200.scheduler.planner import stage_memory_model
+
+    costs = layer_costs(spec.model)
+    host = spec.optimizer == "adamw-host"
+    need: dict = {}
+
+    def fits(r, lo, hi):
+        if (r, lo, hi) not in need:
+            s2 = copy.copy(spec)
+            s2.partition = [list(x) for x in spec.partition]
+            s2.partition[r] = [lo, hi]
+            mf, _, _ = stage_memory_model(s2, r)
+            t = ad.stage_terms(s2, r)
+            need[(r, lo, hi)] = ad.device_bytes(t, spec.stage_widths[r], spec.shard, 0, host) + \
+                max(1, spec.stages - r) * max(0.0, mf)
+        return need[(r, lo, hi)] <= budgets[r]
+
+    speed = [float(sum(w)) for w in spec.peer_weights]
+    try:
+        new = [list(x) for x in assign_layers(costs, speed, fits)]
+    except ValueError:
+        return None
+    return None if new == [list(x) for x in spec.partition] else new

@@ -476,3 +476,127 @@ def test_control_channel_streams_large_bodies_to_disk(tmp_path):
     t.join(10)
     a.close()
     b.close()
+
+
+def _fit_rig(tmp_path, spec, mem_of_stage, over=1.3):
+    """A coordinator (not started) whose slots sit on nodes of the given
+    device memory, and a fake FIT whose device uses `over` x what the memory
+    model says: resident state, then the order's in-flight microbatches of F
+    activations."""
+    from elysium_wan_b200.control.coordinator import Coordinator, CoordinatorConfig, _Node
+    from elysium_wan_b200.resources.fit import peak_pending
+    from elysium_wan_b200.resources.node import NodeInfo
+    from elysium_wan_b200.scheduler import admission as ad
+    from elysium_wan_b200.scheduler.planner import stage_memory_model
+
+    co = Coordinator("127.0.0.1", 0, CoordinatorConfig(state_dir=str(tmp_path / "st")))
+    for r, p in spec.slots():
+        nid = f"n{r}{p}"
+        info = NodeInfo(node_id=nid, name=nid, device="cuda", device_class="B200",
+                        vram_gb=mem_of_stage[r] / 2**30)
+        co.nodes[nid] = _Node(info, None)
+        co.slot_node[(r, p)] = nid
+    calls = []
+
+    def fake(kind, result, sp, slots, timeout):
+        assert kind == "FIT"
+        calls.append([list(x) for x in sp.partition])
+        out = {}
+        for r, p in slots:
+            mf = stage_memory_model(sp, r)[0]
+            base = over * ad.device_bytes(ad.stage_terms(sp, r), sp.stage_widths[r], sp.shard, 0)
+            k = peak_pending(sp.schedule_order[r][p])
+            out[(r, p)] = {"ok": True, "fits": True, "peak_bytes": base + over * k * mf,
+                           "base_bytes": base}
+        return out
+
+    co._ask_slots = fake
+    return co, calls
+
+
+def test_fit_loop_recomputes_then_calibrates_the_schedule(tmp_path):
+    """A stage whose measured peak is above its node's budget first recomputes;
+    when that is not enough, its schedule is solved again under a budget
+    calibrated from the measurement (fewer microbatches in flight), and the
+    cut stays."""
+    from elysium_wan_b200.resources.fit import peak_pending
+    from elysium_wan_b200.scheduler import admission as ad
+    from elysium_wan_b200.scheduler.planner import stage_memory_model
+
+    cfg = make_config("toy", n_layer=6, vocab_size=97, d_model=256, n_head=4, seq_len=256)
+    spec = JobSpec(model=cfg, stages=3, microbatches=12, mb_size=4, backend="gloo",
+                   partition=[[0, 3], [3, 5], [5, 8]]).finalize()
+    # stage 0's node: room for its state and about 1.4 microbatches of
+    # recomputed activations in flight (its order holds 3 or more)
+    rec = JobSpec.from_dict(spec.to_dict())
+    rec.recompute = True
+    rec.schedule_order = None
+    rec.finalize()
+    state0 = 1.3 * ad.device_bytes(ad.stage_terms(rec, 0), 1, "zero1", 0)
+    mf0 = stage_memory_model(rec, 0)[0]
+    assert peak_pending(rec.schedule_order[0][0]) >= 3
+    budget0 = state0 + 1.3 * 1.4 * mf0
+    mem0 = budget0 / 0.88 if 0.12 * budget0 / 0.88 >= 2**30 else budget0 + 2**30
+    co, calls = _fit_rig(tmp_path, spec, [mem0, 1e12, 1e12])
+    ok, why, notes = co._fit_loop(spec, spec.slots(), cut_given=True)
+    assert ok, (why, notes)
+    assert "recompute" in notes[0] and "schedule holds at most" in notes[1], notes
+    assert spec.recomputes(0) and not spec.recomputes(1) and not spec.recomputes(2)
+    assert peak_pending(spec.schedule_order[0][0]) == 1
+    assert spec.partition == [[0, 3], [3, 5], [5, 8]] and len(calls) == 3
+
+
+def test_fit_loop_recuts_when_the_state_itself_overflows(tmp_path):
+    """A node too small for its stage's resident state: recompute and a
+    smaller schedule cannot help, so the stage plans with less memory and
+    the chain is cut again, moving layers off it; a pinned cut is refused
+    with the reason instead."""
+    from elysium_wan_b200.scheduler import admission as ad
+
+    cfg = make_config("toy", n_layer=6, vocab_size=97, d_model=256, n_head=4, seq_len=64)
+
+    def fresh(part=None):
+        return JobSpec(model=cfg, stages=2, microbatches=4, mb_size=1, backend="gloo",
+                       partition=part or [[0, 4], [4, 8]]).finalize()
+
+    spec = fresh()
+    state0 = 1.3 * ad.device_bytes(ad.stage_terms(spec, 0), 1, "zero1", 0)
+    budget0 = 0.8 * state0
+    mem0 = budget0 / 0.88 if 0.12 * budget0 / 0.88 >= 2**30 else budget0 + 2**30
+    co, calls = _fit_rig(tmp_path, spec, [mem0, 1e12])
+    ok, why, notes = co._fit_loop(spec, spec.slots(), cut_given=False)
+    assert ok, (why, notes)
+    assert "recompute" in notes[0] and "re-cut" in notes[-1], notes
+    assert spec.partition[0][1] < 4, spec.partition
+    pinned = fresh()
+    co, _ = _fit_rig(tmp_path / "b", pinned, [mem0, 1e12])
+    ok, why, notes = co._fit_loop(pinned, pinned.slots(), cut_given=True)
+    assert not ok and "does not fit" in why and "stage 0 peaks" in why, why
+
+
+def test_fit_check_runs_on_every_slot_before_launch(tmp_path):
+    """With the fit check on, every slot (a pieces replica among them) builds
+    its slice, holds its order's in-flight microbatches and steps its
+    optimizer before launch; the run's rationale records no remedy and the
+    losses equal the oracle."""
+    import json
+    import os
+
+    cfg = make_config("toy", n_layer=4, vocab_size=97, d_model=64, n_head=4, seq_len=16)
+    spec = JobSpec(model=cfg, stages=2, stage_widths=[1, 2], shard="pieces", microbatches=4,
+                   mb_size=2, steps=2, backend="gloo", tag="fit")
+    cl = LocalCluster(str(tmp_path / "cl"), ["r0", "r0", "r0"], coord=dict(no_fit_check=False))
+    try:
+        res = cl.run(Job(spec=spec))
+    finally:
+        cl.close()
+    assert res.ok, res.why
+    with open(os.path.join(res.run_dir, "rationale.json")) as f:
+        assert json.load(f)["fit"] == []
+    with open(os.path.join(res.run_dir, "spec.json")) as f:
+        ran = JobSpec.from_dict(json.load(f))
+    ref = JobSpec.from_dict(ran.to_dict())
+    ref.out_dir = str(tmp_path / "oracle")
+    ref.finalize()
+    r = compare(run_baseline(ref, "reference"), res.losses_path)
+    assert r["ok"] and r["compared"] == 8, r
