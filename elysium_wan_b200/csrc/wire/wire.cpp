@@ -21,6 +21,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <chrono>
 #include <cstdint>
 #include <cstring>
 #include <stdexcept>
@@ -432,6 +433,9 @@ size_t send_frame(int fd, int type, int codec, uint32_t step, uint32_t mb, int c
   const size_t n = static_cast<size_t>(info.size) * info.itemsize;
   std::string hdr = pack_header(type, codec, step, mb, chunk, shape, frag_idx, frag_cnt, n);
   size_t sent_h = 0, sent_p = 0;
+  bool stalled = false;
+  std::chrono::steady_clock::time_point stall_start;
+  long backoff_us = 1000;
   py::gil_scoped_release nogil;
   while (sent_h < hdr.size() || sent_p < n) {
     iovec iov[2];
@@ -450,8 +454,26 @@ size_t send_frame(int fd, int type, int codec, uint32_t step, uint32_t mb, int c
     const ssize_t w = sendmsg(fd, &mh, MSG_NOSIGNAL);
     if (w < 0) {
       if (errno == EINTR) continue;
+      // The kernel refused for lack of buffer space or would block: nothing
+      // was written, so the same bytes go again after a backoff (1 ms
+      // doubling to 100 ms); 5 s without progress raises the last error.
+      if (errno == ENOBUFS || errno == EAGAIN || errno == EWOULDBLOCK) {
+        const auto now = std::chrono::steady_clock::now();
+        if (!stalled) {
+          stalled = true;
+          stall_start = now;
+        } else if (now - stall_start >= std::chrono::seconds(5)) {
+          throw std::runtime_error(std::string("send failed: ") + std::strerror(errno) +
+                                   " for 5 s without progress");
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(backoff_us));
+        backoff_us = std::min(2 * backoff_us, 100000L);
+        continue;
+      }
       throw std::runtime_error(std::string("send failed: ") + std::strerror(errno));
     }
+    stalled = false;
+    backoff_us = 1000;
     size_t left = static_cast<size_t>(w);
     const size_t th = std::min(left, hdr.size() - sent_h);
     sent_h += th;

@@ -25,6 +25,8 @@ import socket
 import struct
 import threading
 
+from elysium_wan_b200.transport.sendall import send_all
+
 MAX_HEADER = 16 << 20
 MAX_BODY = 1 << 40
 SPILL_MIN = 64 << 20  # bodies this large go to a file as they arrive (when the channel has a spill dir)
@@ -102,12 +104,20 @@ class Channel:
         except OSError:
             pass
 
+    def _send(self, data) -> None:
+        """Every byte out; a plain socket retries the kernel's transient
+        refusals (transport/sendall.py), a sealed one does so per record."""
+        if getattr(self.sock, "sealed", False):
+            self.sock.sendall(data)
+        else:
+            send_all(self.sock, data)
+
     def send(self, kind: str, body: bytes = b"", **fields):
         hdr = json.dumps(dict(fields, kind=kind)).encode()
         with self.lock:
-            self.sock.sendall(struct.pack(">I", len(hdr)) + hdr + struct.pack(">Q", len(body)))
+            self._send(struct.pack(">I", len(hdr)) + hdr + struct.pack(">Q", len(body)))
             if body:
-                self.sock.sendall(body)
+                self._send(body)
 
     def send_file(self, kind: str, path: str, **fields):
         """Send a file as the body, streamed from disk in 4 MiB pieces (its
@@ -121,10 +131,10 @@ class Channel:
             fields["sha256"] = h.hexdigest()
         hdr = json.dumps(dict(fields, kind=kind)).encode()
         with self.lock, open(path, "rb") as f:
-            self.sock.sendall(struct.pack(">I", len(hdr)) + hdr + struct.pack(">Q", size))
+            self._send(struct.pack(">I", len(hdr)) + hdr + struct.pack(">Q", size))
             sent = 0
             for piece in iter(lambda: f.read(_CHUNK), b""):
-                self.sock.sendall(piece)
+                self._send(piece)
                 sent += len(piece)
             if sent != size:
                 raise ConnectionError(f"{path} changed size while being sent")

@@ -24,6 +24,8 @@ from cryptography.hazmat.primitives.asymmetric.ed25519 import Ed25519PrivateKey,
 from cryptography.hazmat.primitives.asymmetric.x25519 import X25519PrivateKey, X25519PublicKey
 from cryptography.hazmat.primitives.kdf.hkdf import HKDF
 
+from elysium_wan_b200.transport.sendall import send_all
+
 P2P_DOMAIN = "elysium-p2p|v1|"
 CTL_DOMAIN = "elysium-ctl|v1|"
 COMPLEMENT = {"dialer": "listener", "listener": "dialer", "coordinator": "worker",
@@ -78,7 +80,7 @@ def load_or_create_key(path: str | None = None) -> Ed25519PrivateKey:
 
 def _send(sock, obj: dict) -> bytes:
     b = json.dumps(obj, sort_keys=True, separators=(",", ":")).encode()
-    sock.sendall(struct.pack("<I", len(b)) + b)
+    send_all(sock, struct.pack("<I", len(b)) + b)
     return b
 
 

@@ -18,12 +18,15 @@ mode. The AEAD calls release the interpreter lock on large records.
 
 from __future__ import annotations
 
+import errno
 import struct
 
 from cryptography.exceptions import InvalidTag
 from cryptography.hazmat.primitives import hashes
 from cryptography.hazmat.primitives.ciphers.aead import AESGCM, ChaCha20Poly1305
 from cryptography.hazmat.primitives.kdf.hkdf import HKDFExpand
+
+from elysium_wan_b200.transport.sendall import enobufs_every, send_all
 
 CIPHERS = {"chacha20-poly1305": ChaCha20Poly1305, "aes-256-gcm": AESGCM}
 MAX_RECORD = 1 << 20
@@ -73,6 +76,16 @@ class SecureSocket:
         self._buf = b""
         self._off = 0
         self._failed = False
+        self._every = enobufs_every()
+        self._attempts = 0
+        self._seam = self._refuse if self._every else None
+
+    def _refuse(self):
+        """The ENOBUFS test seam: every N-th send attempt is refused before
+        it reaches the kernel (nothing written)."""
+        self._attempts += 1
+        if self._attempts % self._every == 0:
+            raise OSError(errno.ENOBUFS, "No buffer space available (test seam)")
 
     def fileno(self):
         return self.sock.fileno()
@@ -93,7 +106,8 @@ class SecureSocket:
         for i in range(0, len(view), MAX_RECORD):
             chunk = view[i:i + MAX_RECORD]
             hdr = _LEN.pack(len(chunk) + TAG)
-            self.sock.sendall(hdr + self.tx.aead.encrypt(self.tx.nonce(), bytes(chunk), hdr))
+            send_all(self.sock, hdr + self.tx.aead.encrypt(self.tx.nonce(), bytes(chunk), hdr),
+                     self._seam)
 
     def _fail(self, why: str):
         self._failed = True

@@ -490,3 +490,124 @@ def test_fp8_boundaries_over_tcp_wide_shaped_multiflow(tmp_path, monkeypatch, bo
     r = run_and_compare(spec, timeout=300)
     assert r["ok"], r
     assert r["compared"] == 12
+
+
+# ------------------------------------------------------- transient send refusals
+class _FlakyKernel:
+    """A fake at the kernel boundary: each send attempt takes the next entry
+    of a script (an errno: refused, nothing written; ("cut", n): write at
+    most n bytes; None: pass through) and hands what it lets through to a
+    real socketpair end, so the receiver reads the bytes really written."""
+
+    def __init__(self, sock, script):
+        self.sock, self.script, self.attempts = sock, list(script), 0
+
+    def send(self, data):
+        self.attempts += 1
+        act = self.script.pop(0) if self.script else None
+        if isinstance(act, int):
+            raise OSError(act, os.strerror(act))
+        if isinstance(act, tuple):
+            data = data[:act[1]]
+        return self.sock.send(data)
+
+
+def _drain(sock, n):
+    out = bytearray()
+    while len(out) < n:
+        b = sock.recv(n - len(out))
+        if not b:
+            break
+        out += b
+    return bytes(out)
+
+
+def test_send_all_retries_transient_refusals_from_the_same_offset():
+    import errno
+
+    from elysium_wan_b200.transport.sendall import send_all
+
+    a, b = socket.socketpair()
+    data = os.urandom(200_000)
+    k = _FlakyKernel(a, [errno.ENOBUFS, ("cut", 1000), errno.EAGAIN, errno.ENOBUFS, ("cut", 7),
+                         errno.EWOULDBLOCK])
+    got = []
+    t = threading.Thread(target=lambda: got.append(_drain(b, len(data))))
+    t.start()
+    send_all(k, data)
+    t.join(10)
+    assert got and got[0] == data
+    assert k.attempts >= 7  # four refusals, two cut sends, then the rest
+    a.close()
+    b.close()
+
+
+def test_send_all_raises_other_errors_at_once_and_gives_up_after_the_budget(monkeypatch):
+    import errno
+    import time
+
+    from elysium_wan_b200.transport import sendall
+
+    a, b = socket.socketpair()
+    k = _FlakyKernel(a, [errno.ECONNRESET, None])
+    with pytest.raises(ConnectionResetError):
+        sendall.send_all(k, b"x" * 10)
+    assert k.attempts == 1  # not retried
+    monkeypatch.setattr(sendall, "RETRY_BUDGET_S", 0.05)
+    k = _FlakyKernel(a, [errno.ENOBUFS] * 10_000)
+    t0 = time.monotonic()
+    with pytest.raises(OSError) as e:
+        sendall.send_all(k, b"x" * 10)
+    assert e.value.errno == errno.ENOBUFS and 0.05 <= time.monotonic() - t0 < 2.0
+    with pytest.raises(ValueError):
+        sendall.enobufs_every("1")
+    assert sendall.enobufs_every("") == 0 and sendall.enobufs_every("3") == 3
+    a.close()
+    b.close()
+
+
+def test_native_frame_writer_waits_out_a_full_socket_buffer():
+    """A non-blocking sender whose buffer fills answers EAGAIN; the native
+    frame writer offers the rest again until the reader drains it, and the
+    frame arrives whole."""
+    import time
+
+    a, b = socket.socketpair()
+    a.setsockopt(socket.SOL_SOCKET, socket.SO_SNDBUF, 64 << 10)
+    a.setblocking(False)
+    payload = os.urandom(8 << 20)
+    got = []
+
+    def reader():
+        time.sleep(0.3)  # the writer meets a full buffer first
+        got.append(framing.recv_frame(b))
+
+    t = threading.Thread(target=reader)
+    t.start()
+    n = codec.wire().send_frame(a.fileno(), framing.FWD, framing.RAW_F32, 3, 1, 0,
+                                [len(payload) // 4], payload, 0, 1)
+    t.join(30)
+    assert n > len(payload) and got
+    assert got[0].step == 3 and got[0].mb == 1 and bytes(got[0].payload) == payload
+    a.close()
+    b.close()
+
+
+def test_pipeline_over_sealed_tcp_with_refused_sends_is_bitwise(tmp_path, monkeypatch):
+    """WANTRAIN_TEST_ENOBUFS=3: every third send attempt of every sealed
+    socket is refused with ENOBUFS; the pipeline still equals the oracle."""
+    from elysium_wan_b200.launch.local import run_and_compare
+    from elysium_wan_b200.models.config import make_config
+    from elysium_wan_b200.runtime.spec import JobSpec
+
+    monkeypatch.setenv("ELYSIUM_PEER_KEY", str(tmp_path / "peer.key"))
+    monkeypatch.setenv("WANTRAIN_TEST_ENOBUFS", "3")
+    cfg = make_config("toy", n_layer=4, vocab_size=97, d_model=128, n_head=4, seq_len=16,
+                      boundary_dtype="bf16")
+    port = 31500 + (os.getpid() % 200) * 10
+    spec = JobSpec(model=cfg, stages=2, stage_widths=[1, 2], microbatches=4, mb_size=2, steps=2,
+                   out_dir=str(tmp_path), port_base=port, backend="tcp", wire_codec="planes",
+                   p2p_streams=2)
+    r = run_and_compare(spec, timeout=300)
+    assert r["ok"], r
+    assert r["compared"] == 8
