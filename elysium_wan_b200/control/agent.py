@@ -349,7 +349,8 @@ class WorkerAgent:
         names = sorted(os.listdir(wave_dir), key=lambda n: n == "wave.json")
         for n in names:
             self.ch and self.ch.send_file("CKPT", os.path.join(wave_dir, n), step=step, name=n,
-                                          run_id=a["run_id"], last=(n == "wave.json"))
+                                          run_id=a["run_id"], attempt=a.get("attempt"),
+                                          last=(n == "wave.json"))
 
     def _supervise(self, proc: StageProcess, a: dict):
         rc = proc.wait()

@@ -321,10 +321,12 @@ class Coordinator:
                 st.log_tail = hdr.get("tail", "")
             elif kind == "RESULT" and hdr.get("attempt") == self.attempt:
                 self.results[(hdr["stage"], hdr["peer"])] = hdr["losses"]
-            elif kind == "CKPT" and self.store is not None and hdr.get("run_id") == self.run_id:
+            elif kind == "CKPT" and self.store is not None and hdr.get("run_id") == self.run_id \
+                    and hdr.get("attempt") == self.attempt:
                 # The wave belongs to the slot of the connection that sent it;
                 # only a validated integer step and a plain file name are taken
-                # from the message (reference: checkpoint.py:727-745).
+                # from the message (reference: checkpoint.py:727-745). A part of
+                # an earlier attempt may belong to an abandoned timeline.
                 if slot is not None and body_sha256(body) == hdr.get("sha256"):
                     r, q = slot
                     try:
@@ -640,6 +642,13 @@ class Coordinator:
         t_start = time.time()
         why = ""
         while True:
+            if resume_step is not None:
+                # the run continues from resume_step: newer waves in the store
+                # belong to the abandoned timeline
+                gone = self.store.drop_after(self.run_id, spec.tag, resume_step)
+                if gone:
+                    self.events.append(("waves_dropped", None, {"after": resume_step,
+                                                                "waves": gone}))
             self._launch(spec, resume_step)
             verdict = self._monitor(spec, t_start)
             if verdict.kind == "done":
@@ -1125,9 +1134,7 @@ class Coordinator:
         return new, step
 
     def _resume_point(self, spec) -> int | None:
-        view = copy.copy(spec)
-        view.out_dir = os.path.join(self.store.root, self.run_id)
-        return ckpt.common_step(view)
+        return self.store.common_step(self.run_id, spec)
 
     def _restore(self, spec, slot, nid, step):
         """Ship the slot's wave at `step` from the store to its new worker.

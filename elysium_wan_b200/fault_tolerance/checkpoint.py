@@ -111,14 +111,27 @@ def prune(out_dir, tag, stage, peer, keep: int = WAVE_KEEP):
         shutil.rmtree(wave_dir(out_dir, tag, stage, peer, s), ignore_errors=True)
 
 
-def validate_wave(path: str) -> dict:
-    """Check wave.json and every listed file's size and sha256; returns the meta."""
+def validate_wave(path: str, step: int | None = None) -> dict:
+    """Check wave.json and every listed file's size and sha256, that the
+    directory holds nothing the manifest does not list, and (given `step`)
+    that the manifest names that step; returns the meta."""
     meta_p = os.path.join(path, "wave.json")
     if not os.path.exists(meta_p):
         raise ValueError(f"{path}: no wave.json (incomplete wave)")
-    with open(meta_p) as f:
-        meta = json.load(f)
-    for name, ent in meta["files"].items():
+    try:
+        with open(meta_p) as f:
+            meta = json.load(f)
+        files = dict(meta["files"])
+    except (json.JSONDecodeError, KeyError, TypeError) as e:
+        raise ValueError(f"{path}: unreadable wave.json ({e})") from None
+    if step is not None and meta.get("step") != step:
+        raise ValueError(f"{path}: wave.json names step {meta.get('step')!r}, not {step}")
+    extra = sorted(set(os.listdir(path)) - set(files) - {"wave.json"})
+    if extra:
+        raise ValueError(f"{path}: files the manifest does not list: {extra}")
+    for name, ent in files.items():
+        if not safe_name(name):
+            raise ValueError(f"{path}: bad file name {name!r} in wave.json")
         p = os.path.join(path, name)
         if not os.path.exists(p) or os.path.getsize(p) != ent["size"]:
             raise ValueError(f"{path}: {name} missing or truncated")
@@ -137,17 +150,56 @@ def load_latest(spec, stage: int, peer: int, step: int | None = None):
     for s in reversed(steps):
         path = wave_dir(spec.out_dir, spec.tag, stage, peer, s)
         try:
-            validate_wave(path)
+            validate_wave(path, s)
         except ValueError:
             continue
         # the restricted unpickler: tensors and plain containers only, so a
         # wave shipped from another machine cannot run code when it is read
-        state = torch.load(os.path.join(path, "state.pt"), map_location="cpu", weights_only=True)
+        try:
+            state = torch.load(os.path.join(path, "state.pt"), map_location="cpu",
+                               weights_only=True)
+        except Exception as e:  # noqa: BLE001 - any failure to read means "not a checkpoint"
+            raise ValueError(f"wave {path}: state.pt is not a checkpoint ({type(e).__name__})") \
+                from None
+        if not isinstance(state, dict):
+            raise ValueError(f"wave {path}: state.pt is not a checkpoint")
         diff = first_pin_difference(spec.pins(), state.get("pins", {}))
         if diff is not None:
             raise ValueError(f"wave {path} was written under another recipe: pin {diff!r} differs")
         return state, s
     raise FileNotFoundError(f"no valid wave for slot r{stage}p{peer} in {spec.out_dir}")
+
+
+def drop_after(out_dir: str, tag: str, stage: int, peer: int, step: int) -> list:
+    """Remove the slot's waves newer than `step` and the temporaries of a
+    writer killed mid-commit. A run resumed at `step` abandoned the timeline
+    those waves belong to (after a re-plan they may not even hold the same
+    bits), so a later resume point must never pick one; a fresh launch passes
+    -1 and keeps none. The alias follows the newest wave left. -> the steps
+    removed."""
+    d = slot_dir(out_dir, tag, stage, peer)
+    if not os.path.isdir(d):
+        return []
+    gone = []
+    for name in os.listdir(d):
+        n = _step_of(name)
+        if n is not None and n > step:
+            shutil.rmtree(os.path.join(d, name), ignore_errors=True)
+            gone.append(n)
+        elif n is None and name.startswith("step-") and name.endswith((".staging", ".replaced")):
+            shutil.rmtree(os.path.join(d, name), ignore_errors=True)
+    if gone:
+        alias = os.path.join(out_dir, f"{tag}_ckpt_rank{stage}p{peer}.pt")
+        left = list_waves(out_dir, tag, stage, peer)
+        try:
+            if os.path.exists(alias):
+                os.remove(alias)
+            if left:
+                os.link(os.path.join(wave_dir(out_dir, tag, stage, peer, left[-1]), "state.pt"),
+                        alias)
+        except OSError:
+            pass
+    return sorted(gone)
 
 
 def common_step(spec) -> int | None:
@@ -247,9 +299,33 @@ class CheckpointStore:
             if old not in self.pinned:
                 shutil.rmtree(os.path.join(slot, f"step-{old:08d}"), ignore_errors=True)
 
-    def common_step(self, spec) -> int | None:
+    def drop_after(self, run_id: str, tag: str, step: int) -> list:
+        """Every slot's waves of the run newer than `step`, and the parts
+        staged for them: the run resumes at `step`, so they belong to an
+        abandoned timeline. A pinned wave stays. -> [(slot dir, step)]."""
+        if not safe_name(run_id) or not safe_name(tag):
+            raise ValueError("bad run id or tag")
+        gone = []
+        base = os.path.join(self.root, run_id, "waves", tag)
+        for slot in sorted(os.listdir(base)) if os.path.isdir(base) else []:
+            for name in os.listdir(os.path.join(base, slot)):
+                n = _step_of(name)
+                if n is not None and n > step and n not in self.pinned:
+                    shutil.rmtree(os.path.join(base, slot, name), ignore_errors=True)
+                    gone.append((slot, n))
+        inc = os.path.join(self.root, run_id, ".incoming")
+        for slot in sorted(os.listdir(inc)) if os.path.isdir(inc) else []:
+            for name in os.listdir(os.path.join(inc, slot)):
+                n = _step_of(name)
+                if n is not None and n > step:
+                    shutil.rmtree(os.path.join(inc, slot, name), ignore_errors=True)
+        return sorted(gone)
+
+    def common_step(self, run_id: str, spec) -> int | None:
+        """The newest step every slot of `spec` holds a whole wave of in the
+        run's store (the resume point of a heal)."""
         from copy import copy
 
         s = copy(spec)
-        s.out_dir = self.root
+        s.out_dir = os.path.join(self.root, run_id)
         return common_step(s)

@@ -130,7 +130,8 @@ class FusedZero1:
         self.sync_and_step()
 
     def state_dict(self):
-        return {"t": self.t, "m": self.m.detach().cpu(), "v": self.v.detach().cpu()}
+        return {"t": self.t, "m": self.m.detach().to("cpu", copy=True),
+                "v": self.v.detach().to("cpu", copy=True)}
 
     def load_state_dict(self, sd):
         self.t = int(sd["t"])

@@ -446,10 +446,12 @@ class StageEngine:
 
     # ----------------------------------------------------------------- state
     def state_dict(self) -> dict:
-        return {"step": self.step_done, "params": self.store.master.detach().cpu().clone(),
+        # every tensor is a copy (a wave is written while the next step runs)
+        return {"step": self.step_done, "params": self.store.master.detach().to("cpu", copy=True),
                 "names": self.store.names(), "opt": self.opt.state_dict(),
                 "losses": {f"{s}:{m}": v for s, m, v in self.losses},
-                "buffers": {k: v.detach().cpu().clone() for k, v in self.model.buffers().items()},
+                "buffers": {k: v.detach().to("cpu", copy=True)
+                            for k, v in self.model.buffers().items()},
                 "rng": torch.get_rng_state()}
 
     def load_state_dict(self, sd: dict):

@@ -33,7 +33,9 @@ class DeviceAdamW:
                   self.wd, self.t)
 
     def state_dict(self):
-        return {"t": self.t, "m": self.m.detach().cpu(), "v": self.v.detach().cpu()}
+        # copies on every device: a wave is written while the next step runs
+        return {"t": self.t, "m": self.m.detach().to("cpu", copy=True),
+                "v": self.v.detach().to("cpu", copy=True)}
 
     def load_state_dict(self, sd):
         self.t = int(sd["t"])

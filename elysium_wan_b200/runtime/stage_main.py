@@ -14,6 +14,7 @@ import datetime
 import json
 import os
 import sys
+import threading
 import time
 import traceback
 
@@ -21,8 +22,53 @@ import torch
 import torch.distributed as dist
 
 
+_PRINT_LOCK = threading.Lock()
+
+
 def _print(tag: str, obj) -> None:
-    print(f"{tag} {json.dumps(obj) if not isinstance(obj, str) else obj}", flush=True)
+    # one marker per line even when the wave writer's thread prints too
+    line = f"{tag} {json.dumps(obj) if not isinstance(obj, str) else obj}\n"
+    with _PRINT_LOCK:
+        sys.stdout.write(line)
+        sys.stdout.flush()
+
+
+class WaveWriter:
+    """Commits checkpoint waves off the step (reference behaviour: its
+    background wave commit, RUNTIME-I17): the step's state is copied at the
+    step boundary, then a thread writes, fsyncs, hashes and renames the wave
+    and only then announces it (WT_WAVE). One commit is in flight at a time.
+    `wait()` returns when the commit in flight is done and raises its error,
+    so a failed commit fails the run; a run that fails still waits for the
+    commit of a step it finished, and reports its own error."""
+
+    def __init__(self, spec, stage: int, peer: int):
+        self.spec, self.stage, self.peer = spec, stage, peer
+        self.thread: threading.Thread | None = None
+        self.error: BaseException | None = None
+
+    def submit(self, step: int, state: dict):
+        from elysium_wan_b200.fault_tolerance import checkpoint as ckpt
+
+        self.wait()
+
+        def commit():
+            try:
+                path = ckpt.commit_wave(self.spec, self.stage, self.peer, step, state)
+                _print("WT_WAVE", {"step": step, "dir": path})
+            except BaseException as e:  # noqa: BLE001 - surfaced by wait()
+                self.error = e
+
+        self.thread = threading.Thread(target=commit, name=f"wave-{step}", daemon=True)
+        self.thread.start()
+
+    def wait(self):
+        if self.thread is not None:
+            self.thread.join()
+            self.thread = None
+        if self.error is not None:
+            e, self.error = self.error, None
+            raise RuntimeError(f"checkpoint wave commit failed: {e!r}") from e
 
 
 def init_group(spec, rank: int, timeout_s: float):
@@ -126,54 +172,70 @@ def run_stage(spec, stage: int, peer: int, timeout_s: float = 600.0) -> int:
         eng.load_state_dict(sd)
         start = step
         _print("WT_RESUME", {"step": step})
+    # waves past the start belong to an abandoned timeline (all of them, on a
+    # fresh launch), and a writer killed mid-commit leaves temporaries
+    dropped = ckpt.drop_after(spec.out_dir, spec.tag, stage, peer, start if spec.resume else -1)
+    if dropped:
+        _print("WT_WAVES_DROPPED", {"steps": dropped})
     os.makedirs(spec.out_dir, exist_ok=True)
     stream = open(os.path.join(spec.out_dir, f"{spec.tag}_loss_stream.jsonl"), "a") if eng.last else None
     tel = open(os.path.join(spec.out_dir, f"{spec.tag}_rank{stage}p{peer}_telemetry.jsonl"), "a")
     net0 = (0, 0)
     t_run = time.perf_counter()
-    for step in range(start, spec.steps):
-        t0 = time.perf_counter()
-        res = eng.run_step(step)
-        if eng.timing:
-            torch.cuda.synchronize()
-        dt = time.perf_counter() - t0
-        for mb, v in res:
-            rec = {"step": step, "mb": mb, "loss_hex": float_hex(v), "loss": v}
-            if stream is not None:
-                stream.write(json.dumps(rec) + "\n")
-                stream.flush()
-            _print("WT_METRIC", {"step": step, "mb": mb, "loss": v})
-        summary = summarize_step(step, stage, peer, dt * 1e3, eng.op_times_ms(),
-                                 comm.bytes_sent if comm else 0, comm.frames if comm else 0,
-                                 eng.phase_ms().get("opt_ms"))
-        if "ops" not in summary:
-            print(f"WT_WARN telemetry summary of step {step} exceeded 4096 bytes: its per-op "
-                  f"medians were dropped", flush=True)
-        _print("WT_TELEM", summary)
-        if eng.w_filled:
-            _print("WT_WFILL", {"step": step, "tasks": eng.w_filled})
-        tel.write(json.dumps({"step": step, "events": [[o, m, round(a, 4), round(d, 4)]
-                                                        for o, m, a, d in eng.op_times_ms()]})
-                  + "\n")
-        tel.flush()
-        if comm is not None:
-            net = (comm.frames, comm.bytes_sent)
-            _print("WT_NET", {"step": step, "frames": net[0] - net0[0], "bytes": net[1] - net0[1]})
-            net0 = net
-        if eng.timing:
-            _print("WT_MEM", {"step": step,
-                              "max_alloc_gib": round(torch.cuda.max_memory_allocated() / 2**30, 3),
-                              "reserved_gib": round(torch.cuda.memory_reserved() / 2**30, 3)})
-        if spec.ckpt_every and (step + 1) % spec.ckpt_every == 0:
-            path = ckpt.commit_wave(spec, stage, peer, step + 1, eng.state_dict())
-            _print("WT_WAVE", {"step": step + 1, "dir": path})
-        _print("WT_STEP", {"step": step, "ms": round(dt * 1e3, 3)})
-        if _leaves_after(step, spec):
-            # Test seam: this process leaves between steps (its kernels and
-            # collectives are complete), without a done marker, as a rank whose
-            # machine went away would.
-            sys.stdout.flush()
-            os._exit(17)
+    waves = WaveWriter(spec, stage, peer)
+    try:
+        for step in range(start, spec.steps):
+            t0 = time.perf_counter()
+            res = eng.run_step(step)
+            if eng.timing:
+                torch.cuda.synchronize()
+            dt = time.perf_counter() - t0
+            for mb, v in res:
+                rec = {"step": step, "mb": mb, "loss_hex": float_hex(v), "loss": v}
+                if stream is not None:
+                    stream.write(json.dumps(rec) + "\n")
+                    stream.flush()
+                _print("WT_METRIC", {"step": step, "mb": mb, "loss": v})
+            summary = summarize_step(step, stage, peer, dt * 1e3, eng.op_times_ms(),
+                                     comm.bytes_sent if comm else 0, comm.frames if comm else 0,
+                                     eng.phase_ms().get("opt_ms"))
+            if "ops" not in summary:
+                _print("WT_WARN", f"telemetry summary of step {step} exceeded 4096 bytes: its "
+                                  "per-op medians were dropped")
+            _print("WT_TELEM", summary)
+            if eng.w_filled:
+                _print("WT_WFILL", {"step": step, "tasks": eng.w_filled})
+            tel.write(json.dumps({"step": step, "events": [[o, m, round(a, 4), round(d, 4)]
+                                                            for o, m, a, d in eng.op_times_ms()]})
+                      + "\n")
+            tel.flush()
+            if comm is not None:
+                net = (comm.frames, comm.bytes_sent)
+                _print("WT_NET", {"step": step, "frames": net[0] - net0[0],
+                                  "bytes": net[1] - net0[1]})
+                net0 = net
+            if eng.timing:
+                gib = 2.0 ** 30
+                _print("WT_MEM", {"step": step,
+                                  "max_alloc_gib": round(torch.cuda.max_memory_allocated() / gib, 3),
+                                  "reserved_gib": round(torch.cuda.memory_reserved() / gib, 3)})
+            if spec.ckpt_every and (step + 1) % spec.ckpt_every == 0:
+                waves.submit(step + 1, eng.state_dict())
+            _print("WT_STEP", {"step": step, "ms": round(dt * 1e3, 3)})
+            if _leaves_after(step, spec):
+                # Test seam: this process leaves between steps (its kernels and
+                # collectives are complete, its wave committed), without a done
+                # marker, as a rank whose machine went away would.
+                waves.wait()
+                sys.stdout.flush()
+                os._exit(17)
+    except BaseException:
+        try:
+            waves.wait()  # a step finished before the failure still becomes a wave
+        except Exception as e:  # noqa: BLE001 - the run's own error is the one reported
+            _print("WT_WARN", str(e))
+        raise
+    waves.wait()
     tel.close()
     n_run = spec.steps - start
     _print("WT_TIMING", {"steps": n_run, "total_s": round(time.perf_counter() - t_run, 3),

@@ -189,6 +189,79 @@ def test_wave_commit_validate_prune_and_corruption(tmp_path):
     assert step == 6  # the corrupted newest wave is skipped
 
 
+def test_resume_refuses_mislabelled_padded_and_foreign_waves(tmp_path):
+    """A wave whose manifest names another step, one with a file the manifest
+    does not list, and one whose listed state is not a checkpoint are not
+    resumed from: the first two are skipped like a corrupted wave, the last
+    is refused with the reason."""
+    import json
+
+    spec = _spec(tmp_path)
+    for step in (2, 4, 6):
+        ckpt.commit_wave(spec, 0, 0, step, {"step": step})
+    d6 = ckpt.wave_dir(spec.out_dir, "t", 0, 0, 6)
+    meta = json.load(open(os.path.join(d6, "wave.json")))
+    meta["step"] = 8
+    json.dump(meta, open(os.path.join(d6, "wave.json"), "w"))
+    with pytest.raises(ValueError, match="names step 8"):
+        ckpt.validate_wave(d6, 6)
+    open(os.path.join(ckpt.wave_dir(spec.out_dir, "t", 0, 0, 4), "extra.bin"), "wb").write(b"x")
+    state, step = ckpt.load_latest(spec, 0, 0)
+    assert step == 2  # 6 mislabelled, 4 padded
+    with pytest.raises(FileNotFoundError):
+        ckpt.load_latest(spec, 0, 0, 6)
+    # a manifest that lists garbage as state.pt (its hash is right)
+    d2 = ckpt.wave_dir(spec.out_dir, "t", 0, 0, 2)
+    open(os.path.join(d2, "state.pt"), "wb").write(b"not a torch file")
+    meta = json.load(open(os.path.join(d2, "wave.json")))
+    meta["files"]["state.pt"] = {"sha256": ckpt._sha256(os.path.join(d2, "state.pt")),
+                                 "size": os.path.getsize(os.path.join(d2, "state.pt"))}
+    json.dump(meta, open(os.path.join(d2, "wave.json"), "w"))
+    with pytest.raises(ValueError, match="not a checkpoint"):
+        ckpt.load_latest(spec, 0, 0, 2)
+
+
+def test_resume_drops_the_abandoned_timeline_and_sweeps_temps(tmp_path):
+    """Resuming at step 4 removes the slot's waves 6 and 8 (they belong to the
+    timeline the run abandoned) and a killed writer's temporaries, and the
+    alias follows the newest wave left; a fresh launch keeps none. The
+    coordinator's store drops every slot's newer waves, except a pinned one."""
+    spec = _spec(tmp_path)
+    for step in (4, 6, 8):
+        ckpt.commit_wave(spec, 0, 0, step, {"step": step})
+    d = ckpt.slot_dir(spec.out_dir, "t", 0, 0)
+    os.makedirs(os.path.join(d, "step-00000010.staging"))
+    os.makedirs(os.path.join(d, "step-00000006.replaced"))
+    assert ckpt.drop_after(spec.out_dir, "t", 0, 0, 4) == [6, 8]
+    assert sorted(os.listdir(d)) == ["step-00000004"]
+    alias = os.path.join(spec.out_dir, "t_ckpt_rank0p0.pt")
+    w4 = os.path.join(ckpt.wave_dir(spec.out_dir, "t", 0, 0, 4), "state.pt")
+    assert open(alias, "rb").read() == open(w4, "rb").read()
+    assert ckpt.drop_after(spec.out_dir, "t", 0, 0, -1) == [4]
+    assert ckpt.list_waves(spec.out_dir, "t", 0, 0) == [] and not os.path.exists(alias)
+    # the store
+    store = ckpt.CheckpointStore(str(tmp_path / "store"))
+    src = JobSpec.from_dict(spec.to_dict())
+    src.out_dir = str(tmp_path / "src")
+    for r in (0, 1):
+        for step in (2, 4, 6):
+            ckpt.commit_wave(src, r, 0, step, {"step": step})
+            wd = ckpt.wave_dir(src.out_dir, "t", r, 0, step)
+            for name in ("state.pt", "wave.json"):
+                store.stage_part("run1", r, 0, step, name, open(os.path.join(wd, name), "rb").read())
+            assert store.commit_staged("run1", "t", r, 0, step)
+    store.stage_part("run1", 1, 0, 8, "state.pt", b"half a wave")
+    store.pinned.add(6)
+    assert store.drop_after("run1", "t", 2) == [("r0p0", 4), ("r1p0", 4)]
+    view = JobSpec.from_dict(spec.to_dict())
+    view.out_dir = os.path.join(store.root, "run1")
+    assert ckpt.list_waves(view.out_dir, "t", 0, 0) == [2, 6]
+    assert not os.path.exists(os.path.join(store.root, "run1", ".incoming", "r1p0", "step-00000008"))
+    store.pinned.clear()
+    store.drop_after("run1", "t", 2)
+    assert store.common_step("run1", spec) == 2
+
+
 def test_resume_refuses_other_recipe(tmp_path):
     spec = _spec(tmp_path)
     ckpt.commit_wave(spec, 0, 0, 2, {"step": 2})
@@ -427,3 +500,58 @@ def test_logical_checkpoint_pieces_with_frozen_and_replicated_tensors(tmp_path, 
         got = {(r["step"], r["mb"]): r["loss_hex"] for r in _json.load(f)["losses"]}
     later = {k: v for k, v in want.items() if k[0] >= 2}
     assert later and all(got.get(k) == v for k, v in later.items()), (later, got)
+
+
+def test_waves_commit_off_the_step_and_a_failed_commit_fails_the_run(tmp_path, monkeypatch,
+                                                                     capsys):
+    """The stage's wave writer returns at once while the commit (write, fsync,
+    hash, rename) runs on its thread; the wave is announced only once it is
+    committed; a commit that fails is raised by the next wait, so the run
+    fails with it."""
+    import threading
+
+    from elysium_wan_b200.runtime.stage_main import WaveWriter
+
+    spec = _spec(tmp_path)
+    release = threading.Event()
+    real = ckpt._sha256
+
+    def held(path):
+        assert release.wait(30)
+        return real(path)
+
+    monkeypatch.setattr(ckpt, "_sha256", held)
+    w = WaveWriter(spec, 0, 0)
+    state = {"step": 2, "params": torch.arange(4.0)}
+    w.submit(2, state)
+    assert ckpt.list_waves(spec.out_dir, "t", 0, 0) == []  # still hashing
+    assert "WT_WAVE" not in capsys.readouterr().out
+    release.set()
+    w.wait()
+    assert ckpt.list_waves(spec.out_dir, "t", 0, 0) == [2]
+    assert "WT_WAVE" in capsys.readouterr().out
+
+    def broken(*a, **k):
+        raise OSError(28, "No space left on device")
+
+    monkeypatch.setattr(ckpt, "commit_wave", broken)
+    w.submit(4, state)
+    with pytest.raises(RuntimeError, match="wave commit failed"):
+        w.wait()
+    w.wait()  # the error is reported once
+
+
+def test_engine_state_is_a_copy():
+    """A wave is written while the next step runs: every tensor of the
+    engine's state (parameters, moments) is a copy, also on the CPU where
+    `.cpu()` would alias."""
+    from elysium_wan_b200.runtime.engine import StageEngine
+
+    cfg = make_config("toy", n_layer=2, vocab_size=97, d_model=64, n_head=4, seq_len=16)
+    spec = JobSpec(model=cfg, stages=1, microbatches=2, mb_size=2).finalize()
+    eng = StageEngine(spec, 0, 0, None, "cpu")
+    sd = eng.state_dict()
+    assert sd["params"].data_ptr() != eng.store.master.data_ptr()
+    assert sd["opt"]["m"].data_ptr() != eng.opt.m.data_ptr()
+    eng.opt.m.add_(1.0)
+    assert float(sd["opt"]["m"].abs().sum()) == 0.0
