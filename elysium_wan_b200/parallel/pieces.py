@@ -28,10 +28,9 @@ per stage, not once per replica) and traffic (the matrices move as bf16).
 from __future__ import annotations
 
 import torch
-import torch.distributed as dist
 
 from elysium_wan_b200.models.params import shard_ranges
-from elysium_wan_b200.parallel.zero1 import fold_tree
+from elysium_wan_b200.parallel.zero1 import all_gather, all_to_all, fold_tree
 from elysium_wan_b200.runtime import optim
 
 
@@ -73,7 +72,7 @@ class Pieces:
             send[base: base + rh - rl] = g[rl:rh]
             send[base + rh - rl: base + rh - rl + mh - ml] = g[ml:mh]
         recv = torch.empty_like(send)
-        dist.all_to_all_single(recv, send, group=self.group)
+        all_to_all(self.comm, self.group, recv, send)
         n = self.g.numel()
         self.g.copy_(fold_tree([recv[q * self.S: q * self.S + n] for q in range(self.w)]))
 
@@ -85,7 +84,7 @@ class Pieces:
             mine = torch.zeros(per, dtype=torch.float32, device=st.master.device)
             mine[: self.r_hi - self.r_lo] = st.master[self.r_lo:self.r_hi]
             out = torch.empty(self.w * per, dtype=torch.float32, device=st.master.device)
-            dist.all_gather_into_tensor(out, mine, group=self.group)
+            all_gather(self.comm, self.group, out, mine)
             for q, (l, h) in enumerate(self.rb):
                 if q != self.k:
                     st.master[l:h] = out[q * per: q * per + h - l]
@@ -95,7 +94,7 @@ class Pieces:
             mine = torch.zeros(per, dtype=st.work.dtype, device=st.work.device)
             mine[: self.m_hi - self.m_lo] = st.work[self.m_lo:self.m_hi]
             out = torch.empty(self.w * per, dtype=st.work.dtype, device=st.work.device)
-            dist.all_gather_into_tensor(out, mine, group=self.group)
+            all_gather(self.comm, self.group, out, mine)
             for q, (l, h) in enumerate(self.mb):
                 if q != self.k:
                     st.work[l:h] = out[q * per: q * per + h - l]

@@ -37,6 +37,24 @@ def shard_bounds(n: int, w: int) -> list:
     return [(min(n, k * per), min(n, (k + 1) * per)) for k in range(w)]
 
 
+def all_to_all(comm, group, recv, send):
+    """Equal-split all-to-all among a stage's replicas: over the sealed mesh
+    of the TCP data plane when the stage has one, else the process group."""
+    mesh = getattr(comm, "mesh", None)
+    if mesh is not None:
+        mesh.all_to_all_single(recv, send)
+    else:
+        dist.all_to_all_single(recv, send, group=group)
+
+
+def all_gather(comm, group, out, mine):
+    mesh = getattr(comm, "mesh", None)
+    if mesh is not None:
+        mesh.all_gather_into_tensor(out, mine)
+    else:
+        dist.all_gather_into_tensor(out, mine, group=group)
+
+
 def fold_tree(partials: list) -> torch.Tensor:
     """The declared fold: copy of the first partial, then += in rank order."""
     acc = partials[0].clone()
@@ -78,7 +96,7 @@ class Zero1:
         for q, (l, h) in enumerate(self.bounds):
             send[q * maxlen: q * maxlen + (h - l)] = g[l:h]
         recv = torch.empty_like(send)
-        dist.all_to_all_single(recv, send, group=self.group)
+        all_to_all(self.comm, self.group, recv, send)
         parts = [recv[q * maxlen: q * maxlen + (self.hi - self.lo)] for q in range(self.w)]
         self._g.copy_(fold_tree(parts))
 
@@ -88,7 +106,7 @@ class Zero1:
         mine = torch.zeros(maxlen, dtype=torch.float32, device=st.master.device)
         mine[: self.hi - self.lo] = st.master[self.lo:self.hi]
         out = torch.empty(self.w * maxlen, dtype=torch.float32, device=st.master.device)
-        dist.all_gather_into_tensor(out, mine, group=self.group)
+        all_gather(self.comm, self.group, out, mine)
         for q, (l, h) in enumerate(self.bounds):
             if q != self.k:
                 st.master[l:h] = out[q * maxlen: q * maxlen + (h - l)]

@@ -95,7 +95,7 @@ class StageEngine:
 
                 self.zero1 = Pieces(self, comm)
             elif self.spec.grad_sync == "fused" and self.device.type == "cuda" and \
-                    not self.spec.model.lora_rank:
+                    not self.spec.model.lora_rank and self.spec.backend == "nccl":
                 from elysium_wan_b200.parallel.fused import FusedZero1
 
                 self.zero1 = FusedZero1(self, comm)
@@ -415,7 +415,9 @@ class StageEngine:
         counts = torch.zeros((len(layers), E), dtype=torch.int64)
         for r in recs:
             counts[layers.index(r.layer)] += r.counts
-        if self.width > 1 and self.comm is not None and getattr(self.comm, "g_stage", None):
+        if self.width > 1 and getattr(self.comm, "mesh", None) is not None:
+            self.comm.mesh.all_reduce_sum(counts)  # the sealed mesh of the TCP plane
+        elif self.width > 1 and self.comm is not None and getattr(self.comm, "g_stage", None):
             import torch.distributed as dist
 
             dev_counts = counts.to(self.device)

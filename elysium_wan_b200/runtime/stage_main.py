@@ -162,6 +162,10 @@ def run_stage(spec, stage: int, peer: int, timeout_s: float = 600.0) -> int:
                            "frozen_params": eng.store.numel - eng.store.nt})
     if getattr(comm, "peers_seen", None):
         _print("WT_AEAD", {"cipher": "chacha20-poly1305", "peers": comm.peers_seen})
+    if getattr(comm, "mesh", None) is not None:
+        _print("WT_MESH", {"stage": stage, "peer": peer, "replicas": sorted(comm.mesh.links)})
+    if getattr(comm, "tied_link", None) is not None:
+        _print("WT_TIED_LINK", {"stage": stage, "peer": peer})
     if stage == 0 and peer == 0:
         os.makedirs(spec.out_dir, exist_ok=True)
         with open(os.path.join(spec.out_dir, f"{spec.tag}_env.json"), "w") as f:

@@ -19,6 +19,14 @@ as parallel/p2p.PipeComm, so the engine does not know which plane it runs on:
   (type, microbatch); a WAN shim per outgoing link can pace and delay sends
   for experiments (latency, rate, jitter).
 
+The replicas of a wide stage are joined by sealed links of their own (a
+full mesh: each replica dials the higher-numbered ones), over which the
+ZeRO-1 / pieces exchange runs (`StageMesh`: the partials' scatter to their
+owners, the updated shards' gather, integer sums such as MoE expert counts);
+the first and last stages of a tied-embedding run get a sealed link for the
+table relay. So every byte between machines crosses the sealed plane; the
+gloo group is kept only for process-group plumbing.
+
 Device tensors cross through host memory (a device->host copy before the
 send, a host->device copy after the receive).
 """
@@ -37,7 +45,11 @@ import torch.distributed as dist
 from elysium_wan_b200.models.gpt import Act
 from elysium_wan_b200.transport.pacer import reverse_link
 from elysium_wan_b200.transport import framing
-from elysium_wan_b200.transport.framing import BWD, END, FWD, HELLO
+from elysium_wan_b200.transport.framing import BWD, END, FWD, GRADS, HELLO, PARAMS, TIED
+
+# The `mb` field of a mesh frame names the exchange it belongs to (its `chunk`
+# field names the sending replica).
+MESH_SCATTER, MESH_GATHER, MESH_SUM = 0, 1, 2
 
 
 def slot_endpoint(spec, stage: int, peer: int) -> tuple[str, int]:
@@ -80,10 +92,11 @@ class _Inbox:
 class _Link:
     """The flows to one neighbour slot and the thread that sends on them."""
 
-    def __init__(self, comm, socks, link_cfg: dict):
+    def __init__(self, comm, socks, link_cfg: dict, wire_codec: str | None = None):
         from elysium_wan_b200.parallel.p2p import _Shim
 
         self.comm, self.socks = comm, socks
+        self.wire_codec = wire_codec or comm.wire_codec
         self.frag_size = 0  # 0: one fragment per flow; else the adapted fragment size
         self.clean = 0
         self.q: queue.Queue = queue.Queue()
@@ -99,7 +112,7 @@ class _Link:
         c = self.comm
         # an fp8 boundary is the (codes, scales) pair: one frame, one payload
         payload_t = tuple(tensors) if len(tensors) > 1 else tensors[0]
-        codec_id, payload, shape = framing.encode_tensor(payload_t, c.wire_codec)
+        codec_id, payload, shape = framing.encode_tensor(payload_t, self.wire_codec)
         if self.frag_size:
             # adapted size: fragments taken round-robin by the flows
             n = max(1, -(-len(payload) // self.frag_size))
@@ -208,6 +221,9 @@ class TcpPipeComm:
         self.readers: list = []
         self.next_links: dict = {}  # peer of stage + 1 -> _Link
         self.prev_links: dict = {}  # peer of stage - 1 -> _Link
+        self.mesh = None            # StageMesh of a wide stage
+        self.tied_link = None       # the table relay's link (first <-> last stage)
+        self.tied_seq = 0
         self.sent = collections.Counter()
         self.bytes_sent = 0
         self.frames = 0
@@ -228,7 +244,13 @@ class TcpPipeComm:
     def _connect(self):
         spec, S = self.spec, self.spec.stages
         flows = max(1, int(spec.p2p_streams))
-        n_in = spec.stage_widths[self.stage - 1] * flows if self.stage > 0 else 0
+        width = spec.stage_widths[self.stage]
+        n_prev = spec.stage_widths[self.stage - 1] * flows if self.stage > 0 else 0
+        # a wide stage's mesh: the lower-numbered replicas dial this one
+        n_mesh = self.peer if width > 1 else 0
+        tied = bool(spec.model.tie_embeddings) and S > 1
+        n_tied = 1 if tied and self.stage == S - 1 else 0
+        n_in = n_prev + n_mesh + n_tied
         lsock = None
         if n_in:
             host, port = slot_endpoint(spec, self.stage, self.peer)
@@ -243,6 +265,8 @@ class TcpPipeComm:
             lsock.bind(("0.0.0.0" if host not in ("127.0.0.1", "localhost") else host, int(bind)))
             lsock.listen(n_in + 4)
         accepted: dict = collections.defaultdict(dict)
+        mesh_in: dict = {}
+        tied_in: list = []
         acc_err: list = []
 
         def accept_all():
@@ -256,9 +280,16 @@ class TcpPipeComm:
                     if hello.type != HELLO:
                         raise framing.FrameError("expected HELLO")
                     h = hello.obj()
-                    if h.get("stage") != self.stage - 1:
-                        raise framing.FrameError(f"HELLO from stage {h.get('stage')}")
-                    accepted[int(h["peer"])][int(h["flow"])] = sc
+                    kind = h.get("link", "chain")
+                    if kind == "mesh" and h.get("stage") == self.stage and \
+                            0 <= int(h["peer"]) < self.peer and int(h["peer"]) not in mesh_in:
+                        mesh_in[int(h["peer"])] = sc
+                    elif kind == "tied" and n_tied and h.get("stage") == 0 and not tied_in:
+                        tied_in.append(sc)
+                    elif kind == "chain" and h.get("stage") == self.stage - 1:
+                        accepted[int(h["peer"])][int(h["flow"])] = sc
+                    else:
+                        raise framing.FrameError(f"unexpected HELLO {h}")
                     self.peers_seen[f"{h['stage']}:{h['peer']}"] = sc.peer
             except Exception as e:
                 acc_err.append(e)
@@ -280,16 +311,45 @@ class TcpPipeComm:
                 link = spec.links[self.stage] if self.stage < len(spec.links) else {}
                 self.next_links[q] = _Link(self, socks, link)
                 self._start_readers(socks)
+        # the exchange runs on a lossless codec whatever the boundary's
+        exch = "raw" if self.wire_codec == "raw" else "planes"
+        mesh_out = {}
+        for q in range(self.peer + 1, width) if width > 1 else ():
+            sc = self._dial_sealed(self.stage, q, {"link": "mesh"})
+            mesh_out[q] = sc
+        tied_out = None
+        if tied and self.stage == 0 and self.peer == 0:
+            tied_out = self._dial_sealed(S - 1, 0, {"link": "tied"})
         if t_acc:
             t_acc.join(self.timeout + 5)
             lsock.close()
             if acc_err:
                 raise ConnectionError(f"data plane accept failed: {acc_err[0]}")
             back = spec.links[self.stage - 1] if self.stage - 1 < len(spec.links) else {}
-            for p in range(spec.stage_widths[self.stage - 1]):
+            for p in range(spec.stage_widths[self.stage - 1]) if self.stage > 0 else ():
                 socks = [accepted[p][f] for f in range(flows)]
                 self.prev_links[p] = _Link(self, socks, reverse_link(back))
                 self._start_readers(socks)
+        if width > 1:
+            links = {}
+            for q, sc in sorted({**mesh_in, **mesh_out}.items()):
+                links[q] = _Link(self, [sc], {}, wire_codec=exch)
+                self._start_readers([sc], key=lambda f: ("mesh", f.type, f.mb, f.chunk))
+            if sorted(links) != [q for q in range(width) if q != self.peer]:
+                raise ConnectionError(f"stage mesh incomplete: links to {sorted(links)}")
+            self.mesh = StageMesh(self, links)
+        sc = tied_out or (tied_in[0] if tied_in else None)
+        if sc is not None:
+            self.tied_link = _Link(self, [sc], {}, wire_codec=exch)
+            self._start_readers([sc], key=lambda f: ("tied", f.type))
+
+    def _dial_sealed(self, stage: int, peer: int, hello: dict):
+        """One sealed flow to slot (stage, peer), announced by a HELLO."""
+        host, port = slot_endpoint(self.spec, stage, peer)
+        sc = self._seal(self._dial(host, port), "dialer")
+        framing.send_frame(sc, HELLO, 0, 0, dict(hello, stage=self.stage, peer=self.peer, flow=0))
+        self.peers_seen[f"{stage}:{peer}"] = sc.peer
+        return sc
 
     def _dial(self, host, port):
         from elysium_wan_b200.transport import tuning
@@ -305,11 +365,14 @@ class TcpPipeComm:
                     raise
                 time.sleep(0.05)
 
-    def _start_readers(self, socks):
+    def _start_readers(self, socks, key=None):
         """One reader thread per flow of a link. A frame's fragments travel on
-        different flows (one each), so the link's flows share one reassembler."""
+        different flows (one each), so the link's flows share one reassembler.
+        `key(frame)` files a whole frame in the inbox (default: type and
+        microbatch)."""
         re = framing.Reassembler()
         lock = threading.Lock()
+        key = key or (lambda f: (f.type, f.mb))
 
         def loop(sock):
             try:
@@ -320,7 +383,7 @@ class TcpPipeComm:
                     with lock:
                         whole = re.push(f)
                     if whole is not None:
-                        self.inbox.put((whole.type, whole.mb), whole)
+                        self.inbox.put(key(whole), whole)
             except Exception as e:
                 self.inbox.fail(e)
 
@@ -387,15 +450,71 @@ class TcpPipeComm:
         return Act(bufs[0])
 
     def tied_send(self, t):
-        dist.send(t.contiguous(), self.tied_peer, group=self.g_tied)
+        """The table relay over its sealed link (fp32, lossless codec)."""
+        self.tied_seq += 1
+        self._enqueue(self.tied_link, TIED, 0, [self._host(t.float())])
 
     def tied_recv(self, buf):
-        dist.recv(buf, self.tied_peer, group=self.g_tied)
+        f = self.inbox.get(("tied", TIED), self.timeout)
+        buf.copy_(f.tensor().view_as(buf).to(buf.device))
+
+    def _links(self) -> list:
+        out = list(self.next_links.values()) + list(self.prev_links.values())
+        out += list(self.mesh.links.values()) if self.mesh is not None else []
+        return out + ([self.tied_link] if self.tied_link is not None else [])
 
     def flush(self):
-        for link in list(self.next_links.values()) + list(self.prev_links.values()):
+        for link in self._links():
             link.flush()
 
     def close(self):
-        for link in list(self.next_links.values()) + list(self.prev_links.values()):
+        for link in self._links():
             link.close()
+
+
+class StageMesh:
+    """The ZeRO-1 / pieces exchange of a wide stage over its sealed mesh
+    links; the same calls, equal splits and results as the torch.distributed
+    collectives it replaces on this plane (every part is exact: the links
+    carry fp32 and int64 losslessly, and sums run in rank order)."""
+
+    def __init__(self, comm, links: dict):
+        self.comm, self.links = comm, links
+        self.k = comm.peer
+        self.w = len(links) + 1
+
+    def _send(self, q: int, ftype: int, kind: int, t):
+        self.comm._enqueue(self.links[q], ftype, kind, [self.comm._host(t)])
+
+    def _recv(self, q: int, ftype: int, kind: int):
+        return self.comm.inbox.get(("mesh", ftype, kind, q), self.comm.timeout).tensor()
+
+    def all_to_all_single(self, recv, send):
+        """Part q of `send` goes to replica q; part q of `recv` comes from it."""
+        n = send.numel() // self.w
+        for q in self.links:
+            self._send(q, GRADS, MESH_SCATTER, send[q * n:(q + 1) * n])
+        recv[self.k * n:(self.k + 1) * n].copy_(send[self.k * n:(self.k + 1) * n])
+        for q in sorted(self.links):
+            recv[q * n:(q + 1) * n].copy_(self._recv(q, GRADS, MESH_SCATTER).reshape(-1))
+
+    def all_gather_into_tensor(self, out, mine):
+        n = mine.numel()
+        for q in self.links:
+            self._send(q, PARAMS, MESH_GATHER, mine)
+        out[self.k * n:(self.k + 1) * n].copy_(mine.reshape(-1))
+        for q in sorted(self.links):
+            out[q * n:(q + 1) * n].copy_(
+                self._recv(q, PARAMS, MESH_GATHER).reshape(-1).to(out.dtype))
+
+    def all_reduce_sum(self, t):
+        """t (in place) = the replicas' t summed in rank order."""
+        for q in self.links:
+            self._send(q, GRADS, MESH_SUM, t)
+        parts = {q: self._recv(q, GRADS, MESH_SUM).view_as(t).to(t.device)
+                 for q in sorted(self.links)}
+        parts[self.k] = t.clone()
+        acc = parts[0].clone()
+        for q in range(1, self.w):
+            acc += parts[q]
+        t.copy_(acc)

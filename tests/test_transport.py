@@ -611,3 +611,38 @@ def test_pipeline_over_sealed_tcp_with_refused_sends_is_bitwise(tmp_path, monkey
     r = run_and_compare(spec, timeout=300)
     assert r["ok"], r
     assert r["compared"] == 8
+
+
+@pytest.mark.parametrize("case", ["tied_zero1_1_2_1", "moe_pieces_1_2"])
+def test_wide_stage_exchange_and_tied_relay_cross_the_sealed_plane(tmp_path, monkeypatch, case):
+    """On the TCP data plane a wide stage's ZeRO-1 / pieces exchange (the
+    partials' scatter, the shards' gather, MoE expert counts) runs over the
+    sealed links among its replicas, and a tied table's relay over a sealed
+    link between the first and last stages; the losses equal the oracle."""
+    import glob
+
+    from elysium_wan_b200.launch.local import run_and_compare
+    from elysium_wan_b200.models.config import make_config
+    from elysium_wan_b200.runtime.spec import JobSpec
+
+    monkeypatch.setenv("ELYSIUM_PEER_KEY", str(tmp_path / "peer.key"))
+    if case == "tied_zero1_1_2_1":
+        cfg = make_config("toy", n_layer=4, vocab_size=97, d_model=64, n_head=4, seq_len=16,
+                          tie_embeddings=True)
+        kw = dict(stages=3, stage_widths=[1, 2, 1])
+    else:
+        cfg = make_config("toy", n_layer=4, vocab_size=97, d_model=64, n_head=4, seq_len=16,
+                          norm="rmsnorm", mlp="swiglu", pos="rope", bias=False, moe_experts=4,
+                          moe_top_k=2, moe_d_ff=64, moe_select="score_bias", moe_bias_rate=0.01)
+        kw = dict(stages=2, stage_widths=[1, 2], shard="pieces")
+    port = 32500 + 40 * (case != "tied_zero1_1_2_1") + (os.getpid() % 200) * 7
+    spec = JobSpec(model=cfg, microbatches=4, mb_size=2, steps=3, out_dir=str(tmp_path),
+                   port_base=port, backend="tcp", wire_codec="planes", **kw)
+    r = run_and_compare(spec, timeout=300)
+    assert r["ok"] and r["compared"] == 12, r
+    logs = {os.path.basename(p): open(p).read() for p in glob.glob(str(tmp_path / "*_r*p*.log"))}
+    wide = [t for n, t in logs.items() if "_r1p" in n]
+    assert len(wide) == 2 and all("WT_MESH" in t for t in wide), list(logs)
+    if case == "tied_zero1_1_2_1":
+        ends = [t for n, t in logs.items() if "_r0p0" in n or "_r2p0" in n]
+        assert len(ends) == 2 and all("WT_TIED_LINK" in t for t in ends)
