@@ -142,10 +142,18 @@ class PipeComm:
         self.grad_dtype = torch.bfloat16 if self.cuda else torch.float32  # boundary gradients
         link = spec.links[stage] if stage < len(spec.links) else {}
         back = spec.links[stage - 1] if stage > 0 and stage - 1 < len(spec.links) else {}
-        from elysium_wan_b200.transport.pacer import reverse_link
+        from elysium_wan_b200.transport.pacer import pair_link, reverse_link
+
+        # one pacer per direction serves every peer of the neighbour stage:
+        # its receiver's budgets apply when that stage has one peer
+        def dst(r):
+            return (r, 0) if 0 <= r < spec.stages and spec.stage_widths[r] == 1 else None
+
+        link = pair_link(spec, link, (stage, peer), dst(stage + 1))
+        back = pair_link(spec, reverse_link(back), (stage, peer), dst(stage - 1))
 
         self.shim_next = _Shim(link, spec.tag) if not self.cuda else None
-        self.shim_prev = _Shim(reverse_link(back), spec.tag) if not self.cuda else None
+        self.shim_prev = _Shim(back, spec.tag) if not self.cuda else None
         self.bytes_sent = 0
         self.frames = 0
         if world > 1:

@@ -25,6 +25,8 @@ ADAMW: dict[str, Any] = {"betas": [0.9, 0.95], "eps": 1e-8, "weight_decay": 0.0}
 OPTIMIZERS = ("adamw", "adamw-host")
 BACKENDS = ("nccl", "gloo", "tcp")
 FOLDS = ("dp_tree",)
+PACINGS = ("link", "shared")
+EMISSION_ORDERS = ("store", "forward")
 
 
 @dataclass
@@ -106,8 +108,29 @@ class JobSpec:
     dial_timeout_s: float = 0.0
     wire_codec: str = "raw"
     links: list = field(default_factory=list)
+    # Shared WAN pacing, the reference's spec fields: with pacing "shared"
+    # every connection also draws on its sender's NIC egress budget
+    # (peer_egress_mbps[stage][peer]), its receiver's NIC ingress budget
+    # (peer_ingress_mbps) and, between two sites (sites[stage][peer]), the
+    # uplink of that direction (uplink_mbps["a->b"]), each a token bucket
+    # that every connection of the host shares (transport/pacer.py).
+    pacing: str = "link"
+    peer_egress_mbps: list | None = None
+    peer_ingress_mbps: list | None = None
+    sites: list | None = None
+    uplink_mbps: dict | None = None
     # ------------------------------------------------------------- wide stages
     wire: str = "fp32"
+    # Per stage, the order W emits its deferred gradients ("store" or
+    # "forward"; the reference's field). Accepted and checked; this engine
+    # folds each element in microbatch order whatever the emission order, so
+    # it moves no bit and no byte.
+    emission_order: list | None = None
+    # Reference fields this engine does not take: explicit piece boundaries
+    # (pieces here are cut over the flat store) and the device classes of an
+    # arch "hf" job. Only None is accepted.
+    piece_bounds: list | None = None
+    device_classes: list | None = None
     shard: str = "zero1"
     fold: str = "dp_tree"
     grad_sync: str = "fused"  # fused | nccl
@@ -217,6 +240,18 @@ class JobSpec:
                                       "stages")
         if self.model.arch == "user":
             self._check_user_model()
+        if self.emission_order is None:
+            self.emission_order = ["store"] * self.stages
+        if len(self.emission_order) != self.stages or \
+                any(o not in EMISSION_ORDERS for o in self.emission_order):
+            raise ValueError(f"emission_order must list one of {EMISSION_ORDERS} per stage")
+        if self.piece_bounds is not None or self.device_classes is not None:
+            raise NotImplementedError("piece_bounds and device_classes are not taken: pieces are "
+                                      "cut over the flat store, and arch hf is not built")
+        if self.pacing not in PACINGS:
+            raise ValueError(f"pacing {self.pacing!r} is not one of {PACINGS}")
+        if self.pacing == "shared":
+            self._check_shared_pacing()
         if self.schedule_order is None:
             self.schedule_order = default_schedule(self)
         self._check_schedule_order()
@@ -230,6 +265,50 @@ class JobSpec:
         if self.resume_step is not None and not self.resume:
             raise ValueError("resume_step needs resume")
         return self
+
+    def _check_shared_pacing(self):
+        """pacing "shared": a positive egress and ingress rate and a site name
+        for every slot, and an uplink rate for both directions of every pair
+        of different sites that a connection of this run crosses."""
+        import math
+
+        def grid(name):
+            v = getattr(self, name)
+            if not isinstance(v, list) or [len(row) if isinstance(row, list) else -1
+                                           for row in v] != list(self.stage_widths):
+                raise ValueError(f"pacing='shared' needs {name}[stage][peer] for every slot")
+            return v
+
+        for name in ("peer_egress_mbps", "peer_ingress_mbps"):
+            for r, row in enumerate(grid(name)):
+                for p, x in enumerate(row):
+                    if not (isinstance(x, (int, float)) and math.isfinite(x) and x > 0):
+                        raise ValueError(f"pacing='shared': {name}[{r}][{p}]={x!r} is not > 0")
+        sites = grid("sites")
+        for r, row in enumerate(sites):
+            for p, x in enumerate(row):
+                if not isinstance(x, str) or not x or "->" in x or ">" in x:
+                    raise ValueError(f"pacing='shared': sites[{r}][{p}]={x!r} is not a site name")
+        up = self.uplink_mbps if isinstance(self.uplink_mbps, dict) else {}
+        pairs = set()
+        for r in range(self.stages):
+            for p in range(self.stage_widths[r]):
+                peers = [(r, q) for q in range(self.stage_widths[r]) if q != p]
+                if r + 1 < self.stages:
+                    peers += [(r + 1, q) for q in range(self.stage_widths[r + 1])]
+                for r2, q in peers:
+                    a, b = sites[r][p], sites[r2][q]
+                    if a != b:
+                        pairs |= {(a, b), (b, a)}
+        if self.model.tie_embeddings and self.stages > 1:
+            a, b = sites[0][0], sites[-1][0]
+            if a != b:
+                pairs |= {(a, b), (b, a)}
+        for a, b in sorted(pairs):
+            x = up.get(f"{a}->{b}")
+            if not (isinstance(x, (int, float)) and math.isfinite(x) and x > 0):
+                raise ValueError(f"pacing='shared': uplink_mbps[{a + '->' + b!r}] is missing or "
+                                 "not > 0")
 
     def _check_user_model(self):
         """The structural contract of a user model (validation/model_contract.py):

@@ -150,3 +150,25 @@ def link_buckets(link: dict, tag: str = "run") -> list:
         if key and mbps > 0:
             out.append(bucket(f"{kind}:{key}", mbps, tag))
     return out
+
+
+def pair_link(spec, base: dict, src: tuple, dst: tuple | None) -> dict:
+    """The configuration of the connection from slot `src` to slot `dst`:
+    the hop's own shaping, plus, under the spec's pacing "shared", the
+    sender's NIC egress budget, the receiver's NIC ingress budget and, between
+    two sites, that direction's uplink (the reference's peer_egress_mbps,
+    peer_ingress_mbps, sites and uplink_mbps fields). `dst` None (a plane
+    whose one pacer serves several receivers): the sender's NIC only."""
+    out = dict(base or {})
+    if getattr(spec, "pacing", "link") != "shared":
+        return out
+    r, p = src
+    out["egress_key"], out["egress_mbps"] = f"slot{r}.{p}", float(spec.peer_egress_mbps[r][p])
+    if dst is not None:
+        r2, q = dst
+        out["ingress_key"] = f"slot{r2}.{q}"
+        out["ingress_mbps"] = float(spec.peer_ingress_mbps[r2][q])
+        a, b = spec.sites[r][p], spec.sites[r2][q]
+        if a != b:
+            out["uplink_key"], out["uplink_mbps"] = f"{a}>{b}", float(spec.uplink_mbps[f"{a}->{b}"])
+    return out

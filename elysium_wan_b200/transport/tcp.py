@@ -43,7 +43,7 @@ import torch
 import torch.distributed as dist
 
 from elysium_wan_b200.models.gpt import Act
-from elysium_wan_b200.transport.pacer import reverse_link
+from elysium_wan_b200.transport.pacer import pair_link, reverse_link
 from elysium_wan_b200.transport import framing
 from elysium_wan_b200.transport.framing import BWD, END, FWD, GRADS, HELLO, PARAMS, TIED
 
@@ -309,6 +309,7 @@ class TcpPipeComm:
                     self.peers_seen[f"{self.stage + 1}:{q}"] = sc.peer
                     socks.append(sc)
                 link = spec.links[self.stage] if self.stage < len(spec.links) else {}
+                link = pair_link(spec, link, (self.stage, self.peer), (self.stage + 1, q))
                 self.next_links[q] = _Link(self, socks, link)
                 self._start_readers(socks)
         # the exchange runs on a lossless codec whatever the boundary's
@@ -328,19 +329,24 @@ class TcpPipeComm:
             back = spec.links[self.stage - 1] if self.stage - 1 < len(spec.links) else {}
             for p in range(spec.stage_widths[self.stage - 1]) if self.stage > 0 else ():
                 socks = [accepted[p][f] for f in range(flows)]
-                self.prev_links[p] = _Link(self, socks, reverse_link(back))
+                cfg = pair_link(spec, reverse_link(back), (self.stage, self.peer),
+                                (self.stage - 1, p))
+                self.prev_links[p] = _Link(self, socks, cfg)
                 self._start_readers(socks)
         if width > 1:
             links = {}
             for q, sc in sorted({**mesh_in, **mesh_out}.items()):
-                links[q] = _Link(self, [sc], {}, wire_codec=exch)
+                cfg = pair_link(spec, {}, (self.stage, self.peer), (self.stage, q))
+                links[q] = _Link(self, [sc], cfg, wire_codec=exch)
                 self._start_readers([sc], key=lambda f: ("mesh", f.type, f.mb, f.chunk))
             if sorted(links) != [q for q in range(width) if q != self.peer]:
                 raise ConnectionError(f"stage mesh incomplete: links to {sorted(links)}")
             self.mesh = StageMesh(self, links)
         sc = tied_out or (tied_in[0] if tied_in else None)
         if sc is not None:
-            self.tied_link = _Link(self, [sc], {}, wire_codec=exch)
+            other = (S - 1, 0) if self.stage == 0 else (0, 0)
+            cfg = pair_link(spec, {}, (self.stage, self.peer), other)
+            self.tied_link = _Link(self, [sc], cfg, wire_codec=exch)
             self._start_readers([sc], key=lambda f: ("tied", f.type))
 
     def _dial_sealed(self, stage: int, peer: int, hello: dict):

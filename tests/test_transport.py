@@ -646,3 +646,73 @@ def test_wide_stage_exchange_and_tied_relay_cross_the_sealed_plane(tmp_path, mon
     if case == "tied_zero1_1_2_1":
         ends = [t for n, t in logs.items() if "_r0p0" in n or "_r2p0" in n]
         assert len(ends) == 2 and all("WT_TIED_LINK" in t for t in ends)
+
+
+def _shared_spec(**kw):
+    from elysium_wan_b200.models.config import make_config
+    from elysium_wan_b200.runtime.spec import JobSpec
+
+    cfg = make_config("toy", n_layer=4, vocab_size=97, d_model=64, n_head=4, seq_len=16)
+    base = dict(model=cfg, stages=2, stage_widths=[1, 2], microbatches=4, mb_size=2, steps=2,
+                pacing="shared", peer_egress_mbps=[[400.0], [300.0, 300.0]],
+                peer_ingress_mbps=[[500.0], [200.0, 250.0]], sites=[["us"], ["us", "eu"]],
+                uplink_mbps={"us->eu": 100.0, "eu->us": 120.0})
+    base.update(kw)
+    return JobSpec(**base)
+
+
+def test_shared_pacing_fields_are_checked_and_name_each_connections_budgets():
+    """The reference's shared-pacing spec fields: every slot's NIC rates and
+    site, and an uplink for both directions of every site pair a connection
+    crosses; each connection then draws on its sender's egress, its
+    receiver's ingress and, across sites, that direction's uplink."""
+    from elysium_wan_b200.transport.pacer import link_buckets, pair_link, reverse_link
+
+    spec = _shared_spec().finalize()
+    assert spec.emission_order == ["store", "store"]
+    c = pair_link(spec, {"latency_ms": 5.0}, (0, 0), (1, 1))
+    assert c["latency_ms"] == 5.0
+    assert (c["egress_key"], c["egress_mbps"]) == ("slot0.0", 400.0)
+    assert (c["ingress_key"], c["ingress_mbps"]) == ("slot1.1", 250.0)
+    assert (c["uplink_key"], c["uplink_mbps"]) == ("us>eu", 100.0)
+    same_site = pair_link(spec, {}, (0, 0), (1, 0))
+    assert "uplink_key" not in same_site and same_site["ingress_mbps"] == 200.0
+    back = pair_link(spec, reverse_link({}), (1, 1), (0, 0))
+    assert back["uplink_key"] == "eu>us" and back["uplink_mbps"] == 120.0
+    assert len(link_buckets(c, "pacing-test")) == 3
+    assert pair_link(_shared_spec(pacing="link").finalize(), {}, (0, 0), (1, 1)) == {}
+    for bad in (dict(uplink_mbps={"us->eu": 100.0}),            # eu->us missing
+                dict(peer_egress_mbps=[[400.0], [300.0]]),       # not every slot
+                dict(peer_ingress_mbps=[[0.0], [1.0, 1.0]]),      # not > 0
+                dict(sites=[["us"], ["us", ""]]),
+                dict(pacing="fair"),
+                dict(emission_order=["store"]),
+                dict(piece_bounds=[None, None])):
+        with pytest.raises((ValueError, NotImplementedError)):
+            _shared_spec(**bad).finalize()
+
+
+@pytest.mark.parametrize("backend", ["tcp", "gloo"])
+def test_pipeline_under_shared_pacing_across_sites_is_bitwise(tmp_path, monkeypatch, backend):
+    """A run paced by the spec's shared budgets (two sites, a wide stage whose
+    replicas sit on both): the connections open their budgets (on the gloo
+    plane one pacer per direction serves a whole neighbour stage, so the
+    receiver's budgets apply only toward a one-peer stage), and the losses
+    equal the oracle."""
+    import glob
+
+    from elysium_wan_b200.launch.local import run_and_compare
+
+    monkeypatch.setenv("ELYSIUM_PEER_KEY", str(tmp_path / "peer.key"))
+    port = 33500 + 30 * (backend == "gloo") + (os.getpid() % 200) * 7
+    spec = _shared_spec(out_dir=str(tmp_path), port_base=port, backend=backend,
+                        wire_codec="planes")
+    r = run_and_compare(spec, timeout=300)
+    assert r["ok"] and r["compared"] == 8, r
+    names = {os.path.basename(p).split("-")[0]
+             for p in glob.glob(str(tmp_path / ".pacers" / "*.bucket"))}
+    want = {"egress_slot0.0", "egress_slot1.0", "egress_slot1.1", "ingress_slot0.0",
+            "uplink_eu>us"}
+    if backend == "tcp":
+        want |= {"ingress_slot1.0", "ingress_slot1.1", "uplink_us>eu"}
+    assert want <= names, names
