@@ -114,6 +114,10 @@ class JobSpec:
     # (peer_ingress_mbps) and, between two sites (sites[stage][peer]), the
     # uplink of that direction (uplink_mbps["a->b"]), each a token bucket
     # that every connection of the host shares (transport/pacer.py).
+    # Shim settings of the links among a wide stage's replicas (the TCP
+    # plane's mesh): per stage {"p>q": link}; filled by placement from the
+    # nodes' emulation profiles. This engine's own field.
+    mesh_links: list | None = None
     pacing: str = "link"
     peer_egress_mbps: list | None = None
     peer_ingress_mbps: list | None = None

@@ -105,6 +105,17 @@ def emulated_links(groups, emulations) -> list | None:
     return [_hop(heads[r], heads[(r + 1) % len(heads)], profiles) for r in range(len(heads))]
 
 
+def emulated_mesh_links(groups, emulations) -> list | None:
+    """Per stage, the shim settings of the links among its replicas
+    ({"p>q": link}, from p's emulation profile toward q's region), or None
+    unless every node declared a profile."""
+    profiles = emulations or {}
+    if not profiles or not all(getattr(e, "enabled", False) for e in profiles.values()):
+        return None
+    return [{f"{p}>{q}": _hop(g[p], g[q], profiles) for p in range(len(g)) for q in range(len(g))
+             if p != q} for g in groups]
+
+
 @dataclass
 class Placement:
     widths: list
@@ -115,6 +126,7 @@ class Placement:
     partition: list | None  # None: keep the spec's
     links: list | None
     names: list = field(default_factory=list)
+    mesh_links: list | None = None
 
     def apply(self, spec: JobSpec) -> JobSpec:
         spec.stage_widths = list(self.widths)
@@ -129,6 +141,8 @@ class Placement:
             spec.partition = self.partition
         if self.links is not None:
             spec.links = self.links
+        if self.mesh_links is not None:
+            spec.mesh_links = self.mesh_links
         return spec.reschedule()
 
     def rationale(self, spec: JobSpec) -> dict:
@@ -159,7 +173,8 @@ def plan_placement(spec: JobSpec, groups, emulations=None, keep_partition: bool 
         peer_weights=[[n.speed() / top for n in g] for g, top in zip(groups, fastest)],
         partition=cut,
         links=emulated_links(groups, emulations),
-        names=[[f"{n.name}({n.device})" for n in g] for g in groups])
+        names=[[f"{n.name}({n.device})" for n in g] for g in groups],
+        mesh_links=emulated_mesh_links(groups, emulations))
 
 
 def place(spec: JobSpec, groups, emulations=None, keep_partition: bool = False) -> dict:

@@ -336,7 +336,9 @@ class TcpPipeComm:
         if width > 1:
             links = {}
             for q, sc in sorted({**mesh_in, **mesh_out}.items()):
-                cfg = pair_link(spec, {}, (self.stage, self.peer), (self.stage, q))
+                own = (spec.mesh_links[self.stage] or {}).get(f"{self.peer}>{q}", {}) \
+                    if spec.mesh_links else {}
+                cfg = pair_link(spec, own, (self.stage, self.peer), (self.stage, q))
                 links[q] = _Link(self, [sc], cfg, wire_codec=exch)
                 self._start_readers([sc], key=lambda f: ("mesh", f.type, f.mb, f.chunk))
             if sorted(links) != [q for q in range(width) if q != self.peer]:

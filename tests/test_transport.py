@@ -412,6 +412,15 @@ def test_emulated_links_carry_shared_budgets():
     off = {"n0": Emulation.from_profile("a", {"inter": prof["inter"]}),
            "n1": Emulation.from_profile("b", {"inter": prof["inter"]})}
     assert emulated_links(groups, off)[0]["egress_key"] == ""
+    # a wide stage whose replicas sit in two regions: its mesh links are shaped too
+    from elysium_wan_b200.scheduler.placement import emulated_mesh_links
+
+    wide = [[N(0, "a")], [N(3, "a"), N(2, "b")]]
+    ems["n2"], ems["n3"] = Emulation.from_profile("b", prof), Emulation.from_profile("a", prof)
+    mesh = emulated_mesh_links(wide, ems)
+    assert mesh[0] == {} and set(mesh[1]) == {"0>1", "1>0"}
+    assert mesh[1]["0>1"]["uplink_key"] == "a>b" and mesh[1]["1>0"]["uplink_key"] == "b>a"
+    assert mesh[1]["0>1"]["latency_ms"] == 20.0
 
 
 def test_multi_flow_fragments_reassemble_across_flows(tmp_path, monkeypatch):
@@ -634,7 +643,9 @@ def test_wide_stage_exchange_and_tied_relay_cross_the_sealed_plane(tmp_path, mon
         cfg = make_config("toy", n_layer=4, vocab_size=97, d_model=64, n_head=4, seq_len=16,
                           norm="rmsnorm", mlp="swiglu", pos="rope", bias=False, moe_experts=4,
                           moe_top_k=2, moe_d_ff=64, moe_select="score_bias", moe_bias_rate=0.01)
-        kw = dict(stages=2, stage_widths=[1, 2], shard="pieces")
+        shaped = {"latency_ms": 2.0, "bw_mbps": 400.0}
+        kw = dict(stages=2, stage_widths=[1, 2], shard="pieces",
+                  mesh_links=[{}, {"0>1": shaped, "1>0": shaped}])  # the mesh links shaped
     port = 32500 + 40 * (case != "tied_zero1_1_2_1") + (os.getpid() % 200) * 7
     spec = JobSpec(model=cfg, microbatches=4, mb_size=2, steps=3, out_dir=str(tmp_path),
                    port_base=port, backend="tcp", wire_codec="planes", **kw)
