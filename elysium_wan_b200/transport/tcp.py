@@ -40,7 +40,6 @@ import threading
 import time
 
 import torch
-import torch.distributed as dist
 
 from elysium_wan_b200.models.gpt import Act
 from elysium_wan_b200.transport.pacer import pair_link, reverse_link
@@ -190,22 +189,10 @@ class TcpPipeComm:
         self.rank = spec.rank_of(stage, peer)
         self.timeout = timeout_s
         self.wire_codec = spec.wire_codec if spec.wire_codec != "native" else "raw"
-        world = spec.world_size
-        # intra-stage group for ZeRO-1 (created by every rank in the same order)
+        # The wide-stage exchange and the tied relay run on this plane's own
+        # sealed links (StageMesh, the tied link); no process group carries
+        # their bytes.
         self.g_stage = None
-        for r, w in enumerate(spec.stage_widths):
-            g = dist.new_group([spec.rank_of(r, q) for q in range(w)]) if world > 1 else None
-            if r == stage:
-                self.g_stage = g
-        # Tied embeddings across a cut: stage 0 and the head's stage exchange
-        # the head's table gradient and the updated table once per step.
-        self.g_tied = None
-        if spec.model.tie_embeddings and spec.stages > 1 and world > 1:
-            a, b = spec.rank_of(0, 0), spec.rank_of(spec.stages - 1, 0)
-            g = dist.new_group([a, b])
-            if self.rank in (a, b):
-                self.g_tied = g
-            self.tied_peer = b if self.rank == a else a
         cfg = spec.model
         self.T, self.d = spec.mb_size * cfg.seq_len, cfg.d_model
         self.cuda = self.device.type == "cuda"
