@@ -263,3 +263,70 @@ def test_lane_orders_never_slower_or_deadlocked_random():
         assert t_got <= t_split * (1 + 1e-9)
         chosen += t_got < t_split
     assert chosen > 0
+
+
+@pytest.mark.parametrize("S,M", [(4, 8), (3, 12), (2, 6)])
+def test_memory_budget_is_kept_and_the_bubble_never_grows_with_it(S, M):
+    """Under a per-stage activation budget from one microbatch's F and B up to
+    no limit, every stage's order holds at most its budget in flight, and the
+    simulated step never gets longer as the budget grows (a tight budget
+    degrades the schedule instead of refusing it)."""
+    from elysium_wan_b200.models.config import make_config
+    from elysium_wan_b200.runtime.spec import JobSpec
+    from elysium_wan_b200.scheduler.planner import default_schedule, stage_memory_model, zb_config
+    from elysium_wan_b200.scheduler.rebalance import order_peak
+    from elysium_wan_b200.scheduler.zero_bubble import simulate_slots
+
+    cfg = make_config("toy", n_layer=8, vocab_size=97, d_model=128, n_head=4, seq_len=64)
+    spec = JobSpec(model=cfg, stages=S, microbatches=M, mb_size=2).finalize()
+    mems = [stage_memory_model(spec, r) for r in range(S)]
+    unit = max(max(m[0], m[0] + m[1]) for m in mems)
+    prev = None
+    for k in (1, 1.5, 2, 3, 4, 6, 8, 100):
+        b = k * unit
+        order = default_schedule(spec, [b] * S)
+        for r in range(S):
+            d = {"F": mems[r][0], "B": mems[r][1], "W": mems[r][2]}
+            assert order_peak([(op, mb) for op, mb in order[r][0]], d) <= b * (1 + 1e-9)
+        slots = [[[(op, int(mb)) for op, mb in o] for o in st] for st in order]
+        ms = simulate_slots(zb_config(spec), slots, spec.peer_weights)[1]
+        assert prev is None or ms <= prev * (1 + 1e-9), (k, ms, prev)
+        prev = ms
+
+
+def test_ownership_replan_touches_only_ownership_and_order_and_is_deterministic():
+    """For random per-peer costs on random wide layouts, the re-plan changes
+    only peer_weights, mb_owner and schedule_order, gives every peer a
+    microbatch, yields orders the spec accepts, and gives the same answer
+    twice."""
+    import copy
+    import random
+    from dataclasses import asdict
+
+    from elysium_wan_b200.models.config import make_config
+    from elysium_wan_b200.runtime.spec import JobSpec
+    from elysium_wan_b200.scheduler import rebalance as rb
+
+    rng = random.Random(7)
+    cfg = make_config("toy", n_layer=6, vocab_size=97, d_model=64, n_head=4, seq_len=16)
+    for _ in range(12):
+        S = rng.choice([2, 3])
+        widths = [rng.choice([1, 2, 3]) for _ in range(S)]
+        M = max(widths) * rng.choice([2, 3])
+        spec = JobSpec(model=cfg, stages=S, stage_widths=widths, microbatches=M,
+                       mb_size=1).finalize()
+        prof = [[{"t_f": rng.uniform(1, 8) * 1e-3, "t_b": rng.uniform(2, 16) * 1e-3,
+                  "t_w": rng.uniform(0, 8) * 1e-3} for _ in range(w)] for w in widths]
+        a = rb.replan_ownership(copy.deepcopy(spec), prof)
+        b = rb.replan_ownership(copy.deepcopy(spec), prof)
+        assert a == b
+        new = copy.deepcopy(spec)
+        new.peer_weights, new.mb_owner = a["peer_weights"], a["mb_owner"]
+        new.schedule_order, new.stage_costs = a["schedule_order"], a["stage_costs"]
+        new.finalize()  # the orders cover exactly each peer's microbatches
+        moved = {k for k, v in asdict(spec).items()
+                 if asdict(new)[k] != v} - {"peer_weights", "mb_owner", "schedule_order",
+                                            "stage_costs"}
+        assert not moved, moved
+        for r, w in enumerate(widths):
+            assert set(a["mb_owner"][r]) == set(range(w))
