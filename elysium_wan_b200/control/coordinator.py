@@ -1001,15 +1001,16 @@ class Coordinator:
         owners = None
         try:
             profiles = rb.profiles_from_telemetry(spec, windows)
+            hops = rb.hops_from_telemetry(spec, windows)
             if any(w > 1 for w in spec.stage_widths):
-                got = rb.replan_ownership(spec, profiles, self.cfg.replan_min_gain)
+                got = rb.replan_ownership(spec, profiles, self.cfg.replan_min_gain, hops)
                 self.events.append(("replan_eval", None, {"step": step, "why": got["why"]}))
                 res = None
                 if got["decision"]:
                     res = got["schedule_order"], got["pred_cur_s"], got["pred_new_s"]
                     owners = got
             else:
-                res = rb.replan_schedule(spec, profiles, self.cfg.replan_min_gain)
+                res = rb.replan_schedule(spec, profiles, self.cfg.replan_min_gain, hops)
         except ValueError as e:
             self.events.append(("reschedule_skipped", None, {"step": step, "why": str(e)}))
             return None

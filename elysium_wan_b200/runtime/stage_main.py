@@ -187,6 +187,7 @@ def run_stage(spec, stage: int, peer: int, timeout_s: float = 600.0) -> int:
     net0 = (0, 0)
     t_run = time.perf_counter()
     waves = WaveWriter(spec, stage, peer)
+    links0: dict = {}
     try:
         for step in range(start, spec.steps):
             t0 = time.perf_counter()
@@ -200,9 +201,15 @@ def run_stage(spec, stage: int, peer: int, timeout_s: float = 600.0) -> int:
                     stream.write(json.dumps(rec) + "\n")
                     stream.flush()
                 _print("WT_METRIC", {"step": step, "mb": mb, "loss": v})
+            links = None
+            if hasattr(comm, "link_stats"):
+                now = comm.link_stats()
+                links = {k: {f: round(v[f] - links0.get(k, {}).get(f, 0), 3) for f in v}
+                         for k, v in now.items()}
+                links0 = now
             summary = summarize_step(step, stage, peer, dt * 1e3, eng.op_times_ms(),
                                      comm.bytes_sent if comm else 0, comm.frames if comm else 0,
-                                     eng.phase_ms().get("opt_ms"))
+                                     eng.phase_ms().get("opt_ms"), links)
             if "ops" not in summary:
                 _print("WT_WARN", f"telemetry summary of step {step} exceeded 4096 bytes: its "
                                   "per-op medians were dropped")

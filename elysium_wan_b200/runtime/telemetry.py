@@ -18,7 +18,10 @@ import statistics
 
 
 def summarize_step(step, stage, peer, step_ms, op_times, bytes_sent, frames,
-                   opt_ms: float | None = None) -> dict:
+                   opt_ms: float | None = None, links: dict | None = None) -> dict:
+    """The per-step WT_TELEM summary. `links`: this step's per-link send
+    statistics ({label: {"frames", "bytes", "busy_ms"}}, the TCP plane's),
+    filed under "hops" next to the step's totals."""
     import time as _time
 
     t_emit = _time.perf_counter()
@@ -49,7 +52,7 @@ def summarize_step(step, stage, peer, step_ms, op_times, bytes_sent, frames,
            "emit_us": 0, "ops": ops, "stall_ms": round(max(0.0, span - busy), 3),
            "busy_ms": round(busy, 3),
            "busy_frac": round(busy / span, 4) if span > 0 else None,
-           "hops": {"frames": frames, "bytes": bytes_sent},
+           "hops": {"frames": frames, "bytes": bytes_sent, **(links or {})},
            "recv": {"n": len(gaps), "med_ms": round(statistics.median(gaps), 4) if gaps else 0.0,
                     "max_ms": round(max(gaps), 4) if gaps else 0.0}}
     out["emit_us"] = int((_time.perf_counter() - t_emit) * 1e6)

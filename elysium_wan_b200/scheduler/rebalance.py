@@ -136,7 +136,7 @@ def stage_costs_from_profiles(profiles: list, peer_weights: list | None = None) 
     return out
 
 
-def replan_schedule(spec, profiles: list, min_gain: float = 0.10):
+def replan_schedule(spec, profiles: list, min_gain: float = 0.10, hops: list | None = None):
     """Re-solve the zero-bubble order from measured costs (reference:
     scheduler/zero_bubble.py:1079 `replan`, its order half). Ownership and
     the cut stay, so the run's bits do not change. -> (new schedule_order,
@@ -149,7 +149,7 @@ def replan_schedule(spec, profiles: list, min_gain: float = 0.10):
 
     s2 = copy.deepcopy(spec)
     s2.stage_costs = stage_costs_from_profiles(profiles, spec.peer_weights)
-    cfg = zb_config(s2)
+    cfg = _measured_comm(zb_config(s2), hops)
 
     def makespan(order):
         slots = [[[(op, int(mb)) for op, mb in o] for o in per_stage] for per_stage in order]
@@ -194,13 +194,14 @@ def _with_one_each(n: int, weights: list) -> list:
     raise ValueError("cannot give every peer a microbatch")
 
 
-def replan_ownership(spec, profiles: list, min_gain: float = 0.10) -> dict:
+def replan_ownership(spec, profiles: list, min_gain: float = 0.10, hops: list | None = None) -> dict:
     """Re-solve a job's ownership and order from measured per-peer costs
     (reference: scheduler/zero_bubble.py:1079 `replan`, both halves). Each
     wide stage's peer weights become its peers' measured rates (every peer
     keeps at least one microbatch, so the next window measures it again), the
     microbatches are re-dealt by IWRR and the zero-bubble order re-solved.
-    Both predictions run the same measured model (`measured_model`), so a
+    Both predictions run the same measured model (`measured_model`, and the
+    hops' measured transfer times when given: `hops_from_telemetry`), so a
     bias of the profile cancels. Only peer_weights, mb_owner and
     schedule_order change. Unlike the reference's per-microbatch fold, this
     engine's declared `dp_tree` fold sums each replica's own microbatches
@@ -220,7 +221,7 @@ def replan_ownership(spec, profiles: list, min_gain: float = 0.10) -> dict:
     speeds, costs = measured_model(profiles)
     cur = copy.deepcopy(spec)
     cur.stage_costs = costs
-    cfg = zb_config(cur)
+    cfg = _measured_comm(zb_config(cur), hops)
 
     def predict(order):
         slots = [[[(op, int(mb)) for op, mb in o] for o in per_stage] for per_stage in order]
@@ -318,3 +319,33 @@ def memory_partition(spec, budgets: list) -> list | None:
     except ValueError:
         return None
     return None if new == [list(x) for x in spec.partition] else new
+
+
+def hops_from_telemetry(spec, windows: dict) -> list:
+    """Per hop j -> j + 1, the seconds a sender spends per boundary transfer,
+    measured: the median over the window of busy_ms / frames of every link
+    across the hop (stage j's next<q> links, stage j + 1's prev<p> links), or
+    None for a hop nothing was measured on (a plane without per-link
+    statistics). A frame counts once however many fragments and flows carry
+    it (reference: `hops_from_telemetry`, src/wantrain/scheduler/
+    zero_bubble.py:1030, semantics only)."""
+    out = []
+    for j in range(spec.stages - 1):
+        xs = []
+        for r, head in ((j, "next"), (j + 1, "prev")):
+            for q in range(spec.stage_widths[r]):
+                for summ in windows.get((r, q)) or []:
+                    for label, h in (summ.get("hops") or {}).items():
+                        if not isinstance(h, dict) or label.rstrip("0123456789") != head:
+                            continue
+                        if h.get("frames", 0) > 0:
+                            xs.append(float(h["busy_ms"]) / 1e3 / h["frames"])
+        out.append(statistics.median(xs) if xs else None)
+    return out
+
+
+def _measured_comm(cfg, hops):
+    """cfg with each hop's modelled transfer replaced by its measured one."""
+    if hops:
+        cfg.comm = [c if m is None else float(m) for c, m in zip(cfg.comm, hops)]
+    return cfg

@@ -101,6 +101,9 @@ class _Link:
         self.q: queue.Queue = queue.Queue()
         self.err: Exception | None = None
         self.shim = _Shim(link_cfg or {}, comm.spec.tag)
+        # what this link has sent: whole frames, payload bytes, and the time
+        # its sender spent on them (pacing included) -> per-hop telemetry
+        self.stats = {"frames": 0, "bytes": 0, "busy_ms": 0.0}
         self.t = threading.Thread(target=self._loop, daemon=True)
         self.t.start()
 
@@ -152,12 +155,16 @@ class _Link:
                 if item is None:
                     return
                 ftype, step, mb, tensors = item
+                nbytes = sum(t.numel() * t.element_size() for t in tensors)
+                t0 = time.monotonic()
                 if self.shim.active:
-                    nbytes = sum(t.numel() * t.element_size() for t in tensors)
                     self.shim.submit(lambda: self._send_frame(ftype, step, mb, tensors), nbytes)
                     self.shim.flush()
                 else:
                     self._send_frame(ftype, step, mb, tensors)
+                st = self.stats
+                st["frames"], st["bytes"] = st["frames"] + 1, st["bytes"] + nbytes
+                st["busy_ms"] += (time.monotonic() - t0) * 1e3
             except Exception as e:  # surfaced on the next flush / send
                 self.err = e
             finally:
@@ -452,6 +459,17 @@ class TcpPipeComm:
     def tied_recv(self, buf):
         f = self.inbox.get(("tied", TIED), self.timeout)
         buf.copy_(f.tensor().view_as(buf).to(buf.device))
+
+    def link_stats(self) -> dict:
+        """Cumulative per-link send statistics, labelled by direction and
+        peer (next<q>, prev<p>, mesh<q>, tied)."""
+        out = {f"next{q}": dict(l.stats) for q, l in self.next_links.items()}
+        out.update({f"prev{p}": dict(l.stats) for p, l in self.prev_links.items()})
+        if self.mesh is not None:
+            out.update({f"mesh{q}": dict(l.stats) for q, l in self.mesh.links.items()})
+        if self.tied_link is not None:
+            out["tied"] = dict(self.tied_link.stats)
+        return out
 
     def _links(self) -> list:
         out = list(self.next_links.values()) + list(self.prev_links.values())

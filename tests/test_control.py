@@ -600,3 +600,29 @@ def test_fit_check_runs_on_every_slot_before_launch(tmp_path):
     ref.finalize()
     r = compare(run_baseline(ref, "reference"), res.losses_path)
     assert r["ok"] and r["compared"] == 8, r
+
+
+def test_hops_from_telemetry_counts_transfers_and_feed_the_replan():
+    """Per-hop transfer time from the TCP plane's per-link statistics: the
+    median of busy_ms / frames over the links across the hop (a frame counts
+    once whatever its fragments), None where nothing was measured; a slow
+    measured hop lengthens the re-plan's predicted step."""
+    from elysium_wan_b200.scheduler import rebalance as rb
+
+    cfg = make_config("toy", n_layer=4, vocab_size=97, d_model=64, n_head=4, seq_len=16)
+    spec = JobSpec(model=cfg, stages=3, stage_widths=[1, 2, 1], microbatches=4,
+                   mb_size=1).finalize()
+    ops = {"F": {"n": 2, "med_ms": 1.0}, "B": {"n": 2, "med_ms": 2.0}, "W": {"n": 2, "med_ms": 1.0}}
+    win = {(0, 0): [{"ops": ops, "hops": {"frames": 9, "bytes": 1,
+                                          "next0": {"frames": 2, "bytes": 8, "busy_ms": 40.0},
+                                          "next1": {"frames": 2, "bytes": 8, "busy_ms": 60.0}}}],
+           (1, 0): [{"ops": ops, "hops": {"prev0": {"frames": 2, "bytes": 8, "busy_ms": 50.0},
+                                          "mesh1": {"frames": 1, "bytes": 8, "busy_ms": 999.0}}}],
+           (1, 1): [{"ops": ops, "hops": {"frames": 3, "bytes": 5}}],
+           (2, 0): [{"ops": ops, "hops": {}}]}
+    hops = rb.hops_from_telemetry(spec, win)
+    assert hops[0] == pytest.approx(0.025) and hops[1] is None
+    prof = rb.profiles_from_telemetry(spec, win)
+    fast = rb.replan_ownership(spec, prof, 0.0, [0.0, 0.0])
+    slow = rb.replan_ownership(spec, prof, 0.0, [0.05, 0.0])
+    assert slow["pred_cur_s"] > fast["pred_cur_s"]

@@ -654,6 +654,14 @@ def test_wide_stage_exchange_and_tied_relay_cross_the_sealed_plane(tmp_path, mon
     logs = {os.path.basename(p): open(p).read() for p in glob.glob(str(tmp_path / "*_r*p*.log"))}
     wide = [t for n, t in logs.items() if "_r1p" in n]
     assert len(wide) == 2 and all("WT_MESH" in t for t in wide), list(logs)
+    # per-link send statistics ride in each step's telemetry
+    import json as _json
+
+    telem = [_json.loads(line.split(" ", 1)[1]) for line in wide[0].splitlines()
+             if line.startswith("WT_TELEM ")]
+    mesh = [h for k, h in telem[-1]["hops"].items() if k.startswith("mesh")]
+    assert len(mesh) == 1 and mesh[0]["frames"] > 0 and mesh[0]["busy_ms"] >= 0, telem[-1]
+    assert any(k.startswith("prev") for k in telem[-1]["hops"]), telem[-1]
     if case == "tied_zero1_1_2_1":
         ends = [t for n, t in logs.items() if "_r0p0" in n or "_r2p0" in n]
         assert len(ends) == 2 and all("WT_TIED_LINK" in t for t in ends)
