@@ -59,8 +59,16 @@ class StageProcess:
 
     def _read(self, on_line):
         for line in self.p.stdout:
-            self.log.write(line)
-            self.log.flush()
+            if self.log is not None:
+                # a log that cannot be written (disk full, file gone) never
+                # stops the pump: the stage would block on a full pipe and its
+                # markers would stop reaching the coordinator
+                try:
+                    self.log.write(line)
+                    self.log.flush()
+                except (OSError, ValueError) as e:
+                    print(f"stage log not written from here on: {e}", file=sys.stderr, flush=True)
+                    self.log = None
             line = line.rstrip("\n")
             self.tail = (self.tail + [line])[-40:]
             if line.startswith("WT_DONE"):
@@ -81,13 +89,20 @@ class StageProcess:
                 pass
         self.p.wait()
         self.t.join(timeout=5)
-        self.log.close()
+        self._close_log()
 
     def wait(self) -> int:
         rc = self.p.wait()
         self.t.join(timeout=10)
-        self.log.close()
+        self._close_log()
         return rc
+
+    def _close_log(self):
+        try:
+            if self.log is not None:
+                self.log.close()
+        except OSError:
+            pass
 
 
 class WorkerAgent:

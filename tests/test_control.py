@@ -626,3 +626,42 @@ def test_hops_from_telemetry_counts_transfers_and_feed_the_replan():
     fast = rb.replan_ownership(spec, prof, 0.0, [0.0, 0.0])
     slow = rb.replan_ownership(spec, prof, 0.0, [0.05, 0.0])
     assert slow["pred_cur_s"] > fast["pred_cur_s"]
+
+
+def test_a_stage_log_that_cannot_be_written_never_stops_the_pump(tmp_path):
+    """The agent copies a stage's output to a log file while it forwards the
+    marker lines. When that file cannot be written (disk full), every line
+    still reaches the handler and the stage never blocks on a full pipe."""
+    import sys
+
+    import os
+
+    from elysium_wan_b200.control.agent import StageProcess
+
+    class Full:
+        def write(self, _):
+            raise OSError(28, "No space left on device")
+
+        def flush(self):
+            pass
+
+        def close(self):
+            pass
+
+    seen = []
+    prog = "import sys\nfor i in range(20000): print(f'WT_STEP {i}')\nprint('WT_DONE 0')\n"
+    sp = StageProcess([sys.executable, "-c", prog], dict(os.environ), seen.append,
+                      str(tmp_path / "stage.log"))
+    sp.log.close()
+    sp.log = Full()
+    import threading
+
+    rc: list = []
+    t = threading.Thread(target=lambda: rc.append(sp.wait()), daemon=True)
+    t.start()
+    t.join(60)
+    if not rc:
+        sp.kill()
+        pytest.fail("the stage blocked: its output was no longer read")
+    assert rc == [0]
+    assert len(seen) == 20001 and seen[-1] == "WT_DONE 0" and sp.done_marker
