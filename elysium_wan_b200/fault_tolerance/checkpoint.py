@@ -163,6 +163,9 @@ def load_latest(spec, stage: int, peer: int, step: int | None = None):
                 from None
         if not isinstance(state, dict):
             raise ValueError(f"wave {path}: state.pt is not a checkpoint")
+        if s > spec.steps:
+            raise ValueError(f"wave {path} is at step {s}, past the run's {spec.steps} steps: "
+                             "resume with at least as many steps")
         diff = first_pin_difference(spec.pins(), state.get("pins", {}))
         if diff is not None:
             raise ValueError(f"wave {path} was written under another recipe: pin {diff!r} differs")

@@ -262,6 +262,18 @@ def test_resume_drops_the_abandoned_timeline_and_sweeps_temps(tmp_path):
     assert store.common_step("run1", spec) == 2
 
 
+def test_resume_refuses_fewer_steps_than_the_wave_holds(tmp_path):
+    """A wave of step 6 does not resume a run of 4 steps (it would train
+    nothing and report a finished run); as many or more steps resume."""
+    spec = _spec(tmp_path)
+    ckpt.commit_wave(spec, 0, 0, 6, {"step": 6})
+    spec.steps = 4
+    with pytest.raises(ValueError, match="past the run"):
+        ckpt.load_latest(spec, 0, 0)
+    spec.steps = 6
+    assert ckpt.load_latest(spec, 0, 0)[1] == 6
+
+
 def test_resume_refuses_other_recipe(tmp_path):
     spec = _spec(tmp_path)
     ckpt.commit_wave(spec, 0, 0, 2, {"step": 2})
