@@ -1212,14 +1212,16 @@ class Coordinator:
                 return Verdict("failed", None, "job timeout")
 
     def _abort_all(self):
+        # the channels are picked under the lock and written to outside it: a
+        # send to an agent that is slow to read must not hold up the readers
         with self.lock:
-            for s, nid in self.slot_node.items():
-                n = self.nodes[nid]
-                if n.connected and not n.dead:
-                    try:
-                        n.ch.send("ABORT")
-                    except OSError:
-                        pass
+            chans = [self.nodes[nid].ch for nid in dict.fromkeys(self.slot_node.values())
+                     if self.nodes[nid].connected and not self.nodes[nid].dead]
+        for ch in chans:
+            try:
+                ch.send("ABORT")
+            except (OSError, ConnectionError):
+                pass
         time.sleep(0.5)
 
     def _collect(self, spec, run_dir) -> str:

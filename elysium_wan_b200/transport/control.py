@@ -90,6 +90,9 @@ def _recv_exact(sock: socket.socket, n: int) -> bytes:
     return bytes(buf)
 
 
+SEND_STALL_S = 10
+
+
 class Channel:
     """A framed, thread-safe (for sends) message channel over one socket."""
 
@@ -102,6 +105,18 @@ class Channel:
         try:
             sock.setsockopt(socket.IPPROTO_TCP, socket.TCP_NODELAY, 1)
         except OSError:
+            pass
+        # A send that the peer does not drain must not block forever (two
+        # sides sending at once with full buffers, one of them holding a lock
+        # its own reader needs, would never end): the kernel gives up on a
+        # blocked send after SEND_STALL_S (EAGAIN), send_all retries until it
+        # has made no progress for its budget, and the send then fails like a
+        # lost peer.
+        raw = getattr(sock, "sock", sock)
+        try:
+            raw.setsockopt(socket.SOL_SOCKET, socket.SO_SNDTIMEO,
+                           struct.pack("ll", int(SEND_STALL_S), 0))
+        except (OSError, AttributeError):
             pass
 
     def _send(self, data) -> None:

@@ -207,55 +207,3 @@ def test_heal_over_tcp_with_format_boundaries(tmp_path, monkeypatch, boundary):
     assert res.heals == 1
     _oracle_ok(spec, res, tmp_path)
 
-
-@pytest.mark.slow
-def test_heal_after_an_ownership_replan_keeps_one_timeline(tmp_path):
-    """A wide stage's replica slows down, the coordinator re-deals its
-    microbatches at a wave (the ownership log records the old table), then a
-    worker dies: the heal resumes from a wave of the new timeline, the waves
-    each relaunch abandons are dropped, and every loss equals the oracle that
-    follows the ownership log."""
-    import json
-    import os
-
-    cfg = make_config("toy", n_layer=4, vocab_size=97, d_model=64, n_head=4, seq_len=16)
-    spec = JobSpec(model=cfg, stages=2, stage_widths=[1, 2], microbatches=8, mb_size=1,
-                   steps=12, backend="gloo", tag="owheal", ckpt_every=2,
-                   partition=[[0, 3], [3, 6]])
-    cl = LocalCluster(str(tmp_path / "cl"), ["a"] * 4,
-                      coord=dict(profile=False, recut=False, watch_slow=False, replan_cost_s=0.0,
-                                 replan_min_gain=0.1, replan_min_summaries=2),
-                      worker_env={"WANTRAIN_SIM_SLOW": "1:1:4:2"})
-
-    def after_replan():
-        if not cl.coord.replans:
-            return None
-        cl.kill_worker(cl.worker_of_slot((1, 0)))
-        return True
-
-    done = {}
-
-    def on_progress(slot, s, nid):
-        if not done and s >= 8:
-            got = after_replan()
-            if got:
-                done["x"] = got
-
-    cl.coord.on_progress = on_progress
-    try:
-        res = cl.run(Job(spec=spec))
-        replans = list(cl.coord.replans)
-    finally:
-        cl.close()
-    assert res.ok, res.why
-    assert done and res.heals == 1, (done, res.heals)
-    assert replans and replans[0].get("owner_changed"), replans
-    with open(os.path.join(res.run_dir, "spec.json")) as f:
-        ran = JobSpec.from_dict(json.load(f))
-    assert ran.ownership_log
-    ref = JobSpec.from_dict(ran.to_dict())
-    ref.out_dir = str(tmp_path / "oracle")
-    ref.resume, ref.resume_step = False, None
-    ref.finalize()
-    r = compare(run_baseline(ref, "reference"), res.losses_path)
-    assert r["ok"] and r["compared"] == 96, r

@@ -665,3 +665,25 @@ def test_a_stage_log_that_cannot_be_written_never_stops_the_pump(tmp_path):
         pytest.fail("the stage blocked: its output was no longer read")
     assert rc == [0]
     assert len(seen) == 20001 and seen[-1] == "WT_DONE 0" and sp.done_marker
+
+
+def test_a_send_the_peer_never_drains_fails_instead_of_blocking(monkeypatch):
+    """A control channel whose peer stops reading: once the socket buffers are
+    full, the send gives up after the stall limit and the no-progress budget
+    and fails like a lost peer, instead of blocking its thread (and any lock
+    it holds) for good."""
+    import socket
+    import time
+
+    from elysium_wan_b200.transport import control, sendall
+
+    monkeypatch.setattr(control, "SEND_STALL_S", 1)
+    monkeypatch.setattr(sendall, "RETRY_BUDGET_S", 0.5)
+    a, b = socket.socketpair()
+    ch = control.Channel(a)
+    t0 = time.monotonic()
+    with pytest.raises(OSError):
+        ch.send("BIG", body=b"x" * (64 << 20))  # b never reads
+    assert time.monotonic() - t0 < 30
+    a.close()
+    b.close()
